@@ -1,0 +1,334 @@
+// Python bindings for the sm_100a kernels (module lake_b200._C).
+// Every op runs on the caller's current CUDA stream and raises on a launch or
+// argument error, so a missing or failing kernel is never silently replaced.
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "../kernels/lakeb_kernels.h"
+
+namespace {
+
+using lakeb::GemmArgs;
+using lakeb::KVArenaView;
+using lakeb::PagedAttnArgs;
+
+#define LAKEB_CHECK_RC(rc, what) TORCH_CHECK((rc) == 0, what, " failed with code ", (rc))
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+const __nv_bfloat16* bf(const at::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
+__nv_bfloat16* bfm(const at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+
+void check_bf16_2d(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bf16");
+  TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with unit inner stride");
+}
+
+int* status_ptr(const c10::optional<at::Tensor>& st) {
+  if (!st.has_value()) return nullptr;
+  TORCH_CHECK(st->scalar_type() == at::kInt && st->is_cuda(), "status must be an int32 CUDA tensor");
+  return st->data_ptr<int>();
+}
+
+GemmArgs base_args(const at::Tensor& a, const at::Tensor& w) {
+  check_bf16_2d(a, "A");
+  check_bf16_2d(w, "W");
+  TORCH_CHECK(a.size(1) == w.size(1), "K mismatch: ", a.size(1), " vs ", w.size(1));
+  GemmArgs g;
+  g.A = bf(a);
+  g.lda = a.stride(0);
+  g.B = bf(w);
+  g.ldb = w.stride(0);
+  g.M = static_cast<int>(a.size(0));
+  g.N = static_cast<int>(w.size(0));
+  g.K = static_cast<int>(a.size(1));
+  return g;
+}
+
+KVArenaView arena_view(const at::Tensor& arena, int64_t layer) {
+  TORCH_CHECK(arena.is_cuda() && arena.scalar_type() == at::kBFloat16 && arena.dim() == 6 && arena.is_contiguous(),
+              "arena must be a contiguous bf16 [blocks, layers, 2, kv_heads, block, 128] tensor");
+  TORCH_CHECK(arena.size(5) == 128, "head_dim must be 128");
+  KVArenaView v;
+  v.base = bfm(arena);
+  v.block_stride = arena.stride(0);
+  v.layer_offset = layer * arena.stride(1);
+  v.kv_stride = arena.stride(2);
+  v.head_stride = arena.stride(3);
+  v.block_size = static_cast<int>(arena.size(4));
+  return v;
+}
+
+// out = a @ w.T  (bf16 out) or fp32 out
+void linear(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c10::optional<at::Tensor> status,
+            int64_t max_ctas) {
+  GemmArgs g = base_args(a, w);
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) == a.size(0) && out.size(1) == w.size(0), "out shape");
+  g.C = out.data_ptr();
+  g.ldc = out.stride(0);
+  g.status = status_ptr(status);
+  g.max_ctas = static_cast<int>(max_ctas);
+  int epi = out.scalar_type() == at::kFloat ? lakeb::kEpiStoreF32 : lakeb::kEpiStoreBf16;
+  TORCH_CHECK(out.scalar_type() == at::kFloat || out.scalar_type() == at::kBFloat16, "out dtype");
+  LAKEB_CHECK_RC(lakeb::gemm_bf16(g, epi, cur_stream()), "linear");
+}
+
+// out = residual + a @ w.T   (residual may be out itself)
+void linear_residual(const at::Tensor& a, const at::Tensor& w, const at::Tensor& residual, at::Tensor& out,
+                     c10::optional<at::Tensor> status) {
+  GemmArgs g = base_args(a, w);
+  check_bf16_2d(out, "out");
+  check_bf16_2d(residual, "residual");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w.size(0) && residual.sizes() == out.sizes(), "shapes");
+  g.C = out.data_ptr();
+  g.ldc = out.stride(0);
+  g.R = bf(residual);
+  g.ldr = residual.stride(0);
+  g.status = status_ptr(status);
+  LAKEB_CHECK_RC(lakeb::gemm_bf16(g, lakeb::kEpiResidual, cur_stream()), "linear_residual");
+}
+
+// out[:, j] = silu(gate_j) * up_j with w rows interleaved per 256-row tile: [gate 128 | up 128]
+void linear_swiglu(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c10::optional<at::Tensor> status) {
+  GemmArgs g = base_args(a, w);
+  check_bf16_2d(out, "out");
+  TORCH_CHECK(w.size(0) % 256 == 0, "gate_up rows must be a multiple of 256");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) * 2 == w.size(0), "out shape");
+  g.C = out.data_ptr();
+  g.ldc = out.stride(0);
+  g.status = status_ptr(status);
+  LAKEB_CHECK_RC(lakeb::gemm_bf16(g, lakeb::kEpiSwiGLU, cur_stream()), "linear_swiglu");
+}
+
+// q_out = RoPE(q); K (RoPE) and V written into the paged arena at `slots` (and
+// the peer arena at `peer_slots` when given).
+void linear_qkv(const at::Tensor& a, const at::Tensor& w, at::Tensor& q_out, const at::Tensor& rope_cs,
+                const at::Tensor& positions, const at::Tensor& slots, const at::Tensor& arena, int64_t layer,
+                int64_t n_q_heads, int64_t n_kv_heads, c10::optional<at::Tensor> peer_arena,
+                c10::optional<at::Tensor> peer_slots, c10::optional<at::Tensor> status) {
+  GemmArgs g = base_args(a, w);
+  check_bf16_2d(q_out, "q_out");
+  TORCH_CHECK(q_out.size(0) == a.size(0) && q_out.size(1) == n_q_heads * 128, "q_out shape");
+  TORCH_CHECK(rope_cs.scalar_type() == at::kFloat && rope_cs.is_contiguous() && rope_cs.dim() == 3 &&
+                  rope_cs.size(1) == 64 && rope_cs.size(2) == 2,
+              "rope_cs must be fp32 [max_pos, 64, 2]");
+  TORCH_CHECK(positions.scalar_type() == at::kInt && positions.numel() >= a.size(0), "positions int32");
+  TORCH_CHECK(slots.scalar_type() == at::kLong && slots.numel() >= a.size(0), "slots int64");
+  g.C = q_out.data_ptr();
+  g.ldc = q_out.stride(0);
+  g.rope_cs = reinterpret_cast<const float2*>(rope_cs.data_ptr<float>());
+  g.positions = positions.data_ptr<int>();
+  g.slots = slots.data_ptr<int64_t>();
+  g.kv = arena_view(arena, layer);
+  g.n_q_heads = static_cast<int>(n_q_heads);
+  g.n_kv_heads = static_cast<int>(n_kv_heads);
+  if (peer_arena.has_value() && peer_slots.has_value()) {
+    g.peer_kv = arena_view(*peer_arena, layer);
+    TORCH_CHECK(peer_slots->scalar_type() == at::kLong, "peer_slots int64");
+    g.peer_slots = peer_slots->data_ptr<int64_t>();
+  }
+  g.status = status_ptr(status);
+  LAKEB_CHECK_RC(lakeb::gemm_bf16(g, lakeb::kEpiQKV, cur_stream()), "linear_qkv");
+}
+
+// amax[row] = packed (value, index) of the row's argmax of a @ w.T (bitmask-filtered).
+void linear_argmax(const at::Tensor& a, const at::Tensor& w, at::Tensor& amax, c10::optional<at::Tensor> bitmask,
+                   c10::optional<at::Tensor> status) {
+  GemmArgs g = base_args(a, w);
+  TORCH_CHECK(amax.scalar_type() == at::kLong && amax.numel() >= a.size(0) && amax.is_contiguous(), "amax int64");
+  amax.zero_();
+  g.amax = reinterpret_cast<unsigned long long*>(amax.data_ptr<int64_t>());
+  if (bitmask.has_value()) {
+    TORCH_CHECK(bitmask->scalar_type() == at::kInt && bitmask->dim() == 2 && bitmask->is_contiguous(), "bitmask");
+    g.bitmask = reinterpret_cast<const uint32_t*>(bitmask->data_ptr<int>());
+    g.bitmask_words = static_cast<int>(bitmask->size(1));
+  }
+  g.status = status_ptr(status);
+  LAKEB_CHECK_RC(lakeb::gemm_bf16(g, lakeb::kEpiArgmax, cur_stream()), "linear_argmax");
+}
+
+PagedAttnArgs attn_args(const at::Tensor& q, at::Tensor& out, const at::Tensor& arena, int64_t layer,
+                        const at::Tensor& block_tables, const at::Tensor& seq_lens, int64_t n_q_heads,
+                        int64_t n_kv_heads, double scale, c10::optional<at::Tensor> status) {
+  check_bf16_2d(q, "q");
+  check_bf16_2d(out, "out");
+  TORCH_CHECK(arena.dim() == 6 && arena.is_contiguous() && arena.size(5) == 128 && arena.size(4) == 16,
+              "arena layout");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2 && block_tables.stride(1) == 1,
+              "block_tables int32 [seqs, max_blocks]");
+  TORCH_CHECK(seq_lens.scalar_type() == at::kInt, "seq_lens int32");
+  PagedAttnArgs p;
+  p.q = bf(q);
+  p.q_stride = q.stride(0);
+  p.out = bfm(out);
+  p.out_stride = out.stride(0);
+  p.arena = bf(arena);
+  p.num_blocks = arena.size(0);
+  p.num_layers = static_cast<int>(arena.size(1));
+  p.layer = static_cast<int>(layer);
+  TORCH_CHECK(arena.size(3) == n_kv_heads, "kv heads mismatch");
+  p.n_q_heads = static_cast<int>(n_q_heads);
+  p.n_kv_heads = static_cast<int>(n_kv_heads);
+  p.block_tables = block_tables.data_ptr<int>();
+  p.bt_stride = static_cast<int>(block_tables.stride(0));
+  p.seq_lens = seq_lens.data_ptr<int>();
+  p.num_seqs = static_cast<int>(seq_lens.numel());
+  p.scale = static_cast<float>(scale);
+  p.status = status_ptr(status);
+  return p;
+}
+
+void paged_decode(const at::Tensor& q, at::Tensor& out, const at::Tensor& arena, int64_t layer,
+                  const at::Tensor& block_tables, const at::Tensor& seq_lens, int64_t n_q_heads, int64_t n_kv_heads,
+                  double scale, int64_t splits, c10::optional<at::Tensor> ws_o, c10::optional<at::Tensor> ws_ml,
+                  c10::optional<at::Tensor> status) {
+  PagedAttnArgs p = attn_args(q, out, arena, layer, block_tables, seq_lens, n_q_heads, n_kv_heads, scale, status);
+  TORCH_CHECK(q.size(0) >= p.num_seqs, "one query row per sequence");
+  p.splits = static_cast<int>(splits);
+  if (splits > 1) {
+    TORCH_CHECK(ws_o.has_value() && ws_ml.has_value(), "split-KV needs workspaces");
+    const int64_t G = n_q_heads / n_kv_heads;
+    TORCH_CHECK(ws_o->scalar_type() == at::kFloat && ws_o->numel() >= p.num_seqs * n_kv_heads * splits * G * 128,
+                "ws_o too small");
+    TORCH_CHECK(ws_ml->scalar_type() == at::kFloat && ws_ml->numel() >= p.num_seqs * n_kv_heads * splits * G * 2,
+                "ws_ml too small");
+    p.ws_o = ws_o->data_ptr<float>();
+    p.ws_ml = ws_ml->data_ptr<float>();
+  }
+  LAKEB_CHECK_RC(lakeb::paged_decode(p, cur_stream()), "paged_decode");
+}
+
+int64_t decode_splits(int64_t num_seqs, int64_t n_kv_heads, int64_t max_blocks) {
+  return lakeb::paged_decode_splits(static_cast<int>(num_seqs), static_cast<int>(n_kv_heads),
+                                    static_cast<int>(max_blocks));
+}
+
+void paged_prefill(const at::Tensor& q, at::Tensor& out, const at::Tensor& arena, int64_t layer,
+                   const at::Tensor& block_tables, const at::Tensor& seq_lens, const at::Tensor& tiles,
+                   int64_t n_q_heads, int64_t n_kv_heads, double scale, c10::optional<at::Tensor> status) {
+  PagedAttnArgs p = attn_args(q, out, arena, layer, block_tables, seq_lens, n_q_heads, n_kv_heads, scale, status);
+  TORCH_CHECK(tiles.scalar_type() == at::kInt && tiles.dim() == 2 && tiles.size(1) == 4 && tiles.is_contiguous(),
+              "tiles int32 [n, 4]");
+  p.tiles = reinterpret_cast<const int4*>(tiles.data_ptr<int>());
+  p.num_tiles = static_cast<int>(tiles.size(0));
+  LAKEB_CHECK_RC(lakeb::paged_prefill(p, cur_stream()), "paged_prefill");
+}
+
+void rmsnorm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, double eps) {
+  check_bf16_2d(x, "x");
+  check_bf16_2d(out, "out");
+  TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.numel() == x.size(1), "w");
+  LAKEB_CHECK_RC(lakeb::rmsnorm_bf16(bf(x), x.stride(0), bf(w), bfm(out), out.stride(0), static_cast<int>(x.size(0)),
+                                     static_cast<int>(x.size(1)), static_cast<float>(eps), cur_stream()),
+                 "rmsnorm");
+}
+
+void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out, c10::optional<at::Tensor> status) {
+  TORCH_CHECK(ids.scalar_type() == at::kInt && ids.is_contiguous(), "ids int32");
+  check_bf16_2d(table, "table");
+  check_bf16_2d(out, "out");
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && out.size(1) == table.size(1), "shapes");
+  LAKEB_CHECK_RC(lakeb::embedding_bf16(ids.data_ptr<int>(), bf(table), bfm(out), static_cast<int>(ids.numel()),
+                                       static_cast<int>(table.size(1)), static_cast<int>(table.size(0)),
+                                       status_ptr(status), cur_stream()),
+                 "embedding");
+}
+
+void argmax(const at::Tensor& logits, c10::optional<at::Tensor> bitmask, at::Tensor& out) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "logits fp32 2-D");
+  TORCH_CHECK(out.scalar_type() == at::kInt && out.numel() >= logits.size(0), "out int32");
+  const uint32_t* bm = nullptr;
+  int words = 0;
+  if (bitmask.has_value()) {
+    bm = reinterpret_cast<const uint32_t*>(bitmask->data_ptr<int>());
+    words = static_cast<int>(bitmask->size(1));
+  }
+  LAKEB_CHECK_RC(lakeb::argmax_f32(logits.data_ptr<float>(), logits.stride(0), static_cast<int>(logits.size(0)),
+                                   static_cast<int>(logits.size(1)), bm, words, out.data_ptr<int>(), cur_stream()),
+                 "argmax");
+}
+
+void unpack_argmax(const at::Tensor& keys, at::Tensor& out, int64_t n) {
+  TORCH_CHECK(keys.scalar_type() == at::kLong && out.scalar_type() == at::kInt, "dtypes");
+  LAKEB_CHECK_RC(lakeb::unpack_argmax(reinterpret_cast<const unsigned long long*>(keys.data_ptr<int64_t>()),
+                                      out.data_ptr<int>(), static_cast<int>(n), cur_stream()),
+                 "unpack_argmax");
+}
+
+void apply_bitmask(at::Tensor& logits, const at::Tensor& bitmask) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "logits");
+  TORCH_CHECK(bitmask.scalar_type() == at::kInt && bitmask.dim() == 2, "bitmask");
+  LAKEB_CHECK_RC(lakeb::apply_bitmask_f32(logits.data_ptr<float>(), logits.stride(0), static_cast<int>(logits.size(0)),
+                                          static_cast<int>(logits.size(1)),
+                                          reinterpret_cast<const uint32_t*>(bitmask.data_ptr<int>()),
+                                          static_cast<int>(bitmask.size(1)), cur_stream()),
+                 "apply_bitmask");
+}
+
+void chain_reject(const at::Tensor& draft, const at::Tensor& draft_off, const at::Tensor& target,
+                  const at::Tensor& target_off, at::Tensor& out, at::Tensor& out_len) {
+  for (auto* t : {&draft, &draft_off, &target, &target_off})
+    TORCH_CHECK(t->scalar_type() == at::kInt && t->is_contiguous(), "int32 inputs");
+  const int nreq = static_cast<int>(draft_off.numel() - 1);
+  LAKEB_CHECK_RC(lakeb::chain_reject(draft.data_ptr<int>(), draft_off.data_ptr<int>(), target.data_ptr<int>(),
+                                     target_off.data_ptr<int>(), out.data_ptr<int>(), out_len.data_ptr<int>(),
+                                     static_cast<int>(out.stride(0)), nreq, cur_stream()),
+                 "chain_reject");
+}
+
+// Copy pages between two page-major buffers (either may be a peer GPU's buffer).
+void page_copy(const at::Tensor& src, at::Tensor& dst, const at::Tensor& src_ids, const at::Tensor& dst_ids,
+               int64_t page_bytes, int64_t sub_off, int64_t sub_bytes) {
+  TORCH_CHECK(src_ids.scalar_type() == at::kLong && dst_ids.scalar_type() == at::kLong, "ids int64");
+  TORCH_CHECK(src_ids.numel() == dst_ids.numel(), "id count mismatch");
+  LAKEB_CHECK_RC(lakeb::page_copy(src.data_ptr(), dst.data_ptr(), src_ids.data_ptr<int64_t>(),
+                                  dst_ids.data_ptr<int64_t>(), static_cast<int>(src_ids.numel()), page_bytes,
+                                  sub_off, sub_bytes, cur_stream()),
+                 "page_copy");
+}
+
+// Same as page_copy but the destination is given as a raw device address
+// (an IPC-mapped peer buffer that has no tensor of its own in this process).
+void page_copy_to_ptr(const at::Tensor& src, int64_t dst_ptr, const at::Tensor& src_ids, const at::Tensor& dst_ids,
+                      int64_t page_bytes, int64_t sub_off, int64_t sub_bytes) {
+  TORCH_CHECK(src_ids.scalar_type() == at::kLong && dst_ids.scalar_type() == at::kLong, "ids int64");
+  LAKEB_CHECK_RC(lakeb::page_copy(src.data_ptr(), reinterpret_cast<void*>(dst_ptr), src_ids.data_ptr<int64_t>(),
+                                  dst_ids.data_ptr<int64_t>(), static_cast<int>(src_ids.numel()), page_bytes,
+                                  sub_off, sub_bytes, cur_stream()),
+                 "page_copy_to_ptr");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_C, m) {
+  m.doc() = "lake_b200 sm_100a kernels";
+  namespace py = pybind11;
+  m.def("linear", &linear, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("status") = py::none(),
+        py::arg("max_ctas") = 0);
+  m.def("linear_residual", &linear_residual, py::arg("a"), py::arg("w"), py::arg("residual"), py::arg("out"),
+        py::arg("status") = py::none());
+  m.def("linear_swiglu", &linear_swiglu, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("status") = py::none());
+  m.def("linear_qkv", &linear_qkv, py::arg("a"), py::arg("w"), py::arg("q_out"), py::arg("rope_cs"),
+        py::arg("positions"), py::arg("slots"), py::arg("arena"), py::arg("layer"), py::arg("n_q_heads"),
+        py::arg("n_kv_heads"), py::arg("peer_arena") = py::none(), py::arg("peer_slots") = py::none(),
+        py::arg("status") = py::none());
+  m.def("linear_argmax", &linear_argmax, py::arg("a"), py::arg("w"), py::arg("amax"), py::arg("bitmask") = py::none(),
+        py::arg("status") = py::none());
+  m.def("paged_decode", &paged_decode, py::arg("q"), py::arg("out"), py::arg("arena"), py::arg("layer"),
+        py::arg("block_tables"), py::arg("seq_lens"), py::arg("n_q_heads"), py::arg("n_kv_heads"), py::arg("scale"),
+        py::arg("splits") = 1, py::arg("ws_o") = py::none(), py::arg("ws_ml") = py::none(),
+        py::arg("status") = py::none());
+  m.def("decode_splits", &decode_splits);
+  m.def("paged_prefill", &paged_prefill, py::arg("q"), py::arg("out"), py::arg("arena"), py::arg("layer"),
+        py::arg("block_tables"), py::arg("seq_lens"), py::arg("tiles"), py::arg("n_q_heads"), py::arg("n_kv_heads"),
+        py::arg("scale"), py::arg("status") = py::none());
+  m.def("rmsnorm", &rmsnorm);
+  m.def("embedding", &embedding, py::arg("ids"), py::arg("table"), py::arg("out"), py::arg("status") = py::none());
+  m.def("argmax", &argmax);
+  m.def("unpack_argmax", &unpack_argmax);
+  m.def("apply_bitmask", &apply_bitmask);
+  m.def("chain_reject", &chain_reject);
+  m.def("page_copy", &page_copy);
+  m.def("page_copy_to_ptr", &page_copy_to_ptr);
+}

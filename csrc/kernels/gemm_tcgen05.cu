@@ -1,0 +1,389 @@
+// Persistent bf16 GEMM for sm_100a: TMA -> shared memory (128-byte swizzle),
+// tcgen05.mma with fp32 accumulators in tensor memory, warp-specialised.
+//
+//   warp 0      : TMA producer (one elected lane)
+//   warp 1      : TMEM allocator + MMA issuer (one elected lane)
+//   warps 2..5  : epilogue (tcgen05.ld -> registers -> fused op -> global)
+//
+// The two accumulator buffers in TMEM let the epilogue of tile t overlap the
+// main loop of tile t+1. Epilogues are fused per call site of the transformer:
+// plain store, residual add (o_proj / down_proj), SwiGLU (gate_up), the QKV
+// projection with RoPE and the paged-KV write (local arena and, for
+// prefill->decode disaggregation, the decode GPU's arena through P2P stores),
+// and a greedy-argmax over the vocabulary (lm_head) that never materialises
+// logits.
+//
+// Reference parity: replaces the nn.Linear shells of the reference model
+// (python/lake/engine/model_executor/models/qwen/qwen3.py:100-113,133-147,230-240),
+// which never execute there.
+#include "common.cuh"
+#include "lakeb_kernels.h"
+#include "tma_host.h"
+
+namespace lakeb {
+namespace {
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int kThreads = 192;
+
+template <int BN, int STAGES>
+struct GemmSmem {
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  // full[S], empty[S], tmem_full[2], tmem_empty[2], tmem slot, abort flag
+  static constexpr int kBytes = kBarOffset + (2 * STAGES + 4) * 8 + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+};
+
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
+    u.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
+    u.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
+    u.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
+    d[i] = u;
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v) {
+  const uint4* s = reinterpret_cast<const uint4*>(src);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint4 u = s[i];
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f = __bfloat1622float2(h[j]);
+      v[8 * i + 2 * j] = f.x;
+      v[8 * i + 2 * j + 1] = f.y;
+    }
+  }
+}
+
+__device__ __forceinline__ __nv_bfloat16* kv_ptr(const KVArenaView& kv, int64_t slot, int head, int which) {
+  const int64_t blk = slot / kv.block_size;
+  const int64_t off = slot - blk * kv.block_size;
+  return kv.base + blk * kv.block_stride + kv.layer_offset + which * kv.kv_stride + head * kv.head_stride +
+         off * 128;
+}
+
+template <int BN, int STAGES, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const GemmArgs p) {
+  using S = GemmSmem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* tmem_empty = tmem_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const int num_m = (p.M + kBM - 1) / kBM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + kBK - 1) / kBK;
+  constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tmem_full[a], 1);
+      mbar_init(&tmem_empty[a], 128);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m_blk = tile % num_m;
+        const int n_blk = tile / num_m;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + stage * S::kStageBytes;
+          uint8_t* sb = sa + S::kABytes;
+          mbar_expect_tx(&full[stage], S::kStageBytes);
+          tma_load_2d(sa, &tmA, &full[stage], kb * kBK, m_blk * kBM);
+          tma_load_2d(sb, &tmB, &full[stage], kb * kBK, n_blk * BN);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      if (!ok) {
+        // Drain loads already in flight before the CTA's shared memory is released.
+        for (int s = 0; s < STAGES; ++s) mbar_wait(&full[s], 0, nullptr, nullptr, 50000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN);
+      uint32_t stage = 0, phase = 0;
+      bool ok = true;
+      int t = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
+        const int acc = t & 1;
+        const uint32_t acc_phase = (t >> 1) & 1;
+        if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
+          const uint32_t sb = sa + S::kABytes;
+          const uint64_t ad = umma_desc_sw128(sa);
+          const uint64_t bd = umma_desc_sw128(sb);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            // advance 16 elements (32 bytes) along K inside the swizzle row
+            umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        umma_commit(&tmem_full[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int row_in_tile = q * 32 + lane;
+    int t = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
+      const int m_blk = tile % num_m;
+      const int n_blk = tile / num_m;
+      const int acc = t & 1;
+      if (!mbar_wait(&tmem_full[acc], (t >> 1) & 1, abort_flag, p.status)) break;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
+      const int row = m_blk * kBM + row_in_tile;
+      const bool row_ok = row < p.M;
+
+      if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = n_blk * BN + c * 32;
+          if (row_ok && col0 < p.N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            if constexpr (EPI == kEpiStoreF32) {
+              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + row * p.ldc + col0);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+            } else {
+              if constexpr (EPI == kEpiResidual) {
+                float rv[32];
+                load_bf16x32(p.R + row * p.ldr + col0, rv);
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += rv[j];
+              }
+              store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
+            }
+          }
+        }
+      } else if constexpr (EPI == kEpiSwiGLU) {
+        constexpr int H = BN / 2;
+#pragma unroll 1
+        for (int c = 0; c < H / 32; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld32(tbase + c * 32, g);
+          tmem_ld32(tbase + H + c * 32, u);
+          tmem_ld_wait();
+          const int col0 = n_blk * H + c * 32;
+          if (row_ok) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
+            store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
+          }
+        }
+      } else if constexpr (EPI == kEpiQKV) {
+        static_assert(BN == 128, "QKV epilogue maps one 128-wide head per tile");
+        const int head = n_blk;
+        const bool is_q = head < p.n_q_heads;
+        const bool is_k = !is_q && head < p.n_q_heads + p.n_kv_heads;
+        int pos = 0;
+        int64_t slot = -1, pslot = -1;
+        if (row_ok) {
+          pos = p.positions[row];
+          if (!is_q) {
+            slot = p.slots ? p.slots[row] : -1;
+            if (p.peer_kv.base && p.peer_slots) pslot = p.peer_slots[row];
+          }
+        }
+        if (is_q || is_k) {
+          const int kvh = head - p.n_q_heads;
+#pragma unroll 1
+          for (int half = 0; half < 2; ++half) {
+            uint32_t r1[32], r2[32];
+            tmem_ld32(tbase + half * 32, r1);
+            tmem_ld32(tbase + 64 + half * 32, r2);
+            tmem_ld_wait();
+            if (row_ok) {
+              float o1[32], o2[32];
+              const float2* cs = p.rope_cs + static_cast<int64_t>(pos) * 64 + half * 32;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float2 c = cs[j];
+                const float x1 = __uint_as_float(r1[j]);
+                const float x2 = __uint_as_float(r2[j]);
+                o1[j] = x1 * c.x - x2 * c.y;
+                o2[j] = x2 * c.x + x1 * c.y;
+              }
+              if (is_q) {
+                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + head * 128;
+                store_bf16x32(dst + half * 32, o1);
+                store_bf16x32(dst + 64 + half * 32, o2);
+              } else {
+                if (slot >= 0) {
+                  __nv_bfloat16* dst = kv_ptr(p.kv, slot, kvh, 0);
+                  store_bf16x32(dst + half * 32, o1);
+                  store_bf16x32(dst + 64 + half * 32, o2);
+                }
+                if (pslot >= 0) {
+                  __nv_bfloat16* dst = kv_ptr(p.peer_kv, pslot, kvh, 0);
+                  store_bf16x32(dst + half * 32, o1);
+                  store_bf16x32(dst + 64 + half * 32, o2);
+                }
+              }
+            }
+          }
+        } else {
+          const int kvh = head - p.n_q_heads - p.n_kv_heads;
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c * 32, r);
+            tmem_ld_wait();
+            if (row_ok) {
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+              if (slot >= 0) store_bf16x32(kv_ptr(p.kv, slot, kvh, 1) + c * 32, v);
+              if (pslot >= 0) store_bf16x32(kv_ptr(p.peer_kv, pslot, kvh, 1) + c * 32, v);
+            }
+          }
+        }
+      } else if constexpr (EPI == kEpiArgmax) {
+        unsigned long long best = 0ull;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = n_blk * BN + c * 32;
+          if (row_ok && col0 < p.N) {
+            uint32_t allow = 0xFFFFFFFFu;
+            if (p.bitmask) allow = p.bitmask[static_cast<int64_t>(row) * p.bitmask_words + (col0 >> 5)];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if ((allow >> j) & 1u) {
+                const unsigned long long key =
+                    (static_cast<unsigned long long>(float_order_key(__uint_as_float(r[j]))) << 32) |
+                    static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col0 + j));
+                best = key > best ? key : best;
+              }
+            }
+          }
+        }
+        if (row_ok && best) atomicMax(p.amax + row, best);
+      }
+      tc_fence_before();
+      mbar_arrive(&tmem_empty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+template <int BN, int STAGES, int EPI>
+int launch(const GemmArgs& a, cudaStream_t stream) {
+  using S = GemmSmem<BN, STAGES>;
+  CUtensorMap ma, mb;
+  if (!make_bf16_map(&ma, a.A, a.M, a.K, a.lda, kBM)) return -10;
+  if (!make_bf16_map(&mb, a.B, a.N, a.K, a.ldb, BN)) return -11;
+  auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
+  int grid = a.max_ctas > 0 ? a.max_ctas : num_sms();
+  if (grid > tiles) grid = tiles;
+  kern<<<grid, kThreads, S::kAlloc, stream>>>(ma, mb, a);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
+  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
+  if ((a.K % 8) || (a.lda % 8) || (a.ldb % 8) || (a.N % 32)) return -1;
+  if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) return -2;
+  switch (epi) {
+    case kEpiStoreBf16:
+      return launch<256, 4, kEpiStoreBf16>(a, stream);
+    case kEpiResidual:
+      return launch<256, 4, kEpiResidual>(a, stream);
+    case kEpiSwiGLU:
+      return launch<256, 4, kEpiSwiGLU>(a, stream);
+    case kEpiQKV:
+      if (a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128) return -3;
+      return launch<128, 6, kEpiQKV>(a, stream);
+    case kEpiArgmax:
+      return launch<256, 4, kEpiArgmax>(a, stream);
+    case kEpiStoreF32:
+      return launch<256, 4, kEpiStoreF32>(a, stream);
+    default:
+      return -4;
+  }
+}
+
+}  // namespace lakeb

@@ -1,0 +1,16 @@
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace lakeb {
+
+// Tensor map for a row-major bf16 matrix [rows, cols] (leading dimension `ld`
+// elements) with boxes of box_rows x box_cols, 128-byte swizzle, zero fill
+// outside the bounds. Cached per (pointer, shape, device).
+bool make_bf16_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                   int box_cols = 64);
+
+int num_sms();
+
+}  // namespace lakeb

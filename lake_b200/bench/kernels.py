@@ -1,0 +1,116 @@
+"""Kernel microbenchmarks on the current GPU: each sm_100a kernel against its
+library counterpart (cuBLAS via torch.matmul, SDPA), timed with CUDA events
+after warm-up, L2 flushed between iterations.
+
+    python -m lake_b200.bench.kernels [--only gemm,decode,prefill,norm]
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+
+import torch
+
+from .. import ops
+from ..oracle import ops_ref as ref
+
+BF = torch.bfloat16
+
+
+class Timer:
+    def __init__(self, iters=20, warmup=5):
+        self.iters, self.warmup = iters, warmup
+        self.flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
+
+    def __call__(self, fn):
+        for _ in range(self.warmup):
+            fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(self.iters):
+            self.flush.zero_()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            torch.cuda.synchronize()
+            times.append(s.elapsed_time(e))
+        times.sort()
+        return times[len(times) // 2]
+
+
+def bench_gemm(t: Timer, out: list):
+    shapes = [(8192, 6144, 4096, "qkv"), (8192, 4096, 4096, "o_proj"), (8192, 28672, 4096, "gate_up"),
+              (8192, 4096, 14336, "down"), (256, 6144, 4096, "decode_qkv"), (256, 28672, 4096, "decode_gate_up"),
+              (256, 128256, 4096, "decode_lm_head")]
+    for m, n, k, name in shapes:
+        a = torch.randn(m, k, device="cuda").to(BF)
+        w = (torch.randn(n, k, device="cuda") / math.sqrt(k)).to(BF)
+        c = torch.empty(m, n, device="cuda", dtype=BF)
+        ms = t(lambda: ops.linear(a, w, out=c))
+        ms_ref = t(lambda: torch.matmul(a, w.t(), out=c))
+        fl = 2 * m * n * k
+        byt = (m * k + n * k + m * n) * 2
+        out.append(dict(kernel="gemm_bf16", shape=name, m=m, n=n, k=k, ms=ms, tflops=fl / ms / 1e9,
+                        gbs=byt / ms / 1e6, cublas_ms=ms_ref, cublas_tflops=fl / ms_ref / 1e9))
+
+
+def bench_decode(t: Timer, out: list):
+    for nseq, ctx in [(256, 2304), (64, 4096), (8, 8192)]:
+        hq, hkv = 32, 8
+        nb = (ctx + 15) // 16
+        arena = torch.randn(nseq * nb + 1, 1, 2, hkv, 16, 128, device="cuda").to(BF)
+        bt = torch.randperm(nseq * nb, device="cuda").view(nseq, nb).to(torch.int32)
+        sl = torch.full((nseq,), ctx, dtype=torch.int32, device="cuda")
+        q = torch.randn(nseq, hq * 128, device="cuda").to(BF)
+        o = torch.empty_like(q)
+        ms = t(lambda: ops.paged_decode_attention(q, arena, 0, bt, sl, hq, hkv, 0.088, out=o))
+        byt = nseq * ctx * hkv * 128 * 2 * 2
+        out.append(dict(kernel="paged_decode", nseq=nseq, ctx=ctx, ms=ms, gbs=byt / ms / 1e6))
+
+
+def bench_prefill(t: Timer, out: list):
+    for nseq, ctx in [(4, 2048), (1, 8192)]:
+        hq, hkv = 32, 8
+        nb = (ctx + 15) // 16
+        arena = torch.randn(nseq * nb + 1, 1, 2, hkv, 16, 128, device="cuda").to(BF)
+        bt = torch.randperm(nseq * nb, device="cuda").view(nseq, nb).to(torch.int32)
+        sl = torch.full((nseq,), ctx, dtype=torch.int32, device="cuda")
+        qs = [i * ctx for i in range(nseq + 1)]
+        tiles = ops.build_prefill_tiles(qs, [0] * nseq, device="cuda")
+        q = torch.randn(nseq * ctx, hq * 128, device="cuda").to(BF)
+        o = torch.empty_like(q)
+        qs_t = torch.tensor(qs, dtype=torch.int32, device="cuda")
+        ms = t(lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv, 0.088, out=o))
+        qd = q.view(nseq, ctx, hq, 128).transpose(1, 2)
+        kd = torch.randn(nseq, hq, ctx, 128, device="cuda").to(BF)
+        ms_ref = t(lambda: torch.nn.functional.scaled_dot_product_attention(qd, kd, kd, is_causal=True))
+        fl = nseq * hq * ctx * ctx * 128 * 2  # causal: half of 4*T^2*D
+        out.append(dict(kernel="paged_prefill", nseq=nseq, ctx=ctx, ms=ms, tflops=fl / ms / 1e9, sdpa_ms=ms_ref,
+                        sdpa_tflops=fl / ms_ref / 1e9))
+
+
+def bench_norm(t: Timer, out: list):
+    x = torch.randn(8192, 4096, device="cuda").to(BF)
+    w = torch.rand(4096, device="cuda").to(BF)
+    o = torch.empty_like(x)
+    ms = t(lambda: ops.rms_norm(x, w, 1e-5, out=o))
+    out.append(dict(kernel="rmsnorm", rows=8192, dim=4096, ms=ms, gbs=2 * x.numel() * 2 / ms / 1e6))
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default="gemm,decode,prefill,norm")
+    ap.add_argument("--iters", type=int, default=20)
+    args = ap.parse_args(argv)
+    t = Timer(args.iters)
+    res: list = []
+    for name in args.only.split(","):
+        {"gemm": bench_gemm, "decode": bench_decode, "prefill": bench_prefill, "norm": bench_norm}[name](t, res)
+    for r in res:
+        print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,35 @@
+"""Loader for the native kernel module ``lake_b200._C``.
+
+CUDA tensors always go to the native kernels; if the extension is missing the
+call raises instead of falling back, so a GPU run can never silently use a
+PyTorch path. CPU tensors use the fp32 reference implementations in
+:mod:`lake_b200.oracle.ops_ref` (the correctness oracle).
+"""
+from __future__ import annotations
+
+import importlib
+
+_C = None
+_ERR: Exception | None = None
+
+
+def native():
+    """Return the compiled module or raise with the build instruction."""
+    global _C, _ERR
+    if _C is None:
+        try:
+            _C = importlib.import_module("lake_b200._C")
+        except ImportError as e:  # pragma: no cover - depends on the build
+            _ERR = e
+            raise RuntimeError(
+                "lake_b200._C is not built (python -m lake_b200._build); CUDA ops have no fallback"
+            ) from e
+    return _C
+
+
+def available() -> bool:
+    try:
+        native()
+        return True
+    except RuntimeError:
+        return False

@@ -1,0 +1,194 @@
+"""Numerics of every sm_100a kernel against the fp32 PyTorch oracle (ops_ref)."""
+import math
+
+import pytest
+import torch
+
+from lake_b200 import ops
+from lake_b200.oracle import ops_ref as ref
+
+pytestmark = pytest.mark.gpu
+
+BF = torch.bfloat16
+
+
+def _close(out, want, tol=2e-2):
+    out = out.float()
+    want = want.float()
+    err = (out - want).abs().max().item()
+    scale = want.abs().max().item() + 1e-6
+    assert err <= tol * scale + 1e-3, f"max err {err} vs scale {scale}"
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 256, 64), (37, 512, 200), (128, 256, 4096), (300, 4096, 4096),
+                                   (1024, 1024, 1024), (4096, 6144, 4096)])
+def test_linear_bf16(cuda_dev, m, n, k):
+    g = torch.Generator(device=cuda_dev).manual_seed(0)
+    a = torch.randn(m, k, device=cuda_dev, generator=g).to(BF)
+    w = (torch.randn(n, k, device=cuda_dev, generator=g) / math.sqrt(k)).to(BF)
+    out = ops.linear(a, w)
+    torch.cuda.synchronize()
+    _close(out, ref.linear(a, w))
+    ops.core.check_status()
+
+
+def test_linear_f32_out(cuda_dev):
+    a = torch.randn(200, 512, device=cuda_dev).to(BF)
+    w = (torch.randn(768, 512, device=cuda_dev) / 20).to(BF)
+    out = ops.linear(a, w, out_dtype=torch.float32)
+    _close(out, ref.linear(a, w), 1e-2)
+
+
+def test_linear_residual_inplace(cuda_dev):
+    a = torch.randn(300, 1024, device=cuda_dev).to(BF)
+    w = (torch.randn(512, 1024, device=cuda_dev) / 32).to(BF)
+    h = torch.randn(300, 512, device=cuda_dev).to(BF)
+    want = h.float() + ref.linear(a, w)
+    ops.linear_residual(a, w, h, out=h)
+    _close(h, want)
+
+
+def test_linear_swiglu(cuda_dev):
+    m, hdim, inter = 257, 512, 768
+    a = torch.randn(m, hdim, device=cuda_dev).to(BF)
+    gate = (torch.randn(inter, hdim, device=cuda_dev) / 20).to(BF)
+    up = (torch.randn(inter, hdim, device=cuda_dev) / 20).to(BF)
+    w = ref.interleave_gate_up(gate, up)
+    out = ops.linear_swiglu(a, w)
+    want = torch.nn.functional.silu(ref.linear(a, gate)) * ref.linear(a, up)
+    _close(out, want)
+
+
+def _arena(dev, blocks=64, layers=2, hkv=2):
+    return torch.zeros(blocks, layers, 2, hkv, 16, 128, dtype=BF, device=dev)
+
+
+def test_linear_qkv_rope_kv_write(cuda_dev):
+    t, hid, hq, hkv = 70, 512, 4, 2
+    a = torch.randn(t, hid, device=cuda_dev).to(BF)
+    w = (torch.randn((hq + 2 * hkv) * 128, hid, device=cuda_dev) / 20).to(BF)
+    cs = ref.rope_cache(4096, 500000.0, device=cuda_dev)
+    pos = torch.randint(0, 4000, (t,), device=cuda_dev, dtype=torch.int32)
+    slots = torch.randperm(64 * 16, device=cuda_dev)[:t].to(torch.int64)
+    slots[5] = -1
+    arena = _arena(cuda_dev)
+    arena_ref = arena.clone()
+    q = torch.empty(t, hq * 128, dtype=BF, device=cuda_dev)
+    ops.linear_qkv(a, w, q, cs, pos, slots, arena, 1, hq, hkv)
+    # recompute the oracle on the GPU tensors for comparison
+    acc = ref.linear(a, w)
+    qq = ref.apply_rope(acc[:, : hq * 128].view(t, hq, 128), pos, cs).reshape(t, -1)
+    kk = ref.apply_rope(acc[:, hq * 128:(hq + hkv) * 128].view(t, hkv, 128), pos, cs)
+    vv = acc[:, (hq + hkv) * 128:].view(t, hkv, 128)
+    ref.write_kv(arena_ref, 1, slots, kk, vv)
+    torch.cuda.synchronize()
+    _close(q, qq)
+    _close(arena, arena_ref)
+
+
+@pytest.mark.parametrize("m,vocab", [(3, 1024), (130, 128256)])
+def test_linear_argmax(cuda_dev, m, vocab):
+    a = torch.randn(m, 512, device=cuda_dev).to(BF)
+    w = (torch.randn(vocab, 512, device=cuda_dev) / 20).to(BF)
+    tok = ops.linear_argmax(a, w)
+    logits = ops.linear(a, w, out_dtype=torch.float32)
+    assert torch.equal(tok.cpu(), logits.argmax(-1).to(torch.int32).cpu())
+    bm = torch.randint(-2**31, 2**31 - 1, (m, (vocab + 31) // 32), device=cuda_dev, dtype=torch.int32)
+    tok2 = ops.linear_argmax(a, w, bitmask=bm)
+    want = ref.greedy(logits, bm)
+    assert torch.equal(tok2.cpu(), want.cpu())
+
+
+def _fill_cache(dev, nseq, lens, hkv, layers=2, layer=1, blocks_per_seq=None):
+    maxb = max((l + 15) // 16 for l in lens)
+    bps = blocks_per_seq or maxb
+    nblocks = nseq * bps + 3
+    arena = (torch.randn(nblocks, layers, 2, hkv, 16, 128, device=dev) * 0.5).to(BF)
+    perm = torch.randperm(nblocks, device=dev)[: nseq * bps].view(nseq, bps).to(torch.int32)
+    return arena, perm
+
+
+@pytest.mark.parametrize("nseq,hq,hkv,lens", [(3, 8, 2, [1, 17, 300]), (64, 32, 8, None), (2, 32, 8, [4096, 2000]),
+                                             (5, 16, 8, [33, 64, 65, 128, 2])])
+def test_paged_decode(cuda_dev, nseq, hq, hkv, lens):
+    if lens is None:
+        lens = torch.randint(1, 700, (nseq,)).tolist()
+    arena, bt = _fill_cache(cuda_dev, nseq, lens, hkv)
+    q = torch.randn(nseq, hq * 128, device=cuda_dev).to(BF)
+    sl = torch.tensor(lens, dtype=torch.int32, device=cuda_dev)
+    scale = 1 / math.sqrt(128)
+    out = ops.paged_decode_attention(q, arena, 1, bt, sl, hq, hkv, scale)
+    qs = torch.arange(nseq + 1, dtype=torch.int32, device=cuda_dev)
+    want = ref.paged_attention(q, arena, 1, bt, sl, qs, sl - 1, hq, hkv, scale)
+    torch.cuda.synchronize()
+    _close(out, want)
+    for splits in (1, 3):
+        out2 = ops.paged_decode_attention(q, arena, 1, bt, sl, hq, hkv, scale, splits=splits)
+        _close(out2, want)
+    ops.core.check_status()
+
+
+@pytest.mark.parametrize("hq,hkv,chunks", [(8, 2, [(0, 100)]), (32, 8, [(0, 2048)]),
+                                           (16, 4, [(64, 37), (0, 1), (500, 200), (16, 64)])])
+def test_paged_prefill(cuda_dev, hq, hkv, chunks):
+    # chunks: (cached prefix length, new query tokens) per sequence
+    lens = [p + n for p, n in chunks]
+    arena, bt = _fill_cache(cuda_dev, len(chunks), lens, hkv)
+    qstart = [0]
+    pos0 = []
+    positions = []
+    for p, n in chunks:
+        qstart.append(qstart[-1] + n)
+        pos0.append(p)
+        positions += list(range(p, p + n))
+    t = qstart[-1]
+    q = torch.randn(t, hq * 128, device=cuda_dev).to(BF)
+    sl = torch.tensor(lens, dtype=torch.int32, device=cuda_dev)
+    tiles = ops.build_prefill_tiles(qstart, pos0, device=cuda_dev)
+    qs_t = torch.tensor(qstart, dtype=torch.int32, device=cuda_dev)
+    pos_t = torch.tensor(positions, dtype=torch.int32, device=cuda_dev)
+    scale = 1 / math.sqrt(128)
+    out = ops.paged_prefill_attention(q, arena, 1, bt, sl, tiles, qs_t, pos_t, hq, hkv, scale)
+    want = ref.paged_attention(q, arena, 1, bt, sl, qs_t, pos_t, hq, hkv, scale)
+    torch.cuda.synchronize()
+    _close(out, want)
+    ops.core.check_status()
+
+
+@pytest.mark.parametrize("rows,dim", [(1, 128), (300, 4096), (17, 8192), (64, 2048)])
+def test_rmsnorm(cuda_dev, rows, dim):
+    x = torch.randn(rows, dim, device=cuda_dev).to(BF)
+    w = torch.rand(dim, device=cuda_dev).to(BF)
+    _close(ops.rms_norm(x, w, 1e-5), ref.rms_norm(x, w, 1e-5))
+
+
+def test_embedding(cuda_dev):
+    table = torch.randn(1000, 512, device=cuda_dev).to(BF)
+    ids = torch.randint(0, 1000, (77,), device=cuda_dev, dtype=torch.int32)
+    assert torch.equal(ops.embedding(ids, table), table[ids.long()])
+
+
+def test_greedy_bitmask_chain(cuda_dev):
+    logits = torch.randn(9, 5000, device=cuda_dev)
+    assert torch.equal(ops.greedy_sample(logits).cpu(), logits.argmax(-1).int().cpu())
+    bm = torch.randint(-2**31, 2**31 - 1, (9, (5000 + 31) // 32), device=cuda_dev, dtype=torch.int32)
+    assert torch.equal(ops.greedy_sample(logits, bm).cpu(), ref.greedy(logits, bm).cpu())
+    l2 = logits.clone()
+    ops.apply_token_bitmask(l2, bm)
+    assert torch.equal(l2, ref.apply_bitmask(logits, bm))
+    draft = torch.tensor([5, 6, 7, 1, 2], dtype=torch.int32, device=cuda_dev)
+    doff = torch.tensor([0, 3, 5], dtype=torch.int32, device=cuda_dev)
+    target = torch.tensor([5, 6, 9, 0, 1, 2, 8], dtype=torch.int32, device=cuda_dev)
+    toff = torch.tensor([0, 4], dtype=torch.int32, device=cuda_dev)
+    out, n = ops.chain_reject_sample(draft, doff, target, toff, 4)
+    assert n.tolist() == [3, 3]
+    assert out[0, :3].tolist() == [5, 6, 9] and out[1, :3].tolist() == [1, 2, 8]
+
+
+def test_page_copy(cuda_dev):
+    src = torch.randn(10, 4096, device=cuda_dev).to(BF)
+    dst = torch.zeros(12, 4096, device=cuda_dev, dtype=BF)
+    si = torch.tensor([3, 7, 1], device=cuda_dev)
+    di = torch.tensor([0, 11, 5], device=cuda_dev)
+    ops.page_copy(src, dst, si, di, 4096 * 2)
+    assert torch.equal(dst[di], src[si])
