@@ -19,10 +19,17 @@ cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 const __nv_bfloat16* bf(const at::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); }
 __nv_bfloat16* bfm(const at::Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
 
+void check_aligned(const at::Tensor& t, const char* name, int64_t bytes = 16) {
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % bytes == 0, name, " must be ", bytes, "-byte aligned");
+}
+
+// Kernels move rows with 16-byte vectors: base 16-byte aligned, row stride a multiple of 8 elements.
 void check_bf16_2d(const at::Tensor& t, const char* name) {
   TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
   TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bf16");
   TORCH_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be 2-D with unit inner stride");
+  check_aligned(t, name);
+  TORCH_CHECK(t.size(0) <= 1 || t.stride(0) % 8 == 0, name, " row stride must be a multiple of 8 elements");
 }
 
 int* status_ptr(const c10::optional<at::Tensor>& st) {
@@ -50,6 +57,7 @@ KVArenaView arena_view(const at::Tensor& arena, int64_t layer) {
   TORCH_CHECK(arena.is_cuda() && arena.scalar_type() == at::kBFloat16 && arena.dim() == 6 && arena.is_contiguous(),
               "arena must be a contiguous bf16 [blocks, layers, 2, kv_heads, block, 128] tensor");
   TORCH_CHECK(arena.size(5) == 128, "head_dim must be 128");
+  check_aligned(arena, "arena");
   KVArenaView v;
   v.base = bfm(arena);
   v.block_stride = arena.stride(0);
@@ -65,6 +73,8 @@ void linear(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c10::opti
             int64_t max_ctas) {
   GemmArgs g = base_args(a, w);
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) == a.size(0) && out.size(1) == w.size(0), "out shape");
+  check_aligned(out, "out");
+  TORCH_CHECK(out.size(0) <= 1 || out.stride(0) % 8 == 0, "out row stride must be a multiple of 8 elements");
   g.C = out.data_ptr();
   g.ldc = out.stride(0);
   g.status = status_ptr(status);
@@ -137,6 +147,7 @@ void linear_argmax(const at::Tensor& a, const at::Tensor& w, at::Tensor& amax, c
                    c10::optional<at::Tensor> status) {
   GemmArgs g = base_args(a, w);
   TORCH_CHECK(amax.scalar_type() == at::kLong && amax.numel() >= a.size(0) && amax.is_contiguous(), "amax int64");
+  check_aligned(amax, "amax", 8);
   amax.zero_();
   g.amax = reinterpret_cast<unsigned long long*>(amax.data_ptr<int64_t>());
   if (bitmask.has_value()) {
@@ -210,6 +221,7 @@ void paged_prefill(const at::Tensor& q, at::Tensor& out, const at::Tensor& arena
   PagedAttnArgs p = attn_args(q, out, arena, layer, block_tables, seq_lens, n_q_heads, n_kv_heads, scale, status);
   TORCH_CHECK(tiles.scalar_type() == at::kInt && tiles.dim() == 2 && tiles.size(1) == 4 && tiles.is_contiguous(),
               "tiles int32 [n, 4]");
+  check_aligned(tiles, "tiles");
   p.tiles = reinterpret_cast<const int4*>(tiles.data_ptr<int>());
   p.num_tiles = static_cast<int>(tiles.size(0));
   LAKEB_CHECK_RC(lakeb::paged_prefill(p, cur_stream()), "paged_prefill");
@@ -219,6 +231,7 @@ void rmsnorm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, double e
   check_bf16_2d(x, "x");
   check_bf16_2d(out, "out");
   TORCH_CHECK(w.scalar_type() == at::kBFloat16 && w.is_contiguous() && w.numel() == x.size(1), "w");
+  check_aligned(w, "w");
   LAKEB_CHECK_RC(lakeb::rmsnorm_bf16(bf(x), x.stride(0), bf(w), bfm(out), out.stride(0), static_cast<int>(x.size(0)),
                                      static_cast<int>(x.size(1)), static_cast<float>(eps), cur_stream()),
                  "rmsnorm");
@@ -282,6 +295,8 @@ void page_copy(const at::Tensor& src, at::Tensor& dst, const at::Tensor& src_ids
                int64_t page_bytes, int64_t sub_off, int64_t sub_bytes) {
   TORCH_CHECK(src_ids.scalar_type() == at::kLong && dst_ids.scalar_type() == at::kLong, "ids int64");
   TORCH_CHECK(src_ids.numel() == dst_ids.numel(), "id count mismatch");
+  check_aligned(src, "src");
+  check_aligned(dst, "dst");
   LAKEB_CHECK_RC(lakeb::page_copy(src.data_ptr(), dst.data_ptr(), src_ids.data_ptr<int64_t>(),
                                   dst_ids.data_ptr<int64_t>(), static_cast<int>(src_ids.numel()), page_bytes,
                                   sub_off, sub_bytes, cur_stream()),
@@ -293,6 +308,8 @@ void page_copy(const at::Tensor& src, at::Tensor& dst, const at::Tensor& src_ids
 void page_copy_to_ptr(const at::Tensor& src, int64_t dst_ptr, const at::Tensor& src_ids, const at::Tensor& dst_ids,
                       int64_t page_bytes, int64_t sub_off, int64_t sub_bytes) {
   TORCH_CHECK(src_ids.scalar_type() == at::kLong && dst_ids.scalar_type() == at::kLong, "ids int64");
+  check_aligned(src, "src");
+  TORCH_CHECK(dst_ptr % 16 == 0, "dst_ptr must be 16-byte aligned");
   LAKEB_CHECK_RC(lakeb::page_copy(src.data_ptr(), reinterpret_cast<void*>(dst_ptr), src_ids.data_ptr<int64_t>(),
                                   dst_ids.data_ptr<int64_t>(), static_cast<int>(src_ids.numel()), page_bytes,
                                   sub_off, sub_bytes, cur_stream()),

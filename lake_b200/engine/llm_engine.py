@@ -1,0 +1,161 @@
+"""Public serving API of one engine instance (one GPU, or the CPU oracle path).
+
+    eng = LLMEngine("llama3-8b", device="cuda")
+    rid = eng.add_request(prompt_token_ids, max_new_tokens=256)
+    while eng.has_unfinished():
+        for out in eng.step():
+            ...
+
+Each ``step()`` schedules a batch, stages its metadata through pinned host
+memory, runs the model on the GPU and reads the sampled tokens back.
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from dataclasses import dataclass, field
+
+import torch
+
+from ..models.config import ModelConfig, get_config
+from ..models.llama import DecoderLM
+from .block_pool import BlockPool
+from .model_runner import ModelRunner
+from .request import Request, RequestStatus, SamplingParams
+from .scheduler import Scheduler, SchedulerConfig, SchedulerOutput
+
+
+@dataclass
+class EngineConfig:
+    model: str | ModelConfig = "llama3-8b"
+    device: str = "cuda"
+    max_running: int = 256
+    max_batched_tokens: int = 8192
+    long_prefill_threshold: int = 0
+    max_model_len: int = 8192
+    num_blocks: int = 0  # 0 = size from free memory
+    kv_mem_fraction: float = 0.90
+    enable_prefix_cache: bool = True
+    use_cuda_graphs: bool = True
+    seed: int = 0
+    block_size: int = 16
+    model_overrides: dict = field(default_factory=dict)
+
+
+@dataclass
+class StepOutput:
+    rid: str
+    new_tokens: list[int]
+    finished: bool
+
+
+def alloc_arena(cfg: ModelConfig, num_blocks: int, device, dtype, block_size: int = 16) -> torch.Tensor:
+    """Page-first KV arena [num_blocks, layers, 2, kv_heads, block_size, head_dim] (zero-filled)."""
+    return torch.zeros(num_blocks, cfg.n_layers, 2, cfg.n_kv_heads, block_size, cfg.head_dim, dtype=dtype,
+                       device=device)
+
+
+def page_bytes(cfg: ModelConfig, block_size: int = 16, elem: int = 2) -> int:
+    return cfg.n_layers * 2 * cfg.n_kv_heads * block_size * cfg.head_dim * elem
+
+
+class LLMEngine:
+    def __init__(self, model: str | ModelConfig = "llama3-8b", device: str = "cuda", **kw):
+        ec = EngineConfig(model=model, device=device, **kw)
+        self.ec = ec
+        cfg = model if isinstance(model, ModelConfig) else get_config(model, **ec.model_overrides)
+        self.cfg = cfg
+        self.device = torch.device(device)
+        dtype = torch.float32 if self.device.type == "cpu" else torch.bfloat16
+        if self.device.type == "cuda":
+            torch.cuda.set_device(self.device)
+        self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed)
+        maxb = (ec.max_model_len + ec.block_size - 1) // ec.block_size
+        max_tokens = ec.max_batched_tokens + ec.max_running
+        num_blocks = ec.num_blocks
+        if not num_blocks:
+            if self.device.type == "cuda":
+                # leave room for activations / graphs: size the runner first, then the arena
+                self.runner = None
+                free, _ = torch.cuda.mem_get_info(self.device)
+                act = max_tokens * (cfg.hidden * 4 + cfg.q_size * 4 + cfg.intermediate * 2) + 2 * 1024**3
+                num_blocks = int((free - act) * ec.kv_mem_fraction) // page_bytes(cfg, ec.block_size)
+            else:
+                num_blocks = 256
+        self.arena = alloc_arena(cfg, num_blocks, self.device, dtype, ec.block_size)
+        self.pool = BlockPool(num_blocks, ec.block_size, ec.enable_prefix_cache)
+        self.scheduler = Scheduler(self.pool, SchedulerConfig(ec.max_running, ec.max_batched_tokens,
+                                                              ec.long_prefill_threshold, ec.max_model_len, maxb))
+        self.runner = ModelRunner(self.model, self.arena, max_tokens, ec.max_running, maxb, ec.use_cuda_graphs,
+                                  ec.block_size)
+        self.requests: dict[str, Request] = {}
+        self._ids = itertools.count()
+        self.step_count = 0
+        self.last_step: SchedulerOutput | None = None
+
+    # ------------------------------------------------------------ requests
+    def add_request(self, prompt: list[int], max_new_tokens: int = 16, rid: str | None = None,
+                    params: SamplingParams | None = None, arrival: float | None = None) -> str:
+        rid = rid or f"req-{next(self._ids)}"
+        p = params or SamplingParams(max_new_tokens=max_new_tokens)
+        req = Request(rid=rid, prompt=list(prompt), params=p)
+        if arrival is not None:
+            req.arrival = arrival
+        self.scheduler.add(req)
+        self.requests[rid] = req
+        return rid
+
+    def abort(self, rid: str) -> bool:
+        return self.scheduler.abort(rid)
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work()
+
+    # ------------------------------------------------------------ stepping
+    def step(self) -> list[StepOutput]:
+        out = self.scheduler.schedule()
+        self.last_step = out
+        if out.is_empty:
+            return []
+        bitmask = self._bitmask(out)
+        sampled = self.runner.execute(out, bitmask)
+        now = time.perf_counter()
+        self.scheduler.update(out, sampled, now)
+        self.step_count += 1
+        res = []
+        it = iter(sampled)
+        for ch in out.chunks:
+            if ch.sample:
+                tok = next(it)
+                res.append(StepOutput(ch.req.rid, [tok], ch.req.finished))
+        return res
+
+    def _bitmask(self, out: SchedulerOutput):
+        rows = [c.req.bitmask for c in out.chunks if c.sample]
+        if not any(r is not None for r in rows):
+            return None
+        words = (self.cfg.vocab + 31) // 32
+        bm = torch.full((len(rows), words), -1, dtype=torch.int32)
+        for i, r in enumerate(rows):
+            if r is not None:
+                bm[i] = torch.as_tensor(r, dtype=torch.int32)
+        return bm.to(self.device, non_blocking=True)
+
+    def generate(self, prompts: list[list[int]], max_new_tokens: int = 16) -> list[list[int]]:
+        rids = [self.add_request(p, max_new_tokens) for p in prompts]
+        while self.has_unfinished():
+            self.step()
+        return [self.requests[r].output for r in rids]
+
+    # ------------------------------------------------------------ metrics
+    def metrics(self) -> dict:
+        fin = [r for r in self.requests.values() if r.status == RequestStatus.FINISHED]
+        ttft = sorted(x for x in (r.ttft() for r in fin) if x is not None)
+        tpot = sorted(x for x in (r.tpot() for r in fin) if x is not None)
+
+        def p50(xs):
+            return xs[len(xs) // 2] if xs else None
+
+        return {"finished": len(fin), "ttft_p50_s": p50(ttft), "tpot_p50_s": p50(tpot),
+                "prefix_hit_blocks": self.pool.stats["hits"], "pool": self.pool.residency(),
+                "h2d_bytes": self.runner.h2d_bytes, "d2h_bytes": self.runner.d2h_bytes}

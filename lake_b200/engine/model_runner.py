@@ -1,0 +1,254 @@
+"""Turns a SchedulerOutput into device tensors, runs the model, returns tokens.
+
+Step metadata (token ids, positions, KV slots, block tables, sequence lengths,
+prefill tiles, sample rows) is packed on the host into pinned staging buffers
+and copied to fixed device buffers with two ``cudaMemcpyAsync`` calls; the
+sampled token ids come back through a pinned buffer. Pure-decode steps replay
+a CUDA graph captured per batch-size bucket (all buffers have fixed
+addresses), mixed prefill/decode steps launch eagerly.
+
+Reference parity: ModelRunner.prepare_inputs / prepare_attn / execute_model
+(python/lake/engine/model_runner.py:182-323) and InputBuffers.materialize
+(python/lake/engine/input_batch.py:81-133), which build the same geometry as
+host lists; AttentionMetadata (python/lake/engine/attention_metadata.py:15-89).
+"""
+from __future__ import annotations
+
+import bisect
+import time
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..models.llama import DecoderLM, ForwardBatch
+from .scheduler import SchedulerOutput
+
+GRAPH_BUCKETS = [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512]
+
+
+class ModelRunner:
+    def __init__(self, model: DecoderLM, arena: torch.Tensor, max_tokens: int, max_seqs: int,
+                 max_blocks_per_seq: int, use_cuda_graphs: bool = True, block_size: int = 16):
+        self.model = model
+        self.arena = arena
+        self.device = model.device
+        self.cuda = self.device.type == "cuda"
+        self.max_tokens = max_tokens
+        self.max_seqs = max_seqs
+        self.maxb = max_blocks_per_seq
+        self.bs = block_size
+        self.vocab_words = (model.cfg.vocab + 31) // 32
+        cfg = model.cfg
+        self.max_splits = 1
+        if self.cuda:
+            self.max_splits = max(ops.decode_splits(n, cfg.n_kv_heads, max_blocks_per_seq)
+                                  for n in range(1, max_seqs + 1))
+        self.ws = model.new_workspace(max_tokens, max_seqs, max_seqs, self.max_splits)
+        # int32 staging: ids | pos | seq_lens | qstart | tiles | block_tables
+        self.max_tiles = max_tokens // 64 + max_seqs
+        self._lay = {}
+        off = 0
+        for name, n in (("ids", max_tokens), ("pos", max_tokens), ("lens", max_seqs), ("qstart", max_seqs + 1),
+                        ("tiles", self.max_tiles * 4), ("bt", max_seqs * max_blocks_per_seq)):
+            self._lay[name] = (off, n)
+            off += (n + 3) // 4 * 4  # keep every region 16-byte aligned (tiles are read as int4)
+        self.n_i32 = off
+        pin = self.cuda
+        self.h_i32 = torch.zeros(off, dtype=torch.int32, pin_memory=pin)
+        self.h_i64 = torch.zeros(2 * max_tokens + max_seqs, dtype=torch.int64, pin_memory=pin)  # slots | rows
+        self.h_tok = torch.zeros(max_seqs, dtype=torch.int32, pin_memory=pin)
+        self.d_i32 = torch.zeros(off, dtype=torch.int32, device=self.device)
+        self.d_i64 = torch.zeros(2 * max_tokens + max_seqs, dtype=torch.int64, device=self.device)
+        self.np_i32 = self.h_i32.numpy()
+        self.np_i64 = self.h_i64.numpy()
+        self.use_graphs = use_cuda_graphs and self.cuda
+        self.graphs: dict[int, tuple] = {}
+        self.graph_launches: dict[int, int] = {}
+        self.stream = torch.cuda.current_stream(self.device) if self.cuda else None
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+        self.last_device_ms = 0.0
+        self.time_device = False
+
+    # ------------------------------------------------------------ views
+    def _v(self, buf, name, n=None, shape=None):
+        off, cap = self._lay[name]
+        t = buf[off: off + (n if n is not None else cap)]
+        return t.reshape(*shape) if shape else t
+
+    def _batch_views(self, t: int, s: int, ntiles: int, nrows: int, nd: int, splits: int,
+                     bitmask=None, peer=None) -> ForwardBatch:
+        d, d64 = self.d_i32, self.d_i64
+        return ForwardBatch(
+            input_ids=self._v(d, "ids", t), positions=self._v(d, "pos", t), slots=d64[:t],
+            block_tables=self._v(d, "bt", s * self.maxb, (s, self.maxb)), seq_lens=self._v(d, "lens", s),
+            n_decode=nd, prefill_tiles=self._v(d, "tiles", ntiles * 4, (ntiles, 4)),
+            query_start=self._v(d, "qstart", s + 1),
+            sample_rows=d64[self.max_tokens: self.max_tokens + nrows], bitmask=bitmask,
+            peer_arena=peer[0] if peer else None, peer_slots=peer[1][:t] if peer else None, decode_splits=splits)
+
+    # ------------------------------------------------------------ host packing
+    def _pack(self, out: SchedulerOutput, pad_decode_to: int = 0):
+        """Fill the pinned staging buffers. Returns (t, s, ntiles, nrows, nd)."""
+        bs, maxb = self.bs, self.maxb
+        ids = self._v(self.np_i32, "ids")
+        pos = self._v(self.np_i32, "pos")
+        lens = self._v(self.np_i32, "lens")
+        qst = self._v(self.np_i32, "qstart")
+        tiles = self._v(self.np_i32, "tiles", shape=(self.max_tiles, 4))
+        bt = self._v(self.np_i32, "bt", shape=(self.max_seqs, maxb))
+        slots = self.np_i64[: self.max_tokens]
+        rows = self.np_i64[self.max_tokens: self.max_tokens + self.max_seqs]
+        row = 0
+        nrows = 0
+        ntiles = 0
+        chunks = out.chunks
+        nd = len(out.decode)
+        s = 0
+        for ch in chunks:
+            req = ch.req
+            n = ch.n
+            p0 = ch.start
+            if n == 1:
+                ids[row] = req.tokens_slice(p0, p0 + 1)[0]
+                pos[row] = p0
+                slots[row] = req.block_ids[p0 // bs] * bs + p0 % bs
+            else:
+                ids[row:row + n] = req.tokens_slice(p0, p0 + n)
+                pr = np.arange(p0, p0 + n, dtype=np.int64)
+                pos[row:row + n] = pr
+                blk = np.asarray(req.block_ids, dtype=np.int64)
+                slots[row:row + n] = blk[pr // bs] * bs + pr % bs
+            nb = len(req.block_ids)
+            bt[s, :nb] = req.block_ids
+            lens[s] = p0 + n
+            qst[s] = row
+            if s >= nd:
+                t0 = row
+                while t0 < row + n:
+                    k = min(64, row + n - t0)
+                    tiles[ntiles] = (s, t0, k, p0 + (t0 - row))
+                    ntiles += 1
+                    t0 += k
+            if ch.sample:
+                rows[nrows] = row + n - 1
+                nrows += 1
+            row += n
+            s += 1
+            if s == nd and pad_decode_to > nd:
+                # padding decode rows for a graph bucket: zero-length sequences, no KV write
+                for j in range(nd, pad_decode_to):
+                    ids[row] = 0
+                    pos[row] = 0
+                    slots[row] = -1
+                    lens[s] = 0
+                    qst[s] = row
+                    rows[nrows] = row
+                    nrows += 1
+                    row += 1
+                    s += 1
+        qst[s] = row
+        return row, s, ntiles, nrows, nd if not pad_decode_to else max(nd, pad_decode_to)
+
+    def _h2d(self, t: int, s: int, nrows: int):
+        # block tables are the largest piece: copy only the used rows
+        off_bt, _ = self._lay["bt"]
+        n32 = off_bt + s * self.maxb
+        self.d_i32[:n32].copy_(self.h_i32[:n32], non_blocking=True)
+        self.d_i64[:t].copy_(self.h_i64[:t], non_blocking=True)
+        self.d_i64[self.max_tokens:self.max_tokens + nrows].copy_(
+            self.h_i64[self.max_tokens:self.max_tokens + nrows], non_blocking=True)
+        self.h2d_bytes += n32 * 4 + (t + nrows) * 8
+
+    # ------------------------------------------------------------ graphs
+    def _bucket(self, nd: int) -> int | None:
+        i = bisect.bisect_left(GRAPH_BUCKETS, nd)
+        if i == len(GRAPH_BUCKETS) or GRAPH_BUCKETS[i] > self.max_seqs:
+            return None
+        return GRAPH_BUCKETS[i]
+
+    def _splits(self, nd: int) -> int:
+        if not self.cuda or nd == 0:
+            return 1
+        return ops.decode_splits(nd, self.model.cfg.n_kv_heads, self.maxb)
+
+    def _get_graph(self, bucket: int):
+        g = self.graphs.get(bucket)
+        if g is not None:
+            return g
+        splits = self._splits(bucket)
+        batch = self._batch_views(bucket, bucket, 0, bucket, bucket, splits)
+        # the captured replay must see valid metadata: zero-length padding sequences
+        self.d_i32.zero_()
+        self.d_i64[:bucket].fill_(-1)
+        self.d_i64[self.max_tokens:self.max_tokens + bucket].copy_(torch.arange(bucket, device=self.device))
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self.model.forward(batch, self.arena, self.ws)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        graph = torch.cuda.CUDAGraph()
+        c0 = ops.core.LAUNCHES[0]
+        with torch.cuda.graph(graph):
+            toks = self.model.forward(batch, self.arena, self.ws)
+        self.graph_launches[bucket] = ops.core.LAUNCHES[0] - c0
+        ops.core.LAUNCHES[0] = c0
+        self.graphs[bucket] = (graph, toks)
+        return self.graphs[bucket]
+
+    def capture_graphs(self, max_bucket: int | None = None) -> None:
+        if not self.use_graphs:
+            return
+        for b in GRAPH_BUCKETS:
+            if b > self.max_seqs or (max_bucket and b > max_bucket):
+                break
+            self._get_graph(b)
+
+    # ------------------------------------------------------------ execute
+    def execute(self, out: SchedulerOutput, bitmask: torch.Tensor | None = None, peer=None) -> list[int]:
+        """Run one step; returns one sampled token per sampling chunk (chunk order)."""
+        if out.is_empty:
+            return []
+        nd = len(out.decode)
+        pure_decode = not out.prefill and bitmask is None and peer is None
+        bucket = self._bucket(nd) if (pure_decode and self.use_graphs) else None
+        t, s, ntiles, nrows, nd_eff = self._pack(out, pad_decode_to=bucket or 0)
+        if not self.cuda:
+            self._copy_cpu(t, s, nrows)
+            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, 1, bitmask, peer)
+            toks = self.model.forward(batch, self.arena, self.ws)
+            return toks[: len([c for c in out.chunks if c.sample])].tolist()
+        graph = None
+        if bucket is not None:
+            graph, toks = self._get_graph(bucket)  # capture (if new) before this step's metadata lands
+        self._h2d(t, s, nrows)
+        ev0 = ev1 = None
+        if self.time_device:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+        if graph is not None:
+            graph.replay()
+            ops.core.LAUNCHES[0] += self.graph_launches[bucket]
+        else:
+            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, self._splits(nd_eff), bitmask, peer)
+            toks = self.model.forward(batch, self.arena, self.ws)
+        if ev1 is not None:
+            ev1.record()
+        nsamp = sum(1 for c in out.chunks if c.sample)
+        self.h_tok[:nsamp].copy_(toks[:nsamp], non_blocking=True)
+        self.d2h_bytes += nsamp * 4
+        torch.cuda.current_stream(self.device).synchronize()
+        if ev1 is not None:
+            self.last_device_ms = ev0.elapsed_time(ev1)
+        return self.h_tok[:nsamp].tolist()
+
+    def _copy_cpu(self, t, s, nrows):
+        self.d_i32.copy_(self.h_i32)
+        self.d_i64.copy_(self.h_i64)
+
+
+def now() -> float:
+    return time.perf_counter()

@@ -1,0 +1,229 @@
+"""Continuous-batching step scheduler.
+
+Each step spends a token budget: every running decode request gets one token
+(decode first), then in-progress prefills and newly admitted requests get
+chunks of their prompt (chunked prefill, optionally capped by
+``long_prefill_threshold``). Admission reuses the longest cached prefix from
+the block pool. When pages run out the most recently admitted request is
+preempted and later recomputed.
+
+Reference parity: the budget / decode-priority / chunked-extend policy of
+python/lake/runtime/node_scheduler.py:396-599 (Pass A decode, Pass B extend)
+and the admission check against max_model_length (:96-103).
+"""
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass, field
+
+from .block_pool import BlockPool, chain_block_hashes
+from .request import Request, RequestStatus
+
+
+@dataclass
+class Chunk:
+    req: Request
+    start: int
+    n: int
+    sample: bool
+
+
+@dataclass
+class SchedulerOutput:
+    step_id: int
+    decode: list[Chunk] = field(default_factory=list)
+    prefill: list[Chunk] = field(default_factory=list)
+    preempted: list[str] = field(default_factory=list)
+
+    @property
+    def num_tokens(self) -> int:
+        return len(self.decode) + sum(c.n for c in self.prefill)
+
+    @property
+    def chunks(self) -> list[Chunk]:
+        return self.decode + self.prefill
+
+    @property
+    def is_empty(self) -> bool:
+        return not self.decode and not self.prefill
+
+
+@dataclass
+class SchedulerConfig:
+    max_running: int = 256
+    max_batched_tokens: int = 8192
+    long_prefill_threshold: int = 0  # 0 = no per-request cap beyond the budget
+    max_model_len: int = 8192
+    max_blocks_per_seq: int = 512
+
+
+class Scheduler:
+    def __init__(self, pool: BlockPool, cfg: SchedulerConfig | None = None):
+        self.pool = pool
+        self.cfg = cfg or SchedulerConfig()
+        self.bs = pool.block_size
+        self.waiting: deque[Request] = deque()
+        self.running: list[Request] = []
+        self.step_id = 0
+        self.finished: list[Request] = []
+
+    # -------------------------------------------------------------- admission
+    def add(self, req: Request) -> None:
+        if len(req.prompt) == 0:
+            raise ValueError("empty prompt")
+        if len(req.prompt) + req.params.max_new_tokens > self.cfg.max_model_len:
+            raise ValueError(f"request {req.rid}: {len(req.prompt)}+{req.params.max_new_tokens} tokens exceed "
+                             f"max_model_len {self.cfg.max_model_len}")
+        req.status = RequestStatus.WAITING
+        self.waiting.append(req)
+
+    def abort(self, rid: str) -> bool:
+        for q in (self.waiting, self.running):
+            for r in list(q):
+                if r.rid == rid:
+                    q.remove(r)
+                    self._release(r)
+                    r.status = RequestStatus.ABORTED
+                    return True
+        return False
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    # -------------------------------------------------------------- helpers
+    def _blocks_needed(self, req: Request, upto: int) -> int:
+        return max(0, (upto + self.bs - 1) // self.bs - len(req.block_ids))
+
+    def _release(self, req: Request) -> None:
+        if req.block_ids:
+            self.pool.release(req.block_ids)
+        req.block_ids = []
+
+    def _preempt_last(self, protect: Request | None = None) -> Request | None:
+        for r in reversed(self.running):
+            if r is protect:
+                continue
+            self.running.remove(r)
+            self._release(r)
+            # recompute from scratch: generated tokens become part of the prompt
+            r.prompt = r.prompt + r.output
+            r.params.max_new_tokens -= len(r.output)
+            r.meta.setdefault("preempted_output", []).extend(r.output)
+            r.output = []
+            r.num_computed = 0
+            r.registered_blocks = 0
+            r.block_hashes = []
+            r.status = RequestStatus.WAITING
+            self.waiting.appendleft(r)
+            return r
+        return None
+
+    def _ensure_blocks(self, req: Request, upto: int, out: SchedulerOutput) -> bool:
+        need = self._blocks_needed(req, upto)
+        while need and not self.pool.can_alloc(need):
+            victim = self._preempt_last(protect=req)
+            if victim is None:
+                return False
+            out.preempted.append(victim.rid)
+            out.decode = [c for c in out.decode if c.req is not victim]
+            out.prefill = [c for c in out.prefill if c.req is not victim]
+        if need:
+            req.block_ids += self.pool.alloc(need)
+        return True
+
+    # -------------------------------------------------------------- schedule
+    def schedule(self) -> SchedulerOutput:
+        out = SchedulerOutput(step_id=self.step_id)
+        self.step_id += 1
+        budget = self.cfg.max_batched_tokens
+        # Pass A: decode
+        for req in list(self.running):
+            if budget <= 0:
+                break
+            if req.is_prefill or req.status != RequestStatus.RUNNING:
+                continue
+            if not self._ensure_blocks(req, req.num_computed + 1, out):
+                continue
+            if req.status != RequestStatus.RUNNING:
+                continue
+            out.decode.append(Chunk(req, req.num_computed, 1, True))
+            budget -= 1
+        # Pass B: continue chunked prefills
+        cap = self.cfg.long_prefill_threshold or budget
+        for req in list(self.running):
+            if budget <= 0:
+                break
+            if not req.is_prefill or req.status != RequestStatus.RUNNING:
+                continue
+            n = min(len(req.prompt) - req.num_computed, budget, cap)
+            if not self._ensure_blocks(req, req.num_computed + n, out):
+                break
+            out.prefill.append(Chunk(req, req.num_computed, n, req.num_computed + n == len(req.prompt)))
+            budget -= n
+        # Pass C: admit
+        while self.waiting and budget > 0 and len(self.running) < self.cfg.max_running:
+            req = self.waiting[0]
+            if not req.block_hashes:
+                req.block_hashes = chain_block_hashes(req.prompt, self.bs, full_only=True)
+            usable = req.block_hashes[: (len(req.prompt) - 1) // self.bs]
+            hit = self.pool.lookup(usable)
+            cached = len(hit) * self.bs
+            n = min(len(req.prompt) - cached, budget, cap)
+            need = (cached + n + self.bs - 1) // self.bs - len(hit)
+            if not self.pool.can_alloc(need):
+                self.pool.release(hit)
+                break
+            self.waiting.popleft()
+            req.block_ids = hit + self.pool.alloc(need)
+            req.num_computed = cached
+            req.num_cached = cached
+            req.registered_blocks = len(hit)
+            req.status = RequestStatus.RUNNING
+            self.running.append(req)
+            out.prefill.append(Chunk(req, cached, n, cached + n == len(req.prompt)))
+            budget -= n
+        return out
+
+    # -------------------------------------------------------------- update
+    def update(self, out: SchedulerOutput, sampled: list[int], now: float) -> list[Request]:
+        """Apply one step's results. `sampled` has one token per sampling chunk, in chunk order."""
+        done = []
+        it = iter(sampled)
+        for ch in out.chunks:
+            req = ch.req
+            if req.status != RequestStatus.RUNNING:
+                if ch.sample:
+                    next(it, None)
+                continue
+            req.num_computed = ch.start + ch.n
+            self._register_full_blocks(req)
+            if ch.sample:
+                tok = next(it)
+                req.output.append(int(tok))
+                if req.first_token_time is None:
+                    req.first_token_time = now
+                req.token_times.append(now)
+                if req.should_stop():
+                    req.status = RequestStatus.FINISHED
+                    req.finish_time = now
+                    done.append(req)
+        for req in done:
+            self.running.remove(req)
+            self._register_full_blocks(req)
+            self._release(req)
+            self.finished.append(req)
+        return done
+
+    def _register_full_blocks(self, req: Request) -> None:
+        full = req.num_computed // self.bs
+        if full <= req.registered_blocks:
+            return
+        toks = req.all_tokens
+        have = len(req.block_hashes)
+        if have < full:
+            parent = req.block_hashes[-1] if have else b""
+            req.block_hashes += chain_block_hashes(toks[have * self.bs: full * self.bs], self.bs, parent=parent,
+                                                   full_only=True)
+        for i in range(req.registered_blocks, full):
+            self.pool.register(req.block_ids[i], req.block_hashes[i])
+        req.registered_blocks = full

@@ -9,6 +9,8 @@ from ..oracle import ops_ref as ref
 from ._ext import native
 
 _STATUS: dict[int, torch.Tensor] = {}
+# Number of lake_b200 kernel launches issued from Python (graph replays add their captured count).
+LAUNCHES = [0]
 
 
 def status_word(device: torch.device) -> torch.Tensor:
@@ -44,6 +46,7 @@ def linear(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
         if out is None:
             out = torch.empty(a.shape[0], w.shape[0], dtype=dt, device=a.device)
         native().linear(a, w, out, status_word(a.device))
+        LAUNCHES[0] += 1
         return out
     r = ref.linear(a, w).to(dt)
     if out is not None:
@@ -59,6 +62,7 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
         if out is None:
             out = torch.empty_like(residual)
         native().linear_residual(a, w, residual, out, status_word(a.device))
+        LAUNCHES[0] += 1
         return out
     r = (residual.float() + ref.linear(a, w)).to(residual.dtype)
     if out is not None:
@@ -73,6 +77,7 @@ def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | 
         out = torch.empty(a.shape[0], w_gate_up.shape[0] // 2, dtype=a.dtype, device=a.device)
     if a.is_cuda:
         native().linear_swiglu(a, w_gate_up, out, status_word(a.device))
+        LAUNCHES[0] += 1
         return out
     out.copy_(ref.swiglu_from_interleaved(ref.linear(a, w_gate_up)).to(out.dtype))
     return out
@@ -86,10 +91,11 @@ def linear_qkv(a: torch.Tensor, w_qkv: torch.Tensor, q_out: torch.Tensor, rope_c
     if a.is_cuda:
         native().linear_qkv(a, w_qkv, q_out, rope_cs, positions, slots, arena, layer, n_q_heads, n_kv_heads,
                             peer_arena, peer_slots, status_word(a.device))
+        LAUNCHES[0] += 1
         return q_out
     acc = ref.linear(a, w_qkv)
     t = a.shape[0]
-    d = ref.HEAD_DIM
+    d = arena.shape[-1]
     q = acc[:, : n_q_heads * d].view(t, n_q_heads, d)
     k = acc[:, n_q_heads * d:(n_q_heads + n_kv_heads) * d].view(t, n_kv_heads, d)
     v = acc[:, (n_q_heads + n_kv_heads) * d:].view(t, n_kv_heads, d)
@@ -113,6 +119,7 @@ def linear_argmax(a: torch.Tensor, w: torch.Tensor, bitmask: torch.Tensor | None
             out = torch.empty(m, dtype=torch.int32, device=a.device)
         native().linear_argmax(a, w, keys, bitmask, status_word(a.device))
         native().unpack_argmax(keys, out, m)
+        LAUNCHES[0] += 2
         return out
     r = ref.greedy(ref.linear(a, w), bitmask)
     if out is not None:
@@ -137,7 +144,7 @@ def paged_decode_attention(q: torch.Tensor, arena: torch.Tensor, layer: int, blo
     """One query row per sequence; row s attends to keys [0, seq_lens[s])."""
     n = seq_lens.shape[0]
     if out is None:
-        out = torch.empty(q.shape[0], n_q_heads * ref.HEAD_DIM, dtype=q.dtype, device=q.device)
+        out = torch.empty(q.shape[0], n_q_heads * arena.shape[-1], dtype=q.dtype, device=q.device)
     if q.is_cuda:
         if splits is None:
             splits = decode_splits(n, n_kv_heads, block_tables.shape[1])
@@ -147,6 +154,7 @@ def paged_decode_attention(q: torch.Tensor, arena: torch.Tensor, layer: int, blo
             ws_ml = torch.empty(n * n_kv_heads * splits * g * 2, dtype=torch.float32, device=q.device)
         native().paged_decode(q, out, arena, layer, block_tables, seq_lens, n_q_heads, n_kv_heads, scale, splits,
                               ws_o, ws_ml, status_word(q.device))
+        LAUNCHES[0] += 2 if splits > 1 else 1
         return out
     qs = torch.arange(n + 1, dtype=torch.int32)
     pos = (seq_lens - 1).to(torch.int32)
@@ -177,10 +185,11 @@ def paged_prefill_attention(q: torch.Tensor, arena: torch.Tensor, layer: int, bl
                             out: torch.Tensor | None = None) -> torch.Tensor:
     """Causal attention of packed query rows against each sequence's paged context."""
     if out is None:
-        out = torch.empty(q.shape[0], n_q_heads * ref.HEAD_DIM, dtype=q.dtype, device=q.device)
+        out = torch.empty(q.shape[0], n_q_heads * arena.shape[-1], dtype=q.dtype, device=q.device)
     if q.is_cuda:
         native().paged_prefill(q, out, arena, layer, block_tables, seq_lens, tiles, n_q_heads, n_kv_heads, scale,
                                status_word(q.device))
+        LAUNCHES[0] += 1
         return out
     r = ref.paged_attention(q, arena, layer, block_tables, seq_lens, query_start, positions, n_q_heads,
                             n_kv_heads, scale)
@@ -194,6 +203,7 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, out: torch.Tensor | N
         out = torch.empty_like(x)
     if x.is_cuda:
         native().rmsnorm(x, w, out, eps)
+        LAUNCHES[0] += 1
         return out
     out.copy_(ref.rms_norm(x, w, eps).to(out.dtype))
     return out
@@ -204,6 +214,7 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: torch.Tensor | None =
         out = torch.empty(ids.shape[0], table.shape[1], dtype=table.dtype, device=table.device)
     if table.is_cuda:
         native().embedding(ids, table, out, status_word(table.device))
+        LAUNCHES[0] += 1
         return out
     out.copy_(table[ids.long()])
     return out
@@ -215,6 +226,7 @@ def greedy_sample(logits: torch.Tensor, bitmask: torch.Tensor | None = None,
         if out is None:
             out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
         native().argmax(logits, bitmask, out)
+        LAUNCHES[0] += 1
         return out
     r = ref.greedy(logits, bitmask)
     if out is not None:
@@ -227,6 +239,7 @@ def apply_token_bitmask(logits: torch.Tensor, bitmask: torch.Tensor) -> torch.Te
     """In place: disallowed tokens (bit 0) -> -inf."""
     if logits.is_cuda:
         native().apply_bitmask(logits, bitmask)
+        LAUNCHES[0] += 1
         return logits
     logits.copy_(ref.apply_bitmask(logits, bitmask))
     return logits
@@ -240,6 +253,7 @@ def chain_reject_sample(draft: torch.Tensor, draft_off: torch.Tensor, target: to
     out_len = torch.zeros(n, dtype=torch.int32, device=draft.device)
     if draft.is_cuda:
         native().chain_reject(draft, draft_off, target, target_off, out, out_len)
+        LAUNCHES[0] += 1
         return out, out_len
     d_off, t_off = draft_off.tolist(), target_off.tolist()
     dl = [draft[d_off[i]:d_off[i + 1]].tolist() for i in range(n)]
@@ -257,6 +271,7 @@ def page_copy(src: torch.Tensor, dst: torch.Tensor, src_ids: torch.Tensor, dst_i
         sub_bytes = page_bytes
     if src.is_cuda or dst.is_cuda:
         native().page_copy(src, dst, src_ids, dst_ids, page_bytes, sub_off, sub_bytes)
+        LAUNCHES[0] += 1
         return
     s = src.view(torch.uint8).view(-1, page_bytes)
     d = dst.view(torch.uint8).view(-1, page_bytes)

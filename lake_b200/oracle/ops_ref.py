@@ -84,19 +84,21 @@ def write_kv(arena: torch.Tensor, layer: int, slots: torch.Tensor, k: torch.Tens
     sl = slots.long()
     keep = sl >= 0
     sl = sl[keep]
-    blk, off = sl // PAGE, sl % PAGE
+    page = arena.shape[4]
+    blk, off = sl // page, sl % page
     arena[blk, layer, 0, :, off, :] = k[keep].to(arena.dtype)
     arena[blk, layer, 1, :, off, :] = v[keep].to(arena.dtype)
 
 
 def gather_kv(arena: torch.Tensor, layer: int, block_table: torch.Tensor, length: int):
     """Return K, V [length, Hkv, D] fp32 for one sequence."""
-    nb = (length + PAGE - 1) // PAGE
+    page = arena.shape[4]
+    nb = (length + page - 1) // page
     ids = block_table[:nb].long()
     k = arena[ids, layer, 0].float()  # [nb, Hkv, 16, D]
     v = arena[ids, layer, 1].float()
-    k = k.permute(0, 2, 1, 3).reshape(nb * PAGE, -1, k.shape[-1])[:length]
-    v = v.permute(0, 2, 1, 3).reshape(nb * PAGE, -1, v.shape[-1])[:length]
+    k = k.permute(0, 2, 1, 3).reshape(nb * page, -1, k.shape[-1])[:length]
+    v = v.permute(0, 2, 1, 3).reshape(nb * page, -1, v.shape[-1])[:length]
     return k, v
 
 
@@ -118,7 +120,8 @@ def paged_attention(q: torch.Tensor, arena: torch.Tensor, layer: int, block_tabl
                     seq_lens: torch.Tensor, query_start: torch.Tensor, positions: torch.Tensor,
                     n_q_heads: int, n_kv_heads: int, scale: float) -> torch.Tensor:
     """Generic paged attention: rows [query_start[s], query_start[s+1]) belong to sequence s."""
-    out = torch.zeros(q.shape[0], n_q_heads * HEAD_DIM, dtype=torch.float32, device=q.device)
+    d = arena.shape[-1]
+    out = torch.zeros(q.shape[0], n_q_heads * d, dtype=torch.float32, device=q.device)
     qs = query_start.tolist()
     lens = seq_lens.tolist()
     for s in range(len(lens)):
@@ -126,7 +129,7 @@ def paged_attention(q: torch.Tensor, arena: torch.Tensor, layer: int, block_tabl
         if b <= a or lens[s] <= 0:
             continue
         k, v = gather_kv(arena, layer, block_tables[s], lens[s])
-        qq = q[a:b].float().view(b - a, n_q_heads, HEAD_DIM)
+        qq = q[a:b].float().view(b - a, n_q_heads, d)
         o = attention_one(qq, k, v, positions[a:b], scale)
         out[a:b] = o.reshape(b - a, -1)
     return out

@@ -1,0 +1,127 @@
+"""CPU tests of the engine: block pool, scheduler policy, hash chain, and the
+2-layer fp32 plumbing model against the dense oracle."""
+import random
+
+import pytest
+import torch
+
+from lake_b200.engine.block_pool import BlockPool, NoFreeBlocks, chain_block_hashes
+from lake_b200.engine.llm_engine import LLMEngine
+from lake_b200.engine.request import Request, SamplingParams
+from lake_b200.engine.scheduler import Scheduler, SchedulerConfig
+from lake_b200.oracle import ops_ref as ref
+from lake_b200.oracle.model_ref import dense_logits, greedy_generate
+
+
+# Cross-language vectors of the reference chain hash (go/router/prefixhash_test.go:13-49).
+def test_chain_hash_vectors():
+    got = [h.hex() for h in chain_block_hashes(list(range(16)), 8)]
+    assert got == ["ff1f6ee5d67458cfac950f62e93042e21fcb867e2234dcc8721801231064ad40",
+                   "db6e3872f1224a65b9d8238ba1f888935fa525fc0883a6d259369139d271ead9"]
+    assert chain_block_hashes([7], 8)[0].hex() == "e8613f5a5bc9f9feeda32a8e7c80b69dd4878e47b6a91723fb15eb84236b6a2b"
+    assert chain_block_hashes([], 8) == []
+    assert len(chain_block_hashes(list(range(17)), 8, full_only=True)) == 2
+
+
+def test_block_pool_prefix_cache_and_eviction():
+    pool = BlockPool(4, 16)
+    a = pool.alloc(3)
+    hs = [bytes([i]) * 32 for i in range(3)]
+    for b, h in zip(a, hs):
+        pool.register(b, h)
+    pool.release(a)
+    assert pool.num_free == 4
+    hit = pool.lookup(hs[:2] + [b"x" * 32])
+    assert hit == a[:2]
+    pool.release(hit)
+    # allocating all four evicts the LRU cached blocks
+    got = pool.alloc(4)
+    assert sorted(got) == list(range(4))
+    assert pool.lookup(hs) == []
+    with pytest.raises(NoFreeBlocks):
+        pool.alloc(1)
+
+
+def _req(rid, n, out=4):
+    return Request(rid=rid, prompt=list(range(n)), params=SamplingParams(max_new_tokens=out))
+
+
+def test_scheduler_budget_decode_first_and_chunking():
+    pool = BlockPool(64, 16)
+    s = Scheduler(pool, SchedulerConfig(max_running=4, max_batched_tokens=40, max_model_len=256))
+    s.add(_req("a", 50))
+    s.add(_req("b", 10))
+    o = s.schedule()
+    assert [(c.req.rid, c.start, c.n, c.sample) for c in o.prefill] == [("a", 0, 40, False)]
+    s.update(o, [], 0.0)
+    o = s.schedule()
+    # a continues (10 tokens, samples), then b is admitted with the remaining 30 budget
+    assert [(c.req.rid, c.start, c.n, c.sample) for c in o.prefill] == [("a", 40, 10, True), ("b", 0, 10, True)]
+    s.update(o, [1, 2], 0.0)
+    o = s.schedule()
+    assert [c.req.rid for c in o.decode] == ["a", "b"] and not o.prefill
+
+
+def test_scheduler_preempts_when_out_of_pages():
+    pool = BlockPool(5, 16)
+    s = Scheduler(pool, SchedulerConfig(max_running=4, max_batched_tokens=200, max_model_len=256))
+    s.add(_req("a", 32, out=40))
+    s.add(_req("b", 32, out=40))
+    o = s.schedule()
+    s.update(o, [0, 0], 0.0)
+    preempted = []
+    for _ in range(40):
+        o = s.schedule()
+        preempted += o.preempted
+        s.update(o, [0] * sum(c.sample for c in o.chunks), 0.0)
+        if not s.has_work():
+            break
+    assert preempted, "expected a preemption when pages run out"
+
+
+def test_rope_cache_llama3_scaling_keeps_high_freq():
+    plain = ref.rope_cache(16, 500000.0)
+    scaled = ref.rope_cache(16, 500000.0, scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                                   "high_freq_factor": 4.0,
+                                                   "original_max_position_embeddings": 8192})
+    assert torch.allclose(plain[:, :8], scaled[:, :8])
+    assert not torch.allclose(plain[:, -4:], scaled[:, -4:])
+
+
+def test_swiglu_interleave_roundtrip():
+    g = torch.randn(256, 8)
+    u = torch.randn(256, 8)
+    x = torch.randn(3, 8)
+    w = ref.interleave_gate_up(g, u)
+    out = ref.swiglu_from_interleaved(x @ w.t())
+    want = torch.nn.functional.silu(x @ g.t()) * (x @ u.t())
+    assert torch.allclose(out, want, atol=1e-5)
+
+
+def test_plumbing_model_matches_dense_oracle():
+    """2-layer fp32 model: chunked, paged, prefix-cached generation == dense recomputation."""
+    eng = LLMEngine("tiny", device="cpu", max_running=4, max_batched_tokens=100, max_model_len=512, num_blocks=64)
+    rng = random.Random(0)
+    prefix = [rng.randrange(1024) for _ in range(128)]
+    prompts = [prefix + [rng.randrange(1024) for _ in range(32)] for _ in range(3)]
+    outs = eng.generate(prompts, max_new_tokens=6)
+    assert eng.pool.stats["hits"] >= 8
+    for p, o in zip(prompts, outs):
+        assert o == greedy_generate(eng.model, p, 6)
+
+
+def test_plumbing_logits_close():
+    eng = LLMEngine("tiny", device="cpu", max_running=2, max_batched_tokens=64, max_model_len=256, num_blocks=32)
+    prompt = list(range(40))
+    eng.add_request(prompt, max_new_tokens=1)
+    from lake_b200.engine.scheduler import Chunk, SchedulerOutput
+    req = eng.scheduler.waiting.popleft()
+    req.block_ids = eng.pool.alloc(3)
+    out = SchedulerOutput(0, prefill=[Chunk(req, 0, 40, True)])
+    eng.runner._pack(out)
+    eng.runner._copy_cpu(0, 0, 0)
+    b = eng.runner._batch_views(40, 1, 1, 1, 0, 1)
+    b.want_logits = True
+    logits = eng.model.forward(b, eng.arena, eng.runner.ws)
+    want = dense_logits(eng.model, prompt)[-1]
+    assert torch.allclose(logits[0], want, atol=1e-4, rtol=1e-4)
