@@ -208,12 +208,13 @@ def main():
     launches = opscore.LAUNCHES[0]
     eng.runner.time_device = False
     ck = clocks.stop() if rank == 0 else {}
-    for r in eng.scheduler.finished:
-        if r.finish_time and r.finish_time >= t0:
-            if r.ttft() is not None and r.first_token_time >= t0:
-                ttft.append(r.ttft())
-            if r.tpot() is not None:
-                tpot.append(r.tpot())
+    t1 = t0 + wall
+    for r in eng.requests.values():
+        if r.first_token_time is not None and t0 <= r.arrival and r.first_token_time <= t1:
+            ttft.append(r.ttft())
+        tt = [x for x in r.token_times if t0 <= x <= t1]
+        if len(tt) >= 2:
+            tpot.append((tt[-1] - tt[0]) / (len(tt) - 1))
     h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
     d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
 
