@@ -217,14 +217,19 @@ int64_t decode_splits(int64_t num_seqs, int64_t n_kv_heads, int64_t max_blocks) 
 
 void paged_prefill(const at::Tensor& q, at::Tensor& out, const at::Tensor& arena, int64_t layer,
                    const at::Tensor& block_tables, const at::Tensor& seq_lens, const at::Tensor& tiles,
-                   int64_t n_q_heads, int64_t n_kv_heads, double scale, c10::optional<at::Tensor> status) {
+                   int64_t n_q_heads, int64_t n_kv_heads, double scale, c10::optional<at::Tensor> status,
+                   bool tensor_core) {
   PagedAttnArgs p = attn_args(q, out, arena, layer, block_tables, seq_lens, n_q_heads, n_kv_heads, scale, status);
   TORCH_CHECK(tiles.scalar_type() == at::kInt && tiles.dim() == 2 && tiles.size(1) == 4 && tiles.is_contiguous(),
               "tiles int32 [n, 4]");
   check_aligned(tiles, "tiles");
   p.tiles = reinterpret_cast<const int4*>(tiles.data_ptr<int>());
   p.num_tiles = static_cast<int>(tiles.size(0));
-  LAKEB_CHECK_RC(lakeb::paged_prefill(p, cur_stream()), "paged_prefill");
+  if (tensor_core) {
+    LAKEB_CHECK_RC(lakeb::paged_prefill_tc(p, q.size(0), cur_stream()), "paged_prefill_tc");
+  } else {
+    LAKEB_CHECK_RC(lakeb::paged_prefill(p, cur_stream()), "paged_prefill");
+  }
 }
 
 void rmsnorm(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, double eps) {
@@ -339,7 +344,7 @@ PYBIND11_MODULE(_C, m) {
   m.def("decode_splits", &decode_splits);
   m.def("paged_prefill", &paged_prefill, py::arg("q"), py::arg("out"), py::arg("arena"), py::arg("layer"),
         py::arg("block_tables"), py::arg("seq_lens"), py::arg("tiles"), py::arg("n_q_heads"), py::arg("n_kv_heads"),
-        py::arg("scale"), py::arg("status") = py::none());
+        py::arg("scale"), py::arg("status") = py::none(), py::arg("tensor_core") = true);
   m.def("rmsnorm", &rmsnorm);
   m.def("embedding", &embedding, py::arg("ids"), py::arg("table"), py::arg("out"), py::arg("status") = py::none());
   m.def("argmax", &argmax);

@@ -178,9 +178,12 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
     const int buf = it % kStages;
     const int first = b0 + it * 4;
     const int n = min(4, b1 - first);
+    int pg[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) pg[b] = b < n ? bt[first + b] : 0;  // all ids before the first TMA issue
     mbar_expect_tx(&full[buf], n * 2 * kPageBytes);
     for (int b = 0; b < n; ++b)
-      load_page(&kvmap, a, smem + buf * kStageBytes + b * 2 * kPageBytes, &full[buf], bt[first + b], kvh);
+      load_page(&kvmap, a, smem + buf * kStageBytes + b * 2 * kPageBytes, &full[buf], pg[b], kvh);
   };
   if (threadIdx.x == 0)
     for (int it = 0; it < min(kStages, iters); ++it) issue(it);
@@ -317,11 +320,12 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(const __grid_constan
   __syncthreads();
   auto issue = [&](int j) {
     const int buf = j % kStages;
+    int pg[4];
+#pragma unroll
+    for (int b = 0; b < 4; ++b) pg[b] = bt[min(j * 4 + b, nblk - 1)];  // past-the-end: last page (masked)
     mbar_expect_tx(&full[buf], kStageBytes);
-    for (int b = 0; b < 4; ++b) {
-      const int blk = min(j * 4 + b, nblk - 1);  // past-the-end pages: reload the last page (masked)
-      load_page(&kvmap, a, smem + buf * kStageBytes + b * 2 * kPageBytes, &full[buf], bt[blk], kvh);
-    }
+    for (int b = 0; b < 4; ++b)
+      load_page(&kvmap, a, smem + buf * kStageBytes + b * 2 * kPageBytes, &full[buf], pg[b], kvh);
   };
   if (threadIdx.x == 0)
     for (int j = 0; j < min(kStages, n_tiles); ++j) issue(j);

@@ -88,8 +88,10 @@ struct PagedAttnArgs {
 int paged_decode(const PagedAttnArgs& a, cudaStream_t stream);
 // Number of split-KV partitions paged_decode will use for a batch shape.
 int paged_decode_splits(int num_seqs, int n_kv_heads, int max_blocks_per_seq);
-// Causal prefill / chunked prefill over query tiles.
+// Causal prefill / chunked prefill over query tiles of <= 64 rows (warp-level MMA).
 int paged_prefill(const PagedAttnArgs& a, cudaStream_t stream);
+// Same on tcgen05 tensor cores over query tiles of <= 128 rows; q has q_rows rows.
+int paged_prefill_tc(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream);
 
 // ----------------------------------------------------------------- misc
 int rmsnorm_bf16(const __nv_bfloat16* x, int64_t sx, const __nv_bfloat16* w, __nv_bfloat16* out, int64_t so, int rows,

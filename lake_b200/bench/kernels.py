@@ -83,11 +83,15 @@ def bench_prefill(t: Timer, out: list):
         o = torch.empty_like(q)
         qs_t = torch.tensor(qs, dtype=torch.int32, device="cuda")
         ms = t(lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv, 0.088, out=o))
+        tiles64 = ops.build_prefill_tiles(qs, [0] * nseq, tile=64, device="cuda")
+        ms_mma = t(lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles64, qs_t, None, hq, hkv, 0.088,
+                                                       out=o, tensor_core=False))
         qd = q.view(nseq, ctx, hq, 128).transpose(1, 2)
         kd = torch.randn(nseq, hq, ctx, 128, device="cuda").to(BF)
         ms_ref = t(lambda: torch.nn.functional.scaled_dot_product_attention(qd, kd, kd, is_causal=True))
         fl = nseq * hq * ctx * ctx * 128 * 2  # causal: half of 4*T^2*D
-        out.append(dict(kernel="paged_prefill", nseq=nseq, ctx=ctx, ms=ms, tflops=fl / ms / 1e9, sdpa_ms=ms_ref,
+        out.append(dict(kernel="paged_prefill", nseq=nseq, ctx=ctx, ms=ms, tflops=fl / ms / 1e9,
+                        warp_mma_tflops=fl / ms_mma / 1e9, sdpa_ms=ms_ref,
                         sdpa_tflops=fl / ms_ref / 1e9))
 
 

@@ -127,7 +127,7 @@ class ModelRunner:
             if s >= nd:
                 t0 = row
                 while t0 < row + n:
-                    k = min(64, row + n - t0)
+                    k = min(ops.core.PREFILL_TILE, row + n - t0)
                     tiles[ntiles] = (s, t0, k, p0 + (t0 - row))
                     ntiles += 1
                     t0 += k

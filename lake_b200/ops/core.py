@@ -163,7 +163,10 @@ def paged_decode_attention(q: torch.Tensor, arena: torch.Tensor, layer: int, blo
     return out
 
 
-def build_prefill_tiles(query_start: list[int], pos_start: list[int], tile: int = 64,
+PREFILL_TILE = 128  # query rows per tile of the tensor-core prefill kernel
+
+
+def build_prefill_tiles(query_start: list[int], pos_start: list[int], tile: int = PREFILL_TILE,
                         device: torch.device | str = "cpu") -> torch.Tensor:
     """int32 [n_tiles, 4] of (seq, first query row, n queries, first query position)."""
     rows = []
@@ -182,13 +185,16 @@ def build_prefill_tiles(query_start: list[int], pos_start: list[int], tile: int 
 def paged_prefill_attention(q: torch.Tensor, arena: torch.Tensor, layer: int, block_tables: torch.Tensor,
                             seq_lens: torch.Tensor, tiles: torch.Tensor, query_start: torch.Tensor,
                             positions: torch.Tensor, n_q_heads: int, n_kv_heads: int, scale: float,
-                            out: torch.Tensor | None = None) -> torch.Tensor:
-    """Causal attention of packed query rows against each sequence's paged context."""
+                            out: torch.Tensor | None = None, tensor_core: bool = True) -> torch.Tensor:
+    """Causal attention of packed query rows against each sequence's paged context.
+
+    tensor_core=True runs the tcgen05 kernel (tiles of up to PREFILL_TILE rows);
+    False runs the warp-MMA kernel (tiles of up to 64 rows)."""
     if out is None:
         out = torch.empty(q.shape[0], n_q_heads * arena.shape[-1], dtype=q.dtype, device=q.device)
     if q.is_cuda:
         native().paged_prefill(q, out, arena, layer, block_tables, seq_lens, tiles, n_q_heads, n_kv_heads, scale,
-                               status_word(q.device))
+                               status_word(q.device), tensor_core)
         LAUNCHES[0] += 1
         return out
     r = ref.paged_attention(q, arena, layer, block_tables, seq_lens, query_start, positions, n_q_heads,

@@ -129,7 +129,8 @@ def test_paged_decode(cuda_dev, nseq, hq, hkv, lens):
 
 
 @pytest.mark.parametrize("hq,hkv,chunks", [(8, 2, [(0, 100)]), (32, 8, [(0, 2048)]),
-                                           (16, 4, [(64, 37), (0, 1), (500, 200), (16, 64)])])
+                                           (16, 4, [(64, 37), (0, 1), (500, 200), (16, 64)]),
+                                           (8, 8, [(0, 129), (130, 300), (1000, 5)])])
 def test_paged_prefill(cuda_dev, hq, hkv, chunks):
     # chunks: (cached prefix length, new query tokens) per sequence
     lens = [p + n for p, n in chunks]
@@ -144,14 +145,15 @@ def test_paged_prefill(cuda_dev, hq, hkv, chunks):
     t = qstart[-1]
     q = torch.randn(t, hq * 128, device=cuda_dev).to(BF)
     sl = torch.tensor(lens, dtype=torch.int32, device=cuda_dev)
-    tiles = ops.build_prefill_tiles(qstart, pos0, device=cuda_dev)
     qs_t = torch.tensor(qstart, dtype=torch.int32, device=cuda_dev)
     pos_t = torch.tensor(positions, dtype=torch.int32, device=cuda_dev)
     scale = 1 / math.sqrt(128)
-    out = ops.paged_prefill_attention(q, arena, 1, bt, sl, tiles, qs_t, pos_t, hq, hkv, scale)
     want = ref.paged_attention(q, arena, 1, bt, sl, qs_t, pos_t, hq, hkv, scale)
-    torch.cuda.synchronize()
-    _close(out, want)
+    for tc, tile in ((True, 128), (False, 64)):
+        tiles = ops.build_prefill_tiles(qstart, pos0, tile=tile, device=cuda_dev)
+        out = ops.paged_prefill_attention(q, arena, 1, bt, sl, tiles, qs_t, pos_t, hq, hkv, scale, tensor_core=tc)
+        torch.cuda.synchronize()
+        _close(out, want)
     ops.core.check_status()
 
 
