@@ -443,6 +443,22 @@ int paged_decode(const PagedAttnArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+int paged_decode_with_map(const PagedAttnArgs& a, const CUtensorMap& map, cudaStream_t stream) {
+  if (a.num_seqs <= 0) return 0;
+  if (a.n_kv_heads <= 0 || a.n_q_heads % a.n_kv_heads || a.n_q_heads / a.n_kv_heads > 16) return -1;
+  if (a.splits > 1 && (!a.ws_o || !a.ws_ml)) return -2;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  dim3 grid(a.splits, a.n_kv_heads, a.num_seqs);
+  paged_decode_kernel<<<grid, 128, kSmemBytes, stream>>>(map, a);
+  if (a.splits > 1) decode_combine_kernel<<<dim3(a.n_q_heads, a.num_seqs), kHeadDim, 0, stream>>>(a);
+  return cudaGetLastError();
+}
+
 int paged_prefill(const PagedAttnArgs& a, cudaStream_t stream) {
   if (a.num_tiles <= 0) return 0;
   if (a.n_kv_heads <= 0 || a.n_q_heads % a.n_kv_heads) return -1;

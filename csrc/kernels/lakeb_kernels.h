@@ -86,6 +86,8 @@ struct PagedAttnArgs {
 
 // One query token per sequence (decode). Query row s belongs to sequence s.
 int paged_decode(const PagedAttnArgs& a, cudaStream_t stream);
+// paged_decode with a caller-encoded tensor map of the arena (no tensor-map cache use).
+int paged_decode_with_map(const PagedAttnArgs& a, const CUtensorMap& arena_map, cudaStream_t stream);
 // Number of split-KV partitions paged_decode will use for a batch shape.
 int paged_decode_splits(int num_seqs, int n_kv_heads, int max_blocks_per_seq);
 // Causal prefill / chunked prefill over query tiles of <= 64 rows (warp-level MMA).

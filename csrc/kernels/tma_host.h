@@ -11,6 +11,10 @@ namespace lakeb {
 bool make_bf16_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
                    int box_cols = 64);
 
+// Same encoding without the cache: fills `out` only (no heap use).
+bool encode_bf16_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                     int box_cols = 64);
+
 int num_sms();
 
 }  // namespace lakeb
