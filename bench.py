@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--budget", type=int, default=8192)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--mode", choices=["colocated", "pd"], default=None,
+                    help="default: pd for an even number of GPUs >= 2, else colocated")
+    ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
     return ap.parse_args()
 
 
@@ -125,42 +128,54 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------- our arm
-def main():
-    args = parse()
-    if args.impl == "reference":
-        return run_reference(args)
-    import torch
-    import torch.distributed as dist
+class Window:
+    """Per-rank accounting of the timed steps."""
 
+    def __init__(self):
+        self.tokens = 0
+        self.dev_ms = 0.0
+        self.wall_s = 0.0
+        self.h2d = 0
+        self.d2h = 0
+        self.launches = 0
+        self.ttft: list[float] = []
+        self.tpot: list[float] = []
+        self.kv_bytes = 0
+
+
+def _latency_stats(eng, t0, t1, w: Window):
+    for r in eng.requests.values():
+        if r.first_token_time is not None and t0 <= r.arrival and r.first_token_time <= t1:
+            w.ttft.append(r.ttft())
+        tt = [x for x in r.token_times if t0 <= x <= t1]
+        if len(tt) >= 2:
+            w.tpot.append((tt[-1] - tt[0]) / (len(tt) - 1))
+
+
+def _make_engine(args, local, max_running, **kw):
     from lake_b200.engine.llm_engine import LLMEngine
+
+    return LLMEngine(args.model, device=f"cuda:{local}", max_running=max_running, max_batched_tokens=args.budget,
+                     max_model_len=args.input_len + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
+                     seed=args.seed, **kw)
+
+
+def run_colocated(args, rank, local, barrier):
+    """One engine per GPU doing prefill and decode (chunked, decode-first)."""
+    import numpy as np
+    import torch
+
     from lake_b200.ops import core as opscore
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world != args.gpus:
-        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-
-        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=600))
-
-    import numpy as np
-
     nprng = np.random.default_rng(args.seed * 1000 + rank)
-    eng = LLMEngine(args.model, device=f"cuda:{local}", max_running=args.running, max_batched_tokens=args.budget,
-                    max_model_len=args.input_len + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
-                    seed=args.seed)
+    eng = _make_engine(args, local, args.running)
     vocab = eng.cfg.vocab
 
     def new_prompt(n):
         return nprng.integers(0, vocab, n).tolist()
 
-    # bring `running` requests into flight with staggered progress
     initial = []
-    for j in range(args.running):
+    for j in range(args.running):  # in flight with staggered progress
         done = (j * args.output_len) // args.running
         initial.append(eng.add_request(new_prompt(args.input_len + done), max_new_tokens=args.output_len - done))
 
@@ -171,7 +186,6 @@ def main():
             live += 1
 
     eng.runner.capture_graphs()
-    # populate: step until every initial request has produced its first token (arrivals replace finishers)
     guard = 0
     while any(eng.requests[r].first_token_time is None for r in initial):
         eng.step()
@@ -179,84 +193,230 @@ def main():
         guard += 1
         if guard > 100000:
             raise RuntimeError("populate did not converge")
-
     for _ in range(args.warmup):
         eng.step()
         top_up()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-
-    clocks = ClockSampler(visible_gpu_indices(world) if rank == 0 else [])
-    if rank == 0:
-        clocks.start()
+    barrier()
+    w = Window()
     eng.runner.time_device = True
     opscore.LAUNCHES[0] = 0
     h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
-    tokens = 0
-    dev_ms = 0.0
-    ttft, tpot = [], []
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         outs = eng.step()
-        tokens += len(outs)
-        dev_ms += eng.runner.last_device_ms
+        w.tokens += len(outs)
+        w.dev_ms += eng.runner.last_device_ms
         top_up()
     torch.cuda.synchronize()
-    wall = time.perf_counter() - t0
-    launches = opscore.LAUNCHES[0]
+    w.wall_s = time.perf_counter() - t0
+    w.launches = opscore.LAUNCHES[0]
+    w.h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
+    w.d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
     eng.runner.time_device = False
-    ck = clocks.stop() if rank == 0 else {}
-    t1 = t0 + wall
-    for r in eng.requests.values():
-        if r.first_token_time is not None and t0 <= r.arrival and r.first_token_time <= t1:
-            ttft.append(r.ttft())
-        tt = [x for x in r.token_times if t0 <= x <= t1]
-        if len(tt) >= 2:
-            tpot.append((tt[-1] - tt[0]) / (len(tt) - 1))
-    h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
-    d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
+    _latency_stats(eng, t0, t0 + w.wall_s, w)
+    barrier()
+    return w
 
-    stats = torch.tensor([dev_ms, wall * 1000.0, float(tokens), h2d, d2h, float(launches)], dtype=torch.float64,
-                         device=dev)
+
+def run_pd(args, rank, world, local, group, barrier):
+    """Prefill ranks [0, N/2) each feed decode rank r + N/2. The decode rank owns the
+    requests and reserves pages; the prefill rank's QKV epilogue writes K/V straight
+    into those pages over NVLink. A step is one decode-rank iteration; prefill ranks
+    work continuously through the same window."""
+    import numpy as np
+    import torch
+
+    from lake_b200.ops import core as opscore
+    from lake_b200.parallel import pd
+
+    half = world // 2
+    role = "prefill" if rank < half else "decode"
+    partner = rank + half if role == "prefill" else rank - half
+    running = args.running if role == "decode" else args.prefill_running
+    eng = _make_engine(args, local, running)
+    job = os.environ.get("TORCHELASTIC_RUN_ID", "bench").replace("-", "")[:16] + str(os.getpid() if world == 1 else 0)
+    side = pd.connect_pair(eng, role, rank, partner, group, job=job)
+    w = Window()
+    if role == "prefill":
+        pd.serve_prefill(side, until_mark=1)          # populate + warm-up
+        barrier()
+        eng.runner.time_device = True
+        opscore.LAUNCHES[0] = 0
+        h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        n0 = side.first_tokens
+        dev = 0.0
+        while not side.exit and 2 not in side.marks:
+            side.poll()
+            if side.idle():
+                time.sleep(0.0002)
+                continue
+            side.step()
+            dev += eng.runner.last_device_ms
+        torch.cuda.synchronize()
+        side.marks.remove(2)
+        w.wall_s = time.perf_counter() - t0
+        w.dev_ms = dev
+        w.tokens = side.first_tokens - n0
+        w.launches = opscore.LAUNCHES[0]
+        w.h2d = (eng.runner.h2d_bytes - h2d0) / max(1, args.steps)
+        w.d2h = (eng.runner.d2h_bytes - d2h0) / max(1, args.steps)
+        eng.runner.time_device = False
+        barrier()
+        pd.serve_prefill(side)                        # until EXIT
+        return w, role
+    nprng = np.random.default_rng(args.seed * 1000 + rank)
+    vocab = eng.cfg.vocab
+    eng.runner.capture_graphs()
+
+    def new_prompt(n):
+        return nprng.integers(0, vocab, n).tolist()
+
+    initial = []
+    for j in range(args.running):
+        done = (j * args.output_len) // args.running
+        idx = side.next_idx
+        if not side.submit(new_prompt(args.input_len + done), args.output_len - done):
+            break
+        initial.append(f"pd-{idx}")
+
+    def top_up():
+        while side.inflight < args.running:
+            if not side.submit(new_prompt(args.input_len), args.output_len):
+                return
+
+    guard = 0
+    while any(r not in eng.requests or eng.requests[r].first_token_time is None for r in initial):
+        side.poll()
+        if eng.has_unfinished():
+            eng.step()
+        else:
+            time.sleep(0.0005)
+        top_up()
+        guard += 1
+        if guard > 2000000:
+            raise RuntimeError("populate did not converge")
+    for _ in range(args.warmup):
+        side.poll()
+        eng.step()
+        top_up()
+    side.mark(1)
+    torch.cuda.synchronize()
+    barrier()
+    eng.runner.time_device = True
+    opscore.LAUNCHES[0] = 0
+    h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
+    kv0 = side.kv_bytes
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        side.poll()
+        outs = eng.step()
+        w.tokens += len(outs)
+        w.dev_ms += eng.runner.last_device_ms
+        top_up()
+    torch.cuda.synchronize()
+    w.wall_s = time.perf_counter() - t0
+    w.launches = opscore.LAUNCHES[0]
+    w.h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
+    w.d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
+    w.kv_bytes = side.kv_bytes - kv0
+    eng.runner.time_device = False
+    _latency_stats(eng, t0, t0 + w.wall_s, w)
+    side.mark(2)
+    barrier()
+    side.shutdown()
+    return w, role
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
     if world > 1:
-        mx = stats.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = stats.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        dev_ms_max, wall_ms_max = mx[0].item(), mx[1].item()
-        tok_total, h2d_t, d2h_t, launches_t = sm[2].item(), sm[3].item(), sm[4].item(), sm[5].item()
+        import datetime
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=900))
+        group = dist.new_group(backend="gloo", timeout=datetime.timedelta(seconds=900))
+
+    def barrier():
+        if world > 1:
+            dist.barrier(group=group)
+
+    mode = args.mode or ("pd" if world >= 2 and world % 2 == 0 else "colocated")
+    clocks = ClockSampler(visible_gpu_indices(world) if rank == 0 else [])
+    if rank == 0:
+        clocks.start()
+    role = "colocated"
+    if mode == "pd":
+        w, role = run_pd(args, rank, world, local, group, barrier)
     else:
-        dev_ms_max, wall_ms_max, tok_total, h2d_t, d2h_t, launches_t = (stats[0].item(), stats[1].item(),
-                                                                         stats[2].item(), stats[3].item(),
-                                                                         stats[4].item(), stats[5].item())
-    value = tok_total / (dev_ms_max / 1000.0)
-    e2e = tok_total / (wall_ms_max / 1000.0)
+        w = run_colocated(args, rank, local, barrier)
+    ck = clocks.stop() if rank == 0 else {}
+
+    # aggregate over ranks (max of times, sum of counts) through the gloo group
+    t = torch.tensor([w.dev_ms if role != "prefill" else 0.0, w.wall_s * 1000.0, float(w.tokens), w.h2d, w.d2h,
+                      float(w.launches), float(w.kv_bytes), w.dev_ms], dtype=torch.float64)
+    lat = (w.ttft, w.tpot)
+    if world > 1:
+        mx, sm = t.clone(), t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM, group=group)
+        lats = [None] * world
+        dist.all_gather_object(lats, lat, group=group)
+        ttft = [x for l in lats for x in l[0]]
+        tpot = [x for l in lats for x in l[1]]
+    else:
+        mx, sm = t, t
+        ttft, tpot = lat
+    # device time of the window: the busiest rank (decode steps, or a prefill rank's busy time)
+    dev_ms = max(mx[0].item(), mx[7].item())
+    wall_ms = mx[1].item()
+    tokens = sm[2].item()
+    value = tokens / (dev_ms / 1000.0)
+    e2e = tokens / (wall_ms / 1000.0)
     if rank == 0:
         p50 = (lambda xs: sorted(xs)[len(xs) // 2] if xs else None)
+        kv_gbs = sm[6].item() / (wall_ms / 1000.0) / 1e9 if sm[6].item() else None
+        par = f"pd: {world // 2} prefill + {world // 2} decode instances (tp1 each)" if mode == "pd" else (
+            f"dp{world}" if world > 1 else "single")
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "output tok/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms_max / args.steps, 3),
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform random token ids, random-init weights)",
             "config": {"model": "Llama-3-8B architecture (32 layers, hidden 4096, 32q/8kv heads, FFN 14336, "
-                                "vocab 128256)", "global_batch": args.running * world,
+                                "vocab 128256)", "global_batch": args.running * (world // 2 if mode == "pd" else world),
                        "seq_len": args.input_len + args.output_len, "input_len": args.input_len,
-                       "output_len": args.output_len, "parallelism": f"dp{world}" if world > 1 else "single",
-                       "mode": "colocated engine per GPU (prefill+decode on the same GPU)",
+                       "output_len": args.output_len, "parallelism": par, "mode": mode,
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",
-                       "step": "one engine iteration: decode all running + chunked prefill of arrivals"},
-            "e2e": {"value": round(e2e, 1), "unit": "output tok/s", "h2d_bytes_per_step": int(h2d_t),
-                    "d2h_bytes_per_step": int(d2h_t), "api": "LLMEngine.step()"},
-            "gpu_launches": int(launches_t),
+                       "step": ("one decode-instance iteration (prefill instances run continuously)" if mode == "pd"
+                                else "one engine iteration: decode all running + chunked prefill of arrivals")},
+            "e2e": {"value": round(e2e, 1), "unit": "output tok/s", "h2d_bytes_per_step": int(sm[3].item()),
+                    "d2h_bytes_per_step": int(sm[4].item()), "api": "LLMEngine.step()"},
+            "gpu_launches": int(sm[5].item()),
             "ttft_p50_ms": round(p50(ttft) * 1000, 2) if ttft else None,
             "tpot_p50_ms": round(p50(tpot) * 1000, 2) if tpot else None,
+            "p2d_kv_gbs": round(kv_gbs, 2) if kv_gbs else None,
             "clocks": ck, "impl": "lakeb",
         }
         print(json.dumps(line))
     if world > 1:
-        dist.barrier()
+        barrier()
         dist.destroy_process_group()
     return 0
 

@@ -40,6 +40,8 @@ class EngineConfig:
     seed: int = 0
     block_size: int = 16
     model_overrides: dict = field(default_factory=dict)
+    # CPU path: back the arena with a /dev/shm file another process can map (PD-split tests)
+    shared_arena: bool = False
 
 
 @dataclass
@@ -82,7 +84,14 @@ class LLMEngine:
                 num_blocks = int((free - act) * ec.kv_mem_fraction) // page_bytes(cfg, ec.block_size)
             else:
                 num_blocks = 256
-        self.arena = alloc_arena(cfg, num_blocks, self.device, dtype, ec.block_size)
+        self.arena_path = None
+        if ec.shared_arena and self.device.type == "cpu":
+            from ..parallel.peer import alloc_shared_cpu_arena
+
+            self.arena, self.arena_path = alloc_shared_cpu_arena(
+                (num_blocks, cfg.n_layers, 2, cfg.n_kv_heads, ec.block_size, cfg.head_dim), dtype)
+        else:
+            self.arena = alloc_arena(cfg, num_blocks, self.device, dtype, ec.block_size)
         self.pool = BlockPool(num_blocks, ec.block_size, ec.enable_prefix_cache)
         self.scheduler = Scheduler(self.pool, SchedulerConfig(ec.max_running, ec.max_batched_tokens,
                                                               ec.long_prefill_threshold, ec.max_model_len, maxb))
@@ -108,6 +117,70 @@ class LLMEngine:
     def abort(self, rid: str) -> bool:
         return self.scheduler.abort(rid)
 
+    # ------------------------------------------------------------ disaggregation hooks
+    def reserve_blocks(self, n_tokens: int) -> list[int] | None:
+        """Pages for a request another instance will prefill into this arena (None if full)."""
+        n = (n_tokens + self.ec.block_size - 1) // self.ec.block_size
+        if not self.pool.can_alloc(n):
+            return None
+        return self.pool.alloc(n)
+
+    def release_blocks(self, blocks: list[int]) -> None:
+        self.pool.release(blocks)
+
+    def adopt_prefilled(self, rid: str, prompt: list[int], first_token: int, block_ids: list[int],
+                        max_new_tokens: int, arrival: float | None = None) -> Request:
+        """Decode side of PD-split: the prompt's KV was written into `block_ids` by a prefill
+        instance, which also sampled `first_token`."""
+        now = time.perf_counter()
+        req = Request(rid=rid, prompt=list(prompt), params=SamplingParams(max_new_tokens=max_new_tokens))
+        if arrival is not None:
+            req.arrival = arrival
+        req.block_ids = list(block_ids)
+        req.output = [int(first_token)]
+        req.first_token_time = now
+        req.token_times.append(now)
+        self.requests[rid] = req
+        if req.should_stop():
+            req.status = RequestStatus.FINISHED
+            req.finish_time = now
+            self.pool.release(req.block_ids)
+            req.block_ids = []
+            return req
+        self.scheduler.adopt(req)
+        return req
+
+    def add_remote_prefill(self, prompt: list[int], remote_blocks: list[int], rid: str | None = None,
+                           arrival: float | None = None) -> str:
+        """Prefill side of PD-split: compute the prompt, write its K/V into the decode
+        instance's pages `remote_blocks` (runner.peer_arena) and sample the first token."""
+        if self.runner.peer_arena is None:
+            raise RuntimeError("no peer arena attached (parallel.pd attaches the decode instance's arena)")
+        rid = self.add_request(prompt, max_new_tokens=1, rid=rid, arrival=arrival)
+        self.requests[rid].remote_blocks = list(remote_blocks)
+        return rid
+
+    def _copy_cached_to_peer(self, out: SchedulerOutput) -> None:
+        """Prefix pages served from this instance's cache are not recomputed, so their
+        K/V go to the peer arena by a page copy (NVLink P2P on the GPU)."""
+        src, dst = [], []
+        for ch in out.prefill:
+            r = ch.req
+            if r.remote_blocks is None or not r.num_cached or r.meta.get("peer_copied"):
+                continue
+            nb = r.num_cached // self.ec.block_size
+            src += r.block_ids[:nb]
+            dst += r.remote_blocks[:nb]
+            r.meta["peer_copied"] = True
+        if not src:
+            return
+        from .. import ops
+
+        dev = self.arena.device
+        ops.page_copy(self.arena, self.runner.peer_arena, torch.tensor(src, device=dev),
+                      torch.tensor(dst, device=dev), page_bytes(self.cfg, self.ec.block_size,
+                                                                self.arena.element_size()))
+
     def has_unfinished(self) -> bool:
         return self.scheduler.has_work()
 
@@ -118,6 +191,8 @@ class LLMEngine:
         if out.is_empty:
             return []
         bitmask = self._bitmask(out)
+        if self.runner.peer_arena is not None:
+            self._copy_cached_to_peer(out)
         sampled = self.runner.execute(out, bitmask)
         now = time.perf_counter()
         self.scheduler.update(out, sampled, now)

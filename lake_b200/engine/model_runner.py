@@ -56,7 +56,10 @@ class ModelRunner:
         self.n_i32 = off
         pin = self.cuda
         self.h_i32 = torch.zeros(off, dtype=torch.int32, pin_memory=pin)
-        self.h_i64 = torch.zeros(2 * max_tokens + max_seqs, dtype=torch.int64, pin_memory=pin)  # slots | rows
+        # int64 staging: slots [max_tokens] | sample rows [max_seqs] | peer slots [max_tokens]
+        self.h_i64 = torch.zeros(2 * max_tokens + max_seqs, dtype=torch.int64, pin_memory=pin)
+        self.peer_off = max_tokens + max_seqs
+        self.peer_arena: torch.Tensor | None = None  # decode instance's arena (IPC-mapped) for fused P->D
         self.h_tok = torch.zeros(max_seqs, dtype=torch.int32, pin_memory=pin)
         self.d_i32 = torch.zeros(off, dtype=torch.int32, device=self.device)
         self.d_i64 = torch.zeros(2 * max_tokens + max_seqs, dtype=torch.int64, device=self.device)
@@ -65,6 +68,7 @@ class ModelRunner:
         self.use_graphs = use_cuda_graphs and self.cuda
         self.graphs: dict[int, tuple] = {}
         self.graph_launches: dict[int, int] = {}
+        self.has_peer = False
         self.stream = torch.cuda.current_stream(self.device) if self.cuda else None
         self.h2d_bytes = 0
         self.d2h_bytes = 0
@@ -86,7 +90,8 @@ class ModelRunner:
             n_decode=nd, prefill_tiles=self._v(d, "tiles", ntiles * 4, (ntiles, 4)),
             query_start=self._v(d, "qstart", s + 1),
             sample_rows=d64[self.max_tokens: self.max_tokens + nrows], bitmask=bitmask,
-            peer_arena=peer[0] if peer else None, peer_slots=peer[1][:t] if peer else None, decode_splits=splits)
+            peer_arena=self.peer_arena if peer else None,
+            peer_slots=d64[self.peer_off:self.peer_off + t] if peer else None, decode_splits=splits)
 
     # ------------------------------------------------------------ host packing
     def _pack(self, out: SchedulerOutput, pad_decode_to: int = 0):
@@ -100,6 +105,8 @@ class ModelRunner:
         bt = self._v(self.np_i32, "bt", shape=(self.max_seqs, maxb))
         slots = self.np_i64[: self.max_tokens]
         rows = self.np_i64[self.max_tokens: self.max_tokens + self.max_seqs]
+        pslots = self.np_i64[self.peer_off:]
+        self.has_peer = False
         row = 0
         nrows = 0
         ntiles = 0
@@ -120,6 +127,14 @@ class ModelRunner:
                 pos[row:row + n] = pr
                 blk = np.asarray(req.block_ids, dtype=np.int64)
                 slots[row:row + n] = blk[pr // bs] * bs + pr % bs
+            rb = req.remote_blocks
+            if rb is not None:
+                self.has_peer = True
+                pr = np.arange(p0, p0 + n, dtype=np.int64)
+                rbk = np.asarray(rb, dtype=np.int64)
+                pslots[row:row + n] = rbk[pr // bs] * bs + pr % bs
+            else:
+                pslots[row:row + n] = -1
             nb = len(req.block_ids)
             bt[s, :nb] = req.block_ids
             lens[s] = p0 + n
@@ -160,6 +175,10 @@ class ModelRunner:
         self.d_i64[self.max_tokens:self.max_tokens + nrows].copy_(
             self.h_i64[self.max_tokens:self.max_tokens + nrows], non_blocking=True)
         self.h2d_bytes += n32 * 4 + (t + nrows) * 8
+        if self.has_peer:
+            o = self.peer_off
+            self.d_i64[o:o + t].copy_(self.h_i64[o:o + t], non_blocking=True)
+            self.h2d_bytes += t * 8
 
     # ------------------------------------------------------------ graphs
     def _bucket(self, nd: int) -> int | None:
@@ -207,17 +226,21 @@ class ModelRunner:
             self._get_graph(b)
 
     # ------------------------------------------------------------ execute
-    def execute(self, out: SchedulerOutput, bitmask: torch.Tensor | None = None, peer=None) -> list[int]:
-        """Run one step; returns one sampled token per sampling chunk (chunk order)."""
+    def execute(self, out: SchedulerOutput, bitmask: torch.Tensor | None = None) -> list[int]:
+        """Run one step; returns one sampled token per sampling chunk (chunk order).
+
+        Requests with ``remote_blocks`` (prefill for a decode instance) get their
+        K/V rows written into ``self.peer_arena`` too, by the QKV epilogue."""
         if out.is_empty:
             return []
         nd = len(out.decode)
-        pure_decode = not out.prefill and bitmask is None and peer is None
+        has_remote = any(c.req.remote_blocks is not None for c in out.prefill)
+        pure_decode = not out.prefill and bitmask is None
         bucket = self._bucket(nd) if (pure_decode and self.use_graphs) else None
         t, s, ntiles, nrows, nd_eff = self._pack(out, pad_decode_to=bucket or 0)
         if not self.cuda:
             self._copy_cpu(t, s, nrows)
-            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, 1, bitmask, peer)
+            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, 1, bitmask, has_remote)
             toks = self.model.forward(batch, self.arena, self.ws)
             return toks[: len([c for c in out.chunks if c.sample])].tolist()
         graph = None
@@ -233,7 +256,7 @@ class ModelRunner:
             graph.replay()
             ops.core.LAUNCHES[0] += self.graph_launches[bucket]
         else:
-            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, self._splits(nd_eff), bitmask, peer)
+            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, self._splits(nd_eff), bitmask, has_remote)
             toks = self.model.forward(batch, self.arena, self.ws)
         if ev1 is not None:
             ev1.record()

@@ -40,7 +40,8 @@ class Request:
     token_times: list[float] = field(default_factory=list)
     # disaggregation hooks
     exec_mode: str = "colocated"
-    remote_slots: object | None = None
+    # pages of this request's KV in a decode instance's arena (prefill side of PD-split)
+    remote_blocks: list[int] | None = None
     meta: dict = field(default_factory=dict)
 
     @property

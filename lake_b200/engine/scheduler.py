@@ -77,6 +77,14 @@ class Scheduler:
         req.status = RequestStatus.WAITING
         self.waiting.append(req)
 
+    def adopt(self, req: Request) -> None:
+        """Take over a request whose prompt KV is already resident in `req.block_ids`
+        (prefilled by another instance); it joins the running batch in decode."""
+        req.status = RequestStatus.RUNNING
+        req.num_computed = len(req.prompt)
+        self.running.append(req)
+        self._register_full_blocks(req)
+
     def abort(self, rid: str) -> bool:
         for q in (self.waiting, self.running):
             for r in list(q):

@@ -1,0 +1,67 @@
+"""PD-split on CPU with two gloo ranks: the prefill rank writes K/V into the
+decode rank's arena (shared /dev/shm mapping standing in for NVLink P2P) and the
+decode rank's tokens must equal a colocated single-process run (the 2-layer
+plumbing model, fp32)."""
+import json
+import os
+import random
+import socket
+
+import pytest
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _prompts():
+    rng = random.Random(5)
+    prefix = [rng.randrange(1024) for _ in range(48)]
+    return [prefix + [rng.randrange(1024) for _ in range(n)] for n in (3, 20, 40, 1)]
+
+
+def _worker(rank, port, out_dir):
+    import torch.distributed as dist
+
+    from lake_b200.engine.llm_engine import LLMEngine
+    from lake_b200.parallel import pd
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    role = "prefill" if rank == 0 else "decode"
+    eng = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512,
+                    num_blocks=96, shared_arena=(role == "decode"))
+    side = pd.connect_pair(eng, role, rank, 1 - rank, None, job=f"t{port}", shm_path=eng.arena_path)
+    if role == "prefill":
+        pd.serve_prefill(side)
+    else:
+        prompts = _prompts()
+        for p in prompts:
+            assert side.submit(p, 8)
+        while side.inflight:
+            side.poll()
+            eng.step()
+        outs = [eng.requests[f"pd-{i}"].output for i in range(len(prompts))]
+        ref = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512, num_blocks=96)
+        want = ref.generate(prompts, max_new_tokens=8)
+        side.shutdown()
+        with open(os.path.join(out_dir, "res.json"), "w") as f:
+            json.dump({"outs": outs, "want": want, "kv_bytes": side.kv_bytes}, f)
+    dist.barrier()
+    dist.destroy_process_group()
+    if eng.arena_path:
+        from lake_b200.parallel.peer import unlink_shared
+
+        unlink_shared(eng.arena_path)
+
+
+def test_pd_split_matches_colocated(tmp_path):
+    port = _free_port()
+    mp.spawn(_worker, args=(port, str(tmp_path)), nprocs=2, join=True)
+    res = json.load(open(tmp_path / "res.json"))
+    assert res["outs"] == res["want"]
+    assert res["kv_bytes"] > 0
