@@ -235,7 +235,7 @@ def run_pd(args, rank, world, local, group, barrier):
     role = "prefill" if rank < half else "decode"
     partner = rank + half if role == "prefill" else rank - half
     running = args.running if role == "decode" else args.prefill_running
-    eng = _make_engine(args, local, running)
+    eng = _make_engine(args, local, running, shared_arena=(role == "decode"))
     job = os.environ.get("TORCHELASTIC_RUN_ID", "bench").replace("-", "")[:16] + str(os.getpid() if world == 1 else 0)
     side = pd.connect_pair(eng, role, rank, partner, group, job=job)
     w = Window()

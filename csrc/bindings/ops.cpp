@@ -4,6 +4,8 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
+#include <cstring>
+
 #include "../kernels/lakeb_kernels.h"
 
 namespace {
@@ -321,9 +323,76 @@ void page_copy_to_ptr(const at::Tensor& src, int64_t dst_ptr, const at::Tensor& 
                  "page_copy_to_ptr");
 }
 
+// Let kernels on the current device address memory that lives on `peer_device`
+// (e.g. an arena mapped from another process through CUDA IPC). Returns true if
+// access is (now) enabled.
+bool enable_peer_access(int64_t peer_device) {
+  int cur = 0;
+  TORCH_CHECK(cudaGetDevice(&cur) == cudaSuccess, "cudaGetDevice failed");
+  if (cur == peer_device) return true;
+  int can = 0;
+  TORCH_CHECK(cudaDeviceCanAccessPeer(&can, cur, static_cast<int>(peer_device)) == cudaSuccess,
+              "cudaDeviceCanAccessPeer failed");
+  if (!can) return false;
+  cudaError_t e = cudaDeviceEnablePeerAccess(static_cast<int>(peer_device), 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    cudaGetLastError();
+    return true;
+  }
+  TORCH_CHECK(e == cudaSuccess, "cudaDeviceEnablePeerAccess failed: ", cudaGetErrorString(e));
+  return true;
+}
+
+// ---------------------------------------------------------------- IPC-shared buffers
+// A buffer other processes can map: its own cudaMalloc allocation (so the IPC
+// handle covers exactly this tensor), zero-filled, freed with the tensor.
+at::Tensor alloc_ipc_tensor(std::vector<int64_t> sizes, at::ScalarType dtype) {
+  int64_t n = 1;
+  for (auto s : sizes) n *= s;
+  const size_t bytes = static_cast<size_t>(n) * c10::elementSize(dtype);
+  void* ptr = nullptr;
+  cudaError_t e = cudaMalloc(&ptr, bytes);
+  TORCH_CHECK(e == cudaSuccess, "cudaMalloc(", bytes, ") failed: ", cudaGetErrorString(e));
+  e = cudaMemset(ptr, 0, bytes);
+  TORCH_CHECK(e == cudaSuccess, "cudaMemset failed: ", cudaGetErrorString(e));
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto opts = at::TensorOptions().dtype(dtype).device(at::Device(at::kCUDA, dev));
+  return torch::from_blob(ptr, sizes, [](void* p) { cudaFree(p); }, opts);
+}
+
+// IPC handle (64 bytes) of a tensor made by alloc_ipc_tensor.
+py::bytes ipc_export(const at::Tensor& t) {
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, t.data_ptr());
+  TORCH_CHECK(e == cudaSuccess, "cudaIpcGetMemHandle failed: ", cudaGetErrorString(e));
+  return py::bytes(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+
+// Map another process's buffer into the *current* device's context (peer access
+// from this device to the owner is enabled by the driver as needed). The tensor
+// reports the current device; its memory may physically live on a peer GPU.
+at::Tensor ipc_import(const py::bytes& handle, std::vector<int64_t> sizes, at::ScalarType dtype) {
+  std::string hs(handle);
+  TORCH_CHECK(hs.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, hs.data(), sizeof(h));
+  void* ptr = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  TORCH_CHECK(e == cudaSuccess, "cudaIpcOpenMemHandle failed: ", cudaGetErrorString(e));
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto opts = at::TensorOptions().dtype(dtype).device(at::Device(at::kCUDA, dev));
+  return torch::from_blob(ptr, sizes, [](void* p) { cudaIpcCloseMemHandle(p); }, opts);
+}
+
 }  // namespace
 
 PYBIND11_MODULE(_C, m) {
+  m.def("enable_peer_access", &enable_peer_access);
+  m.def("alloc_ipc_tensor", &alloc_ipc_tensor);
+  m.def("ipc_export", &ipc_export);
+  m.def("ipc_import", &ipc_import);
   m.doc() = "lake_b200 sm_100a kernels";
   namespace py = pybind11;
   m.def("linear", &linear, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("status") = py::none(),

@@ -40,7 +40,8 @@ class EngineConfig:
     seed: int = 0
     block_size: int = 16
     model_overrides: dict = field(default_factory=dict)
-    # CPU path: back the arena with a /dev/shm file another process can map (PD-split tests)
+    # Arena other processes can map: a /dev/shm file on the CPU path, its own IPC-exportable
+    # cudaMalloc allocation on the GPU (decode instances of PD-split)
     shared_arena: bool = False
 
 
@@ -85,11 +86,15 @@ class LLMEngine:
             else:
                 num_blocks = 256
         self.arena_path = None
+        shape = (num_blocks, cfg.n_layers, 2, cfg.n_kv_heads, ec.block_size, cfg.head_dim)
         if ec.shared_arena and self.device.type == "cpu":
             from ..parallel.peer import alloc_shared_cpu_arena
 
-            self.arena, self.arena_path = alloc_shared_cpu_arena(
-                (num_blocks, cfg.n_layers, 2, cfg.n_kv_heads, ec.block_size, cfg.head_dim), dtype)
+            self.arena, self.arena_path = alloc_shared_cpu_arena(shape, dtype)
+        elif ec.shared_arena:
+            from ..parallel.peer import alloc_ipc_arena
+
+            self.arena = alloc_ipc_arena(shape, dtype, self.device)
         else:
             self.arena = alloc_arena(cfg, num_blocks, self.device, dtype, ec.block_size)
         self.pool = BlockPool(num_blocks, ec.block_size, ec.enable_prefix_cache)

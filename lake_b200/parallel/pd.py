@@ -137,6 +137,8 @@ def connect_pair(eng: LLMEngine, role: str, rank: int, partner: int, group, job:
     if role == "decode":
         return DecodeSide(eng, to_p, from_p)
     h = [g for g in gathered if g[0] == partner][0][2]
+    if eng.arena.is_cuda:
+        torch.cuda.set_device(eng.arena.device)
     peer = import_tensor(h)
     if peer.shape[1:] != eng.arena.shape[1:]:
         raise ValueError(f"peer arena layout {tuple(peer.shape)} does not match {tuple(eng.arena.shape)}")

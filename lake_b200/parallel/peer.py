@@ -29,13 +29,21 @@ def alloc_shared_cpu_arena(shape, dtype, name: str | None = None) -> tuple[torch
     return t.view(*shape), path
 
 
-def export_tensor(t: torch.Tensor, shm_path: str | None = None):
-    """Picklable handle from which another process can map `t`."""
-    if t.is_cuda:
-        from torch.multiprocessing.reductions import reduce_tensor
+def alloc_ipc_arena(shape, dtype, device) -> torch.Tensor:
+    """Zero-filled device tensor in its own cudaMalloc allocation, exportable with export_tensor."""
+    from ..ops._ext import native
 
-        fn, args = reduce_tensor(t)
-        return ("cuda", fn, args)
+    with torch.cuda.device(device):
+        return native().alloc_ipc_tensor(list(shape), dtype)
+
+
+def export_tensor(t: torch.Tensor, shm_path: str | None = None):
+    """Picklable handle from which another process can map `t` (CUDA tensors must come from
+    alloc_ipc_arena so the IPC handle covers exactly the tensor)."""
+    if t.is_cuda:
+        from ..ops._ext import native
+
+        return ("cuda", native().ipc_export(t), tuple(t.shape), t.dtype, t.device.index)
     if shm_path is None:
         raise ValueError("CPU tensors are shared through their /dev/shm path")
     return ("cpu", shm_path, tuple(t.shape), t.dtype)
@@ -44,8 +52,12 @@ def export_tensor(t: torch.Tensor, shm_path: str | None = None):
 def import_tensor(handle) -> torch.Tensor:
     kind = handle[0]
     if kind == "cuda":
-        _, fn, args = handle
-        return fn(*args)
+        # Opened with this process's current device current: its kernels address the
+        # peer GPU's memory through the mapping (P2P over NVLink).
+        from ..ops._ext import native
+
+        _, h, shape, dtype, _owner = handle
+        return native().ipc_import(h, list(shape), dtype)
     _, path, shape, dtype = handle
     n = 1
     for d in shape:
