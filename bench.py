@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--mode", choices=["colocated", "pd"], default=None,
                     help="default: pd for an even number of GPUs >= 2, else colocated")
     ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
+    ap.add_argument("--prefill-queue", type=int, default=8,
+                    help="pd mode: grants outstanding at a prefill rank (bounds queueing delay)")
     return ap.parse_args()
 
 
@@ -141,6 +143,20 @@ class Window:
         self.ttft: list[float] = []
         self.tpot: list[float] = []
         self.kv_bytes = 0
+        self.decode_rows = 0
+        self.prefill_rows = 0
+        self.role = "colocated"
+
+    def count(self, eng):
+        out = eng.last_step
+        if out is not None:
+            self.decode_rows += len(out.decode)
+            self.prefill_rows += sum(c.n for c in out.prefill)
+
+    def diag(self, steps):
+        return {"role": self.role, "tokens": self.tokens, "dev_ms": round(self.dev_ms, 2),
+                "wall_ms": round(self.wall_s * 1000, 2), "avg_decode_batch": round(self.decode_rows / max(1, steps), 1),
+                "avg_prefill_tokens": round(self.prefill_rows / max(1, steps), 1)}
 
 
 def _latency_stats(eng, t0, t1, w: Window):
@@ -208,6 +224,7 @@ def run_colocated(args, rank, local, barrier):
         outs = eng.step()
         w.tokens += len(outs)
         w.dev_ms += eng.runner.last_device_ms
+        w.count(eng)
         top_up()
     torch.cuda.synchronize()
     w.wall_s = time.perf_counter() - t0
@@ -256,7 +273,9 @@ def run_pd(args, rank, world, local, group, barrier):
                 continue
             side.step()
             dev += eng.runner.last_device_ms
+            w.count(eng)
         torch.cuda.synchronize()
+        w.role = "prefill"
         side.marks.remove(2)
         w.wall_s = time.perf_counter() - t0
         w.dev_ms = dev
@@ -275,30 +294,25 @@ def run_pd(args, rank, world, local, group, barrier):
     def new_prompt(n):
         return nprng.integers(0, vocab, n).tolist()
 
-    initial = []
-    for j in range(args.running):
-        done = (j * args.output_len) // args.running
-        idx = side.next_idx
-        if not side.submit(new_prompt(args.input_len + done), args.output_len - done):
-            break
-        initial.append(f"pd-{idx}")
-
     def top_up():
-        while side.inflight < args.running:
+        # keep the prefill partner's queue short (bounded TTFT) and the decode batch <= running
+        while len(side.pending) < args.prefill_queue and side.inflight < args.running:
             if not side.submit(new_prompt(args.input_len), args.output_len):
                 return
 
-    guard = 0
-    while any(r not in eng.requests or eng.requests[r].first_token_time is None for r in initial):
+    # populate: run the closed loop until a full request lifetime of completions has passed,
+    # so the decode batch holds requests at every stage of their output
+    target = max(32, args.running // 4)
+    t_pop = time.perf_counter()
+    while len(eng.scheduler.finished) < target:
         side.poll()
         if eng.has_unfinished():
             eng.step()
         else:
             time.sleep(0.0005)
         top_up()
-        guard += 1
-        if guard > 2000000:
-            raise RuntimeError("populate did not converge")
+        if time.perf_counter() - t_pop > 600:
+            raise RuntimeError("populate did not reach steady state in 600 s")
     for _ in range(args.warmup):
         side.poll()
         eng.step()
@@ -312,11 +326,13 @@ def run_pd(args, rank, world, local, group, barrier):
     kv0 = side.kv_bytes
     torch.cuda.synchronize()
     t0 = time.perf_counter()
+    w.role = "decode"
     for _ in range(args.steps):
         side.poll()
         outs = eng.step()
         w.tokens += len(outs)
         w.dev_ms += eng.runner.last_device_ms
+        w.count(eng)
         top_up()
     torch.cuda.synchronize()
     w.wall_s = time.perf_counter() - t0
@@ -371,7 +387,7 @@ def main():
     # aggregate over ranks (max of times, sum of counts) through the gloo group
     t = torch.tensor([w.dev_ms if role != "prefill" else 0.0, w.wall_s * 1000.0, float(w.tokens), w.h2d, w.d2h,
                       float(w.launches), float(w.kv_bytes), w.dev_ms], dtype=torch.float64)
-    lat = (w.ttft, w.tpot)
+    lat = (w.ttft, w.tpot, w.diag(args.steps))
     if world > 1:
         mx, sm = t.clone(), t.clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX, group=group)
@@ -380,9 +396,11 @@ def main():
         dist.all_gather_object(lats, lat, group=group)
         ttft = [x for l in lats for x in l[0]]
         tpot = [x for l in lats for x in l[1]]
+        ranks = [l[2] for l in lats]
     else:
         mx, sm = t, t
-        ttft, tpot = lat
+        ttft, tpot = lat[0], lat[1]
+        ranks = [lat[2]]
     # device time of the window: the busiest rank (decode steps, or a prefill rank's busy time)
     dev_ms = max(mx[0].item(), mx[7].item())
     wall_ms = mx[1].item()
@@ -412,7 +430,7 @@ def main():
             "ttft_p50_ms": round(p50(ttft) * 1000, 2) if ttft else None,
             "tpot_p50_ms": round(p50(tpot) * 1000, 2) if tpot else None,
             "p2d_kv_gbs": round(kv_gbs, 2) if kv_gbs else None,
-            "clocks": ck, "impl": "lakeb",
+            "clocks": ck, "impl": "lakeb", "ranks": ranks,
         }
         print(json.dumps(line))
     if world > 1:

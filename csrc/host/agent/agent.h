@@ -16,6 +16,7 @@
 #include <chrono>
 #include <cstdint>
 #include <memory>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -60,6 +61,11 @@ class PutEndSession {
  public:
   PutEndSession(std::string request_id, std::string node_id, std::string model_id, std::string revision = "");
   void put_start(const std::string& block_hash, const uint8_t* bytes, size_t n);
+  // Extend the prefix chain with a block that is already durable (no bytes, not re-registered).
+  void add_prefix(const std::string& block_hash) {
+    if (!blocks_.empty()) throw std::invalid_argument("add_prefix: chain blocks must precede new blocks");
+    prefix_.push_back(block_hash);
+  }
   std::vector<cp::BlockMeta> metas(const tier::TierEngine& store) const;
   std::vector<std::string> flush_durable(tier::TierEngine& store);
   void commit_through(ControlPlanePort& cp, tier::TierEngine& store);

@@ -78,6 +78,7 @@ void register_agent(py::module_& m) {
            [](PutEndSession& s, const py::bytes& h, uintptr_t ptr, size_t n) {
              s.put_start(std::string(h), reinterpret_cast<const uint8_t*>(ptr), n);
            })
+      .def("add_prefix", [](PutEndSession& s, const py::bytes& h) { s.add_prefix(std::string(h)); })
       .def("metas", &PutEndSession::metas)
       .def("flush_durable", [](PutEndSession& s, tier::TierEngine& st) { return pybytes(s.flush_durable(st)); })
       .def("commit_through", &PutEndSession::commit_through, py::call_guard<py::gil_scoped_release>())

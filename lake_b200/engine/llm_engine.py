@@ -103,6 +103,7 @@ class LLMEngine:
         self.runner = ModelRunner(self.model, self.arena, max_tokens, ec.max_running, maxb, ec.use_cuda_graphs,
                                   ec.block_size)
         self.requests: dict[str, Request] = {}
+        self.pool_iface = None  # PoolIface (storage-pool fences), attached by attach_pool
         self._ids = itertools.count()
         self.step_count = 0
         self.last_step: SchedulerOutput | None = None
@@ -115,9 +116,17 @@ class LLMEngine:
         req = Request(rid=rid, prompt=list(prompt), params=p)
         if arrival is not None:
             req.arrival = arrival
+        if self.pool_iface is not None:
+            prefetch = getattr(self.pool_iface.agent, "prefetch", None)
+            if callable(prefetch):
+                prefetch(req)  # bring pool-resident prefix pages into HBM before admission
         self.scheduler.add(req)
         self.requests[rid] = req
         return rid
+
+    def attach_pool(self, pool) -> None:
+        """Route every step through a storage-pool interface (lake_b200.pool.PoolIface)."""
+        self.pool_iface = pool
 
     def abort(self, rid: str) -> bool:
         return self.scheduler.abort(rid)
@@ -198,9 +207,19 @@ class LLMEngine:
         bitmask = self._bitmask(out)
         if self.runner.peer_arena is not None:
             self._copy_cached_to_peer(out)
-        sampled = self.runner.execute(out, bitmask)
+        if self.pool_iface is not None:
+            self.pool_iface.prepare_step(out)  # ready fence
+            try:
+                sampled = self.runner.execute(out, bitmask)
+            finally:
+                self.pool_iface.done(out.step_id)  # compute fence
+        else:
+            sampled = self.runner.execute(out, bitmask)
         now = time.perf_counter()
-        self.scheduler.update(out, sampled, now)
+        finished = self.scheduler.update(out, sampled, now)
+        if self.pool_iface is not None:
+            for r in finished:
+                self.pool_iface.on_request_finished(r, self.cfg.name)
         self.step_count += 1
         res = []
         it = iter(sampled)

@@ -218,6 +218,7 @@ class Scheduler:
         for req in done:
             self.running.remove(req)
             self._register_full_blocks(req)
+            req.meta["final_block_ids"] = list(req.block_ids)  # pages stay resident (prefix cache)
             self._release(req)
             self.finished.append(req)
         return done
