@@ -1,0 +1,78 @@
+"""WorkerService gRPC facade of a compute worker.
+
+Generate builds a request from the proto, consumes the router's execution
+mode and reuse hint when present (empty exec_mode = a caller that did not go
+through the router: COLOCATED, no reuse hint), submits it to the WorkerEngine
+and maps pool errors onto gRPC status codes: TIMEOUT / DOWNSTREAM /
+PROTOCOL_ERROR -> UNAVAILABLE (the router's signal to re-dispatch elsewhere),
+CAPACITY -> RESOURCE_EXHAUSTED, INVALID_ARG -> INVALID_ARGUMENT.
+
+Reference parity: python/lake/runtime/worker.py:42-162, __main__.py:18-23.
+"""
+from __future__ import annotations
+
+import logging
+import os
+from concurrent import futures
+
+import grpc
+
+from ..api import proto
+from ..pool.types import PoolError, PoolErrorCode, PrefixHint
+from .config import RoleConfig
+from .worker_engine import WorkerEngine
+
+LOG = logging.getLogger("lake_b200.worker")
+
+POOL_ERROR_STATUS = {
+    PoolErrorCode.TIMEOUT: grpc.StatusCode.UNAVAILABLE,
+    PoolErrorCode.DOWNSTREAM: grpc.StatusCode.UNAVAILABLE,
+    PoolErrorCode.PROTOCOL_ERROR: grpc.StatusCode.UNAVAILABLE,
+    PoolErrorCode.CAPACITY: grpc.StatusCode.RESOURCE_EXHAUSTED,
+    PoolErrorCode.INVALID_ARG: grpc.StatusCode.INVALID_ARGUMENT,
+}
+
+
+class WorkerServicer:
+    def __init__(self, engine: WorkerEngine):
+        self.engine = engine
+        self.pb = proto.messages()
+
+    def Generate(self, request, context):
+        hint = PrefixHint(computed_tokens=request.computed_tokens, reused_blocks=request.reused_blocks,
+                          local_hit=request.local_hit)
+        try:
+            res = self.engine.submit(request.request_id, list(request.prompt_tokens),
+                                     request.max_new_tokens or 16, request.exec_mode, hint)
+        except PoolError as e:
+            context.abort(POOL_ERROR_STATUS.get(e.code, grpc.StatusCode.INTERNAL), str(e))
+        return self.pb.GenerateResponse(request_id=res.request_id, output_tokens=res.output_tokens,
+                                        reused_blocks=res.reused_blocks, prefill_blocks=res.prefill_blocks,
+                                        mode=res.mode)
+
+
+def serve(bind: str = "0.0.0.0:50053", cfg: RoleConfig | None = None, pool=None, engine=None,
+          max_workers: int = 8, block: bool = True):
+    cfg = cfg or RoleConfig.from_env()
+    eng = WorkerEngine(cfg, pool=pool, engine=engine)
+    eng.start()
+    server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers))
+    proto.add_service(server, "WorkerService", WorkerServicer(eng))
+    port = server.add_insecure_port(bind)
+    server.start()
+    LOG.info("worker serving on %s (port %d)", bind, port)
+    if block:
+        try:
+            server.wait_for_termination()
+        finally:
+            eng.stop(drain=False)
+    return server, eng, port
+
+
+def main() -> None:
+    logging.basicConfig(level=os.environ.get("LAKE_LOG", "INFO"))
+    serve(os.environ.get("LAKE_WORKER_BIND", "0.0.0.0:50053"))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,142 @@
+"""Runtime layer on CPU: role config, lifecycle, mode selection, the worker engine
+loop and the WorkerService gRPC facade (python/lake/runtime tests' behaviour)."""
+import threading
+from concurrent import futures
+
+import grpc
+import pytest
+
+from lake_b200.api import proto
+from lake_b200.engine.llm_engine import LLMEngine
+from lake_b200.pool.types import PoolError, PoolErrorCode, PrefixHint
+from lake_b200.runtime.config import (ExecMode, RoleConfig, WorkerLifecycle, WorkerRole, WorkerState,
+                                      full_local_hit, select_exec_mode)
+from lake_b200.runtime.worker import WorkerServicer
+from lake_b200.runtime.worker_engine import WorkerEngine
+
+
+def tiny_engine(**kw):
+    args = dict(max_running=4, max_batched_tokens=128, max_model_len=512, num_blocks=64)
+    args.update(kw)
+    return LLMEngine("tiny", device="cpu", **args)
+
+
+def test_role_config_env(monkeypatch):
+    monkeypatch.setenv("LAKE_WORKER_ROLE", "DECODE")
+    monkeypatch.setenv("LAKE_MAX_RUNNING_REQS", "32")
+    monkeypatch.setenv("LAKE_MAX_NUM_SCHEDULED_TOKENS", "bogus")
+    monkeypatch.setenv("LAKE_ENABLE_DRAFTER", "yes")
+    cfg = RoleConfig.from_env()
+    assert cfg.role == WorkerRole.DECODE and cfg.max_running_reqs == 32
+    assert cfg.max_num_scheduled_tokens == 8192 and cfg.enable_drafter
+    monkeypatch.setenv("LAKE_WORKER_ROLE", "nonsense")
+    assert RoleConfig.from_env().role == WorkerRole.HYBRID
+    with pytest.raises(ValueError):
+        RoleConfig(max_running_reqs=0)
+
+
+def test_lifecycle_order():
+    lc = WorkerLifecycle()
+    assert not lc.accepting
+    lc.warm()
+    assert lc.state == WorkerState.WARM and not lc.accepting
+    lc.ready()
+    lc.serve()
+    assert lc.accepting
+    with pytest.raises(ValueError):
+        lc.advance(WorkerState.BOOT)
+    lc.drain()
+    assert not lc.accepting
+    lc.terminate()
+    assert lc.state == WorkerState.TERMINATE
+
+
+def test_select_exec_mode():
+    assert select_exec_mode(PrefixHint(computed_tokens=32, local_hit=True), 64, WorkerRole.HYBRID) == ExecMode.D_DIRECT
+    assert select_exec_mode(PrefixHint(reused_blocks=2), 64, WorkerRole.PREFILL, bw_gbps=0.5) == ExecMode.COLOCATED
+    assert select_exec_mode(PrefixHint(), 64, WorkerRole.PREFILL) == ExecMode.PD_DISAGG
+    assert select_exec_mode(PrefixHint(), 64, WorkerRole.HYBRID) == ExecMode.COLOCATED
+    assert full_local_hit(PrefixHint(computed_tokens=64, local_hit=True), 64)
+    assert not full_local_hit(PrefixHint(computed_tokens=32, local_hit=True), 64)
+
+
+def test_worker_engine_concurrent_submit():
+    eng = tiny_engine()
+    ref = tiny_engine()
+    prompts = [[(7 * i + j) % 1000 for j in range(20 + i)] for i in range(6)]
+    want = ref.generate(prompts, max_new_tokens=5)
+    we = WorkerEngine(RoleConfig(device="cpu", model_backend="mock"), engine=eng)
+    we.start()
+    assert we.state == WorkerState.SERVING
+    got = [None] * len(prompts)
+
+    def run(i):
+        got[i] = we.submit(f"r{i}", prompts[i], 5).output_tokens
+
+    ts = [threading.Thread(target=run, args=(i,)) for i in range(len(prompts))]
+    [t.start() for t in ts]
+    [t.join(60) for t in ts]
+    assert got == want
+    sig = we.capacity_signal()
+    assert sig.inflight_reqs == 0 and sig.model_warmed and sig.remaining_slots == 4
+    we.stop()
+    assert we.state == WorkerState.TERMINATE
+    with pytest.raises(PoolError) as e:
+        we.submit("late", [1, 2, 3], 2)
+    assert e.value.code == PoolErrorCode.CAPACITY
+
+
+def test_worker_engine_step_failure_fails_inflight():
+    eng = tiny_engine()
+    we = WorkerEngine(RoleConfig(device="cpu", model_backend="mock"), engine=eng)
+    we.start()
+    real_step = eng.step
+
+    def bad_step():
+        raise RuntimeError("device lost")
+
+    eng.step = bad_step
+    with pytest.raises(PoolError) as e:
+        we.submit("x", [1, 2, 3, 4], 3, timeout_s=30)
+    assert e.value.code == PoolErrorCode.DOWNSTREAM and "device lost" in str(e.value)
+    with pytest.raises(PoolError) as e:
+        we.submit("y", [1, 2, 3], 3, timeout_s=30)
+    assert e.value.code == PoolErrorCode.DOWNSTREAM
+    eng.step = real_step
+    we.stop(drain=False)
+
+
+def test_worker_grpc_generate_and_error_mapping():
+    eng = tiny_engine()
+    ref = tiny_engine()
+    prompt = list(range(40))
+    want = ref.generate([prompt], max_new_tokens=4)[0]
+    we = WorkerEngine(RoleConfig(device="cpu", model_backend="mock"), engine=eng)
+    we.start()
+    server = grpc.server(futures.ThreadPoolExecutor(max_workers=4))
+    proto.add_service(server, "WorkerService", WorkerServicer(we))
+    port = server.add_insecure_port("127.0.0.1:0")
+    server.start()
+    pb = proto.messages()
+    try:
+        with grpc.insecure_channel(f"127.0.0.1:{port}") as ch:
+            stub = proto.Stub(ch, "WorkerService")
+            resp = stub.Generate(pb.GenerateRequest(request_id="g1", prompt_tokens=prompt, max_new_tokens=4),
+                                 timeout=60)
+            assert list(resp.output_tokens) == want and resp.mode == "COLOCATED"
+            # same prompt again: the radix prefix cache serves the full blocks
+            resp2 = stub.Generate(pb.GenerateRequest(request_id="g2", prompt_tokens=prompt, max_new_tokens=4,
+                                                     exec_mode="D_DIRECT", computed_tokens=32, local_hit=True),
+                                  timeout=60)
+            assert list(resp2.output_tokens) == want and resp2.reused_blocks == 2 and resp2.mode == "D_DIRECT"
+            with pytest.raises(grpc.RpcError) as e:
+                stub.Generate(pb.GenerateRequest(request_id="g3", max_new_tokens=4), timeout=30)
+            assert e.value.code() == grpc.StatusCode.INVALID_ARGUMENT
+            we.lifecycle.drain()
+            with pytest.raises(grpc.RpcError) as e:
+                stub.Generate(pb.GenerateRequest(request_id="g4", prompt_tokens=[1, 2], max_new_tokens=1),
+                              timeout=30)
+            assert e.value.code() == grpc.StatusCode.RESOURCE_EXHAUSTED
+    finally:
+        server.stop(0)
+        we.stop(drain=False)
