@@ -15,6 +15,7 @@ using namespace lakeb::cp;
 void register_tier(py::module_& m);
 void register_router(py::module_& m);
 void register_agent(py::module_& m);
+void register_transfer(py::module_& m);
 
 namespace {
 
@@ -312,4 +313,5 @@ PYBIND11_MODULE(_host, m) {
   register_tier(m);
   register_router(m);
   register_agent(m);
+  register_transfer(m);
 }

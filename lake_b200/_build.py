@@ -4,7 +4,7 @@ Compiles
   * ``csrc/kernels/*.cu``   -> sm_100a objects (nvcc, no torch headers)
   * ``csrc/bindings/ops.cpp`` -> torch/pybind11 binding
   * links both into ``lake_b200/_C.so`` (CUDA runtime linked statically)
-  * ``csrc/host/**/*.cpp``  -> ``lake_b200/_host.so`` (pybind11, no torch)
+  * ``csrc/host/**/*.cpp``  -> ``lake_b200/_host.so`` (pybind11 + static CUDA runtime, no torch)
 
 The build is driven by a generated ninja file under ``_build/`` so repeated
 builds are incremental. Nothing is JIT-compiled at import time: the ``.so``
@@ -61,7 +61,7 @@ def write_ninja() -> str:
     ext_flags = ["-O2", "-fPIC", "-std=c++17", f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_API_INCLUDE_EXTENSION_H",
                  "-DTORCH_EXTENSION_NAME=_C", f"-I{pyinc}", f"-I{cuda_inc}", f"-I{kdir}"] + [f"-I{i}" for i in tinc]
     host_flags = ["-O2", "-fPIC", "-std=c++17", f"-I{pyinc}", f"-I{_pybind_inc()}",
-                  f"-I{os.path.join(ROOT, 'csrc', 'host')}", "-fvisibility=hidden", "-Wall", "-Wno-unused-function"]
+                  f"-I{os.path.join(ROOT, 'csrc', 'host')}", f"-I{cuda_inc}", "-fvisibility=hidden", "-Wall", "-Wno-unused-function"]
 
     lines = [
         "ninja_required_version = 1.3",
@@ -90,7 +90,7 @@ def write_ninja() -> str:
         f"-ltorch_python -L{cuda_lib} -lcudart_static -ldl -lrt -lpthread -Wl,-rpath,{tlib}",
         "  description = LINK $out",
         "rule link_host",
-        "  command = $cxx -shared $in -o $out -lpthread",
+        f"  command = $cxx -shared $in -o $out -L{cuda_lib} -lcudart_static -ldl -lrt -lpthread",
         "  description = LINK $out",
     ]
     kobjs = []
