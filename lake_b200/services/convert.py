@@ -116,3 +116,19 @@ def shard_map_out(s):
 def migration_out(m):
     return pb.ShardMigration(id=kid_out(m.id), from_node=m.from_node, to_node=m.to_node,
                              push_l2_first=m.push_l2_first)
+
+
+def update_in(m) -> "H.ViewUpdate":
+    u = H.ViewUpdate()
+    u.seq = int(m.seq)
+    evs = []
+    for e in m.events:
+        ev = H.ViewEvent()
+        ev.kind = int(e.kind)
+        ev.id = kid_in(e.id)
+        ev.locations = [loc_in(x) for x in e.locations]
+        ev.l3_present = bool(e.l3_present)
+        ev.block_kind = int(e.block_kind)
+        evs.append(ev)
+    u.events = evs
+    return u

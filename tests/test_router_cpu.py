@@ -1,0 +1,150 @@
+"""Router end to end on CPU: HTTP chat -> mode select -> agent Dispatch ->
+worker Generate (tiny CPU engine), with the control plane's view mirrored
+into the router (reference: go/router/server_test.go, modeselect_test.go)."""
+import asyncio
+from concurrent import futures
+
+import grpc
+import pytest
+from aiohttp.test_utils import TestClient, TestServer
+
+from lake_b200.api import proto
+from lake_b200.engine.llm_engine import LLMEngine, page_bytes
+from lake_b200.router.http import make_app
+from lake_b200.router.server import Router, RouterConfig, RouterError, tokenize_mock
+from lake_b200.runtime.config import RoleConfig
+from lake_b200.runtime.cp_reporter import ControlPlaneReporter
+from lake_b200.runtime.worker import WorkerServicer
+from lake_b200.runtime.worker_engine import WorkerEngine
+from lake_b200.services.agent_service import AgentServer
+from lake_b200.services.controlplane import ControlPlane
+
+pb = proto.messages()
+
+
+def test_tokenize_mock():
+    assert tokenize_mock("") == list(range(1, 9))
+    t = tokenize_mock("abc")
+    assert t[:3] == [98, 99, 100] and len(t) == 8 and t[3:] == [42] * 5
+
+
+@pytest.fixture
+def stack():
+    cp = ControlPlane()
+    agent = AgentServer("worker-0")
+    eng = LLMEngine("tiny", device="cpu", max_running=4, max_batched_tokens=256, max_model_len=1024, num_blocks=128)
+    we = WorkerEngine(RoleConfig(device="cpu", model_backend="mock"), engine=eng)
+    server = grpc.server(futures.ThreadPoolExecutor(max_workers=16))
+    proto.add_service(server, "ControlPlaneService", cp)
+    proto.add_service(server, "AgentService", agent)
+    proto.add_service(server, "WorkerService", WorkerServicer(we))
+    port = server.add_insecure_port("127.0.0.1:0")
+    server.start()
+    addr = f"127.0.0.1:{port}"
+    ch = grpc.insecure_channel(addr)
+    we.on_finished = ControlPlaneReporter(proto.Stub(ch, "ControlPlaneService"), "worker-0", "tiny",
+                                          page_bytes(eng.cfg, 16, 4))
+    we.start()
+    yield addr, cp, agent, we
+    we.stop(drain=False)
+    ch.close()
+    cp.stop()
+    server.stop(0)
+
+
+def test_chat_completion_modes_and_metrics(stack):
+    addr, cp, agent, we = stack
+    cfg = RouterConfig(worker_addr=addr, agent_addr=addr, cp_addr=addr, max_inflight=2, request_timeout_s=60)
+
+    async def run():
+        router = Router(cfg)
+        async with TestClient(TestServer(make_app(router))) as client:
+            assert (await client.get("/healthz")).status == 200
+            prompt = list(range(100, 180))  # 5 full blocks
+            body = {"model": "tiny", "prompt_token_ids": prompt, "max_tokens": 3}
+            r1 = await client.post("/v1/chat/completions", json=body)
+            assert r1.status == 200
+            j1 = await r1.json()
+            assert j1["object"] == "chat.completion" and j1["lake"]["mode"] == "COLOCATED"
+            assert j1["choices"][0]["message"]["content"].startswith("mock:")
+            # the worker registered its prefix blocks; wait for the mirror to see them
+            for _ in range(100):
+                if router.mirror.size() >= 5:
+                    break
+                await asyncio.sleep(0.05)
+            assert router.mirror.size() >= 5
+            r2 = await client.post("/v1/chat/completions", json=body)
+            j2 = await r2.json()
+            assert j2["lake"]["mode"] == "D_DIRECT" and j2["lake"]["reused_blocks"] >= 4
+            assert j2["choices"][0]["message"]["content"] == j1["choices"][0]["message"]["content"]
+            r3 = await client.post("/v1/chat/completions",
+                                   json={"messages": [{"role": "user", "content": "hello there"}], "max_tokens": 2})
+            assert r3.status == 200
+            assert (await client.post("/v1/chat/completions", data=b"{nope")).status == 400
+            m = await (await client.get("/metrics")).text()
+            assert "lake_router_requests_total 3" in m and 'mode="D_DIRECT"' in m
+            assert router.local_hit_rate() > 0
+            assert agent.dispatch_count == 3
+    asyncio.run(run())
+
+
+def test_worker_down_maps_to_503(stack):
+    addr, cp, agent, we = stack
+    we.lifecycle.drain()
+    cfg = RouterConfig(worker_addr=addr, agent_addr=addr, cp_addr=addr, request_timeout_s=20)
+
+    async def run():
+        router = Router(cfg)
+        async with TestClient(TestServer(make_app(router))) as client:
+            r = await client.post("/v1/chat/completions", json={"prompt_token_ids": [1, 2, 3], "max_tokens": 1})
+            assert r.status == 503
+    asyncio.run(run())
+
+
+def test_priority_preemption_requeues():
+    """A higher-priority arrival preempts the running request; the victim is requeued and completes."""
+    from lake_b200 import _host as H
+
+    async def run():
+        router = Router(RouterConfig(max_inflight=1))
+        order = []
+        gate = asyncio.Event()
+
+        class FakeCall:
+            def __init__(self, name):
+                self.name = name
+                self.task = None
+
+            def cancel(self):
+                self.task.cancel()
+
+        async def make_exec(name, wait):
+            async def exec_fn(ticket):
+                call = FakeCall(name)
+                call.task = asyncio.current_task()
+                router._running[ticket] = call
+                try:
+                    if wait:
+                        await gate.wait()
+                    order.append(name)
+                    return name
+                except asyncio.CancelledError:
+                    order.append(f"{name}-preempted")
+                    from lake_b200.router.server import Preempted
+                    raise Preempted()
+                finally:
+                    router._running.pop(ticket, None)
+            return exec_fn
+
+        low_exec = await make_exec("low", True)
+        t_low = asyncio.create_task(router.admit_and_run(0, "m", low_exec, 10))
+        await asyncio.sleep(0.05)
+        high_exec = await make_exec("high", False)
+        t_high = asyncio.create_task(router.admit_and_run(5, "m", high_exec, 10))
+        await asyncio.sleep(0.05)
+        gate.set()
+        assert await t_high == "high"
+        assert await t_low == "low"
+        assert order == ["low-preempted", "high", "low"]
+        assert router.stats["preemptions"] == 1
+    asyncio.run(run())
