@@ -1,0 +1,64 @@
+#!/usr/bin/env bash
+# Start the whole stack locally in the foreground (Ctrl-C stops everything):
+# control plane, node storage services (agent + transfer + kv byte store),
+# one worker and the HTTP router. Run from the repository root:
+#   ./deploy/run_local.sh            # LAKE_MODEL_BACKEND=mock -> tiny CPU model
+#   LAKE_MODEL_BACKEND=llama3-8b LAKE_DEVICE=cuda ./deploy/run_local.sh
+#   ./deploy/smoke.sh                # in another shell
+set -euo pipefail
+ROOT="$(cd "$(dirname "$0")/.." && pwd)"
+cd "$ROOT"
+
+export LAKE_CP_ADDR="${LAKE_CP_ADDR:-127.0.0.1:50051}"
+export LAKE_WORKER_BIND="${LAKE_WORKER_BIND:-127.0.0.1:50053}"
+export LAKE_WORKER_ADDR="${LAKE_WORKER_ADDR:-127.0.0.1:50053}"
+export LAKE_AGENT_ADDR="${LAKE_AGENT_ADDR:-127.0.0.1:50054}"
+export LAKE_HTTP_ADDR="${LAKE_HTTP_ADDR:-127.0.0.1:8080}"
+export LAKE_MODEL_BACKEND="${LAKE_MODEL_BACKEND:-mock}"
+export LAKE_SERVED_MODEL_NAME="${LAKE_SERVED_MODEL_NAME:-mock-llm}"
+export LAKE_NODE_ID="${LAKE_NODE_ID:-worker-0}"
+PY="${PYTHON:-python}"
+
+wait_tcp() {
+  local hostport="$1" name="$2" tries="${3:-240}"
+  local host="${hostport%:*}" port="${hostport##*:}"
+  for ((i=1; i<=tries; i++)); do
+    if (echo >/dev/tcp/"$host"/"$port") >/dev/null 2>&1; then
+      echo "  ready: $name ($hostport)"
+      return 0
+    fi
+    sleep 0.25
+  done
+  echo "ERROR: timeout waiting for $name ($hostport)" >&2
+  return 1
+}
+
+PIDS=()
+cleanup() {
+  for p in "${PIDS[@]:-}"; do kill "$p" 2>/dev/null || true; done
+}
+trap cleanup EXIT INT TERM
+
+for hp in "$LAKE_CP_ADDR" "$LAKE_WORKER_ADDR" "$LAKE_AGENT_ADDR" "$LAKE_HTTP_ADDR"; do
+  if (echo >/dev/tcp/"${hp%:*}"/"${hp##*:}") >/dev/null 2>&1; then
+    echo "ERROR: $hp already in use; stop the old stack first" >&2
+    exit 1
+  fi
+done
+
+"$PY" -c "import lake_b200._host" 2>/dev/null || "$PY" -m lake_b200._build
+
+echo "==> control plane"
+"$PY" -m lake_b200.services.controlplane & PIDS+=($!)
+wait_tcp "$LAKE_CP_ADDR" controlplane
+echo "==> node services"
+"$PY" -m lake_b200.services.node & PIDS+=($!)
+wait_tcp "$LAKE_AGENT_ADDR" node-services
+echo "==> worker ($LAKE_MODEL_BACKEND)"
+"$PY" -m lake_b200.runtime & PIDS+=($!)
+wait_tcp "$LAKE_WORKER_ADDR" worker 1200
+echo "==> router"
+"$PY" -m lake_b200.router & PIDS+=($!)
+wait_tcp "$LAKE_HTTP_ADDR" router
+echo "stack up: http://$LAKE_HTTP_ADDR/v1/chat/completions"
+wait

@@ -71,7 +71,23 @@ def serve(bind: str = "0.0.0.0:50053", cfg: RoleConfig | None = None, pool=None,
 
 def main() -> None:
     logging.basicConfig(level=os.environ.get("LAKE_LOG", "INFO"))
-    serve(os.environ.get("LAKE_WORKER_BIND", "0.0.0.0:50053"))
+    cfg = RoleConfig.from_env()
+    server, eng, port = serve(os.environ.get("LAKE_WORKER_BIND", "0.0.0.0:50053"), cfg, block=False)
+    cp_addr = os.environ.get("LAKE_CP_ADDR", "")
+    if cp_addr:  # publish resident prefix blocks to the control plane's view
+        from ..engine.llm_engine import page_bytes
+        from .cp_reporter import ControlPlaneReporter
+
+        e = eng.engine
+        ch = grpc.insecure_channel(cp_addr)
+        eng.on_finished = ControlPlaneReporter(
+            proto.Stub(ch, "ControlPlaneService"), os.environ.get("LAKE_NODE_ID", "worker-0"),
+            cfg.served_model_name, page_bytes(e.cfg, e.ec.block_size, e.arena.element_size()), e.ec.block_size,
+            e.cfg.n_layers)
+    try:
+        server.wait_for_termination()
+    finally:
+        eng.stop(drain=False)
 
 
 if __name__ == "__main__":
