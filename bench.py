@@ -48,6 +48,7 @@ def parse():
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--mode", choices=["colocated", "pd"], default=None,
                     help="default: pd for an even number of GPUs >= 2, else colocated")
+    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (colocated mode)")
     ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
     ap.add_argument("--prefill-queue", type=int, default=8,
                     help="pd mode: grants outstanding at a prefill rank (bounds queueing delay)")
@@ -176,15 +177,19 @@ def _make_engine(args, local, max_running, **kw):
                      seed=args.seed, **kw)
 
 
-def run_colocated(args, rank, local, barrier):
-    """One engine per GPU doing prefill and decode (chunked, decode-first)."""
+def run_colocated(args, rank, local, barrier, tp=None):
+    """One engine per GPU (or per tensor-parallel group) doing prefill and decode
+    (chunked, decode-first). Ranks of a TP group submit identical requests and count
+    tokens once (on the group's first rank)."""
     import numpy as np
     import torch
 
     from lake_b200.ops import core as opscore
 
-    nprng = np.random.default_rng(args.seed * 1000 + rank)
-    eng = _make_engine(args, local, args.running)
+    stream_id = rank if tp is None else rank // tp[1]
+    nprng = np.random.default_rng(args.seed * 1000 + stream_id)
+    eng = _make_engine(args, local, args.running, tp=tp)
+    counts = tp is None or tp[0] == 0
     vocab = eng.cfg.vocab
 
     def new_prompt(n):
@@ -222,7 +227,7 @@ def run_colocated(args, rank, local, barrier):
     t0 = time.perf_counter()
     for _ in range(args.steps):
         outs = eng.step()
-        w.tokens += len(outs)
+        w.tokens += len(outs) if counts else 0
         w.dev_ms += eng.runner.last_device_ms
         w.count(eng)
         top_up()
@@ -232,7 +237,8 @@ def run_colocated(args, rank, local, barrier):
     w.h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
     w.d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
     eng.runner.time_device = False
-    _latency_stats(eng, t0, t0 + w.wall_s, w)
+    if counts:
+        _latency_stats(eng, t0, t0 + w.wall_s, w)
     barrier()
     return w
 
@@ -373,7 +379,15 @@ def main():
         if world > 1:
             dist.barrier(group=group)
 
-    mode = args.mode or ("pd" if world >= 2 and world % 2 == 0 else "colocated")
+    mode = args.mode or ("pd" if world >= 2 and world % 2 == 0 and args.tp == 1 else "colocated")
+    tp = None
+    if args.tp > 1:
+        if mode != "colocated" or world % args.tp:
+            raise SystemExit("--tp needs colocated mode and a GPU count divisible by it")
+        gid = rank // args.tp
+        tp_groups = [dist.new_group(list(range(g * args.tp, (g + 1) * args.tp)), backend="gloo")
+                     for g in range(world // args.tp)]
+        tp = (rank % args.tp, args.tp, tp_groups[gid])
     clocks = ClockSampler(visible_gpu_indices(world) if rank == 0 else [])
     if rank == 0:
         clocks.start()
@@ -381,7 +395,7 @@ def main():
     if mode == "pd":
         w, role = run_pd(args, rank, world, local, group, barrier)
     else:
-        w = run_colocated(args, rank, local, barrier)
+        w = run_colocated(args, rank, local, barrier, tp)
     ck = clocks.stop() if rank == 0 else {}
 
     # aggregate over ranks (max of times, sum of counts) through the gloo group
@@ -411,14 +425,16 @@ def main():
         p50 = (lambda xs: sorted(xs)[len(xs) // 2] if xs else None)
         kv_gbs = sm[6].item() / (wall_ms / 1000.0) / 1e9 if sm[6].item() else None
         par = f"pd: {world // 2} prefill + {world // 2} decode instances (tp1 each)" if mode == "pd" else (
-            f"dp{world}" if world > 1 else "single")
+            f"dp{world // args.tp} x tp{args.tp} (fused NVLink collectives)" if args.tp > 1 else
+            (f"dp{world}" if world > 1 else "single"))
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "output tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform random token ids, random-init weights)",
             "config": {"model": "Llama-3-8B architecture (32 layers, hidden 4096, 32q/8kv heads, FFN 14336, "
-                                "vocab 128256)", "global_batch": args.running * (world // 2 if mode == "pd" else world),
+                                "vocab 128256)",
+                       "global_batch": args.running * (world // 2 if mode == "pd" else world // args.tp),
                        "seq_len": args.input_len + args.output_len, "input_len": args.input_len,
                        "output_len": args.output_len, "parallelism": par, "mode": mode,
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",

@@ -70,6 +70,40 @@ KVArenaView arena_view(const at::Tensor& arena, int64_t layer) {
   return v;
 }
 
+template <class T>
+T* ptr_of(const py::handle& o) {
+  return reinterpret_cast<T*>(static_cast<uintptr_t>(o.cast<int64_t>()));
+}
+
+// Tensor-parallel fusion arguments (lake_b200.parallel.tp builds the dict):
+// world, rank, rows_per_rank, m_rot, ag_cnt, ag_off, rs_recv[], rs_cnt[], done_cnt[], col_offset.
+void apply_tp(GemmArgs& g, const c10::optional<py::dict>& tp) {
+  if (!tp.has_value()) return;
+  const py::dict& d = *tp;
+  auto& t = g.tp;
+  t.world = d["world"].cast<int>();
+  TORCH_CHECK(t.world >= 1 && t.world <= lakeb::kMaxTP, "tp world out of range");
+  t.rank = d["rank"].cast<int>();
+  t.rows_per_rank = d["rows_per_rank"].cast<int>();
+  if (d.contains("m_rot")) t.m_rot = d["m_rot"].cast<int>();
+  if (d.contains("ag_cnt")) {
+    t.ag_cnt = ptr_of<const unsigned long long>(d["ag_cnt"]);
+    t.ag_off = d["ag_off"].cast<unsigned long long>();
+    if (d.contains("ag_all")) t.ag_all = d["ag_all"].cast<int>();
+  }
+  auto fill = [&](const char* key, auto* arr) {
+    if (!d.contains(key)) return;
+    py::list l = d[key];
+    TORCH_CHECK(static_cast<int>(l.size()) == t.world, key, " needs one pointer per rank");
+    using P = std::remove_reference_t<decltype(arr[0])>;  // element pointer type
+    for (int i = 0; i < t.world; ++i) arr[i] = reinterpret_cast<P>(static_cast<uintptr_t>(l[i].cast<int64_t>()));
+  };
+  fill("rs_recv", t.rs_recv);
+  fill("rs_cnt", t.rs_cnt);
+  fill("done_cnt", t.done_cnt);
+  if (d.contains("col_offset")) t.col_offset = d["col_offset"].cast<int>();
+}
+
 // out = a @ w.T  (bf16 out) or fp32 out
 void linear(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c10::optional<at::Tensor> status,
             int64_t max_ctas) {
@@ -102,8 +136,10 @@ void linear_residual(const at::Tensor& a, const at::Tensor& w, const at::Tensor&
 }
 
 // out[:, j] = silu(gate_j) * up_j with w rows interleaved per 256-row tile: [gate 128 | up 128]
-void linear_swiglu(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c10::optional<at::Tensor> status) {
+void linear_swiglu(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c10::optional<at::Tensor> status,
+                   c10::optional<py::dict> tp) {
   GemmArgs g = base_args(a, w);
+  apply_tp(g, tp);
   check_bf16_2d(out, "out");
   TORCH_CHECK(w.size(0) % 256 == 0, "gate_up rows must be a multiple of 256");
   TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) * 2 == w.size(0), "out shape");
@@ -118,8 +154,9 @@ void linear_swiglu(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c1
 void linear_qkv(const at::Tensor& a, const at::Tensor& w, at::Tensor& q_out, const at::Tensor& rope_cs,
                 const at::Tensor& positions, const at::Tensor& slots, const at::Tensor& arena, int64_t layer,
                 int64_t n_q_heads, int64_t n_kv_heads, c10::optional<at::Tensor> peer_arena,
-                c10::optional<at::Tensor> peer_slots, c10::optional<at::Tensor> status) {
+                c10::optional<at::Tensor> peer_slots, c10::optional<at::Tensor> status, c10::optional<py::dict> tp) {
   GemmArgs g = base_args(a, w);
+  apply_tp(g, tp);
   check_bf16_2d(q_out, "q_out");
   TORCH_CHECK(q_out.size(0) == a.size(0) && q_out.size(1) == n_q_heads * 128, "q_out shape");
   TORCH_CHECK(rope_cs.scalar_type() == at::kFloat && rope_cs.is_contiguous() && rope_cs.dim() == 3 &&
@@ -146,8 +183,9 @@ void linear_qkv(const at::Tensor& a, const at::Tensor& w, at::Tensor& q_out, con
 
 // amax[row] = packed (value, index) of the row's argmax of a @ w.T (bitmask-filtered).
 void linear_argmax(const at::Tensor& a, const at::Tensor& w, at::Tensor& amax, c10::optional<at::Tensor> bitmask,
-                   c10::optional<at::Tensor> status) {
+                   c10::optional<at::Tensor> status, c10::optional<py::dict> tp) {
   GemmArgs g = base_args(a, w);
+  apply_tp(g, tp);
   TORCH_CHECK(amax.scalar_type() == at::kLong && amax.numel() >= a.size(0) && amax.is_contiguous(), "amax int64");
   check_aligned(amax, "amax", 8);
   amax.zero_();
@@ -159,6 +197,65 @@ void linear_argmax(const at::Tensor& a, const at::Tensor& w, at::Tensor& amax, c
   }
   g.status = status_ptr(status);
   LAKEB_CHECK_RC(lakeb::gemm_bf16(g, lakeb::kEpiArgmax, cur_stream()), "linear_argmax");
+}
+
+// GEMM -> reduce-scatter: each partial row of a @ w.T goes to its owner rank's receive buffer.
+void linear_rs(const at::Tensor& a, const at::Tensor& w, const py::dict& tp, c10::optional<at::Tensor> status) {
+  GemmArgs g = base_args(a, w);
+  apply_tp(g, tp);
+  g.ldc = w.size(0);  // receive rows are dense [world][rows_per_rank][N]
+  g.status = status_ptr(status);
+  LAKEB_CHECK_RC(lakeb::gemm_bf16(g, lakeb::kEpiRSPush, cur_stream()), "linear_rs");
+}
+
+// Reduce-scatter completion + residual + RMSNorm + all-gather push (see tp_comm.cu).
+void tp_norm_push(at::Tensor& h, const at::Tensor& w, double eps, const py::dict& d, c10::optional<at::Tensor> status) {
+  check_bf16_2d(h, "h");
+  TORCH_CHECK(h.is_contiguous() && w.is_contiguous() && w.numel() == h.size(1), "h / w layout");
+  lakeb::TPNormArgs a;
+  a.world = d["world"].cast<int>();
+  a.rank = d["rank"].cast<int>();
+  a.rows_per_rank = d["rows_per_rank"].cast<int>();
+  TORCH_CHECK(h.size(0) >= a.rows_per_rank, "h has fewer rows than rows_per_rank");
+  a.dim = static_cast<int>(h.size(1));
+  a.h = bfm(h);
+  a.w = bf(w);
+  a.eps = static_cast<float>(eps);
+  if (d.contains("recv") && !d["recv"].is_none()) {
+    a.recv = ptr_of<const __nv_bfloat16>(d["recv"]);
+    a.rs_cnt = ptr_of<const unsigned long long>(d["rs_cnt"]);
+    a.rs_off = d["rs_off"].cast<unsigned long long>();
+  }
+  if (d.contains("store_h")) a.store_h = d["store_h"].cast<int>();
+  py::list dst = d["dst"];
+  py::list cnt = d["ag_cnt"];
+  TORCH_CHECK(static_cast<int>(dst.size()) == a.world && static_cast<int>(cnt.size()) == a.world, "per-rank lists");
+  for (int i = 0; i < a.world; ++i) {
+    a.dst[i] = ptr_of<__nv_bfloat16>(dst[i]);
+    a.ag_cnt[i] = ptr_of<unsigned long long>(cnt[i]);
+  }
+  a.dst_ld = d["dst_ld"].cast<int64_t>();
+  if (d.contains("row_map") && !d["row_map"].is_none()) a.row_map = ptr_of<const int>(d["row_map"]);
+  if (d.contains("reset_ptr") && !d["reset_ptr"].is_none()) {
+    a.reset_ptr = ptr_of<unsigned long long>(d["reset_ptr"]);
+    a.reset_n = d["reset_n"].cast<int>();
+  }
+  a.status = status_ptr(status);
+  LAKEB_CHECK_RC(lakeb::tp_norm_push(a, cur_stream()), "tp_norm_push");
+}
+
+void tp_argmax_combine(const std::vector<int64_t>& amax_ptrs, int64_t done_cnt, int64_t off, at::Tensor& out,
+                       int64_t n, c10::optional<at::Tensor> status) {
+  TORCH_CHECK(out.scalar_type() == at::kInt && out.is_cuda() && out.numel() >= n, "out int32");
+  lakeb::TPPtrs p;
+  TORCH_CHECK(amax_ptrs.size() >= 1 && amax_ptrs.size() <= static_cast<size_t>(lakeb::kMaxTP), "world");
+  for (size_t i = 0; i < amax_ptrs.size(); ++i)
+    p.p[i] = reinterpret_cast<const unsigned long long*>(static_cast<uintptr_t>(amax_ptrs[i]));
+  LAKEB_CHECK_RC(lakeb::tp_argmax_combine(p, static_cast<int>(amax_ptrs.size()),
+                                           reinterpret_cast<const unsigned long long*>(done_cnt), nullptr,
+                                           static_cast<unsigned long long>(off), out.data_ptr<int>(),
+                                           static_cast<int>(n), status_ptr(status), cur_stream()),
+                 "tp_argmax_combine");
 }
 
 PagedAttnArgs attn_args(const at::Tensor& q, at::Tensor& out, const at::Tensor& arena, int64_t layer,
@@ -399,13 +496,23 @@ PYBIND11_MODULE(_C, m) {
         py::arg("max_ctas") = 0);
   m.def("linear_residual", &linear_residual, py::arg("a"), py::arg("w"), py::arg("residual"), py::arg("out"),
         py::arg("status") = py::none());
-  m.def("linear_swiglu", &linear_swiglu, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("status") = py::none());
+  m.def("linear_swiglu", &linear_swiglu, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("status") = py::none(),
+        py::arg("tp") = py::none());
+  m.def("linear_rs", &linear_rs, py::arg("a"), py::arg("w"), py::arg("tp"), py::arg("status") = py::none());
+  m.def("tp_norm_push", &tp_norm_push, py::arg("h"), py::arg("w"), py::arg("eps"), py::arg("tp"),
+        py::arg("status") = py::none());
+  m.def("tp_argmax_combine", &tp_argmax_combine, py::arg("amax_ptrs"), py::arg("done_cnt"), py::arg("off"),
+        py::arg("out"), py::arg("n"), py::arg("status") = py::none());
+  m.def("gemm_grid", [](int64_t M, int64_t N, int64_t epi) {
+    return lakeb::gemm_grid(static_cast<int>(M), static_cast<int>(N), static_cast<int>(epi), 0);
+  });
+  m.def("tp_norm_grid", [](int64_t rows) { return lakeb::tp_norm_grid(static_cast<int>(rows)); });
   m.def("linear_qkv", &linear_qkv, py::arg("a"), py::arg("w"), py::arg("q_out"), py::arg("rope_cs"),
         py::arg("positions"), py::arg("slots"), py::arg("arena"), py::arg("layer"), py::arg("n_q_heads"),
         py::arg("n_kv_heads"), py::arg("peer_arena") = py::none(), py::arg("peer_slots") = py::none(),
-        py::arg("status") = py::none());
+        py::arg("status") = py::none(), py::arg("tp") = py::none());
   m.def("linear_argmax", &linear_argmax, py::arg("a"), py::arg("w"), py::arg("amax"), py::arg("bitmask") = py::none(),
-        py::arg("status") = py::none());
+        py::arg("status") = py::none(), py::arg("tp") = py::none());
   m.def("paged_decode", &paged_decode, py::arg("q"), py::arg("out"), py::arg("arena"), py::arg("layer"),
         py::arg("block_tables"), py::arg("seq_lens"), py::arg("n_q_heads"), py::arg("n_kv_heads"), py::arg("scale"),
         py::arg("splits") = 1, py::arg("ws_o") = py::none(), py::arg("ws_ml") = py::none(),

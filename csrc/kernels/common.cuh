@@ -89,6 +89,42 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// ---------------------------------------------------------------- cross-GPU flags
+// Counters live in device memory that peers map through CUDA IPC; writers
+// release at system scope after their data stores, readers acquire.
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_add_release_sys(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Wait until *cnt >= target. Returns false after the time bound (status gets
+// kErrTimeoutFlag) or when the CTA's abort flag is raised.
+__device__ __forceinline__ bool wait_counter(const unsigned long long* cnt, unsigned long long target,
+                                             volatile int* abort_flag, int* status,
+                                             uint64_t limit_ns = kWaitLimitNs) {
+  if (ld_acquire_sys(cnt) >= target) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_sys(cnt) >= target) return true;
+    __nanosleep(32);
+    if ((i & 15) == 0) {
+      if (abort_flag && *abort_flag) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        if (abort_flag) *abort_flag = 1;
+        record_error(status, kErrTimeoutFlag);
+        return false;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");

@@ -73,6 +73,13 @@ __device__ __forceinline__ __nv_bfloat16* kv_ptr(const KVArenaView& kv, int64_t 
          off * 128;
 }
 
+// Tile t -> (m-block, n-block): m fastest, rotated so the walk starts at tp.m_rot.
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int m_rot, int& m_blk, int& n_blk) {
+  n_blk = tile / num_m;
+  m_blk = tile - n_blk * num_m + m_rot;
+  if (m_blk >= num_m) m_blk -= num_m;
+}
+
 template <int BN, int STAGES, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -120,9 +127,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       bool ok = true;
+      // all-gather -> GEMM: A rows of a peer's shard are read only after its push landed
+      const bool ag = p.tp.ag_cnt != nullptr;
+      const unsigned long long ag_target = ag ? (p.tp.ag_base ? *p.tp.ag_base : 0ull) + p.tp.ag_off : 0ull;
+      uint32_t ready = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m_blk = tile % num_m;
-        const int n_blk = tile / num_m;
+        int m_blk, n_blk;
+        tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+        if (ag) {
+          const int r0 = m_blk * kBM;
+          const int r1 = min(p.M, r0 + kBM) - 1;
+          const int sh0 = p.tp.ag_all ? 0 : r0 / p.tp.rows_per_rank;
+          const int sh1 = p.tp.ag_all ? p.tp.world - 1 : r1 / p.tp.rows_per_rank;
+          for (int sh = sh0; sh <= sh1 && ok; ++sh) {
+            if ((ready >> sh) & 1u) continue;
+            ok = wait_counter(p.tp.ag_cnt + sh, ag_target, abort_flag, p.status);
+            ready |= 1u << sh;
+          }
+          if (!ok) break;
+          fence_proxy_async_global();  // peer stores (generic proxy) before this CTA's TMA reads
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) {
             ok = false;
@@ -187,8 +211,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row_in_tile = q * 32 + lane;
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
-      const int m_blk = tile % num_m;
-      const int n_blk = tile / num_m;
+      int m_blk, n_blk;
+      tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
       const int acc = t & 1;
       if (!mbar_wait(&tmem_full[acc], (t >> 1) & 1, abort_flag, p.status)) break;
       tc_fence_after();
@@ -220,6 +244,27 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
               store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
             }
+          }
+        }
+      } else if constexpr (EPI == kEpiRSPush) {
+        // partial sums of this rank's K-slice go straight to the row's owner (P2P stores over NVLink)
+        __nv_bfloat16* dst_row = nullptr;
+        if (row_ok) {
+          const int d = row / p.tp.rows_per_rank;
+          const int lr = row - d * p.tp.rows_per_rank;
+          dst_row = p.tp.rs_recv[d] + (static_cast<int64_t>(p.tp.rank) * p.tp.rows_per_rank + lr) * p.ldc;
+        }
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = n_blk * BN + c * 32;
+          if (row_ok && col0 < p.N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            store_bf16x32(dst_row + col0, v);
           }
         }
       } else if constexpr (EPI == kEpiSwiGLU) {
@@ -321,7 +366,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               if ((allow >> j) & 1u) {
                 const unsigned long long key =
                     (static_cast<unsigned long long>(float_order_key(__uint_as_float(r[j]))) << 32) |
-                    static_cast<unsigned long long>(0xFFFFFFFFu - static_cast<uint32_t>(col0 + j));
+                    static_cast<unsigned long long>(0xFFFFFFFFu -
+                                                    static_cast<uint32_t>(col0 + j + p.tp.col_offset));
                 best = key > best ? key : best;
               }
             }
@@ -332,6 +378,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(&tmem_empty[acc]);
     }
+    // Cross-GPU signal: this CTA's stores are visible system-wide before the counters move.
+    // (every epilogue thread reaches the named barrier; only a CTA that did not abort signals)
+    if (p.tp.rs_cnt[0] || p.tp.done_cnt[0]) {
+      __threadfence_system();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == 2 && lane == 0 && !*abort_flag) {
+        for (int d = 0; d < p.tp.world; ++d) {
+          if (p.tp.rs_cnt[d]) red_add_release_sys(p.tp.rs_cnt[d] + p.tp.rank, 1ull);
+          if (p.tp.done_cnt[d]) red_add_release_sys(p.tp.done_cnt[d] + p.tp.rank, 1ull);
+        }
+      }
+    }
   }
 
   __syncthreads();
@@ -339,6 +397,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, kTmemCols);
   }
+}
+
+int grid_for(int M, int N, int BN, int max_ctas) {
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + BN - 1) / BN);
+  int grid = max_ctas > 0 ? max_ctas : num_sms();
+  return grid > tiles ? tiles : grid;
 }
 
 template <int BN, int STAGES, int EPI>
@@ -354,17 +418,20 @@ int launch(const GemmArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + BN - 1) / BN);
-  int grid = a.max_ctas > 0 ? a.max_ctas : num_sms();
-  if (grid > tiles) grid = tiles;
-  kern<<<grid, kThreads, S::kAlloc, stream>>>(ma, mb, a);
+  kern<<<grid_for(a.M, a.N, BN, a.max_ctas), kThreads, S::kAlloc, stream>>>(ma, mb, a);
   return cudaGetLastError();
 }
 
+int bn_of(int epi) { return epi == kEpiQKV ? 128 : 256; }
+
 }  // namespace
+
+int gemm_grid(int M, int N, int epi, int max_ctas) { return grid_for(M, N, bn_of(epi), max_ctas); }
 
 int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
+  if (a.tp.ag_cnt && !a.tp.ag_all && (a.tp.rows_per_rank <= 0 || a.M > a.tp.world * a.tp.rows_per_rank)) return -6;
+  if (a.tp.ag_cnt && (a.tp.world < 1 || a.tp.world > kMaxTP)) return -6;
   if ((a.K % 8) || (a.lda % 8) || (a.ldb % 8) || (a.N % 32)) return -1;
   if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) return -2;
   switch (epi) {
@@ -381,6 +448,11 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
       return launch<256, 4, kEpiArgmax>(a, stream);
     case kEpiStoreF32:
       return launch<256, 4, kEpiStoreF32>(a, stream);
+    case kEpiRSPush:
+      if (a.tp.world < 1 || a.tp.world > kMaxTP || a.tp.rows_per_rank <= 0 ||
+          a.M != a.tp.world * a.tp.rows_per_rank)
+        return -5;
+      return launch<256, 4, kEpiRSPush>(a, stream);
     default:
       return -4;
   }

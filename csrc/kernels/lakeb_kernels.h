@@ -18,6 +18,32 @@ enum GemmEpi : int {
   kEpiQKV = 3,        // q -> C with RoPE; k (RoPE) and v -> paged KV arena (+ optional peer arena)
   kEpiArgmax = 4,     // per-row argmax (optionally bitmask-filtered) via 64-bit atomicMax
   kEpiStoreF32 = 5,   // C (fp32) = acc
+  kEpiRSPush = 6,     // partial rows -> owner rank's receive buffer over NVLink (GEMM + reduce-scatter)
+};
+
+constexpr int kMaxTP = 8;
+
+// Tensor-parallel fusion of a GEMM with the collective beside it. The residual
+// stream is split by rows: rank r owns rows [r*rows_per_rank, (r+1)*rows_per_rank).
+// Counters are monotonically increasing; a wait on counter c completes when
+// c >= (base ? *base : 0) + off. Every CTA of a signalling kernel adds 1 to the
+// counter slot of its rank at every destination rank.
+struct TPGemmArgs {
+  int world = 1, rank = 0;
+  int rows_per_rank = 0;
+  int m_rot = 0;  // m-block the tile walk starts at (own rows first for all-gather, peers' rows first for RS)
+  // all-gather -> GEMM: A rows of shard s are usable once ag_cnt[s] reaches the target
+  const unsigned long long* ag_cnt = nullptr;
+  const unsigned long long* ag_base = nullptr;
+  unsigned long long ag_off = 0;
+  int ag_all = 0;  // 1: wait for every shard before the first tile (rows not laid out by shard)
+  // GEMM -> reduce-scatter: partial row g goes to rank g / rows_per_rank at
+  // rs_recv[dst] + (rank * rows_per_rank + g % rows_per_rank) * ldc, then rs_cnt[dst][rank] += 1 per CTA
+  __nv_bfloat16* rs_recv[kMaxTP] = {};
+  unsigned long long* rs_cnt[kMaxTP] = {};
+  // completion signal of any epilogue (done_cnt[dst][rank] += 1 per CTA)
+  unsigned long long* done_cnt[kMaxTP] = {};
+  int col_offset = 0;  // global index of this rank's first output column (vocab-parallel argmax)
 };
 
 struct KVArenaView {
@@ -53,7 +79,11 @@ struct GemmArgs {
   int bitmask_words = 0;
   int* status = nullptr;               // device status word
   int max_ctas = 0;                    // 0 = number of SMs
+  TPGemmArgs tp;
 };
+
+// Number of CTAs gemm_bf16 launches for a shape (the per-call increment of TP counters).
+int gemm_grid(int M, int N, int epi, int max_ctas);
 
 // Returns 0 on success, otherwise a cudaError_t or negative argument error.
 int gemm_bf16(const GemmArgs& args, int epi, cudaStream_t stream);
@@ -107,6 +137,40 @@ int apply_bitmask_f32(float* logits, int64_t stride, int rows, int vocab, const 
                       cudaStream_t stream);
 int chain_reject(const int* draft, const int* draft_off, const int* target, const int* target_off, int* out,
                  int* out_len, int out_stride, int nreq, cudaStream_t stream);
+// ----------------------------------------------------------------- tensor parallel
+// Reduce-scatter completion + residual + RMSNorm + all-gather push, per owned row:
+//   h = h + sum_src recv[src][row]          (when recv != nullptr, after rs_cnt waits)
+//   y = rmsnorm(h) * w                      -> dst[d][row_map(global row)] for every rank d
+// then ag_cnt[d][rank] += 1 per CTA. rows_per_rank rows are owned; global row = rank*rows_per_rank + row.
+struct TPNormArgs {
+  int world = 1, rank = 0, rows_per_rank = 0, dim = 0;
+  const __nv_bfloat16* recv = nullptr;  // local [world][rows_per_rank][dim]
+  const unsigned long long* rs_cnt = nullptr;
+  const unsigned long long* rs_base = nullptr;
+  unsigned long long rs_off = 0;
+  __nv_bfloat16* h = nullptr;  // local [rows_per_rank][dim]
+  int store_h = 1;
+  const __nv_bfloat16* w = nullptr;
+  float eps = 1e-5f;
+  __nv_bfloat16* dst[kMaxTP] = {};
+  int64_t dst_ld = 0;
+  const int* row_map = nullptr;  // [world*rows_per_rank] destination row or -1; null = identity
+  unsigned long long* ag_cnt[kMaxTP] = {};
+  unsigned long long* reset_ptr = nullptr;  // zeroed by block 0 before signalling (local array)
+  int reset_n = 0;
+  int* status = nullptr;
+};
+int tp_norm_push(const TPNormArgs& a, cudaStream_t stream);
+int tp_norm_grid(int rows_per_rank);
+
+// Vocab-parallel argmax combine: waits done_cnt[src] targets, token[r] = argmax over ranks of amax[d][r].
+struct TPPtrs {
+  const unsigned long long* p[kMaxTP] = {};
+};
+int tp_argmax_combine(const TPPtrs& amax, int world, const unsigned long long* done_cnt,
+                      const unsigned long long* base, unsigned long long off, int* out, int n, int* status,
+                      cudaStream_t stream);
+
 int page_copy(const void* src, void* dst, const int64_t* src_ids, const int64_t* dst_ids, int n, int64_t page_bytes,
               int64_t sub_off, int64_t sub_bytes, cudaStream_t stream);
 

@@ -43,6 +43,9 @@ class EngineConfig:
     # Arena other processes can map: a /dev/shm file on the CPU path, its own IPC-exportable
     # cudaMalloc allocation on the GPU (decode instances of PD-split)
     shared_arena: bool = False
+    # Tensor parallel: (rank, world, process group for the handle exchange); every rank of the
+    # group runs an engine with the same requests and makes the same scheduling decisions.
+    tp: tuple | None = None
 
 
 @dataclass
@@ -56,6 +59,13 @@ def alloc_arena(cfg: ModelConfig, num_blocks: int, device, dtype, block_size: in
     """Page-first KV arena [num_blocks, layers, 2, kv_heads, block_size, head_dim] (zero-filled)."""
     return torch.zeros(num_blocks, cfg.n_layers, 2, cfg.n_kv_heads, block_size, cfg.head_dim, dtype=dtype,
                        device=device)
+
+
+def _local_kv_cfg(cfg: ModelConfig, world: int) -> ModelConfig:
+    """The per-rank view of a tensor-parallel model's KV geometry."""
+    import dataclasses
+
+    return dataclasses.replace(cfg, n_kv_heads=cfg.n_kv_heads // world, n_q_heads=cfg.n_q_heads // world)
 
 
 def page_bytes(cfg: ModelConfig, block_size: int = 16, elem: int = 2) -> int:
@@ -72,9 +82,23 @@ class LLMEngine:
         dtype = torch.float32 if self.device.type == "cpu" else torch.bfloat16
         if self.device.type == "cuda":
             torch.cuda.set_device(self.device)
-        self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed)
         maxb = (ec.max_model_len + ec.block_size - 1) // ec.block_size
         max_tokens = ec.max_batched_tokens + ec.max_running
+        self.tp_world = 1
+        if ec.tp is not None and ec.tp[1] > 1:
+            from ..models.llama_tp import TPDecoderLM
+            from ..parallel.tp import TPGroup
+
+            rank, world, pg = ec.tp
+            self.tp_world = world
+            max_tokens += world  # rows padded to a multiple of the group size
+            self.tp_group = TPGroup(rank, world, self.device, max_tokens, cfg.hidden, ec.max_running, group=pg,
+                                    status=None)
+            self.model = TPDecoderLM(cfg, self.tp_group, self.device, seed=ec.seed)
+            cfg = self._arena_cfg = _local_kv_cfg(cfg, world)
+        else:
+            self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed)
+            self._arena_cfg = cfg
         num_blocks = ec.num_blocks
         if not num_blocks:
             if self.device.type == "cuda":
@@ -87,6 +111,7 @@ class LLMEngine:
                 num_blocks = 256
         self.arena_path = None
         shape = (num_blocks, cfg.n_layers, 2, cfg.n_kv_heads, ec.block_size, cfg.head_dim)
+        cfg = self.cfg
         if ec.shared_arena and self.device.type == "cpu":
             from ..parallel.peer import alloc_shared_cpu_arena
 
@@ -96,12 +121,12 @@ class LLMEngine:
 
             self.arena = alloc_ipc_arena(shape, dtype, self.device)
         else:
-            self.arena = alloc_arena(cfg, num_blocks, self.device, dtype, ec.block_size)
+            self.arena = torch.zeros(shape, dtype=dtype, device=self.device)
         self.pool = BlockPool(num_blocks, ec.block_size, ec.enable_prefix_cache)
         self.scheduler = Scheduler(self.pool, SchedulerConfig(ec.max_running, ec.max_batched_tokens,
                                                               ec.long_prefill_threshold, ec.max_model_len, maxb))
-        self.runner = ModelRunner(self.model, self.arena, max_tokens, ec.max_running, maxb, ec.use_cuda_graphs,
-                                  ec.block_size)
+        self.runner = ModelRunner(self.model, self.arena, max_tokens, ec.max_running, maxb,
+                                  ec.use_cuda_graphs and self.tp_world == 1, ec.block_size, row_multiple=self.tp_world)
         self.requests: dict[str, Request] = {}
         self.pool_iface = None  # PoolIface (storage-pool fences), attached by attach_pool
         self._ids = itertools.count()
@@ -192,7 +217,7 @@ class LLMEngine:
 
         dev = self.arena.device
         ops.page_copy(self.arena, self.runner.peer_arena, torch.tensor(src, device=dev),
-                      torch.tensor(dst, device=dev), page_bytes(self.cfg, self.ec.block_size,
+                      torch.tensor(dst, device=dev), page_bytes(self._arena_cfg, self.ec.block_size,
                                                                 self.arena.element_size()))
 
     def has_unfinished(self) -> bool:

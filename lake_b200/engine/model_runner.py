@@ -29,7 +29,7 @@ GRAPH_BUCKETS = [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 32
 
 class ModelRunner:
     def __init__(self, model: DecoderLM, arena: torch.Tensor, max_tokens: int, max_seqs: int,
-                 max_blocks_per_seq: int, use_cuda_graphs: bool = True, block_size: int = 16):
+                 max_blocks_per_seq: int, use_cuda_graphs: bool = True, block_size: int = 16, row_multiple: int = 1):
         self.model = model
         self.arena = arena
         self.device = model.device
@@ -38,11 +38,12 @@ class ModelRunner:
         self.max_seqs = max_seqs
         self.maxb = max_blocks_per_seq
         self.bs = block_size
+        self.row_multiple = row_multiple  # tensor parallel: rows padded to a multiple of the group size
         self.vocab_words = (model.cfg.vocab + 31) // 32
         cfg = model.cfg
         self.max_splits = 1
         if self.cuda:
-            self.max_splits = max(ops.decode_splits(n, cfg.n_kv_heads, max_blocks_per_seq)
+            self.max_splits = max(ops.decode_splits(n, cfg.n_kv_heads // row_multiple, max_blocks_per_seq)
                                   for n in range(1, max_seqs + 1))
         self.ws = model.new_workspace(max_tokens, max_seqs, max_seqs, self.max_splits)
         # int32 staging: ids | pos | seq_lens | qstart | tiles | block_tables
@@ -164,6 +165,13 @@ class ModelRunner:
                     row += 1
                     s += 1
         qst[s] = row
+        pad = -row % self.row_multiple
+        if pad:  # rows outside every sequence: no KV write, never sampled
+            ids[row:row + pad] = 0
+            pos[row:row + pad] = 0
+            slots[row:row + pad] = -1
+            pslots[row:row + pad] = -1
+            row += pad
         return row, s, ntiles, nrows, nd if not pad_decode_to else max(nd, pad_decode_to)
 
     def _h2d(self, t: int, s: int, nrows: int):
@@ -190,7 +198,7 @@ class ModelRunner:
     def _splits(self, nd: int) -> int:
         if not self.cuda or nd == 0:
             return 1
-        return ops.decode_splits(nd, self.model.cfg.n_kv_heads, self.maxb)
+        return ops.decode_splits(nd, self.model.cfg.n_kv_heads // self.row_multiple, self.maxb)
 
     def _get_graph(self, bucket: int):
         g = self.graphs.get(bucket)
