@@ -45,6 +45,7 @@ class BlockPool:
         self.block_of: dict[bytes, int] = {}
         self.evictable: OrderedDict[int, None] = OrderedDict()
         self.stats = {"hits": 0, "queries": 0, "evictions": 0}
+        self.on_evict = None  # callback(block, hash) before a cached page is handed out again
 
     # -------------------------------------------------------------- queries
     @property
@@ -67,6 +68,8 @@ class BlockPool:
                 h = self.hash_of.pop(b, None)
                 if h is not None and self.block_of.get(h) == b:
                     del self.block_of[h]
+                if h is not None and self.on_evict is not None:
+                    self.on_evict(b, h)
                 self.stats["evictions"] += 1
             self.ref[b] = 1
             out.append(b)

@@ -1,0 +1,151 @@
+"""L1 (pinned host DRAM) tier under the engine's HBM prefix cache.
+
+D -> pool: when a request finishes, every full page of its KV (prompt and
+decode-extended tokens) that the pool does not hold yet is copied device ->
+pinned host on a side stream (one cudaMemcpyAsync per page: pages are
+contiguous in the page-first arena), ordered after the step that produced it
+by an event. Pages stay resident in HBM as prefix cache.
+
+pool -> P: when a request arrives, prompt pages missing from HBM but present
+in L1 are copied host -> device into fresh pages on the same side stream and
+registered in the engine's prefix cache; the compute stream waits for that
+stream before the next step, so admission reuses them instead of recomputing.
+
+HBM eviction: before the block pool hands out a cached page again, the
+compute stream waits for that page's write-behind copy (if still in flight).
+L1 itself is an LRU over pinned slots; its evictions are counted.
+
+Reference parity: the L0<->L1 promote/demote path of
+rust/tiered-store/src/engine.rs:495-606 and the SGLang-style host cache the
+reference's engine targets (python/lake/engine/agent.py:15-41 contract).
+"""
+from __future__ import annotations
+
+import time
+from collections import OrderedDict
+
+import torch
+
+from ...engine.block_pool import chain_block_hashes
+from ..types import FinishRequest, PreparePlan, ReadyHandle, StepStats
+
+
+class HostCacheAgent:
+    def __init__(self, engine, l1_blocks: int, node_id: str = "node-0"):
+        self.eng = engine
+        self.node_id = node_id
+        self.bs = engine.ec.block_size
+        arena = engine.arena
+        self.page_elems = arena[0].numel()
+        cuda = arena.is_cuda
+        self.l1 = torch.empty(l1_blocks, self.page_elems, dtype=arena.dtype, pin_memory=cuda)
+        self.slot_of: OrderedDict[bytes, int] = OrderedDict()  # LRU: oldest first
+        self.free_slots = list(range(l1_blocks - 1, -1, -1))
+        self.pending: dict[int, torch.cuda.Event] = {}  # device page -> write-behind copy event
+        self.stream = torch.cuda.Stream(arena.device) if cuda else None
+        self.stats = {"writeback_blocks": 0, "promoted_blocks": 0, "l1_evictions": 0, "evict_waits": 0,
+                      "writeback_ms": 0.0, "promote_ms": 0.0}
+        engine.pool.on_evict = self._on_evict
+        self._ready: int | None = None
+
+    # ------------------------------------------------------------ L1 slots
+    def _slot_for(self, h: bytes) -> int:
+        s = self.slot_of.get(h)
+        if s is not None:
+            self.slot_of.move_to_end(h)
+            return s
+        if self.free_slots:
+            s = self.free_slots.pop()
+        else:
+            _, s = self.slot_of.popitem(last=False)
+            self.stats["l1_evictions"] += 1
+        self.slot_of[h] = s
+        return s
+
+    def _page(self, page: int) -> torch.Tensor:
+        return self.eng.arena[page].view(-1)
+
+    def _on_evict(self, page: int, h: bytes) -> None:
+        ev = self.pending.pop(page, None)
+        if ev is not None and not ev.query():
+            torch.cuda.current_stream(self.eng.arena.device).wait_event(ev)
+            self.stats["evict_waits"] += 1
+
+    # ------------------------------------------------------------ D -> pool
+    def on_request_finished(self, finish: FinishRequest) -> None:
+        req = self.eng.requests.get(finish.req_id)
+        if req is None:
+            return
+        t0 = time.perf_counter()
+        toks = req.all_tokens
+        n_full = min(req.num_computed, len(toks)) // self.bs
+        hashes = chain_block_hashes(toks[: n_full * self.bs], self.bs, full_only=True)
+        pages = req.meta.get("final_block_ids") or req.block_ids
+        todo = [(h, p) for h, p in zip(hashes, pages) if h not in self.slot_of]
+        if not todo:
+            return
+        if self.stream is None:
+            for h, p in todo:
+                self.l1[self._slot_for(h)].copy_(self._page(p))
+        else:
+            dev = self.eng.arena.device
+            produced = torch.cuda.current_stream(dev).record_event()
+            self.stream.wait_event(produced)
+            with torch.cuda.stream(self.stream):
+                for h, p in todo:
+                    self.l1[self._slot_for(h)].copy_(self._page(p), non_blocking=True)
+                ev = self.stream.record_event()
+            for _, p in todo:
+                self.pending[p] = ev
+        self.stats["writeback_blocks"] += len(todo)
+        self.stats["writeback_ms"] += (time.perf_counter() - t0) * 1000
+
+    # ------------------------------------------------------------ pool -> P
+    def prefetch(self, req) -> int:
+        t0 = time.perf_counter()
+        pool = self.eng.pool
+        usable = max(0, (len(req.prompt) - 1) // self.bs)  # the last prompt token is always computed
+        hashes = chain_block_hashes(req.prompt[: usable * self.bs], self.bs, full_only=True)
+        n_local = pool.peek(hashes)
+        todo = []
+        for h in hashes[n_local:]:
+            s = self.slot_of.get(h)
+            if s is None or not pool.can_alloc(1):
+                break
+            page = pool.alloc(1)[0]
+            self.slot_of.move_to_end(h)
+            todo.append((h, s, page))
+        if not todo:
+            return 0
+        if self.stream is None:
+            for h, s, page in todo:
+                self._page(page).copy_(self.l1[s])
+        else:
+            dev = self.eng.arena.device
+            self.stream.wait_event(torch.cuda.current_stream(dev).record_event())
+            with torch.cuda.stream(self.stream):
+                for h, s, page in todo:
+                    self._page(page).copy_(self.l1[s], non_blocking=True)
+            torch.cuda.current_stream(dev).wait_stream(self.stream)
+        for h, s, page in todo:
+            pool.register(page, h)
+            pool.release([page])  # resident and cached; admission takes its own reference
+        self.stats["promoted_blocks"] += len(todo)
+        self.stats["promote_ms"] += (time.perf_counter() - t0) * 1000
+        return len(todo)
+
+    # ------------------------------------------------------------ fences (pages are the engine's)
+    def prepare_step(self, plan: PreparePlan) -> ReadyHandle:
+        self._ready = plan.step_id
+        stats = {io.req_id: StepStats() for io in plan.write_set}
+        return ReadyHandle(plan.step_id, stats, list(plan.read_set), list(plan.write_set), {}, {})
+
+    def done(self, step_id: int) -> None:
+        self._ready = None
+
+    def commit_write_extent(self, req_id: str, token_end: int) -> None:
+        return None
+
+    @property
+    def l1_len(self) -> int:
+        return len(self.slot_of)

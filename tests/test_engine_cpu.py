@@ -2,6 +2,8 @@
 2-layer fp32 plumbing model against the dense oracle."""
 import random
 
+import numpy as np
+
 import pytest
 import torch
 
@@ -125,3 +127,28 @@ def test_plumbing_logits_close():
     logits = eng.model.forward(b, eng.arena, eng.runner.ws)
     want = dense_logits(eng.model, prompt)[-1]
     assert torch.allclose(logits[0], want, atol=1e-4, rtol=1e-4)
+
+
+def test_host_cache_agent_writeback_and_promote():
+    """L1 host tier: finished pages are written behind, evicted from HBM by other
+    traffic, promoted back on reuse; tokens match an engine without the tier."""
+    from lake_b200.pool.agents.hostcache import HostCacheAgent
+    from lake_b200.pool.pool_iface import PoolIface
+
+    rng = np.random.default_rng(3)
+    sys_prompt = rng.integers(0, 1024, 96).tolist()
+    first = sys_prompt + rng.integers(0, 1024, 20).tolist()
+    others = [rng.integers(0, 1024, 100).tolist() for _ in range(3)]
+    eng = LLMEngine("tiny", device="cpu", max_running=2, max_batched_tokens=128, max_model_len=512, num_blocks=20)
+    agent = HostCacheAgent(eng, l1_blocks=64)
+    eng.attach_pool(PoolIface(agent))
+    out1 = eng.generate([first], max_new_tokens=6)[0]
+    assert agent.stats["writeback_blocks"] >= 7
+    for p in others:  # push the first request's pages out of the 20-page HBM pool
+        eng.generate([p], max_new_tokens=2)
+    assert eng.pool.stats["evictions"] > 0
+    follow = first + out1 + rng.integers(0, 1024, 10).tolist()
+    got = eng.generate([follow], max_new_tokens=4)[0]
+    assert agent.stats["promoted_blocks"] >= 6
+    ref = LLMEngine("tiny", device="cpu", max_running=2, max_batched_tokens=128, max_model_len=512, num_blocks=64)
+    assert got == ref.generate([follow], max_new_tokens=4)[0]
