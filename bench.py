@@ -354,6 +354,16 @@ def run_pd(args, rank, world, local, group, barrier):
     return w, role
 
 
+def _model_desc(name):
+    from lake_b200.models.config import get_config
+
+    c = get_config(name)
+    desc = {"llama3-8b": "Llama-3-8B", "llama3-70b": "Llama-3-70B", "mixtral-8x7b": "Mixtral-8x7B"}.get(name, name)
+    moe = f", {c.n_experts} experts top-{c.top_k}" if c.n_experts else ""
+    return (f"{desc} architecture ({c.n_layers} layers, hidden {c.hidden}, {c.n_q_heads}q/{c.n_kv_heads}kv heads, "
+            f"FFN {c.intermediate}{moe}, vocab {c.vocab})")
+
+
 def main():
     args = parse()
     if args.impl == "reference":
@@ -432,8 +442,7 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform random token ids, random-init weights)",
-            "config": {"model": "Llama-3-8B architecture (32 layers, hidden 4096, 32q/8kv heads, FFN 14336, "
-                                "vocab 128256)",
+            "config": {"model": _model_desc(args.model),
                        "global_batch": args.running * (world // 2 if mode == "pd" else world // args.tp),
                        "seq_len": args.input_len + args.output_len, "input_len": args.input_len,
                        "output_len": args.output_len, "parallelism": par, "mode": mode,

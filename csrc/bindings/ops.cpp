@@ -258,6 +258,99 @@ void tp_argmax_combine(const std::vector<int64_t>& amax_ptrs, int64_t done_cnt, 
                  "tp_argmax_combine");
 }
 
+// Grouped expert GEMM over gathered rows: w is [groups, N, K]; rows of group g are
+// a[g*group_rows, g*group_rows + group_count[g]). epi: swiglu (out [groups*group_rows, N/2])
+// or scatter (each row to dst_ptrs[row_rank[row] or 0] + row_slot[row]*N).
+void gemm_grouped(const at::Tensor& a, const at::Tensor& w, c10::optional<at::Tensor> out, int64_t epi,
+                  const at::Tensor& group_count, int64_t group_rows, c10::optional<at::Tensor> row_slot,
+                  c10::optional<at::Tensor> row_rank, std::vector<int64_t> dst_ptrs, c10::optional<py::dict> tp,
+                  c10::optional<at::Tensor> status) {
+  TORCH_CHECK(w.dim() == 3 && w.is_contiguous() && w.scalar_type() == at::kBFloat16, "w must be [G, N, K] bf16");
+  const int64_t G = w.size(0), N = w.size(1), K = w.size(2);
+  at::Tensor w2 = w.view({G * N, K});
+  GemmArgs g = base_args(a, w2);
+  g.N = static_cast<int>(N);
+  g.groups = static_cast<int>(G);
+  g.group_rows = static_cast<int>(group_rows);
+  TORCH_CHECK(group_count.scalar_type() == at::kInt && group_count.numel() >= G, "group_count int32 [G]");
+  g.group_count = group_count.data_ptr<int>();
+  TORCH_CHECK(a.size(0) == G * group_rows, "a must have groups*group_rows rows");
+  apply_tp(g, tp);
+  if (epi == lakeb::kEpiSwiGLU) {
+    TORCH_CHECK(out.has_value(), "out required");
+    check_bf16_2d(*out, "out");
+    TORCH_CHECK(out->size(0) == a.size(0) && out->size(1) * 2 == N && N % 256 == 0, "out shape");
+    g.C = out->data_ptr();
+    g.ldc = out->stride(0);
+  } else if (epi == lakeb::kEpiScatter) {
+    TORCH_CHECK(row_slot.has_value() && row_slot->scalar_type() == at::kInt, "row_slot int32");
+    g.row_slot = row_slot->data_ptr<int>();
+    if (row_rank.has_value()) g.row_rank = row_rank->data_ptr<int>();
+    TORCH_CHECK(!dst_ptrs.empty() && dst_ptrs.size() <= static_cast<size_t>(lakeb::kMaxTP), "dst_ptrs");
+    for (size_t i = 0; i < dst_ptrs.size(); ++i)
+      g.tp.rs_recv[i] = reinterpret_cast<__nv_bfloat16*>(static_cast<uintptr_t>(dst_ptrs[i]));
+    g.ldc = N;
+  } else {
+    TORCH_CHECK(false, "gemm_grouped: epi must be swiglu or scatter");
+  }
+  g.status = status_ptr(status);
+  LAKEB_CHECK_RC(lakeb::gemm_bf16(g, static_cast<int>(epi), cur_stream()), "gemm_grouped");
+}
+
+// Router top-k + gather into expert segments (+ all-to-all dispatch over NVLink when world > 1).
+void moe_dispatch(const at::Tensor& logits, const at::Tensor& x, at::Tensor& weights, int64_t n_experts,
+                  int64_t top_k, int64_t cap, int64_t world, int64_t rank, std::vector<int64_t> gathered,
+                  std::vector<int64_t> row_slot, std::vector<int64_t> row_rank, std::vector<int64_t> count,
+                  std::vector<int64_t> done_cnt, c10::optional<at::Tensor> status) {
+  TORCH_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1, "logits fp32 2-D");
+  check_bf16_2d(x, "x");
+  TORCH_CHECK(x.is_contiguous() && weights.scalar_type() == at::kFloat && weights.is_contiguous(), "x / weights");
+  lakeb::MoEDispatchArgs a;
+  a.logits = logits.data_ptr<float>();
+  a.ld_logits = static_cast<int>(logits.stride(0));
+  a.x = bf(x);
+  a.M = static_cast<int>(x.size(0));
+  a.dim = static_cast<int>(x.size(1));
+  a.n_experts = static_cast<int>(n_experts);
+  a.top_k = static_cast<int>(top_k);
+  a.cap = static_cast<int>(cap);
+  a.weights = weights.data_ptr<float>();
+  a.world = static_cast<int>(world);
+  a.rank = static_cast<int>(rank);
+  a.experts_per_rank = static_cast<int>(n_experts / world);
+  auto P = [](int64_t v) { return static_cast<uintptr_t>(v); };
+  TORCH_CHECK(static_cast<int64_t>(gathered.size()) == world && static_cast<int64_t>(count.size()) == world &&
+                  static_cast<int64_t>(row_slot.size()) == world, "per-rank pointer lists");
+  for (int i = 0; i < world; ++i) {
+    a.gathered[i] = reinterpret_cast<__nv_bfloat16*>(P(gathered[i]));
+    a.row_slot[i] = reinterpret_cast<int*>(P(row_slot[i]));
+    a.row_rank[i] = row_rank.empty() ? nullptr : reinterpret_cast<int*>(P(row_rank[i]));
+    a.count[i] = reinterpret_cast<int*>(P(count[i]));
+    a.done_cnt[i] = done_cnt.empty() ? nullptr : reinterpret_cast<unsigned long long*>(P(done_cnt[i]));
+  }
+  a.status = status_ptr(status);
+  LAKEB_CHECK_RC(lakeb::moe_dispatch(a, cur_stream()), "moe_dispatch");
+}
+
+void moe_combine(at::Tensor& h, const at::Tensor& comb, const at::Tensor& weights, int64_t top_k, int64_t wait_cnt,
+                 int64_t wait_n, int64_t target, c10::optional<at::Tensor> status) {
+  check_bf16_2d(h, "h");
+  TORCH_CHECK(h.is_contiguous() && comb.is_contiguous() && comb.scalar_type() == at::kBFloat16, "layouts");
+  LAKEB_CHECK_RC(lakeb::moe_combine(bfm(h), bf(comb), weights.data_ptr<float>(), static_cast<int>(h.size(0)),
+                                     static_cast<int>(h.size(1)), static_cast<int>(top_k),
+                                     reinterpret_cast<const unsigned long long*>(static_cast<uintptr_t>(wait_cnt)),
+                                     static_cast<int>(wait_n), static_cast<unsigned long long>(target),
+                                     status_ptr(status), cur_stream()),
+                 "moe_combine");
+}
+
+void wait_counters(int64_t cnt, int64_t n, int64_t target, c10::optional<at::Tensor> status) {
+  LAKEB_CHECK_RC(lakeb::wait_counters(reinterpret_cast<const unsigned long long*>(static_cast<uintptr_t>(cnt)),
+                                       static_cast<int>(n), static_cast<unsigned long long>(target),
+                                       status_ptr(status), cur_stream()),
+                 "wait_counters");
+}
+
 PagedAttnArgs attn_args(const at::Tensor& q, at::Tensor& out, const at::Tensor& arena, int64_t layer,
                         const at::Tensor& block_tables, const at::Tensor& seq_lens, int64_t n_q_heads,
                         int64_t n_kv_heads, double scale, c10::optional<at::Tensor> status) {
@@ -503,6 +596,18 @@ PYBIND11_MODULE(_C, m) {
         py::arg("status") = py::none());
   m.def("tp_argmax_combine", &tp_argmax_combine, py::arg("amax_ptrs"), py::arg("done_cnt"), py::arg("off"),
         py::arg("out"), py::arg("n"), py::arg("status") = py::none());
+  m.def("gemm_grouped", &gemm_grouped, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("epi"),
+        py::arg("group_count"), py::arg("group_rows"), py::arg("row_slot") = py::none(),
+        py::arg("row_rank") = py::none(), py::arg("dst_ptrs") = std::vector<int64_t>{}, py::arg("tp") = py::none(),
+        py::arg("status") = py::none());
+  m.def("moe_dispatch", &moe_dispatch, py::arg("logits"), py::arg("x"), py::arg("weights"), py::arg("n_experts"),
+        py::arg("top_k"), py::arg("cap"), py::arg("world"), py::arg("rank"), py::arg("gathered"), py::arg("row_slot"),
+        py::arg("row_rank"), py::arg("count"), py::arg("done_cnt"), py::arg("status") = py::none());
+  m.def("moe_combine", &moe_combine, py::arg("h"), py::arg("comb"), py::arg("weights"), py::arg("top_k"),
+        py::arg("wait_cnt") = 0, py::arg("wait_n") = 0, py::arg("target") = 0, py::arg("status") = py::none());
+  m.def("wait_counters", &wait_counters, py::arg("cnt"), py::arg("n"), py::arg("target"),
+        py::arg("status") = py::none());
+  m.def("moe_dispatch_grid", []() { return lakeb::kMoEDispatchGrid; });
   m.def("gemm_grid", [](int64_t M, int64_t N, int64_t epi) {
     return lakeb::gemm_grid(static_cast<int>(M), static_cast<int>(N), static_cast<int>(epi), 0);
   });

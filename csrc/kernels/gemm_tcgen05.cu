@@ -74,10 +74,22 @@ __device__ __forceinline__ __nv_bfloat16* kv_ptr(const KVArenaView& kv, int64_t 
 }
 
 // Tile t -> (m-block, n-block): m fastest, rotated so the walk starts at tp.m_rot.
+// For a grouped GEMM the m-blocks of all groups are enumerated together
+// (group-major), so m_blk indexes A rows directly.
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int m_rot, int& m_blk, int& n_blk) {
   n_blk = tile / num_m;
   m_blk = tile - n_blk * num_m + m_rot;
   if (m_blk >= num_m) m_blk -= num_m;
+}
+
+// Grouped GEMM: is this m-block inside its group's valid rows? (always true otherwise)
+__device__ __forceinline__ bool tile_live(const GemmArgs& p, int m_blk, int num_m_group, int& group) {
+  if (!p.groups) {
+    group = 0;
+    return true;
+  }
+  group = m_blk / num_m_group;
+  return (m_blk - group * num_m_group) * 128 < __ldg(p.group_count + group);
 }
 
 template <int BN, int STAGES, int EPI>
@@ -97,6 +109,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int num_m = (p.M + kBM - 1) / kBM;
+  const int num_m_group = p.groups ? p.group_rows / kBM : num_m;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
   const int num_kb = (p.K + kBK - 1) / kBK;
@@ -129,11 +142,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       // all-gather -> GEMM: A rows of a peer's shard are read only after its push landed
       const bool ag = p.tp.ag_cnt != nullptr;
+      if (p.groups) fence_proxy_async_global();  // rows other GPUs stored (expert dispatch) before TMA reads
       const unsigned long long ag_target = ag ? (p.tp.ag_base ? *p.tp.ag_base : 0ull) + p.tp.ag_off : 0ull;
       uint32_t ready = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        int m_blk, n_blk;
+        int m_blk, n_blk, grp;
         tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+        if (!tile_live(p, m_blk, num_m_group, grp)) continue;
         if (ag) {
           const int r0 = m_blk * kBM;
           const int r1 = min(p.M, r0 + kBM) - 1;
@@ -156,7 +171,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + S::kABytes;
           mbar_expect_tx(&full[stage], S::kStageBytes);
           tma_load_2d(sa, &tmA, &full[stage], kb * kBK, m_blk * kBM);
-          tma_load_2d(sb, &tmB, &full[stage], kb * kBK, n_blk * BN);
+          tma_load_2d(sb, &tmB, &full[stage], kb * kBK, grp * p.N + n_blk * BN);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -175,7 +190,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       int t = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++t) {
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        {
+          int m_blk, n_blk, grp;
+          tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+          if (!tile_live(p, m_blk, num_m_group, grp)) continue;
+        }
         const int acc = t & 1;
         const uint32_t acc_phase = (t >> 1) & 1;
         if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, p.status)) break;
@@ -203,6 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
         umma_commit(&tmem_full[acc]);
+        ++t;
       }
     }
   } else {
@@ -210,15 +231,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     int t = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++t) {
-      int m_blk, n_blk;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int m_blk, n_blk, grp;
       tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+      if (!tile_live(p, m_blk, num_m_group, grp)) continue;
       const int acc = t & 1;
-      if (!mbar_wait(&tmem_full[acc], (t >> 1) & 1, abort_flag, p.status)) break;
+      const uint32_t acc_phase = (t >> 1) & 1;
+      ++t;
+      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, p.status)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
       const int row = m_blk * kBM + row_in_tile;
-      const bool row_ok = row < p.M;
+      const bool row_ok = row < p.M && (!p.groups || row - grp * p.group_rows < __ldg(p.group_count + grp));
 
       if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32) {
 #pragma unroll 1
@@ -261,6 +285,26 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           const int col0 = n_blk * BN + c * 32;
           if (row_ok && col0 < p.N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            store_bf16x32(dst_row + col0, v);
+          }
+        }
+      } else if constexpr (EPI == kEpiScatter) {
+        // indirect row store: the token slot this gathered row came from (local or a peer's buffer)
+        __nv_bfloat16* dst_row = nullptr;
+        if (row_ok) {
+          const int slot = p.row_slot[row];
+          if (slot >= 0) dst_row = p.tp.rs_recv[p.row_rank ? p.row_rank[row] : 0] + static_cast<int64_t>(slot) * p.ldc;
+        }
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = n_blk * BN + c * 32;
+          if (dst_row && col0 < p.N) {
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
@@ -410,7 +454,7 @@ int launch(const GemmArgs& a, cudaStream_t stream) {
   using S = GemmSmem<BN, STAGES>;
   CUtensorMap ma, mb;
   if (!make_bf16_map(&ma, a.A, a.M, a.K, a.lda, kBM)) return -10;
-  if (!make_bf16_map(&mb, a.B, a.N, a.K, a.ldb, BN)) return -11;
+  if (!make_bf16_map(&mb, a.B, static_cast<int64_t>(a.N) * (a.groups ? a.groups : 1), a.K, a.ldb, BN)) return -11;
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
   static bool attr = false;
   if (!attr) {
@@ -432,6 +476,7 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
   if (a.tp.ag_cnt && !a.tp.ag_all && (a.tp.rows_per_rank <= 0 || a.M > a.tp.world * a.tp.rows_per_rank)) return -6;
   if (a.tp.ag_cnt && (a.tp.world < 1 || a.tp.world > kMaxTP)) return -6;
+  if (a.groups && (a.group_rows % kBM || !a.group_count || a.M != a.groups * a.group_rows)) return -8;
   if ((a.K % 8) || (a.lda % 8) || (a.ldb % 8) || (a.N % 32)) return -1;
   if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) return -2;
   switch (epi) {
@@ -448,6 +493,9 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
       return launch<256, 4, kEpiArgmax>(a, stream);
     case kEpiStoreF32:
       return launch<256, 4, kEpiStoreF32>(a, stream);
+    case kEpiScatter:
+      if (!a.row_slot || !a.tp.rs_recv[0]) return -7;
+      return launch<256, 4, kEpiScatter>(a, stream);
     case kEpiRSPush:
       if (a.tp.world < 1 || a.tp.world > kMaxTP || a.tp.rows_per_rank <= 0 ||
           a.M != a.tp.world * a.tp.rows_per_rank)

@@ -19,6 +19,7 @@ enum GemmEpi : int {
   kEpiArgmax = 4,     // per-row argmax (optionally bitmask-filtered) via 64-bit atomicMax
   kEpiStoreF32 = 5,   // C (fp32) = acc
   kEpiRSPush = 6,     // partial rows -> owner rank's receive buffer over NVLink (GEMM + reduce-scatter)
+  kEpiScatter = 7,    // row r -> rs_recv[row_rank[r] or 0] + row_slot[r] * ldc (skip if slot < 0), bf16
 };
 
 constexpr int kMaxTP = 8;
@@ -80,6 +81,15 @@ struct GemmArgs {
   int* status = nullptr;               // device status word
   int max_ctas = 0;                    // 0 = number of SMs
   TPGemmArgs tp;
+  // Grouped GEMM (one group per expert): group g owns A rows [g*group_rows, g*group_rows + group_count[g])
+  // and B rows [g*N, (g+1)*N); output row r of the group is A row r. group_count must be final when
+  // the kernel starts (written by an earlier kernel on the stream); tiles past a group's count are skipped.
+  int groups = 0;
+  int group_rows = 0;  // multiple of 128
+  const int* group_count = nullptr;
+  // kEpiScatter destinations (rows indexed like A)
+  const int* row_slot = nullptr;
+  const int* row_rank = nullptr;
 };
 
 // Number of CTAs gemm_bf16 launches for a shape (the per-call increment of TP counters).
@@ -170,6 +180,37 @@ struct TPPtrs {
 int tp_argmax_combine(const TPPtrs& amax, int world, const unsigned long long* done_cnt,
                       const unsigned long long* base, unsigned long long off, int* out, int n, int* status,
                       cudaStream_t stream);
+
+// ----------------------------------------------------------------- mixture of experts
+// Top-k routing + gather of token rows into per-expert segments (and, across GPUs, the
+// all-to-all dispatch over NVLink). Local form: logits [M, ld_logits] fp32 (first E used),
+// x [M, dim] bf16 -> gathered [E*cap, dim], row_slot[E*cap] = token*top_k + j, weights [M, top_k],
+// count[E] (zeroed by the caller). Expert e lives on rank e / experts_per_rank.
+struct MoEDispatchArgs {
+  const float* logits = nullptr;
+  int ld_logits = 0;
+  const __nv_bfloat16* x = nullptr;
+  int M = 0, dim = 0, n_experts = 0, top_k = 2, cap = 0;
+  float* weights = nullptr;  // [M, top_k]
+  int world = 1, rank = 0, experts_per_rank = 0;
+  // per destination rank: its gathered rows, row_slot, row_rank, count arrays (peer pointers for EP)
+  __nv_bfloat16* gathered[kMaxTP] = {};
+  int* row_slot[kMaxTP] = {};
+  int* row_rank[kMaxTP] = {};
+  int* count[kMaxTP] = {};
+  unsigned long long* done_cnt[kMaxTP] = {};  // EP: +1 per CTA at every destination after the writes
+  int* status = nullptr;
+};
+int moe_dispatch(const MoEDispatchArgs& a, cudaStream_t stream);
+constexpr int kMoEDispatchGrid = 64;  // fixed, so every rank adds the same count per call
+
+// h[t] += sum_j weights[t, j] * comb[t*top_k + j]   (after waiting for EP combine counters)
+int moe_combine(__nv_bfloat16* h, const __nv_bfloat16* comb, const float* weights, int M, int dim, int top_k,
+                const unsigned long long* wait_cnt, int wait_n, unsigned long long wait_target, int* status,
+                cudaStream_t stream);
+// Waits until wait_cnt[0..n) >= target (EP: all sources dispatched) - a launch-ordering point.
+int wait_counters(const unsigned long long* cnt, int n, unsigned long long target, int* status,
+                  cudaStream_t stream);
 
 int page_copy(const void* src, void* dst, const int64_t* src_ids, const int64_t* dst_ids, int n, int64_t page_bytes,
               int64_t sub_off, int64_t sub_bytes, cudaStream_t stream);

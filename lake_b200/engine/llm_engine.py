@@ -46,6 +46,9 @@ class EngineConfig:
     # Tensor parallel: (rank, world, process group for the handle exchange); every rank of the
     # group runs an engine with the same requests and makes the same scheduling decisions.
     tp: tuple | None = None
+    # Expert parallel (MoE): (rank, world, process group). Each rank serves its own requests and
+    # steps in lockstep with the group (a step with no work still runs the expert exchange).
+    ep: tuple | None = None
 
 
 @dataclass
@@ -96,6 +99,14 @@ class LLMEngine:
                                     status=None)
             self.model = TPDecoderLM(cfg, self.tp_group, self.device, seed=ec.seed)
             cfg = self._arena_cfg = _local_kv_cfg(cfg, world)
+        elif ec.ep is not None and ec.ep[1] > 1:
+            from ..parallel.ep import EPGroup
+
+            rank, world, pg = ec.ep
+            self.ep_group = EPGroup(rank, world, self.device, max_tokens, cfg.hidden, cfg.n_experts, cfg.top_k,
+                                    group=pg)
+            self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed, ep=self.ep_group)
+            self._arena_cfg = cfg
         else:
             self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed)
             self._arena_cfg = cfg
@@ -126,7 +137,8 @@ class LLMEngine:
         self.scheduler = Scheduler(self.pool, SchedulerConfig(ec.max_running, ec.max_batched_tokens,
                                                               ec.long_prefill_threshold, ec.max_model_len, maxb))
         self.runner = ModelRunner(self.model, self.arena, max_tokens, ec.max_running, maxb,
-                                  ec.use_cuda_graphs and self.tp_world == 1, ec.block_size, row_multiple=self.tp_world)
+                                  ec.use_cuda_graphs and self.tp_world == 1 and not (ec.ep and ec.ep[1] > 1), ec.block_size,
+                                  row_multiple=self.tp_world)
         self.requests: dict[str, Request] = {}
         self.pool_iface = None  # PoolIface (storage-pool fences), attached by attach_pool
         self._ids = itertools.count()
@@ -141,17 +153,17 @@ class LLMEngine:
         req = Request(rid=rid, prompt=list(prompt), params=p)
         if arrival is not None:
             req.arrival = arrival
-        if self.pool_iface is not None:
-            prefetch = getattr(self.pool_iface.agent, "prefetch", None)
-            if callable(prefetch):
-                prefetch(req)  # bring pool-resident prefix pages into HBM before admission
         self.scheduler.add(req)
         self.requests[rid] = req
         return rid
 
     def attach_pool(self, pool) -> None:
-        """Route every step through a storage-pool interface (lake_b200.pool.PoolIface)."""
+        """Route every step through a storage-pool interface (lake_b200.pool.PoolIface).
+        An agent with ``prefetch(req)`` is called at admission, right before the prefix
+        lookup, to bring pool-resident prefix pages back into HBM."""
         self.pool_iface = pool
+        prefetch = getattr(pool.agent, "prefetch", None)
+        self.scheduler.on_admit = prefetch if callable(prefetch) else None
 
     def abort(self, rid: str) -> bool:
         return self.scheduler.abort(rid)
@@ -228,6 +240,9 @@ class LLMEngine:
         out = self.scheduler.schedule()
         self.last_step = out
         if out.is_empty:
+            if self.ec.ep is not None and self.ec.ep[1] > 1:
+                self.runner.execute_null()  # the group's expert exchange needs every rank
+                self.step_count += 1
             return []
         bitmask = self._bitmask(out)
         if self.runner.peer_arena is not None:

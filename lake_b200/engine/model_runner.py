@@ -276,6 +276,12 @@ class ModelRunner:
             self.last_device_ms = ev0.elapsed_time(ev1)
         return self.h_tok[:nsamp].tolist()
 
+    def execute_null(self) -> None:
+        """A zero-token forward: every collective the model issues still runs (expert parallel)."""
+        batch = self._batch_views(0, 0, 0, 0, 0, 1)
+        self.model.forward(batch, self.arena, self.ws)
+        torch.cuda.current_stream(self.device).synchronize()
+
     def _copy_cpu(self, t, s, nrows):
         self.d_i32.copy_(self.h_i32)
         self.d_i64.copy_(self.h_i64)

@@ -66,6 +66,7 @@ class Scheduler:
         self.running: list[Request] = []
         self.step_id = 0
         self.finished: list[Request] = []
+        self.on_admit = None  # callback(req) before the prefix lookup of an admission (tier promotion)
 
     # -------------------------------------------------------------- admission
     def add(self, req: Request) -> None:
@@ -174,6 +175,8 @@ class Scheduler:
             if not req.block_hashes:
                 req.block_hashes = chain_block_hashes(req.prompt, self.bs, full_only=True)
             usable = req.block_hashes[: (len(req.prompt) - 1) // self.bs]
+            if self.on_admit is not None:
+                self.on_admit(req)
             hit = self.pool.lookup(usable)
             cached = len(hit) * self.bs
             n = min(len(req.prompt) - cached, budget, cap)

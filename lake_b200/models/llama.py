@@ -80,7 +80,7 @@ class Workspace:
 
 class DecoderLM:
     def __init__(self, cfg: ModelConfig, device: torch.device | str = "cpu", dtype: torch.dtype | None = None,
-                 seed: int = 0, init: str = "random"):
+                 seed: int = 0, init: str = "random", ep=None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype or (torch.float32 if self.device.type == "cpu" else torch.bfloat16)
@@ -94,7 +94,7 @@ class DecoderLM:
         if cfg.n_experts:
             from .moe import MoE
 
-            self.moe = MoE(self)
+            self.moe = MoE(self, ep)
 
     # ------------------------------------------------------------ weights
     def _param(self, name, shape, gen, std=0.02, ones=False):
@@ -190,6 +190,8 @@ class DecoderLM:
                                    device=dev)
         if c.qk_norm:
             ws.extra["qkv"] = torch.zeros(max_tokens, c.q_size + 2 * c.kv_size, dtype=dt, device=dev)
+        if self.moe is not None and dev.type == "cuda":
+            self.moe.workspace(ws, max_tokens)
         return ws
 
     def _attention(self, i: int, b: ForwardBatch, arena: torch.Tensor, ws: Workspace, t: int) -> torch.Tensor:
