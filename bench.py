@@ -49,6 +49,7 @@ def parse():
     ap.add_argument("--mode", choices=["colocated", "pd"], default=None,
                     help="default: pd for an even number of GPUs >= 2, else colocated")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (colocated mode)")
+    ap.add_argument("--ep", action="store_true", help="expert parallel over all ranks (MoE models, colocated mode)")
     ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
     ap.add_argument("--prefill-queue", type=int, default=8,
                     help="pd mode: grants outstanding at a prefill rank (bounds queueing delay)")
@@ -177,7 +178,7 @@ def _make_engine(args, local, max_running, **kw):
                      seed=args.seed, **kw)
 
 
-def run_colocated(args, rank, local, barrier, tp=None):
+def run_colocated(args, rank, local, barrier, tp=None, ep=None):
     """One engine per GPU (or per tensor-parallel group) doing prefill and decode
     (chunked, decode-first). Ranks of a TP group submit identical requests and count
     tokens once (on the group's first rank)."""
@@ -188,8 +189,18 @@ def run_colocated(args, rank, local, barrier, tp=None):
 
     stream_id = rank if tp is None else rank // tp[1]
     nprng = np.random.default_rng(args.seed * 1000 + stream_id)
-    eng = _make_engine(args, local, args.running, tp=tp)
+    eng = _make_engine(args, local, args.running, tp=tp, ep=ep)
     counts = tp is None or tp[0] == 0
+
+    def everyone(flag: bool) -> bool:
+        # expert parallel: ranks step in lockstep, so loop conditions are agreed on
+        if ep is None:
+            return flag
+        import torch.distributed as dist
+
+        t = torch.tensor([1 if flag else 0])
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=ep[2])
+        return bool(t.item())
     vocab = eng.cfg.vocab
 
     def new_prompt(n):
@@ -208,7 +219,7 @@ def run_colocated(args, rank, local, barrier, tp=None):
 
     eng.runner.capture_graphs()
     guard = 0
-    while any(eng.requests[r].first_token_time is None for r in initial):
+    while everyone(any(eng.requests[r].first_token_time is None for r in initial)):
         eng.step()
         top_up()
         guard += 1
@@ -389,7 +400,8 @@ def main():
         if world > 1:
             dist.barrier(group=group)
 
-    mode = args.mode or ("pd" if world >= 2 and world % 2 == 0 and args.tp == 1 else "colocated")
+    mode = args.mode or ("pd" if world >= 2 and world % 2 == 0 and args.tp == 1 and not args.ep else "colocated")
+    ep = (rank, world, group) if args.ep and world > 1 else None
     tp = None
     if args.tp > 1:
         if mode != "colocated" or world % args.tp:
@@ -405,7 +417,7 @@ def main():
     if mode == "pd":
         w, role = run_pd(args, rank, world, local, group, barrier)
     else:
-        w = run_colocated(args, rank, local, barrier, tp)
+        w = run_colocated(args, rank, local, barrier, tp, ep)
     ck = clocks.stop() if rank == 0 else {}
 
     # aggregate over ranks (max of times, sum of counts) through the gloo group
@@ -436,6 +448,7 @@ def main():
         kv_gbs = sm[6].item() / (wall_ms / 1000.0) / 1e9 if sm[6].item() else None
         par = f"pd: {world // 2} prefill + {world // 2} decode instances (tp1 each)" if mode == "pd" else (
             f"dp{world // args.tp} x tp{args.tp} (fused NVLink collectives)" if args.tp > 1 else
+            f"ep{world} (experts split, attention data-parallel, fused dispatch/combine)" if ep else
             (f"dp{world}" if world > 1 else "single"))
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "output tok/s", "n_gpus": world,

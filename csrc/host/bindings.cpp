@@ -16,6 +16,7 @@ void register_tier(py::module_& m);
 void register_router(py::module_& m);
 void register_agent(py::module_& m);
 void register_transfer(py::module_& m);
+void register_weights(py::module_& m);
 
 namespace {
 
@@ -314,4 +315,5 @@ PYBIND11_MODULE(_host, m) {
   register_router(m);
   register_agent(m);
   register_transfer(m);
+  register_weights(m);
 }

@@ -244,7 +244,8 @@ class ModelRunner:
         nd = len(out.decode)
         has_remote = any(c.req.remote_blocks is not None for c in out.prefill)
         pure_decode = not out.prefill and bitmask is None
-        bucket = self._bucket(nd) if (pure_decode and self.use_graphs) else None
+        streaming = getattr(self.model, "layer_ready", None) is not None  # weights still loading: run eagerly
+        bucket = self._bucket(nd) if (pure_decode and self.use_graphs and not streaming) else None
         t, s, ntiles, nrows, nd_eff = self._pack(out, pad_decode_to=bucket or 0)
         if not self.cuda:
             self._copy_cpu(t, s, nrows)

@@ -90,6 +90,7 @@ class DecoderLM:
             self._random_init(seed)
         self.rope_cs = ref.rope_cache(cfg.max_position, cfg.rope_theta, cfg.head_dim, cfg.rope_scaling,
                                       device=self.device)
+        self.layer_ready = None  # per-layer CUDA events while weights stream in (runtime.coldstart)
         self.moe = None
         if cfg.n_experts:
             from .moe import MoE
@@ -247,9 +248,14 @@ class DecoderLM:
         c = self.cfg
         t = b.num_tokens
         h, x = ws.h[:t], ws.x[:t]
+        ready = self.layer_ready
+        if ready is not None:
+            torch.cuda.current_stream(self.device).wait_event(ready["embed"])
         ops.embedding(b.input_ids, self.w["embed_tokens"], out=h)
         for i in range(c.n_layers):
             p = f"layers.{i}."
+            if ready is not None:  # layer-async cold start: this layer's weights may still be in flight
+                torch.cuda.current_stream(self.device).wait_event(ready[i])
             ops.rms_norm(h, self.w[p + "input_layernorm"], c.rms_eps, out=x)
             self._qkv(i, x, b, arena, ws, t)
             attn = self._attention(i, b, arena, ws, t)
@@ -260,6 +266,8 @@ class DecoderLM:
         if r == 0:
             return ws.tokens[:0]
         fx = ws.fx[:r]
+        if ready is not None:
+            torch.cuda.current_stream(self.device).wait_event(ready["head"])
         torch.index_select(h, 0, b.sample_rows, out=fx)
         ops.rms_norm(fx, self.w["norm"], c.rms_eps, out=fx)
         if b.want_logits:
