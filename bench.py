@@ -35,6 +35,7 @@ METRIC = "output tok/s per box (Llama-3-8B PD-split); p50 TTFT/TPOT; P→D KV GB
 
 def parse():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--config", default=None, help="run configuration file (configs/*.yaml) supplying defaults")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
@@ -53,6 +54,14 @@ def parse():
     ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
     ap.add_argument("--prefill-queue", type=int, default=8,
                     help="pd mode: grants outstanding at a prefill rank (bounds queueing delay)")
+    pre, _ = ap.parse_known_args()
+    if pre.config:
+        from lake_b200.utils.config_files import apply_env, bench_defaults, load_run_config
+
+        cfg = load_run_config(pre.config)
+        apply_env(cfg)
+        known = {a.dest for a in ap._actions}
+        ap.set_defaults(**{k: v for k, v in bench_defaults(cfg).items() if k in known})
     return ap.parse_args()
 
 
@@ -471,6 +480,9 @@ def main():
             "clocks": ck, "impl": "lakeb", "ranks": ranks,
         }
         print(json.dumps(line))
+        from lake_b200.utils.trace import emit
+
+        emit(line)
     if world > 1:
         barrier()
         dist.destroy_process_group()

@@ -2,7 +2,12 @@
 library counterpart (cuBLAS via torch.matmul, SDPA), timed with CUDA events
 after warm-up, L2 flushed between iterations.
 
-    python -m lake_b200.bench.kernels [--only gemm,decode,prefill,norm]
+    python -m lake_b200.bench.kernels [--only gemm,decode,prefill,norm,moe]
+    python -m lake_b200.bench.kernels --profile CASE   # 3 launches of one kernel, for an ncu capture
+
+Profile cases (inputs larger than the 126 MB L2, a few GB on the device at most):
+gemm_gate_up (M=4096 K=4096 N=28672), decode (256 seqs x 2304 ctx, 1 layer),
+prefill_tc (4 x 2048), moe_decode (8 experts, 128 tokens top-2, grouped GEMM).
 """
 from __future__ import annotations
 
@@ -103,15 +108,96 @@ def bench_norm(t: Timer, out: list):
     out.append(dict(kernel="rmsnorm", rows=8192, dim=4096, ms=ms, gbs=2 * x.numel() * 2 / ms / 1e6))
 
 
+def _moe_case(tokens=128, hidden=4096, inter=14336, experts=8, top_k=2):
+    from ..ops._ext import native
+
+    C = native()
+    cap = (tokens + 127) // 128 * 128
+    x = torch.randn(tokens, hidden, device="cuda").to(BF)
+    logits = torch.randn(tokens, 32, device="cuda")
+    wts = torch.empty(tokens * top_k, device="cuda")
+    count = torch.zeros(experts, dtype=torch.int32, device="cuda")
+    gathered = torch.zeros(experts * cap, hidden, device="cuda", dtype=BF)
+    slot = torch.zeros(experts * cap, dtype=torch.int32, device="cuda")
+    gu = (torch.randn(experts, 2 * inter, hidden, device="cuda") * 0.02).to(BF)
+    dn = (torch.randn(experts, hidden, inter, device="cuda") * 0.02).to(BF)
+    act = torch.empty(experts * cap, inter, device="cuda", dtype=BF)
+    comb = torch.empty(tokens * top_k, hidden, device="cuda", dtype=BF)
+    h = torch.zeros(tokens, hidden, device="cuda", dtype=BF)
+
+    def run():
+        count.zero_()
+        C.moe_dispatch(logits, x, wts, experts, top_k, cap, 1, 0, [gathered.data_ptr()], [slot.data_ptr()], [],
+                       [count.data_ptr()], [])
+        C.gemm_grouped(gathered, gu, act, 2, count, cap)
+        C.gemm_grouped(act, dn, None, 7, count, cap, row_slot=slot, dst_ptrs=[comb.data_ptr()])
+        C.moe_combine(h, comb, wts, top_k)
+
+    wbytes = (gu.numel() + dn.numel()) * 2
+    return run, wbytes
+
+
+def bench_moe(t: Timer, out: list):
+    for tokens in (128, 1024):
+        run, wbytes = _moe_case(tokens)
+        ms = t(run)
+        out.append(dict(kernel="moe_layer (dispatch+grouped gate_up+grouped down+combine)", tokens=tokens,
+                        experts=8, ms=ms, weight_gbs=wbytes / ms / 1e6))
+
+
+def profile(case: str) -> None:
+    """Three launches of one kernel on a small case (for `ncu -k <kernel> -c 3`)."""
+    if case == "gemm_gate_up":
+        a = torch.randn(4096, 4096, device="cuda").to(BF)
+        w = (torch.randn(28672, 4096, device="cuda") * 0.02).to(BF)
+        c = torch.empty(4096, 28672, device="cuda", dtype=BF)
+        fn = lambda: ops.linear(a, w, out=c)  # noqa: E731
+    elif case == "decode":
+        nseq, ctx, hq, hkv = 256, 2304, 32, 8
+        nb = ctx // 16
+        arena = torch.randn(nseq * nb + 1, 1, 2, hkv, 16, 128, device="cuda").to(BF)
+        bt = torch.randperm(nseq * nb, device="cuda").view(nseq, nb).to(torch.int32)
+        sl = torch.full((nseq,), ctx, dtype=torch.int32, device="cuda")
+        q = torch.randn(nseq, hq * 128, device="cuda").to(BF)
+        o = torch.empty_like(q)
+        fn = lambda: ops.paged_decode_attention(q, arena, 0, bt, sl, hq, hkv, 0.088, out=o)  # noqa: E731
+    elif case == "prefill_tc":
+        nseq, ctx, hq, hkv = 4, 2048, 32, 8
+        nb = ctx // 16
+        arena = torch.randn(nseq * nb + 1, 1, 2, hkv, 16, 128, device="cuda").to(BF)
+        bt = torch.randperm(nseq * nb, device="cuda").view(nseq, nb).to(torch.int32)
+        sl = torch.full((nseq,), ctx, dtype=torch.int32, device="cuda")
+        qs = [i * ctx for i in range(nseq + 1)]
+        tiles = ops.build_prefill_tiles(qs, [0] * nseq, device="cuda")
+        q = torch.randn(nseq * ctx, hq * 128, device="cuda").to(BF)
+        o = torch.empty_like(q)
+        qs_t = torch.tensor(qs, dtype=torch.int32, device="cuda")
+        fn = lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv, 0.088,  # noqa
+                                                 out=o)
+    elif case == "moe_decode":
+        fn, _ = _moe_case(128)
+    else:
+        raise SystemExit(f"unknown profile case {case}")
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    ops.core.check_status()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default="gemm,decode,prefill,norm")
+    ap.add_argument("--only", default="gemm,decode,prefill,norm,moe")
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--profile", default=None)
     args = ap.parse_args(argv)
+    if args.profile:
+        profile(args.profile)
+        return
     t = Timer(args.iters)
     res: list = []
     for name in args.only.split(","):
-        {"gemm": bench_gemm, "decode": bench_decode, "prefill": bench_prefill, "norm": bench_norm}[name](t, res)
+        {"gemm": bench_gemm, "decode": bench_decode, "prefill": bench_prefill, "norm": bench_norm,
+         "moe": bench_moe}[name](t, res)
     for r in res:
         print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}))
 

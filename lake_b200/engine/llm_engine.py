@@ -18,6 +18,7 @@ from dataclasses import dataclass, field
 import torch
 
 from ..models.config import ModelConfig, get_config
+from ..utils.trace import nvtx
 from ..models.llama import DecoderLM
 from .block_pool import BlockPool
 from .model_runner import ModelRunner
@@ -237,6 +238,10 @@ class LLMEngine:
 
     # ------------------------------------------------------------ stepping
     def step(self) -> list[StepOutput]:
+        with nvtx("engine.step"):
+            return self._step()
+
+    def _step(self) -> list[StepOutput]:
         out = self.scheduler.schedule()
         self.last_step = out
         if out.is_empty:

@@ -30,6 +30,7 @@ import torch
 
 from .. import ops
 from ..oracle import ops_ref as ref
+from ..utils.trace import nvtx
 from .config import ModelConfig
 
 
@@ -256,12 +257,13 @@ class DecoderLM:
             p = f"layers.{i}."
             if ready is not None:  # layer-async cold start: this layer's weights may still be in flight
                 torch.cuda.current_stream(self.device).wait_event(ready[i])
-            ops.rms_norm(h, self.w[p + "input_layernorm"], c.rms_eps, out=x)
-            self._qkv(i, x, b, arena, ws, t)
-            attn = self._attention(i, b, arena, ws, t)
-            ops.linear_residual(attn, self.w[p + "o_proj"], h, out=h)
-            ops.rms_norm(h, self.w[p + "post_attention_layernorm"], c.rms_eps, out=x)
-            self._mlp(i, x, h, ws, t)
+            with nvtx(p):
+                ops.rms_norm(h, self.w[p + "input_layernorm"], c.rms_eps, out=x)
+                self._qkv(i, x, b, arena, ws, t)
+                attn = self._attention(i, b, arena, ws, t)
+                ops.linear_residual(attn, self.w[p + "o_proj"], h, out=h)
+                ops.rms_norm(h, self.w[p + "post_attention_layernorm"], c.rms_eps, out=x)
+                self._mlp(i, x, h, ws, t)
         r = b.sample_rows.shape[0]
         if r == 0:
             return ws.tokens[:0]

@@ -30,6 +30,7 @@ loadsync.go, autoscale.go:339-473.
 from __future__ import annotations
 
 import asyncio
+import bisect
 import logging
 import os
 import time
@@ -47,6 +48,7 @@ LOG = logging.getLogger("lake_b200.router")
 pb = proto.messages()
 BLOCK_SIZE = 16
 MAX_BODY = 1 << 20
+LATENCY_BOUNDS_S = (0.05, 0.1, 0.25, 0.5, 1.0, 2.5, 5.0, 10.0, 30.0)
 ROLE = {"hybrid": H.Role.HYBRID, "prefill": H.Role.PREFILL, "decode": H.Role.DECODE}
 
 
@@ -77,6 +79,7 @@ class RouterConfig:
     workers: dict = field(default_factory=dict)  # node id -> worker address
     request_timeout_s: float = 30.0
     block_size: int = BLOCK_SIZE
+    max_reroutes: int = 1
 
     @classmethod
     def from_env(cls) -> "RouterConfig":
@@ -121,7 +124,8 @@ class Router:
         self.hot = H.HotSet(256)
         self.mode_counts: dict[str, int] = {}
         self.stats = {"requests": 0, "errors": 0, "hit_blocks": 0, "total_blocks": 0, "local_hit_blocks": 0,
-                      "reusable_blocks": 0, "preemptions": 0, "latency_sum_s": 0.0}
+                      "reusable_blocks": 0, "preemptions": 0, "reroutes": 0, "latency_sum_s": 0.0}
+        self.latency_buckets = [0] * (len(LATENCY_BOUNDS_S) + 1)
         self.last_ready_latency_s = 0.0
         self._waiters: dict[int, asyncio.Future] = {}
         self._running: dict[int, object] = {}  # ticket -> in-flight grpc call (cancelled on preemption)
@@ -243,11 +247,31 @@ class Router:
 
     async def generate(self, model: str, tokens: list[int], max_new: int, priority: int = 0,
                        session: bytes = b"", rid: str | None = None) -> dict:
+        """Route and run one request. A node whose worker answers UNAVAILABLE (a failed or
+        draining worker: the F4 signal) is skipped and the request re-dispatched to the next
+        ready node, up to cfg.max_reroutes times; the reuse hint and mode are recomputed for
+        the new node."""
         rid = rid or uuid.uuid4().hex
-        t0 = time.perf_counter()
         hashes = H.chain_block_hashes(tokens, self.cfg.block_size, True)
         key = session or H.prefix_anchor(hashes)
         node = H.pick_node(self.nodes, self.mirror, model, hashes, key, self.cfg.affinity_guard)
+        tried = [node]
+        for attempt in range(self.cfg.max_reroutes + 1):
+            try:
+                return await self._generate_on(node, model, tokens, hashes, max_new, priority,
+                                               rid if attempt == 0 else f"{rid}-n{attempt}")
+            except RouterError as e:
+                alt = [n for n in self.nodes.ready_ids() if n not in tried]
+                if e.status != 503 or attempt == self.cfg.max_reroutes or not alt:
+                    raise
+                node = alt[0]
+                tried.append(node)
+                self.stats["reroutes"] += 1
+        raise RouterError(503, "no node available")
+
+    async def _generate_on(self, node: str, model: str, tokens: list[int], hashes: list[bytes], max_new: int,
+                           priority: int, rid: str) -> dict:
+        t0 = time.perf_counter()
         self.nodes.inc_inflight(node)
         attempt = [0]
         last_hint = [H.PrefixHint()]
@@ -302,7 +326,9 @@ class Router:
         st["hit_blocks"] += gen.reused_blocks
         st["reusable_blocks"] += last_hint[0].reused_blocks
         st["local_hit_blocks"] += last_hint[0].local_hit_blocks
-        st["latency_sum_s"] += time.perf_counter() - t0
+        lat = time.perf_counter() - t0
+        st["latency_sum_s"] += lat
+        self.latency_buckets[bisect.bisect_left(LATENCY_BOUNDS_S, lat)] += 1
         return {"request_id": rid, "node": node, "output_tokens": list(gen.output_tokens),
                 "reused_blocks": gen.reused_blocks, "prefill_blocks": gen.prefill_blocks, "mode": gen.mode}
 
@@ -321,6 +347,7 @@ class Router:
             "# TYPE lake_router_requests_total counter", f"lake_router_requests_total {st['requests']}",
             "# TYPE lake_router_errors_total counter", f"lake_router_errors_total {st['errors']}",
             "# TYPE lake_router_preemptions_total counter", f"lake_router_preemptions_total {st['preemptions']}",
+            "# TYPE lake_router_reroutes_total counter", f"lake_router_reroutes_total {st['reroutes']}",
             "# TYPE lake_router_latency_seconds_sum counter", f"lake_router_latency_seconds_sum {st['latency_sum_s']:.6f}",
             "# TYPE lake_router_prefix_hit_rate gauge", f"lake_router_prefix_hit_rate {self.hit_rate():.6f}",
             "# TYPE lake_router_local_hit_rate gauge", f"lake_router_local_hit_rate {self.local_hit_rate():.6f}",
@@ -332,6 +359,14 @@ class Router:
         ]
         for m, n in sorted(self.mode_counts.items()):
             lines.append(f'lake_router_mode_total{{mode="{m}"}} {n}')
+        lines.append("# TYPE lake_router_request_seconds histogram")
+        cum = 0
+        for b, n in zip(LATENCY_BOUNDS_S + (float("inf"),), self.latency_buckets):
+            cum += n
+            le = "+Inf" if b == float("inf") else f"{b}"
+            lines.append(f'lake_router_request_seconds_bucket{{le="{le}"}} {cum}')
+        lines.append(f"lake_router_request_seconds_count {cum}")
+        lines.append(f"lake_router_request_seconds_sum {st['latency_sum_s']:.6f}")
         return "\n".join(lines) + "\n"
 
     # ---------------------------------------------------------------- background loops

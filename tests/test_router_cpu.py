@@ -148,3 +148,47 @@ def test_priority_preemption_requeues():
         assert order == ["low-preempted", "high", "low"]
         assert router.stats["preemptions"] == 1
     asyncio.run(run())
+
+
+def test_reroute_away_from_unavailable_worker():
+    """F4: a worker that refuses (drained) is skipped and the request re-dispatched."""
+    cp = ControlPlane()
+    agent = AgentServer("w0")
+    engines, servers, addrs = [], [], []
+    for n in range(2):
+        eng = LLMEngine("tiny", device="cpu", max_running=4, max_batched_tokens=128, max_model_len=512, num_blocks=64)
+        we = WorkerEngine(RoleConfig(device="cpu", model_backend="mock"), engine=eng)
+        we.start()
+        srv = grpc.server(futures.ThreadPoolExecutor(max_workers=8))
+        proto.add_service(srv, "WorkerService", WorkerServicer(we))
+        if n == 0:
+            proto.add_service(srv, "ControlPlaneService", cp)
+            proto.add_service(srv, "AgentService", agent)
+        port = srv.add_insecure_port("127.0.0.1:0")
+        srv.start()
+        engines.append(we)
+        servers.append(srv)
+        addrs.append(f"127.0.0.1:{port}")
+    engines[0].lifecycle.drain()  # w0 refuses new work
+    cfg = RouterConfig(worker_addr=addrs[0], agent_addr=addrs[0], cp_addr=addrs[0], max_inflight=4,
+                       workers={"w0": addrs[0], "w1": addrs[1]}, request_timeout_s=30)
+
+    async def run():
+        router = Router(cfg)
+        async with TestClient(TestServer(make_app(router))) as client:
+            for i in range(6):
+                r = await client.post("/v1/chat/completions", json={"prompt_token_ids": list(range(i, i + 40)),
+                                                                    "max_tokens": 2},
+                                      headers={"X-Lake-Session-Id": f"s{i}"})
+                assert r.status == 200, await r.text()
+                assert (await r.json())["lake"]["node"] == "w1"
+            assert router.stats["reroutes"] >= 1
+            m = await (await client.get("/metrics")).text()
+            assert "lake_router_request_seconds_count 6" in m
+    try:
+        asyncio.run(run())
+    finally:
+        for we, srv in zip(engines, servers):
+            srv.stop(0)
+            we.stop(drain=False)
+        cp.stop()
