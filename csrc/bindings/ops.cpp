@@ -154,9 +154,18 @@ void linear_swiglu(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c1
 void linear_qkv(const at::Tensor& a, const at::Tensor& w, at::Tensor& q_out, const at::Tensor& rope_cs,
                 const at::Tensor& positions, const at::Tensor& slots, const at::Tensor& arena, int64_t layer,
                 int64_t n_q_heads, int64_t n_kv_heads, c10::optional<at::Tensor> peer_arena,
-                c10::optional<at::Tensor> peer_slots, c10::optional<at::Tensor> status, c10::optional<py::dict> tp) {
+                c10::optional<at::Tensor> peer_slots, c10::optional<at::Tensor> status, c10::optional<py::dict> tp,
+                c10::optional<at::Tensor> q_norm, c10::optional<at::Tensor> k_norm, double qk_eps) {
   GemmArgs g = base_args(a, w);
   apply_tp(g, tp);
+  if (q_norm.has_value() && k_norm.has_value()) {
+    TORCH_CHECK(q_norm->numel() == 128 && k_norm->numel() == 128 && q_norm->scalar_type() == at::kBFloat16 &&
+                    k_norm->scalar_type() == at::kBFloat16 && q_norm->is_contiguous() && k_norm->is_contiguous(),
+                "q_norm / k_norm must be bf16 [128]");
+    g.q_norm_w = bf(*q_norm);
+    g.k_norm_w = bf(*k_norm);
+    g.qk_eps = static_cast<float>(qk_eps);
+  }
   check_bf16_2d(q_out, "q_out");
   TORCH_CHECK(q_out.size(0) == a.size(0) && q_out.size(1) == n_q_heads * 128, "q_out shape");
   TORCH_CHECK(rope_cs.scalar_type() == at::kFloat && rope_cs.is_contiguous() && rope_cs.dim() == 3 &&
@@ -608,6 +617,8 @@ PYBIND11_MODULE(_C, m) {
   m.def("wait_counters", &wait_counters, py::arg("cnt"), py::arg("n"), py::arg("target"),
         py::arg("status") = py::none());
   m.def("moe_dispatch_grid", []() { return lakeb::kMoEDispatchGrid; });
+  m.def("set_gemm_pair_mode", [](int64_t mode) { lakeb::set_gemm_pair_mode(static_cast<int>(mode)); });
+  m.def("gemm_pair_mode", []() { return lakeb::gemm_pair_mode(); });
   m.def("gemm_grid", [](int64_t M, int64_t N, int64_t epi) {
     return lakeb::gemm_grid(static_cast<int>(M), static_cast<int>(N), static_cast<int>(epi), 0);
   });
@@ -615,7 +626,8 @@ PYBIND11_MODULE(_C, m) {
   m.def("linear_qkv", &linear_qkv, py::arg("a"), py::arg("w"), py::arg("q_out"), py::arg("rope_cs"),
         py::arg("positions"), py::arg("slots"), py::arg("arena"), py::arg("layer"), py::arg("n_q_heads"),
         py::arg("n_kv_heads"), py::arg("peer_arena") = py::none(), py::arg("peer_slots") = py::none(),
-        py::arg("status") = py::none(), py::arg("tp") = py::none());
+        py::arg("status") = py::none(), py::arg("tp") = py::none(), py::arg("q_norm") = py::none(),
+        py::arg("k_norm") = py::none(), py::arg("qk_eps") = 1e-6);
   m.def("linear_argmax", &linear_argmax, py::arg("a"), py::arg("w"), py::arg("amax"), py::arg("bitmask") = py::none(),
         py::arg("status") = py::none(), py::arg("tp") = py::none());
   m.def("paged_decode", &paged_decode, py::arg("q"), py::arg("out"), py::arg("arena"), py::arg("layer"),

@@ -343,6 +343,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (is_q || is_k) {
           const int kvh = head - p.n_q_heads;
+          // per-head RMSNorm before RoPE (Qwen3): one pass over the head's 128 accumulators first
+          const __nv_bfloat16* nw = is_q ? p.q_norm_w : p.k_norm_w;
+          float inv = 1.f;
+          if (nw) {
+            float ss = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld32(tbase + c * 32, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) ss += __uint_as_float(r[j]) * __uint_as_float(r[j]);
+            }
+            inv = rsqrtf(ss * (1.f / 128.f) + p.qk_eps);
+          }
 #pragma unroll 1
           for (int half = 0; half < 2; ++half) {
             uint32_t r1[32], r2[32];
@@ -355,8 +370,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 const float2 c = cs[j];
-                const float x1 = __uint_as_float(r1[j]);
-                const float x2 = __uint_as_float(r2[j]);
+                float x1 = __uint_as_float(r1[j]);
+                float x2 = __uint_as_float(r2[j]);
+                if (nw) {
+                  x1 *= inv * __bfloat162float(nw[half * 32 + j]);
+                  x2 *= inv * __bfloat162float(nw[64 + half * 32 + j]);
+                }
                 o1[j] = x1 * c.x - x2 * c.y;
                 o2[j] = x2 * c.x + x1 * c.y;
               }
@@ -466,14 +485,45 @@ int launch(const GemmArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
-int bn_of(int epi) { return epi == kEpiQKV ? 128 : 256; }
+// Tile width: 256 keeps the tensor cores busiest, but a small M (decode batches) leaves most SMs
+// idle with 128x256 tiles, so epilogues that do not depend on the tile width step down to 128
+// columns when 256-wide tiles would cover less than ~3/4 of the SMs. SwiGLU (256-row gate/up interleave),
+// QKV (one 128-wide head per tile), argmax and grouped GEMMs keep their widths.
+int bn_for(int M, int N, int epi, bool grouped) {
+  if (epi == kEpiQKV) return 128;
+  if (epi == kEpiSwiGLU || epi == kEpiArgmax || grouped) return 256;
+  const int target = (num_sms() * 3) / 4;
+  const int mb = (M + kBM - 1) / kBM;
+  // (64-wide tiles measured slower than 128 at M=256: the K loop per CTA is latency-bound either way)
+  return mb * ((N + 255) / 256) >= target ? 256 : 128;
+}
+
+template <int EPI>
+int launch_bn(const GemmArgs& a, cudaStream_t stream) {
+  switch (bn_for(a.M, a.N, EPI, a.groups != 0)) {
+    case 128:
+      return launch<128, 6, EPI>(a, stream);
+    default:
+      return launch<256, 4, EPI>(a, stream);
+  }
+}
 
 }  // namespace
 
-int gemm_grid(int M, int N, int epi, int max_ctas) { return grid_for(M, N, bn_of(epi), max_ctas); }
+int gemm_grid(int M, int N, int epi, int max_ctas) {
+  return grid_for(M, N, bn_for(M, N, epi, false), max_ctas);
+}
+
+static int g_pair_mode = 0;
+void set_gemm_pair_mode(int mode) { g_pair_mode = mode; }
+int gemm_pair_mode() { return g_pair_mode; }
 
 int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
+  const bool plain = !a.groups && !a.tp.ag_cnt && !a.tp.rs_cnt[0] && !a.tp.done_cnt[0] && a.max_ctas == 0;
+  if (g_pair_mode && plain && a.M >= 512 &&
+      (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiSwiGLU || epi == kEpiStoreF32))
+    return gemm_bf16_pair(a, epi, stream);
   if (a.tp.ag_cnt && !a.tp.ag_all && (a.tp.rows_per_rank <= 0 || a.M > a.tp.world * a.tp.rows_per_rank)) return -6;
   if (a.tp.ag_cnt && (a.tp.world < 1 || a.tp.world > kMaxTP)) return -6;
   if (a.groups && (a.group_rows % kBM || !a.group_count || a.M != a.groups * a.group_rows)) return -8;
@@ -481,9 +531,9 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
   if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) return -2;
   switch (epi) {
     case kEpiStoreBf16:
-      return launch<256, 4, kEpiStoreBf16>(a, stream);
+      return launch_bn<kEpiStoreBf16>(a, stream);
     case kEpiResidual:
-      return launch<256, 4, kEpiResidual>(a, stream);
+      return launch_bn<kEpiResidual>(a, stream);
     case kEpiSwiGLU:
       return launch<256, 4, kEpiSwiGLU>(a, stream);
     case kEpiQKV:
@@ -492,7 +542,7 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
     case kEpiArgmax:
       return launch<256, 4, kEpiArgmax>(a, stream);
     case kEpiStoreF32:
-      return launch<256, 4, kEpiStoreF32>(a, stream);
+      return launch_bn<kEpiStoreF32>(a, stream);
     case kEpiScatter:
       if (!a.row_slot || !a.tp.rs_recv[0]) return -7;
       return launch<256, 4, kEpiScatter>(a, stream);
@@ -500,7 +550,7 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
       if (a.tp.world < 1 || a.tp.world > kMaxTP || a.tp.rows_per_rank <= 0 ||
           a.M != a.tp.world * a.tp.rows_per_rank)
         return -5;
-      return launch<256, 4, kEpiRSPush>(a, stream);
+      return launch_bn<kEpiRSPush>(a, stream);
     default:
       return -4;
   }

@@ -74,6 +74,10 @@ struct GemmArgs {
   const int64_t* peer_slots = nullptr;  // [M] slot in the peer arena, <0 = skip
   KVArenaView peer_kv;                  // arena on another GPU (P2P-mapped), base==nullptr = none
   int n_q_heads = 0, n_kv_heads = 0;
+  // optional per-head RMSNorm of q and k before RoPE (Qwen3): weights [128] bf16
+  const __nv_bfloat16* q_norm_w = nullptr;
+  const __nv_bfloat16* k_norm_w = nullptr;
+  float qk_eps = 1e-6f;
   // argmax epilogue
   unsigned long long* amax = nullptr;  // [M], zero-initialised by the caller
   const uint32_t* bitmask = nullptr;   // [M, bitmask_words], bit=1 allowed
@@ -91,6 +95,12 @@ struct GemmArgs {
   const int* row_slot = nullptr;
   const int* row_rank = nullptr;
 };
+
+// Two-SM (cta_group::2) GEMM for large M; epilogues: store bf16, residual, SwiGLU, fp32.
+int gemm_bf16_pair(const GemmArgs& args, int epi, cudaStream_t stream);
+// 0 = never use the two-SM kernel from gemm_bf16, 1 = use it for large plain GEMMs (M >= 512).
+void set_gemm_pair_mode(int mode);
+int gemm_pair_mode();
 
 // Number of CTAs gemm_bf16 launches for a shape (the per-call increment of TP counters).
 int gemm_grid(int M, int N, int epi, int max_ctas);

@@ -137,6 +137,34 @@ def _moe_case(tokens=128, hidden=4096, inter=14336, experts=8, top_k=2):
     return run, wbytes
 
 
+def bench_pd_qkv(t: Timer, out: list):
+    """Fused P->D: the QKV GEMM epilogue writes K/V into this GPU's arena and, over NVLink, into a
+    second GPU's arena (peer-mapped). Compared with the same GEMM writing only locally."""
+    if torch.cuda.device_count() < 2:
+        return
+    from ..ops._ext import native
+
+    torch.cuda.set_device(0)
+    native().enable_peer_access(1)
+    m, hq, hkv, hidden = 8192, 32, 8, 4096
+    nb = m // 16
+    arena = torch.zeros(nb + 1, 1, 2, hkv, 16, 128, device="cuda:0", dtype=BF)
+    peer = torch.zeros(nb + 1, 1, 2, hkv, 16, 128, device="cuda:1", dtype=BF)
+    x = torch.randn(m, hidden, device="cuda").to(BF)
+    w = (torch.randn((hq + 2 * hkv) * 128, hidden, device="cuda") * 0.02).to(BF)
+    q = torch.empty(m, hq * 128, device="cuda", dtype=BF)
+    cs = ref.rope_cache(8192, 5e5, 128, None, device="cuda")
+    pos = torch.arange(m, dtype=torch.int32, device="cuda") % 2048
+    slots = torch.arange(m, dtype=torch.int64, device="cuda")
+    ms_local = t(lambda: ops.linear_qkv(x, w, q, cs, pos, slots, arena, 0, hq, hkv))
+    ms_peer = t(lambda: ops.linear_qkv(x, w, q, cs, pos, slots, arena, 0, hq, hkv, peer, slots))
+    kv_bytes = m * 2 * hkv * 128 * 2
+    fl = 2 * m * w.shape[0] * hidden
+    out.append(dict(kernel="linear_qkv + P->D peer KV stores", m=m, ms_local_only=ms_local, ms_with_peer=ms_peer,
+                    tflops_with_peer=fl / ms_peer / 1e9, peer_kv_gbs=kv_bytes / ms_peer / 1e6,
+                    overhead_frac=ms_peer / ms_local - 1))
+
+
 def bench_moe(t: Timer, out: list):
     for tokens in (128, 1024):
         run, wbytes = _moe_case(tokens)
@@ -197,7 +225,7 @@ def main(argv=None):
     res: list = []
     for name in args.only.split(","):
         {"gemm": bench_gemm, "decode": bench_decode, "prefill": bench_prefill, "norm": bench_norm,
-         "moe": bench_moe}[name](t, res)
+         "moe": bench_moe, "pd_qkv": bench_pd_qkv}[name](t, res)
     for r in res:
         print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}))
 

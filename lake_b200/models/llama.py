@@ -216,6 +216,11 @@ class DecoderLM:
             ops.linear_qkv(x, self.w[p + "qkv_proj"], ws.q[:t], self.rope_cs, b.positions, b.slots, arena, i,
                            c.n_q_heads, c.n_kv_heads, b.peer_arena, b.peer_slots)
             return
+        if x.is_cuda and c.head_dim == 128:  # per-head q/k RMSNorm fused into the QKV epilogue
+            ops.linear_qkv(x, self.w[p + "qkv_proj"], ws.q[:t], self.rope_cs, b.positions, b.slots, arena, i,
+                           c.n_q_heads, c.n_kv_heads, b.peer_arena, b.peer_slots, self.w[p + "q_norm"],
+                           self.w[p + "k_norm"], c.rms_eps)
+            return
         # Qwen3: per-head RMSNorm on q and k before RoPE.
         qkv = ops.linear(x, self.w[p + "qkv_proj"], out=ws.extra["qkv"][:t])
         d = c.head_dim

@@ -8,6 +8,7 @@ PyTorch path. CPU tensors use the fp32 reference implementations in
 from __future__ import annotations
 
 import importlib
+import os
 
 _C = None
 _ERR: Exception | None = None
@@ -19,6 +20,8 @@ def native():
     if _C is None:
         try:
             _C = importlib.import_module("lake_b200._C")
+            # two-SM tcgen05 GEMM for large plain projections (LAKEB_GEMM_PAIR=0 turns it off)
+            _C.set_gemm_pair_mode(int(os.environ.get("LAKEB_GEMM_PAIR", "1") or 0))
         except ImportError as e:  # pragma: no cover - depends on the build
             _ERR = e
             raise RuntimeError(

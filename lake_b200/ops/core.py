@@ -86,11 +86,13 @@ def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | 
 def linear_qkv(a: torch.Tensor, w_qkv: torch.Tensor, q_out: torch.Tensor, rope_cs: torch.Tensor,
                positions: torch.Tensor, slots: torch.Tensor, arena: torch.Tensor, layer: int,
                n_q_heads: int, n_kv_heads: int, peer_arena: torch.Tensor | None = None,
-               peer_slots: torch.Tensor | None = None) -> torch.Tensor:
-    """QKV projection with RoPE. q -> q_out; K, V -> arena at `slots` (and peer_arena at peer_slots)."""
+               peer_slots: torch.Tensor | None = None, q_norm: torch.Tensor | None = None,
+               k_norm: torch.Tensor | None = None, qk_eps: float = 1e-6) -> torch.Tensor:
+    """QKV projection with RoPE (and, with q_norm/k_norm, per-head RMSNorm before RoPE as in
+    Qwen3). q -> q_out; K, V -> arena at `slots` (and peer_arena at peer_slots)."""
     if a.is_cuda:
         native().linear_qkv(a, w_qkv, q_out, rope_cs, positions, slots, arena, layer, n_q_heads, n_kv_heads,
-                            peer_arena, peer_slots, status_word(a.device))
+                            peer_arena, peer_slots, status_word(a.device), None, q_norm, k_norm, qk_eps)
         LAUNCHES[0] += 1
         return q_out
     acc = ref.linear(a, w_qkv)
@@ -99,6 +101,9 @@ def linear_qkv(a: torch.Tensor, w_qkv: torch.Tensor, q_out: torch.Tensor, rope_c
     q = acc[:, : n_q_heads * d].view(t, n_q_heads, d)
     k = acc[:, n_q_heads * d:(n_q_heads + n_kv_heads) * d].view(t, n_kv_heads, d)
     v = acc[:, (n_q_heads + n_kv_heads) * d:].view(t, n_kv_heads, d)
+    if q_norm is not None and k_norm is not None:
+        q = ref.rms_norm(q, q_norm, qk_eps)
+        k = ref.rms_norm(k, k_norm, qk_eps)
     q = ref.apply_rope(q, positions, rope_cs)
     k = ref.apply_rope(k, positions, rope_cs)
     q_out.copy_(q.reshape(t, -1).to(q_out.dtype))

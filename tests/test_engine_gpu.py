@@ -87,3 +87,15 @@ def test_engine_moe_matches_oracle(cuda_dev):
     torch.cuda.synchronize()
     for p, o in zip(prompts, outs):
         _check_tokens(eng.model, p, o, tol_frac=0.1)
+
+
+def test_engine_qwen3_qk_norm_matches_oracle(cuda_dev):
+    """Qwen3-style per-head q/k RMSNorm fused into the QKV epilogue."""
+    eng = LLMEngine("tiny-gpu", device="cuda:0", max_running=8, max_batched_tokens=200, max_model_len=1024,
+                    num_blocks=256, model_overrides={"qk_norm": True, "arch": "qwen3"})
+    rng = random.Random(6)
+    prompts = [[rng.randrange(eng.cfg.vocab) for _ in range(n)] for n in (3, 60, 140)]
+    outs = eng.generate(prompts, max_new_tokens=8)
+    torch.cuda.synchronize()
+    for p, o in zip(prompts, outs):
+        _check_tokens(eng.model, p, o)

@@ -194,3 +194,33 @@ def test_page_copy(cuda_dev):
     di = torch.tensor([0, 11, 5], device=cuda_dev)
     ops.page_copy(src, dst, si, di, 4096 * 2)
     assert torch.equal(dst[di], src[si])
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 4096, 4096), (777, 6144, 512), (1300, 2080, 1024), (4096, 28672, 4096)])
+def test_gemm_pair_kernel_matches_fp32(cuda_dev, m, n, k):
+    """Two-SM (cta_group::2) GEMM: plain store, residual, SwiGLU and fp32 epilogues vs fp32."""
+    from lake_b200.ops._ext import native
+
+    C = native()
+    old = C.gemm_pair_mode()
+    C.set_gemm_pair_mode(1)
+    try:
+        g = torch.Generator(device="cuda").manual_seed(m + n)
+        a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+        w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).to(torch.bfloat16)
+        want = a.float() @ w.float().t()
+        out = ops.linear(a, w)
+        assert (out.float() - want).abs().max().item() < 3e-2 * want.abs().max().item()
+        out32 = ops.linear(a, w, out_dtype=torch.float32)
+        assert (out32 - want).abs().max().item() < 1e-2 * want.abs().max().item()
+        r = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+        res = ops.linear_residual(a, w, r)
+        assert (res.float() - (want + r.float())).abs().max().item() < 3e-2 * (want + r.float()).abs().max().item()
+        if n % 256 == 0:
+            act = ops.linear_swiglu(a, w)
+            ref_act = ref.swiglu_from_interleaved(want)
+            assert (act.float() - ref_act).abs().max().item() < 3e-2 * ref_act.abs().max().item() + 1e-3
+        torch.cuda.synchronize()
+        ops.core.check_status()
+    finally:
+        C.set_gemm_pair_mode(old)
