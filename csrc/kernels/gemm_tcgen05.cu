@@ -105,14 +105,17 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tmem_empty = tmem_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* split_last = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   const int num_m = (p.M + kBM - 1) / kBM;
   const int num_m_group = p.groups ? p.group_rows / kBM : num_m;
   const int num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
-  const int num_kb = (p.K + kBK - 1) / kBK;
+  const int base_tiles = num_m * num_n;
+  const int num_tiles = base_tiles * p.splits;
+  const int num_kb_all = (p.K + kBK - 1) / kBK;
+  const int kpb = (num_kb_all + p.splits - 1) / p.splits;  // k-blocks per split
   constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
 
   if (threadIdx.x == 0) {
@@ -147,8 +150,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t ready = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         int m_blk, n_blk, grp;
-        tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+        const int split = tile / base_tiles;
+        tile_coords(tile - split * base_tiles, num_m, p.tp.m_rot, m_blk, n_blk);
         if (!tile_live(p, m_blk, num_m_group, grp)) continue;
+        const int kb0 = split * kpb, kb1 = min(num_kb_all, kb0 + kpb);
         if (ag) {
           const int r0 = m_blk * kBM;
           const int r1 = min(p.M, r0 + kBM) - 1;
@@ -162,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           fence_proxy_async_global();  // peer stores (generic proxy) before this CTA's TMA reads
         }
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) {
             ok = false;
             break;
@@ -191,17 +196,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       int t = 0;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int kb0, kb1;
         {
           int m_blk, n_blk, grp;
-          tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+          const int split = tile / base_tiles;
+          tile_coords(tile - split * base_tiles, num_m, p.tp.m_rot, m_blk, n_blk);
           if (!tile_live(p, m_blk, num_m_group, grp)) continue;
+          kb0 = split * kpb;
+          kb1 = min(num_kb_all, kb0 + kpb);
         }
         const int acc = t & 1;
         const uint32_t acc_phase = (t >> 1) & 1;
         if (!mbar_wait(&tmem_empty[acc], acc_phase ^ 1, abort_flag, p.status)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.status)) {
             ok = false;
             break;
@@ -214,7 +223,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
             // advance 16 elements (32 bytes) along K inside the swizzle row
-            umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb | k) != 0);
+            umma_f16(d_tmem, ad + 2 * k, bd + 2 * k, idesc, (kb != kb0) || (k != 0));
           }
           umma_commit(&empty[stage]);
           if (++stage == STAGES) {
@@ -233,8 +242,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     int t = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int m_blk, n_blk, grp;
-      tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+      const int split = tile / base_tiles;
+      tile_coords(tile - split * base_tiles, num_m, p.tp.m_rot, m_blk, n_blk);
       if (!tile_live(p, m_blk, num_m_group, grp)) continue;
+      (void)split;
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
       ++t;
@@ -245,6 +256,67 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.M && (!p.groups || row - grp * p.group_rows < __ldg(p.group_count + grp));
 
       if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32) {
+        if (p.splits > 1) {
+          // split-K: add this K range's partial into the fp32 workspace; the last split applies the epilogue
+          float* wrow = p.split_ws + static_cast<int64_t>(row) * p.N;
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c * 32, r);
+            tmem_ld_wait();
+            const int col0 = n_blk * BN + c * 32;
+            if (row_ok && col0 < p.N) {
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + col0 + 4 * i),
+                             "f"(__uint_as_float(r[4 * i])), "f"(__uint_as_float(r[4 * i + 1])),
+                             "f"(__uint_as_float(r[4 * i + 2])), "f"(__uint_as_float(r[4 * i + 3]))
+                             : "memory");
+            }
+          }
+          tc_fence_before();
+          mbar_arrive(&tmem_empty[acc]);  // accumulator free for the next tile
+          __threadfence();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const int tid_id = m_blk * num_n + n_blk;
+          if (warp == 2 && lane == 0) *split_last = atomicAdd(p.split_cnt + tid_id, 1) == p.splits - 1;
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (*split_last) {
+            __threadfence();
+#pragma unroll 1
+            for (int c = 0; c < BN / 32; ++c) {
+              const int col0 = n_blk * BN + c * 32;
+              if (!(row_ok && col0 < p.N)) continue;
+              float v[32];
+              float4* src = reinterpret_cast<float4*>(wrow + col0);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 f = __ldcg(src + i);
+                v[4 * i] = f.x;
+                v[4 * i + 1] = f.y;
+                v[4 * i + 2] = f.z;
+                v[4 * i + 3] = f.w;
+                __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
+              }
+              if constexpr (EPI == kEpiStoreF32) {
+                float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + row * p.ldc + col0);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              } else {
+                if constexpr (EPI == kEpiResidual) {
+                  float rv[32];
+                  load_bf16x32(p.R + row * p.ldr + col0, rv);
+#pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += rv[j];
+                }
+                store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
+              }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (warp == 2 && lane == 0) p.split_cnt[tid_id] = 0;
+          }
+          continue;  // TMEM already released
+        }
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -481,7 +553,9 @@ int launch(const GemmArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  kern<<<grid_for(a.M, a.N, BN, a.max_ctas), kThreads, S::kAlloc, stream>>>(ma, mb, a);
+  int grid = grid_for(a.M, a.N, BN, a.max_ctas) * a.splits;
+  if (grid > num_sms()) grid = num_sms();
+  kern<<<grid, kThreads, S::kAlloc, stream>>>(ma, mb, a);
   return cudaGetLastError();
 }
 
@@ -515,6 +589,45 @@ int gemm_grid(int M, int N, int epi, int max_ctas) {
 }
 
 static int g_pair_mode = 0;
+
+// Per-device split-K workspace: fp32 partial sums (zero between uses: the last split of a tile
+// zeroes what it read) and one arrival counter per tile. Allocated on first use (outside any
+// graph capture: engines run every shape once before capturing it).
+constexpr int64_t kSplitWsFloats = 16ll << 20;  // 64 MB
+constexpr int kSplitMaxTiles = 4096;
+static bool split_workspace(int64_t floats, int tiles, float** ws, int** cnt, cudaStream_t stream) {
+  static float* s_ws[16] = {};
+  static int* s_cnt[16] = {};
+  if (floats > kSplitWsFloats || tiles > kSplitMaxTiles) return false;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 16) return false;
+  if (!s_ws[dev]) {
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+      cudaGetLastError();
+      return false;  // never allocate inside a capture: this call runs unsplit
+    }
+    void* w = nullptr;
+    void* c = nullptr;
+    if (cudaMalloc(&w, kSplitWsFloats * sizeof(float)) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    if (cudaMalloc(&c, kSplitMaxTiles * sizeof(int)) != cudaSuccess) {
+      cudaGetLastError();
+      cudaFree(w);
+      return false;
+    }
+    cudaMemset(w, 0, kSplitWsFloats * sizeof(float));
+    cudaMemset(c, 0, kSplitMaxTiles * sizeof(int));
+    cudaDeviceSynchronize();
+    s_ws[dev] = static_cast<float*>(w);
+    s_cnt[dev] = static_cast<int*>(c);
+  }
+  *ws = s_ws[dev];
+  *cnt = s_cnt[dev];
+  return true;
+}
 void set_gemm_pair_mode(int mode) { g_pair_mode = mode; }
 int gemm_pair_mode() { return g_pair_mode; }
 
@@ -529,6 +642,23 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
   if (a.groups && (a.group_rows % kBM || !a.group_count || a.M != a.groups * a.group_rows)) return -8;
   if ((a.K % 8) || (a.lda % 8) || (a.ldb % 8) || (a.N % 32)) return -1;
   if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) return -2;
+  if (plain && (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiStoreF32) && a.splits <= 1) {
+    const int bn = bn_for(a.M, a.N, epi, false);
+    const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + bn - 1) / bn);
+    const int kbs = (a.K + kBK - 1) / kBK;
+    int splits = num_sms() / tiles;
+    if (splits > 8) splits = 8;
+    if (splits > kbs / 8) splits = kbs / 8;
+    if (splits >= 2) {
+      GemmArgs b = a;
+      if (split_workspace(static_cast<int64_t>(a.M) * a.N, tiles, &b.split_ws, &b.split_cnt, stream)) {
+        b.splits = splits;
+        return epi == kEpiStoreBf16 ? launch_bn<kEpiStoreBf16>(b, stream)
+                                    : epi == kEpiResidual ? launch_bn<kEpiResidual>(b, stream)
+                                                          : launch_bn<kEpiStoreF32>(b, stream);
+      }
+    }
+  }
   switch (epi) {
     case kEpiStoreBf16:
       return launch_bn<kEpiStoreBf16>(a, stream);

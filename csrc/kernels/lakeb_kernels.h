@@ -91,6 +91,11 @@ struct GemmArgs {
   int groups = 0;
   int group_rows = 0;  // multiple of 128
   const int* group_count = nullptr;
+  // split-K (small M): `splits` CTAs share a tile's K range, add partials into split_ws (fp32 [M, N],
+  // zero between uses) and the last one to finish (split_cnt per tile) applies the epilogue
+  int splits = 1;
+  float* split_ws = nullptr;
+  int* split_cnt = nullptr;
   // kEpiScatter destinations (rows indexed like A)
   const int* row_slot = nullptr;
   const int* row_rank = nullptr;

@@ -224,3 +224,23 @@ def test_gemm_pair_kernel_matches_fp32(cuda_dev, m, n, k):
         ops.core.check_status()
     finally:
         C.set_gemm_pair_mode(old)
+
+
+@pytest.mark.parametrize("m,n,k", [(200, 4096, 14336), (64, 2048, 4096), (256, 4096, 4096)])
+def test_gemm_split_k_small_m_matches_fp32(cuda_dev, m, n, k):
+    """Small-M GEMMs split K across CTAs (fp32 workspace, last split applies the epilogue);
+    repeated calls check the workspace is left zeroed."""
+    g = torch.Generator(device="cuda").manual_seed(m * 7 + n)
+    a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    w = (torch.randn(n, k, device="cuda", generator=g) / k ** 0.5).to(torch.bfloat16)
+    r = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+    want = a.float() @ w.float().t()
+    for _ in range(3):
+        out = ops.linear(a, w)
+        assert (out.float() - want).abs().max().item() < 3e-2 * want.abs().max().item()
+        res = ops.linear_residual(a, w, r)
+        assert (res.float() - (want + r.float())).abs().max().item() < 3e-2 * (want + r.float()).abs().max().item()
+        o32 = ops.linear(a, w, out_dtype=torch.float32)
+        assert (o32 - want).abs().max().item() < 1e-2 * want.abs().max().item()
+    torch.cuda.synchronize()
+    ops.core.check_status()
