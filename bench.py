@@ -245,8 +245,13 @@ def run_colocated(args, rank, local, barrier, tp=None, ep=None):
     h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    for _ in range(args.steps):
+    prof = os.environ.get("LAKEB_PROFILE_STEP")  # one timed step inside an NVTX range for `ncu --nvtx-include`
+    for i in range(args.steps):
+        if prof and i == 1:
+            torch.cuda.nvtx.range_push("profile_step")
         outs = eng.step()
+        if prof and i == 1:
+            torch.cuda.nvtx.range_pop()
         w.tokens += len(outs) if counts else 0
         w.dev_ms += eng.runner.last_device_ms
         w.count(eng)

@@ -255,68 +255,93 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int row = m_blk * kBM + row_in_tile;
       const bool row_ok = row < p.M && (!p.groups || row - grp * p.group_rows < __ldg(p.group_count + grp));
 
-      if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32) {
-        if (p.splits > 1) {
-          // split-K: add this K range's partial into the fp32 workspace; the last split applies the epilogue
-          float* wrow = p.split_ws + static_cast<int64_t>(row) * p.N;
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tbase + c * 32, r);
-            tmem_ld_wait();
-            const int col0 = n_blk * BN + c * 32;
-            if (row_ok && col0 < p.N) {
-#pragma unroll
-              for (int i = 0; i < 8; ++i)
-                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + col0 + 4 * i),
-                             "f"(__uint_as_float(r[4 * i])), "f"(__uint_as_float(r[4 * i + 1])),
-                             "f"(__uint_as_float(r[4 * i + 2])), "f"(__uint_as_float(r[4 * i + 3]))
-                             : "memory");
-            }
-          }
-          tc_fence_before();
-          mbar_arrive(&tmem_empty[acc]);  // accumulator free for the next tile
-          __threadfence();
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          const int tid_id = m_blk * num_n + n_blk;
-          if (warp == 2 && lane == 0) *split_last = atomicAdd(p.split_cnt + tid_id, 1) == p.splits - 1;
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (*split_last) {
-            __threadfence();
+      if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32 || EPI == kEpiSwiGLU) {
+          if (p.splits > 1) {
+            // split-K: add this K range's partial into the fp32 workspace; the last split applies the epilogue
+            float* wrow = p.split_ws + static_cast<int64_t>(row) * p.N;
 #pragma unroll 1
             for (int c = 0; c < BN / 32; ++c) {
+              uint32_t r[32];
+              tmem_ld32(tbase + c * 32, r);
+              tmem_ld_wait();
               const int col0 = n_blk * BN + c * 32;
-              if (!(row_ok && col0 < p.N)) continue;
-              float v[32];
-              float4* src = reinterpret_cast<float4*>(wrow + col0);
+              if (row_ok && col0 < p.N) {
 #pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                const float4 f = __ldcg(src + i);
-                v[4 * i] = f.x;
-                v[4 * i + 1] = f.y;
-                v[4 * i + 2] = f.z;
-                v[4 * i + 3] = f.w;
-                __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
-              }
-              if constexpr (EPI == kEpiStoreF32) {
-                float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + row * p.ldc + col0);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-              } else {
-                if constexpr (EPI == kEpiResidual) {
-                  float rv[32];
-                  load_bf16x32(p.R + row * p.ldr + col0, rv);
-#pragma unroll
-                  for (int j = 0; j < 32; ++j) v[j] += rv[j];
-                }
-                store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
+                for (int i = 0; i < 8; ++i)
+                  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + col0 + 4 * i),
+                               "f"(__uint_as_float(r[4 * i])), "f"(__uint_as_float(r[4 * i + 1])),
+                               "f"(__uint_as_float(r[4 * i + 2])), "f"(__uint_as_float(r[4 * i + 3]))
+                               : "memory");
               }
             }
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[acc]);  // accumulator free for the next tile
+            __threadfence();
             asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (warp == 2 && lane == 0) p.split_cnt[tid_id] = 0;
+            const int tid_id = m_blk * num_n + n_blk;
+            if (warp == 2 && lane == 0) *split_last = atomicAdd(p.split_cnt + tid_id, 1) == p.splits - 1;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if (*split_last && EPI == kEpiSwiGLU) {
+              __threadfence();
+              constexpr int H = BN / 2;
+#pragma unroll 1
+              for (int c = 0; c < H / 32; ++c) {
+                if (!row_ok) continue;
+                float v[32];
+                float4* gs = reinterpret_cast<float4*>(wrow + n_blk * BN + c * 32);
+                float4* us = reinterpret_cast<float4*>(wrow + n_blk * BN + H + c * 32);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const float4 g = __ldcg(gs + i), u = __ldcg(us + i);
+                  v[4 * i] = silu_f(g.x) * u.x;
+                  v[4 * i + 1] = silu_f(g.y) * u.y;
+                  v[4 * i + 2] = silu_f(g.z) * u.z;
+                  v[4 * i + 3] = silu_f(g.w) * u.w;
+                  __stcg(gs + i, make_float4(0.f, 0.f, 0.f, 0.f));
+                  __stcg(us + i, make_float4(0.f, 0.f, 0.f, 0.f));
+                }
+                store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + n_blk * H + c * 32, v);
+              }
+              asm volatile("bar.sync 1, 128;" ::: "memory");
+              if (warp == 2 && lane == 0) p.split_cnt[tid_id] = 0;
+            } else if (*split_last) {
+              __threadfence();
+#pragma unroll 1
+              for (int c = 0; c < BN / 32; ++c) {
+                const int col0 = n_blk * BN + c * 32;
+                if (!(row_ok && col0 < p.N)) continue;
+                float v[32];
+                float4* src = reinterpret_cast<float4*>(wrow + col0);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                  const float4 f = __ldcg(src + i);
+                  v[4 * i] = f.x;
+                  v[4 * i + 1] = f.y;
+                  v[4 * i + 2] = f.z;
+                  v[4 * i + 3] = f.w;
+                  __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
+                }
+                if constexpr (EPI == kEpiStoreF32) {
+                  float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + row * p.ldc + col0);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                } else {
+                  if constexpr (EPI == kEpiResidual) {
+                    float rv[32];
+                    load_bf16x32(p.R + row * p.ldr + col0, rv);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) v[j] += rv[j];
+                  }
+                  store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
+                }
+              }
+              asm volatile("bar.sync 1, 128;" ::: "memory");
+              if (warp == 2 && lane == 0) p.split_cnt[tid_id] = 0;
+            }
+            continue;  // TMEM already released
           }
-          continue;  // TMEM already released
-        }
+      }
+      if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -642,7 +667,8 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
   if (a.groups && (a.group_rows % kBM || !a.group_count || a.M != a.groups * a.group_rows)) return -8;
   if ((a.K % 8) || (a.lda % 8) || (a.ldb % 8) || (a.N % 32)) return -1;
   if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) return -2;
-  if (plain && (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiStoreF32) && a.splits <= 1) {
+  if (plain && (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiStoreF32 || epi == kEpiSwiGLU) &&
+      a.splits <= 1) {
     const int bn = bn_for(a.M, a.N, epi, false);
     const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + bn - 1) / bn);
     const int kbs = (a.K + kBK - 1) / kBK;
@@ -653,9 +679,12 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
       GemmArgs b = a;
       if (split_workspace(static_cast<int64_t>(a.M) * a.N, tiles, &b.split_ws, &b.split_cnt, stream)) {
         b.splits = splits;
-        return epi == kEpiStoreBf16 ? launch_bn<kEpiStoreBf16>(b, stream)
-                                    : epi == kEpiResidual ? launch_bn<kEpiResidual>(b, stream)
-                                                          : launch_bn<kEpiStoreF32>(b, stream);
+        switch (epi) {
+          case kEpiStoreBf16: return launch_bn<kEpiStoreBf16>(b, stream);
+          case kEpiResidual: return launch_bn<kEpiResidual>(b, stream);
+          case kEpiSwiGLU: return launch<256, 4, kEpiSwiGLU>(b, stream);
+          default: return launch_bn<kEpiStoreF32>(b, stream);
+        }
       }
     }
   }

@@ -48,6 +48,7 @@ class Timer:
 def bench_gemm(t: Timer, out: list):
     shapes = [(8192, 6144, 4096, "qkv"), (8192, 4096, 4096, "o_proj"), (8192, 28672, 4096, "gate_up"),
               (8192, 4096, 14336, "down"), (256, 6144, 4096, "decode_qkv"), (256, 28672, 4096, "decode_gate_up"),
+              (256, 4096, 4096, "decode_o_proj"), (256, 4096, 14336, "decode_down"),
               (256, 128256, 4096, "decode_lm_head")]
     for m, n, k, name in shapes:
         a = torch.randn(m, k, device="cuda").to(BF)

@@ -242,5 +242,9 @@ def test_gemm_split_k_small_m_matches_fp32(cuda_dev, m, n, k):
         assert (res.float() - (want + r.float())).abs().max().item() < 3e-2 * (want + r.float()).abs().max().item()
         o32 = ops.linear(a, w, out_dtype=torch.float32)
         assert (o32 - want).abs().max().item() < 1e-2 * want.abs().max().item()
+        if n % 256 == 0:
+            act = ops.linear_swiglu(a, w)
+            ref_act = ref.swiglu_from_interleaved(want)
+            assert (act.float() - ref_act).abs().max().item() < 3e-2 * ref_act.abs().max().item() + 1e-3
     torch.cuda.synchronize()
     ops.core.check_status()
