@@ -268,20 +268,30 @@ def run_colocated(args, rank, local, barrier, tp=None, ep=None):
     return w
 
 
+def pd_split(world: int) -> tuple[int, int]:
+    """(prefill, decode) instance counts. Prefill of a 2048-token prompt costs more GPU time
+    than its 256 decode steps at full batch, so ~60% of the GPUs prefill: 1+1, 2+2, 5+3."""
+    n_d = max(1, round(world * 0.4))
+    return world - n_d, n_d
+
+
 def run_pd(args, rank, world, local, group, barrier):
-    """Prefill ranks [0, N/2) each feed decode rank r + N/2. The decode rank owns the
-    requests and reserves pages; the prefill rank's QKV epilogue writes K/V straight
-    into those pages over NVLink. A step is one decode-rank iteration; prefill ranks
-    work continuously through the same window."""
+    """Prefill ranks [0, P) feed decode ranks [P, N) (prefill rank i -> decode rank P + i % D).
+    A decode rank owns its requests and reserves pages; its prefill partners' QKV epilogue
+    writes K/V straight into those pages over NVLink. A step is one decode-rank iteration;
+    prefill ranks work continuously through the same window."""
     import numpy as np
     import torch
 
     from lake_b200.ops import core as opscore
     from lake_b200.parallel import pd
 
-    half = world // 2
-    role = "prefill" if rank < half else "decode"
-    partner = rank + half if role == "prefill" else rank - half
+    n_p, n_d = pd_split(world)
+    role = "prefill" if rank < n_p else "decode"
+    if role == "prefill":
+        partner = n_p + rank % n_d  # this prefill instance's decode instance
+    else:
+        partner = [i for i in range(n_p) if i % n_d == rank - n_p]  # prefill instances feeding this one
     running = args.running if role == "decode" else args.prefill_running
     eng = _make_engine(args, local, running, shared_arena=(role == "decode"))
     job = os.environ.get("TORCHELASTIC_RUN_ID", "bench").replace("-", "")[:16] + str(os.getpid() if world == 1 else 0)
@@ -327,7 +337,7 @@ def run_pd(args, rank, world, local, group, barrier):
 
     def top_up():
         # keep the prefill partner's queue short (bounded TTFT) and the decode batch <= running
-        while len(side.pending) < args.prefill_queue and side.inflight < args.running:
+        while len(side.pending) < args.prefill_queue * len(side.links) and side.inflight < args.running:
             if not side.submit(new_prompt(args.input_len), args.output_len):
                 return
 
@@ -460,7 +470,8 @@ def main():
     if rank == 0:
         p50 = (lambda xs: sorted(xs)[len(xs) // 2] if xs else None)
         kv_gbs = sm[6].item() / (wall_ms / 1000.0) / 1e9 if sm[6].item() else None
-        par = f"pd: {world // 2} prefill + {world // 2} decode instances (tp1 each)" if mode == "pd" else (
+        n_p, n_d = pd_split(world)
+        par = f"pd: {n_p} prefill + {n_d} decode instances (tp1 each)" if mode == "pd" else (
             f"dp{world // args.tp} x tp{args.tp} (fused NVLink collectives)" if args.tp > 1 else
             f"ep{world} (experts split, attention data-parallel, fused dispatch/combine)" if ep else
             (f"dp{world}" if world > 1 else "single"))
@@ -470,7 +481,7 @@ def main():
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (uniform random token ids, random-init weights)",
             "config": {"model": _model_desc(args.model),
-                       "global_batch": args.running * (world // 2 if mode == "pd" else world // args.tp),
+                       "global_batch": args.running * (pd_split(world)[1] if mode == "pd" else world // args.tp),
                        "seq_len": args.input_len + args.output_len, "input_len": args.input_len,
                        "output_len": args.output_len, "parallelism": par, "mode": mode,
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",

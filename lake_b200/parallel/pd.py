@@ -30,10 +30,15 @@ GRANT, DONE, MARK, EXIT = 1, 2, 3, 4
 
 
 class DecodeSide:
-    def __init__(self, eng: LLMEngine, to_p: ShmRing, from_p: ShmRing):
+    """Decode instance's side of PD-split. It may be fed by several prefill instances
+    (many-to-one): each grant goes to the partner with the fewest requests outstanding."""
+
+    def __init__(self, eng: LLMEngine, links: list[tuple[ShmRing, ShmRing]]):
         self.eng = eng
-        self.to_p, self.from_p = to_p, from_p
+        self.links = links  # (to_p, from_p) per prefill partner
+        self.to_p, self.from_p = links[0]
         self.pending: dict[int, tuple] = {}
+        self.outstanding = [0] * len(links)
         self.next_idx = 0
         self.kv_bytes = 0  # prompt KV bytes P wrote into this arena
         self.page_bytes = eng.arena[0].numel() * eng.arena.element_size()
@@ -44,33 +49,40 @@ class DecodeSide:
             return False
         idx = self.next_idx
         self.next_idx += 1
-        self.pending[idx] = (list(prompt), blocks, max_new_tokens, time.perf_counter())
+        li = min(range(len(self.links)), key=lambda i: self.outstanding[i])
+        self.outstanding[li] += 1
+        self.pending[idx] = (list(prompt), blocks, max_new_tokens, time.perf_counter(), li)
         msg = np.empty(5 + len(blocks) + len(prompt), dtype=np.int64)
         msg[:4] = (GRANT, idx, max_new_tokens, len(blocks))
         msg[4:4 + len(blocks)] = blocks
         msg[4 + len(blocks)] = len(prompt)
         msg[5 + len(blocks):] = prompt
-        self.to_p.put_wait(msg)
+        self.links[li][0].put_wait(msg)
         return True
 
     def poll(self) -> int:
         n = 0
-        while True:
-            m = self.from_p.get()
-            if m is None:
-                return n
-            if m[0] == DONE:
-                idx, tok = int(m[1]), int(m[2])
-                prompt, blocks, max_new, arrival = self.pending.pop(idx)
-                self.eng.adopt_prefilled(f"pd-{idx}", prompt, tok, blocks, max_new, arrival=arrival)
-                self.kv_bytes += len(blocks) * self.page_bytes
-                n += 1
+        for _, from_p in self.links:
+            while True:
+                m = from_p.get()
+                if m is None:
+                    break
+                if m[0] == DONE:
+                    idx, tok = int(m[1]), int(m[2])
+                    prompt, blocks, max_new, arrival, li = self.pending.pop(idx)
+                    self.outstanding[li] -= 1
+                    self.eng.adopt_prefilled(f"pd-{idx}", prompt, tok, blocks, max_new, arrival=arrival)
+                    self.kv_bytes += len(blocks) * self.page_bytes
+                    n += 1
+        return n
 
     def mark(self, code: int) -> None:
-        self.to_p.put_wait([MARK, code])
+        for to_p, _ in self.links:
+            to_p.put_wait([MARK, code])
 
     def shutdown(self) -> None:
-        self.to_p.put_wait([EXIT])
+        for to_p, _ in self.links:
+            to_p.put_wait([EXIT])
 
     @property
     def inflight(self) -> int:
@@ -115,27 +127,30 @@ class PrefillSide:
         return not self.eng.has_unfinished()
 
 
-def ring_names(job: str, d_rank: int) -> tuple[str, str]:
-    return f"lakeb_{job}_d{d_rank}_to_p", f"lakeb_{job}_d{d_rank}_from_p"
+def ring_names(job: str, d_rank: int, p_rank: int) -> tuple[str, str]:
+    return f"lakeb_{job}_d{d_rank}p{p_rank}_to_p", f"lakeb_{job}_d{d_rank}p{p_rank}_from_p"
 
 
-def connect_pair(eng: LLMEngine, role: str, rank: int, partner: int, group, job: str,
+def connect_pair(eng: LLMEngine, role: str, rank: int, partner, group, job: str,
                  shm_path: str | None = None):
-    """Wire a prefill/decode pair of processes: D exports its arena and creates the rings,
-    P maps the arena and opens the rings. Collective over `group` (every rank calls it)."""
+    """Wire prefill and decode processes: each decode instance D exports its arena and
+    creates one ring pair per prefill partner; a prefill instance P maps its D's arena and
+    opens their rings. `partner` is D's list of prefill ranks (or one rank) on the decode
+    side and P's decode rank on the prefill side. Collective over `group` (every rank calls it)."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
     handle = export_tensor(eng.arena, shm_path) if role == "decode" else None
-    d_rank = rank if role == "decode" else partner
-    to_p_name, from_p_name = ring_names(job, d_rank)
     if role == "decode":
-        to_p = ShmRing(to_p_name, create=True)
-        from_p = ShmRing(from_p_name, create=True)
+        partners = list(partner) if isinstance(partner, (list, tuple)) else [partner]
+        links = []
+        for p in partners:
+            a, b = ring_names(job, rank, p)
+            links.append((ShmRing(a, create=True), ShmRing(b, create=True)))
     gathered = [None] * world
     dist.all_gather_object(gathered, (rank, role, handle), group=group)
     if role == "decode":
-        return DecodeSide(eng, to_p, from_p)
+        return DecodeSide(eng, links)
     h = [g for g in gathered if g[0] == partner][0][2]
     if eng.arena.is_cuda:
         torch.cuda.set_device(eng.arena.device)
@@ -143,6 +158,7 @@ def connect_pair(eng: LLMEngine, role: str, rank: int, partner: int, group, job:
     if peer.shape[1:] != eng.arena.shape[1:]:
         raise ValueError(f"peer arena layout {tuple(peer.shape)} does not match {tuple(eng.arena.shape)}")
     eng.runner.peer_arena = peer
+    to_p_name, from_p_name = ring_names(job, partner, rank)
     return PrefillSide(eng, ShmRing(to_p_name), ShmRing(from_p_name))
 
 

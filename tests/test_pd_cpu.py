@@ -65,3 +65,49 @@ def test_pd_split_matches_colocated(tmp_path):
     res = json.load(open(tmp_path / "res.json"))
     assert res["outs"] == res["want"]
     assert res["kv_bytes"] > 0
+
+
+def _worker_m2o(rank, port, out_dir):
+    """Two prefill ranks feed one decode rank (many-to-one)."""
+    import torch.distributed as dist
+
+    from lake_b200.engine.llm_engine import LLMEngine
+    from lake_b200.parallel import pd
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=3)
+    role = "prefill" if rank < 2 else "decode"
+    eng = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512,
+                    num_blocks=96, shared_arena=(role == "decode"))
+    partner = 2 if role == "prefill" else [0, 1]
+    side = pd.connect_pair(eng, role, rank, partner, None, job=f"m{port}", shm_path=eng.arena_path)
+    if role == "prefill":
+        pd.serve_prefill(side)
+    else:
+        prompts = _prompts()
+        for p in prompts:
+            assert side.submit(p, 6)
+        assert min(side.outstanding) >= 1  # both prefill instances got work
+        while side.inflight:
+            side.poll()
+            eng.step()
+        outs = [eng.requests[f"pd-{i}"].output for i in range(len(prompts))]
+        want = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512,
+                         num_blocks=96).generate(prompts, max_new_tokens=6)
+        side.shutdown()
+        with open(os.path.join(out_dir, "m2o.json"), "w") as f:
+            json.dump({"outs": outs, "want": want}, f)
+    dist.barrier()
+    dist.destroy_process_group()
+    if eng.arena_path:
+        from lake_b200.parallel.peer import unlink_shared
+
+        unlink_shared(eng.arena_path)
+
+
+def test_pd_many_prefill_to_one_decode(tmp_path):
+    port = _free_port()
+    mp.spawn(_worker_m2o, args=(port, str(tmp_path)), nprocs=3, join=True)
+    res = json.load(open(tmp_path / "m2o.json"))
+    assert res["outs"] == res["want"]
