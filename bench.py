@@ -57,6 +57,8 @@ def parse():
                     help="default: pd for an even number of GPUs >= 2, else colocated")
     ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (colocated mode)")
     ap.add_argument("--ep", action="store_true", help="expert parallel over all ranks (MoE models, colocated mode)")
+    ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
+                    help="projection weight format (fp8 = block-scaled e4m3, W8A16 GEMMs)")
     ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
     ap.add_argument("--prefill-queue", type=int, default=8,
                     help="pd mode: grants outstanding at a prefill rank (bounds queueing delay)")
@@ -190,7 +192,7 @@ def _make_engine(args, local, max_running, **kw):
 
     return LLMEngine(args.model, device=f"cuda:{local}", max_running=max_running, max_batched_tokens=args.budget,
                      max_model_len=args.input_len + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
-                     seed=args.seed, **kw)
+                     seed=args.seed, weight_dtype=args.weights, **kw)
 
 
 def run_colocated(args, rank, local, barrier, tp=None, ep=None):
@@ -489,7 +491,8 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "output tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if args.weights == "bf16" else "bf16 activations/KV, fp8 block-scaled weights",
             "data": "synthetic (uniform random token ids, random-init weights)",
             "config": {"model": _model_desc(args.model),
                        "global_batch": args.running * (pd_split(world)[1] if mode == "pd" else world // args.tp),

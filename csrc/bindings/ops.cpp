@@ -40,15 +40,29 @@ int* status_ptr(const c10::optional<at::Tensor>& st) {
   return st->data_ptr<int>();
 }
 
-GemmArgs base_args(const at::Tensor& a, const at::Tensor& w) {
+// w is bf16 [N, K], or fp8 e4m3 bytes (uint8 [N, K]) with w_scale fp32 [ceil(N/128), ceil(K/128)].
+GemmArgs base_args(const at::Tensor& a, const at::Tensor& w, const c10::optional<at::Tensor>& w_scale = {}) {
   check_bf16_2d(a, "A");
-  check_bf16_2d(w, "W");
   TORCH_CHECK(a.size(1) == w.size(1), "K mismatch: ", a.size(1), " vs ", w.size(1));
   GemmArgs g;
   g.A = bf(a);
   g.lda = a.stride(0);
-  g.B = bf(w);
-  g.ldb = w.stride(0);
+  if (w.scalar_type() == at::kByte) {
+    TORCH_CHECK(w.is_cuda() && w.dim() == 2 && w.stride(1) == 1, "fp8 weight must be a 2-D uint8 CUDA tensor");
+    check_aligned(w, "W8");
+    TORCH_CHECK(w_scale.has_value() && w_scale->scalar_type() == at::kFloat && w_scale->dim() == 2 &&
+                    w_scale->is_contiguous() && w_scale->size(0) == (w.size(0) + 127) / 128 &&
+                    w_scale->size(1) == (w.size(1) + 127) / 128,
+                "fp8 weight needs fp32 block scales [ceil(N/128), ceil(K/128)]");
+    g.B8 = w.data_ptr<uint8_t>();
+    g.ldb8 = w.stride(0);
+    g.b_scale = w_scale->data_ptr<float>();
+    g.b_scale_ld = static_cast<int>(w_scale->size(1));
+  } else {
+    check_bf16_2d(w, "W");
+    g.B = bf(w);
+    g.ldb = w.stride(0);
+  }
   g.M = static_cast<int>(a.size(0));
   g.N = static_cast<int>(w.size(0));
   g.K = static_cast<int>(a.size(1));
@@ -106,8 +120,8 @@ void apply_tp(GemmArgs& g, const c10::optional<py::dict>& tp) {
 
 // out = a @ w.T  (bf16 out) or fp32 out
 void linear(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c10::optional<at::Tensor> status,
-            int64_t max_ctas) {
-  GemmArgs g = base_args(a, w);
+            int64_t max_ctas, c10::optional<at::Tensor> w_scale) {
+  GemmArgs g = base_args(a, w, w_scale);
   TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) == a.size(0) && out.size(1) == w.size(0), "out shape");
   check_aligned(out, "out");
   TORCH_CHECK(out.size(0) <= 1 || out.stride(0) % 8 == 0, "out row stride must be a multiple of 8 elements");
@@ -122,8 +136,8 @@ void linear(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c10::opti
 
 // out = residual + a @ w.T   (residual may be out itself)
 void linear_residual(const at::Tensor& a, const at::Tensor& w, const at::Tensor& residual, at::Tensor& out,
-                     c10::optional<at::Tensor> status) {
-  GemmArgs g = base_args(a, w);
+                     c10::optional<at::Tensor> status, c10::optional<at::Tensor> w_scale) {
+  GemmArgs g = base_args(a, w, w_scale);
   check_bf16_2d(out, "out");
   check_bf16_2d(residual, "residual");
   TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == w.size(0) && residual.sizes() == out.sizes(), "shapes");
@@ -137,8 +151,8 @@ void linear_residual(const at::Tensor& a, const at::Tensor& w, const at::Tensor&
 
 // out[:, j] = silu(gate_j) * up_j with w rows interleaved per 256-row tile: [gate 128 | up 128]
 void linear_swiglu(const at::Tensor& a, const at::Tensor& w, at::Tensor& out, c10::optional<at::Tensor> status,
-                   c10::optional<py::dict> tp) {
-  GemmArgs g = base_args(a, w);
+                   c10::optional<py::dict> tp, c10::optional<at::Tensor> w_scale) {
+  GemmArgs g = base_args(a, w, w_scale);
   apply_tp(g, tp);
   check_bf16_2d(out, "out");
   TORCH_CHECK(w.size(0) % 256 == 0, "gate_up rows must be a multiple of 256");
@@ -155,8 +169,8 @@ void linear_qkv(const at::Tensor& a, const at::Tensor& w, at::Tensor& q_out, con
                 const at::Tensor& positions, const at::Tensor& slots, const at::Tensor& arena, int64_t layer,
                 int64_t n_q_heads, int64_t n_kv_heads, c10::optional<at::Tensor> peer_arena,
                 c10::optional<at::Tensor> peer_slots, c10::optional<at::Tensor> status, c10::optional<py::dict> tp,
-                c10::optional<at::Tensor> q_norm, c10::optional<at::Tensor> k_norm, double qk_eps) {
-  GemmArgs g = base_args(a, w);
+                c10::optional<at::Tensor> q_norm, c10::optional<at::Tensor> k_norm, double qk_eps, c10::optional<at::Tensor> w_scale) {
+  GemmArgs g = base_args(a, w, w_scale);
   apply_tp(g, tp);
   if (q_norm.has_value() && k_norm.has_value()) {
     TORCH_CHECK(q_norm->numel() == 128 && k_norm->numel() == 128 && q_norm->scalar_type() == at::kBFloat16 &&
@@ -192,8 +206,8 @@ void linear_qkv(const at::Tensor& a, const at::Tensor& w, at::Tensor& q_out, con
 
 // amax[row] = packed (value, index) of the row's argmax of a @ w.T (bitmask-filtered).
 void linear_argmax(const at::Tensor& a, const at::Tensor& w, at::Tensor& amax, c10::optional<at::Tensor> bitmask,
-                   c10::optional<at::Tensor> status, c10::optional<py::dict> tp) {
-  GemmArgs g = base_args(a, w);
+                   c10::optional<at::Tensor> status, c10::optional<py::dict> tp, c10::optional<at::Tensor> w_scale) {
+  GemmArgs g = base_args(a, w, w_scale);
   apply_tp(g, tp);
   TORCH_CHECK(amax.scalar_type() == at::kLong && amax.numel() >= a.size(0) && amax.is_contiguous(), "amax int64");
   check_aligned(amax, "amax", 8);
@@ -209,8 +223,8 @@ void linear_argmax(const at::Tensor& a, const at::Tensor& w, at::Tensor& amax, c
 }
 
 // GEMM -> reduce-scatter: each partial row of a @ w.T goes to its owner rank's receive buffer.
-void linear_rs(const at::Tensor& a, const at::Tensor& w, const py::dict& tp, c10::optional<at::Tensor> status) {
-  GemmArgs g = base_args(a, w);
+void linear_rs(const at::Tensor& a, const at::Tensor& w, const py::dict& tp, c10::optional<at::Tensor> status, c10::optional<at::Tensor> w_scale) {
+  GemmArgs g = base_args(a, w, w_scale);
   apply_tp(g, tp);
   g.ldc = w.size(0);  // receive rows are dense [world][rows_per_rank][N]
   g.status = status_ptr(status);
@@ -595,12 +609,12 @@ PYBIND11_MODULE(_C, m) {
   m.doc() = "lake_b200 sm_100a kernels";
   namespace py = pybind11;
   m.def("linear", &linear, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("status") = py::none(),
-        py::arg("max_ctas") = 0);
+        py::arg("max_ctas") = 0, py::arg("w_scale") = py::none());
   m.def("linear_residual", &linear_residual, py::arg("a"), py::arg("w"), py::arg("residual"), py::arg("out"),
-        py::arg("status") = py::none());
+        py::arg("status") = py::none(), py::arg("w_scale") = py::none());
   m.def("linear_swiglu", &linear_swiglu, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("status") = py::none(),
-        py::arg("tp") = py::none());
-  m.def("linear_rs", &linear_rs, py::arg("a"), py::arg("w"), py::arg("tp"), py::arg("status") = py::none());
+        py::arg("tp") = py::none(), py::arg("w_scale") = py::none());
+  m.def("linear_rs", &linear_rs, py::arg("a"), py::arg("w"), py::arg("tp"), py::arg("status") = py::none(), py::arg("w_scale") = py::none());
   m.def("tp_norm_push", &tp_norm_push, py::arg("h"), py::arg("w"), py::arg("eps"), py::arg("tp"),
         py::arg("status") = py::none());
   m.def("tp_argmax_combine", &tp_argmax_combine, py::arg("amax_ptrs"), py::arg("done_cnt"), py::arg("off"),
@@ -627,9 +641,9 @@ PYBIND11_MODULE(_C, m) {
         py::arg("positions"), py::arg("slots"), py::arg("arena"), py::arg("layer"), py::arg("n_q_heads"),
         py::arg("n_kv_heads"), py::arg("peer_arena") = py::none(), py::arg("peer_slots") = py::none(),
         py::arg("status") = py::none(), py::arg("tp") = py::none(), py::arg("q_norm") = py::none(),
-        py::arg("k_norm") = py::none(), py::arg("qk_eps") = 1e-6);
+        py::arg("k_norm") = py::none(), py::arg("qk_eps") = 1e-6, py::arg("w_scale") = py::none());
   m.def("linear_argmax", &linear_argmax, py::arg("a"), py::arg("w"), py::arg("amax"), py::arg("bitmask") = py::none(),
-        py::arg("status") = py::none(), py::arg("tp") = py::none());
+        py::arg("status") = py::none(), py::arg("tp") = py::none(), py::arg("w_scale") = py::none());
   m.def("paged_decode", &paged_decode, py::arg("q"), py::arg("out"), py::arg("arena"), py::arg("layer"),
         py::arg("block_tables"), py::arg("seq_lens"), py::arg("n_q_heads"), py::arg("n_kv_heads"), py::arg("scale"),
         py::arg("splits") = 1, py::arg("ws_o") = py::none(), py::arg("ws_ml") = py::none(),

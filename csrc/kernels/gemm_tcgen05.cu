@@ -17,6 +17,8 @@
 // (python/lake/engine/model_executor/models/qwen/qwen3.py:100-113,133-147,230-240),
 // which never execute there.
 #include "common.cuh"
+#include <cuda_fp8.h>
+
 #include "lakeb_kernels.h"
 #include "tma_host.h"
 
@@ -27,16 +29,47 @@ constexpr int kBM = 128;
 constexpr int kBK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kThreads = 192;
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool W8 = false>
 struct GemmSmem {
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kB8Bytes = W8 ? BN * kBK : 0;  // fp8 staging of B (W8A16)
+  static constexpr int kStageBytes = kABytes + kBBytes + kB8Bytes;
   static constexpr int kBarOffset = STAGES * kStageBytes;
-  // full[S], empty[S], tmem_full[2], tmem_empty[2], tmem slot, abort flag
-  static constexpr int kBytes = kBarOffset + (2 * STAGES + 4) * 8 + 16;
+  // full[S], empty[S], land[S] (W8), tmem_full[2], tmem_empty[2], tmem slot, abort flag, split flag
+  static constexpr int kBytes = kBarOffset + (3 * STAGES + 4) * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
+
+// Threads per CTA: TMA warp, MMA warp, 4 epilogue warps (+ 4 fp8 converter warps for W8A16).
+template <bool W8>
+constexpr int threads_of() {
+  return W8 ? 320 : 192;
+}
+
+// Dequantise one 64-byte fp8 row (64 e4m3 values of one output column n) into a bf16 row of the
+// 128-byte-swizzled K-major B tile, scaled by the row's block scale.
+__device__ __forceinline__ void convert_fp8_row(const uint8_t* src, uint8_t* dst_row, int row, float scale) {
+  const int sw = row & 7;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const uint4 u = reinterpret_cast<const uint4*>(src)[q];
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    uint32_t out[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __half2_raw lo = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[i] & 0xFFFFu), __NV_E4M3);
+      const __half2_raw hi = __nv_cvt_fp8x2_to_halfraw2(static_cast<__nv_fp8x2_storage_t>(w[i] >> 16), __NV_E4M3);
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&lo));
+      const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&hi));
+      out[2 * i] = pack_bf16x2(a.x * scale, a.y * scale);
+      out[2 * i + 1] = pack_bf16x2(b.x * scale, b.y * scale);
+    }
+    // 16 fp8 in -> 32 bytes of bf16 out = chunks 2q, 2q+1 of the 128-byte row
+    *reinterpret_cast<uint4*>(dst_row + (((2 * q) ^ sw) << 4)) = make_uint4(out[0], out[1], out[2], out[3]);
+    *reinterpret_cast<uint4*>(dst_row + (((2 * q + 1) ^ sw) << 4)) = make_uint4(out[4], out[5], out[6], out[7]);
+  }
+}
 
 __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
   uint4* d = reinterpret_cast<uint4*>(dst);
@@ -92,16 +125,17 @@ __device__ __forceinline__ bool tile_live(const GemmArgs& p, int m_blk, int num_
   return (m_blk - group * num_m_group) * 128 < __ldg(p.group_count + group);
 }
 
-template <int BN, int STAGES, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int BN, int STAGES, int EPI, bool W8 = false>
+__global__ void __launch_bounds__(threads_of<W8>(), 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const GemmArgs p) {
-  using S = GemmSmem<BN, STAGES>;
+  using S = GemmSmem<BN, STAGES, W8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kBarOffset);
   uint64_t* empty = full + STAGES;
-  uint64_t* tmem_full = empty + STAGES;
+  uint64_t* land = empty + STAGES;  // W8: A + fp8 B landed (the converters then fill full[])
+  uint64_t* tmem_full = land + STAGES;
   uint64_t* tmem_empty = tmem_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -120,8 +154,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full[s], 1);
+      mbar_init(&full[s], W8 ? 128 : 1);
       mbar_init(&empty[s], 1);
+      mbar_init(&land[s], 1);
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tmem_full[a], 1);
@@ -174,9 +209,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           uint8_t* sa = smem + stage * S::kStageBytes;
           uint8_t* sb = sa + S::kABytes;
-          mbar_expect_tx(&full[stage], S::kStageBytes);
-          tma_load_2d(sa, &tmA, &full[stage], kb * kBK, m_blk * kBM);
-          tma_load_2d(sb, &tmB, &full[stage], kb * kBK, grp * p.N + n_blk * BN);
+          if constexpr (W8) {
+            uint8_t* sb8 = sb + S::kBBytes;
+            mbar_expect_tx(&land[stage], S::kABytes + S::kB8Bytes);
+            tma_load_2d(sa, &tmA, &land[stage], kb * kBK, m_blk * kBM);
+            tma_load_2d(sb8, &tmB, &land[stage], kb * kBK, grp * p.N + n_blk * BN);
+          } else {
+            mbar_expect_tx(&full[stage], S::kStageBytes);
+            tma_load_2d(sa, &tmA, &full[stage], kb * kBK, m_blk * kBM);
+            tma_load_2d(sb, &tmB, &full[stage], kb * kBK, grp * p.N + n_blk * BN);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -185,7 +227,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) {
         // Drain loads already in flight before the CTA's shared memory is released.
-        for (int s = 0; s < STAGES; ++s) mbar_wait(&full[s], 0, nullptr, nullptr, 50000000ull);
+        for (int s = 0; s < STAGES; ++s) mbar_wait(W8 ? &land[s] : &full[s], 0, nullptr, nullptr, 50000000ull);
       }
     }
   } else if (warp == 1) {
@@ -234,6 +276,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         umma_commit(&tmem_full[acc]);
         ++t;
       }
+    }
+  } else if (W8 && warp >= 6) {
+    // ------------------------------------------------------------ fp8 -> bf16 converters (W8A16)
+    const int ct = threadIdx.x - 192;  // 0..127: rows ct and ct + 128 of the B tile
+    uint32_t stage = 0, phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int m_blk, n_blk, grp;
+      const int split = tile / base_tiles;
+      tile_coords(tile - split * base_tiles, num_m, p.tp.m_rot, m_blk, n_blk);
+      if (!tile_live(p, m_blk, num_m_group, grp)) continue;
+      const int kb0 = split * kpb, kb1 = min(num_kb_all, kb0 + kpb);
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(&land[stage], phase, abort_flag, p.status)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sb = smem + stage * S::kStageBytes + S::kABytes;
+        const uint8_t* sb8 = sb + S::kBBytes;
+        for (int row = ct; row < BN; row += 128) {
+          const int n = grp * p.N + n_blk * BN + row;
+          const float sc = (n_blk * BN + row < p.N) ? __ldg(p.b_scale + static_cast<int64_t>(n >> 7) * p.b_scale_ld +
+                                                            ((kb * kBK) >> 7))
+                                                    : 0.f;
+          convert_fp8_row(sb8 + row * kBK, sb + row * 128, row, sc);
+        }
+        fence_proxy_async_smem();  // generic stores -> visible to the tensor core's operand reads
+        mbar_arrive(&full[stage]);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1;
+        }
+      }
+      if (!ok) break;
     }
   } else {
     // ------------------------------------------------------------ epilogue
@@ -565,13 +641,19 @@ int grid_for(int M, int N, int BN, int max_ctas) {
   return grid > tiles ? tiles : grid;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, bool W8 = false>
 int launch(const GemmArgs& a, cudaStream_t stream) {
-  using S = GemmSmem<BN, STAGES>;
+  using S = GemmSmem<BN, STAGES, W8>;
+  static_assert(S::kAlloc <= 227 * 1024, "shared memory");
   CUtensorMap ma, mb;
   if (!make_bf16_map(&ma, a.A, a.M, a.K, a.lda, kBM)) return -10;
-  if (!make_bf16_map(&mb, a.B, static_cast<int64_t>(a.N) * (a.groups ? a.groups : 1), a.K, a.ldb, BN)) return -11;
-  auto kern = gemm_bf16_kernel<BN, STAGES, EPI>;
+  const int64_t brows = static_cast<int64_t>(a.N) * (a.groups ? a.groups : 1);
+  if constexpr (W8) {
+    if (!make_u8_map(&mb, a.B8, brows, a.K, a.ldb8, BN, kBK)) return -11;
+  } else {
+    if (!make_bf16_map(&mb, a.B, brows, a.K, a.ldb, BN)) return -11;
+  }
+  auto kern = gemm_bf16_kernel<BN, STAGES, EPI, W8>;
   static bool attr = false;
   if (!attr) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
@@ -580,7 +662,7 @@ int launch(const GemmArgs& a, cudaStream_t stream) {
   }
   int grid = grid_for(a.M, a.N, BN, a.max_ctas) * a.splits;
   if (grid > num_sms()) grid = num_sms();
-  kern<<<grid, kThreads, S::kAlloc, stream>>>(ma, mb, a);
+  kern<<<grid, threads_of<W8>(), S::kAlloc, stream>>>(ma, mb, a);
   return cudaGetLastError();
 }
 
@@ -658,6 +740,28 @@ int gemm_pair_mode() { return g_pair_mode; }
 
 int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
+  if (a.B8) {  // fp8 weights: converter-warp kernel, no pair / split-K variants
+    if (!a.b_scale || a.b_scale_ld <= 0 || (a.K % 64) || (a.ldb8 % 16) ||
+        (reinterpret_cast<uintptr_t>(a.B8) & 15) || (reinterpret_cast<uintptr_t>(a.A) & 15))
+      return -9;
+    switch (epi) {
+      case kEpiStoreBf16: return launch<256, 3, kEpiStoreBf16, true>(a, stream);
+      case kEpiResidual: return launch<256, 3, kEpiResidual, true>(a, stream);
+      case kEpiSwiGLU: return launch<256, 3, kEpiSwiGLU, true>(a, stream);
+      case kEpiStoreF32: return launch<256, 3, kEpiStoreF32, true>(a, stream);
+      case kEpiArgmax: return launch<256, 3, kEpiArgmax, true>(a, stream);
+      case kEpiQKV:
+        if (a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128) return -3;
+        return launch<128, 5, kEpiQKV, true>(a, stream);
+      case kEpiRSPush:
+        if (a.tp.world < 1 || a.tp.world > kMaxTP || a.tp.rows_per_rank <= 0 ||
+            a.M != a.tp.world * a.tp.rows_per_rank)
+          return -5;
+        return launch<256, 3, kEpiRSPush, true>(a, stream);
+      default:
+        return -4;
+    }
+  }
   const bool plain = !a.groups && !a.tp.ag_cnt && !a.tp.rs_cnt[0] && !a.tp.done_cnt[0] && a.max_ctas == 0;
   if (g_pair_mode && plain && a.M >= 512 &&
       (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiSwiGLU || epi == kEpiStoreF32))

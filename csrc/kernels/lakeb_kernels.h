@@ -91,6 +91,13 @@ struct GemmArgs {
   int groups = 0;
   int group_rows = 0;  // multiple of 128
   const int* group_count = nullptr;
+  // fp8 weights (W8A16): B is e4m3 [N (x groups), K] bytes with one fp32 scale per 128x128 block,
+  // b_scale[(n / 128) * b_scale_ld + k / 128]; converter warps dequantise each stage to bf16 in
+  // shared memory and the MMA runs on bf16 (kind::f16)
+  const uint8_t* B8 = nullptr;
+  int64_t ldb8 = 0;  // bytes between rows of B8
+  const float* b_scale = nullptr;
+  int b_scale_ld = 0;
   // split-K (small M): `splits` CTAs share a tile's K range, add partials into split_ws (fp32 [M, N],
   // zero between uses) and the last one to finish (split_cnt per tile) applies the epilogue
   int splits = 1;

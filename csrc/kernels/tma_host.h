@@ -15,6 +15,9 @@ bool make_bf16_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols
 bool encode_bf16_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
                      int box_cols = 64);
 
+// Byte-element 2-D map without swizzle (fp8 operands staged for conversion).
+bool make_u8_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
+                 int box_cols);
 int num_sms();
 
 }  // namespace lakeb

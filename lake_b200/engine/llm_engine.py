@@ -47,6 +47,7 @@ class EngineConfig:
     # Tensor parallel: (rank, world, process group for the handle exchange); every rank of the
     # group runs an engine with the same requests and makes the same scheduling decisions.
     tp: tuple | None = None
+    weight_dtype: str = "bf16"  # "fp8": block-scaled e4m3 projection weights (W8A16 GEMMs)
     # Expert parallel (MoE): (rank, world, process group). Each rank serves its own requests and
     # steps in lockstep with the group (a step with no work still runs the expert exchange).
     ep: tuple | None = None
@@ -98,7 +99,7 @@ class LLMEngine:
             max_tokens += world  # rows padded to a multiple of the group size
             self.tp_group = TPGroup(rank, world, self.device, max_tokens, cfg.hidden, ec.max_running, group=pg,
                                     status=None)
-            self.model = TPDecoderLM(cfg, self.tp_group, self.device, seed=ec.seed)
+            self.model = TPDecoderLM(cfg, self.tp_group, self.device, seed=ec.seed, weight_dtype=ec.weight_dtype)
             cfg = self._arena_cfg = _local_kv_cfg(cfg, world)
         elif ec.ep is not None and ec.ep[1] > 1:
             from ..parallel.ep import EPGroup
@@ -111,6 +112,8 @@ class LLMEngine:
         else:
             self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed)
             self._arena_cfg = cfg
+            if ec.weight_dtype == "fp8" and self.device.type == "cuda":
+                self.model.quantize_fp8()
         num_blocks = ec.num_blocks
         if not num_blocks:
             if self.device.type == "cuda":

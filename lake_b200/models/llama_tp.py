@@ -66,7 +66,7 @@ def shard_weights(full: dict[str, torch.Tensor], cfg: ModelConfig, rank: int, wo
 
 class TPDecoderLM:
     def __init__(self, cfg: ModelConfig, group: TPGroup, device, seed: int = 0,
-                 full_weights: dict[str, torch.Tensor] | None = None):
+                 full_weights: dict[str, torch.Tensor] | None = None, weight_dtype: str = "bf16"):
         T = group.world
         for n, what in ((cfg.n_q_heads, "q heads"), (cfg.n_kv_heads, "kv heads"), (cfg.vocab, "vocab")):
             if n % T:
@@ -97,6 +97,12 @@ class TPDecoderLM:
             self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.w = {k: v.to(self.device) for k, v in shard_weights(full_weights, cfg, self.rank, T).items()}
         del full_weights
+        if weight_dtype == "fp8":  # block-scaled e4m3 projections (W8A16 GEMMs); norms/embeddings stay bf16
+            from ..ops.fp8 import quantize_blockwise
+
+            for k in list(self.w):
+                if k.endswith(("qkv_proj", "o_proj", "gate_up_proj", "down_proj")) or k == "lm_head":
+                    self.w[k] = quantize_blockwise(self.w[k])
         torch.cuda.empty_cache()
         self.tp_world = T
 

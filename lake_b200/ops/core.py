@@ -7,6 +7,11 @@ import torch
 
 from ..oracle import ops_ref as ref
 from ._ext import native
+from .fp8 import Fp8Weight, unpack
+
+
+def _dense(w):
+    return w.dequant() if isinstance(w, Fp8Weight) else w
 
 _STATUS: dict[int, torch.Tensor] = {}
 # Number of lake_b200 kernel launches issued from Python (graph replays add their captured count).
@@ -45,10 +50,11 @@ def linear(a: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None,
     if a.is_cuda:
         if out is None:
             out = torch.empty(a.shape[0], w.shape[0], dtype=dt, device=a.device)
-        native().linear(a, w, out, status_word(a.device))
+        wq, ws = unpack(w)
+        native().linear(a, wq, out, status_word(a.device), 0, ws)
         LAUNCHES[0] += 1
         return out
-    r = ref.linear(a, w).to(dt)
+    r = ref.linear(a, _dense(w)).to(dt)
     if out is not None:
         out.copy_(r)
         return out
@@ -61,10 +67,11 @@ def linear_residual(a: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
     if a.is_cuda:
         if out is None:
             out = torch.empty_like(residual)
-        native().linear_residual(a, w, residual, out, status_word(a.device))
+        wq, ws = unpack(w)
+        native().linear_residual(a, wq, residual, out, status_word(a.device), ws)
         LAUNCHES[0] += 1
         return out
-    r = (residual.float() + ref.linear(a, w)).to(residual.dtype)
+    r = (residual.float() + ref.linear(a, _dense(w))).to(residual.dtype)
     if out is not None:
         out.copy_(r)
         return out
@@ -76,10 +83,11 @@ def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | 
     if out is None:
         out = torch.empty(a.shape[0], w_gate_up.shape[0] // 2, dtype=a.dtype, device=a.device)
     if a.is_cuda:
-        native().linear_swiglu(a, w_gate_up, out, status_word(a.device))
+        wq, ws = unpack(w_gate_up)
+        native().linear_swiglu(a, wq, out, status_word(a.device), None, ws)
         LAUNCHES[0] += 1
         return out
-    out.copy_(ref.swiglu_from_interleaved(ref.linear(a, w_gate_up)).to(out.dtype))
+    out.copy_(ref.swiglu_from_interleaved(ref.linear(a, _dense(w_gate_up))).to(out.dtype))
     return out
 
 
@@ -91,11 +99,12 @@ def linear_qkv(a: torch.Tensor, w_qkv: torch.Tensor, q_out: torch.Tensor, rope_c
     """QKV projection with RoPE (and, with q_norm/k_norm, per-head RMSNorm before RoPE as in
     Qwen3). q -> q_out; K, V -> arena at `slots` (and peer_arena at peer_slots)."""
     if a.is_cuda:
-        native().linear_qkv(a, w_qkv, q_out, rope_cs, positions, slots, arena, layer, n_q_heads, n_kv_heads,
-                            peer_arena, peer_slots, status_word(a.device), None, q_norm, k_norm, qk_eps)
+        wq, ws = unpack(w_qkv)
+        native().linear_qkv(a, wq, q_out, rope_cs, positions, slots, arena, layer, n_q_heads, n_kv_heads,
+                            peer_arena, peer_slots, status_word(a.device), None, q_norm, k_norm, qk_eps, ws)
         LAUNCHES[0] += 1
         return q_out
-    acc = ref.linear(a, w_qkv)
+    acc = ref.linear(a, _dense(w_qkv))
     t = a.shape[0]
     d = arena.shape[-1]
     q = acc[:, : n_q_heads * d].view(t, n_q_heads, d)
@@ -122,11 +131,12 @@ def linear_argmax(a: torch.Tensor, w: torch.Tensor, bitmask: torch.Tensor | None
             keys = torch.empty(m, dtype=torch.int64, device=a.device)
         if out is None:
             out = torch.empty(m, dtype=torch.int32, device=a.device)
-        native().linear_argmax(a, w, keys, bitmask, status_word(a.device))
+        wq, ws = unpack(w)
+        native().linear_argmax(a, wq, keys, bitmask, status_word(a.device), None, ws)
         native().unpack_argmax(keys, out, m)
         LAUNCHES[0] += 2
         return out
-    r = ref.greedy(ref.linear(a, w), bitmask)
+    r = ref.greedy(ref.linear(a, _dense(w)), bitmask)
     if out is not None:
         out.copy_(r)
         return out

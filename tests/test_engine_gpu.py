@@ -99,3 +99,22 @@ def test_engine_qwen3_qk_norm_matches_oracle(cuda_dev):
     torch.cuda.synchronize()
     for p, o in zip(prompts, outs):
         _check_tokens(eng.model, p, o)
+
+
+def test_engine_fp8_weights_match_dequantized_oracle(cuda_dev):
+    """Block-scaled e4m3 projection weights (W8A16 GEMMs) vs the oracle on the dequantised weights."""
+    from types import SimpleNamespace
+
+    from lake_b200.ops.fp8 import Fp8Weight
+
+    eng = LLMEngine("tiny-gpu", device="cuda:0", max_running=8, max_batched_tokens=200, max_model_len=1024,
+                    num_blocks=256, weight_dtype="fp8")
+    assert isinstance(eng.model.w["layers.0.qkv_proj"], Fp8Weight)
+    rng = random.Random(8)
+    prompts = [[rng.randrange(eng.cfg.vocab) for _ in range(n)] for n in (5, 70, 130)]
+    outs = eng.generate(prompts, max_new_tokens=6)
+    torch.cuda.synchronize()
+    oracle = SimpleNamespace(cfg=eng.model.cfg, w={k: (v.dequant(torch.bfloat16) if isinstance(v, Fp8Weight) else v)
+                                                   for k, v in eng.model.w.items()})
+    for p, o in zip(prompts, outs):
+        _check_tokens(oracle, p, o)

@@ -248,3 +248,31 @@ def test_gemm_split_k_small_m_matches_fp32(cuda_dev, m, n, k):
             assert (act.float() - ref_act).abs().max().item() < 3e-2 * ref_act.abs().max().item() + 1e-3
     torch.cuda.synchronize()
     ops.core.check_status()
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 1024, 512), (64, 4096, 4096), (2048, 2304, 1024)])
+def test_gemm_fp8_weights_match_dequantized(cuda_dev, m, n, k):
+    """W8A16: block-scaled e4m3 weights dequantised in shared memory by converter warps."""
+    from lake_b200.ops.fp8 import quantize_blockwise
+
+    g = torch.Generator(device="cuda").manual_seed(m + k)
+    a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+    w = torch.randn(n, k, device="cuda", generator=g) / k ** 0.5
+    w[:128, :128] *= 40.0  # blocks with very different scales
+    w8 = quantize_blockwise(w)
+    wd = w8.dequant().to(torch.bfloat16).float()  # the kernel rounds value x scale to bf16
+    want = a.float() @ wd.t()
+    tol = 2e-2 * want.abs().max().item()
+    out = ops.linear(a, w8)
+    assert (out.float() - want).abs().max().item() < tol
+    r = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+    res = ops.linear_residual(a, w8, r)
+    assert (res.float() - (want + r.float())).abs().max().item() < tol + 2e-2
+    if n % 256 == 0:
+        act = ops.linear_swiglu(a, w8)
+        ref_act = ref.swiglu_from_interleaved(want)
+        assert (act.float() - ref_act).abs().max().item() < 3e-2 * ref_act.abs().max().item() + 1e-3
+    toks = ops.linear_argmax(a, w8)
+    assert (toks.long().cpu() == want.argmax(-1).cpu()).float().mean().item() > 0.97
+    torch.cuda.synchronize()
+    ops.core.check_status()
