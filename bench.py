@@ -60,6 +60,7 @@ def parse():
     ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
                     help="projection weight format (fp8 = block-scaled e4m3, W8A16 GEMMs)")
     ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
+    ap.add_argument("--prefill-ranks", type=int, default=0, help="pd mode: prefill instance count (0 = ~60%%)")
     ap.add_argument("--prefill-queue", type=int, default=8,
                     help="pd mode: grants outstanding at a prefill rank (bounds queueing delay)")
     pre, _ = ap.parse_known_args()
@@ -276,9 +277,11 @@ def run_colocated(args, rank, local, barrier, tp=None, ep=None):
     return w
 
 
-def pd_split(world: int) -> tuple[int, int]:
+def pd_split(world: int, prefill_ranks: int = 0) -> tuple[int, int]:
     """(prefill, decode) instance counts. Prefill of a 2048-token prompt costs more GPU time
     than its 256 decode steps at full batch, so ~60% of the GPUs prefill: 1+1, 2+2, 5+3."""
+    if 0 < prefill_ranks < world:
+        return prefill_ranks, world - prefill_ranks
     n_d = max(1, round(world * 0.4))
     return world - n_d, n_d
 
@@ -294,7 +297,7 @@ def run_pd(args, rank, world, local, group, barrier):
     from lake_b200.ops import core as opscore
     from lake_b200.parallel import pd
 
-    n_p, n_d = pd_split(world)
+    n_p, n_d = pd_split(world, args.prefill_ranks)
     role = "prefill" if rank < n_p else "decode"
     if role == "prefill":
         partner = n_p + rank % n_d  # this prefill instance's decode instance
@@ -483,7 +486,7 @@ def main():
     if rank == 0:
         p50 = (lambda xs: sorted(xs)[len(xs) // 2] if xs else None)
         kv_gbs = sm[6].item() / (wall_ms / 1000.0) / 1e9 if sm[6].item() else None
-        n_p, n_d = pd_split(world)
+        n_p, n_d = pd_split(world, args.prefill_ranks)
         par = f"pd: {n_p} prefill + {n_d} decode instances (tp1 each)" if mode == "pd" else (
             f"dp{world // args.tp} x tp{args.tp} (fused NVLink collectives)" if args.tp > 1 else
             f"ep{world} (experts split, attention data-parallel, fused dispatch/combine)" if ep else
@@ -495,7 +498,8 @@ def main():
             "dtype": "bf16" if args.weights == "bf16" else "bf16 activations/KV, fp8 block-scaled weights",
             "data": "synthetic (uniform random token ids, random-init weights)",
             "config": {"model": _model_desc(args.model),
-                       "global_batch": args.running * (pd_split(world)[1] if mode == "pd" else world // args.tp),
+                       "global_batch": args.running * (pd_split(world, args.prefill_ranks)[1] if mode == "pd"
+                                                       else world // args.tp),
                        "seq_len": args.input_len + args.output_len, "input_len": args.input_len,
                        "output_len": args.output_len, "parallelism": par, "mode": mode,
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",

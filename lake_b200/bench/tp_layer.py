@@ -77,6 +77,22 @@ def main():
         gu = (xfull @ w_gu.t()).view(t, -1, 2, 128)
         return torch.nn.functional.silu(gu[:, :, 0]) * gu[:, :, 1]
 
+    # per-kernel split of the fused hop (CUDA events between the three launches, rank 0's view)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    split = [0.0, 0.0, 0.0]
+    for it in range(args.warmup + args.iters):
+        ev[0].record()
+        tpops.linear_rs(act, w_down, g.gemm_rs(0, mr, H))
+        ev[1].record()
+        tpops.norm_push(h, w_n, 1e-5, g.norm_push(mr, 0, 0))
+        ev[2].record()
+        tpops.linear_swiglu_ag(g.a_full[0][:t], w_gu, out_act, g.gemm_ag(0, mr))
+        ev[3].record()
+        torch.cuda.synchronize()
+        if it >= args.warmup:
+            for j in range(3):
+                split[j] += ev[j].elapsed_time(ev[j + 1]) / args.iters
+
     res = {}
     for name, fn in (("fused", fused), ("library", library)):
         for _ in range(args.warmup):
@@ -110,6 +126,8 @@ def main():
                           "speedup": round(res["library"] / res["fused"], 3), "roofline_ms": round(roof, 4),
                           "fused_frac_of_roofline": round(roof / res["fused"], 3),
                           "compute_ms_at_peak": round(t_compute, 4), "nvlink_ms_at_770": round(t_link, 4),
+                          "fused_split_ms": {"gemm_rs": round(split[0], 4), "norm_push": round(split[1], 4),
+                                             "ag_gemm_swiglu": round(split[2], 4)},
                           "peak_source": "MEASURED_PEAKS.json" if peaks else "fallback 1590 TFLOP/s"}))
     dist.barrier(group=gloo)
     dist.destroy_process_group()
