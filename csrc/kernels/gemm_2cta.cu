@@ -10,7 +10,13 @@
 //   warp 0     : TMA producer of this CTA's halves (no multicast; the pair's
 //                loads complete on the even CTA's full barrier)
 //   warp 1     : TMEM allocation (both CTAs); MMA issue + commits (even CTA)
-//   warps 2..5 : epilogue of this CTA's 128 rows (store / residual / SwiGLU / fp32)
+//   warps 2..5 : epilogue of this CTA's 128 rows (store / residual / SwiGLU / fp32 /
+//                tensor-parallel reduce-scatter push to the row owner's buffer)
+//
+// Tensor-parallel variants: with tp.ag_cnt set the producer waits, per 128-row
+// half, for the all-gather counters of the row shards it reads; with
+// tp.rs_cnt set every CTA bumps each owner's counter once its pushes are
+// visible (one count per CTA, gemm_pair_grid() of them per launch).
 //
 // Barriers: full[s] on the even CTA expects both CTAs' bytes; empty[s] and
 // tmem_full[a] live in both CTAs and receive one commit from the MMA issuer
@@ -70,6 +76,13 @@ __device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster) {
 }
 __device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster) : "memory");
+}
+
+// Pair tile t -> (256-row m-block, n-block), m fastest; tp.m_rot is in 128-row units.
+__device__ __forceinline__ void pair_tile(int tile, int num_m, int m_rot128, int& m_blk, int& n_blk) {
+  n_blk = tile / num_m;
+  m_blk = tile - n_blk * num_m + m_rot128 / 2;
+  if (m_blk >= num_m) m_blk -= num_m;
 }
 
 __device__ __forceinline__ void store32_bf16(__nv_bfloat16* dst, const float* v) {
@@ -153,9 +166,26 @@ __global__ void __launch_bounds__(kThreads2, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       bool ok = true;
+      // all-gather -> GEMM: this CTA's A rows of a peer's shard are read only after its push landed
+      const bool ag = p.tp.ag_cnt != nullptr;
+      const unsigned long long ag_target = ag ? (p.tp.ag_base ? *p.tp.ag_base : 0ull) + p.tp.ag_off : 0ull;
+      uint32_t ready = 0;
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        const int m_blk = tile % num_m;
-        const int n_blk = tile / num_m;
+        int m_blk, n_blk;
+        pair_tile(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+        if (ag) {
+          const int r0 = m_blk * 2 * kBM2 + crank * kBM2;
+          const int r1 = min(p.M, r0 + kBM2) - 1;
+          const int sh0 = p.tp.ag_all ? 0 : r0 / p.tp.rows_per_rank;
+          const int sh1 = p.tp.ag_all ? p.tp.world - 1 : (r0 <= r1 ? r1 / p.tp.rows_per_rank : -1);
+          for (int sh = sh0; sh <= sh1 && ok; ++sh) {
+            if ((ready >> sh) & 1u) continue;
+            ok = wait_counter(p.tp.ag_cnt + sh, ag_target, abort_flag, p.status);
+            ready |= 1u << sh;
+          }
+          if (!ok) break;
+          fence_proxy_async_global();
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, abort_flag, p.status)) {
             ok = false;
@@ -218,15 +248,36 @@ __global__ void __launch_bounds__(kThreads2, 1)
     const uint32_t tempty_leader0 = map_to_rank(&tmem_empty[0], 0);
     int t = 0;
     for (int tile = pair; tile < num_tiles; tile += npairs, ++t) {
-      const int m_blk = tile % num_m;
-      const int n_blk = tile / num_m;
+      int m_blk, n_blk;
+      pair_tile(tile, num_m, p.tp.m_rot, m_blk, n_blk);
       const int acc = t & 1;
       if (!mbar_wait(&tmem_full[acc], (t >> 1) & 1, abort_flag, p.status)) break;
       tc_fence_after();
       const uint32_t tbase = tmem_base + acc * kBN2 + (static_cast<uint32_t>(q * 32) << 16);
       const int row = m_blk * 2 * kBM2 + crank * kBM2 + row_in_tile;
       const bool row_ok = row < p.M;
-      if constexpr (EPI == kEpiSwiGLU) {
+      if constexpr (EPI == kEpiRSPush) {
+        // partial rows of this rank's K-slice go straight to the row's owner (P2P stores over NVLink)
+        __nv_bfloat16* dst_row = nullptr;
+        if (row_ok) {
+          const int d = row / p.tp.rows_per_rank;
+          const int lr = row - d * p.tp.rows_per_rank;
+          dst_row = p.tp.rs_recv[d] + (static_cast<int64_t>(p.tp.rank) * p.tp.rows_per_rank + lr) * p.ldc;
+        }
+#pragma unroll 1
+        for (int c = 0; c < kBN2 / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          const int col0 = n_blk * kBN2 + c * 32;
+          if (dst_row && col0 < p.N) {
+            float v[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+            store32_bf16(dst_row + col0, v);
+          }
+        }
+      } else if constexpr (EPI == kEpiSwiGLU) {
         constexpr int H = kBN2 / 2;
 #pragma unroll 1
         for (int c = 0; c < H / 32; ++c) {
@@ -273,6 +324,13 @@ __global__ void __launch_bounds__(kThreads2, 1)
       tc_fence_before();
       mbar_arrive_cluster(tempty_leader0 + acc * 8);
     }
+    // cross-GPU signal (reduce-scatter push): this CTA's stores are visible system-wide first
+    if (p.tp.rs_cnt[0]) {
+      __threadfence_system();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (warp == 2 && lane == 0 && !*abort_flag)
+        for (int d = 0; d < p.tp.world; ++d) red_add_release_sys(p.tp.rs_cnt[d] + p.tp.rank, 1ull);
+    }
   }
 
   tc_fence_before();
@@ -295,11 +353,8 @@ int launch_pair(const GemmArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  const int tiles = ((a.M + 2 * kBM2 - 1) / (2 * kBM2)) * ((a.N + kBN2 - 1) / kBN2);
-  int pairs = num_sms() / 2;
-  if (pairs > tiles) pairs = tiles;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.gridDim = dim3(gemm_pair_grid(a.M, a.N), 1, 1);
   cfg.blockDim = dim3(kThreads2, 1, 1);
   cfg.dynamicSmemBytes = kSmem2;
   cfg.stream = stream;
@@ -329,9 +384,18 @@ int gemm_bf16_pair(const GemmArgs& a, int epi, cudaStream_t stream) {
       return launch_pair<kEpiSwiGLU>(a, stream);
     case kEpiStoreF32:
       return launch_pair<kEpiStoreF32>(a, stream);
+    case kEpiRSPush:
+      return launch_pair<kEpiRSPush>(a, stream);
     default:
       return -4;
   }
+}
+
+int gemm_pair_grid(int M, int N) {
+  const int tiles = ((M + 2 * kBM2 - 1) / (2 * kBM2)) * ((N + kBN2 - 1) / kBN2);
+  int pairs = num_sms() / 2;
+  if (pairs > tiles) pairs = tiles;
+  return 2 * pairs;
 }
 
 }  // namespace lakeb

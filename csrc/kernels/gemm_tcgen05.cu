@@ -691,11 +691,21 @@ int launch_bn(const GemmArgs& a, cudaStream_t stream) {
 
 }  // namespace
 
-int gemm_grid(int M, int N, int epi, int max_ctas) {
-  return grid_for(M, N, bn_for(M, N, epi, false), max_ctas);
+static int g_pair_mode = 0;
+
+// The two-SM kernel takes large plain / residual / SwiGLU / fp32 GEMMs, including the
+// tensor-parallel all-gather GEMMs and the reduce-scatter push GEMM; QKV, argmax, grouped,
+// split-K and fp8 GEMMs stay on the single-SM kernel.
+static bool use_pair(int M, int epi, bool grouped, int max_ctas, bool done_signal) {
+  return g_pair_mode && M >= 512 && !grouped && max_ctas == 0 && !done_signal &&
+         (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiSwiGLU || epi == kEpiStoreF32 ||
+          epi == kEpiRSPush);
 }
 
-static int g_pair_mode = 0;
+int gemm_grid(int M, int N, int epi, int max_ctas) {
+  if (use_pair(M, epi, false, max_ctas, false)) return gemm_pair_grid(M, N);
+  return grid_for(M, N, bn_for(M, N, epi, false), max_ctas);
+}
 
 // Per-device split-K workspace: fp32 partial sums (zero between uses: the last split of a tile
 // zeroes what it read) and one arrival counter per tile. Allocated on first use (outside any
@@ -763,11 +773,13 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
     }
   }
   const bool plain = !a.groups && !a.tp.ag_cnt && !a.tp.rs_cnt[0] && !a.tp.done_cnt[0] && a.max_ctas == 0;
-  if (g_pair_mode && plain && a.M >= 512 &&
-      (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiSwiGLU || epi == kEpiStoreF32))
-    return gemm_bf16_pair(a, epi, stream);
   if (a.tp.ag_cnt && !a.tp.ag_all && (a.tp.rows_per_rank <= 0 || a.M > a.tp.world * a.tp.rows_per_rank)) return -6;
   if (a.tp.ag_cnt && (a.tp.world < 1 || a.tp.world > kMaxTP)) return -6;
+  if (epi == kEpiRSPush && (a.tp.world < 1 || a.tp.world > kMaxTP || a.tp.rows_per_rank <= 0 ||
+                            a.M != a.tp.world * a.tp.rows_per_rank))
+    return -5;
+  if (use_pair(a.M, epi, a.groups != 0, a.max_ctas, a.tp.done_cnt[0] != nullptr) && a.splits <= 1)
+    return gemm_bf16_pair(a, epi, stream);
   if (a.groups && (a.group_rows % kBM || !a.group_count || a.M != a.groups * a.group_rows)) return -8;
   if ((a.K % 8) || (a.lda % 8) || (a.ldb % 8) || (a.N % 32)) return -1;
   if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) return -2;

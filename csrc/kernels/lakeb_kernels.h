@@ -110,6 +110,7 @@ struct GemmArgs {
 
 // Two-SM (cta_group::2) GEMM for large M; epilogues: store bf16, residual, SwiGLU, fp32.
 int gemm_bf16_pair(const GemmArgs& args, int epi, cudaStream_t stream);
+int gemm_pair_grid(int M, int N);
 // 0 = never use the two-SM kernel from gemm_bf16, 1 = use it for large plain GEMMs (M >= 512).
 void set_gemm_pair_mode(int mode);
 int gemm_pair_mode();
