@@ -55,7 +55,8 @@ def parse():
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--mode", choices=["colocated", "pd"], default=None,
                     help="default: pd for an even number of GPUs >= 2, else colocated")
-    ap.add_argument("--tp", type=int, default=1, help="tensor-parallel group size (colocated mode)")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel instance size (pd: prefill and decode instances of this many GPUs)")
     ap.add_argument("--ep", action="store_true", help="expert parallel over all ranks (MoE models, colocated mode)")
     ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
                     help="projection weight format (fp8 = block-scaled e4m3, W8A16 GEMMs)")
@@ -286,27 +287,41 @@ def pd_split(world: int, prefill_ranks: int = 0) -> tuple[int, int]:
     return world - n_d, n_d
 
 
-def run_pd(args, rank, world, local, group, barrier):
-    """Prefill ranks [0, P) feed decode ranks [P, N) (prefill rank i -> decode rank P + i % D).
-    A decode rank owns its requests and reserves pages; its prefill partners' QKV epilogue
-    writes K/V straight into those pages over NVLink. A step is one decode-rank iteration;
-    prefill ranks work continuously through the same window."""
+def pd_layout(world: int, tp: int, prefill_instances: int = 0) -> tuple[int, int]:
+    """(prefill, decode) instance counts for instances of `tp` GPUs each."""
+    return pd_split(world // tp, prefill_instances)
+
+
+def run_pd(args, rank, world, local, group, barrier, tp_groups=None):
+    """Prefill instances [0, P) feed decode instances [P, P + D) (prefill instance i -> decode
+    instance P + i % D). An instance is `args.tp` consecutive ranks (a tensor-parallel group
+    led by its first rank) or one rank. A decode instance owns its requests and reserves
+    pages; its prefill partners' QKV epilogue writes K/V straight into those pages over
+    NVLink. A step is one decode-instance iteration; prefill instances work continuously
+    through the same window."""
     import numpy as np
     import torch
 
     from lake_b200.ops import core as opscore
     from lake_b200.parallel import pd
 
-    n_p, n_d = pd_split(world, args.prefill_ranks)
-    role = "prefill" if rank < n_p else "decode"
+    T = args.tp
+    n_p, n_d = pd_layout(world, T, args.prefill_ranks)
+    inst = rank // T
+    members = list(range(inst * T, inst * T + T))
+    leader = members[0] == rank
+    role = "prefill" if inst < n_p else "decode"
     if role == "prefill":
-        partner = n_p + rank % n_d  # this prefill instance's decode instance
+        d_inst = n_p + inst % n_d
+        partner = list(range(d_inst * T, d_inst * T + T))  # the decode instance's ranks
     else:
-        partner = [i for i in range(n_p) if i % n_d == rank - n_p]  # prefill instances feeding this one
+        partner = [i * T for i in range(n_p) if i % n_d == inst - n_p]  # leaders of the prefill instances
     running = args.running if role == "decode" else args.prefill_running
-    eng = _make_engine(args, local, running, shared_arena=(role == "decode"))
+    tp = (rank % T, T, tp_groups[inst]) if T > 1 else None
+    eng = _make_engine(args, local, running, shared_arena=(role == "decode"), tp=tp)
     job = os.environ.get("TORCHELASTIC_RUN_ID", "bench").replace("-", "")[:16] + str(os.getpid() if world == 1 else 0)
-    side = pd.connect_pair(eng, role, rank, partner, group, job=job)
+    side = pd.connect_pair(eng, role, rank, partner if T > 1 or role == "decode" else partner[0], group, job=job,
+                           members=members)
     w = Window()
     if role == "prefill":
         pd.serve_prefill(side, until_mark=1)          # populate + warm-up
@@ -317,21 +332,18 @@ def run_pd(args, rank, world, local, group, barrier):
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         n0 = side.first_tokens
-        dev = 0.0
-        while not side.exit and 2 not in side.marks:
-            side.poll()
-            if side.idle():
-                time.sleep(0.0002)
-                continue
-            side.step()
-            dev += eng.runner.last_device_ms
+        acc = {"dev": 0.0}
+
+        def on_step():
+            acc["dev"] += eng.runner.last_device_ms
             w.count(eng)
+
+        pd.serve_prefill(side, until_mark=2, on_step=on_step)
         torch.cuda.synchronize()
         w.role = "prefill"
-        side.marks.remove(2)
         w.wall_s = time.perf_counter() - t0
-        w.dev_ms = dev
-        w.tokens = side.first_tokens - n0
+        w.dev_ms = acc["dev"]
+        w.tokens = side.first_tokens - n0 if leader else 0
         w.launches = opscore.LAUNCHES[0]
         w.h2d = (eng.runner.h2d_bytes - h2d0) / max(1, args.steps)
         w.d2h = (eng.runner.d2h_bytes - d2h0) / max(1, args.steps)
@@ -339,9 +351,35 @@ def run_pd(args, rank, world, local, group, barrier):
         barrier()
         pd.serve_prefill(side)                        # until EXIT
         return w, role
+    eng.runner.capture_graphs()
+    if not leader:
+        # tensor-parallel decode follower: replay the leader's decisions and steps
+        side.follow()                                 # populate + warm-up (phase 1)
+        torch.cuda.synchronize()
+        barrier()
+        eng.runner.time_device = True
+        opscore.LAUNCHES[0] = 0
+        h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        w.role = "decode"
+
+        def on_step(outs):
+            w.dev_ms += eng.runner.last_device_ms
+            w.count(eng)
+
+        side.follow(on_step)                          # the timed window (phase 2)
+        torch.cuda.synchronize()
+        w.wall_s = time.perf_counter() - t0
+        w.launches = opscore.LAUNCHES[0]
+        w.h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
+        w.d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
+        eng.runner.time_device = False
+        barrier()
+        side.follow()                                 # until EXIT
+        return w, role
     nprng = np.random.default_rng(args.seed * 1000 + rank)
     vocab = eng.cfg.vocab
-    eng.runner.capture_graphs()
 
     def new_prompt(n):
         return nprng.integers(0, vocab, n).tolist()
@@ -359,7 +397,7 @@ def run_pd(args, rank, world, local, group, barrier):
     while len(eng.scheduler.finished) < target:
         side.poll()
         if eng.has_unfinished():
-            eng.step()
+            side.step()
         else:
             time.sleep(0.0005)
         top_up()
@@ -367,9 +405,10 @@ def run_pd(args, rank, world, local, group, barrier):
             raise RuntimeError("populate did not reach steady state in 600 s")
     for _ in range(args.warmup):
         side.poll()
-        eng.step()
+        side.step()
         top_up()
     side.mark(1)
+    side.phase(1)
     torch.cuda.synchronize()
     barrier()
     eng.runner.time_device = True
@@ -381,7 +420,7 @@ def run_pd(args, rank, world, local, group, barrier):
     w.role = "decode"
     for _ in range(args.steps):
         side.poll()
-        outs = eng.step()
+        outs = side.step()
         w.tokens += len(outs)
         w.dev_ms += eng.runner.last_device_ms
         w.count(eng)
@@ -395,6 +434,7 @@ def run_pd(args, rank, world, local, group, barrier):
     eng.runner.time_device = False
     _latency_stats(eng, t0, t0 + w.wall_s, w)
     side.mark(2)
+    side.phase(2)
     barrier()
     side.shutdown()
     return w, role
@@ -435,12 +475,13 @@ def main():
         if world > 1:
             dist.barrier(group=group)
 
-    mode = args.mode or ("pd" if world >= 2 and world % 2 == 0 and args.tp == 1 and not args.ep else "colocated")
+    if world % args.tp:
+        raise SystemExit("--tp must divide the GPU count")
+    mode = args.mode or ("pd" if world // args.tp >= 2 and not args.ep else "colocated")
     ep = (rank, world, group) if args.ep and world > 1 else None
     tp = None
+    tp_groups = None
     if args.tp > 1:
-        if mode != "colocated" or world % args.tp:
-            raise SystemExit("--tp needs colocated mode and a GPU count divisible by it")
         gid = rank // args.tp
         tp_groups = [dist.new_group(list(range(g * args.tp, (g + 1) * args.tp)), backend="gloo")
                      for g in range(world // args.tp)]
@@ -450,7 +491,7 @@ def main():
         clocks.start()
     role = "colocated"
     if mode == "pd":
-        w, role = run_pd(args, rank, world, local, group, barrier)
+        w, role = run_pd(args, rank, world, local, group, barrier, tp_groups)
     else:
         w = run_colocated(args, rank, local, barrier, tp, ep)
     ck = clocks.stop() if rank == 0 else {}
@@ -486,8 +527,8 @@ def main():
     if rank == 0:
         p50 = (lambda xs: sorted(xs)[len(xs) // 2] if xs else None)
         kv_gbs = sm[6].item() / (wall_ms / 1000.0) / 1e9 if sm[6].item() else None
-        n_p, n_d = pd_split(world, args.prefill_ranks)
-        par = f"pd: {n_p} prefill + {n_d} decode instances (tp1 each)" if mode == "pd" else (
+        n_p, n_d = pd_layout(world, args.tp, args.prefill_ranks)
+        par = f"pd: {n_p} prefill + {n_d} decode instances (tp{args.tp} each)" if mode == "pd" else (
             f"dp{world // args.tp} x tp{args.tp} (fused NVLink collectives)" if args.tp > 1 else
             f"ep{world} (experts split, attention data-parallel, fused dispatch/combine)" if ep else
             (f"dp{world}" if world > 1 else "single"))
@@ -498,8 +539,8 @@ def main():
             "dtype": "bf16" if args.weights == "bf16" else "bf16 activations/KV, fp8 block-scaled weights",
             "data": "synthetic (uniform random token ids, random-init weights)",
             "config": {"model": _model_desc(args.model),
-                       "global_batch": args.running * (pd_split(world, args.prefill_ranks)[1] if mode == "pd"
-                                                       else world // args.tp),
+                       "global_batch": args.running * (pd_layout(world, args.tp, args.prefill_ranks)[1]
+                                                       if mode == "pd" else world // args.tp),
                        "seq_len": args.input_len + args.output_len, "input_len": args.input_len,
                        "output_len": args.output_len, "parallelism": par, "mode": mode,
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",

@@ -111,3 +111,72 @@ def test_pd_many_prefill_to_one_decode(tmp_path):
     mp.spawn(_worker_m2o, args=(port, str(tmp_path)), nprocs=3, join=True)
     res = json.load(open(tmp_path / "m2o.json"))
     assert res["outs"] == res["want"]
+
+
+def _worker_groups(rank, port, out_dir):
+    """Two-rank prefill instance [0, 1] feeds a two-rank decode instance [2, 3]: the leaders
+    decide, the followers replay (page grants, adoptions, steps) through GroupCtl, and P's
+    rank i writes into D's rank i arena. Plain engines stand in for the TP shards, so every
+    rank must produce the colocated tokens."""
+    import time
+
+    import torch.distributed as dist
+
+    from lake_b200.engine.llm_engine import LLMEngine
+    from lake_b200.parallel import pd
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=4)
+    role = "prefill" if rank < 2 else "decode"
+    members = [0, 1] if role == "prefill" else [2, 3]
+    eng = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512,
+                    num_blocks=96, shared_arena=(role == "decode"))
+    partner = [2, 3] if role == "prefill" else [0]
+    side = pd.connect_pair(eng, role, rank, partner, None, job=f"g{port}", shm_path=eng.arena_path,
+                           members=members)
+    prompts = _prompts()
+    res = None
+    if role == "prefill":
+        pd.serve_prefill(side)
+        res = {"prefill_steps": side.steps}
+    elif rank == 2:
+        for p in prompts:
+            assert side.submit(p, 8)
+        t0 = time.perf_counter()
+        while side.inflight:
+            side.poll()
+            if eng.has_unfinished():
+                side.step()
+            else:
+                time.sleep(0.001)
+            assert time.perf_counter() - t0 < 120
+        side.phase(7)
+        res = {"outs": [eng.requests[f"pd-{i}"].output for i in range(len(prompts))], "kv": side.kv_bytes}
+        side.shutdown()
+    else:
+        assert side.follow() == 7
+        res = {"outs": [eng.requests[f"pd-{i}"].output for i in range(len(prompts))]}
+        assert side.follow() == -1
+    if rank == 0:
+        res["want"] = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512,
+                                num_blocks=96).generate(prompts, max_new_tokens=8)
+    with open(os.path.join(out_dir, f"g{rank}.json"), "w") as f:
+        json.dump(res, f)
+    dist.barrier()
+    dist.destroy_process_group()
+    if eng.arena_path:
+        from lake_b200.parallel.peer import unlink_shared
+
+        unlink_shared(eng.arena_path)
+
+
+def test_pd_tensor_parallel_instances_replay_leader(tmp_path):
+    port = _free_port()
+    mp.spawn(_worker_groups, args=(port, str(tmp_path)), nprocs=4, join=True)
+    r = [json.load(open(tmp_path / f"g{i}.json")) for i in range(4)]
+    want = r[0]["want"]
+    assert r[2]["outs"] == want
+    assert r[3]["outs"] == want
+    assert r[0]["prefill_steps"] == r[1]["prefill_steps"] > 0
+    assert r[2]["kv"] > 0

@@ -35,39 +35,41 @@ def _fused_numerics(rank, world, out):
 
     dev = torch.device(f"cuda:{rank}")
     H, K, I = 512, 768, 512  # hidden, K per rank (o_proj input slice), intermediate per rank
-    M = 300  # not a multiple of 128: shards straddle GEMM tiles
-    g = TPGroup(rank, world, dev, M + world, H, 64)
-    mr = g.rows_per_rank(M)
-    t = mr * world
-    gen = torch.Generator().manual_seed(100 + rank)
-    a = (torch.randn(t, K, generator=gen) * 0.5).to(torch.bfloat16)
-    w_o = (torch.randn(H, K, generator=gen) * 0.05).to(torch.bfloat16)
-    h = torch.randn(mr, H, generator=gen).to(torch.bfloat16)
-    w_n = (1.0 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(7))).to(torch.bfloat16)  # replicated
-    w_gu = (torch.randn(2 * I, H, generator=gen) * 0.05).to(torch.bfloat16)
-    parts = [None] * world
-    dist.all_gather_object(parts, (a, w_o, h))
-    # fp32 reference over the whole group
-    full = sum(ref.linear(p[0].float(), p[1].float()) for p in parts)  # [t, H]
-    h_full = torch.cat([p[2].float() for p in parts]) + full
-    h_full = h_full.to(torch.bfloat16).float()
-    y = h_full * torch.rsqrt(h_full.pow(2).mean(-1, keepdim=True) + 1e-5) * w_n.float()
-    act_ref = ref.swiglu_from_interleaved(ref.linear(y.to(torch.bfloat16).float(), w_gu.float()))
+    # 300 tokens: shards straddle 128-row tiles (single-SM kernel); 1100: the two-SM kernel's
+    # 256-row pair tiles straddle the shard boundary at row 550
+    g = TPGroup(rank, world, dev, 1100 + world, H, 64)
+    for M in (300, 1100):
+        mr = g.rows_per_rank(M)
+        t = mr * world
+        gen = torch.Generator().manual_seed(100 + rank + M)
+        a = (torch.randn(t, K, generator=gen) * 0.5).to(torch.bfloat16)
+        w_o = (torch.randn(H, K, generator=gen) * 0.05).to(torch.bfloat16)
+        h = torch.randn(mr, H, generator=gen).to(torch.bfloat16)
+        w_n = (1.0 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(7))).to(torch.bfloat16)
+        w_gu = (torch.randn(2 * I, H, generator=gen) * 0.05).to(torch.bfloat16)
+        parts = [None] * world
+        dist.all_gather_object(parts, (a, w_o, h))
+        # fp32 reference over the whole group
+        full = sum(ref.linear(p[0].float(), p[1].float()) for p in parts)  # [t, H]
+        h_full = torch.cat([p[2].float() for p in parts]) + full
+        h_full = h_full.to(torch.bfloat16).float()
+        y = h_full * torch.rsqrt(h_full.pow(2).mean(-1, keepdim=True) + 1e-5) * w_n.float()
+        act_ref = ref.swiglu_from_interleaved(ref.linear(y.to(torch.bfloat16).float(), w_gu.float()))
 
-    a_d, w_o_d, h_d, w_n_d, w_gu_d = (x.to(dev) for x in (a, w_o, h, w_n, w_gu))
-    act = torch.empty(t, I, dtype=torch.bfloat16, device=dev)
-    for _ in range(3):  # repeated calls exercise the counter totals and slot rotation
-        h_d.copy_(h.to(dev))
-        tpops.linear_rs(a_d, w_o_d, g.gemm_rs(0, mr, H))
-        tpops.norm_push(h_d, w_n_d, 1e-5, g.norm_push(mr, 0, 0))
-        tpops.linear_swiglu_ag(g.a_full[0][:t], w_gu_d, act, g.gemm_ag(0, mr))
-    torch.cuda.synchronize(dev)
-    core.check_status(dev)
-    r0 = rank * mr
-    err_h = (h_d.float().cpu() - h_full[r0:r0 + mr]).abs().max().item()
-    err_y = (g.a_full[0][:t].float().cpu() - y).abs().max().item()
-    err_act = ((act.float().cpu() - act_ref).abs().max() / act_ref.abs().max()).item()
-    out.update(err_h=err_h, err_y=err_y, err_act=err_act)
+        a_d, w_o_d, h_d, w_n_d, w_gu_d = (x.to(dev) for x in (a, w_o, h, w_n, w_gu))
+        act = torch.empty(t, I, dtype=torch.bfloat16, device=dev)
+        for _ in range(3):  # repeated calls exercise the counter totals and slot rotation
+            h_d.copy_(h.to(dev))
+            tpops.linear_rs(a_d, w_o_d, g.gemm_rs(0, mr, H))
+            tpops.norm_push(h_d, w_n_d, 1e-5, g.norm_push(mr, 0, 0))
+            tpops.linear_swiglu_ag(g.a_full[0][:t], w_gu_d, act, g.gemm_ag(0, mr))
+        torch.cuda.synchronize(dev)
+        core.check_status(dev)
+        r0 = rank * mr
+        err_h = (h_d.float().cpu() - h_full[r0:r0 + mr]).abs().max().item()
+        err_y = (g.a_full[0][:t].float().cpu() - y).abs().max().item()
+        err_act = ((act.float().cpu() - act_ref).abs().max() / act_ref.abs().max()).item()
+        out[f"m{M}"] = dict(err_h=err_h, err_y=err_y, err_act=err_act)
 
 
 def _worker(rank, world, port, out_dir):
@@ -107,9 +109,10 @@ def test_tp2_fused_collectives_and_engine(tmp_path):
     r0 = json.load(open(tmp_path / "res0.json"))
     r1 = json.load(open(tmp_path / "res1.json"))
     for r in (r0, r1):
-        assert r["err_h"] < 0.1, r
-        assert r["err_y"] < 0.1, r
-        assert r["err_act"] < 3e-2, r
+        for m in ("m300", "m1100"):
+            assert r[m]["err_h"] < 0.1, (m, r[m])
+            assert r[m]["err_y"] < 0.1, (m, r[m])
+            assert r[m]["err_act"] < 3e-2, (m, r[m])
     assert r0["outs"] == r1["outs"]  # every rank computes the same tokens
     flat_got = [t for o in r0["outs"] for t in o]
     flat_want = [t for o in r0["want"] for t in o]
