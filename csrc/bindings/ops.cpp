@@ -104,6 +104,7 @@ void apply_tp(GemmArgs& g, const c10::optional<py::dict>& tp) {
     t.ag_cnt = ptr_of<const unsigned long long>(d["ag_cnt"]);
     t.ag_off = d["ag_off"].cast<unsigned long long>();
     if (d.contains("ag_all")) t.ag_all = d["ag_all"].cast<int>();
+    if (d.contains("ag_base") && !d["ag_base"].is_none()) t.ag_base = ptr_of<const unsigned long long>(d["ag_base"]);
   }
   auto fill = [&](const char* key, auto* arr) {
     if (!d.contains(key)) return;
@@ -248,6 +249,7 @@ void tp_norm_push(at::Tensor& h, const at::Tensor& w, double eps, const py::dict
     a.recv = ptr_of<const __nv_bfloat16>(d["recv"]);
     a.rs_cnt = ptr_of<const unsigned long long>(d["rs_cnt"]);
     a.rs_off = d["rs_off"].cast<unsigned long long>();
+    if (d.contains("rs_base") && !d["rs_base"].is_none()) a.rs_base = ptr_of<const unsigned long long>(d["rs_base"]);
   }
   if (d.contains("store_h")) a.store_h = d["store_h"].cast<int>();
   py::list dst = d["dst"];
@@ -268,17 +270,27 @@ void tp_norm_push(at::Tensor& h, const at::Tensor& w, double eps, const py::dict
 }
 
 void tp_argmax_combine(const std::vector<int64_t>& amax_ptrs, int64_t done_cnt, int64_t off, at::Tensor& out,
-                       int64_t n, c10::optional<at::Tensor> status) {
+                       int64_t n, c10::optional<at::Tensor> status, int64_t base) {
   TORCH_CHECK(out.scalar_type() == at::kInt && out.is_cuda() && out.numel() >= n, "out int32");
   lakeb::TPPtrs p;
   TORCH_CHECK(amax_ptrs.size() >= 1 && amax_ptrs.size() <= static_cast<size_t>(lakeb::kMaxTP), "world");
   for (size_t i = 0; i < amax_ptrs.size(); ++i)
     p.p[i] = reinterpret_cast<const unsigned long long*>(static_cast<uintptr_t>(amax_ptrs[i]));
   LAKEB_CHECK_RC(lakeb::tp_argmax_combine(p, static_cast<int>(amax_ptrs.size()),
-                                           reinterpret_cast<const unsigned long long*>(done_cnt), nullptr,
+                                           reinterpret_cast<const unsigned long long*>(done_cnt),
+                                           reinterpret_cast<const unsigned long long*>(base),
                                            static_cast<unsigned long long>(off), out.data_ptr<int>(),
                                            static_cast<int>(n), status_ptr(status), cur_stream()),
                  "tp_argmax_combine");
+}
+
+// base[i] += deltas[i] on the current stream (captured into a graph with the deltas as constants).
+void tp_advance(int64_t base, const std::vector<int64_t>& deltas) {
+  lakeb::TPDeltas d;
+  TORCH_CHECK(base != 0 && deltas.size() <= static_cast<size_t>(lakeb::kMaxTPDeltas), "tp_advance arguments");
+  d.n = static_cast<int>(deltas.size());
+  for (size_t i = 0; i < deltas.size(); ++i) d.v[i] = static_cast<unsigned long long>(deltas[i]);
+  LAKEB_CHECK_RC(lakeb::tp_advance(reinterpret_cast<unsigned long long*>(base), d, cur_stream()), "tp_advance");
 }
 
 // Grouped expert GEMM over gathered rows: w is [groups, N, K]; rows of group g are
@@ -618,7 +630,8 @@ PYBIND11_MODULE(_C, m) {
   m.def("tp_norm_push", &tp_norm_push, py::arg("h"), py::arg("w"), py::arg("eps"), py::arg("tp"),
         py::arg("status") = py::none());
   m.def("tp_argmax_combine", &tp_argmax_combine, py::arg("amax_ptrs"), py::arg("done_cnt"), py::arg("off"),
-        py::arg("out"), py::arg("n"), py::arg("status") = py::none());
+        py::arg("out"), py::arg("n"), py::arg("status") = py::none(), py::arg("base") = 0);
+  m.def("tp_advance", &tp_advance, py::arg("base"), py::arg("deltas"));
   m.def("gemm_grouped", &gemm_grouped, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("epi"),
         py::arg("group_count"), py::arg("group_rows"), py::arg("row_slot") = py::none(),
         py::arg("row_rank") = py::none(), py::arg("dst_ptrs") = std::vector<int64_t>{}, py::arg("tp") = py::none(),
@@ -633,9 +646,9 @@ PYBIND11_MODULE(_C, m) {
   m.def("moe_dispatch_grid", []() { return lakeb::kMoEDispatchGrid; });
   m.def("set_gemm_pair_mode", [](int64_t mode) { lakeb::set_gemm_pair_mode(static_cast<int>(mode)); });
   m.def("gemm_pair_mode", []() { return lakeb::gemm_pair_mode(); });
-  m.def("gemm_grid", [](int64_t M, int64_t N, int64_t epi) {
-    return lakeb::gemm_grid(static_cast<int>(M), static_cast<int>(N), static_cast<int>(epi), 0);
-  });
+  m.def("gemm_grid", [](int64_t M, int64_t N, int64_t epi, bool w8) {
+    return lakeb::gemm_grid(static_cast<int>(M), static_cast<int>(N), static_cast<int>(epi), 0, w8);
+  }, py::arg("M"), py::arg("N"), py::arg("epi"), py::arg("w8") = false);
   m.def("tp_norm_grid", [](int64_t rows) { return lakeb::tp_norm_grid(static_cast<int>(rows)); });
   m.def("linear_qkv", &linear_qkv, py::arg("a"), py::arg("w"), py::arg("q_out"), py::arg("rope_cs"),
         py::arg("positions"), py::arg("slots"), py::arg("arena"), py::arg("layer"), py::arg("n_q_heads"),

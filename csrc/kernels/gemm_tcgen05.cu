@@ -672,7 +672,8 @@ int launch(const GemmArgs& a, cudaStream_t stream) {
 // QKV (one 128-wide head per tile), argmax and grouped GEMMs keep their widths.
 int bn_for(int M, int N, int epi, bool grouped) {
   if (epi == kEpiQKV) return 128;
-  if (epi == kEpiSwiGLU || epi == kEpiArgmax || grouped) return 256;
+  // (scatter runs only inside grouped GEMMs: the host sizes its counter waits with gemm_grid)
+  if (epi == kEpiSwiGLU || epi == kEpiArgmax || epi == kEpiScatter || grouped) return 256;
   const int target = (num_sms() * 3) / 4;
   const int mb = (M + kBM - 1) / kBM;
   // (64-wide tiles measured slower than 128 at M=256: the K loop per CTA is latency-bound either way)
@@ -702,7 +703,8 @@ static bool use_pair(int M, int epi, bool grouped, int max_ctas, bool done_signa
           epi == kEpiRSPush);
 }
 
-int gemm_grid(int M, int N, int epi, int max_ctas) {
+int gemm_grid(int M, int N, int epi, int max_ctas, bool w8) {
+  if (w8) return grid_for(M, N, epi == kEpiQKV ? 128 : 256, max_ctas);  // fp8-weight kernels: fixed widths
   if (use_pair(M, epi, false, max_ctas, false)) return gemm_pair_grid(M, N);
   return grid_for(M, N, bn_for(M, N, epi, false), max_ctas);
 }

@@ -116,7 +116,7 @@ void set_gemm_pair_mode(int mode);
 int gemm_pair_mode();
 
 // Number of CTAs gemm_bf16 launches for a shape (the per-call increment of TP counters).
-int gemm_grid(int M, int N, int epi, int max_ctas);
+int gemm_grid(int M, int N, int epi, int max_ctas, bool w8 = false);
 
 // Returns 0 on success, otherwise a cudaError_t or negative argument error.
 int gemm_bf16(const GemmArgs& args, int epi, cudaStream_t stream);
@@ -200,6 +200,12 @@ int tp_norm_grid(int rows_per_rank);
 struct TPPtrs {
   const unsigned long long* p[kMaxTP] = {};
 };
+constexpr int kMaxTPDeltas = 16;
+struct TPDeltas {
+  int n = 0;
+  unsigned long long v[kMaxTPDeltas] = {};
+};
+int tp_advance(unsigned long long* base, const TPDeltas& d, cudaStream_t stream);
 int tp_argmax_combine(const TPPtrs& amax, int world, const unsigned long long* done_cnt,
                       const unsigned long long* base, unsigned long long off, int* out, int n, int* status,
                       cudaStream_t stream);

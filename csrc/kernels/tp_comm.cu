@@ -220,4 +220,20 @@ int tp_argmax_combine(const TPPtrs& amax, int world, const unsigned long long* d
   return cudaGetLastError();
 }
 
+// Step epilogue of a tensor-parallel group: base[i] += delta[i]. Waits compare counters with
+// base + a within-step offset, so a captured step replays with fresh targets.
+namespace {
+__global__ void tp_advance_kernel(unsigned long long* base, TPDeltas d) {
+  const int i = threadIdx.x;
+  if (i < d.n) base[i] += d.v[i];
+}
+}  // namespace
+
+int tp_advance(unsigned long long* base, const TPDeltas& d, cudaStream_t stream) {
+  if (d.n <= 0) return 0;
+  if (d.n > kMaxTPDeltas) return -1;
+  tp_advance_kernel<<<1, 32, 0, stream>>>(base, d);
+  return cudaGetLastError();
+}
+
 }  // namespace lakeb

@@ -64,6 +64,7 @@ def main():
         tpops.linear_rs(act, w_down, g.gemm_rs(0, mr, H))
         tpops.norm_push(h, w_n, 1e-5, g.norm_push(mr, 0, 0))
         tpops.linear_swiglu_ag(g.a_full[0][:t], w_gu, out_act, g.gemm_ag(0, mr))
+        g.end_step()
 
     shard = torch.empty(mr, H, dtype=torch.bfloat16, device=dev)
     xfull = torch.empty(t, H, dtype=torch.bfloat16, device=dev)
@@ -87,6 +88,7 @@ def main():
         tpops.norm_push(h, w_n, 1e-5, g.norm_push(mr, 0, 0))
         ev[2].record()
         tpops.linear_swiglu_ag(g.a_full[0][:t], w_gu, out_act, g.gemm_ag(0, mr))
+        g.end_step()
         ev[3].record()
         torch.cuda.synchronize()
         if it >= args.warmup:

@@ -141,7 +141,7 @@ class LLMEngine:
         self.scheduler = Scheduler(self.pool, SchedulerConfig(ec.max_running, ec.max_batched_tokens,
                                                               ec.long_prefill_threshold, ec.max_model_len, maxb))
         self.runner = ModelRunner(self.model, self.arena, max_tokens, ec.max_running, maxb,
-                                  ec.use_cuda_graphs and self.tp_world == 1 and not (ec.ep and ec.ep[1] > 1), ec.block_size,
+                                  ec.use_cuda_graphs and not (ec.ep and ec.ep[1] > 1), ec.block_size,
                                   row_multiple=self.tp_world)
         self.requests: dict[str, Request] = {}
         self.pool_iface = None  # PoolIface (storage-pool fences), attached by attach_pool

@@ -5,7 +5,8 @@ prefill tiles, sample rows) is packed on the host into pinned staging buffers
 and copied to fixed device buffers with two ``cudaMemcpyAsync`` calls; the
 sampled token ids come back through a pinned buffer. Pure-decode steps replay
 a CUDA graph captured per batch-size bucket (all buffers have fixed
-addresses), mixed prefill/decode steps launch eagerly.
+addresses; tensor-parallel steps included, their collective targets are
+device-resident), mixed prefill/decode steps launch eagerly.
 
 Reference parity: ModelRunner.prepare_inputs / prepare_attn / execute_model
 (python/lake/engine/model_runner.py:182-323) and InputBuffers.materialize
@@ -205,10 +206,11 @@ class ModelRunner:
         if g is not None:
             return g
         splits = self._splits(bucket)
-        batch = self._batch_views(bucket, bucket, 0, bucket, bucket, splits)
+        t = bucket + (-bucket) % self.row_multiple  # rows as _pack pads them (tensor parallel)
+        batch = self._batch_views(t, bucket, 0, bucket, bucket, splits)
         # the captured replay must see valid metadata: zero-length padding sequences
         self.d_i32.zero_()
-        self.d_i64[:bucket].fill_(-1)
+        self.d_i64[:t].fill_(-1)
         self.d_i64[self.max_tokens:self.max_tokens + bucket].copy_(torch.arange(bucket, device=self.device))
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))

@@ -105,6 +105,7 @@ class TPDecoderLM:
                     self.w[k] = quantize_blockwise(self.w[k])
         torch.cuda.empty_cache()
         self.tp_world = T
+        self.fp8 = weight_dtype == "fp8"
 
     # ------------------------------------------------------------------ workspace
     def new_workspace(self, max_tokens: int, max_samples: int, max_seqs: int = 0, max_splits: int = 1) -> Workspace:
@@ -147,14 +148,14 @@ class TPDecoderLM:
                                 b.slots, arena, i, self.hq, self.hk, g.gemm_ag(ag_slot, mr), b.peer_arena,
                                 b.peer_slots)
             attn = self._attention(i, b, arena, ws, t)
-            tpops.linear_rs(attn, w[p + "o_proj"], g.gemm_rs(rs_slot, mr, c.hidden))
+            tpops.linear_rs(attn, w[p + "o_proj"], g.gemm_rs(rs_slot, mr, c.hidden, self.fp8))
             k += 1
             ag_slot = k % 2
             tpops.norm_push(h, w[p + "post_attention_layernorm"], c.rms_eps, g.norm_push(mr, rs_slot, ag_slot))
             act = ws.act[:t]
             tpops.linear_swiglu_ag(g.a_full[ag_slot][:t], w[p + "gate_up_proj"], act, g.gemm_ag(ag_slot, mr))
             rs_slot ^= 1
-            tpops.linear_rs(act, w[p + "down_proj"], g.gemm_rs(rs_slot, mr, c.hidden))
+            tpops.linear_rs(act, w[p + "down_proj"], g.gemm_rs(rs_slot, mr, c.hidden, self.fp8))
             k += 1
             if i + 1 < c.n_layers:
                 ag_slot = k % 2
@@ -169,9 +170,13 @@ class TPDecoderLM:
                                                                     store_h=False))
             rs_slot ^= 1
         if nr == 0:
+            g.end_step()
             return ws.tokens[:0]
-        tpops.linear_argmax_tp(g.fx[:nr], w["lm_head"], g.amax[:nr], g.lm_argmax(mr, nr, self.vocab_local))
-        return g.argmax_combine(ws.tokens, nr)
+        tpops.linear_argmax_tp(g.fx[:nr], w["lm_head"], g.amax[:nr],
+                               g.lm_argmax(mr, nr, self.vocab_local, self.fp8))
+        toks = g.argmax_combine(ws.tokens, nr)
+        g.end_step()
+        return toks
 
     def _attention(self, i, b, arena, ws, t):
         c = self.cfg

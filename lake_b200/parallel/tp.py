@@ -20,8 +20,13 @@ data-dependent waits that includes every reader's finish (two-deep rotation
 for all-gather and reduce-scatter, a dedicated slot for the first norm of a
 step, a dedicated lm_head buffer).
 
-Expected totals are kernel arguments, so a step that uses this group runs
-eagerly (no CUDA-graph replay, which would replay stale totals).
+Expected totals are split in two: a device-resident base per counter family
+(the totals at the start of the current step, in local memory) and a
+within-step offset that is a kernel argument. A waiting kernel compares with
+base + offset; end_step() launches a one-block kernel that adds the step's
+totals to the bases. A step's offsets and totals depend only on its shape, so
+a captured step replays with correct targets (CUDA graphs for decode) and
+eager and replayed steps mix freely.
 """
 from __future__ import annotations
 
@@ -85,6 +90,8 @@ class TPGroup:
         self.expect = {("ag", s): 0 for s in range(4)}
         self.expect.update({("rs", s): 0 for s in range(2)})
         self.expect[("done", 0)] = 0
+        self._fam = list(self.expect)  # family -> index into bases
+        self.bases = torch.zeros(len(self._fam), dtype=torch.int64, device=self.device)
         self._c = C
         dist.barrier(group=group)
 
@@ -101,6 +108,18 @@ class TPGroup:
     def _ptr(self, rank: int, name: str) -> int:
         return self.base[rank] + self.lay[name]
 
+    def _base_ptr(self, family: str, slot: int) -> int:
+        return self.bases.data_ptr() + self._fam.index((family, slot)) * 8
+
+    def end_step(self) -> None:
+        """Close a step: advance the device bases by the step's totals (stream-ordered after
+        every kernel of the step; captured along with a graph) and restart the offsets."""
+        deltas = [self.expect[f] for f in self._fam]
+        if any(deltas):
+            self._c.tp_advance(self.bases.data_ptr(), deltas)
+        for f in self._fam:
+            self.expect[f] = 0
+
     # ---------------------------------------------------------------- call builders
     def rows_per_rank(self, t: int) -> int:
         return math.ceil(t / self.world)
@@ -108,19 +127,21 @@ class TPGroup:
     def gemm_ag(self, slot: int, mr: int, wait_all: bool = False) -> dict:
         """Column-parallel GEMM over a_full[slot] (or fx): wait per row shard (or for all shards)."""
         d = dict(world=self.world, rank=self.rank, rows_per_rank=mr, ag_cnt=self._cnt_ptr(self.rank, "ag", slot),
-                 ag_off=self.expect[("ag", slot)], m_rot=0 if wait_all else (self.rank * mr) // 128)
+                 ag_off=self.expect[("ag", slot)], ag_base=self._base_ptr("ag", slot),
+                 m_rot=0 if wait_all else (self.rank * mr) // 128)
         if wait_all:
             d["rows_per_rank"] = 1 << 30
             d["ag_all"] = 1
         return d
 
-    def gemm_rs(self, slot: int, mr: int, n: int) -> dict:
-        """Row-parallel GEMM whose epilogue pushes partial rows to their owners' recv[slot]."""
+    def gemm_rs(self, slot: int, mr: int, n: int, fp8: bool = False) -> dict:
+        """Row-parallel GEMM whose epilogue pushes partial rows to their owners' recv[slot]
+        (`fp8`: block-scaled fp8 weights, whose kernel has its own grid)."""
         d = dict(world=self.world, rank=self.rank, rows_per_rank=mr,
                  m_rot=(((self.rank + 1) % self.world) * mr) // 128,
                  rs_recv=[self._ptr(r, f"r{slot}") for r in range(self.world)],
                  rs_cnt=[self._cnt_ptr(r, "rs", slot) for r in range(self.world)])
-        self.expect[("rs", slot)] += self._c.gemm_grid(self.world * mr, n, 6)
+        self.expect[("rs", slot)] += self._c.gemm_grid(self.world * mr, n, 6, fp8)
         return d
 
     def norm_push(self, mr: int, rs_slot: int | None, ag_slot: int, row_map: torch.Tensor | None = None,
@@ -135,19 +156,19 @@ class TPGroup:
                  row_map=None if row_map is None else row_map.data_ptr())
         if rs_slot is not None:
             d.update(recv=self._ptr(self.rank, f"r{rs_slot}"), rs_cnt=self._cnt_ptr(self.rank, "rs", rs_slot),
-                     rs_off=self.expect[("rs", rs_slot)])
+                     rs_off=self.expect[("rs", rs_slot)], rs_base=self._base_ptr("rs", rs_slot))
         self.expect[("ag", ag_slot)] += self._c.tp_norm_grid(mr)
         return d
 
-    def lm_argmax(self, mr_unused: int, n_rows: int, vocab_local: int) -> dict:
+    def lm_argmax(self, mr_unused: int, n_rows: int, vocab_local: int, fp8: bool = False) -> dict:
         d = self.gemm_ag(SLOT_FX, 0, wait_all=True)
         d.update(done_cnt=[self._cnt_ptr(r, "done", 0) for r in range(self.world)],
                  col_offset=self.rank * vocab_local)
-        self.expect[("done", 0)] += self._c.gemm_grid(n_rows, vocab_local, 4)
+        self.expect[("done", 0)] += self._c.gemm_grid(n_rows, vocab_local, 4, fp8)
         return d
 
     def argmax_combine(self, out: torch.Tensor, n: int) -> torch.Tensor:
         self._c.tp_argmax_combine([self._ptr(r, "amax") for r in range(self.world)],
                                   self._cnt_ptr(self.rank, "done", 0), self.expect[("done", 0)], out, n,
-                                  self.status)
+                                  self.status, self._base_ptr("done", 0))
         return out[:n]

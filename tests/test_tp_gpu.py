@@ -63,6 +63,7 @@ def _fused_numerics(rank, world, out):
             tpops.linear_rs(a_d, w_o_d, g.gemm_rs(0, mr, H))
             tpops.norm_push(h_d, w_n_d, 1e-5, g.norm_push(mr, 0, 0))
             tpops.linear_swiglu_ag(g.a_full[0][:t], w_gu_d, act, g.gemm_ag(0, mr))
+            g.end_step()
         torch.cuda.synchronize(dev)
         core.check_status(dev)
         r0 = rank * mr
@@ -86,15 +87,28 @@ def _worker(rank, world, port, out_dir):
     _fused_numerics(rank, world, res)
     rng = random.Random(5)
     prompts = [[rng.randrange(2048) for _ in range(n)] for n in (7, 64, 150, 33, 1, 90)]
+    # decode steps replay CUDA graphs (collective targets device-resident); mixed steps run eagerly
     eng = LLMEngine("tiny-gpu", device=f"cuda:{rank}", max_running=8, max_batched_tokens=256, max_model_len=1024,
-                    num_blocks=256, use_cuda_graphs=False, tp=(rank, world, None))
+                    num_blocks=256, use_cuda_graphs=True, tp=(rank, world, None))
+    eng.runner.capture_graphs()
     outs = eng.generate(prompts, max_new_tokens=8)
     core.check_status()
     res["outs"] = outs
+    del eng
+    # block-scaled fp8 weights under TP (the fp8 kernels' own grids size the counter waits)
+    eng8 = LLMEngine("tiny-gpu", device=f"cuda:{rank}", max_running=8, max_batched_tokens=256, max_model_len=1024,
+                     num_blocks=256, use_cuda_graphs=True, tp=(rank, world, None), weight_dtype="fp8")
+    eng8.runner.capture_graphs()
+    res["outs8"] = eng8.generate(prompts, max_new_tokens=8)
+    core.check_status()
+    del eng8
     if rank == 0:
         want = LLMEngine("tiny-gpu", device="cuda:0", max_running=8, max_batched_tokens=256, max_model_len=1024,
                          num_blocks=256, use_cuda_graphs=False).generate(prompts, max_new_tokens=8)
         res["want"] = want
+        res["want8"] = LLMEngine("tiny-gpu", device="cuda:0", max_running=8, max_batched_tokens=256,
+                                 max_model_len=1024, num_blocks=256, use_cuda_graphs=False,
+                                 weight_dtype="fp8").generate(prompts, max_new_tokens=8)
     with open(os.path.join(out_dir, f"res{rank}.json"), "w") as f:
         json.dump(res, f)
     dist.barrier()
@@ -118,3 +132,8 @@ def test_tp2_fused_collectives_and_engine(tmp_path):
     flat_want = [t for o in r0["want"] for t in o]
     agree = sum(a == b for a, b in zip(flat_got, flat_want)) / len(flat_want)
     assert agree >= 0.9, (agree, r0["outs"], r0["want"])
+    assert r0["outs8"] == r1["outs8"]
+    got8 = [t for o in r0["outs8"] for t in o]
+    want8 = [t for o in r0["want8"] for t in o]
+    agree8 = sum(a == b for a, b in zip(got8, want8)) / len(want8)
+    assert agree8 >= 0.9, (agree8, r0["outs8"], r0["want8"])
