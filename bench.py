@@ -53,6 +53,8 @@ def parse():
     ap.add_argument("--budget", type=int, default=8192)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--no-overlap", action="store_true",
+                    help="synchronous steps (default: schedule and launch step n+1 before finishing step n)")
     ap.add_argument("--mode", choices=["colocated", "pd"], default=None,
                     help="default: pd for an even number of GPUs >= 2, else colocated")
     ap.add_argument("--tp", type=int, default=1,
@@ -192,6 +194,7 @@ def _latency_stats(eng, t0, t1, w: Window):
 def _make_engine(args, local, max_running, **kw):
     from lake_b200.engine.llm_engine import LLMEngine
 
+    kw.setdefault("overlap", not args.no_overlap)
     return LLMEngine(args.model, device=f"cuda:{local}", max_running=max_running, max_batched_tokens=args.budget,
                      max_model_len=args.input_len + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
                      seed=args.seed, weight_dtype=args.weights, **kw)
@@ -318,7 +321,10 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None):
         partner = [i * T for i in range(n_p) if i % n_d == inst - n_p]  # leaders of the prefill instances
     running = args.running if role == "decode" else args.prefill_running
     tp = (rank % T, T, tp_groups[inst]) if T > 1 else None
-    eng = _make_engine(args, local, running, shared_arena=(role == "decode"), tp=tp)
+    # decode instances overlap host scheduling with the device; prefill instances report each
+    # first token as soon as its step completes (overlap would hold it back one long step)
+    eng = _make_engine(args, local, running, shared_arena=(role == "decode"), tp=tp,
+                       overlap=role == "decode" and not args.no_overlap)
     job = os.environ.get("TORCHELASTIC_RUN_ID", "bench").replace("-", "")[:16] + str(os.getpid() if world == 1 else 0)
     side = pd.connect_pair(eng, role, rank, partner if T > 1 or role == "decode" else partner[0], group, job=job,
                            members=members)

@@ -523,6 +523,15 @@ void chain_reject(const at::Tensor& draft, const at::Tensor& draft_off, const at
 }
 
 // Copy pages between two page-major buffers (either may be a peer GPU's buffer).
+void resolve_tokens(at::Tensor& ids, const at::Tensor& prev) {
+  TORCH_CHECK(ids.is_cuda() && prev.is_cuda() && ids.scalar_type() == at::kInt && prev.scalar_type() == at::kInt &&
+                  ids.is_contiguous() && prev.is_contiguous(),
+              "ids / prev: contiguous int32 CUDA tensors");
+  LAKEB_CHECK_RC(lakeb::resolve_tokens(ids.data_ptr<int>(), prev.data_ptr<int>(), static_cast<int>(ids.numel()),
+                                       static_cast<int>(prev.numel()), cur_stream()),
+                 "resolve_tokens");
+}
+
 void page_copy(const at::Tensor& src, at::Tensor& dst, const at::Tensor& src_ids, const at::Tensor& dst_ids,
                int64_t page_bytes, int64_t sub_off, int64_t sub_bytes) {
   TORCH_CHECK(src_ids.scalar_type() == at::kLong && dst_ids.scalar_type() == at::kLong, "ids int64");
@@ -632,6 +641,7 @@ PYBIND11_MODULE(_C, m) {
   m.def("tp_argmax_combine", &tp_argmax_combine, py::arg("amax_ptrs"), py::arg("done_cnt"), py::arg("off"),
         py::arg("out"), py::arg("n"), py::arg("status") = py::none(), py::arg("base") = 0);
   m.def("tp_advance", &tp_advance, py::arg("base"), py::arg("deltas"));
+  m.def("resolve_tokens", &resolve_tokens, py::arg("ids"), py::arg("prev"));
   m.def("gemm_grouped", &gemm_grouped, py::arg("a"), py::arg("w"), py::arg("out"), py::arg("epi"),
         py::arg("group_count"), py::arg("group_rows"), py::arg("row_slot") = py::none(),
         py::arg("row_rank") = py::none(), py::arg("dst_ptrs") = std::vector<int64_t>{}, py::arg("tp") = py::none(),

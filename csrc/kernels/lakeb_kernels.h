@@ -241,6 +241,8 @@ int moe_combine(__nv_bfloat16* h, const __nv_bfloat16* comb, const float* weight
 int wait_counters(const unsigned long long* cnt, int n, unsigned long long target, int* status,
                   cudaStream_t stream);
 
+// ids[i] < 0 -> prev[-1 - ids[i]] (tokens sampled by the previous, still in-flight step)
+int resolve_tokens(int* ids, const int* prev, int n, int n_prev, cudaStream_t stream);
 int page_copy(const void* src, void* dst, const int64_t* src_ids, const int64_t* dst_ids, int n, int64_t page_bytes,
               int64_t sub_off, int64_t sub_bytes, cudaStream_t stream);
 

@@ -211,6 +211,18 @@ __global__ void page_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __res
     d[v] = s[v];
 }
 
+// Overlapped scheduling: a token id < 0 names a token the previous step sampled on the device
+// (-1 - its sample index); resolve it from that step's output before the embedding reads it.
+__global__ void resolve_tokens_kernel(int* __restrict__ ids, const int* __restrict__ prev, int n, int n_prev) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    const int v = ids[i];
+    if (v < 0) {
+      const int j = -1 - v;
+      ids[i] = j < n_prev ? prev[j] : 0;
+    }
+  }
+}
+
 }  // namespace
 
 int rmsnorm_bf16(const __nv_bfloat16* x, int64_t sx, const __nv_bfloat16* w, __nv_bfloat16* out, int64_t so, int rows,
@@ -271,6 +283,15 @@ int page_copy(const void* src, void* dst, const int64_t* src_ids, const int64_t*
   if (gx > 64) gx = 64;
   page_copy_kernel<<<dim3(gx, n), 256, 0, stream>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst),
                                                     src_ids, dst_ids, page_bytes, sub_off, sub_bytes);
+  return cudaGetLastError();
+}
+
+int resolve_tokens(int* ids, const int* prev, int n, int n_prev, cudaStream_t stream) {
+  if (n <= 0) return 0;
+  const int threads = 256;
+  int blocks = (n + threads - 1) / threads;
+  if (blocks > 64) blocks = 64;
+  resolve_tokens_kernel<<<blocks, threads, 0, stream>>>(ids, prev, n, n_prev);
   return cudaGetLastError();
 }
 

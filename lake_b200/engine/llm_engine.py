@@ -51,6 +51,10 @@ class EngineConfig:
     # Expert parallel (MoE): (rank, world, process group). Each rank serves its own requests and
     # steps in lockstep with the group (a step with no work still runs the expert exchange).
     ep: tuple | None = None
+    # Overlapped scheduling: step() launches step n+1 before it waits for step n, so host
+    # scheduling and metadata packing hide behind the device. A step's tokens are returned by
+    # the following step() call. Not combined with a storage pool or expert parallel.
+    overlap: bool = False
 
 
 @dataclass
@@ -145,6 +149,12 @@ class LLMEngine:
                                   row_multiple=self.tp_world)
         self.requests: dict[str, Request] = {}
         self.pool_iface = None  # PoolIface (storage-pool fences), attached by attach_pool
+        self.overlap = ec.overlap and not (ec.ep and ec.ep[1] > 1)
+        self.inflight = None  # (SchedulerOutput, runner handle) of the launched, unfinished step
+        self._drained: list[StepOutput] = []
+        if self.overlap:
+            self.runner.relay = True
+            self.scheduler.before_preempt = self._drain
         self._ids = itertools.count()
         self.step_count = 0
         self.last_step: SchedulerOutput | None = None
@@ -237,7 +247,7 @@ class LLMEngine:
                                                                 self.arena.element_size()))
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.has_work()
+        return self.scheduler.has_work() or self.inflight is not None
 
     # ------------------------------------------------------------ stepping
     def step(self) -> list[StepOutput]:
@@ -245,6 +255,8 @@ class LLMEngine:
             return self._step()
 
     def _step(self) -> list[StepOutput]:
+        if self.overlap and self.pool_iface is None:
+            return self._step_overlap()
         out = self.scheduler.schedule()
         self.last_step = out
         if out.is_empty:
@@ -276,6 +288,45 @@ class LLMEngine:
                 tok = next(it)
                 res.append(StepOutput(ch.req.rid, [tok], ch.req.finished))
         return res
+
+    # ------------------------------------------------------------ overlapped stepping
+    def _step_overlap(self) -> list[StepOutput]:
+        """Schedule and launch step n+1, then finish step n (wait, fill in its tokens) and
+        return step n's outputs. Steps with token bitmasks run synchronously."""
+        out = self.scheduler.schedule()  # may drain the in-flight step to preempt
+        self.last_step = out
+        # a drain during scheduling may have finished (stop token) requests it had already placed
+        out.decode = [c for c in out.decode if c.req.status == RequestStatus.RUNNING]
+        out.prefill = [c for c in out.prefill if c.req.status == RequestStatus.RUNNING]
+        res, self._drained = self._drained, []
+        if out.is_empty:
+            return res + self._finish_inflight()
+        bitmask = self._bitmask(out)
+        if bitmask is not None:
+            res += self._finish_inflight()  # the masks apply to the tokens after the in-flight ones
+        if self.runner.peer_arena is not None:
+            self._copy_cached_to_peer(out)
+        handle = self.runner.launch(out, bitmask)
+        res += self._finish_inflight()
+        self.scheduler.advance(out)
+        self.inflight = (out, handle)
+        self.step_count += 1
+        if bitmask is not None:
+            res += self._finish_inflight()
+        return res
+
+    def _finish_inflight(self) -> list[StepOutput]:
+        if self.inflight is None:
+            return []
+        out, handle = self.inflight
+        self.inflight = None
+        sampled = self.runner.collect(handle)
+        applied = self.scheduler.resolve(out, sampled, time.perf_counter())
+        return [StepOutput(r.rid, [tok], r.finished) for r, tok in applied]
+
+    def _drain(self) -> None:
+        """Scheduler hook before a preemption: finish the in-flight step now."""
+        self._drained += self._finish_inflight()
 
     def _bitmask(self, out: SchedulerOutput):
         rows = [c.req.bitmask for c in out.chunks if c.sample]

@@ -23,6 +23,7 @@ import torch
 
 from .. import ops
 from ..models.llama import DecoderLM, ForwardBatch
+from .request import PENDING
 from .scheduler import SchedulerOutput
 
 GRAPH_BUCKETS = [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 320, 384, 448, 512]
@@ -62,7 +63,16 @@ class ModelRunner:
         self.h_i64 = torch.zeros(2 * max_tokens + max_seqs, dtype=torch.int64, pin_memory=pin)
         self.peer_off = max_tokens + max_seqs
         self.peer_arena: torch.Tensor | None = None  # decode instance's arena (IPC-mapped) for fused P->D
-        self.h_tok = torch.zeros(max_seqs, dtype=torch.int32, pin_memory=pin)
+        # sampled ids come back through two pinned buffers (one step may be in flight while the
+        # previous one is read); d_prev keeps the last step's ids on the device for the next
+        # step's PENDING inputs (overlapped scheduling)
+        self.h_toks = [torch.zeros(max_seqs, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self.h_tok = self.h_toks[0]
+        self._tok_flip = 0
+        self.d_prev = torch.zeros(max(1, max_seqs), dtype=torch.int32, device=self.device)
+        self.has_pending = False
+        self.relay = False  # keep sampled ids in d_prev (set by an engine that overlaps steps)
+        self._staged = None  # event after the last metadata copy: the pinned staging is reusable
         self.d_i32 = torch.zeros(off, dtype=torch.int32, device=self.device)
         self.d_i64 = torch.zeros(2 * max_tokens + max_seqs, dtype=torch.int64, device=self.device)
         self.np_i32 = self.h_i32.numpy()
@@ -98,6 +108,9 @@ class ModelRunner:
     # ------------------------------------------------------------ host packing
     def _pack(self, out: SchedulerOutput, pad_decode_to: int = 0):
         """Fill the pinned staging buffers. Returns (t, s, ntiles, nrows, nd)."""
+        if self._staged is not None:  # the previous step's copies may still be queued on the stream
+            self._staged.synchronize()
+            self._staged = None
         bs, maxb = self.bs, self.maxb
         ids = self._v(self.np_i32, "ids")
         pos = self._v(self.np_i32, "pos")
@@ -109,6 +122,7 @@ class ModelRunner:
         rows = self.np_i64[self.max_tokens: self.max_tokens + self.max_seqs]
         pslots = self.np_i64[self.peer_off:]
         self.has_peer = False
+        self.has_pending = False
         row = 0
         nrows = 0
         ntiles = 0
@@ -120,7 +134,11 @@ class ModelRunner:
             n = ch.n
             p0 = ch.start
             if n == 1:
-                ids[row] = req.tokens_slice(p0, p0 + 1)[0]
+                tok = req.tokens_slice(p0, p0 + 1)[0]
+                if tok == PENDING:  # sampled by the in-flight step: resolved on the device
+                    tok = -1 - req.meta["pslot"]
+                    self.has_pending = True
+                ids[row] = tok
                 pos[row] = p0
                 slots[row] = req.block_ids[p0 // bs] * bs + p0 % bs
             else:
@@ -188,6 +206,8 @@ class ModelRunner:
             o = self.peer_off
             self.d_i64[o:o + t].copy_(self.h_i64[o:o + t], non_blocking=True)
             self.h2d_bytes += t * 8
+        self._staged = torch.cuda.Event()
+        self._staged.record()
 
     # ------------------------------------------------------------ graphs
     def _bucket(self, nd: int) -> int | None:
@@ -216,12 +236,12 @@ class ModelRunner:
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             for _ in range(2):
-                self.model.forward(batch, self.arena, self.ws)
+                self._forward(batch, self.relay)
         torch.cuda.current_stream(self.device).wait_stream(s)
         graph = torch.cuda.CUDAGraph()
         c0 = ops.core.LAUNCHES[0]
         with torch.cuda.graph(graph):
-            toks = self.model.forward(batch, self.arena, self.ws)
+            toks = self._forward(batch, self.relay)
         self.graph_launches[bucket] = ops.core.LAUNCHES[0] - c0
         ops.core.LAUNCHES[0] = c0
         self.graphs[bucket] = (graph, toks)
@@ -235,14 +255,30 @@ class ModelRunner:
                 break
             self._get_graph(b)
 
+    def _forward(self, batch: ForwardBatch, resolve: bool):
+        """Model forward with the overlapped-scheduling token relay around it: PENDING inputs
+        are read from d_prev first, and this step's sampled ids are kept in d_prev after."""
+        if resolve:
+            ops.resolve_tokens(batch.input_ids, self.d_prev)
+        toks = self.model.forward(batch, self.arena, self.ws)
+        n = toks.shape[0]
+        if n and self.relay:
+            self.d_prev[:n].copy_(toks[:n])
+        return toks
+
     # ------------------------------------------------------------ execute
     def execute(self, out: SchedulerOutput, bitmask: torch.Tensor | None = None) -> list[int]:
         """Run one step; returns one sampled token per sampling chunk (chunk order).
 
         Requests with ``remote_blocks`` (prefill for a decode instance) get their
         K/V rows written into ``self.peer_arena`` too, by the QKV epilogue."""
+        return self.collect(self.launch(out, bitmask))
+
+    def launch(self, out: SchedulerOutput, bitmask: torch.Tensor | None = None):
+        """Enqueue one step (metadata copies, graph replay or eager forward, the async copy of
+        the sampled ids to a pinned buffer) without waiting for it; collect() returns its ids."""
         if out.is_empty:
-            return []
+            return None
         nd = len(out.decode)
         has_remote = any(c.req.remote_blocks is not None for c in out.prefill)
         pure_decode = not out.prefill and bitmask is None
@@ -252,8 +288,8 @@ class ModelRunner:
         if not self.cuda:
             self._copy_cpu(t, s, nrows)
             batch = self._batch_views(t, s, ntiles, nrows, nd_eff, 1, bitmask, has_remote)
-            toks = self.model.forward(batch, self.arena, self.ws)
-            return toks[: len([c for c in out.chunks if c.sample])].tolist()
+            toks = self._forward(batch, self.has_pending)
+            return ("cpu", toks[: len([c for c in out.chunks if c.sample])].tolist())
         graph = None
         if bucket is not None:
             graph, toks = self._get_graph(bucket)  # capture (if new) before this step's metadata lands
@@ -268,16 +304,29 @@ class ModelRunner:
             ops.core.LAUNCHES[0] += self.graph_launches[bucket]
         else:
             batch = self._batch_views(t, s, ntiles, nrows, nd_eff, self._splits(nd_eff), bitmask, has_remote)
-            toks = self.model.forward(batch, self.arena, self.ws)
+            toks = self._forward(batch, self.has_pending)
         if ev1 is not None:
             ev1.record()
         nsamp = sum(1 for c in out.chunks if c.sample)
-        self.h_tok[:nsamp].copy_(toks[:nsamp], non_blocking=True)
+        h = self.h_toks[self._tok_flip]
+        self._tok_flip ^= 1
+        h[:nsamp].copy_(toks[:nsamp], non_blocking=True)
         self.d2h_bytes += nsamp * 4
-        torch.cuda.current_stream(self.device).synchronize()
+        done = torch.cuda.Event()
+        done.record()
+        return ("cuda", h, nsamp, done, ev0, ev1)
+
+    def collect(self, handle) -> list[int]:
+        """Wait for a launched step and return its sampled ids (chunk order)."""
+        if handle is None:
+            return []
+        if handle[0] == "cpu":
+            return handle[1]
+        _, h, nsamp, done, ev0, ev1 = handle
+        done.synchronize()
         if ev1 is not None:
             self.last_device_ms = ev0.elapsed_time(ev1)
-        return self.h_tok[:nsamp].tolist()
+        return h[:nsamp].tolist()
 
     def execute_null(self) -> None:
         """A zero-token forward: every collective the model issues still runs (expert parallel)."""

@@ -6,6 +6,11 @@ import time
 from dataclasses import dataclass, field
 
 
+# Placeholder for a token an in-flight step is still sampling (overlapped scheduling); the
+# engine replaces it when the step completes. Real token ids are >= 0.
+PENDING = -1
+
+
 class RequestStatus(enum.Enum):
     WAITING = "waiting"
     RUNNING = "running"

@@ -7,9 +7,18 @@ chunks of their prompt (chunked prefill, optionally capped by
 the block pool. When pages run out the most recently admitted request is
 preempted and later recomputed.
 
+Overlapped scheduling (one step in flight): advance() applies a launched step
+to the host state before its tokens exist (positions advance, each sampled
+request gets a PENDING token, length limits finish requests), so the next step
+can be scheduled and launched while the device still runs this one; resolve()
+fills the tokens in when the step completes and applies stop tokens. Before a
+preemption the engine finishes the in-flight step (before_preempt), so a
+preempted request never carries a PENDING token into its recomputed prompt.
+
 Reference parity: the budget / decode-priority / chunked-extend policy of
-python/lake/runtime/node_scheduler.py:396-599 (Pass A decode, Pass B extend)
-and the admission check against max_model_length (:96-103).
+python/lake/runtime/node_scheduler.py:396-599 (Pass A decode, Pass B extend),
+the admission check against max_model_length (:96-103) and the overlap loop
+with its FutureMap token relay (node_scheduler.py:190-228, future_map.py:13-30).
 """
 from __future__ import annotations
 
@@ -17,7 +26,7 @@ from collections import deque
 from dataclasses import dataclass, field
 
 from .block_pool import BlockPool, chain_block_hashes
-from .request import Request, RequestStatus
+from .request import PENDING, Request, RequestStatus
 
 
 @dataclass
@@ -67,6 +76,7 @@ class Scheduler:
         self.step_id = 0
         self.finished: list[Request] = []
         self.on_admit = None  # callback(req) before the prefix lookup of an admission (tier promotion)
+        self.before_preempt = None  # callback() before a preemption (overlap: finish the in-flight step)
 
     # -------------------------------------------------------------- admission
     def add(self, req: Request) -> None:
@@ -129,6 +139,11 @@ class Scheduler:
 
     def _ensure_blocks(self, req: Request, upto: int, out: SchedulerOutput) -> bool:
         need = self._blocks_needed(req, upto)
+        if need and not self.pool.can_alloc(need) and self.before_preempt is not None:
+            self.before_preempt()  # may finish requests and free their pages
+            if req.status != RequestStatus.RUNNING:
+                return False
+            need = self._blocks_needed(req, upto)
         while need and not self.pool.can_alloc(need):
             victim = self._preempt_last(protect=req)
             if victim is None:
@@ -225,6 +240,64 @@ class Scheduler:
             self._release(req)
             self.finished.append(req)
         return done
+
+    # -------------------------------------------------------------- overlapped steps
+    def advance(self, out: SchedulerOutput) -> None:
+        """A step was launched: advance positions, give each sampled request a PENDING token
+        (meta['pslot'] = its index among the step's samples) and finish requests that reach
+        their length limit (pages released now: later steps run after this one on the stream)."""
+        j = 0
+        for ch in out.chunks:
+            req = ch.req
+            slot = j
+            if ch.sample:
+                j += 1
+            if req.status != RequestStatus.RUNNING:
+                continue
+            req.num_computed = ch.start + ch.n
+            self._register_full_blocks(req)
+            if not ch.sample:
+                continue
+            req.output.append(PENDING)
+            req.meta["pslot"] = slot
+            if len(req.output) >= req.params.max_new_tokens:
+                req.status = RequestStatus.FINISHED
+                req.meta["stop_pending"] = True
+                self.running.remove(req)
+                req.meta["final_block_ids"] = list(req.block_ids)
+                self._release(req)
+
+    def resolve(self, out: SchedulerOutput, sampled: list[int], now: float) -> list[tuple[Request, int]]:
+        """The step `out` completed: replace its PENDING tokens, stamp times, apply stop tokens.
+        Returns (request, token) for every token applied."""
+        applied = []
+        done = []
+        it = iter(sampled)
+        for ch in out.chunks:
+            if not ch.sample:
+                continue
+            tok = int(next(it))
+            req = ch.req
+            if not req.output or req.output[-1] != PENDING:
+                continue  # finished by a stop token one step earlier: this token is dropped
+            req.output[-1] = tok
+            if req.first_token_time is None:
+                req.first_token_time = now
+            req.token_times.append(now)
+            applied.append((req, tok))
+            if req.meta.pop("stop_pending", False):
+                req.finish_time = now
+                self.finished.append(req)
+            elif req.status == RequestStatus.RUNNING and req.should_stop():
+                req.status = RequestStatus.FINISHED
+                req.finish_time = now
+                done.append(req)
+        for req in done:
+            self.running.remove(req)
+            req.meta["final_block_ids"] = list(req.block_ids)
+            self._release(req)
+            self.finished.append(req)
+        return applied
 
     def _register_full_blocks(self, req: Request) -> None:
         full = req.num_computed // self.bs

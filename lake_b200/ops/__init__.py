@@ -16,6 +16,7 @@ from .core import (  # noqa: F401
     page_copy,
     paged_decode_attention,
     paged_prefill_attention,
+    resolve_tokens,
     rms_norm,
 )
 from ..oracle.ops_ref import interleave_gate_up, rope_cache  # noqa: F401

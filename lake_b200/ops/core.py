@@ -285,6 +285,19 @@ def chain_reject_sample(draft: torch.Tensor, draft_off: torch.Tensor, target: to
     return out, out_len
 
 
+def resolve_tokens(ids: torch.Tensor, prev: torch.Tensor) -> None:
+    """In place: ids[i] < 0 -> prev[-1 - ids[i]] (tokens the previous, still in-flight step sampled)."""
+    if ids.is_cuda:
+        native().resolve_tokens(ids, prev)
+        LAUNCHES[0] += 1
+        return
+    neg = ids < 0
+    if bool(neg.any()):
+        j = (-1 - ids[neg]).long()
+        ids[neg] = torch.where(j < prev.numel(), prev[j.clamp(max=max(prev.numel() - 1, 0))], torch.zeros_like(j)).to(
+            ids.dtype)
+
+
 def page_copy(src: torch.Tensor, dst: torch.Tensor, src_ids: torch.Tensor, dst_ids: torch.Tensor,
               page_bytes: int, sub_off: int = 0, sub_bytes: int | None = None) -> None:
     """dst page dst_ids[i] <- src page src_ids[i] (page-major byte buffers)."""

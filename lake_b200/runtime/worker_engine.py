@@ -66,7 +66,7 @@ def build_engine(cfg: RoleConfig):
                      max_batched_tokens=cfg.max_num_scheduled_tokens,
                      long_prefill_threshold=cfg.long_prefill_token_threshold,
                      max_model_len=cfg.max_model_length or 8192, num_blocks=cfg.num_blocks,
-                     use_cuda_graphs=device != "cpu")
+                     use_cuda_graphs=device != "cpu", overlap=cfg.enable_overlap)
 
 
 class WorkerEngine:

@@ -33,6 +33,21 @@ def test_engine_matches_oracle(cuda_dev, graphs):
         _check_tokens(eng.model, p, o)
 
 
+def test_engine_overlap_matches_synchronous(cuda_dev):
+    """Overlapped steps on the GPU (graph replays whose PENDING inputs the token relay kernel
+    resolves from the previous step's device output) give the synchronous engine's tokens."""
+    rng = random.Random(4)
+    prompts = [[rng.randrange(1000) for _ in range(n)] for n in (1, 30, 77, 150, 5, 64, 9)]
+    outs = []
+    for overlap in (False, True):
+        eng = LLMEngine("tiny-gpu", device="cuda:0", max_running=8, max_batched_tokens=200, max_model_len=1024,
+                        num_blocks=256, use_cuda_graphs=True, overlap=overlap)
+        eng.runner.capture_graphs()
+        outs.append(eng.generate(prompts, max_new_tokens=12))
+        torch.cuda.synchronize()
+    assert outs[0] == outs[1]
+
+
 def test_engine_llama8b_shapes_two_layers(cuda_dev):
     eng = LLMEngine("llama3-8b", device="cuda:0", max_running=4, max_batched_tokens=512, max_model_len=1024,
                     num_blocks=128, model_overrides={"n_layers": 2})
