@@ -656,9 +656,12 @@ PYBIND11_MODULE(_C, m) {
   m.def("moe_dispatch_grid", []() { return lakeb::kMoEDispatchGrid; });
   m.def("set_gemm_pair_mode", [](int64_t mode) { lakeb::set_gemm_pair_mode(static_cast<int>(mode)); });
   m.def("gemm_pair_mode", []() { return lakeb::gemm_pair_mode(); });
-  m.def("gemm_grid", [](int64_t M, int64_t N, int64_t epi, bool w8) {
-    return lakeb::gemm_grid(static_cast<int>(M), static_cast<int>(N), static_cast<int>(epi), 0, w8);
-  }, py::arg("M"), py::arg("N"), py::arg("epi"), py::arg("w8") = false);
+  m.def("gemm_grid", [](int64_t M, int64_t N, int64_t K, int64_t epi, bool w8) {
+    return lakeb::gemm_grid(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), static_cast<int>(epi), 0,
+                            w8);
+  }, py::arg("M"), py::arg("N"), py::arg("K"), py::arg("epi"), py::arg("w8") = false);
+  m.def("gemm_workspace_init", &lakeb::gemm_workspace_init,
+        "allocate the current device's stream-K workspace (outside any graph capture)");
   m.def("tp_norm_grid", [](int64_t rows) { return lakeb::tp_norm_grid(static_cast<int>(rows)); });
   m.def("linear_qkv", &linear_qkv, py::arg("a"), py::arg("w"), py::arg("q_out"), py::arg("rope_cs"),
         py::arg("positions"), py::arg("slots"), py::arg("arena"), py::arg("layer"), py::arg("n_q_heads"),

@@ -125,6 +125,45 @@ __device__ __forceinline__ bool tile_live(const GemmArgs& p, int m_blk, int num_
   return (m_blk - group * num_m_group) * 128 < __ldg(p.group_count + group);
 }
 
+// Work distribution, identical in every role of a CTA. Data-parallel: CTA c takes tiles c, c + G,
+// ... with their whole K range. Stream-K (p.streamk): the num_tiles x kbs (tile, k-block) units are
+// cut into G equal contiguous ranges, one per CTA, so every SM streams the same number of weight
+// bytes however few tiles there are; a tile cut between CTAs is summed in the fp32 workspace.
+struct WorkIter {
+  int cur, end, kbs;
+  bool sk;
+  __device__ WorkIter(const GemmArgs& p, int num_tiles, int kbs_) : kbs(kbs_), sk(p.streamk != 0) {
+    if (sk) {
+      const long long total = static_cast<long long>(num_tiles) * kbs;
+      cur = static_cast<int>(blockIdx.x * total / gridDim.x);
+      end = static_cast<int>((blockIdx.x + 1) * total / gridDim.x);
+    } else {
+      cur = blockIdx.x;
+      end = num_tiles;
+    }
+  }
+  __device__ bool next(int& tile, int& kb0, int& kb1) {
+    if (cur >= end) return false;
+    if (sk) {
+      tile = cur / kbs;
+      kb0 = cur - tile * kbs;
+      kb1 = min(kbs, end - tile * kbs);
+      cur = tile * kbs + kb1;
+    } else {
+      tile = cur;
+      kb0 = 0;
+      kb1 = kbs;
+      cur += gridDim.x;
+    }
+    return true;
+  }
+};
+
+// Stream-K: the CTA whose range holds unit u (inverse of the range cut above).
+__device__ __forceinline__ int sk_owner(long long u, long long total, int grid) {
+  return static_cast<int>(((u + 1) * grid - 1) / total);
+}
+
 template <int BN, int STAGES, int EPI, bool W8 = false>
 __global__ void __launch_bounds__(threads_of<W8>(), 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -146,10 +185,8 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
   const int num_m = (p.M + kBM - 1) / kBM;
   const int num_m_group = p.groups ? p.group_rows / kBM : num_m;
   const int num_n = (p.N + BN - 1) / BN;
-  const int base_tiles = num_m * num_n;
-  const int num_tiles = base_tiles * p.splits;
+  const int num_tiles = num_m * num_n;
   const int num_kb_all = (p.K + kBK - 1) / kBK;
-  const int kpb = (num_kb_all + p.splits - 1) / p.splits;  // k-blocks per split
   constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
 
   if (threadIdx.x == 0) {
@@ -183,12 +220,12 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
       if (p.groups) fence_proxy_async_global();  // rows other GPUs stored (expert dispatch) before TMA reads
       const unsigned long long ag_target = ag ? (p.tp.ag_base ? *p.tp.ag_base : 0ull) + p.tp.ag_off : 0ull;
       uint32_t ready = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      WorkIter it(p, num_tiles, num_kb_all);
+      int tile, kb0, kb1;
+      while (ok && it.next(tile, kb0, kb1)) {
         int m_blk, n_blk, grp;
-        const int split = tile / base_tiles;
-        tile_coords(tile - split * base_tiles, num_m, p.tp.m_rot, m_blk, n_blk);
+        tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
         if (!tile_live(p, m_blk, num_m_group, grp)) continue;
-        const int kb0 = split * kpb, kb1 = min(num_kb_all, kb0 + kpb);
         if (ag) {
           const int r0 = m_blk * kBM;
           const int r1 = min(p.M, r0 + kBM) - 1;
@@ -237,15 +274,13 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
       uint32_t stage = 0, phase = 0;
       bool ok = true;
       int t = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        int kb0, kb1;
+      WorkIter it(p, num_tiles, num_kb_all);
+      int tile, kb0, kb1;
+      while (ok && it.next(tile, kb0, kb1)) {
         {
           int m_blk, n_blk, grp;
-          const int split = tile / base_tiles;
-          tile_coords(tile - split * base_tiles, num_m, p.tp.m_rot, m_blk, n_blk);
+          tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
           if (!tile_live(p, m_blk, num_m_group, grp)) continue;
-          kb0 = split * kpb;
-          kb1 = min(num_kb_all, kb0 + kpb);
         }
         const int acc = t & 1;
         const uint32_t acc_phase = (t >> 1) & 1;
@@ -281,12 +316,12 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
     // ------------------------------------------------------------ fp8 -> bf16 converters (W8A16)
     const int ct = threadIdx.x - 192;  // 0..127: rows ct and ct + 128 of the B tile
     uint32_t stage = 0, phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    WorkIter it(p, num_tiles, num_kb_all);
+    int tile, kb0, kb1;
+    while (it.next(tile, kb0, kb1)) {
       int m_blk, n_blk, grp;
-      const int split = tile / base_tiles;
-      tile_coords(tile - split * base_tiles, num_m, p.tp.m_rot, m_blk, n_blk);
+      tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
       if (!tile_live(p, m_blk, num_m_group, grp)) continue;
-      const int kb0 = split * kpb, kb1 = min(num_kb_all, kb0 + kpb);
       bool ok = true;
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(&land[stage], phase, abort_flag, p.status)) {
@@ -316,12 +351,12 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int row_in_tile = q * 32 + lane;
     int t = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    WorkIter it(p, num_tiles, num_kb_all);
+    int tile, kb0, kb1;
+    while (it.next(tile, kb0, kb1)) {
       int m_blk, n_blk, grp;
-      const int split = tile / base_tiles;
-      tile_coords(tile - split * base_tiles, num_m, p.tp.m_rot, m_blk, n_blk);
+      tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
       if (!tile_live(p, m_blk, num_m_group, grp)) continue;
-      (void)split;
       const int acc = t & 1;
       const uint32_t acc_phase = (t >> 1) & 1;
       ++t;
@@ -331,91 +366,58 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
       const int row = m_blk * kBM + row_in_tile;
       const bool row_ok = row < p.M && (!p.groups || row - grp * p.group_rows < __ldg(p.group_count + grp));
 
-      if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32 || EPI == kEpiSwiGLU) {
-          if (p.splits > 1) {
-            // split-K: add this K range's partial into the fp32 workspace; the last split applies the epilogue
-            float* wrow = p.split_ws + static_cast<int64_t>(row) * p.N;
+      if (p.streamk && (kb0 != 0 || kb1 != num_kb_all)) {
+        // Stream-K: this CTA holds part of the tile's K range. Add it into the tile's workspace
+        // slot (named by the tile's last contributor, unique per cut tile); the last contributor
+        // to arrive loads the full sum back into its accumulator and runs the epilogue below.
+        const long long total = static_cast<long long>(num_tiles) * num_kb_all;
+        const long long u_first = static_cast<long long>(tile) * num_kb_all;
+        const int first = sk_owner(u_first, total, gridDim.x);
+        const int slot = sk_owner(u_first + num_kb_all - 1, total, gridDim.x);
+        float* wrow = p.split_ws + (static_cast<int64_t>(slot) * kBM + row_in_tile) * BN;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-              uint32_t r[32];
-              tmem_ld32(tbase + c * 32, r);
-              tmem_ld_wait();
-              const int col0 = n_blk * BN + c * 32;
-              if (row_ok && col0 < p.N) {
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tbase + c * 32, r);
+          tmem_ld_wait();
+          if (row_ok) {
 #pragma unroll
-                for (int i = 0; i < 8; ++i)
-                  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + col0 + 4 * i),
-                               "f"(__uint_as_float(r[4 * i])), "f"(__uint_as_float(r[4 * i + 1])),
-                               "f"(__uint_as_float(r[4 * i + 2])), "f"(__uint_as_float(r[4 * i + 3]))
-                               : "memory");
-              }
-            }
-            tc_fence_before();
-            mbar_arrive(&tmem_empty[acc]);  // accumulator free for the next tile
-            __threadfence();
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            const int tid_id = m_blk * num_n + n_blk;
-            if (warp == 2 && lane == 0) *split_last = atomicAdd(p.split_cnt + tid_id, 1) == p.splits - 1;
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            if (*split_last && EPI == kEpiSwiGLU) {
-              __threadfence();
-              constexpr int H = BN / 2;
-#pragma unroll 1
-              for (int c = 0; c < H / 32; ++c) {
-                if (!row_ok) continue;
-                float v[32];
-                float4* gs = reinterpret_cast<float4*>(wrow + n_blk * BN + c * 32);
-                float4* us = reinterpret_cast<float4*>(wrow + n_blk * BN + H + c * 32);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  const float4 g = __ldcg(gs + i), u = __ldcg(us + i);
-                  v[4 * i] = silu_f(g.x) * u.x;
-                  v[4 * i + 1] = silu_f(g.y) * u.y;
-                  v[4 * i + 2] = silu_f(g.z) * u.z;
-                  v[4 * i + 3] = silu_f(g.w) * u.w;
-                  __stcg(gs + i, make_float4(0.f, 0.f, 0.f, 0.f));
-                  __stcg(us + i, make_float4(0.f, 0.f, 0.f, 0.f));
-                }
-                store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + n_blk * H + c * 32, v);
-              }
-              asm volatile("bar.sync 1, 128;" ::: "memory");
-              if (warp == 2 && lane == 0) p.split_cnt[tid_id] = 0;
-            } else if (*split_last) {
-              __threadfence();
-#pragma unroll 1
-              for (int c = 0; c < BN / 32; ++c) {
-                const int col0 = n_blk * BN + c * 32;
-                if (!(row_ok && col0 < p.N)) continue;
-                float v[32];
-                float4* src = reinterpret_cast<float4*>(wrow + col0);
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                  const float4 f = __ldcg(src + i);
-                  v[4 * i] = f.x;
-                  v[4 * i + 1] = f.y;
-                  v[4 * i + 2] = f.z;
-                  v[4 * i + 3] = f.w;
-                  __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
-                }
-                if constexpr (EPI == kEpiStoreF32) {
-                  float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + row * p.ldc + col0);
-#pragma unroll
-                  for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                } else {
-                  if constexpr (EPI == kEpiResidual) {
-                    float rv[32];
-                    load_bf16x32(p.R + row * p.ldr + col0, rv);
-#pragma unroll
-                    for (int j = 0; j < 32; ++j) v[j] += rv[j];
-                  }
-                  store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
-                }
-              }
-              asm volatile("bar.sync 1, 128;" ::: "memory");
-              if (warp == 2 && lane == 0) p.split_cnt[tid_id] = 0;
-            }
-            continue;  // TMEM already released
+            for (int i = 0; i < 8; ++i)
+              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + c * 32 + 4 * i),
+                           "f"(__uint_as_float(r[4 * i])), "f"(__uint_as_float(r[4 * i + 1])),
+                           "f"(__uint_as_float(r[4 * i + 2])), "f"(__uint_as_float(r[4 * i + 3]))
+                           : "memory");
           }
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (warp == 2 && lane == 0) *split_last = atomicAdd(p.split_cnt + slot, 1) == slot - first;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!*split_last) {
+          tc_fence_before();
+          mbar_arrive(&tmem_empty[acc]);
+          continue;
+        }
+        __threadfence();
+        if (row_ok) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            float4* src = reinterpret_cast<float4*>(wrow + c * 32);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 f = __ldcg(src + i);
+              r[4 * i] = __float_as_uint(f.x);
+              r[4 * i + 1] = __float_as_uint(f.y);
+              r[4 * i + 2] = __float_as_uint(f.z);
+              r[4 * i + 3] = __float_as_uint(f.w);
+              __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
+            }
+            tmem_st32(tbase + c * 32, r);
+          }
+        }
+        tmem_st_wait();
+        if (warp == 2 && lane == 0) p.split_cnt[slot] = 0;
       }
       if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32) {
 #pragma unroll 1
@@ -660,8 +662,8 @@ int launch(const GemmArgs& a, cudaStream_t stream) {
     if (e != cudaSuccess) return e;
     attr = true;
   }
-  int grid = grid_for(a.M, a.N, BN, a.max_ctas) * a.splits;
-  if (grid > num_sms()) grid = num_sms();
+  int grid = grid_for(a.M, a.N, BN, a.max_ctas);
+  if (a.streamk) grid = a.streamk;  // the dispatcher's stream-K grid
   kern<<<grid, threads_of<W8>(), S::kAlloc, stream>>>(ma, mb, a);
   return cudaGetLastError();
 }
@@ -695,64 +697,131 @@ int launch_bn(const GemmArgs& a, cudaStream_t stream) {
 static int g_pair_mode = 0;
 
 // The two-SM kernel takes large plain / residual / SwiGLU / fp32 GEMMs, including the
-// tensor-parallel all-gather GEMMs and the reduce-scatter push GEMM; QKV, argmax, grouped,
-// split-K and fp8 GEMMs stay on the single-SM kernel.
+// tensor-parallel all-gather GEMMs and the reduce-scatter push GEMM; QKV, argmax, grouped and
+// fp8 GEMMs stay on the single-SM kernel.
 static bool use_pair(int M, int epi, bool grouped, int max_ctas, bool done_signal) {
   return g_pair_mode && M >= 512 && !grouped && max_ctas == 0 && !done_signal &&
          (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiSwiGLU || epi == kEpiStoreF32 ||
           epi == kEpiRSPush);
 }
 
-int gemm_grid(int M, int N, int epi, int max_ctas, bool w8) {
-  if (w8) return grid_for(M, N, epi == kEpiQKV ? 128 : 256, max_ctas);  // fp8-weight kernels: fixed widths
-  if (use_pair(M, epi, false, max_ctas, false)) return gemm_pair_grid(M, N);
-  return grid_for(M, N, bn_for(M, N, epi, false), max_ctas);
+// Per-device stream-K workspace: fp32 partial tiles (zero between uses: the finishing CTA zeroes
+// what it read), one slot of 128 x 256 floats per CTA, and one arrival counter per slot. It is
+// allocated outside any graph capture (gemm_workspace_init, or the first eager GEMM on the
+// device); until it exists every GEMM runs data-parallel, and gemm_grid() plans the same way.
+constexpr int kSkMaxSlots = 1024;
+constexpr int64_t kSkWsFloats = static_cast<int64_t>(kSkMaxSlots) * 128 * 256;
+static float* s_sk_ws[16] = {};
+static int* s_sk_cnt[16] = {};
+
+static int cur_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 16) return -1;
+  return dev;
 }
 
-// Per-device split-K workspace: fp32 partial sums (zero between uses: the last split of a tile
-// zeroes what it read) and one arrival counter per tile. Allocated on first use (outside any
-// graph capture: engines run every shape once before capturing it).
-constexpr int64_t kSplitWsFloats = 16ll << 20;  // 64 MB
-constexpr int kSplitMaxTiles = 4096;
-static bool split_workspace(int64_t floats, int tiles, float** ws, int** cnt, cudaStream_t stream) {
-  static float* s_ws[16] = {};
-  static int* s_cnt[16] = {};
-  if (floats > kSplitWsFloats || tiles > kSplitMaxTiles) return false;
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev >= 16) return false;
-  if (!s_ws[dev]) {
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
-      cudaGetLastError();
-      return false;  // never allocate inside a capture: this call runs unsplit
-    }
-    void* w = nullptr;
-    void* c = nullptr;
-    if (cudaMalloc(&w, kSplitWsFloats * sizeof(float)) != cudaSuccess) {
-      cudaGetLastError();
-      return false;
-    }
-    if (cudaMalloc(&c, kSplitMaxTiles * sizeof(int)) != cudaSuccess) {
-      cudaGetLastError();
-      cudaFree(w);
-      return false;
-    }
-    cudaMemset(w, 0, kSplitWsFloats * sizeof(float));
-    cudaMemset(c, 0, kSplitMaxTiles * sizeof(int));
-    cudaDeviceSynchronize();
-    s_ws[dev] = static_cast<float*>(w);
-    s_cnt[dev] = static_cast<int*>(c);
+bool gemm_workspace_init() {
+  const int dev = cur_device();
+  if (dev < 0) return false;
+  if (s_sk_ws[dev]) return true;
+  void* w = nullptr;
+  void* c = nullptr;
+  if (cudaMalloc(&w, kSkWsFloats * sizeof(float)) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
   }
-  *ws = s_ws[dev];
-  *cnt = s_cnt[dev];
+  if (cudaMalloc(&c, kSkMaxSlots * sizeof(int)) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(w);
+    return false;
+  }
+  cudaMemset(w, 0, kSkWsFloats * sizeof(float));
+  cudaMemset(c, 0, kSkMaxSlots * sizeof(int));
+  cudaDeviceSynchronize();
+  s_sk_ws[dev] = static_cast<float*>(w);
+  s_sk_cnt[dev] = static_cast<int*>(c);
   return true;
 }
+
+static bool sk_workspace(float** ws, int** cnt) {
+  const int dev = cur_device();
+  if (dev < 0 || !s_sk_ws[dev]) return false;
+  *ws = s_sk_ws[dev];
+  *cnt = s_sk_cnt[dev];
+  return true;
+}
+
+// Stream-K grid for a tiles x kbs problem, or 0 for data-parallel. Used when cutting the K ranges
+// lets the busiest CTA stream >10% fewer k-blocks than whole tiles would (fewer tiles than SMs, or
+// a ragged last wave), with at least 4 k-blocks per CTA.
+static int streamk_grid(int tiles, int kbs) {
+  const int sms = num_sms();
+  const long long total = static_cast<long long>(tiles) * kbs;
+  const long long dp = static_cast<long long>((tiles + sms - 1) / sms) * kbs;
+  int g = sms < kSkMaxSlots ? sms : kSkMaxSlots;
+  if (total < 4LL * g) g = static_cast<int>(total / 4);
+  if (g < 2) return 0;
+  const long long sk = (total + g - 1) / g;
+  return sk * 10 < dp * 9 ? g : 0;
+}
+
+static bool sk_epilogue(int epi) {
+  return epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiStoreF32 || epi == kEpiSwiGLU ||
+         epi == kEpiQKV || epi == kEpiArgmax || epi == kEpiRSPush;
+}
+
+static int tile_width(int M, int N, int epi, bool w8) {
+  if (w8) return epi == kEpiQKV ? 128 : 256;
+  return bn_for(M, N, epi, false);
+}
+
+// Stream-K grid this call will use (0 = data-parallel).
+static int plan_streamk(int M, int N, int K, int epi, bool grouped, int max_ctas, bool w8) {
+  if (grouped || max_ctas > 0 || !sk_epilogue(epi)) return 0;
+  float* ws;
+  int* cnt;
+  if (!sk_workspace(&ws, &cnt)) return 0;
+  const int bn = tile_width(M, N, epi, w8);
+  const int tiles = ((M + kBM - 1) / kBM) * ((N + bn - 1) / bn);
+  return streamk_grid(tiles, (K + kBK - 1) / kBK);
+}
+
+int gemm_grid(int M, int N, int K, int epi, int max_ctas, bool w8) {
+  if (!w8 && use_pair(M, epi, false, max_ctas, false)) return gemm_pair_grid(M, N);
+  const int g = plan_streamk(M, N, K, epi, false, max_ctas, w8);
+  if (g) return g;
+  return grid_for(M, N, tile_width(M, N, epi, w8), max_ctas);
+}
+
 void set_gemm_pair_mode(int mode) { g_pair_mode = mode; }
 int gemm_pair_mode() { return g_pair_mode; }
 
-int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
-  if (a.M <= 0 || a.N <= 0 || a.K <= 0) return 0;
-  if (a.B8) {  // fp8 weights: converter-warp kernel, no pair / split-K variants
+int gemm_bf16(const GemmArgs& a_in, int epi, cudaStream_t stream) {
+  if (a_in.M <= 0 || a_in.N <= 0 || a_in.K <= 0) return 0;
+  GemmArgs a = a_in;
+  {
+    // first eager GEMM on a device allocates the stream-K workspace (never inside a capture)
+    const int dev = cur_device();
+    if (dev >= 0 && !s_sk_ws[dev]) {
+      cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+      if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone)
+        gemm_workspace_init();
+      cudaGetLastError();
+    }
+  }
+  if (epi == kEpiRSPush && (a.tp.world < 1 || a.tp.world > kMaxTP || a.tp.rows_per_rank <= 0 ||
+                            a.M != a.tp.world * a.tp.rows_per_rank))
+    return -5;
+  if (a.tp.ag_cnt && !a.tp.ag_all && (a.tp.rows_per_rank <= 0 || a.M > a.tp.world * a.tp.rows_per_rank)) return -6;
+  if (a.tp.ag_cnt && (a.tp.world < 1 || a.tp.world > kMaxTP)) return -6;
+  if (epi == kEpiQKV && a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128) return -3;
+  const bool w8 = a.B8 != nullptr;
+  // plan order shared with gemm_grid(): two-SM kernel, else stream-K, else data-parallel
+  if (!w8 && use_pair(a.M, epi, a.groups != 0, a.max_ctas, a.tp.done_cnt[0] != nullptr))
+    return gemm_bf16_pair(a, epi, stream);
+  a.streamk = plan_streamk(a.M, a.N, a.K, epi, a.groups != 0, a.max_ctas, w8);
+  if (a.streamk) sk_workspace(&a.split_ws, &a.split_cnt);
+  if (w8) {  // fp8 weights: converter-warp kernel (no two-SM variant)
     if (!a.b_scale || a.b_scale_ld <= 0 || (a.K % 64) || (a.ldb8 % 16) ||
         (reinterpret_cast<uintptr_t>(a.B8) & 15) || (reinterpret_cast<uintptr_t>(a.A) & 15))
       return -9;
@@ -762,50 +831,15 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
       case kEpiSwiGLU: return launch<256, 3, kEpiSwiGLU, true>(a, stream);
       case kEpiStoreF32: return launch<256, 3, kEpiStoreF32, true>(a, stream);
       case kEpiArgmax: return launch<256, 3, kEpiArgmax, true>(a, stream);
-      case kEpiQKV:
-        if (a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128) return -3;
-        return launch<128, 5, kEpiQKV, true>(a, stream);
-      case kEpiRSPush:
-        if (a.tp.world < 1 || a.tp.world > kMaxTP || a.tp.rows_per_rank <= 0 ||
-            a.M != a.tp.world * a.tp.rows_per_rank)
-          return -5;
-        return launch<256, 3, kEpiRSPush, true>(a, stream);
+      case kEpiQKV: return launch<128, 5, kEpiQKV, true>(a, stream);
+      case kEpiRSPush: return launch<256, 3, kEpiRSPush, true>(a, stream);
       default:
         return -4;
     }
   }
-  const bool plain = !a.groups && !a.tp.ag_cnt && !a.tp.rs_cnt[0] && !a.tp.done_cnt[0] && a.max_ctas == 0;
-  if (a.tp.ag_cnt && !a.tp.ag_all && (a.tp.rows_per_rank <= 0 || a.M > a.tp.world * a.tp.rows_per_rank)) return -6;
-  if (a.tp.ag_cnt && (a.tp.world < 1 || a.tp.world > kMaxTP)) return -6;
-  if (epi == kEpiRSPush && (a.tp.world < 1 || a.tp.world > kMaxTP || a.tp.rows_per_rank <= 0 ||
-                            a.M != a.tp.world * a.tp.rows_per_rank))
-    return -5;
-  if (use_pair(a.M, epi, a.groups != 0, a.max_ctas, a.tp.done_cnt[0] != nullptr) && a.splits <= 1)
-    return gemm_bf16_pair(a, epi, stream);
   if (a.groups && (a.group_rows % kBM || !a.group_count || a.M != a.groups * a.group_rows)) return -8;
   if ((a.K % 8) || (a.lda % 8) || (a.ldb % 8) || (a.N % 32)) return -1;
   if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B) & 15)) return -2;
-  if (plain && (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiStoreF32 || epi == kEpiSwiGLU) &&
-      a.splits <= 1) {
-    const int bn = bn_for(a.M, a.N, epi, false);
-    const int tiles = ((a.M + kBM - 1) / kBM) * ((a.N + bn - 1) / bn);
-    const int kbs = (a.K + kBK - 1) / kBK;
-    int splits = num_sms() / tiles;
-    if (splits > 8) splits = 8;
-    if (splits > kbs / 8) splits = kbs / 8;
-    if (splits >= 2) {
-      GemmArgs b = a;
-      if (split_workspace(static_cast<int64_t>(a.M) * a.N, tiles, &b.split_ws, &b.split_cnt, stream)) {
-        b.splits = splits;
-        switch (epi) {
-          case kEpiStoreBf16: return launch_bn<kEpiStoreBf16>(b, stream);
-          case kEpiResidual: return launch_bn<kEpiResidual>(b, stream);
-          case kEpiSwiGLU: return launch<256, 4, kEpiSwiGLU>(b, stream);
-          default: return launch_bn<kEpiStoreF32>(b, stream);
-        }
-      }
-    }
-  }
   switch (epi) {
     case kEpiStoreBf16:
       return launch_bn<kEpiStoreBf16>(a, stream);
@@ -814,7 +848,6 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
     case kEpiSwiGLU:
       return launch<256, 4, kEpiSwiGLU>(a, stream);
     case kEpiQKV:
-      if (a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128) return -3;
       return launch<128, 6, kEpiQKV>(a, stream);
     case kEpiArgmax:
       return launch<256, 4, kEpiArgmax>(a, stream);
@@ -824,9 +857,6 @@ int gemm_bf16(const GemmArgs& a, int epi, cudaStream_t stream) {
       if (!a.row_slot || !a.tp.rs_recv[0]) return -7;
       return launch<256, 4, kEpiScatter>(a, stream);
     case kEpiRSPush:
-      if (a.tp.world < 1 || a.tp.world > kMaxTP || a.tp.rows_per_rank <= 0 ||
-          a.M != a.tp.world * a.tp.rows_per_rank)
-        return -5;
       return launch_bn<kEpiRSPush>(a, stream);
     default:
       return -4;

@@ -98,9 +98,10 @@ struct GemmArgs {
   int64_t ldb8 = 0;  // bytes between rows of B8
   const float* b_scale = nullptr;
   int b_scale_ld = 0;
-  // split-K (small M): `splits` CTAs share a tile's K range, add partials into split_ws (fp32 [M, N],
-  // zero between uses) and the last one to finish (split_cnt per tile) applies the epilogue
-  int splits = 1;
+  // stream-K (set by the dispatcher): the (tile, k-block) units are cut into one contiguous range
+  // per CTA; a tile cut between CTAs is summed in split_ws (fp32 [grid][128][BN], zero between
+  // uses) and the last contributor to arrive (split_cnt per slot) applies the epilogue
+  int streamk = 0;
   float* split_ws = nullptr;
   int* split_cnt = nullptr;
   // kEpiScatter destinations (rows indexed like A)
@@ -116,7 +117,10 @@ void set_gemm_pair_mode(int mode);
 int gemm_pair_mode();
 
 // Number of CTAs gemm_bf16 launches for a shape (the per-call increment of TP counters).
-int gemm_grid(int M, int N, int epi, int max_ctas, bool w8 = false);
+// CTAs a gemm_bf16 launch of this shape uses (one cross-GPU signal per CTA): the TP host code
+// sizes its counter waits with it.
+int gemm_grid(int M, int N, int K, int epi, int max_ctas, bool w8 = false);
+bool gemm_workspace_init();  // current device's stream-K workspace (call outside graph capture)
 
 // Returns 0 on success, otherwise a cudaError_t or negative argument error.
 int gemm_bf16(const GemmArgs& args, int epi, cudaStream_t stream);

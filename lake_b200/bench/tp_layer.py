@@ -61,7 +61,7 @@ def main():
     out_act = torch.empty(t, I, dtype=torch.bfloat16, device=dev)
 
     def fused():
-        tpops.linear_rs(act, w_down, g.gemm_rs(0, mr, H))
+        tpops.linear_rs(act, w_down, g.gemm_rs(0, mr, H, I))
         tpops.norm_push(h, w_n, 1e-5, g.norm_push(mr, 0, 0))
         tpops.linear_swiglu_ag(g.a_full[0][:t], w_gu, out_act, g.gemm_ag(0, mr))
         g.end_step()
@@ -83,7 +83,7 @@ def main():
     split = [0.0, 0.0, 0.0]
     for it in range(args.warmup + args.iters):
         ev[0].record()
-        tpops.linear_rs(act, w_down, g.gemm_rs(0, mr, H))
+        tpops.linear_rs(act, w_down, g.gemm_rs(0, mr, H, I))
         ev[1].record()
         tpops.norm_push(h, w_n, 1e-5, g.norm_push(mr, 0, 0))
         ev[2].record()

@@ -148,14 +148,15 @@ class TPDecoderLM:
                                 b.slots, arena, i, self.hq, self.hk, g.gemm_ag(ag_slot, mr), b.peer_arena,
                                 b.peer_slots)
             attn = self._attention(i, b, arena, ws, t)
-            tpops.linear_rs(attn, w[p + "o_proj"], g.gemm_rs(rs_slot, mr, c.hidden, self.fp8))
+            tpops.linear_rs(attn, w[p + "o_proj"], g.gemm_rs(rs_slot, mr, c.hidden, self.hq * c.head_dim, self.fp8))
             k += 1
             ag_slot = k % 2
             tpops.norm_push(h, w[p + "post_attention_layernorm"], c.rms_eps, g.norm_push(mr, rs_slot, ag_slot))
             act = ws.act[:t]
             tpops.linear_swiglu_ag(g.a_full[ag_slot][:t], w[p + "gate_up_proj"], act, g.gemm_ag(ag_slot, mr))
             rs_slot ^= 1
-            tpops.linear_rs(act, w[p + "down_proj"], g.gemm_rs(rs_slot, mr, c.hidden, self.fp8))
+            tpops.linear_rs(act, w[p + "down_proj"],
+                            g.gemm_rs(rs_slot, mr, c.hidden, c.intermediate // self.world, self.fp8))
             k += 1
             if i + 1 < c.n_layers:
                 ag_slot = k % 2

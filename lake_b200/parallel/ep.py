@@ -82,7 +82,7 @@ class EPGroup:
         self.expect = {("d", p): 0 for p in range(2)}
         self.expect.update({("c", p): 0 for p in range(2)})
         self._c = C
-        self.down_grid = C.gemm_grid(rows, hidden, 7)
+        self.down_grid = C.gemm_grid(rows, hidden, hidden, 7)  # grouped: data-parallel, K does not change the grid
         dist.barrier(group=group)
 
     def _view(self, name, dtype, shape):

@@ -93,6 +93,8 @@ class TPGroup:
         self._fam = list(self.expect)  # family -> index into bases
         self.bases = torch.zeros(len(self._fam), dtype=torch.int64, device=self.device)
         self._c = C
+        with torch.cuda.device(self.device):
+            C.gemm_workspace_init()  # GEMM grids (and so the counter totals) are planned with it present
         dist.barrier(group=group)
 
     def _view(self, buf, name, dtype, shape):
@@ -134,14 +136,14 @@ class TPGroup:
             d["ag_all"] = 1
         return d
 
-    def gemm_rs(self, slot: int, mr: int, n: int, fp8: bool = False) -> dict:
-        """Row-parallel GEMM whose epilogue pushes partial rows to their owners' recv[slot]
-        (`fp8`: block-scaled fp8 weights, whose kernel has its own grid)."""
+    def gemm_rs(self, slot: int, mr: int, n: int, k: int, fp8: bool = False) -> dict:
+        """Row-parallel GEMM ([world*mr, k] x [n, k]^T) whose epilogue pushes partial rows to their
+        owners' recv[slot] (`fp8`: block-scaled fp8 weights, whose kernel has its own grid)."""
         d = dict(world=self.world, rank=self.rank, rows_per_rank=mr,
                  m_rot=(((self.rank + 1) % self.world) * mr) // 128,
                  rs_recv=[self._ptr(r, f"r{slot}") for r in range(self.world)],
                  rs_cnt=[self._cnt_ptr(r, "rs", slot) for r in range(self.world)])
-        self.expect[("rs", slot)] += self._c.gemm_grid(self.world * mr, n, 6, fp8)
+        self.expect[("rs", slot)] += self._c.gemm_grid(self.world * mr, n, k, 6, fp8)
         return d
 
     def norm_push(self, mr: int, rs_slot: int | None, ag_slot: int, row_map: torch.Tensor | None = None,
@@ -161,10 +163,11 @@ class TPGroup:
         return d
 
     def lm_argmax(self, mr_unused: int, n_rows: int, vocab_local: int, fp8: bool = False) -> dict:
+        """lm_head GEMM over the gathered sampled rows (fx, [n_rows, hidden]) with the argmax epilogue."""
         d = self.gemm_ag(SLOT_FX, 0, wait_all=True)
         d.update(done_cnt=[self._cnt_ptr(r, "done", 0) for r in range(self.world)],
                  col_offset=self.rank * vocab_local)
-        self.expect[("done", 0)] += self._c.gemm_grid(n_rows, vocab_local, 4, fp8)
+        self.expect[("done", 0)] += self._c.gemm_grid(n_rows, vocab_local, self.hidden, 4, fp8)
         return d
 
     def argmax_combine(self, out: torch.Tensor, n: int) -> torch.Tensor:

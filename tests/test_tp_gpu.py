@@ -60,7 +60,7 @@ def _fused_numerics(rank, world, out):
         act = torch.empty(t, I, dtype=torch.bfloat16, device=dev)
         for _ in range(3):  # repeated calls exercise the counter totals and slot rotation
             h_d.copy_(h.to(dev))
-            tpops.linear_rs(a_d, w_o_d, g.gemm_rs(0, mr, H))
+            tpops.linear_rs(a_d, w_o_d, g.gemm_rs(0, mr, H, K))
             tpops.norm_push(h_d, w_n_d, 1e-5, g.norm_push(mr, 0, 0))
             tpops.linear_swiglu_ag(g.a_full[0][:t], w_gu_d, act, g.gemm_ag(0, mr))
             g.end_step()
