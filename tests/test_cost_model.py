@@ -23,3 +23,25 @@ def test_modes_and_tiers():
     assert load_or_recompute("L3", 2048, p) == "recompute"
     r = report(p)
     assert r["link_sweep"][-1]["gbs"] == 770 and r["tiers"]["L1"]["breakeven_tokens"] is not None
+
+
+def test_kv_planner_arithmetic():
+    from lake_b200.bench import kv_planner as kp
+    from lake_b200.models.config import get_config
+
+    cfg = get_config("llama3-8b")
+    per = 32 * 2 * 8 * 128 * 2  # 131072 bytes per token
+    assert kp.kv_bytes_per_token(cfg) == per
+    assert kp.matched_tokens(8192, 0.9, 16) == 7360  # whole blocks of the 7372.8-token hit
+    assert kp.matched_tokens(100, 1.0, 16) == 96
+    p = kp.prefill(cfg, 8192, 0.9, 16, gpus=2, tps_gpu=1000.0, remote=0.5)
+    assert p["unique_tokens"] == 832
+    assert abs(p["req_s"] - 2000.0 / 832) < 1e-9
+    assert p["load_bytes_per_req"] == 7360 * per * 0.5
+    c = kp.capacity(cfg, 4096, 0.5, users=10, gpus=1, tps_gpu=2048.0, copies=2, usable=0.5)
+    assert c["anchor_bytes_per_user"] == 2048 * per and c["req_s"] == 1.0
+    w = c["windows"][0]
+    assert w["seconds"] == 300 and w["logical_bytes"] == 10 * 2048 * per + 300 * 2048 * per
+    assert w["raw_bytes"] == w["logical_bytes"] * 4
+    cmp = kp.compare(cfg, 0.5, 0.75, 4096, 10, 1, 2048.0)
+    assert abs(cmp["increase"]["req_s"] - 1.0) < 1e-9  # half the unique tokens: twice the requests
