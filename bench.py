@@ -59,7 +59,8 @@ def parse():
                     help="default: pd for an even number of GPUs >= 2, else colocated")
     ap.add_argument("--tp", type=int, default=1,
                     help="tensor-parallel instance size (pd: prefill and decode instances of this many GPUs)")
-    ap.add_argument("--ep", action="store_true", help="expert parallel over all ranks (MoE models, colocated mode)")
+    ap.add_argument("--ep", action="store_true",
+                    help="expert parallel (MoE models): over the decode ranks in pd mode, over all ranks colocated")
     ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
                     help="projection weight format (fp8 = block-scaled e4m3, W8A16 GEMMs)")
     ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
@@ -290,18 +291,26 @@ def pd_split(world: int, prefill_ranks: int = 0) -> tuple[int, int]:
     return world - n_d, n_d
 
 
-def pd_layout(world: int, tp: int, prefill_instances: int = 0) -> tuple[int, int]:
-    """(prefill, decode) instance counts for instances of `tp` GPUs each."""
+def pd_layout(world: int, tp: int, prefill_instances: int = 0, n_experts: int = 0) -> tuple[int, int]:
+    """(prefill, decode) instance counts for instances of `tp` GPUs each. With expert-parallel
+    decode (`n_experts` > 0) the decode ranks form one EP group, so their count divides the
+    expert count: the divisor nearest the ~40% share (8 GPUs: 4 + 4)."""
+    if n_experts and not prefill_instances:
+        share = world * 0.4
+        n_d = min((d for d in range(1, world) if n_experts % d == 0), key=lambda d: (abs(d - share), -d))
+        return world - n_d, n_d
     return pd_split(world // tp, prefill_instances)
 
 
-def run_pd(args, rank, world, local, group, barrier, tp_groups=None):
+def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=None):
     """Prefill instances [0, P) feed decode instances [P, P + D) (prefill instance i -> decode
     instance P + i % D). An instance is `args.tp` consecutive ranks (a tensor-parallel group
     led by its first rank) or one rank. A decode instance owns its requests and reserves
     pages; its prefill partners' QKV epilogue writes K/V straight into those pages over
     NVLink. A step is one decode-instance iteration; prefill instances work continuously
-    through the same window."""
+    through the same window. With `--ep` (MoE) the decode ranks form one expert-parallel
+    group: each is its own instance (attention data-parallel) and they step in lockstep for
+    the fused expert exchange; prefill instances hold every expert."""
     import numpy as np
     import torch
 
@@ -309,7 +318,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None):
     from lake_b200.parallel import pd
 
     T = args.tp
-    n_p, n_d = pd_layout(world, T, args.prefill_ranks)
+    n_p, n_d = pd_layout(world, T, args.prefill_ranks, _n_experts(args) if args.ep else 0)
     inst = rank // T
     members = list(range(inst * T, inst * T + T))
     leader = members[0] == rank
@@ -321,10 +330,21 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None):
         partner = [i * T for i in range(n_p) if i % n_d == inst - n_p]  # leaders of the prefill instances
     running = args.running if role == "decode" else args.prefill_running
     tp = (rank % T, T, tp_groups[inst]) if T > 1 else None
+    ep = (rank - n_p, n_d, ep_group) if (ep_group is not None and role == "decode") else None
     # decode instances overlap host scheduling with the device; prefill instances report each
     # first token as soon as its step completes (overlap would hold it back one long step)
-    eng = _make_engine(args, local, running, shared_arena=(role == "decode"), tp=tp,
+    eng = _make_engine(args, local, running, shared_arena=(role == "decode"), tp=tp, ep=ep,
                        overlap=role == "decode" and not args.no_overlap)
+
+    def agree(flag: bool) -> bool:
+        # expert-parallel decode ranks step in lockstep: loop conditions are agreed on
+        if ep is None:
+            return flag
+        import torch.distributed as dist
+
+        t = torch.tensor([1 if flag else 0])
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=ep_group)
+        return bool(t.item())
     job = os.environ.get("TORCHELASTIC_RUN_ID", "bench").replace("-", "")[:16] + str(os.getpid() if world == 1 else 0)
     side = pd.connect_pair(eng, role, rank, partner if T > 1 or role == "decode" else partner[0], group, job=job,
                            members=members)
@@ -400,10 +420,10 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None):
     # so the decode batch holds requests at every stage of their output
     target = max(32, args.running // 4)
     t_pop = time.perf_counter()
-    while len(eng.scheduler.finished) < target:
+    while agree(len(eng.scheduler.finished) < target):
         side.poll()
-        if eng.has_unfinished():
-            side.step()
+        if eng.has_unfinished() or ep is not None:
+            side.step()  # (an idle expert-parallel rank still joins the group's exchange)
         else:
             time.sleep(0.0005)
         top_up()
@@ -446,6 +466,12 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None):
     return w, role
 
 
+def _n_experts(args) -> int:
+    from lake_b200.models.config import get_config
+
+    return get_config(args.model).n_experts or 0
+
+
 def _model_desc(name):
     from lake_b200.models.config import get_config
 
@@ -483,8 +509,13 @@ def main():
 
     if world % args.tp:
         raise SystemExit("--tp must divide the GPU count")
-    mode = args.mode or ("pd" if world // args.tp >= 2 and not args.ep else "colocated")
-    ep = (rank, world, group) if args.ep and world > 1 else None
+    mode = args.mode or ("pd" if world // args.tp >= 2 else "colocated")
+    ep = (rank, world, group) if args.ep and world > 1 and mode == "colocated" else None
+    ep_group = None
+    if args.ep and mode == "pd":
+        n_p, n_d = pd_layout(world, args.tp, args.prefill_ranks, _n_experts(args))
+        if n_d > 1:  # every rank creates the group (collective), decode ranks use it
+            ep_group = dist.new_group(list(range(n_p, world)), backend="gloo")
     tp = None
     tp_groups = None
     if args.tp > 1:
@@ -497,7 +528,7 @@ def main():
         clocks.start()
     role = "colocated"
     if mode == "pd":
-        w, role = run_pd(args, rank, world, local, group, barrier, tp_groups)
+        w, role = run_pd(args, rank, world, local, group, barrier, tp_groups, ep_group)
     else:
         w = run_colocated(args, rank, local, barrier, tp, ep)
     ck = clocks.stop() if rank == 0 else {}
@@ -533,8 +564,10 @@ def main():
     if rank == 0:
         p50 = (lambda xs: sorted(xs)[len(xs) // 2] if xs else None)
         kv_gbs = sm[6].item() / (wall_ms / 1000.0) / 1e9 if sm[6].item() else None
-        n_p, n_d = pd_layout(world, args.tp, args.prefill_ranks)
-        par = f"pd: {n_p} prefill + {n_d} decode instances (tp{args.tp} each)" if mode == "pd" else (
+        n_p, n_d = pd_layout(world, args.tp, args.prefill_ranks, _n_experts(args) if args.ep else 0)
+        par = (f"pd: {n_p} prefill + {n_d} decode instances (tp{args.tp} each)" +
+               (f", decode ranks expert-parallel ep{n_d} (fused dispatch/combine)" if ep_group is not None else "")
+               ) if mode == "pd" else (
             f"dp{world // args.tp} x tp{args.tp} (fused NVLink collectives)" if args.tp > 1 else
             f"ep{world} (experts split, attention data-parallel, fused dispatch/combine)" if ep else
             (f"dp{world}" if world > 1 else "single"))
@@ -545,8 +578,7 @@ def main():
             "dtype": "bf16" if args.weights == "bf16" else "bf16 activations/KV, fp8 block-scaled weights",
             "data": "synthetic (uniform random token ids, random-init weights)",
             "config": {"model": _model_desc(args.model),
-                       "global_batch": args.running * (pd_layout(world, args.tp, args.prefill_ranks)[1]
-                                                       if mode == "pd" else world // args.tp),
+                       "global_batch": args.running * (n_d if mode == "pd" else world // args.tp),
                        "seq_len": args.input_len + args.output_len, "input_len": args.input_len,
                        "output_len": args.output_len, "parallelism": par, "mode": mode,
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",
