@@ -58,7 +58,8 @@ def parse():
     ap.add_argument("--mode", choices=["colocated", "pd"], default=None,
                     help="default: pd for an even number of GPUs >= 2, else colocated")
     ap.add_argument("--tp", type=int, default=1,
-                    help="tensor-parallel instance size (pd: prefill and decode instances of this many GPUs)")
+                    help="tensor-parallel instance size (pd: prefill and decode instances of this many GPUs; "
+                         "0 = half the GPUs per instance from 4 GPUs up)")
     ap.add_argument("--ep", action="store_true",
                     help="expert parallel (MoE models): over the decode ranks in pd mode, over all ranks colocated")
     ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
@@ -507,6 +508,8 @@ def main():
         if world > 1:
             dist.barrier(group=group)
 
+    if args.tp == 0:  # auto: half the GPUs per PD-split instance, as the prefill/decode TP groups of 8 GPUs
+        args.tp = max(1, min(4, world // 2)) if (args.mode in (None, "pd") and not args.ep and world >= 4) else 1
     if world % args.tp:
         raise SystemExit("--tp must divide the GPU count")
     mode = args.mode or ("pd" if world // args.tp >= 2 else "colocated")

@@ -161,9 +161,22 @@ def bench_pd_qkv(t: Timer, out: list):
     ms_peer = t(lambda: ops.linear_qkv(x, w, q, cs, pos, slots, arena, 0, hq, hkv, peer, slots))
     kv_bytes = m * 2 * hkv * 128 * 2
     fl = 2 * m * w.shape[0] * hidden
+    # roofline of the fused kernel: the slower of the GEMM at the measured cuBLAS peak and the
+    # K/V bytes that cross NVLink at the measured 770 GB/s peer-copy rate
+    roof = max(fl / (_peak_tflops() * 1e12), kv_bytes / 770e9) * 1e3
     out.append(dict(kernel="linear_qkv + P->D peer KV stores", m=m, ms_local_only=ms_local, ms_with_peer=ms_peer,
                     tflops_with_peer=fl / ms_peer / 1e9, peer_kv_gbs=kv_bytes / ms_peer / 1e6,
-                    overhead_frac=ms_peer / ms_local - 1))
+                    overhead_frac=ms_peer / ms_local - 1, roofline_ms=roof, frac_of_roofline=roof / ms_peer))
+
+
+def _peak_tflops() -> float:
+    import os
+
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))),
+                     "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        return float(json.load(open(p)).get("bf16_tflops", 1590.0))
+    return 1590.0
 
 
 def bench_moe(t: Timer, out: list):

@@ -232,12 +232,17 @@ class ModelRunner:
         self.d_i32.zero_()
         self.d_i64[:t].fill_(-1)
         self.d_i64[self.max_tokens:self.max_tokens + bucket].copy_(torch.arange(bucket, device=self.device))
+        # the warm-up forwards overwrite d_prev, which may hold the in-flight step's sampled ids
+        # (overlapped scheduling, graph captured on first use): keep them
+        prev = self.d_prev.clone() if self.relay else None
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
             for _ in range(2):
                 self._forward(batch, self.relay)
         torch.cuda.current_stream(self.device).wait_stream(s)
+        if prev is not None:
+            self.d_prev.copy_(prev)
         graph = torch.cuda.CUDAGraph()
         c0 = ops.core.LAUNCHES[0]
         with torch.cuda.graph(graph):
