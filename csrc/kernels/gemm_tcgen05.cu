@@ -399,22 +399,24 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
           continue;
         }
         __threadfence();
-        if (row_ok) {
+        // tcgen05.st is warp-aligned: every lane issues it (rows past M store zeros)
 #pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            float4* src = reinterpret_cast<float4*>(wrow + c * 32);
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          float4* src = reinterpret_cast<float4*>(wrow + c * 32);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const float4 f = __ldcg(src + i);
-              r[4 * i] = __float_as_uint(f.x);
-              r[4 * i + 1] = __float_as_uint(f.y);
-              r[4 * i + 2] = __float_as_uint(f.z);
-              r[4 * i + 3] = __float_as_uint(f.w);
+          for (int i = 0; i < 8; ++i) {
+            float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (row_ok) {
+              f = __ldcg(src + i);
               __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
             }
-            tmem_st32(tbase + c * 32, r);
+            r[4 * i] = __float_as_uint(f.x);
+            r[4 * i + 1] = __float_as_uint(f.y);
+            r[4 * i + 2] = __float_as_uint(f.z);
+            r[4 * i + 3] = __float_as_uint(f.w);
           }
+          tmem_st32(tbase + c * 32, r);
         }
         tmem_st_wait();
         if (warp == 2 && lane == 0) p.split_cnt[slot] = 0;
