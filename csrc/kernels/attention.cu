@@ -417,9 +417,21 @@ bool arena_map(CUtensorMap* map, const PagedAttnArgs& a) {
 // shared memory each). A ragged last wave idles SMs (80 x 8 CTAs on 296 slots is 2.16 waves,
 // 72% busy), so pick the split count with the best wave efficiency, moving to more splits only
 // for a >3% gain (each split adds a partial-O write and the combine), with >= 8 pages per split.
+static int g_split_mode = 1;
+void set_decode_split_mode(int mode) { g_split_mode = mode; }
+
 int paged_decode_splits(int num_seqs, int n_kv_heads, int max_blocks_per_seq) {
   const long long ctas = static_cast<long long>(num_seqs) * n_kv_heads;
   if (ctas <= 0) return 1;
+  if (g_split_mode == 0) {  // fill: just enough splits for 2 CTAs per SM
+    const long long target = 2LL * num_sms();
+    if (ctas >= target) return 1;
+    int s = static_cast<int>((target + ctas - 1) / ctas);
+    int cap = max_blocks_per_seq / 8;
+    if (cap < 1) cap = 1;
+    if (s > cap) s = cap;
+    return s > 32 ? 32 : s;
+  }
   const long long slots = 2LL * num_sms();
   int cap = max_blocks_per_seq / 8;
   if (cap < 1) cap = 1;

@@ -777,9 +777,12 @@ static int tile_width(int M, int N, int epi, bool w8) {
   return bn_for(M, N, epi, false);
 }
 
+static int g_streamk_mode = 1;
+void set_gemm_streamk_mode(int mode) { g_streamk_mode = mode; }
+
 // Stream-K grid this call will use (0 = data-parallel).
 static int plan_streamk(int M, int N, int K, int epi, bool grouped, int max_ctas, bool w8) {
-  if (grouped || max_ctas > 0 || !sk_epilogue(epi)) return 0;
+  if (!g_streamk_mode || grouped || max_ctas > 0 || !sk_epilogue(epi)) return 0;
   float* ws;
   int* cnt;
   if (!sk_workspace(&ws, &cnt)) return 0;
