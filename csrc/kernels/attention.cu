@@ -414,16 +414,17 @@ bool arena_map(CUtensorMap* map, const PagedAttnArgs& a) {
 }  // namespace
 
 // Split-KV count: the grid is seqs x kv_heads x splits CTAs, two resident per SM (97 KB of
-// shared memory each). A ragged last wave idles SMs (80 x 8 CTAs on 296 slots is 2.16 waves,
-// 72% busy), so pick the split count with the best wave efficiency, moving to more splits only
-// for a >3% gain (each split adds a partial-O write and the combine), with >= 8 pages per split.
-static int g_split_mode = 1;
+// shared memory each). Default (mode 0, fill): just enough splits for two CTAs per SM. Mode 1
+// picks the split count with the best last-wave fill (80 x 8 CTAs on 296 slots is 2.16 waves),
+// moving to more splits only for a >3% gain, with >= 8 pages per split; on B200 at 80 x 2196
+// it measured 0.3 ms per step slower (more, shorter CTAs plus the combine kernel).
+static int g_split_mode = 0;
 void set_decode_split_mode(int mode) { g_split_mode = mode; }
 
 int paged_decode_splits(int num_seqs, int n_kv_heads, int max_blocks_per_seq) {
   const long long ctas = static_cast<long long>(num_seqs) * n_kv_heads;
   if (ctas <= 0) return 1;
-  if (g_split_mode == 0) {  // fill: just enough splits for 2 CTAs per SM
+  if (g_split_mode == 0) {
     const long long target = 2LL * num_sms();
     if (ctas >= target) return 1;
     int s = static_cast<int>((target + ctas - 1) / ctas);

@@ -157,7 +157,7 @@ int paged_decode(const PagedAttnArgs& a, cudaStream_t stream);
 int paged_decode_with_map(const PagedAttnArgs& a, const CUtensorMap& arena_map, cudaStream_t stream);
 // Number of split-KV partitions paged_decode will use for a batch shape.
 int paged_decode_splits(int num_seqs, int n_kv_heads, int max_blocks_per_seq);
-void set_decode_split_mode(int mode);  // 1: best wave efficiency (default), 0: fill 2 CTAs per SM
+void set_decode_split_mode(int mode);  // 0: fill 2 CTAs per SM (default), 1: best wave efficiency
 void set_gemm_streamk_mode(int mode);  // 1: stream-K where it balances SMs (default), 0: data-parallel only
 // Causal prefill / chunked prefill over query tiles of <= 64 rows (warp-level MMA).
 int paged_prefill(const PagedAttnArgs& a, cudaStream_t stream);

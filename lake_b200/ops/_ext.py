@@ -23,7 +23,7 @@ def native():
             # two-SM tcgen05 GEMM for large plain projections (LAKEB_GEMM_PAIR=0 turns it off)
             _C.set_gemm_pair_mode(int(os.environ.get("LAKEB_GEMM_PAIR", "1") or 0))
             _C.set_gemm_streamk_mode(int(os.environ.get("LAKEB_GEMM_STREAMK", "1") or 0))
-            _C.set_decode_split_mode(int(os.environ.get("LAKEB_DECODE_SPLITS", "1") or 0))
+            _C.set_decode_split_mode(int(os.environ.get("LAKEB_DECODE_SPLITS", "0") or 0))
         except ImportError as e:  # pragma: no cover - depends on the build
             _ERR = e
             raise RuntimeError(
