@@ -185,8 +185,10 @@ class Window:
 
 
 def _latency_stats(eng, t0, t1, w: Window):
+    """TTFT of every request whose first token came inside the window (arrival may precede it);
+    TPOT from each request's token times inside the window."""
     for r in eng.requests.values():
-        if r.first_token_time is not None and t0 <= r.arrival and r.first_token_time <= t1:
+        if r.first_token_time is not None and t0 <= r.first_token_time <= t1:
             w.ttft.append(r.ttft())
         tt = [x for x in r.token_times if t0 <= x <= t1]
         if len(tt) >= 2:
