@@ -21,9 +21,13 @@ time of the K public-API `LLMEngine.step()` calls, which include scheduling, the
 pinned host->device copy of each step's metadata and the device->host read of
 the sampled tokens.
 
-PD-split uses ~60% of the GPUs for prefill (1+1, 2+2, 5+3): a decode instance is
-fed by one or more prefill instances whose QKV epilogue writes K/V straight into
-its paged arena over NVLink.
+PD-split (the default from 2 GPUs): one prefill and one decode instance of N/2
+GPUs each (2 GPUs: 1 + 1; 4: TP2 + TP2; 8: TP4 + TP4, the tensor-parallel
+groups running the fused NVLink collectives). The prefill instance's QKV
+epilogue writes K/V straight into the decode instance's paged arena over NVLink
+(TP rank i into TP rank i). `--tp 1` instead runs single-GPU instances with ~60%
+of the GPUs prefilling (2+2, 5+3; a decode instance fed by several prefill
+instances).
 """
 from __future__ import annotations
 
@@ -57,9 +61,9 @@ def parse():
                     help="synchronous steps (default: schedule and launch step n+1 before finishing step n)")
     ap.add_argument("--mode", choices=["colocated", "pd"], default=None,
                     help="default: pd for an even number of GPUs >= 2, else colocated")
-    ap.add_argument("--tp", type=int, default=1,
+    ap.add_argument("--tp", type=int, default=0,
                     help="tensor-parallel instance size (pd: prefill and decode instances of this many GPUs; "
-                         "0 = half the GPUs per instance from 4 GPUs up)")
+                         "0 = half the GPUs per instance from 4 GPUs up, else 1)")
     ap.add_argument("--ep", action="store_true",
                     help="expert parallel (MoE models): over the decode ranks in pd mode, over all ranks colocated")
     ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
@@ -510,8 +514,11 @@ def main():
         if world > 1:
             dist.barrier(group=group)
 
-    if args.tp == 0:  # auto: half the GPUs per PD-split instance, as the prefill/decode TP groups of 8 GPUs
-        args.tp = max(1, min(4, world // 2)) if (args.mode in (None, "pd") and not args.ep and world >= 4) else 1
+    if args.tp == 0:  # auto: half the GPUs per PD-split instance (8 GPUs: TP4 prefill + TP4 decode)
+        args.tp = 1
+        if args.mode in (None, "pd") and not args.ep and world >= 4:
+            while args.tp * 2 <= min(4, world // 2) and world % (args.tp * 2) == 0:
+                args.tp *= 2
     if world % args.tp:
         raise SystemExit("--tp must divide the GPU count")
     mode = args.mode or ("pd" if world // args.tp >= 2 else "colocated")
