@@ -81,6 +81,7 @@ KVArenaView arena_view(const at::Tensor& arena, int64_t layer) {
   v.kv_stride = arena.stride(2);
   v.head_stride = arena.stride(3);
   v.block_size = static_cast<int>(arena.size(4));
+  v.num_slots = arena.size(0) * arena.size(4);
   return v;
 }
 
@@ -533,14 +534,17 @@ void resolve_tokens(at::Tensor& ids, const at::Tensor& prev) {
 }
 
 void page_copy(const at::Tensor& src, at::Tensor& dst, const at::Tensor& src_ids, const at::Tensor& dst_ids,
-               int64_t page_bytes, int64_t sub_off, int64_t sub_bytes) {
+               int64_t page_bytes, int64_t sub_off, int64_t sub_bytes, c10::optional<at::Tensor> status) {
   TORCH_CHECK(src_ids.scalar_type() == at::kLong && dst_ids.scalar_type() == at::kLong, "ids int64");
   TORCH_CHECK(src_ids.numel() == dst_ids.numel(), "id count mismatch");
+  TORCH_CHECK(page_bytes > 0, "page_bytes must be positive");
   check_aligned(src, "src");
   check_aligned(dst, "dst");
+  const int64_t src_pages = static_cast<int64_t>(src.numel()) * src.element_size() / page_bytes;
+  const int64_t dst_pages = static_cast<int64_t>(dst.numel()) * dst.element_size() / page_bytes;
   LAKEB_CHECK_RC(lakeb::page_copy(src.data_ptr(), dst.data_ptr(), src_ids.data_ptr<int64_t>(),
                                   dst_ids.data_ptr<int64_t>(), static_cast<int>(src_ids.numel()), page_bytes,
-                                  sub_off, sub_bytes, cur_stream()),
+                                  sub_off, sub_bytes, cur_stream(), src_pages, dst_pages, status_ptr(status)),
                  "page_copy");
 }
 
@@ -622,7 +626,10 @@ at::Tensor ipc_import(const py::bytes& handle, std::vector<int64_t> sizes, at::S
 
 }  // namespace
 
-PYBIND11_MODULE(_C, m) {
+#ifndef LAKEB_MODULE
+#define LAKEB_MODULE _C
+#endif
+PYBIND11_MODULE(LAKEB_MODULE, m) {
   m.def("enable_peer_access", &enable_peer_access);
   m.def("alloc_ipc_tensor", &alloc_ipc_tensor);
   m.def("ipc_export", &ipc_export);
@@ -686,6 +693,9 @@ PYBIND11_MODULE(_C, m) {
   m.def("unpack_argmax", &unpack_argmax);
   m.def("apply_bitmask", &apply_bitmask);
   m.def("chain_reject", &chain_reject);
-  m.def("page_copy", &page_copy);
+  m.def("page_copy", &page_copy, py::arg("src"), py::arg("dst"), py::arg("src_ids"), py::arg("dst_ids"),
+        py::arg("page_bytes"), py::arg("sub_off"), py::arg("sub_bytes"), py::arg("status") = py::none());
+  m.def("debug_checks", &lakeb::debug_checks_enabled,
+        "true in the bounds-checked debug build (lake_b200/_C_debug.so)");
   m.def("page_copy_to_ptr", &page_copy_to_ptr);
 }

@@ -180,7 +180,10 @@ __global__ void __launch_bounds__(128) paged_decode_kernel(const __grid_constant
     const int n = min(4, b1 - first);
     int pg[4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) pg[b] = b < n ? bt[first + b] : 0;  // all ids before the first TMA issue
+    for (int b = 0; b < 4; ++b) {  // all ids before the first TMA issue
+      pg[b] = b < n ? bt[first + b] : 0;
+      if (!in_bounds(pg[b] >= 0 && pg[b] < a.num_blocks, a.status)) pg[b] = 0;  // debug build only
+    }
     mbar_expect_tx(&full[buf], n * 2 * kPageBytes);
     for (int b = 0; b < n; ++b)
       load_page(&kvmap, a, smem + buf * kStageBytes + b * 2 * kPageBytes, &full[buf], pg[b], kvh);
@@ -322,7 +325,10 @@ __global__ void __launch_bounds__(128) paged_prefill_kernel(const __grid_constan
     const int buf = j % kStages;
     int pg[4];
 #pragma unroll
-    for (int b = 0; b < 4; ++b) pg[b] = bt[min(j * 4 + b, nblk - 1)];  // past-the-end: last page (masked)
+    for (int b = 0; b < 4; ++b) {
+      pg[b] = bt[min(j * 4 + b, nblk - 1)];  // past-the-end: last page (masked)
+      if (!in_bounds(pg[b] >= 0 && pg[b] < a.num_blocks, a.status)) pg[b] = 0;  // debug build only
+    }
     mbar_expect_tx(&full[buf], kStageBytes);
     for (int b = 0; b < 4; ++b)
       load_page(&kvmap, a, smem + buf * kStageBytes + b * 2 * kPageBytes, &full[buf], pg[b], kvh);

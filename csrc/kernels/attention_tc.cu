@@ -139,7 +139,10 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
         const uint32_t ph = ((j >> 1) & 1) ^ 1;
         int pg[8];
 #pragma unroll
-        for (int p = 0; p < 8; ++p) pg[p] = pg_next[p];
+        for (int p = 0; p < 8; ++p) {
+          pg[p] = pg_next[p];
+          if (!in_bounds(pg[p] >= 0 && pg[p] < a.num_blocks, a.status)) pg[p] = 0;  // debug build only
+        }
         if (j + 1 < n_tiles) {
 #pragma unroll
           for (int p = 0; p < 8; ++p) pg_next[p] = bt[min((j + 1) * 8 + p, nblk - 1)];

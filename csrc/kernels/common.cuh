@@ -38,6 +38,21 @@ __device__ __forceinline__ void record_error(int* status, int code) {
   if (status) atomicCAS(status, 0, code);
 }
 
+// Index check of the bounds-checked debug build (nvcc -DLAKEB_DEBUG_CHECKS, built as
+// lake_b200/_C_debug.so by `python -m lake_b200._build --debug`): a failed check records
+// kErrBounds in the status word and returns false so the caller skips or clamps the access.
+// In the release build it is the constant true and the condition compiles away.
+__device__ __forceinline__ bool in_bounds(bool ok, int* status) {
+#ifdef LAKEB_DEBUG_CHECKS
+  if (!ok) record_error(status, kErrBounds);
+  return ok;
+#else
+  (void)ok;
+  (void)status;
+  return true;
+#endif
+}
+
 // ---------------------------------------------------------------- mbarrier
 __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));

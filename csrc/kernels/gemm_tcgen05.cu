@@ -516,6 +516,10 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
           if (!is_q) {
             slot = p.slots ? p.slots[row] : -1;
             if (p.peer_kv.base && p.peer_slots) pslot = p.peer_slots[row];
+            // debug build: a slot past the arena is reported and its store skipped
+            if (slot >= 0 && !in_bounds(p.kv.num_slots <= 0 || slot < p.kv.num_slots, p.status)) slot = -1;
+            if (pslot >= 0 && !in_bounds(p.peer_kv.num_slots <= 0 || pslot < p.peer_kv.num_slots, p.status))
+              pslot = -1;
           }
         }
         if (is_q || is_k) {

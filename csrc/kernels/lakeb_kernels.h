@@ -54,6 +54,7 @@ struct KVArenaView {
   int64_t kv_stride = 0;          // elements from the K half to the V half
   int64_t head_stride = 0;        // elements between kv heads
   int block_size = 16;            // tokens per block
+  int64_t num_slots = 0;          // blocks x block_size (index checks of the debug build)
 };
 
 struct GemmArgs {
@@ -249,7 +250,10 @@ int wait_counters(const unsigned long long* cnt, int n, unsigned long long targe
 
 // ids[i] < 0 -> prev[-1 - ids[i]] (tokens sampled by the previous, still in-flight step)
 int resolve_tokens(int* ids, const int* prev, int n, int n_prev, cudaStream_t stream);
+// src_pages / dst_pages bound the page ids in the debug build (0 = unknown)
 int page_copy(const void* src, void* dst, const int64_t* src_ids, const int64_t* dst_ids, int n, int64_t page_bytes,
-              int64_t sub_off, int64_t sub_bytes, cudaStream_t stream);
+              int64_t sub_off, int64_t sub_bytes, cudaStream_t stream, int64_t src_pages = 0, int64_t dst_pages = 0,
+              int* status = nullptr);
+bool debug_checks_enabled();  // true in the bounds-checked debug build
 
 }  // namespace lakeb

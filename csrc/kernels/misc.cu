@@ -202,10 +202,15 @@ __global__ void chain_reject_kernel(const int* __restrict__ draft, const int* __
 // Copy whole pages: dst_base[dst_ids[i]] <- src_base[src_ids[i]], page_bytes each.
 // Either side may be a peer GPU's memory mapped into this context.
 __global__ void page_copy_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst, const int64_t* __restrict__ src_ids,
-                                 const int64_t* __restrict__ dst_ids, int64_t page_bytes, int64_t sub_off, int64_t sub_bytes) {
+                                 const int64_t* __restrict__ dst_ids, int64_t page_bytes, int64_t sub_off, int64_t sub_bytes,
+                                 int64_t src_pages, int64_t dst_pages, int* status) {
   const int64_t p = blockIdx.y;
-  const uint4* s = reinterpret_cast<const uint4*>(src + src_ids[p] * page_bytes + sub_off);
-  uint4* d = reinterpret_cast<uint4*>(dst + dst_ids[p] * page_bytes + sub_off);
+  const int64_t si = src_ids[p], di = dst_ids[p];
+  if (!in_bounds(si >= 0 && di >= 0 && (src_pages <= 0 || si < src_pages) && (dst_pages <= 0 || di < dst_pages),
+                 status))
+    return;
+  const uint4* s = reinterpret_cast<const uint4*>(src + si * page_bytes + sub_off);
+  uint4* d = reinterpret_cast<uint4*>(dst + di * page_bytes + sub_off);
   const int64_t nvec = sub_bytes / 16;
   for (int64_t v = blockIdx.x * blockDim.x + threadIdx.x; v < nvec; v += static_cast<int64_t>(gridDim.x) * blockDim.x)
     d[v] = s[v];
@@ -275,15 +280,25 @@ int chain_reject(const int* draft, const int* draft_off, const int* target, cons
 }
 
 int page_copy(const void* src, void* dst, const int64_t* src_ids, const int64_t* dst_ids, int n, int64_t page_bytes,
-              int64_t sub_off, int64_t sub_bytes, cudaStream_t stream) {
+              int64_t sub_off, int64_t sub_bytes, cudaStream_t stream, int64_t src_pages, int64_t dst_pages,
+              int* status) {
   if (n <= 0) return 0;
   if (page_bytes % 16 || sub_off % 16 || sub_bytes % 16) return -1;
   const int64_t nvec = sub_bytes / 16;
   int gx = static_cast<int>((nvec + 255) / 256);
   if (gx > 64) gx = 64;
   page_copy_kernel<<<dim3(gx, n), 256, 0, stream>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst),
-                                                    src_ids, dst_ids, page_bytes, sub_off, sub_bytes);
+                                                    src_ids, dst_ids, page_bytes, sub_off, sub_bytes, src_pages,
+                                                    dst_pages, status);
   return cudaGetLastError();
+}
+
+bool debug_checks_enabled() {
+#ifdef LAKEB_DEBUG_CHECKS
+  return true;
+#else
+  return false;
+#endif
 }
 
 int resolve_tokens(int* ids, const int* prev, int n, int n_prev, cudaStream_t stream) {

@@ -6,11 +6,16 @@ Compiles
   * links both into ``lake_b200/_C.so`` (CUDA runtime linked statically)
   * ``csrc/host/**/*.cpp``  -> ``lake_b200/_host.so`` (pybind11 + static CUDA runtime, no torch)
 
+``--debug`` builds the bounds-checked variant of the kernels and bindings instead
+(``-DLAKEB_DEBUG_CHECKS``) into ``lake_b200/_C_debug.so``: index checks record an
+error code in the status word and skip the access. ``LAKEB_DEBUG_CHECKS=1`` makes
+``lake_b200.ops`` load it in place of ``_C``.
+
 The build is driven by a generated ninja file under ``_build/`` so repeated
 builds are incremental. Nothing is JIT-compiled at import time: the ``.so``
 files live next to the Python sources and travel with the tree.
 
-Usage: ``python -m lake_b200._build [-j N]``.
+Usage: ``python -m lake_b200._build [-j N] [--debug]``.
 """
 from __future__ import annotations
 
@@ -48,7 +53,7 @@ def _q(xs):
     return " ".join(xs)
 
 
-def write_ninja() -> str:
+def write_ninja(debug: bool = False) -> str:
     tinc, tlib, abi = _torch_paths()
     pyinc = sysconfig.get_paths()["include"]
     nvcc = os.path.join(CUDA_HOME, "bin", "nvcc")
@@ -56,10 +61,13 @@ def write_ninja() -> str:
     cuda_lib = os.path.join(CUDA_HOME, "lib64")
     kdir = os.path.join(ROOT, "csrc", "kernels")
 
+    mod = "_C_debug" if debug else "_C"
+    build_dir = BUILD + ("_debug" if debug else "")
     nv_flags = ARCH + ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
-                       f"-I{kdir}", "-DNDEBUG"]
+                       f"-I{kdir}", "-DNDEBUG"] + (["-DLAKEB_DEBUG_CHECKS"] if debug else [])
     ext_flags = ["-O2", "-fPIC", "-std=c++17", f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_API_INCLUDE_EXTENSION_H",
-                 "-DTORCH_EXTENSION_NAME=_C", f"-I{pyinc}", f"-I{cuda_inc}", f"-I{kdir}"] + [f"-I{i}" for i in tinc]
+                 f"-DTORCH_EXTENSION_NAME={mod}", f"-DLAKEB_MODULE={mod}", f"-I{pyinc}", f"-I{cuda_inc}",
+                 f"-I{kdir}"] + [f"-I{i}" for i in tinc] + (["-DLAKEB_DEBUG_CHECKS"] if debug else [])
     host_flags = ["-O2", "-fPIC", "-std=c++17", f"-I{pyinc}", f"-I{_pybind_inc()}",
                   f"-I{os.path.join(ROOT, 'csrc', 'host')}", f"-I{cuda_inc}", "-fvisibility=hidden", "-Wall", "-Wno-unused-function"]
 
@@ -95,13 +103,13 @@ def write_ninja() -> str:
     ]
     kobjs = []
     for src in sorted(glob.glob(os.path.join(kdir, "*.cu"))):
-        obj = os.path.join(BUILD, "kernels", os.path.basename(src) + ".o")
+        obj = os.path.join(build_dir, "kernels", os.path.basename(src) + ".o")
         lines.append(f"build {obj}: nvcc {src}")
         kobjs.append(obj)
     bind_src = os.path.join(ROOT, "csrc", "bindings", "ops.cpp")
-    bind_obj = os.path.join(BUILD, "bindings", "ops.o")
+    bind_obj = os.path.join(build_dir, "bindings", "ops.o")
     lines.append(f"build {bind_obj}: cxx_ext {bind_src}")
-    lines.append(f"build {os.path.join(PKG, '_C.so')}: link_ext {_q(kobjs + [bind_obj])}")
+    lines.append(f"build {os.path.join(PKG, mod + '.so')}: link_ext {_q(kobjs + [bind_obj])}")
 
     hobjs = []
     for src in sorted(glob.glob(os.path.join(ROOT, "csrc", "host", "**", "*.cpp"), recursive=True)):
@@ -109,10 +117,10 @@ def write_ninja() -> str:
         obj = os.path.join(BUILD, "host", rel + ".o")
         lines.append(f"build {obj}: cxx_host {src}")
         hobjs.append(obj)
-    if hobjs:
+    if hobjs and not debug:
         lines.append(f"build {os.path.join(PKG, '_host.so')}: link_host {_q(hobjs)}")
-    os.makedirs(BUILD, exist_ok=True)
-    path = os.path.join(BUILD, "build.ninja")
+    os.makedirs(build_dir, exist_ok=True)
+    path = os.path.join(build_dir, "build.ninja")
     text = "\n".join(lines) + "\n"
     old = open(path).read() if os.path.exists(path) else None
     if old != text:
@@ -121,9 +129,9 @@ def write_ninja() -> str:
     return path
 
 
-def build(jobs: int | None = None, verbose: bool = False) -> None:
-    write_ninja()
-    cmd = ["ninja", "-C", BUILD]
+def build(jobs: int | None = None, verbose: bool = False, debug: bool = False) -> None:
+    write_ninja(debug)
+    cmd = ["ninja", "-C", BUILD + ("_debug" if debug else "")]
     if jobs:
         cmd += ["-j", str(jobs)]
     if verbose:
@@ -135,8 +143,9 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("-j", type=int, default=None)
     ap.add_argument("-v", action="store_true")
+    ap.add_argument("--debug", action="store_true", help="bounds-checked build -> lake_b200/_C_debug.so")
     args = ap.parse_args(argv)
-    build(args.j, args.v)
+    build(args.j, args.v, args.debug)
 
 
 if __name__ == "__main__":

@@ -19,7 +19,9 @@ def native():
     global _C, _ERR
     if _C is None:
         try:
-            _C = importlib.import_module("lake_b200._C")
+            # LAKEB_DEBUG_CHECKS=1: the bounds-checked build (python -m lake_b200._build --debug)
+            debug = os.environ.get("LAKEB_DEBUG_CHECKS", "0") not in ("", "0")
+            _C = importlib.import_module("lake_b200._C_debug" if debug else "lake_b200._C")
             # two-SM tcgen05 GEMM for large plain projections (LAKEB_GEMM_PAIR=0 turns it off)
             _C.set_gemm_pair_mode(int(os.environ.get("LAKEB_GEMM_PAIR", "1") or 0))
             _C.set_gemm_streamk_mode(int(os.environ.get("LAKEB_GEMM_STREAMK", "1") or 0))

@@ -304,7 +304,8 @@ def page_copy(src: torch.Tensor, dst: torch.Tensor, src_ids: torch.Tensor, dst_i
     if sub_bytes is None:
         sub_bytes = page_bytes
     if src.is_cuda or dst.is_cuda:
-        native().page_copy(src, dst, src_ids, dst_ids, page_bytes, sub_off, sub_bytes)
+        native().page_copy(src, dst, src_ids, dst_ids, page_bytes, sub_off, sub_bytes,
+                           status_word(src.device if src.is_cuda else dst.device))
         LAUNCHES[0] += 1
         return
     s = src.view(torch.uint8).view(-1, page_bytes)
