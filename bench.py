@@ -383,6 +383,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
         eng.runner.time_device = False
         barrier()
         pd.serve_prefill(side)                        # until EXIT
+        side.close()
         return w, role
     eng.runner.capture_graphs()
     if not leader:
@@ -410,6 +411,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
         eng.runner.time_device = False
         barrier()
         side.follow()                                 # until EXIT
+        side.close()
         return w, role
     nprng = np.random.default_rng(args.seed * 1000 + rank)
     vocab = eng.cfg.vocab
@@ -470,6 +472,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
     side.phase(2)
     barrier()
     side.shutdown()
+    side.close()
     return w, role
 
 

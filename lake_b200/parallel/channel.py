@@ -16,6 +16,16 @@ import numpy as np
 HDR = 8  # head, tail, ... (int64 slots)
 
 
+def _untrack(shm) -> None:
+    """An attaching process must not unlink the segment at exit (its resource tracker would)."""
+    try:
+        from multiprocessing import resource_tracker
+
+        resource_tracker.unregister(shm._name, "shared_memory")
+    except Exception:  # pragma: no cover - tracker layout differs across Python versions
+        pass
+
+
 class ShmRing:
     def __init__(self, name: str, capacity_words: int = 1 << 20, create: bool = False):
         self.name = name
@@ -34,6 +44,7 @@ class ShmRing:
         else:
             self.shm = shared_memory.SharedMemory(name=name)
             self.buf = np.ndarray((HDR + capacity_words,), dtype=np.int64, buffer=self.shm.buf)
+            _untrack(self.shm)  # the creating process owns the name and unlinks it
         self.owner = create
 
     # head: total words written; tail: total words consumed
@@ -83,6 +94,8 @@ class ShmRing:
         return out
 
     def close(self):
+        if self.buf is None:
+            return
         self.buf = None
         self.shm.close()
         if self.owner:

@@ -238,6 +238,10 @@ class DecodeSide:
         for to_p, _ in self.links:
             to_p.put_wait([MARK, code])
 
+    def close(self) -> None:
+        """Release this side's rings (the creator's close also unlinks them)."""
+        _close_rings([r for link in self.links for r in link], self.ctl)
+
     def shutdown(self) -> None:
         for to_p, _ in self.links:
             to_p.put_wait([EXIT])
@@ -332,6 +336,22 @@ class PrefillSide:
 
     def idle(self) -> bool:
         return not self.eng.has_unfinished()
+
+    def close(self) -> None:
+        _close_rings([r for r in (self.from_d, self.to_d) if r is not None], self.ctl)
+
+
+def _close_rings(rings, ctl) -> None:
+    for r in rings:
+        r.close()
+    if ctl is not None:
+        if ctl.rings:
+            for cmd, ack in ctl.rings.values():
+                cmd.close()
+                ack.close()
+        for r in (getattr(ctl, "cmd", None), getattr(ctl, "ackr", None)):
+            if r is not None:
+                r.close()
 
 
 def ring_names(job: str, d_rank: int, p_rank: int) -> tuple[str, str]:

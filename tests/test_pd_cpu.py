@@ -158,6 +158,7 @@ def _worker_groups(rank, port, out_dir):
         assert side.follow() == 7
         res = {"outs": [eng.requests[f"pd-{i}"].output for i in range(len(prompts))]}
         assert side.follow() == -1
+    side.close()
     if rank == 0:
         res["want"] = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512,
                                 num_blocks=96).generate(prompts, max_new_tokens=8)
