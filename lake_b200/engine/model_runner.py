@@ -70,6 +70,8 @@ class ModelRunner:
         self.h_tok = self.h_toks[0]
         self._tok_flip = 0
         self.d_prev = torch.zeros(max(1, max_seqs), dtype=torch.int32, device=self.device)
+        # the device status word comes back with each step's tokens (one pinned int per in-flight step)
+        self.h_status = [torch.zeros(1, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         self.has_pending = False
         self.relay = False  # keep sampled ids in d_prev (set by an engine that overlaps steps)
         self._staged = None  # event after the last metadata copy: the pinned staging is reusable
@@ -314,12 +316,14 @@ class ModelRunner:
             ev1.record()
         nsamp = sum(1 for c in out.chunks if c.sample)
         h = self.h_toks[self._tok_flip]
+        hs = self.h_status[self._tok_flip]
         self._tok_flip ^= 1
         h[:nsamp].copy_(toks[:nsamp], non_blocking=True)
-        self.d2h_bytes += nsamp * 4
+        hs.copy_(ops.core.status_word(self.device), non_blocking=True)
+        self.d2h_bytes += nsamp * 4 + 4
         done = torch.cuda.Event()
         done.record()
-        return ("cuda", h, nsamp, done, ev0, ev1)
+        return ("cuda", h, nsamp, done, ev0, ev1, hs)
 
     def collect(self, handle) -> list[int]:
         """Wait for a launched step and return its sampled ids (chunk order)."""
@@ -327,10 +331,14 @@ class ModelRunner:
             return []
         if handle[0] == "cpu":
             return handle[1]
-        _, h, nsamp, done, ev0, ev1 = handle
+        _, h, nsamp, done, ev0, ev1, hs = handle
         done.synchronize()
         if ev1 is not None:
             self.last_device_ms = ev0.elapsed_time(ev1)
+        code = int(hs[0])
+        if code:  # a kernel of this step recorded an error: clear the word, fail the step
+            ops.core.status_word(self.device).zero_()
+            raise ops.core.KernelError(self.device.index or 0, code)
         return h[:nsamp].tolist()
 
     def execute_null(self) -> None:

@@ -31,15 +31,28 @@ def status_word(device: torch.device) -> torch.Tensor:
 _ERRORS = {1: "mbarrier wait timed out", 2: "peer flag wait timed out", 3: "index out of bounds", 4: "bad argument"}
 
 
+class KernelError(RuntimeError):
+    """A kernel recorded an error code in its device's status word. `timeout`: a bounded wait
+    (an mbarrier phase or a peer's flag) ran out of time, the code a lost peer produces."""
+
+    def __init__(self, device_index: int, code: int):
+        self.device_index, self.code = device_index, code
+        super().__init__(f"lake_b200 kernel error on cuda:{device_index}: {_ERRORS.get(code, code)}")
+
+    @property
+    def timeout(self) -> bool:
+        return self.code in (1, 2)
+
+
 def check_status(device: torch.device | None = None) -> None:
-    """Raise if any kernel on `device` recorded an error (synchronises on the word)."""
+    """Raise KernelError if any kernel on `device` recorded an error (synchronises on the word)."""
     for idx, t in list(_STATUS.items()):
         if device is not None and device.index is not None and idx != device.index:
             continue
         code = int(t.item())
         if code:
             t.zero_()
-            raise RuntimeError(f"lake_b200 kernel error on cuda:{idx}: {_ERRORS.get(code, code)}")
+            raise KernelError(idx, code)
 
 
 # ------------------------------------------------------------------ GEMMs

@@ -32,6 +32,14 @@ LOG = logging.getLogger("lake_b200.worker")
 COALESCE_S = 0.005
 
 
+def _step_error_code(e: Exception) -> PoolErrorCode:
+    """A kernel's bounded wait that ran out (a peer GPU stopped answering) is a TIMEOUT; any other
+    step failure is DOWNSTREAM. Both reach the router as UNAVAILABLE and trigger re-dispatch."""
+    from ..ops.core import KernelError
+
+    return PoolErrorCode.TIMEOUT if isinstance(e, KernelError) and e.timeout else PoolErrorCode.DOWNSTREAM
+
+
 @dataclass
 class GenerateResult:
     request_id: str
@@ -179,7 +187,7 @@ class WorkerEngine:
             except Exception as e:  # step failure: fail in-flight work and stop accepting
                 LOG.exception("engine step failed")
                 self._failed = e
-                err = e if isinstance(e, PoolError) else PoolError(PoolErrorCode.DOWNSTREAM, str(e))
+                err = e if isinstance(e, PoolError) else PoolError(_step_error_code(e), str(e))
                 self._fail_inflight(err)
                 self._reject_inbound(err)
                 self.lifecycle.drain()

@@ -140,3 +140,17 @@ def test_worker_grpc_generate_and_error_mapping():
     finally:
         server.stop(0)
         we.stop(drain=False)
+
+
+def test_kernel_timeout_maps_to_pool_timeout():
+    """A step that failed because a kernel's bounded wait ran out (a peer GPU stopped answering)
+    surfaces as PoolError TIMEOUT; other kernel errors as DOWNSTREAM (both UNAVAILABLE at gRPC)."""
+    from lake_b200.ops.core import KernelError
+    from lake_b200.pool.types import PoolErrorCode
+    from lake_b200.runtime.worker_engine import _step_error_code
+
+    assert _step_error_code(KernelError(0, 2)) == PoolErrorCode.TIMEOUT
+    assert _step_error_code(KernelError(0, 1)) == PoolErrorCode.TIMEOUT
+    assert _step_error_code(KernelError(0, 3)) == PoolErrorCode.DOWNSTREAM
+    assert _step_error_code(ValueError("x")) == PoolErrorCode.DOWNSTREAM
+    assert "peer flag wait timed out" in str(KernelError(1, 2))
