@@ -158,7 +158,7 @@ class ModelRunner:
             else:
                 pslots[row:row + n] = -1
             nb = len(req.block_ids)
-            bt[s, :nb] = req.block_ids
+            bt[s, :nb] = _block_ids_np(req)
             lens[s] = p0 + n
             qst[s] = row
             if s >= nd:
@@ -350,6 +350,26 @@ class ModelRunner:
     def _copy_cpu(self, t, s, nrows):
         self.d_i32.copy_(self.h_i32)
         self.d_i64.copy_(self.h_i64)
+
+
+def _block_ids_np(req) -> np.ndarray:
+    """The request's page ids as an int32 array, kept in step with `req.block_ids`: pages are
+    only appended to the same list (a new list means a new allocation), so the cached array
+    grows by its tail instead of converting the whole Python list every step."""
+    ids = req.block_ids
+    c = req.meta.get("bt_np")
+    if c is None or req.meta.get("bt_src") is not ids or c[1] > len(ids):
+        arr = np.asarray(ids, dtype=np.int32)
+        req.meta["bt_np"] = (np.resize(arr, max(16, 2 * len(ids))), len(ids))
+        req.meta["bt_src"] = ids
+        return arr
+    buf, n = c
+    if n < len(ids):
+        if len(ids) > buf.shape[0]:
+            buf = np.resize(buf, 2 * len(ids))
+        buf[n:len(ids)] = ids[n:]
+        req.meta["bt_np"] = (buf, len(ids))
+    return buf[:len(ids)]
 
 
 def now() -> float:
