@@ -7,7 +7,9 @@ after warm-up, L2 flushed between iterations.
 
 Profile cases (inputs larger than the 126 MB L2, a few GB on the device at most):
 gemm_gate_up (M=4096 K=4096 N=28672), decode (256 seqs x 2304 ctx, 1 layer),
-prefill_tc (4 x 2048), moe_decode (8 experts, 128 tokens top-2, grouped GEMM).
+prefill_tc (4 x 2048), moe_decode (8 experts, 128 tokens top-2, grouped GEMM),
+gemm_decode_qkv (M=80 QKV + RoPE + KV write, stream-K; 50 MB of weights: ncu flushes
+the caches between passes, so its DRAM figures still count the weight stream).
 """
 from __future__ import annotations
 
@@ -216,6 +218,17 @@ def profile(case: str) -> None:
         qs_t = torch.tensor(qs, dtype=torch.int32, device="cuda")
         fn = lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv, 0.088,  # noqa
                                                  out=o)
+    elif case == "gemm_decode_qkv":
+        # decode-size QKV projection (80 tokens, 4096 -> 6144) with RoPE + paged KV write: stream-K
+        m, hq, hkv, hidden = 80, 32, 8, 4096
+        x = torch.randn(m, hidden, device="cuda").to(BF)
+        w = (torch.randn((hq + 2 * hkv) * 128, hidden, device="cuda") * 0.02).to(BF)
+        q = torch.empty(m, hq * 128, device="cuda", dtype=BF)
+        arena = torch.zeros(m // 16 + 1, 1, 2, hkv, 16, 128, device="cuda", dtype=BF)
+        cs = ref.rope_cache(4096, 5e5, 128, None, device="cuda")
+        pos = torch.arange(m, dtype=torch.int32, device="cuda") + 2000
+        slots = torch.arange(m, dtype=torch.int64, device="cuda")
+        fn = lambda: ops.linear_qkv(x, w, q, cs, pos, slots, arena, 0, hq, hkv)  # noqa: E731
     elif case == "moe_decode":
         fn, _ = _moe_case(128)
     else:
