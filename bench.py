@@ -70,6 +70,9 @@ def parse():
                     help="projection weight format (fp8 = block-scaled e4m3, W8A16 GEMMs)")
     ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
     ap.add_argument("--prefill-ranks", type=int, default=0, help="pd mode: prefill instance count (0 = ~60%%)")
+    ap.add_argument("--arrival-rate", type=float, default=0.0,
+                    help="open loop: Poisson arrivals at this many requests/s per request source "
+                         "(colocated engine or decode instance); 0 = closed loop (saturated)")
     ap.add_argument("--prefill-queue", type=int, default=8,
                     help="pd mode: grants outstanding at a prefill rank (bounds queueing delay)")
     pre, _ = ap.parse_known_args()
@@ -188,6 +191,33 @@ class Window:
                 "avg_prefill_tokens": round(self.prefill_rows / max(1, steps), 1)}
 
 
+class Arrivals:
+    """Open-loop request source: Poisson arrivals at `rate` requests/s (exponential gaps from a
+    seeded generator). `due()` is how many requests have arrived since the last call; with
+    rate 0 the source is closed-loop and always has a request ready."""
+
+    def __init__(self, rate: float, seed: int, clock=time.perf_counter):
+        import numpy as np
+
+        self.rate, self.clock = rate, clock
+        self.rng = np.random.default_rng(seed)
+        self.next = clock() + (self.rng.exponential(1.0 / rate) if rate > 0 else 0.0)
+        self.backlog = 0
+
+    def due(self) -> int:
+        if self.rate <= 0:
+            return 1 << 30
+        now = self.clock()
+        while self.next <= now:
+            self.backlog += 1
+            self.next += self.rng.exponential(1.0 / self.rate)
+        return self.backlog
+
+    def take(self) -> None:
+        if self.rate > 0:
+            self.backlog -= 1
+
+
 def _latency_stats(eng, t0, t1, w: Window):
     """TTFT of every request whose first token came inside the window (arrival may precede it);
     TPOT from each request's token times inside the window."""
@@ -241,9 +271,12 @@ def run_colocated(args, rank, local, barrier, tp=None, ep=None):
         done = (j * args.output_len) // args.running
         initial.append(eng.add_request(new_prompt(args.input_len + done), max_new_tokens=args.output_len - done))
 
+    src = Arrivals(args.arrival_rate, args.seed * 1000 + stream_id + 7)
+
     def top_up():
         live = len(eng.scheduler.running) + len(eng.scheduler.waiting)
-        while live < args.running:
+        while live < args.running and src.due() > 0:
+            src.take()
             eng.add_request(new_prompt(args.input_len), max_new_tokens=args.output_len)
             live += 1
 
@@ -419,11 +452,15 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
     def new_prompt(n):
         return nprng.integers(0, vocab, n).tolist()
 
+    src = Arrivals(args.arrival_rate, args.seed * 1000 + rank + 7)
+
     def top_up():
         # keep the prefill partner's queue short (bounded TTFT) and the decode batch <= running
-        while len(side.pending) < args.prefill_queue * len(side.links) and side.inflight < args.running:
+        while (len(side.pending) < args.prefill_queue * len(side.links) and side.inflight < args.running
+               and src.due() > 0):
             if not side.submit(new_prompt(args.input_len), args.output_len):
                 return
+            src.take()
 
     # populate: run the closed loop until a full request lifetime of completions has passed,
     # so the decode batch holds requests at every stage of their output
@@ -597,6 +634,8 @@ def main():
                        "seq_len": args.input_len + args.output_len, "input_len": args.input_len,
                        "output_len": args.output_len, "parallelism": par, "mode": mode,
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",
+                       "arrivals": (f"poisson {args.arrival_rate:g} req/s per request source" if args.arrival_rate
+                                    else "closed loop: a new request whenever one finishes (saturated)"),
                        "step": ("one decode-instance iteration (prefill instances run continuously)" if mode == "pd"
                                 else "one engine iteration: decode all running + chunked prefill of arrivals")},
             "e2e": {"value": round(e2e, 1), "unit": "output tok/s", "h2d_bytes_per_step": int(sm[3].item()),
