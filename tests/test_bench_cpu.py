@@ -31,3 +31,13 @@ def test_pd_layouts():
     assert b.pd_split(2) == (1, 1) and b.pd_split(4) == (2, 2) and b.pd_split(8) == (5, 3)
     assert b.pd_layout(8, 4) == (1, 1) and b.pd_layout(4, 2) == (1, 1)
     assert b.pd_layout(8, 1, n_experts=8) == (4, 4)  # expert-parallel decode ranks divide the experts
+
+
+def test_sweep_commands():
+    from lake_b200.bench import sweep
+
+    one = sweep.command(1, 12.5, ["--steps", "10"])
+    assert one[1].endswith("bench.py") and "--arrival-rate" in one and "12.5" in one and one[-1] == "10"
+    many = sweep.command(8, 0.0, [], port=29611)
+    assert "torch.distributed.run" in many and "--nproc-per-node=8" in many and "127.0.0.1" in many
+    assert "29611" in many and many[many.index("--arrival-rate") + 1] == "0"
