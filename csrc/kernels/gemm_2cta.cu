@@ -11,7 +11,8 @@
 //                loads complete on the even CTA's full barrier)
 //   warp 1     : TMEM allocation (both CTAs); MMA issue + commits (even CTA)
 //   warps 2..5 : epilogue of this CTA's 128 rows (store / residual / SwiGLU / fp32 /
-//                tensor-parallel reduce-scatter push to the row owner's buffer)
+//                tensor-parallel reduce-scatter push to the row owner's buffer / QKV with
+//                RoPE and the paged K/V stores, two heads per tile)
 //
 // Tensor-parallel variants: with tp.ag_cnt set the producer waits, per 128-row
 // half, for the all-gather counters of the row shards it reads; with
@@ -24,6 +25,7 @@
 // Every wait is bounded (2 s) and reports through the status word.
 #include "common.cuh"
 #include "lakeb_kernels.h"
+#include "qkv_epilogue.cuh"
 #include "tma_host.h"
 
 namespace lakeb {
@@ -256,7 +258,11 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const uint32_t tbase = tmem_base + acc * kBN2 + (static_cast<uint32_t>(q * 32) << 16);
       const int row = m_blk * 2 * kBM2 + crank * kBM2 + row_in_tile;
       const bool row_ok = row < p.M;
-      if constexpr (EPI == kEpiRSPush) {
+      if constexpr (EPI == kEpiQKV) {
+        // this CTA's 256 accumulator columns are two whole heads (RoPE, K/V to the arena(s))
+        qkv_head_epilogue(p, tbase, 2 * n_blk, row, row_ok);
+        qkv_head_epilogue(p, tbase + 128, 2 * n_blk + 1, row, row_ok);
+      } else if constexpr (EPI == kEpiRSPush) {
         // partial rows of this rank's K-slice go straight to the row's owner (P2P stores over NVLink)
         __nv_bfloat16* dst_row = nullptr;
         if (row_ok) {
@@ -386,6 +392,9 @@ int gemm_bf16_pair(const GemmArgs& a, int epi, cudaStream_t stream) {
       return launch_pair<kEpiStoreF32>(a, stream);
     case kEpiRSPush:
       return launch_pair<kEpiRSPush>(a, stream);
+    case kEpiQKV:
+      if (a.N % kBN2 || a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128) return -3;
+      return launch_pair<kEpiQKV>(a, stream);
     default:
       return -4;
   }

@@ -20,6 +20,7 @@
 #include <cuda_fp8.h>
 
 #include "lakeb_kernels.h"
+#include "qkv_epilogue.cuh"
 #include "tma_host.h"
 
 namespace lakeb {
@@ -71,19 +72,6 @@ __device__ __forceinline__ void convert_fp8_row(const uint8_t* src, uint8_t* dst
   }
 }
 
-__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint4 u;
-    u.x = pack_bf16x2(v[8 * i + 0], v[8 * i + 1]);
-    u.y = pack_bf16x2(v[8 * i + 2], v[8 * i + 3]);
-    u.z = pack_bf16x2(v[8 * i + 4], v[8 * i + 5]);
-    u.w = pack_bf16x2(v[8 * i + 6], v[8 * i + 7]);
-    d[i] = u;
-  }
-}
-
 __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v) {
   const uint4* s = reinterpret_cast<const uint4*>(src);
 #pragma unroll
@@ -97,13 +85,6 @@ __device__ __forceinline__ void load_bf16x32(const __nv_bfloat16* src, float* v)
       v[8 * i + 2 * j + 1] = f.y;
     }
   }
-}
-
-__device__ __forceinline__ __nv_bfloat16* kv_ptr(const KVArenaView& kv, int64_t slot, int head, int which) {
-  const int64_t blk = slot / kv.block_size;
-  const int64_t off = slot - blk * kv.block_size;
-  return kv.base + blk * kv.block_stride + kv.layer_offset + which * kv.kv_stride + head * kv.head_stride +
-         off * 128;
 }
 
 // Tile t -> (m-block, n-block): m fastest, rotated so the walk starts at tp.m_rot.
@@ -506,94 +487,7 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
         }
       } else if constexpr (EPI == kEpiQKV) {
         static_assert(BN == 128, "QKV epilogue maps one 128-wide head per tile");
-        const int head = n_blk;
-        const bool is_q = head < p.n_q_heads;
-        const bool is_k = !is_q && head < p.n_q_heads + p.n_kv_heads;
-        int pos = 0;
-        int64_t slot = -1, pslot = -1;
-        if (row_ok) {
-          pos = p.positions[row];
-          if (!is_q) {
-            slot = p.slots ? p.slots[row] : -1;
-            if (p.peer_kv.base && p.peer_slots) pslot = p.peer_slots[row];
-            // debug build: a slot past the arena is reported and its store skipped
-            if (slot >= 0 && !in_bounds(p.kv.num_slots <= 0 || slot < p.kv.num_slots, p.status)) slot = -1;
-            if (pslot >= 0 && !in_bounds(p.peer_kv.num_slots <= 0 || pslot < p.peer_kv.num_slots, p.status))
-              pslot = -1;
-          }
-        }
-        if (is_q || is_k) {
-          const int kvh = head - p.n_q_heads;
-          // per-head RMSNorm before RoPE (Qwen3): one pass over the head's 128 accumulators first
-          const __nv_bfloat16* nw = is_q ? p.q_norm_w : p.k_norm_w;
-          float inv = 1.f;
-          if (nw) {
-            float ss = 0.f;
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-              uint32_t r[32];
-              tmem_ld32(tbase + c * 32, r);
-              tmem_ld_wait();
-#pragma unroll
-              for (int j = 0; j < 32; ++j) ss += __uint_as_float(r[j]) * __uint_as_float(r[j]);
-            }
-            inv = rsqrtf(ss * (1.f / 128.f) + p.qk_eps);
-          }
-#pragma unroll 1
-          for (int half = 0; half < 2; ++half) {
-            uint32_t r1[32], r2[32];
-            tmem_ld32(tbase + half * 32, r1);
-            tmem_ld32(tbase + 64 + half * 32, r2);
-            tmem_ld_wait();
-            if (row_ok) {
-              float o1[32], o2[32];
-              const float2* cs = p.rope_cs + static_cast<int64_t>(pos) * 64 + half * 32;
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const float2 c = cs[j];
-                float x1 = __uint_as_float(r1[j]);
-                float x2 = __uint_as_float(r2[j]);
-                if (nw) {
-                  x1 *= inv * __bfloat162float(nw[half * 32 + j]);
-                  x2 *= inv * __bfloat162float(nw[64 + half * 32 + j]);
-                }
-                o1[j] = x1 * c.x - x2 * c.y;
-                o2[j] = x2 * c.x + x1 * c.y;
-              }
-              if (is_q) {
-                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + head * 128;
-                store_bf16x32(dst + half * 32, o1);
-                store_bf16x32(dst + 64 + half * 32, o2);
-              } else {
-                if (slot >= 0) {
-                  __nv_bfloat16* dst = kv_ptr(p.kv, slot, kvh, 0);
-                  store_bf16x32(dst + half * 32, o1);
-                  store_bf16x32(dst + 64 + half * 32, o2);
-                }
-                if (pslot >= 0) {
-                  __nv_bfloat16* dst = kv_ptr(p.peer_kv, pslot, kvh, 0);
-                  store_bf16x32(dst + half * 32, o1);
-                  store_bf16x32(dst + 64 + half * 32, o2);
-                }
-              }
-            }
-          }
-        } else {
-          const int kvh = head - p.n_q_heads - p.n_kv_heads;
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t r[32];
-            tmem_ld32(tbase + c * 32, r);
-            tmem_ld_wait();
-            if (row_ok) {
-              float v[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-              if (slot >= 0) store_bf16x32(kv_ptr(p.kv, slot, kvh, 1) + c * 32, v);
-              if (pslot >= 0) store_bf16x32(kv_ptr(p.peer_kv, pslot, kvh, 1) + c * 32, v);
-            }
-          }
-        }
+        qkv_head_epilogue(p, tbase, n_blk, row, row_ok);
       } else if constexpr (EPI == kEpiArgmax) {
         unsigned long long best = 0ull;
 #pragma unroll 1
@@ -703,12 +597,14 @@ int launch_bn(const GemmArgs& a, cudaStream_t stream) {
 static int g_pair_mode = 0;
 
 // The two-SM kernel takes large plain / residual / SwiGLU / fp32 GEMMs, including the
-// tensor-parallel all-gather GEMMs and the reduce-scatter push GEMM; QKV, argmax, grouped and
-// fp8 GEMMs stay on the single-SM kernel.
-static bool use_pair(int M, int epi, bool grouped, int max_ctas, bool done_signal) {
-  return g_pair_mode && M >= 512 && !grouped && max_ctas == 0 && !done_signal &&
-         (epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiSwiGLU || epi == kEpiStoreF32 ||
-          epi == kEpiRSPush);
+// tensor-parallel all-gather GEMMs and the reduce-scatter push GEMM, and the QKV GEMM when its
+// heads pair up into 256-wide tiles (LAKEB_GEMM_PAIR=2 keeps QKV on the single-SM kernel);
+// argmax, grouped and fp8 GEMMs stay on the single-SM kernel.
+static bool use_pair(int M, int N, int epi, bool grouped, int max_ctas, bool done_signal) {
+  if (!g_pair_mode || M < 512 || grouped || max_ctas != 0 || done_signal) return false;
+  if (epi == kEpiQKV) return g_pair_mode == 1 && N % 256 == 0;
+  return epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiSwiGLU || epi == kEpiStoreF32 ||
+         epi == kEpiRSPush;
 }
 
 // Per-device stream-K workspace: fp32 partial tiles (zero between uses: the finishing CTA zeroes
@@ -798,7 +694,7 @@ static int plan_streamk(int M, int N, int K, int epi, bool grouped, int max_ctas
 }
 
 int gemm_grid(int M, int N, int K, int epi, int max_ctas, bool w8) {
-  if (!w8 && use_pair(M, epi, false, max_ctas, false)) return gemm_pair_grid(M, N);
+  if (!w8 && use_pair(M, N, epi, false, max_ctas, false)) return gemm_pair_grid(M, N);
   const int g = plan_streamk(M, N, K, epi, false, max_ctas, w8);
   if (g) return g;
   return grid_for(M, N, tile_width(M, N, epi, w8), max_ctas);
@@ -828,7 +724,7 @@ int gemm_bf16(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   if (epi == kEpiQKV && a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128) return -3;
   const bool w8 = a.B8 != nullptr;
   // plan order shared with gemm_grid(): two-SM kernel, else stream-K, else data-parallel
-  if (!w8 && use_pair(a.M, epi, a.groups != 0, a.max_ctas, a.tp.done_cnt[0] != nullptr))
+  if (!w8 && use_pair(a.M, a.N, epi, a.groups != 0, a.max_ctas, a.tp.done_cnt[0] != nullptr))
     return gemm_bf16_pair(a, epi, stream);
   a.streamk = plan_streamk(a.M, a.N, a.K, epi, a.groups != 0, a.max_ctas, w8);
   if (a.streamk) sk_workspace(&a.split_ws, &a.split_cnt);

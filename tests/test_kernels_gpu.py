@@ -63,8 +63,9 @@ def _arena(dev, blocks=64, layers=2, hkv=2):
     return torch.zeros(blocks, layers, 2, hkv, 16, 128, dtype=BF, device=dev)
 
 
-def test_linear_qkv_rope_kv_write(cuda_dev):
-    t, hid, hq, hkv = 70, 512, 4, 2
+@pytest.mark.parametrize("t", [70, 600])  # 600: two-SM kernel, two heads per 256-wide tile, ragged rows
+def test_linear_qkv_rope_kv_write(cuda_dev, t):
+    hid, hq, hkv = 512, 4, 2
     a = torch.randn(t, hid, device=cuda_dev).to(BF)
     w = (torch.randn((hq + 2 * hkv) * 128, hid, device=cuda_dev) / 20).to(BF)
     cs = ref.rope_cache(4096, 500000.0, device=cuda_dev)
