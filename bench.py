@@ -70,6 +70,8 @@ def parse():
                     help="projection weight format (fp8 = block-scaled e4m3, W8A16 GEMMs)")
     ap.add_argument("--prefill-running", type=int, default=16, help="max concurrent prefills per prefill rank")
     ap.add_argument("--prefill-ranks", type=int, default=0, help="pd mode: prefill instance count (0 = ~60%%)")
+    ap.add_argument("--spec-tokens", type=int, default=0,
+                    help="speculative decoding: prompt-lookup draft tokens per decode request (0 = off)")
     ap.add_argument("--arrival-rate", type=float, default=0.0,
                     help="open loop: Poisson arrivals at this many requests/s per request source "
                          "(colocated engine or decode instance); 0 = closed loop (saturated)")
@@ -233,6 +235,7 @@ def _make_engine(args, local, max_running, **kw):
     from lake_b200.engine.llm_engine import LLMEngine
 
     kw.setdefault("overlap", not args.no_overlap)
+    kw.setdefault("spec_tokens", args.spec_tokens)
     return LLMEngine(args.model, device=f"cuda:{local}", max_running=max_running, max_batched_tokens=args.budget,
                      max_model_len=args.input_len + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
                      seed=args.seed, weight_dtype=args.weights, **kw)

@@ -55,6 +55,11 @@ class EngineConfig:
     # scheduling and metadata packing hide behind the device. A step's tokens are returned by
     # the following step() call. Not combined with a storage pool or expert parallel.
     overlap: bool = False
+    # Speculative decoding (greedy): up to `spec_tokens` draft tokens per decode request from
+    # prompt lookup (an earlier occurrence of the last `spec_ngram` tokens), verified in one
+    # chunk per request. Steps with drafts run synchronously (no overlap).
+    spec_tokens: int = 0
+    spec_ngram: int = 3
 
 
 @dataclass
@@ -101,8 +106,8 @@ class LLMEngine:
             rank, world, pg = ec.tp
             self.tp_world = world
             max_tokens += world  # rows padded to a multiple of the group size
-            self.tp_group = TPGroup(rank, world, self.device, max_tokens, cfg.hidden, ec.max_running, group=pg,
-                                    status=None)
+            self.tp_group = TPGroup(rank, world, self.device, max_tokens, cfg.hidden,
+                                    ec.max_running * (1 + ec.spec_tokens), group=pg, status=None)
             self.model = TPDecoderLM(cfg, self.tp_group, self.device, seed=ec.seed, weight_dtype=ec.weight_dtype)
             cfg = self._arena_cfg = _local_kv_cfg(cfg, world)
         elif ec.ep is not None and ec.ep[1] > 1:
@@ -143,13 +148,14 @@ class LLMEngine:
             self.arena = torch.zeros(shape, dtype=dtype, device=self.device)
         self.pool = BlockPool(num_blocks, ec.block_size, ec.enable_prefix_cache)
         self.scheduler = Scheduler(self.pool, SchedulerConfig(ec.max_running, ec.max_batched_tokens,
-                                                              ec.long_prefill_threshold, ec.max_model_len, maxb))
+                                                              ec.long_prefill_threshold, ec.max_model_len, maxb,
+                                                              ec.spec_tokens, ec.spec_ngram))
         self.runner = ModelRunner(self.model, self.arena, max_tokens, ec.max_running, maxb,
                                   ec.use_cuda_graphs and not (ec.ep and ec.ep[1] > 1), ec.block_size,
-                                  row_multiple=self.tp_world)
+                                  row_multiple=self.tp_world, max_samples=ec.max_running * (1 + ec.spec_tokens))
         self.requests: dict[str, Request] = {}
         self.pool_iface = None  # PoolIface (storage-pool fences), attached by attach_pool
-        self.overlap = ec.overlap and not (ec.ep and ec.ep[1] > 1)
+        self.overlap = ec.overlap and not (ec.ep and ec.ep[1] > 1) and ec.spec_tokens == 0
         self.inflight = None  # (SchedulerOutput, runner handle) of the launched, unfinished step
         self._drained: list[StepOutput] = []
         if self.overlap:
@@ -281,13 +287,9 @@ class LLMEngine:
             for r in finished:
                 self.pool_iface.on_request_finished(r, self.cfg.name)
         self.step_count += 1
-        res = []
-        it = iter(sampled)
-        for ch in out.chunks:
-            if ch.sample:
-                tok = next(it)
-                res.append(StepOutput(ch.req.rid, [tok], ch.req.finished))
-        return res
+        # one output per sampling chunk: its token, or every verified token of a verify chunk
+        return [StepOutput(ch.req.rid, list(ch.accepted), ch.req.finished)
+                for ch in out.chunks if ch.sample and ch.accepted]
 
     # ------------------------------------------------------------ overlapped stepping
     def _step_overlap(self) -> list[StepOutput]:

@@ -31,13 +31,16 @@ GRAPH_BUCKETS = [1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256, 32
 
 class ModelRunner:
     def __init__(self, model: DecoderLM, arena: torch.Tensor, max_tokens: int, max_seqs: int,
-                 max_blocks_per_seq: int, use_cuda_graphs: bool = True, block_size: int = 16, row_multiple: int = 1):
+                 max_blocks_per_seq: int, use_cuda_graphs: bool = True, block_size: int = 16, row_multiple: int = 1,
+                 max_samples: int | None = None):
         self.model = model
         self.arena = arena
         self.device = model.device
         self.cuda = self.device.type == "cuda"
         self.max_tokens = max_tokens
         self.max_seqs = max_seqs
+        # sampled rows per step: one per sequence, or one per position of a verify chunk
+        self.max_samples = max_samples = max(max_samples or max_seqs, max_seqs)
         self.maxb = max_blocks_per_seq
         self.bs = block_size
         self.row_multiple = row_multiple  # tensor parallel: rows padded to a multiple of the group size
@@ -47,7 +50,7 @@ class ModelRunner:
         if self.cuda:
             self.max_splits = max(ops.decode_splits(n, cfg.n_kv_heads // row_multiple, max_blocks_per_seq)
                                   for n in range(1, max_seqs + 1))
-        self.ws = model.new_workspace(max_tokens, max_seqs, max_seqs, self.max_splits)
+        self.ws = model.new_workspace(max_tokens, max_samples, max_seqs, self.max_splits)
         # int32 staging: ids | pos | seq_lens | qstart | tiles | block_tables
         self.max_tiles = max_tokens // 64 + max_seqs
         self._lay = {}
@@ -59,14 +62,14 @@ class ModelRunner:
         self.n_i32 = off
         pin = self.cuda
         self.h_i32 = torch.zeros(off, dtype=torch.int32, pin_memory=pin)
-        # int64 staging: slots [max_tokens] | sample rows [max_seqs] | peer slots [max_tokens]
-        self.h_i64 = torch.zeros(2 * max_tokens + max_seqs, dtype=torch.int64, pin_memory=pin)
-        self.peer_off = max_tokens + max_seqs
+        # int64 staging: slots [max_tokens] | sample rows [max_samples] | peer slots [max_tokens]
+        self.h_i64 = torch.zeros(2 * max_tokens + max_samples, dtype=torch.int64, pin_memory=pin)
+        self.peer_off = max_tokens + max_samples
         self.peer_arena: torch.Tensor | None = None  # decode instance's arena (IPC-mapped) for fused P->D
         # sampled ids come back through two pinned buffers (one step may be in flight while the
         # previous one is read); d_prev keeps the last step's ids on the device for the next
         # step's PENDING inputs (overlapped scheduling)
-        self.h_toks = [torch.zeros(max_seqs, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
+        self.h_toks = [torch.zeros(max_samples, dtype=torch.int32, pin_memory=pin) for _ in range(2)]
         self.h_tok = self.h_toks[0]
         self._tok_flip = 0
         self.d_prev = torch.zeros(max(1, max_seqs), dtype=torch.int32, device=self.device)
@@ -76,7 +79,7 @@ class ModelRunner:
         self.relay = False  # keep sampled ids in d_prev (set by an engine that overlaps steps)
         self._staged = None  # event after the last metadata copy: the pinned staging is reusable
         self.d_i32 = torch.zeros(off, dtype=torch.int32, device=self.device)
-        self.d_i64 = torch.zeros(2 * max_tokens + max_seqs, dtype=torch.int64, device=self.device)
+        self.d_i64 = torch.zeros(2 * max_tokens + max_samples, dtype=torch.int64, device=self.device)
         self.np_i32 = self.h_i32.numpy()
         self.np_i64 = self.h_i64.numpy()
         self.use_graphs = use_cuda_graphs and self.cuda
@@ -121,7 +124,7 @@ class ModelRunner:
         tiles = self._v(self.np_i32, "tiles", shape=(self.max_tiles, 4))
         bt = self._v(self.np_i32, "bt", shape=(self.max_seqs, maxb))
         slots = self.np_i64[: self.max_tokens]
-        rows = self.np_i64[self.max_tokens: self.max_tokens + self.max_seqs]
+        rows = self.np_i64[self.max_tokens: self.max_tokens + self.max_samples]
         pslots = self.np_i64[self.peer_off:]
         self.has_peer = False
         self.has_pending = False
@@ -144,7 +147,9 @@ class ModelRunner:
                 pos[row] = p0
                 slots[row] = req.block_ids[p0 // bs] * bs + p0 % bs
             else:
-                ids[row:row + n] = req.tokens_slice(p0, p0 + n)
+                # a verify chunk is the last token followed by its draft
+                ids[row:row + n] = (req.tokens_slice(p0, p0 + n) if not ch.draft
+                                    else req.tokens_slice(p0, p0 + 1) + ch.draft)
                 pr = np.arange(p0, p0 + n, dtype=np.int64)
                 pos[row:row + n] = pr
                 blk = np.asarray(req.block_ids, dtype=np.int64)
@@ -168,9 +173,10 @@ class ModelRunner:
                     tiles[ntiles] = (s, t0, k, p0 + (t0 - row))
                     ntiles += 1
                     t0 += k
-            if ch.sample:
-                rows[nrows] = row + n - 1
-                nrows += 1
+            ns = ch.n_samples  # the last row, or every row of a verify chunk
+            if ns:
+                rows[nrows:nrows + ns] = np.arange(row + n - ns, row + n)
+                nrows += ns
             row += n
             s += 1
             if s == nd and pad_decode_to > nd:
@@ -296,7 +302,7 @@ class ModelRunner:
             self._copy_cpu(t, s, nrows)
             batch = self._batch_views(t, s, ntiles, nrows, nd_eff, 1, bitmask, has_remote)
             toks = self._forward(batch, self.has_pending)
-            return ("cpu", toks[: len([c for c in out.chunks if c.sample])].tolist())
+            return ("cpu", toks[: sum(c.n_samples for c in out.chunks)].tolist())
         graph = None
         if bucket is not None:
             graph, toks = self._get_graph(bucket)  # capture (if new) before this step's metadata lands
@@ -314,7 +320,7 @@ class ModelRunner:
             toks = self._forward(batch, self.has_pending)
         if ev1 is not None:
             ev1.record()
-        nsamp = sum(1 for c in out.chunks if c.sample)
+        nsamp = sum(c.n_samples for c in out.chunks)
         h = self.h_toks[self._tok_flip]
         hs = self.h_status[self._tok_flip]
         self._tok_flip ^= 1

@@ -35,6 +35,16 @@ class Chunk:
     start: int
     n: int
     sample: bool
+    # speculative decoding: draft tokens after the request's last token; every position of
+    # the chunk is sampled and `accepted` receives the verified tokens
+    draft: list[int] | None = None
+    accepted: list[int] | None = None
+
+    @property
+    def n_samples(self) -> int:
+        if not self.sample:
+            return 0
+        return 1 + len(self.draft) if self.draft else 1
 
 
 @dataclass
@@ -64,6 +74,8 @@ class SchedulerConfig:
     long_prefill_threshold: int = 0  # 0 = no per-request cap beyond the budget
     max_model_len: int = 8192
     max_blocks_per_seq: int = 512
+    spec_tokens: int = 0  # draft tokens per decode request (prompt lookup); 0 = off
+    spec_ngram: int = 3
 
 
 class Scheduler:
@@ -77,6 +89,12 @@ class Scheduler:
         self.finished: list[Request] = []
         self.on_admit = None  # callback(req) before the prefix lookup of an admission (tier promotion)
         self.before_preempt = None  # callback() before a preemption (overlap: finish the in-flight step)
+        self.drafter = None
+        if self.cfg.spec_tokens > 0:
+            from .spec import NgramDrafter
+
+            self.drafter = NgramDrafter(self.cfg.spec_ngram, self.cfg.spec_tokens)
+        self.spec_stats = {"proposed": 0, "accepted": 0, "verify_chunks": 0}
 
     # -------------------------------------------------------------- admission
     def add(self, req: Request) -> None:
@@ -166,12 +184,17 @@ class Scheduler:
                 break
             if req.is_prefill or req.status != RequestStatus.RUNNING:
                 continue
-            if not self._ensure_blocks(req, req.num_computed + 1, out):
+            draft = self._draft(req, budget)
+            if not self._ensure_blocks(req, req.num_computed + 1 + len(draft), out):
                 continue
             if req.status != RequestStatus.RUNNING:
                 continue
-            out.decode.append(Chunk(req, req.num_computed, 1, True))
-            budget -= 1
+            if draft:  # a multi-token verify chunk: runs with the prefill-shaped chunks
+                out.prefill.append(Chunk(req, req.num_computed, 1 + len(draft), True, draft=draft))
+                budget -= 1 + len(draft)
+            else:
+                out.decode.append(Chunk(req, req.num_computed, 1, True))
+                budget -= 1
         # Pass B: continue chunked prefills
         cap = self.cfg.long_prefill_threshold or budget
         for req in list(self.running):
@@ -210,22 +233,44 @@ class Scheduler:
             budget -= n
         return out
 
+    def _draft(self, req: Request, budget: int) -> list[int]:
+        """Draft tokens for a decode request (speculative decoding), within the budget, the
+        request's remaining output and the model length."""
+        if self.drafter is None or req.bitmask is not None:
+            return []
+        room = min(budget - 1, req.params.max_new_tokens - len(req.output) - 1,
+                   self.cfg.max_model_len - req.num_tokens - 1)
+        if room <= 0:
+            return []
+        d = self.drafter.propose(req)[:room]
+        if d:
+            self.spec_stats["proposed"] += len(d)
+            self.spec_stats["verify_chunks"] += 1
+        return d
+
     # -------------------------------------------------------------- update
     def update(self, out: SchedulerOutput, sampled: list[int], now: float) -> list[Request]:
-        """Apply one step's results. `sampled` has one token per sampling chunk, in chunk order."""
+        """Apply one step's results. `sampled` has `n_samples` tokens per sampling chunk (one, or
+        one per position of a verify chunk), in chunk order."""
         done = []
         it = iter(sampled)
         for ch in out.chunks:
             req = ch.req
             if req.status != RequestStatus.RUNNING:
-                if ch.sample:
+                for _ in range(ch.n_samples):
                     next(it, None)
                 continue
-            req.num_computed = ch.start + ch.n
-            self._register_full_blocks(req)
-            if ch.sample:
-                tok = next(it)
-                req.output.append(int(tok))
+            if ch.draft:
+                target = [int(next(it)) for _ in range(ch.n_samples)]
+                acc = self._verify(ch.draft, target)
+                self.spec_stats["accepted"] += len(acc) - 1
+            else:
+                req.num_computed = ch.start + ch.n
+                acc = [int(next(it))] if ch.sample else []
+            ch.accepted = []
+            for tok in acc:
+                req.output.append(tok)
+                ch.accepted.append(tok)
                 if req.first_token_time is None:
                     req.first_token_time = now
                 req.token_times.append(now)
@@ -233,6 +278,10 @@ class Scheduler:
                     req.status = RequestStatus.FINISHED
                     req.finish_time = now
                     done.append(req)
+                    break
+            if ch.draft:  # K/V stays valid for the last token and the accepted drafts
+                req.num_computed = ch.start + len(ch.accepted)
+            self._register_full_blocks(req)  # after the append: accepted drafts are in its K/V
         for req in done:
             self.running.remove(req)
             self._register_full_blocks(req)
@@ -298,6 +347,12 @@ class Scheduler:
             self._release(req)
             self.finished.append(req)
         return applied
+
+    @staticmethod
+    def _verify(draft: list[int], target: list[int]) -> list[int]:
+        from .spec import accept
+
+        return accept(draft, target)
 
     def _register_full_blocks(self, req: Request) -> None:
         full = req.num_computed // self.bs

@@ -191,3 +191,44 @@ def test_overlapped_scheduling_matches_synchronous():
     got, streamed, _ = _overlap_run(True, 96, eos=eos)
     assert got == want and streamed == got
     assert len(want[0]) == 4
+
+
+def _spec_run(spec, blocks=128, eos=None, max_new=30):
+    import random
+
+    from lake_b200.engine.llm_engine import LLMEngine
+    from lake_b200.engine.request import SamplingParams
+
+    rng = random.Random(1)
+    base = [rng.randrange(1000) for _ in range(40)]
+    prompts = [base * 3, [rng.randrange(1000) for _ in range(50)], base[:20] * 4, [5, 6, 7] * 20]
+    eng = LLMEngine("tiny", device="cpu", max_running=4, max_batched_tokens=128, max_model_len=512,
+                    num_blocks=blocks, spec_tokens=spec)
+    rids = [eng.add_request(p, params=SamplingParams(max_new_tokens=max_new, eos_token_id=eos,
+                                                     ignore_eos=eos is None)) for p in prompts]
+    streamed = {}
+    while eng.has_unfinished():
+        for o in eng.step():
+            streamed.setdefault(o.rid, []).extend(o.new_tokens)
+    full = [eng.requests[r].meta.get("preempted_output", []) + eng.requests[r].output for r in rids]
+    return full, [streamed.get(r, []) for r in rids], eng
+
+
+def test_speculative_decoding_matches_greedy():
+    """Prompt-lookup drafts verified in one chunk per request give exactly the greedy tokens,
+    stream every verified token once, stop at the length limit and at a stop token inside an
+    accepted run, and survive preemption (few pages)."""
+    want, _, _ = _spec_run(0)
+    got, streamed, eng = _spec_run(4)
+    assert got == want and streamed == got
+    st = eng.scheduler.spec_stats
+    assert st["verify_chunks"] > 0 and st["accepted"] > 0 and st["accepted"] <= st["proposed"]
+    assert all(len(o) == 30 for o in got)
+    for blocks in (24,):
+        a, _, _ = _spec_run(0, blocks=blocks)
+        b, _, _ = _spec_run(4, blocks=blocks)
+        assert a == b
+    eos = want[0][5]
+    a, _, _ = _spec_run(0, eos=eos)
+    b, s, _ = _spec_run(4, eos=eos)
+    assert a == b and s == b
