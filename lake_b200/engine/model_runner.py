@@ -174,7 +174,10 @@ class ModelRunner:
                     ntiles += 1
                     t0 += k
             ns = ch.n_samples  # the last row, or every row of a verify chunk
-            if ns:
+            if ns == 1:
+                rows[nrows] = row + n - 1
+                nrows += 1
+            elif ns:
                 rows[nrows:nrows + ns] = np.arange(row + n - ns, row + n)
                 nrows += ns
             row += n
