@@ -225,3 +225,51 @@ def test_defrag_plans_and_relocate():
     assert a.l2_fragmentation_ratio(M, "", 1, 4096) == 0.0
     col = a.plan_defrag(M, "", 1, 2, 4096)  # COLOCATE: hs[2] moves next to its parent
     assert any(m.to_segment == 1 for m in col)
+
+
+def test_frequency_buckets_order_inactive_eviction():
+    """Inactive blocks leave in frequency-bucket order (lookups touch the counter; thresholds
+    3 / 8 / 15), least recently used first inside a bucket."""
+    a = auth()
+    A, B, C = chain(1, seed=0), chain(1, seed=1000), chain(1, seed=2000)
+    for X in (A, B, C):
+        a.register_blocks("n0", X, [meta(h) for h in X])
+        a.report_refs([ref(X[0], REQUEST, 1), ref(X[0], REQUEST, -1)])
+    assert a.inactive_len(M, "", 1) == 3
+    for _ in range(10):
+        a.lookup_prefix(M, "", 0, A, "")
+    for _ in range(4):
+        a.lookup_prefix(M, "", 0, C, "")
+    assert a.evict_n(M, "", 1, 1) == 1  # B: never looked up
+    assert a.evict_n(M, "", 1, 1) == 1  # C: lower bucket than A
+    assert [a.lookup_prefix(M, "", 0, X, "").hit_length for X in (A, B, C)] == [1, 0, 0]
+
+
+def test_quota_locate_l3_barrier_pause_and_deregister():
+    a = auth()
+    hs = chain(2)
+    a.register_blocks("n0", hs, [meta(h) for h in hs])
+    q = H.Quota()
+    q.soft_bytes, q.hard_bytes, q.borrow_enabled = 5 * BPB, 8 * BPB, True
+    a.set_quota(M, "", q)
+    g = a.get_quota(M, "")
+    assert (g.soft_bytes, g.hard_bytes, g.borrow_enabled) == (5 * BPB, 8 * BPB, True)
+    # locate reports every location and the L3 flag (which the object store sets separately)
+    loc = a.locate([H.KVBlockID(M, hs[0])])
+    assert [(l.tier, l.node_id) for l in loc[0].locations] == [(L2, "n0")] and not loc[0].l3_present
+    a.set_l3_present(H.KVBlockID(M, hs[0]), True)
+    assert a.locate([H.KVBlockID(M, hs[0])])[0].l3_present
+    # request barrier: complete once a node acknowledges
+    assert not a.barrier_completed("req-1")
+    a.complete_barrier("req-1", "n0")
+    assert a.barrier_completed("req-1")
+    a.set_background_paused(True)
+    assert a.background_paused()
+    a.set_background_paused(False)
+    assert not a.background_paused()
+    # deregistering drops the namespace with its blocks
+    assert a.has_namespace(M, "")
+    a.deregister_model(M, "")
+    assert not a.has_namespace(M, "")
+    with pytest.raises(ValueError, match="not registered"):
+        a.register_blocks("n0", hs, [meta(h) for h in hs])
