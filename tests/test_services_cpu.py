@@ -272,3 +272,64 @@ def test_byte_store_lru_bound():
         s.put(bytes([i]), b"x" * 30)
     assert len(s) == 3 and s.bytes == 90 and s.evictions == 2
     assert s.get(bytes([0])) is None and s.get(bytes([4])) == b"x" * 30
+
+
+def test_subscribe_view_lagging_subscriber_gets_a_fresh_snapshot(monkeypatch):
+    """A subscriber whose queue overflows is resynchronised: the next message is a seq-0
+    snapshot holding every block, then an anchor at the latest seq; stale queued updates are
+    dropped (reference behaviour: lib.rs subscribe_view, lag -> resnapshot)."""
+    from lake_b200.services import controlplane as cpmod
+
+    monkeypatch.setattr(cpmod, "SUBSCRIBER_QUEUE", 2)
+    cp = ControlPlane()
+    cp.RegisterModel(pb.RegisterModelRequest(model=pb.ModelDescriptor(
+        model_id=M, num_layers=2, block_spec=pb.BlockSpec(block_tokens=16, bytes_per_block=1000), hash_algo=1,
+        quota=pb.Quota(soft_bytes=10 ** 9, hard_bytes=2 * 10 ** 9))), None)
+    gen = cp.SubscribeView(pb.SubscribeRequest(subscriber_id="slow"), None)
+    snap = next(gen)
+    assert snap.seq == 0 and not snap.events
+    for k in range(5):  # five commits into a queue of two
+        cp.RegisterBlocks(reg_req(chain(1, seed=1000 * k)), None)
+    resync = next(gen)
+    assert resync.seq == 0 and len(resync.events) == 5
+    anchor = next(gen)
+    assert anchor.seq == cp.auth.last_seq() and not anchor.events
+    cp.RegisterBlocks(reg_req(chain(1, seed=9000)), None)
+    live = next(gen)
+    assert live.seq == anchor.seq + 1 and len(live.events) == 1
+    gen.close()
+    cp.stop()
+
+
+def test_warmup_sink_runs_outside_the_lock():
+    """The warm-up sink of a shard join is called after the control-plane lock is released, so a
+    sink that calls back into the service from another thread does not deadlock (reference:
+    lib.rs 'sink delivered outside lock')."""
+    from lake_b200.services.controlplane import ControlPlane
+
+    done = []
+    cp_box = []
+
+    def sink(node, ids):
+        t = threading.Thread(target=lambda: done.append(cp_box[0].GetShardMap(pb.GetShardMapRequest(), None)))
+        t.start()
+        t.join(timeout=5)
+        done.append(("joined", not t.is_alive(), len(ids)))
+
+    cp = ControlPlane(warmup_sink=sink)
+    cp_box.append(cp)
+    cp.RegisterModel(pb.RegisterModelRequest(model=pb.ModelDescriptor(
+        model_id=M, num_layers=2, block_spec=pb.BlockSpec(block_tokens=16, bytes_per_block=1000), hash_algo=1,
+        quota=pb.Quota(soft_bytes=10 ** 9, hard_bytes=2 * 10 ** 9))), None)
+    cp.JoinShardNode(pb.JoinShardNodeRequest(node_id="a", vnode_count=8), None)
+    hs = [h for k in range(24) for h in chain(1, seed=1000 * k)]
+    for h in hs:
+        cp.RegisterBlocks(reg_req([h], node="a"), None)
+    for _ in range(5):
+        cp.ReportHits(pb.ReportHitsRequest(node_id="a", ids=[pb.KVBlockID(model_id=M, block_hash=h, pool_kind=1)
+                                                             for h in hs]), None)
+    r = cp.JoinShardNode(pb.JoinShardNodeRequest(node_id="b", vnode_count=8), None)
+    assert r.ok
+    joined = [d for d in done if isinstance(d, tuple)]
+    assert joined and all(ok for _, ok, _ in joined) and joined[0][2] > 0
+    cp.stop()
