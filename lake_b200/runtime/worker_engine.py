@@ -119,7 +119,7 @@ class WorkerEngine:
         self._stop.set()
         if self._thread is not None:
             self._thread.join(timeout=timeout_s)
-        self._fail_inflight(RuntimeError("worker stopped"))
+        self._fail_inflight(PoolError(PoolErrorCode.DOWNSTREAM, "worker stopped"))
         self.lifecycle.terminate()
 
     @property

@@ -154,3 +154,39 @@ def test_kernel_timeout_maps_to_pool_timeout():
     assert _step_error_code(KernelError(0, 3)) == PoolErrorCode.DOWNSTREAM
     assert _step_error_code(ValueError("x")) == PoolErrorCode.DOWNSTREAM
     assert "peer flag wait timed out" in str(KernelError(1, 2))
+
+
+def test_stop_without_drain_fails_every_orphaned_request():
+    """Stopping mid-flight (no drain) ends every waiting submitter with an error instead of leaving
+    it blocked, and the worker refuses new work (reference: test_lifecycle stop races)."""
+    import time
+
+    eng = tiny_engine()
+    we = WorkerEngine(RoleConfig(device="cpu", model_backend="mock"), engine=eng)
+    we.start()
+    real_step = eng.step
+
+    def slow_step():
+        time.sleep(0.05)
+        return real_step()
+
+    eng.step = slow_step
+    results = [None] * 6
+
+    def run(i):
+        try:
+            results[i] = we.submit(f"s{i}", [(i + j) % 900 for j in range(30)], 200, timeout_s=60)
+        except PoolError as e:
+            results[i] = e
+
+    ts = [threading.Thread(target=run, args=(i,)) for i in range(6)]
+    [t.start() for t in ts]
+    time.sleep(0.3)
+    we.stop(drain=False, timeout_s=30)
+    [t.join(30) for t in ts]
+    assert not any(t.is_alive() for t in ts)
+    assert all(r is not None for r in results)
+    assert any(isinstance(r, PoolError) for r in results)  # 200 tokens at 50 ms/step cannot finish
+    assert we.state == WorkerState.TERMINATE
+    with pytest.raises(PoolError):
+        we.submit("after", [1, 2, 3], 2)
