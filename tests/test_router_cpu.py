@@ -192,3 +192,58 @@ def test_reroute_away_from_unavailable_worker():
             srv.stop(0)
             we.stop(drain=False)
         cp.stop()
+
+
+def test_autoscale_out_in_and_rollback():
+    """Scale-out joins a shard node and widens admission; scale-in drains the newest node and
+    removes it; a drain the control plane rejects is rolled back (the node keeps serving), and a
+    removal it refuses leaves the node draining for the next reap (reference: autoscale_test.go)."""
+    import asyncio
+    import types
+
+    from lake_b200 import _host as H
+    from lake_b200.api import proto
+    from lake_b200.router.server import Router, RouterConfig
+
+    pb = proto.messages()
+
+    class FakeCP:
+        def __init__(self):
+            self.drain_ok, self.remove_ok, self.calls = True, True, []
+
+        async def JoinShardNode(self, req, timeout=None):
+            self.calls.append(("join", req.node_id))
+            return pb.JoinShardNodeResponse(ok=True)
+
+        async def DrainShardNode(self, req, timeout=None):
+            self.calls.append(("drain", req.node_id))
+            return pb.DrainShardNodeResponse(ok=self.drain_ok, err="" if self.drain_ok else "busy")
+
+        async def RemoveShardNode(self, req, timeout=None):
+            self.calls.append(("remove", req.node_id))
+            return types.SimpleNamespace(ok=self.remove_ok)
+
+    fake = FakeCP()
+
+    class R(Router):
+        cp = property(lambda self: fake)
+
+    r = R(RouterConfig(workers={"w0": "127.0.0.1:1"}))
+
+    async def run():
+        await r.apply_scale(H.ScaleDecision.SCALE_OUT)
+        assert r.nodes.count() == 2
+        new = r.nodes.ready_ids()[-1]
+        fake.drain_ok = False
+        with pytest.raises(RuntimeError):
+            await r.apply_scale(H.ScaleDecision.SCALE_IN)
+        assert r.nodes.count() == 2 and not r.nodes.draining()  # rolled back
+        fake.drain_ok, fake.remove_ok = True, False
+        await r.apply_scale(H.ScaleDecision.SCALE_IN)
+        assert r.nodes.draining() == [new]  # removal refused: still draining
+        fake.remove_ok = True
+        await r._reap_draining()
+        assert r.nodes.count() == 1 and new not in r.nodes.ready_ids()
+
+    asyncio.run(run())
+    assert [c[0] for c in fake.calls] == ["join", "drain", "drain", "remove", "remove"]
