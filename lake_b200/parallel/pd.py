@@ -39,7 +39,7 @@ from .peer import export_tensor, import_tensor
 GRANT, DONE, MARK, EXIT = 1, 2, 3, 4
 # leader -> follower commands inside a TP instance
 G_STEP, G_PHASE, G_EXIT, G_EVENTS = 11, 12, 13, 14
-EV_SUBMIT, EV_ADOPT, EV_GRANT = 21, 22, 23
+EV_SUBMIT, EV_ADOPT, EV_GRANT, EV_DIRECT = 21, 22, 23, 24
 
 
 class GroupCtl:
@@ -136,8 +136,13 @@ class DecodeSide:
     """Decode instance's side of PD-split. It may be fed by several prefill instances
     (many-to-one): each grant goes to the partner with the fewest requests outstanding."""
 
-    def __init__(self, eng: LLMEngine, links: list[tuple[ShmRing, ShmRing]], ctl: GroupCtl | None = None):
+    def __init__(self, eng: LLMEngine, links: list[tuple[ShmRing, ShmRing]], ctl: GroupCtl | None = None,
+                 direct_min_hit: float = 0.5):
         self.eng = eng
+        # D-direct: a prompt whose prefix this instance already holds (a session's next turn) is
+        # prefilled here instead of on a prefill instance, when its cached share is at least this
+        self.direct_min_hit = direct_min_hit
+        self.direct = 0
         self.links = links  # (to_p, from_p) per prefill partner (the leader's; empty on followers)
         self.ctl = ctl
         self.pending: dict[int, tuple] = {}
@@ -153,7 +158,25 @@ class DecodeSide:
     def is_follower(self) -> bool:
         return self.ctl is not None and not self.ctl.is_leader
 
+    def local_hit(self, prompt: list[int]) -> int:
+        """Prompt tokens this instance's prefix cache holds (whole blocks, last token excluded)."""
+        from ..engine.block_pool import chain_block_hashes
+
+        bs = self.eng.ec.block_size
+        hashes = chain_block_hashes(prompt, bs, full_only=True)[:(len(prompt) - 1) // bs]
+        return self.eng.pool.peek(hashes) * bs
+
     def submit(self, prompt: list[int], max_new_tokens: int) -> bool:
+        if (self.direct_min_hit > 0 and len(prompt) > 1
+                and self.local_hit(prompt) >= self.direct_min_hit * len(prompt)):
+            # D-direct (reference mode selection: local hit -> D_DIRECT): extend the cached prefix here
+            rid = f"dd-{self.next_idx}"
+            if self.ctl is not None:
+                self.events.append((EV_DIRECT, self.next_idx, max_new_tokens, 0, list(prompt), []))
+            self.next_idx += 1
+            self.eng.add_request(list(prompt), max_new_tokens, rid=rid)
+            self.direct += 1
+            return True
         blocks = self.eng.reserve_blocks(len(prompt))
         if self.ctl is not None:
             self.events.append((EV_SUBMIT, self.next_idx if blocks is not None else -1, max_new_tokens, 0,
@@ -228,6 +251,9 @@ class DecodeSide:
                 elif ev == EV_ADOPT:
                     prompt, blocks, max_new, arrival, _ = self.pending.pop(idx)
                     self.eng.adopt_prefilled(f"pd-{idx}", prompt, a, blocks, max_new, arrival=arrival)
+                elif ev == EV_DIRECT:
+                    self.next_idx = idx + 1
+                    self.eng.add_request(l1, a, rid=f"dd-{idx}")
             if kind == G_EVENTS:
                 continue
             outs = self.eng.step()

@@ -181,3 +181,71 @@ def test_pd_tensor_parallel_instances_replay_leader(tmp_path):
     assert r[3]["outs"] == want
     assert r[0]["prefill_steps"] == r[1]["prefill_steps"] > 0
     assert r[2]["kv"] > 0
+
+
+def _worker_direct(rank, port, out_dir):
+    """A session's second turn extends a prefix the decode instance already holds: it is
+    prefilled there (D-direct) instead of on the prefill instance, with the same tokens."""
+    import time
+
+    import torch.distributed as dist
+
+    from lake_b200.engine.llm_engine import LLMEngine
+    from lake_b200.parallel import pd
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    role = "prefill" if rank == 0 else "decode"
+    eng = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512,
+                    num_blocks=96, shared_arena=(role == "decode"))
+    side = pd.connect_pair(eng, role, rank, 1 - rank, None, job=f"d{port}", shm_path=eng.arena_path)
+    if role == "prefill":
+        pd.serve_prefill(side)
+        res = {"prefills": side.first_tokens}
+    else:
+        import random
+
+        rng = random.Random(9)
+        turn1 = [rng.randrange(1024) for _ in range(70)]
+
+        def run_until_idle():
+            t0 = time.perf_counter()
+            while side.inflight:
+                side.poll()
+                if eng.has_unfinished():
+                    eng.step()
+                else:
+                    time.sleep(0.001)
+                assert time.perf_counter() - t0 < 60
+
+        assert side.submit(turn1, 6)
+        run_until_idle()
+        out1 = eng.requests["pd-0"].output
+        turn2 = turn1 + out1 + [rng.randrange(1024) for _ in range(20)]
+        assert side.local_hit(turn2) >= 64
+        assert side.submit(turn2, 6)
+        run_until_idle()
+        out2 = eng.requests["dd-1"].output
+        ref = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512, num_blocks=96)
+        want = ref.generate([turn1, turn2], max_new_tokens=6)
+        res = {"outs": [out1, out2], "want": want, "direct": side.direct}
+        side.shutdown()
+    with open(os.path.join(out_dir, f"d{rank}.json"), "w") as f:
+        json.dump(res, f)
+    dist.barrier()
+    dist.destroy_process_group()
+    side.close()
+    if eng.arena_path:
+        from lake_b200.parallel.peer import unlink_shared
+
+        unlink_shared(eng.arena_path)
+
+
+def test_pd_decode_direct_for_a_cached_prefix(tmp_path):
+    port = _free_port()
+    mp.spawn(_worker_direct, args=(port, str(tmp_path)), nprocs=2, join=True)
+    d = json.load(open(tmp_path / "d1.json"))
+    p = json.load(open(tmp_path / "d0.json"))
+    assert d["outs"] == d["want"]
+    assert d["direct"] == 1 and p["prefills"] == 1  # only the first turn went to the prefill instance
