@@ -7,8 +7,8 @@
 // work of the single-SM 128 x 256 form. The even CTA of the pair issues the
 // MMAs into both CTAs' tensor memory (each holds 128 accumulator rows).
 //
-//   warp 0     : TMA producer of this CTA's halves (no multicast; the pair's
-//                loads complete on the even CTA's full barrier)
+//   warp 0     : TMA producer of this CTA's own halves (each CTA loads only what it
+//                stages; the pair's loads complete on the even CTA's full barrier)
 //   warp 1     : TMEM allocation (both CTAs); MMA issue + commits (even CTA)
 //   warps 2..5 : epilogue of this CTA's 128 rows (store / residual / SwiGLU / fp32 /
 //                tensor-parallel reduce-scatter push to the row owner's buffer / QKV with
