@@ -60,6 +60,9 @@ class EngineConfig:
     # chunk per request. Steps with drafts run synchronously (no overlap).
     spec_tokens: int = 0
     spec_ngram: int = 3
+    # Checkpoint: a safetensors file or directory (HF names). A model given as a directory with
+    # config.json and safetensors shards loads both; otherwise weights are random-init.
+    weights: str | None = None
 
 
 @dataclass
@@ -99,6 +102,12 @@ class LLMEngine:
         maxb = (ec.max_model_len + ec.block_size - 1) // ec.block_size
         max_tokens = ec.max_batched_tokens + ec.max_running
         self.tp_world = 1
+        weights = ec.weights
+        if weights is None and isinstance(model, str) and not isinstance(model, ModelConfig):
+            from ..models.checkpoint import has_checkpoint
+
+            weights = model if has_checkpoint(model) else None
+        init = "zeros" if weights else "random"
         if ec.tp is not None and ec.tp[1] > 1:
             from ..models.llama_tp import TPDecoderLM
             from ..parallel.tp import TPGroup
@@ -108,7 +117,11 @@ class LLMEngine:
             max_tokens += world  # rows padded to a multiple of the group size
             self.tp_group = TPGroup(rank, world, self.device, max_tokens, cfg.hidden,
                                     ec.max_running * (1 + ec.spec_tokens), group=pg, status=None)
-            self.model = TPDecoderLM(cfg, self.tp_group, self.device, seed=ec.seed, weight_dtype=ec.weight_dtype)
+            full = None
+            if weights:  # the whole checkpoint on the host, then this rank's shard
+                full = DecoderLM(cfg, "cpu", torch.bfloat16, init="zeros", weights=weights).w
+            self.model = TPDecoderLM(cfg, self.tp_group, self.device, seed=ec.seed, weight_dtype=ec.weight_dtype,
+                                     full_weights=full)
             cfg = self._arena_cfg = _local_kv_cfg(cfg, world)
         elif ec.ep is not None and ec.ep[1] > 1:
             from ..parallel.ep import EPGroup
@@ -116,10 +129,11 @@ class LLMEngine:
             rank, world, pg = ec.ep
             self.ep_group = EPGroup(rank, world, self.device, max_tokens, cfg.hidden, cfg.n_experts, cfg.top_k,
                                     group=pg)
-            self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed, ep=self.ep_group)
+            self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed, ep=self.ep_group, init=init,
+                                   weights=weights)
             self._arena_cfg = cfg
         else:
-            self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed)
+            self.model = DecoderLM(cfg, self.device, dtype, seed=ec.seed, init=init, weights=weights)
             self._arena_cfg = cfg
             if ec.weight_dtype == "fp8" and self.device.type == "cuda":
                 self.model.quantize_fp8()

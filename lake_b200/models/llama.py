@@ -81,14 +81,18 @@ class Workspace:
 
 class DecoderLM:
     def __init__(self, cfg: ModelConfig, device: torch.device | str = "cpu", dtype: torch.dtype | None = None,
-                 seed: int = 0, init: str = "random", ep=None):
+                 seed: int = 0, init: str = "random", ep=None, weights: str | None = None):
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype or (torch.float32 if self.device.type == "cpu" else torch.bfloat16)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.w: dict[str, torch.Tensor] = {}
-        if init == "random":
-            self._random_init(seed)
+        if init in ("random", "zeros"):  # zeros: allocate only (a checkpoint overwrites every tensor)
+            self._random_init(seed, zeros=init == "zeros")
+        if weights:
+            from .checkpoint import load_checkpoint
+
+            load_checkpoint(self, weights)  # before the MoE set-up re-lays out the expert weights
         self.rope_cs = ref.rope_cache(cfg.max_position, cfg.rope_theta, cfg.head_dim, cfg.rope_scaling,
                                       device=self.device)
         self.layer_ready = None  # per-layer CUDA events while weights stream in (runtime.coldstart)
@@ -102,6 +106,8 @@ class DecoderLM:
     def _param(self, name, shape, gen, std=0.02, ones=False):
         if ones:
             t = torch.ones(shape, dtype=self.dtype, device=self.device)
+        elif getattr(self, "_zeros", False):
+            t = torch.zeros(shape, dtype=self.dtype, device=self.device)
         else:
             t = torch.empty(shape, dtype=torch.float32, device=self.device)
             t.normal_(0.0, std, generator=gen)
@@ -109,7 +115,8 @@ class DecoderLM:
         self.w[name] = t
         return t
 
-    def _random_init(self, seed: int) -> None:
+    def _random_init(self, seed: int, zeros: bool = False) -> None:
+        self._zeros = zeros
         c = self.cfg
         gen = torch.Generator(device=self.device).manual_seed(seed)
         h, d = c.hidden, c.head_dim
@@ -146,6 +153,9 @@ class DecoderLM:
         for name, t in named.items():
             n = name.replace("model.", "").replace(".self_attn.", ".").replace(".mlp.", ".")
             n = n.replace(".weight", "")
+            if c.n_experts and self._load_expert(n, t):  # Mixtral block_sparse_moe naming
+                done.append(n)
+                continue
             for part in ("q_proj", "k_proj", "v_proj", "gate_proj", "up_proj"):
                 if n.endswith(part):
                     staged.setdefault(n[: -len(part)], {})[part] = t
@@ -167,6 +177,27 @@ class DecoderLM:
                 self.w[prefix + "gate_up_proj"].copy_(w.to(self.dtype))
                 done.append(prefix + "gate_up_proj")
         return done
+
+    def _load_expert(self, n: str, t: torch.Tensor) -> bool:
+        """layers.L.block_sparse_moe.gate -> router; experts.E.w1 / w3 / w2 -> rows of the packed
+        [gate; up] and down tensors of expert E (the MoE set-up interleaves them afterwards)."""
+        import re
+
+        m = re.fullmatch(r"layers\.(\d+)\.block_sparse_moe\.gate", n)
+        if m:
+            self.w[f"layers.{m.group(1)}.router"].copy_(t.to(self.dtype))
+            return True
+        m = re.fullmatch(r"layers\.(\d+)\.block_sparse_moe\.experts\.(\d+)\.(w1|w2|w3)", n)
+        if not m:
+            return False
+        i, e, which = m.group(1), int(m.group(2)), m.group(3)
+        I = self.cfg.intermediate
+        if which == "w2":
+            self.w[f"layers.{i}.experts.down_proj"][e].copy_(t.to(self.dtype))
+        else:
+            rows = slice(0, I) if which == "w1" else slice(I, 2 * I)
+            self.w[f"layers.{i}.experts.gate_up_proj"][e, rows].copy_(t.to(self.dtype))
+        return True
 
     def quantize_fp8(self) -> None:
         """Replace the dense projection weights by block-scaled e4m3 (W8A16 GEMMs); norms,
