@@ -18,12 +18,15 @@ import time
 
 from aiohttp import web
 
-from .server import MAX_BODY, Router, RouterConfig, RouterError, detokenize_mock, tokenize_mock
+from .server import MAX_BODY, Router, RouterConfig, RouterError
+from .tokenizer import Tokenizer
 
 LOG = logging.getLogger("lake_b200.router")
 
 
-def make_app(router: Router) -> web.Application:
+def make_app(router: Router, tokenizer: Tokenizer | None = None) -> web.Application:
+    tokenizer = tokenizer or Tokenizer.from_env()
+
     async def healthz(_req):
         return web.Response(text="ok")
 
@@ -45,12 +48,10 @@ def make_app(router: Router) -> web.Application:
                 raise ValueError
         except ValueError:
             return web.Response(status=400, text="invalid JSON request")
-        if isinstance(data.get("prompt_token_ids"), list):
-            tokens = [int(t) for t in data["prompt_token_ids"]]
-        else:
-            text = "\n".join(m.get("content", "") for m in data.get("messages", []) or []
-                             if isinstance(m, dict) and m.get("role") in ("user", "system"))
-            tokens = tokenize_mock(text)
+        try:
+            tokens = tokenizer.encode_request(data)
+        except Exception as e:  # a message the chat template cannot render
+            return web.Response(status=400, text=f"cannot tokenize request: {e}")
         max_new = int(data.get("max_tokens") or 0) or 4
         model = data.get("model") or "mock-llm"
         session = req.headers.get("X-Lake-Session-Id", "").encode()
@@ -61,7 +62,7 @@ def make_app(router: Router) -> web.Application:
         return web.json_response({
             "id": "chatcmpl-" + out["request_id"][:8], "object": "chat.completion", "created": int(time.time()),
             "model": model,
-            "choices": [{"index": 0, "message": {"role": "assistant", "content": detokenize_mock(out["output_tokens"])},
+            "choices": [{"index": 0, "message": {"role": "assistant", "content": tokenizer.decode(out["output_tokens"])},
                          "finish_reason": "stop"}],
             "lake": {"reused_blocks": out["reused_blocks"], "prefill_blocks": out["prefill_blocks"],
                      "mode": out["mode"], "node": out["node"]},

@@ -247,3 +247,29 @@ def test_autoscale_out_in_and_rollback():
 
     asyncio.run(run())
     assert [c[0] for c in fake.calls] == ["join", "drain", "drain", "remove", "remove"]
+
+
+def test_tokenizer_mock_default_and_local_hf_tokenizer(tmp_path):
+    """Without LAKE_TOKENIZER the router keeps the mock ids; with a locally saved Hugging Face
+    tokenizer it encodes the messages and decodes the output to text (no network)."""
+    from tokenizers import Tokenizer as TK
+    from tokenizers import models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    from lake_b200.router.server import tokenize_mock
+    from lake_b200.router.tokenizer import Tokenizer
+
+    mock = Tokenizer(None)
+    req = {"messages": [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hello lake"},
+                        {"role": "assistant", "content": "ignored"}]}
+    assert mock.is_mock and mock.encode_request(req) == tokenize_mock("be brief\nhello lake")
+    assert mock.encode_request({"prompt_token_ids": [5, 6]}) == [5, 6]
+
+    vocab = {"[UNK]": 0, "hello": 1, "lake": 2, "be": 3, "brief": 4}
+    tk = TK(models.WordLevel(vocab, unk_token="[UNK]"))
+    tk.pre_tokenizer = pre_tokenizers.Whitespace()
+    PreTrainedTokenizerFast(tokenizer_object=tk, unk_token="[UNK]").save_pretrained(str(tmp_path))
+    real = Tokenizer(str(tmp_path))
+    assert not real.is_mock
+    assert real.encode_request(req) == [3, 4, 1, 2]
+    assert real.decode([1, 2]) == "hello lake"
