@@ -74,7 +74,7 @@ class RoleConfig:
     max_model_length: int = 8192
     pull_budget_ms: int = 0
     allow_partial_hit: bool = False
-    model_backend: str = "llama3-8b"  # a preset name, a config.json path, or "mock"
+    model_backend: str = "llama3-8b"  # a preset name, a config.json path, a checkpoint directory, or "mock"
     model_path: str = ""
     served_model_name: str = "model"
     model_revision: str = ""
