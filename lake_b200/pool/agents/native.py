@@ -38,10 +38,20 @@ from ..types import FinishRequest, PoolError, PoolErrorCode, PreparePlan, Prefix
 L0, L1, L2 = 1, 2, 3
 
 
+def make_pool_node(model_id: str, page_bytes: int, l0_blocks: int, l1_blocks: int = 64, l2_blocks: int = 256,
+                   storage_dir: str | None = None, pinned: bool = False):
+    """A KV pool node (tier engine + its L1 slab) for NativeAgent(shared_tiers=...)."""
+    root = storage_dir or tempfile.mkdtemp(prefix="lakeb_pool_")
+    l1 = torch.zeros(l1_blocks * page_bytes, dtype=torch.uint8, pin_memory=pinned)
+    tiers = H.TierEngine(H.TierCaps(l0_blocks, l1_blocks, l2_blocks), page_bytes, l1.data_ptr(),
+                         os.path.join(root, "l2"), os.path.join(root, "l3"), model_id)
+    return tiers, l1
+
+
 class NativeAgent:
     def __init__(self, engine, node_id: str = "node-0", model_id: str | None = None, revision: str = "",
                  authority: "H.Authority | None" = None, port=None, l1_blocks: int = 64, l2_blocks: int = 256,
-                 storage_dir: str | None = None, writeback: str = "all"):
+                 storage_dir: str | None = None, writeback: str = "all", shared_tiers=None):
         self.eng = engine
         self.node_id = node_id
         self.model_id = model_id or engine.cfg.name
@@ -53,12 +63,17 @@ class NativeAgent:
         if authority is None or not self.authority.has_namespace(self.model_id, revision):
             self.authority.register_model(H.ModelDescriptor(self.model_id, revision, engine.cfg.n_layers, self.bs,
                                                             self.page_bytes))
-        root = storage_dir or tempfile.mkdtemp(prefix="lakeb_tiers_")
         pin = engine.arena.is_cuda
-        self.l1 = torch.zeros(l1_blocks * self.page_bytes, dtype=torch.uint8, pin_memory=pin)
-        self.tiers = H.TierEngine(H.TierCaps(engine.pool.num_blocks, l1_blocks, l2_blocks), self.page_bytes,
-                                  self.l1.data_ptr(), os.path.join(root, "l2"), os.path.join(root, "l3"),
-                                  self.model_id)
+        if shared_tiers is not None:
+            # a pool node several engines use (its L1 slab and tier engine): what one engine wrote
+            # back, another promotes
+            self.tiers, self.l1 = shared_tiers
+        else:
+            root = storage_dir or tempfile.mkdtemp(prefix="lakeb_tiers_")
+            self.l1 = torch.zeros(l1_blocks * self.page_bytes, dtype=torch.uint8, pin_memory=pin)
+            self.tiers = H.TierEngine(H.TierCaps(engine.pool.num_blocks, l1_blocks, l2_blocks), self.page_bytes,
+                                      self.l1.data_ptr(), os.path.join(root, "l2"), os.path.join(root, "l3"),
+                                      self.model_id)
         self.stream = torch.cuda.Stream(engine.arena.device) if engine.arena.is_cuda else None
         self.writeback = writeback
         self._ready_step: int | None = None

@@ -249,3 +249,16 @@ def test_pd_decode_direct_for_a_cached_prefix(tmp_path):
     p = json.load(open(tmp_path / "d0.json"))
     assert d["outs"] == d["want"]
     assert d["direct"] == 1 and p["prefills"] == 1  # only the first turn went to the prefill instance
+
+
+def test_cpu_plumbing_prefill_pool_decode():
+    """The CPU plumbing configuration: a prefill worker writes every prompt's pages to the KV pool
+    (radix/location authority + tier storage), a separate decode worker promotes them at admission
+    and decodes 16 greedy steps; its logits equal a colocated run's to 1e-5."""
+    from lake_b200.bench.cpu_plumbing import run
+
+    r = run()
+    assert r["pool_written_blocks"] == 8 + 8 * 2  # the shared 128-token prefix is stored once
+    assert r["pool_prefix_hit_blocks"] == [10] * 8
+    assert r["promoted_blocks"] > 0 and r["tokens_equal"]
+    assert r["compared_positions"] == 8 * 16 and r["logits_match_1e-5"]
