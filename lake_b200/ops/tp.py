@@ -4,8 +4,6 @@ reduce-scatter, and the reduce + residual + RMSNorm + all-gather kernel.
 The ``tp`` dicts come from lake_b200.parallel.tp.TPGroup."""
 from __future__ import annotations
 
-import torch
-
 from ._ext import native
 from .core import LAUNCHES, status_word
 from .fp8 import unpack

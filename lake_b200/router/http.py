@@ -10,7 +10,6 @@ Reference parity: go/router/server.go:193-421.
 """
 from __future__ import annotations
 
-import asyncio
 import json
 import logging
 import os

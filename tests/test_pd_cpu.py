@@ -7,7 +7,6 @@ import os
 import random
 import socket
 
-import pytest
 import torch.multiprocessing as mp
 
 
