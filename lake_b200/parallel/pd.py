@@ -166,7 +166,9 @@ class DecodeSide:
         hashes = chain_block_hashes(prompt, bs, full_only=True)[:(len(prompt) - 1) // bs]
         return self.eng.pool.peek(hashes) * bs
 
-    def submit(self, prompt: list[int], max_new_tokens: int) -> bool:
+    def submit(self, prompt: list[int], max_new_tokens: int) -> str | None:
+        """Start a request: returns the engine request id it will run under ("pd-N" once its
+        prefill instance reports back, "dd-N" when prefilled here), or None if no pages are free."""
         if (self.direct_min_hit > 0 and len(prompt) > 1
                 and self.local_hit(prompt) >= self.direct_min_hit * len(prompt)):
             # D-direct (reference mode selection: local hit -> D_DIRECT): extend the cached prefix here
@@ -176,13 +178,13 @@ class DecodeSide:
             self.next_idx += 1
             self.eng.add_request(list(prompt), max_new_tokens, rid=rid)
             self.direct += 1
-            return True
+            return rid
         blocks = self.eng.reserve_blocks(len(prompt))
         if self.ctl is not None:
             self.events.append((EV_SUBMIT, self.next_idx if blocks is not None else -1, max_new_tokens, 0,
                                 list(prompt), blocks or []))
         if blocks is None:
-            return False
+            return None
         idx = self.next_idx
         self.next_idx += 1
         li = min(range(len(self.links)), key=lambda i: self.outstanding[i])
@@ -194,7 +196,7 @@ class DecodeSide:
         msg[4 + len(blocks)] = len(prompt)
         msg[5 + len(blocks):] = prompt
         self.links[li][0].put_wait(msg)
-        return True
+        return f"pd-{idx}"
 
     def poll(self) -> int:
         n = 0

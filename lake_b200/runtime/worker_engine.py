@@ -24,7 +24,7 @@ import threading
 import time
 from dataclasses import dataclass, field
 
-from ..engine.request import RequestStatus
+from ..engine.request import PENDING, RequestStatus
 from ..pool.types import PoolError, PoolErrorCode, PrefixHint
 from .config import CapacitySignal, ExecMode, RoleConfig, WorkerLifecycle, WorkerState, select_exec_mode
 
@@ -61,7 +61,7 @@ class _Inbound:
     result: GenerateResult | None = None
 
 
-def build_engine(cfg: RoleConfig):
+def build_engine(cfg: RoleConfig, **kw):
     from ..engine.llm_engine import LLMEngine
 
     model = cfg.model_backend
@@ -74,7 +74,9 @@ def build_engine(cfg: RoleConfig):
                      max_batched_tokens=cfg.max_num_scheduled_tokens,
                      long_prefill_threshold=cfg.long_prefill_token_threshold,
                      max_model_len=cfg.max_model_length or 8192, num_blocks=cfg.num_blocks,
-                     use_cuda_graphs=device != "cpu", overlap=cfg.enable_overlap)
+                     use_cuda_graphs=device != "cpu",
+                     **{"overlap": cfg.enable_overlap,
+                        "spec_tokens": cfg.num_draft_tokens if cfg.enable_drafter else 0, **kw})
 
 
 class WorkerEngine:
@@ -91,6 +93,10 @@ class WorkerEngine:
         self._failed: Exception | None = None
         self.steps = 0
         self.on_finished = None  # optional callback(request) after a request completes
+        # PD-split: a decode worker's link to its prefill instance(s) (parallel.pd.DecodeSide);
+        # PD_DISAGG requests are granted pages here and prefilled there
+        self.pd_side = None
+        self._engine_rid: dict[str, str] = {}  # request id -> the engine's id for it
 
     # ------------------------------------------------------------ lifecycle
     def start(self, timeout_s: float = 600.0) -> None:
@@ -168,18 +174,36 @@ class WorkerEngine:
                 return
             first = False
             try:
-                self.engine.add_request(job.prompt, max_new_tokens=job.max_new_tokens, rid=job.rid)
+                if job.mode == ExecMode.PD_DISAGG and self.pd_side is not None:
+                    local = self.pd_side.submit(job.prompt, job.max_new_tokens)
+                    if local is None:
+                        job.result = GenerateResult(job.rid, error=PoolError(
+                            PoolErrorCode.CAPACITY, "no free KV pages for a prefill grant"))
+                        job.event.set()
+                        continue
+                    if local.startswith("dd-"):  # the prefix is held here: prefilled locally
+                        job.mode = ExecMode.D_DIRECT
+                    self._engine_rid[job.rid] = local
+                else:
+                    self.engine.add_request(job.prompt, max_new_tokens=job.max_new_tokens, rid=job.rid)
                 self._inflight[job.rid] = job
             except Exception as e:  # invalid request: fail just this one
                 job.result = GenerateResult(job.rid, error=PoolError(PoolErrorCode.INVALID_ARG, str(e)))
                 job.event.set()
 
+    def _busy(self) -> bool:
+        return self.engine.has_unfinished() or bool(self.pd_side is not None and self.pd_side.pending)
+
     def _loop(self) -> None:
         eng = self.engine
         while not self._stop.is_set():
             try:
-                self._drain_inbound(block=not eng.has_unfinished())
+                self._drain_inbound(block=not self._busy())
+                if self.pd_side is not None:
+                    self.pd_side.poll()  # prefilled requests join the decode batch
                 if not eng.has_unfinished():
+                    if self._busy():
+                        time.sleep(0.0005)  # waiting on a prefill instance
                     continue
                 eng.step()
                 self.steps += 1
@@ -196,10 +220,13 @@ class WorkerEngine:
     def _complete_finished(self) -> None:
         bs = self.engine.ec.block_size
         for rid in list(self._inflight):
-            req = self.engine.requests.get(rid)
+            req = self.engine.requests.get(self._engine_rid.get(rid, rid))
             if req is None or req.status not in (RequestStatus.FINISHED, RequestStatus.ABORTED):
                 continue
+            if req.output and req.output[-1] == PENDING:
+                continue  # overlapped steps: its last token is still being sampled
             job = self._inflight.pop(rid)
+            self._engine_rid.pop(rid, None)
             prefill_tokens = len(req.prompt) - req.num_cached
             job.result = GenerateResult(rid, list(req.output), req.num_cached // bs, (prefill_tokens + bs - 1) // bs,
                                         job.mode.value)

@@ -60,8 +60,9 @@ def test_select_exec_mode():
     assert not full_local_hit(PrefixHint(computed_tokens=32, local_hit=True), 64)
 
 
-def test_worker_engine_concurrent_submit():
-    eng = tiny_engine()
+@pytest.mark.parametrize("overlap", [False, True])  # overlapped steps resolve the last token one step later
+def test_worker_engine_concurrent_submit(overlap):
+    eng = tiny_engine(overlap=overlap)
     ref = tiny_engine()
     prompts = [[(7 * i + j) % 1000 for j in range(20 + i)] for i in range(6)]
     want = ref.generate(prompts, max_new_tokens=5)
@@ -190,3 +191,55 @@ def test_stop_without_drain_fails_every_orphaned_request():
     assert we.state == WorkerState.TERMINATE
     with pytest.raises(PoolError):
         we.submit("after", [1, 2, 3], 2)
+
+
+def test_pd_pair_serves_pd_disagg_requests(tmp_path):
+    """The PD serving pair (prefill process + decode worker with WorkerService): a PD_DISAGG
+    request is prefilled by the prefill process into the decode worker's arena and decoded there;
+    the tokens equal a colocated engine's, and a COLOCATED request runs on the decode worker."""
+    import os
+    import signal
+    import socket
+    import subprocess
+    import sys
+    import time
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    env = dict(os.environ, LAKE_MODEL_BACKEND="mock", LAKE_DEVICE="cpu", LAKE_MAX_RUNNING_REQS="8",
+               LAKE_LOG="WARNING")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    proc = subprocess.Popen([sys.executable, "-m", "lake_b200.runtime.pd_pair", "--bind", f"127.0.0.1:{port}"],
+                            cwd=root, env=env, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
+    pb = proto.messages()
+    try:
+        ch = grpc.insecure_channel(f"127.0.0.1:{port}")
+        grpc.channel_ready_future(ch).result(timeout=120)
+        stub = proto.Stub(ch, "WorkerService")
+        prompt = [(5 * j + 3) % 1000 for j in range(50)]
+        t0 = time.time()
+        while True:  # the worker answers once it has warmed up
+            try:
+                resp = stub.Generate(pb.GenerateRequest(request_id="pd1", prompt_tokens=prompt, max_new_tokens=6,
+                                                        exec_mode="PD_DISAGG"), timeout=60)
+                break
+            except grpc.RpcError:
+                if time.time() - t0 > 120:
+                    raise
+                time.sleep(0.5)
+        want = tiny_engine().generate([prompt], max_new_tokens=6)[0]
+        assert resp.mode == "PD_DISAGG" and list(resp.output_tokens) == want
+        other = [(7 * j + 1) % 1000 for j in range(40)]
+        r2 = stub.Generate(pb.GenerateRequest(request_id="c1", prompt_tokens=other, max_new_tokens=4,
+                                              exec_mode="COLOCATED"), timeout=60)
+        assert r2.mode == "COLOCATED" and list(r2.output_tokens) == tiny_engine().generate([other], 4)[0]
+        ch.close()
+    finally:
+        proc.send_signal(signal.SIGTERM)
+        try:
+            out, _ = proc.communicate(timeout=60)
+        except subprocess.TimeoutExpired:
+            proc.kill()
+            out, _ = proc.communicate()
+    assert proc.returncode == 0, out[-2000:]
