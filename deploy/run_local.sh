@@ -4,6 +4,7 @@
 # one worker and the HTTP router. Run from the repository root:
 #   ./deploy/run_local.sh            # LAKE_MODEL_BACKEND=mock -> tiny CPU model
 #   LAKE_MODEL_BACKEND=llama3-8b LAKE_DEVICE=cuda ./deploy/run_local.sh
+#   LAKE_PD_PAIR=1 ./deploy/run_local.sh   # the worker as a PD-split pair (prefill + decode process)
 #   ./deploy/smoke.sh                # in another shell
 set -euo pipefail
 ROOT="$(cd "$(dirname "$0")/.." && pwd)"
@@ -54,8 +55,13 @@ wait_tcp "$LAKE_CP_ADDR" controlplane
 echo "==> node services"
 "$PY" -m lake_b200.services.node & PIDS+=($!)
 wait_tcp "$LAKE_AGENT_ADDR" node-services
-echo "==> worker ($LAKE_MODEL_BACKEND)"
-"$PY" -m lake_b200.runtime & PIDS+=($!)
+if [[ "${LAKE_PD_PAIR:-0}" == "1" ]]; then
+  echo "==> PD worker pair ($LAKE_MODEL_BACKEND)"
+  "$PY" -m lake_b200.runtime.pd_pair --bind "$LAKE_WORKER_BIND" & PIDS+=($!)
+else
+  echo "==> worker ($LAKE_MODEL_BACKEND)"
+  "$PY" -m lake_b200.runtime & PIDS+=($!)
+fi
 wait_tcp "$LAKE_WORKER_ADDR" worker 1200
 echo "==> router"
 "$PY" -m lake_b200.router & PIDS+=($!)
