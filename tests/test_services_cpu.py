@@ -333,3 +333,19 @@ def test_warmup_sink_runs_outside_the_lock():
     joined = [d for d in done if isinstance(d, tuple)]
     assert joined and all(ok for _, ok, _ in joined) and joined[0][2] > 0
     cp.stop()
+
+
+def test_standalone_kvpool_service_roundtrip():
+    from lake_b200.services import kvpool
+
+    server, port = kvpool.serve("127.0.0.1:0", max_workers=2)
+    ch = grpc.insecure_channel(f"127.0.0.1:{port}")
+    try:
+        tcp = proto.Stub(ch, "TcpDataService")
+        assert tcp.PutBlocks(pb.PutBlocksRequest(node_id="n0", blocks=[pb.OpaqueBlock(id=kid(b"k0"), data=b"xyz")]),
+                             timeout=10).ok
+        g = tcp.GetBlocks(pb.GetBlocksRequest(ids=[kid(b"k0"), kid(b"missing")]), timeout=10)
+        assert [b.data for b in g.blocks] == [b"xyz"]
+    finally:
+        ch.close()
+        server.stop(0)
