@@ -1,7 +1,7 @@
 #!/usr/bin/env bash
 # Start the whole stack locally in the foreground (Ctrl-C stops everything):
-# control plane, node storage services (agent + transfer + kv byte store),
-# one worker and the HTTP router. Run from the repository root:
+# control plane, the kv-pool byte service, node storage services (agent + transfer +
+# kv byte store), one worker and the HTTP router. Run from the repository root:
 #   ./deploy/run_local.sh            # LAKE_MODEL_BACKEND=mock -> tiny CPU model
 #   LAKE_MODEL_BACKEND=llama3-8b LAKE_DEVICE=cuda ./deploy/run_local.sh
 #   LAKE_PD_PAIR=1 ./deploy/run_local.sh   # the worker as a PD-split pair (prefill + decode process)
@@ -11,6 +11,7 @@ ROOT="$(cd "$(dirname "$0")/.." && pwd)"
 cd "$ROOT"
 
 export LAKE_CP_ADDR="${LAKE_CP_ADDR:-127.0.0.1:50051}"
+export LAKE_KV_ADDR="${LAKE_KV_ADDR:-127.0.0.1:50052}"
 export LAKE_WORKER_BIND="${LAKE_WORKER_BIND:-127.0.0.1:50053}"
 export LAKE_WORKER_ADDR="${LAKE_WORKER_ADDR:-127.0.0.1:50053}"
 export LAKE_AGENT_ADDR="${LAKE_AGENT_ADDR:-127.0.0.1:50054}"
@@ -40,7 +41,7 @@ cleanup() {
 }
 trap cleanup EXIT INT TERM
 
-for hp in "$LAKE_CP_ADDR" "$LAKE_WORKER_ADDR" "$LAKE_AGENT_ADDR" "$LAKE_HTTP_ADDR"; do
+for hp in "$LAKE_CP_ADDR" "$LAKE_KV_ADDR" "$LAKE_WORKER_ADDR" "$LAKE_AGENT_ADDR" "$LAKE_HTTP_ADDR"; do
   if (echo >/dev/tcp/"${hp%:*}"/"${hp##*:}") >/dev/null 2>&1; then
     echo "ERROR: $hp already in use; stop the old stack first" >&2
     exit 1
@@ -52,6 +53,9 @@ done
 echo "==> control plane"
 "$PY" -m lake_b200.services.controlplane & PIDS+=($!)
 wait_tcp "$LAKE_CP_ADDR" controlplane
+echo "==> kv-pool"
+"$PY" -m lake_b200.services.kvpool & PIDS+=($!)
+wait_tcp "$LAKE_KV_ADDR" kv-pool
 echo "==> node services"
 "$PY" -m lake_b200.services.node & PIDS+=($!)
 wait_tcp "$LAKE_AGENT_ADDR" node-services

@@ -32,7 +32,7 @@ def serve(bind: str, max_workers: int = 16, capacity_bytes: int = 0):
 
 def main() -> None:
     logging.basicConfig(level=os.environ.get("LAKE_LOG", "INFO"))
-    bind = os.environ.get("LAKE_KV_BIND", os.environ.get("LAKE_KV_ADDR", "0.0.0.0:50052"))
+    bind = os.environ.get("LAKE_KV_ADDR", "0.0.0.0:50052")
     cap = int(os.environ.get("LAKE_KV_CAPACITY_BYTES", "0") or 0)
     server, port = serve(bind, capacity_bytes=cap)
     LOG.info("kv-pool byte service on port %d", port)
