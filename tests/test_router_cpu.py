@@ -273,3 +273,60 @@ def test_tokenizer_mock_default_and_local_hf_tokenizer(tmp_path):
     assert not real.is_mock
     assert real.encode_request(req) == [3, 4, 1, 2]
     assert real.decode([1, 2]) == "hello lake"
+
+
+def _local_hit_rate(policy: str, n_nodes: int, sessions: int = 7, rounds: int = 6, seed: int = 76):
+    """Multi-turn sessions routed by `policy` ("session", "anchor" or "rr") over n_nodes; each
+    served request stores its blocks on the node it ran on, and the router's mirror catches up at
+    the end of every round. Returns (local-hit blocks / reusable blocks, reusable, local)."""
+    import numpy as np
+
+    from lake_b200 import _host as H
+
+    rng = np.random.default_rng(seed)
+    names = [f"w{i}" for i in range(n_nodes)]
+    nodes = H.NodeRegistry(names)
+    auth = H.Authority()
+    auth.register_model(H.ModelDescriptor("m", "", 2, 16, 100))
+    mirror = H.ViewMirror()
+    mirror.apply(auth.snapshot())
+    convo = [rng.integers(0, 32000, 64).tolist() for _ in range(sessions)]
+    reusable = local = turn = 0
+    for _ in range(rounds):
+        for s in range(sessions):
+            convo[s] += rng.integers(0, 32000, 40).tolist()  # the user's next turn
+            hs = H.chain_block_hashes(convo[s], 16, True)
+            if policy == "rr":
+                node = names[turn % n_nodes]
+            else:  # the router's own choice: session header, else the prefix anchor
+                key = f"session-{s}".encode() if policy == "session" else H.prefix_anchor(hs)
+                node = H.pick_node(nodes, mirror, "m", hs, key, 8)
+            turn += 1
+            blocks = mirror.prefix_lookup("m", "", 1, hs, node)
+            reusable += len(blocks)
+            k = 0
+            while k < len(blocks) and blocks[k].local_hit:
+                k += 1
+            local += k
+            have = auth.lookup_prefix("m", "", 1, hs, node).hit_length
+            for x in hs[:have]:
+                auth.publish_location(H.KVBlockID("m", x), 1, node)
+            if have < len(hs):
+                auth.register_blocks(node, hs, [H.BlockMeta(H.KVBlockID("m", x), [H.Location(1, node)])
+                                                for x in hs[have:]])
+            convo[s] += rng.integers(0, 32000, 24).tolist()  # the answer
+        assert mirror.apply(auth.commit_pending()) == 0
+    return (local / reusable if reusable else 0.0), reusable, local
+
+
+@pytest.mark.parametrize("n_nodes", [2, 4])
+def test_local_hit_rate_gate_affinity_vs_round_robin(n_nodes):
+    """Regression gate on routing metadata (no timing): with prefix affinity the repeated
+    sessions' reusable blocks are local at least 40% of the time, and more often than under
+    round robin (the reference's go/router/bench_p76_test.go:389 gate, slo.md's >40% target)."""
+    rr, reusable, _ = _local_hit_rate("rr", n_nodes)
+    assert reusable > 0
+    for policy in ("session", "anchor"):
+        rate, reusable_p, local_p = _local_hit_rate(policy, n_nodes)
+        assert reusable_p == reusable and local_p <= reusable_p
+        assert rate >= 0.4 and rate > rr, (policy, rate, rr)
