@@ -232,3 +232,44 @@ def test_speculative_decoding_matches_greedy():
     a, _, _ = _spec_run(0, eos=eos)
     b, s, _ = _spec_run(4, eos=eos)
     assert a == b and s == b
+
+
+def test_runner_packs_mixed_batch_metadata():
+    """Host packing of one mixed step (decode rows first, then a prefill chunk): token ids,
+    positions, KV slots from the block tables, query starts, prefill tiles, sample rows and the
+    graph-bucket padding rows (the role of the reference's engine/tests/test_input_batch.py)."""
+    from lake_b200 import ops
+
+    eng = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=512, max_model_len=512, num_blocks=64)
+    a = eng.add_request(list(range(1, 21)), max_new_tokens=4)
+    b = eng.add_request(list(range(30, 63)), max_new_tokens=4)
+    eng.step()  # both prompts prefilled: a and b decode next
+    c = eng.add_request(list(range(100, 100 + 150)), max_new_tokens=2)
+    out = eng.scheduler.schedule()
+    assert [ch.req.rid for ch in out.chunks] == [a, b, c] and len(out.decode) == 2
+    r = eng.runner
+    t, s, ntiles, nrows, nd = r._pack(out, pad_decode_to=4)
+    assert (s, nd, nrows) == (5, 4, 5) and t == 2 + 2 + 150
+    ids, pos = r._v(r.np_i32, "ids"), r._v(r.np_i32, "pos")
+    lens, qst = r._v(r.np_i32, "lens"), r._v(r.np_i32, "qstart")
+    tiles = r._v(r.np_i32, "tiles", shape=(r.max_tiles, 4))
+    bt = r._v(r.np_i32, "bt", shape=(r.max_seqs, r.maxb))
+    slots, rows = r.np_i64[:t], r.np_i64[r.max_tokens:r.max_tokens + nrows]
+    reqs = eng.requests
+    for row, rid in enumerate([a, b]):  # decode rows: the last sampled token at its position
+        req = reqs[rid]
+        p = len(req.prompt) + len(req.output) - 1
+        assert ids[row] == req.output[-1] and pos[row] == p and lens[row] == p + 1
+        assert slots[row] == req.block_ids[p // 16] * 16 + p % 16
+        assert list(bt[row, :len(req.block_ids)]) == list(req.block_ids)
+    # two padding rows: zero-length sequences that write no KV and are sampled but ignored
+    assert list(slots[2:4]) == [-1, -1] and list(lens[2:4]) == [0, 0]
+    # the prefill chunk of c: rows 4.., one sample row (its last), tiles of PREFILL_TILE rows
+    rc = reqs[c]
+    assert list(qst[:6]) == [0, 1, 2, 3, 4, 154] and lens[4] == 150
+    assert list(ids[4:154]) == list(range(100, 250)) and list(pos[4:154]) == list(range(150))
+    want_slots = [rc.block_ids[p // 16] * 16 + p % 16 for p in range(150)]
+    assert list(slots[4:154]) == want_slots
+    k = ops.core.PREFILL_TILE
+    assert ntiles == 2 and [list(x) for x in tiles[:2]] == [[4, 4, k, 0], [4, 4 + k, 150 - k, k]]
+    assert list(rows) == [0, 1, 2, 3, 153]
