@@ -17,10 +17,16 @@ HDR = 8  # head, tail, ... (int64 slots)
 
 
 def _untrack(shm) -> None:
-    """An attaching process must not unlink the segment at exit (its resource tracker would)."""
+    """An attaching process must not unlink the segment at exit (its own resource tracker
+    would). A process spawned by the creator shares the creator's tracker instead (it inherited
+    the tracker's pipe and did not start one: `_fd` set, `_pid` unset); unregistering there would
+    drop the creator's entry, and the creator's unlink would then fail inside the tracker."""
     try:
         from multiprocessing import resource_tracker
 
+        rt = resource_tracker._resource_tracker
+        if getattr(rt, "_fd", None) is not None and getattr(rt, "_pid", None) is None:
+            return
         resource_tracker.unregister(shm._name, "shared_memory")
     except Exception:  # pragma: no cover - tracker layout differs across Python versions
         pass

@@ -51,6 +51,7 @@ def _worker(rank, port, out_dir):
         with open(os.path.join(out_dir, "res.json"), "w") as f:
             json.dump({"outs": outs, "want": want, "kv_bytes": side.kv_bytes}, f)
     dist.barrier()
+    side.close()  # every rank is done with the rings: the creator unlinks them
     dist.destroy_process_group()
     if eng.arena_path:
         from lake_b200.parallel.peer import unlink_shared
@@ -98,6 +99,7 @@ def _worker_m2o(rank, port, out_dir):
         with open(os.path.join(out_dir, "m2o.json"), "w") as f:
             json.dump({"outs": outs, "want": want}, f)
     dist.barrier()
+    side.close()  # every rank is done with the rings: the creator unlinks them
     dist.destroy_process_group()
     if eng.arena_path:
         from lake_b200.parallel.peer import unlink_shared
