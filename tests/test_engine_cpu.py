@@ -273,3 +273,31 @@ def test_runner_packs_mixed_batch_metadata():
     k = ops.core.PREFILL_TILE
     assert ntiles == 2 and [list(x) for x in tiles[:2]] == [[4, 4, k, 0], [4, 4 + k, 150 - k, k]]
     assert list(rows) == [0, 1, 2, 3, 153]
+
+
+def test_overlap_timeline_launches_next_step_before_collecting():
+    """Launch/collect order with overlapped scheduling (the reference's
+    runtime/tests/test_node_scheduler_mock.py:92-134 timeline check): step n+1 is launched
+    before step n is collected, every launched step is collected exactly once, in order."""
+    eng = LLMEngine("tiny", device="cpu", max_running=4, max_batched_tokens=64, max_model_len=256, num_blocks=64,
+                    overlap=True)
+    timeline, handles = [], []  # handles stay referenced so their ids are never reused
+    launch, collect = eng.runner.launch, eng.runner.collect
+
+    def rec_launch(out, bitmask=None):
+        h = launch(out, bitmask)
+        handles.append(h)
+        timeline.append(("launch", id(h)))
+        return h
+
+    def rec_collect(h):
+        timeline.append(("collect", id(h)))
+        return collect(h)
+
+    eng.runner.launch, eng.runner.collect = rec_launch, rec_collect
+    eng.generate([[3, 4, 5] * 10, [7] * 12], max_new_tokens=6)
+    launches = [h for k, h in timeline if k == "launch"]
+    collects = [h for k, h in timeline if k == "collect"]
+    assert launches == collects and len(launches) >= 6  # each step collected once, in launch order
+    for i in range(len(launches) - 1):  # collect(n) only after launch(n + 1)
+        assert timeline.index(("collect", launches[i])) > timeline.index(("launch", launches[i + 1]))
