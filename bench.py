@@ -13,13 +13,14 @@ has already produced j*256/running tokens, its prompt covers them), and the
 closed-loop source submits a fresh 2048/256 request whenever one finishes, so
 the timed steps run the steady state of the serving loop.
 
-`value` = output tokens / summed device time of the K steps (CUDA events around
-each step's kernels, max over the ranks that produce output tokens: colocated
-ranks, or the decode ranks of PD-split, whose prefill partners run concurrently
-and report their own busy time in `ranks`); `e2e.value` = the same tokens / wall
-time of the K public-API `LLMEngine.step()` calls, which include scheduling, the
-pinned host->device copy of each step's metadata and the device->host read of
-the sampled tokens.
+`value` = output tokens / device time of the window, the MAX over every rank of
+its summed per-step device time (CUDA events around each step's kernels): the
+colocated ranks, or under PD-split both the decode ranks (K steps) and the
+prefill ranks (every prefill step they ran inside the same window, which can
+overrun it by up to one prefill step); `e2e.value` = the same tokens / the max
+over ranks of the wall time of the window's public-API `LLMEngine.step()` calls,
+which include scheduling, the pinned host->device copy of each step's metadata
+and the device->host read of the sampled tokens.
 
 PD-split (the default from 2 GPUs): one prefill and one decode instance of N/2
 GPUs each (2 GPUs: 1 + 1; 4: TP2 + TP2; 8: TP4 + TP4, the tensor-parallel
@@ -588,13 +589,10 @@ def main():
         w = run_colocated(args, rank, local, barrier, tp, ep)
     ck = clocks.stop() if rank == 0 else {}
 
-    # aggregate over ranks (max of times, sum of counts) through the gloo group
-    # The output tokens come from the decode (or colocated) ranks, so the window is theirs: summed
-    # step device time and wall time of their K steps. Prefill ranks of PD-split run concurrently;
-    # their busy time is reported per rank but does not stretch the window (their last step
-    # overruns the decode window by up to one prefill step).
-    producer = role != "prefill"
-    t = torch.tensor([w.dev_ms if producer else 0.0, w.wall_s * 1000.0 if producer else 0.0, float(w.tokens),
+    # aggregate over ranks (max of times, sum of counts) through the gloo group. The window's
+    # device time is the busiest rank's: decode (or colocated) ranks' K steps, or a prefill rank's
+    # summed step time over the same window (PD-split), whichever is larger.
+    t = torch.tensor([w.dev_ms, w.wall_s * 1000.0, float(w.tokens),
                       w.h2d, w.d2h, float(w.launches), float(w.kv_bytes), w.dev_ms], dtype=torch.float64)
     lat = (w.ttft, w.tpot, w.diag(args.steps))
     if world > 1:
@@ -612,6 +610,10 @@ def main():
         ranks = [lat[2]]
     # device time of the window: the busiest rank (decode steps, or a prefill rank's busy time)
     dev_ms = mx[0].item()
+    producer_ms = {}
+    if world > 1:
+        for l in lats:
+            producer_ms[l[2]["role"]] = max(producer_ms.get(l[2]["role"], 0.0), l[2]["dev_ms"])
     wall_ms = mx[1].item()
     tokens = sm[2].item()
     value = tokens / (dev_ms / 1000.0)
@@ -647,7 +649,7 @@ def main():
             "ttft_p50_ms": round(p50(ttft) * 1000, 2) if ttft else None,
             "tpot_p50_ms": round(p50(tpot) * 1000, 2) if tpot else None,
             "p2d_kv_gbs": round(kv_gbs, 2) if kv_gbs else None,
-            "clocks": ck, "impl": "lakeb", "ranks": ranks,
+            "clocks": ck, "impl": "lakeb", "busiest_ms_by_role": producer_ms or None, "ranks": ranks,
         }
         print(json.dumps(line))
         from lake_b200.utils.trace import emit

@@ -465,12 +465,7 @@ int paged_decode(const PagedAttnArgs& a, cudaStream_t stream) {
   if (a.splits > 1 && (!a.ws_o || !a.ws_ml)) return -2;
   CUtensorMap map;
   if (!arena_map(&map, a)) return -3;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  if (int e = ensure_smem_attr(reinterpret_cast<const void*>(paged_decode_kernel), kSmemBytes)) return e;
   dim3 grid(a.splits, a.n_kv_heads, a.num_seqs);
   paged_decode_kernel<<<grid, 128, kSmemBytes, stream>>>(map, a);
   if (a.splits > 1) decode_combine_kernel<<<dim3(a.n_q_heads, a.num_seqs), kHeadDim, 0, stream>>>(a);
@@ -481,12 +476,7 @@ int paged_decode_with_map(const PagedAttnArgs& a, const CUtensorMap& map, cudaSt
   if (a.num_seqs <= 0) return 0;
   if (a.n_kv_heads <= 0 || a.n_q_heads % a.n_kv_heads || a.n_q_heads / a.n_kv_heads > 16) return -1;
   if (a.splits > 1 && (!a.ws_o || !a.ws_ml)) return -2;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(paged_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  if (int e = ensure_smem_attr(reinterpret_cast<const void*>(paged_decode_kernel), kSmemBytes)) return e;
   dim3 grid(a.splits, a.n_kv_heads, a.num_seqs);
   paged_decode_kernel<<<grid, 128, kSmemBytes, stream>>>(map, a);
   if (a.splits > 1) decode_combine_kernel<<<dim3(a.n_q_heads, a.num_seqs), kHeadDim, 0, stream>>>(a);
@@ -498,13 +488,7 @@ int paged_prefill(const PagedAttnArgs& a, cudaStream_t stream) {
   if (a.n_kv_heads <= 0 || a.n_q_heads % a.n_kv_heads) return -1;
   CUtensorMap map;
   if (!arena_map(&map, a)) return -3;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(paged_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  if (int e = ensure_smem_attr(reinterpret_cast<const void*>(paged_prefill_kernel), kSmemBytes)) return e;
   dim3 grid(a.num_tiles, a.n_q_heads);
   paged_prefill_kernel<<<grid, 128, kSmemBytes, stream>>>(map, a);
   return cudaGetLastError();

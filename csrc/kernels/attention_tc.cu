@@ -360,13 +360,7 @@ int paged_prefill_tc(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream
   if (rows >= (int64_t(1) << 31)) return -3;
   if (!make_bf16_map(&kvmap, a.arena, rows, 128, 128, 16, 64)) return -4;
   if (!make_bf16_map(&qmap, a.q, q_rows, static_cast<int64_t>(a.n_q_heads) * 128, a.q_stride, 128, 64)) return -5;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e =
-        cudaFuncSetAttribute(paged_prefill_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  if (int e = ensure_smem_attr(reinterpret_cast<const void*>(paged_prefill_tc_kernel), kSmemBytes)) return e;
   dim3 grid(a.num_tiles, a.n_q_heads);
   paged_prefill_tc_kernel<<<grid, kThreadsTC, kSmemBytes, stream>>>(kvmap, qmap, a);
   return cudaGetLastError();

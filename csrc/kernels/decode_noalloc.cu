@@ -53,7 +53,12 @@ extern "C" int lakeb_paged_decode_noalloc(const void* q, int64_t q_stride, void*
                                           const int* seq_lens, int num_seqs, float scale, int splits, void* stream) {
   if (num_seqs <= 0) return 0;
   if (!q || !out || !arena || !block_tables || !seq_lens || n_kv_heads <= 0 || n_q_heads % n_kv_heads ||
-      n_q_heads / n_kv_heads > 16 || q_stride % 8 || out_stride % 8 || (reinterpret_cast<uintptr_t>(q) & 15))
+      n_q_heads / n_kv_heads > 16 || q_stride % 8 || out_stride % 8 || (reinterpret_cast<uintptr_t>(q) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(arena) & 15))
+    return LAKEB_NOALLOC_EARG;
+  // A layer outside the arena would still be inside the tensor map (rows of another block), so
+  // nothing would fault and the result would be silently wrong: refuse it here.
+  if (num_blocks <= 0 || num_layers <= 0 || layer < 0 || layer >= num_layers || bt_stride < 1)
     return LAKEB_NOALLOC_EARG;
   if (splits <= 0) splits = lakeb::paged_decode_splits(num_seqs, n_kv_heads, bt_stride);
   const int64_t need = lakeb_paged_decode_noalloc_scratch_bytes(num_seqs, n_q_heads, n_kv_heads, splits);

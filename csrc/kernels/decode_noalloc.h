@@ -27,10 +27,20 @@
 //    process exits. A batch whose split-KV partials need more returns
 //    LAKEB_NOALLOC_ETOO_LARGE and launches nothing.
 //  * The first call on a device looks up the scratch array's device address
-//    (cudaGetSymbolAddress) with that device current. Make that first call
-//    before any stream capture on the device.
-//  * No device memory is allocated or freed, by this code or by any library
-//    it calls.
+//    (cudaGetSymbolAddress) with that device current. With CUDA's lazy module
+//    loading (the default), that first call is also what loads this library's
+//    GPU module on the device, which creates the 8 MiB array (the driver's
+//    memory, not cudaMalloc) and can synchronise the device. Make that first
+//    call before any stream capture on the device, and outside
+//    latency-critical paths; every later call allocates nothing.
+//  * No call allocates or frees device memory through cudaMalloc/cudaFree or
+//    an allocating library routine (torch's included).
+//  * The bounds-checked debug build records index errors in a status word;
+//    this entry point passes none, so those checks are not reported through
+//    it (out-of-range page ids are skipped silently in that build). Argument
+//    errors (layer outside [0, num_layers), num_blocks <= 0, bt_stride < 1,
+//    misaligned pointers or strides) return LAKEB_NOALLOC_EARG before any
+//    launch.
 //  * Every call shares the one scratch array, which keeps the previous call's
 //    contents. The kernels overwrite every partial result they later read, so
 //    nothing has to start at zero. Calls whose kernels overlap on the GPU

@@ -353,12 +353,7 @@ int launch_pair(const GemmArgs& a, cudaStream_t stream) {
   if (!make_bf16_map(&ma, a.A, a.M, a.K, a.lda, kBM2)) return -10;
   if (!make_bf16_map(&mb, a.B, a.N, a.K, a.ldb, kBN2 / 2)) return -11;
   auto kern = gemm_pair_kernel<EPI>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  if (int e = ensure_smem_attr(reinterpret_cast<const void*>(kern), kSmem2)) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gemm_pair_grid(a.M, a.N), 1, 1);
   cfg.blockDim = dim3(kThreads2, 1, 1);

@@ -556,12 +556,7 @@ int launch(const GemmArgs& a, cudaStream_t stream) {
     if (!make_bf16_map(&mb, a.B, brows, a.K, a.ldb, BN)) return -11;
   }
   auto kern = gemm_bf16_kernel<BN, STAGES, EPI, W8>;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kAlloc);
-    if (e != cudaSuccess) return e;
-    attr = true;
-  }
+  if (int e = ensure_smem_attr(reinterpret_cast<const void*>(kern), S::kAlloc)) return e;
   int grid = grid_for(a.M, a.N, BN, a.max_ctas);
   if (a.streamk) grid = a.streamk;  // the dispatcher's stream-K grid
   kern<<<grid, threads_of<W8>(), S::kAlloc, stream>>>(ma, mb, a);

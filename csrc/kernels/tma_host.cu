@@ -4,6 +4,8 @@
 #include <cudaTypedefs.h>
 
 #include <mutex>
+#include <set>
+#include <tuple>
 #include <unordered_map>
 
 #include "tma_host.h"
@@ -128,6 +130,21 @@ int num_sms() {
   if (dev < 0 || dev >= 64) dev = 0;
   if (!cached[dev]) cudaDeviceGetAttribute(&cached[dev], cudaDevAttrMultiProcessorCount, dev);
   return cached[dev];
+}
+
+int ensure_smem_attr(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::set<std::tuple<const void*, int, int>> done;  // (kernel, device, bytes)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const auto key = std::make_tuple(kernel, dev, bytes);
+  std::lock_guard<std::mutex> g(mu);
+  if (done.count(key)) return 0;
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return e;
+  done.insert(key);
+  return 0;
 }
 
 }  // namespace lakeb

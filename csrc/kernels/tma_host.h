@@ -20,4 +20,10 @@ bool make_u8_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, 
                  int box_cols);
 int num_sms();
 
+// Raises a kernel's dynamic shared-memory limit to `bytes` on the CURRENT device.
+// cudaFuncSetAttribute is per device, so the call is remembered per (kernel, device):
+// a process that launches on several GPUs sets it once on each of them. Thread-safe.
+// Returns 0 or the cudaError_t of the failed call.
+int ensure_smem_attr(const void* kernel, int bytes);
+
 }  // namespace lakeb
