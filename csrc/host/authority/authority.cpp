@@ -61,34 +61,89 @@ uint8_t FrequencySketch::estimate(uint64_t key) const {
 }
 
 // ------------------------------------------------------------------ inactive index
-bool InactiveIndex::insert(uint64_t lin) {
-  if (order_.count(lin) || order_.size() >= cap_) return false;
-  order_[lin] = tick_++;
+bool InactiveIndex::has(uint64_t lin) const {
+  auto it = slots_.find(lin);
+  return it != slots_.end() && !it->second.spilled;
+}
+
+void InactiveIndex::admit(uint64_t lin, Slot& s) {
+  if (indexed_ >= cap_) {
+    s.spilled = true;
+    spill_at_[lin] = spill_.insert(spill_.end(), lin);
+    return;
+  }
+  s.spilled = false;
+  s.tick = tick_++;
+  ++indexed_;
+  if (s.leaf) leaves_.emplace(s.tick, lin);
+}
+
+void InactiveIndex::release(uint64_t lin, bool leaf) {
+  if (slots_.count(lin)) return;  // already zero-ref
+  Slot& s = slots_[lin];
+  s.leaf = leaf;
+  admit(lin, s);
+}
+
+bool InactiveIndex::retain(uint64_t lin) {
+  auto it = slots_.find(lin);
+  if (it == slots_.end()) return false;
+  Slot s = it->second;
+  slots_.erase(it);
+  if (s.spilled) {
+    auto at = spill_at_.find(lin);
+    spill_.erase(at->second);
+    spill_at_.erase(at);
+    return true;
+  }
+  if (s.leaf) leaves_.erase(s.tick);
+  --indexed_;
+  refill();
   return true;
 }
-bool InactiveIndex::take(uint64_t lin) { return order_.erase(lin) != 0; }
-std::vector<uint64_t> InactiveIndex::allocate(size_t n, const std::function<bool(uint64_t)>& is_leaf,
-                                              const std::function<uint8_t(uint64_t)>& freq) {
-  std::vector<uint64_t> out;
-  while (out.size() < n && !order_.empty()) {
-    // candidates: leaves; order by (frequency bucket, insertion tick)
-    uint64_t best = 0;
-    std::pair<uint8_t, uint64_t> best_key{255, ~0ull};
-    bool found = false;
-    for (auto& [lin, tick] : order_) {
-      if (!is_leaf(lin)) continue;
-      std::pair<uint8_t, uint64_t> k{bucket_of(freq(lin)), tick};
-      if (!found || k < best_key) {
-        best_key = k;
-        best = lin;
-        found = true;
-      }
-    }
-    if (!found) break;
-    order_.erase(best);
-    out.push_back(best);
+
+void InactiveIndex::set_leaf(uint64_t lin, bool leaf) {
+  auto it = slots_.find(lin);
+  if (it == slots_.end() || it->second.leaf == leaf) return;
+  Slot& s = it->second;
+  s.leaf = leaf;
+  if (s.spilled) return;
+  if (leaf)
+    leaves_.emplace(s.tick, lin);
+  else
+    leaves_.erase(s.tick);
+}
+
+void InactiveIndex::refill() {
+  while (indexed_ < cap_ && !spill_.empty()) {
+    uint64_t lin = spill_.front();
+    spill_.pop_front();
+    spill_at_.erase(lin);
+    admit(lin, slots_[lin]);
   }
-  return out;
+}
+
+size_t InactiveIndex::evict(size_t n, const std::function<uint8_t(uint64_t)>& freq,
+                            const std::function<void(uint64_t)>& drop) {
+  size_t taken = 0;
+  while (taken < n && !leaves_.empty()) {
+    // rank this pass's leaves: coldest bucket first, oldest release first inside a bucket
+    std::vector<uint64_t> ranked[4];
+    for (auto& [tick, lin] : leaves_) ranked[bucket_of(freq(lin))].push_back(lin);
+    for (auto& tier : ranked)
+      for (uint64_t lin : tier) {
+        if (taken == n) break;
+        auto it = slots_.find(lin);
+        if (it == slots_.end() || it->second.spilled || !it->second.leaf) continue;  // changed by a drop
+        leaves_.erase(it->second.tick);
+        slots_.erase(it);
+        --indexed_;
+        drop(lin);
+        ++taken;
+      }
+    refill();
+  }
+  return taken;
 }
 
 // ------------------------------------------------------------------ authority basics
@@ -211,189 +266,165 @@ std::vector<ModelDescriptor> Authority::models() const {
   return out;
 }
 
-// ------------------------------------------------------------------ quota admission
-int64_t Authority::free_bytes() const {
-  if (pool_capacity_bytes_ <= 0) return INT64_MAX / 4;
+// ------------------------------------------------------------------ admission
+// A namespace's usage has three levels: up to its soft quota the bytes are its own
+// reservation; between soft and hard they are borrowed (only with borrow_enabled, and
+// only while the pool has room); the hard quota is never crossed. Admitting `fresh`
+// blocks first makes room from the namespace's own zero-ref blocks, down to whichever
+// of its two limits is tighter. What still lies above the hard quota is refused as
+// HARD_QUOTA. A borrower that would push the pool past its capacity takes the excess
+// back from namespaces that are themselves above their soft quota (their zero-ref
+// blocks), largest excess first; if they cannot cover it, the admission is refused
+// as POOL_CAPACITY. A refused admission changes nothing.
+int64_t Authority::pool_used_bytes() const {
   int64_t used = 0;
-  for (auto& [k, n] : namespaces_) used += n->used_bytes;
-  return std::max<int64_t>(0, pool_capacity_bytes_ - used);
+  for (auto& kv : namespaces_) used += kv.second->used_bytes;
+  return used;
 }
 
-int64_t Authority::reclaimable_borrowed(const std::string& m, const std::string& r) const {
-  int64_t total = 0;
-  for (auto& [k, n] : namespaces_) {
-    if (k.first == m && k.second == r) continue;
-    int64_t soft = n->desc.quota.soft_bytes;
-    int64_t over = soft > 0 ? std::max<int64_t>(0, n->used_bytes - soft) : 0;
-    if (over <= 0) continue;
-    int64_t inactive = 0;
-    for (auto& [pk, p] : n->pools) inactive += int64_t(p->inactive.size());
-    total += std::min(over, inactive * n->bytes_per_block());
+int64_t Authority::lendable_bytes(const Namespace& n) const {
+  const int64_t soft = n.desc.quota.soft_bytes;
+  if (soft <= 0 || n.used_bytes <= soft) return 0;
+  size_t zero_ref = 0;
+  for (auto& kv : n.pools) zero_ref += kv.second->inactive.evictable();
+  return std::min<int64_t>(n.used_bytes - soft, int64_t(zero_ref) * n.bytes_per_block());
+}
+
+int64_t Authority::take_from_lenders(const Namespace* borrower, int64_t bytes) {
+  std::vector<std::pair<int64_t, Namespace*>> lenders;  // (lendable bytes, namespace)
+  for (auto& kv : namespaces_)
+    if (kv.second.get() != borrower)
+      if (int64_t l = lendable_bytes(*kv.second)) lenders.emplace_back(l, kv.second.get());
+  std::stable_sort(lenders.begin(), lenders.end(), [](auto& x, auto& y) { return x.first > y.first; });
+  int64_t got = 0;
+  for (auto& [lendable, n] : lenders) {
+    if (got >= bytes) break;
+    const int64_t unit = n->bytes_per_block();
+    const int64_t ask = std::min(lendable, bytes - got);
+    got += int64_t(evict_ns(n, size_t((ask + unit - 1) / unit))) * unit;
   }
-  return total;
+  return got;
 }
 
-void Authority::reclaim_borrowed(const std::string& m, const std::string& r, int64_t want) {
-  int64_t freed = 0;
-  for (auto& [k, n] : namespaces_) {
-    if (freed >= want) break;
-    if (k.first == m && k.second == r) continue;
-    int64_t soft = n->desc.quota.soft_bytes;
-    int64_t over = soft > 0 ? std::max<int64_t>(0, n->used_bytes - soft) : 0;
-    if (over <= 0) continue;
-    int64_t bpb = n->bytes_per_block();
-    int64_t target = std::min(want - freed, over);
-    size_t blocks = size_t(std::max<int64_t>(1, (target + bpb - 1) / bpb));
-    auto removed = evict_ns(n.get(), blocks, k.first, k.second);
-    freed += int64_t(removed.size()) * bpb;
-  }
-}
-
-Authority::AdmitPlan Authority::plan_admit(const std::string& m, const std::string& r, size_t new_blocks) const {
+Authority::AdmitPlan Authority::plan_admit(const Namespace& n, size_t fresh_blocks) const {
   AdmitPlan plan;
-  if (new_blocks == 0) return plan;
-  const Namespace* n = ns(m, r);
-  if (!n) fail("admit: unknown namespace (" + m + ")");
-  const Quota& q = n->desc.quota;
-  int64_t bpb = n->bytes_per_block();
-  int64_t used = n->used_bytes;
-  int64_t delta = int64_t(new_blocks) * bpb;
-  size_t inactive_n = 0;
-  for (auto& [pk, p] : n->pools) inactive_n += p->inactive.size();
-  int64_t inactive_bytes = int64_t(inactive_n) * bpb;
-  auto reject = [&](int64_t used_b, int64_t deficit, const char* reason) {
+  if (!fresh_blocks) return plan;
+  constexpr int64_t kUnbounded = INT64_MAX / 4;
+  const Quota& q = n.desc.quota;
+  const int64_t unit = n.bytes_per_block();
+  const int64_t incoming = int64_t(fresh_blocks) * unit;
+  const int64_t hard = q.hard_bytes > 0 ? q.hard_bytes : kUnbounded;
+  const int64_t soft = q.soft_bytes > 0 ? q.soft_bytes : kUnbounded;
+  auto refuse = [&](int64_t used, int64_t short_by, const char* why) {
     plan.accept = false;
-    plan.bp = BackpressureSignal{m, r, used_b, q.soft_bytes, q.hard_bytes, deficit, reason};
+    plan.bp = BackpressureSignal{n.desc.model_id, n.desc.revision, used, q.soft_bytes, q.hard_bytes, short_by, why};
     return plan;
   };
-  if (q.hard_bytes > 0 && used + delta > q.hard_bytes) {
-    int64_t need = used + delta - q.hard_bytes;
-    if (inactive_bytes < need) return reject(used, need - inactive_bytes, "HARD_QUOTA");
-  }
-  size_t own = 0;
-  if (q.hard_bytes > 0 && used + delta > q.hard_bytes)
-    own = std::max(own, size_t((used + delta - q.hard_bytes + bpb - 1) / bpb));
-  if (q.soft_bytes > 0 && used + delta > q.soft_bytes)
-    own = std::max(own, size_t((used + delta - q.soft_bytes + bpb - 1) / bpb));
-  own = std::min(own, inactive_n);
-  int64_t sim_used = used - int64_t(own) * bpb;
-  int64_t reclaim = 0;
-  if (q.borrow_enabled && q.soft_bytes > 0) {
-    int64_t projected = sim_used + delta;
-    if (projected > q.soft_bytes) {
-      int64_t need_borrow = projected - q.soft_bytes;
-      int64_t fr = free_bytes();
-      if (pool_capacity_bytes_ > 0) fr = std::max<int64_t>(0, fr + int64_t(own) * bpb);
-      if (fr < need_borrow) {
-        int64_t want = need_borrow - fr;
-        int64_t avail = reclaimable_borrowed(m, r);
-        if (avail < want && pool_capacity_bytes_ > 0 && (q.hard_bytes == 0 || projected <= q.hard_bytes))
-          return reject(projected, want - avail, "POOL_CAPACITY");
-        reclaim = std::min(want, avail);
-      }
+
+  size_t own_zero_ref = 0;
+  for (auto& kv : n.pools) own_zero_ref += kv.second->inactive.evictable();
+  const int64_t over_limit = n.used_bytes + incoming - std::min(hard, soft);
+  if (over_limit > 0) plan.evict_own = std::min<size_t>(own_zero_ref, size_t((over_limit + unit - 1) / unit));
+  const int64_t freed = int64_t(plan.evict_own) * unit;
+  const int64_t after = n.used_bytes - freed + incoming;
+  if (after > hard) return refuse(n.used_bytes, after - hard, "HARD_QUOTA");
+
+  if (q.borrow_enabled && after > soft && pool_capacity_bytes_ > 0) {
+    const int64_t pool_after = pool_used_bytes() - freed + incoming;
+    const int64_t excess = pool_after - pool_capacity_bytes_;
+    if (excess > 0) {
+      int64_t lendable = 0;
+      for (auto& kv : namespaces_)
+        if (kv.second.get() != &n) lendable += lendable_bytes(*kv.second);
+      if (lendable < excess) return refuse(after, excess - lendable, "POOL_CAPACITY");
+      plan.from_lenders = excess;
     }
   }
-  if (q.hard_bytes > 0 && sim_used + delta > q.hard_bytes)
-    return reject(sim_used, sim_used + delta - q.hard_bytes, "HARD_QUOTA");
-  plan.own_evict = own;
-  plan.reclaim = reclaim;
   return plan;
+}
+
+Authority::RegisterBatch Authority::check_register(const std::vector<std::string>& prefix_hashes,
+                                                   const std::vector<BlockMeta>& metas, bool need_durable) {
+  RegisterBatch b;
+  const KVBlockID& first = metas.front().id;
+  b.pool_kind = resolve_pool_kind(first.pool_kind);
+  if (prefix_hashes.empty()) fail("RegisterBlocks: prefix_hashes required (lineage)");
+  std::unordered_map<std::string, size_t> at;
+  for (size_t i = 0; i < prefix_hashes.size(); ++i) at.emplace(prefix_hashes[i], i);
+  std::set<size_t> covered;
+  for (auto& m : metas) {
+    if (m.id.model_id != first.model_id) fail("RegisterBlocks: mixed model_id " + first.model_id + " vs " + m.id.model_id);
+    if (m.id.revision != first.revision) fail("RegisterBlocks: mixed revision");
+    if (resolve_pool_kind(m.id.pool_kind) != b.pool_kind) fail("RegisterBlocks: mixed pool_kind");
+    auto it = at.find(m.id.block_hash);
+    if (it == at.end()) fail("RegisterBlocks: block hash not in prefix_hashes");
+    b.pos.push_back(it->second);
+    covered.insert(it->second);
+    if (need_durable && m.locations.empty() && !m.l3_present)
+      fail("RegisterBlocks: need L2 location or l3_present (durable first)");
+  }
+  if (*covered.rbegin() - *covered.begin() + 1 != covered.size())
+    fail("RegisterBlocks: blocks must be a contiguous segment of prefix_hashes");
+  b.n = ns(first.model_id, first.revision);
+  if (!b.n) fail("RegisterBlocks: model not registered (" + first.model_id + "); call RegisterModel first");
+  const PoolView* p = pool(b.n, b.pool_kind);
+  for (size_t i : covered)
+    if (!p || !p->by_flat.count(prefix_hashes[i])) ++b.fresh;
+  return b;
 }
 
 RegisterResult Authority::preflight_register(const std::string& model_id, const std::string& revision, int pool_kind,
                                              const std::vector<std::string>& block_hashes) const {
-  int pk = resolve_pool_kind(pool_kind);
+  const int pk = resolve_pool_kind(pool_kind);
   const Namespace* n = ns(model_id, revision);
   if (!n) fail("AdmitRegisterBlocks: model not registered (" + model_id + "); call RegisterModel first");
   const PoolView* p = pool(n, pk);
-  std::unordered_set<std::string> seen;
-  size_t fresh = 0;
-  for (auto& h : block_hashes) {
-    if (!seen.insert(h).second) continue;
-    if (!p || !p->by_flat.count(h)) ++fresh;
-  }
-  AdmitPlan plan = plan_admit(model_id, revision, fresh);
+  std::set<std::string> fresh;
+  for (auto& h : block_hashes)
+    if (!p || !p->by_flat.count(h)) fresh.insert(h);
+  AdmitPlan plan = plan_admit(*n, fresh.size());
   RegisterResult res;
   res.accepted = plan.accept;
   res.backpressure = plan.bp;
   return res;
 }
 
-// ------------------------------------------------------------------ register
 RegisterResult Authority::register_blocks(const std::string& node_id, const std::vector<std::string>& prefix_hashes,
                                           std::vector<BlockMeta> metas) {
   RegisterResult res;
   if (metas.empty()) return res;
-  const std::string model_id = metas.front().id.model_id;
-  const std::string revision = metas.front().id.revision;
-  const int pk = resolve_pool_kind(metas.front().id.pool_kind);
-  if (prefix_hashes.empty()) fail("RegisterBlocks: prefix_hashes required (lineage)");
-  std::unordered_map<std::string, size_t> index_of;
-  for (size_t i = 0; i < prefix_hashes.size(); ++i) index_of.emplace(prefix_hashes[i], i);
-  std::vector<size_t> positions;
-  for (auto& m : metas) {
-    if (m.id.model_id != model_id) fail("RegisterBlocks: mixed model_id " + model_id + " vs " + m.id.model_id);
-    if (m.id.revision != revision) fail("RegisterBlocks: mixed revision");
-    if (resolve_pool_kind(m.id.pool_kind) != pk) fail("RegisterBlocks: mixed pool_kind");
-    auto it = index_of.find(m.id.block_hash);
-    if (it == index_of.end()) fail("RegisterBlocks: block hash not in prefix_hashes");
-    positions.push_back(it->second);
-  }
-  std::sort(positions.begin(), positions.end());
-  positions.erase(std::unique(positions.begin(), positions.end()), positions.end());
-  for (size_t i = 1; i < positions.size(); ++i)
-    if (positions[i] != positions[i - 1] + 1)
-      fail("RegisterBlocks: blocks must be a contiguous segment of prefix_hashes");
-  Namespace* n = ns(model_id, revision);
-  if (!n) fail("RegisterBlocks: model not registered (" + model_id + "); call RegisterModel first");
-  // count new flats
-  PoolView* p = pool(n, pk, true);
-  std::unordered_set<std::string> seen;
-  size_t fresh = 0;
-  for (auto& m : metas)
-    if (seen.insert(m.id.block_hash).second && !p->by_flat.count(m.id.block_hash)) ++fresh;
-  AdmitPlan plan = plan_admit(model_id, revision, fresh);
+  RegisterBatch b = check_register(prefix_hashes, metas, true);
+  AdmitPlan plan = plan_admit(*b.n, b.fresh);
   if (!plan.accept) {
     res.accepted = false;
     res.backpressure = plan.bp;
     return res;
   }
-  // validate durability before any mutation
-  for (auto& m : metas)
-    if (m.locations.empty() && !m.l3_present) fail("RegisterBlocks: need L2 location or l3_present (durable first)");
-  if (plan.own_evict) evict_ns(n, plan.own_evict, model_id, revision);
-  if (plan.reclaim) reclaim_borrowed(model_id, revision, plan.reclaim);
-  p = pool(n, pk, true);
+  if (plan.evict_own) evict_ns(b.n, plan.evict_own);
+  if (plan.from_lenders) take_from_lenders(b.n, plan.from_lenders);
 
-  auto lineage = lineage_from_prefix(prefix_hashes);
-  int64_t bpb = n->bytes_per_block();
-  for (auto& m : metas) {
-    m.id.pool_kind = pk;
+  PoolView* p = pool(b.n, b.pool_kind, true);
+  const auto lineage = lineage_from_prefix(prefix_hashes);
+  for (size_t i = 0; i < metas.size(); ++i) {
+    BlockMeta& m = metas[i];
+    const size_t pos = b.pos[i];
+    m.id.pool_kind = b.pool_kind;
     for (auto& l : m.locations)
       if (l.node_id.empty()) l.node_id = node_id;
-    size_t pos = index_of[m.id.block_hash];
-    uint64_t lin = lineage[pos];
-    auto it = p->by_flat.find(m.id.block_hash);
-    bool is_new = it == p->by_flat.end();
-    Entry e;
-    if (!is_new) {
-      e = it->second;
-    } else {
+    auto [it, inserted] = p->by_flat.try_emplace(m.id.block_hash);
+    Entry& e = it->second;
+    if (inserted) {
       e.block_id = p->next_block_id++;
-      n->used_bytes += bpb;
       e.parent = pos ? lineage[pos - 1] : 0;
-      if (e.parent) {
-        auto pit = p->lin_to_flat.find(e.parent);
-        if (pit != p->lin_to_flat.end()) p->by_flat[pit->second].registered_children++;
-      }
+      b.n->used_bytes += b.n->bytes_per_block();
+      link_child(p, e.parent, +1);
     }
-    e.lineage = lin;
+    e.lineage = lineage[pos];
     e.meta = m;
     e.prefix_chain.assign(prefix_hashes.begin(), prefix_hashes.begin() + pos + 1);
-    p->lin_to_flat[lin] = m.id.block_hash;
-    p->by_flat[m.id.block_hash] = e;
-    p->freq.touch(lin);
-    emit_upsert(is_new ? REGISTERED : MOVED, m);
+    p->lin_to_flat[e.lineage] = m.id.block_hash;
+    p->freq.touch(e.lineage);
+    emit_upsert(inserted ? REGISTERED : MOVED, m);
     orphans_.erase(key_of(m.id));
   }
   return res;
@@ -449,79 +480,91 @@ std::vector<BlockMeta> Authority::locate(const std::vector<KVBlockID>& ids) cons
 }
 
 // ------------------------------------------------------------------ refs
-void Authority::apply_ref(const RefDelta& d, bool track_node) {
-  PoolView* p = nullptr;
-  Entry* e = find(d.id, &p);
-  if (!e) fail("RefDelta: unknown block_hash");
-  int kind = resolve_ref_kind(d.kind);
-  auto& acc = p->refs[e->lineage];
-  int64_t before = acc.total();
-  int64_t after_b = acc.bucket(kind) + d.delta;
-  if (after_b < 0) fail(std::string("RefDelta: ref_count underflow (kind=") + ref_kind_name(kind) + ")");
-  acc.bucket(kind) = after_b;
-  int64_t after = acc.total();
-  if (before > 0 && after == 0) {
-    p->inactive.insert(e->lineage);
-  } else if (before == 0 && after > 0) {
-    p->inactive.take(e->lineage);
-  }
-  if (track_node && !d.node_id.empty() && d.delta != 0) {
-    auto& held = node_refs_[d.node_id];
-    auto bk = key_of(d.id);
-    auto& a = held[bk];
-    a.bucket(kind) += d.delta;
-    if (a.total() <= 0) held.erase(bk);
-  }
+void Authority::settle_refs(PoolView* p, const Entry& e, const RefAccounts& was, bool held_between) {
+  const auto it = p->refs.find(e.lineage);
+  const int64_t now = it == p->refs.end() ? 0 : it->second.total();
+  if ((was.total() > 0 || held_between) && now == 0)
+    p->inactive.release(e.lineage, e.registered_children <= 0);
+  else if (was.total() == 0 && now > 0)
+    p->inactive.retain(e.lineage);
 }
 
+// A batch applies delta by delta to the block ledgers and to the per-node ledgers that
+// let a dead node's references be released later. The first write to each ledger cell
+// saves the cell's old value; a failing delta puts every saved value back, so a batch is
+// all-or-nothing. Zero crossings (block becomes evictable or stops being so) are settled
+// once per block after the whole batch went through.
 void Authority::report_refs(const std::vector<RefDelta>& deltas) {
-  // project the whole batch first: any failure leaves state untouched
-  std::map<std::pair<const PoolView*, uint64_t>, RefAccounts> proj;
-  std::map<std::pair<std::string, BlockKey>, RefAccounts> proj_node;
-  for (size_t i = 0; i < deltas.size(); ++i) {
-    const auto& d = deltas[i];
-    const std::string at = "ReportRef batch[" + std::to_string(i) + "]: ";
-    PoolView* p = nullptr;
-    Entry* e = nullptr;
-    try {
-      e = find(d.id, &p);
-    } catch (const std::exception& ex) {
-      fail(at + ex.what());
+  struct BlockCell {
+    PoolView* p;
+    const Entry* e;
+    RefAccounts was;
+    bool held = false;  // referenced at some point inside the batch
+  };
+  std::vector<BlockCell> blocks;
+  std::map<std::pair<const PoolView*, uint64_t>, size_t> block_at;
+  std::map<std::pair<std::string, BlockKey>, std::pair<bool, RefAccounts>> node_was;  // existed, value
+  auto rollback = [&]() {
+    for (auto& c : blocks) {
+      if (c.was.request == 0 && c.was.writeback == 0)
+        c.p->refs.erase(c.e->lineage);
+      else
+        c.p->refs[c.e->lineage] = c.was;
     }
-    if (!e) fail(at + "unknown block_hash");
-    int kind;
-    try {
-      kind = resolve_ref_kind(d.kind);
-    } catch (const std::exception& ex) {
-      fail(at + ex.what());
-    }
-    std::pair<const PoolView*, uint64_t> key{p, e->lineage};
-    auto it = proj.find(key);
-    if (it == proj.end()) {
-      auto rit = p->refs.find(e->lineage);
-      it = proj.emplace(key, rit == p->refs.end() ? RefAccounts{} : rit->second).first;
-    }
-    int64_t next = it->second.bucket(kind) + d.delta;
-    if (next < 0) fail(at + "ref_count underflow (kind=" + ref_kind_name(kind) + ")");
-    it->second.bucket(kind) = next;
-    if (!d.node_id.empty() && d.delta != 0) {
-      auto nk = std::make_pair(d.node_id, key_of(d.id));
-      auto nit = proj_node.find(nk);
-      if (nit == proj_node.end()) {
-        RefAccounts cur;
-        auto hit = node_refs_.find(d.node_id);
-        if (hit != node_refs_.end()) {
-          auto b = hit->second.find(nk.second);
-          if (b != hit->second.end()) cur = b->second;
-        }
-        nit = proj_node.emplace(nk, cur).first;
+    for (auto& [k, v] : node_was) {
+      if (v.first)
+        node_refs_[k.first][k.second] = v.second;
+      else if (auto h = node_refs_.find(k.first); h != node_refs_.end()) {
+        h->second.erase(k.second);
+        if (h->second.empty()) node_refs_.erase(h);
       }
-      int64_t nn = nit->second.bucket(kind) + d.delta;
-      if (nn < 0) fail(at + "node_ref underflow (kind=" + ref_kind_name(kind) + ")");
-      nit->second.bucket(kind) = nn;
+    }
+  };
+  for (size_t i = 0; i < deltas.size(); ++i) {
+    const RefDelta& d = deltas[i];
+    std::string err;
+    try {
+      PoolView* p = nullptr;
+      const Entry* e = find(d.id, &p);
+      if (!e) throw std::invalid_argument("unknown block_hash");
+      const int kind = resolve_ref_kind(d.kind);
+      auto key = std::make_pair(static_cast<const PoolView*>(p), e->lineage);
+      if (!block_at.count(key)) {
+        auto cur = p->refs.find(e->lineage);
+        block_at[key] = blocks.size();
+        blocks.push_back(BlockCell{p, e, cur == p->refs.end() ? RefAccounts{} : cur->second});
+      }
+      RefAccounts& acc = p->refs[e->lineage];
+      if (acc.get(kind) + d.delta < 0)
+        throw std::invalid_argument(std::string("ref_count underflow (kind=") + ref_kind_name(kind) + ")");
+      if (!d.node_id.empty() && d.delta != 0) {
+        const BlockKey bk = key_of(d.id);
+        auto nk = std::make_pair(d.node_id, bk);
+        auto& held = node_refs_[d.node_id];
+        auto hit = held.find(bk);
+        if (!node_was.count(nk)) node_was[nk] = {hit != held.end(), hit != held.end() ? hit->second : RefAccounts{}};
+        RefAccounts& mine = held[bk];
+        if (mine.get(kind) + d.delta < 0)
+          throw std::invalid_argument(std::string("node_ref underflow (kind=") + ref_kind_name(kind) + ")");
+        mine.bucket(kind) += d.delta;
+        if (mine.total() == 0) held.erase(bk);
+        if (held.empty()) node_refs_.erase(d.node_id);
+      }
+      acc.bucket(kind) += d.delta;
+      if (acc.total() > 0) blocks[block_at[key]].held = true;
+    } catch (const std::exception& ex) {
+      err = "ReportRef batch[" + std::to_string(i) + "]: " + ex.what();
+    }
+    if (!err.empty()) {
+      rollback();
+      fail(err);
     }
   }
-  for (auto& d : deltas) apply_ref(d, true);
+  for (auto& c : blocks) {
+    auto it = c.p->refs.find(c.e->lineage);
+    if (it != c.p->refs.end() && it->second.total() == 0) c.p->refs.erase(it);
+    settle_refs(c.p, *c.e, c.was, c.held);
+  }
 }
 
 std::pair<int64_t, int64_t> Authority::refs_by_kind(const KVBlockID& id) const {
@@ -552,6 +595,12 @@ void Authority::publish_location(const KVBlockID& id, int tier, const std::strin
   auto same = [&](const Location& l) { return l.tier == tier && l.node_id == node_id; };
   locs.erase(std::remove_if(locs.begin(), locs.end(), same), locs.end());
   if (present) locs.push_back(Location{tier, node_id, segment_id, offset});
+  if (tier == L0 && !present) {
+    // the copy a placement plan put there is gone: the node may be planned again
+    PoolView* p = nullptr;
+    find(id, &p);
+    p->placement_marks.erase({id.block_hash, node_id});
+  }
   emit_upsert(MOVED, e->meta);
 }
 
@@ -578,70 +627,61 @@ size_t Authority::block_count(const std::string& m, const std::string& r) const 
 }
 
 // ------------------------------------------------------------------ eviction
+void Authority::link_child(PoolView* p, uint64_t parent, int step) {
+  if (!parent) return;
+  auto f = p->lin_to_flat.find(parent);
+  if (f == p->lin_to_flat.end()) return;
+  auto pe = p->by_flat.find(f->second);
+  if (pe == p->by_flat.end()) return;
+  Entry& par = pe->second;
+  const bool was_leaf = par.registered_children <= 0;
+  par.registered_children = std::max<int64_t>(0, par.registered_children + step);
+  const bool leaf = par.registered_children <= 0;
+  if (leaf != was_leaf) p->inactive.set_leaf(parent, leaf);
+}
+
 void Authority::remove_entry(PoolView* p, const std::string& flat) {
   auto it = p->by_flat.find(flat);
   if (it == p->by_flat.end()) return;
-  const Entry& e = it->second;
-  if (e.parent) {
-    auto pit = p->lin_to_flat.find(e.parent);
-    if (pit != p->lin_to_flat.end()) {
-      auto fit = p->by_flat.find(pit->second);
-      if (fit != p->by_flat.end()) fit->second.registered_children--;
-    }
-  }
-  p->inactive.take(e.lineage);
-  p->refs.erase(e.lineage);
-  p->lin_to_flat.erase(e.lineage);
+  const uint64_t lin = it->second.lineage, parent = it->second.parent;
+  p->inactive.retain(lin);
+  p->refs.erase(lin);
+  p->lin_to_flat.erase(lin);
   p->hit_counts.erase(flat);
-  for (auto m = p->placement_marks.begin(); m != p->placement_marks.end();)
-    m = m->first == flat ? p->placement_marks.erase(m) : std::next(m);
+  p->placement_marks.erase(p->placement_marks.lower_bound({flat, std::string()}),
+                           p->placement_marks.lower_bound({flat + '\0', std::string()}));
   p->by_flat.erase(it);
+  link_child(p, parent, -1);
 }
 
-std::vector<std::string> Authority::drop_victims(PoolView* p, size_t n) {
-  auto is_leaf = [p](uint64_t lin) {
-    auto f = p->lin_to_flat.find(lin);
-    if (f == p->lin_to_flat.end()) return true;
-    return p->by_flat[f->second].registered_children <= 0;
-  };
+size_t Authority::evict_in(Namespace* n, PoolView* p, size_t count) {
   auto freq = [p](uint64_t lin) { return p->freq.estimate(lin); };
-  std::vector<std::string> removed;
-  for (uint64_t lin : p->inactive.allocate(n, is_leaf, freq)) {
-    auto r = p->refs.find(lin);
-    if (r != p->refs.end() && r->second.total() > 0) continue;
+  auto drop = [&](uint64_t lin) {
     auto f = p->lin_to_flat.find(lin);
-    if (f == p->lin_to_flat.end()) continue;
-    std::string flat = f->second;
+    if (f == p->lin_to_flat.end()) return;
+    const std::string flat = f->second;
     emit_invalidated(p->by_flat[flat].meta.id);
     remove_entry(p, flat);
-    removed.push_back(flat);
-  }
-  return removed;
+  };
+  const size_t gone = p->inactive.evict(count, freq, drop);
+  n->used_bytes = std::max<int64_t>(0, n->used_bytes - int64_t(gone) * n->bytes_per_block());
+  return gone;
 }
 
-std::vector<std::pair<int, std::string>> Authority::evict_ns(Namespace* n, size_t count, const std::string&,
-                                                              const std::string&) {
-  std::vector<std::pair<int, std::string>> out;
-  size_t left = count;
-  for (auto& [pk, p] : n->pools) {  // std::map: TARGET before DRAFT
-    if (!left) break;
-    for (auto& f : drop_victims(p.get(), left)) {
-      out.emplace_back(pk, f);
-      --left;
-    }
+size_t Authority::evict_ns(Namespace* n, size_t count) {
+  size_t gone = 0;
+  for (auto& kv : n->pools) {  // TARGET before DRAFT
+    if (gone >= count) break;
+    gone += evict_in(n, kv.second.get(), count - gone);
   }
-  n->used_bytes = std::max<int64_t>(0, n->used_bytes - int64_t(out.size()) * n->bytes_per_block());
-  return out;
+  return gone;
 }
 
 size_t Authority::evict_n(const std::string& m, const std::string& r, int pool_kind, size_t n) {
-  Namespace* ns_ = ns(m, r);
-  if (!ns_) return 0;
-  PoolView* p = pool(ns_, resolve_pool_kind(pool_kind), false);
-  if (!p) return 0;
-  auto removed = drop_victims(p, n);
-  ns_->used_bytes = std::max<int64_t>(0, ns_->used_bytes - int64_t(removed.size()) * ns_->bytes_per_block());
-  return removed.size();
+  Namespace* space = ns(m, r);
+  if (!space) return 0;
+  PoolView* p = pool(space, resolve_pool_kind(pool_kind), false);
+  return p ? evict_in(space, p, n) : 0;
 }
 
 // ------------------------------------------------------------------ view log
@@ -724,7 +764,7 @@ std::vector<KVBlockID> Authority::discard_blocks(const std::vector<KVBlockID>& i
     if (!e) continue;
     auto r = p->refs.find(e->lineage);
     if (r != p->refs.end() && r->second.total() > 0)
-      fail("DiscardBlocks: block still referenced (refs=" + std::to_string(r->second.total()) + ")");
+      fail("DiscardBlocks: block still referenced (global_refs=" + std::to_string(r->second.total()) + ")");
     emit_invalidated(e->meta.id);
     remove_entry(p, id.block_hash);
     n->used_bytes = std::max<int64_t>(0, n->used_bytes - n->bytes_per_block());
@@ -749,6 +789,8 @@ std::vector<KVBlockID> Authority::sweep_orphans(uint64_t ttl_ms) {
   return out;
 }
 
+// Cold GC: the coldest zero-ref leaves lose their L0/L1 copies. A block with a durable
+// copy (L2 or L3) stays registered and evictable; any other block leaves the view.
 std::pair<std::vector<KVBlockID>, std::vector<KVBlockID>> Authority::gc_cold(const std::string& m,
                                                                              const std::string& r, int pool_kind,
                                                                              size_t count) {
@@ -758,73 +800,71 @@ std::pair<std::vector<KVBlockID>, std::vector<KVBlockID>> Authority::gc_cold(con
   if (!n) fail("gc_cold: unknown namespace (" + m + ")");
   PoolView* p = pool(n, resolve_pool_kind(pool_kind), false);
   if (!p) return {discarded, stripped};
-  auto is_leaf = [p](uint64_t lin) {
-    auto f = p->lin_to_flat.find(lin);
-    return f == p->lin_to_flat.end() || p->by_flat[f->second].registered_children <= 0;
-  };
+  std::vector<uint64_t> keep;
   auto freq = [p](uint64_t lin) { return p->freq.estimate(lin); };
-  std::vector<uint64_t> reinsert;
-  for (uint64_t lin : p->inactive.allocate(count, is_leaf, freq)) {
-    auto rf = p->refs.find(lin);
-    if (rf != p->refs.end() && rf->second.total() > 0) continue;
+  auto visit = [&](uint64_t lin) {
     auto f = p->lin_to_flat.find(lin);
-    if (f == p->lin_to_flat.end()) continue;
+    if (f == p->lin_to_flat.end()) return;
     Entry& e = p->by_flat[f->second];
-    bool durable = has_tier(e.meta, L2) || e.meta.l3_present;
     auto& locs = e.meta.locations;
     locs.erase(std::remove_if(locs.begin(), locs.end(), [](const Location& l) { return l.tier == L0 || l.tier == L1; }),
                locs.end());
-    if (durable) {
+    if (has_tier(e.meta, L2) || e.meta.l3_present) {
       emit_upsert(MOVED, e.meta);
       stripped.push_back(e.meta.id);
-      reinsert.push_back(lin);
-    } else {
-      KVBlockID id = e.meta.id;
-      emit_invalidated(id);
-      remove_entry(p, f->second);
-      n->used_bytes = std::max<int64_t>(0, n->used_bytes - n->bytes_per_block());
-      discarded.push_back(id);
+      keep.push_back(lin);
+      return;
     }
+    discarded.push_back(e.meta.id);
+    emit_invalidated(e.meta.id);
+    remove_entry(p, f->second);
+    n->used_bytes = std::max<int64_t>(0, n->used_bytes - n->bytes_per_block());
+  };
+  p->inactive.evict(count, freq, visit);
+  for (uint64_t lin : keep) {  // durable: back among the zero-ref blocks (newest release)
+    auto f = p->lin_to_flat.find(lin);
+    p->inactive.release(lin, f == p->lin_to_flat.end() || p->by_flat[f->second].registered_children <= 0);
   }
-  for (uint64_t lin : reinsert) p->inactive.insert(lin);
   return {discarded, stripped};
 }
 
+// A node that died holds references it will never release, and L0 copies that are gone.
+// Its per-node ledger is released block by block (each kind it held), and every L0
+// location on it is stripped from the view. Returns the number of blocks whose
+// references were released and the blocks that lost an L0 location.
 std::pair<uint32_t, std::vector<KVBlockID>> Authority::reconcile_dead_node(const std::string& node_id) {
   if (node_id.empty()) fail("reconcile_dead_node: node_id required");
-  uint32_t cleared = 0;
-  std::vector<KVBlockID> stripped;
+  uint32_t released = 0;
   auto held = node_refs_.find(node_id);
   if (held != node_refs_.end()) {
-    auto copy = held->second;
-    for (auto& [bk, acc] : copy) {
+    for (auto& [bk, mine] : held->second) {
+      PoolView* p = nullptr;
       KVBlockID id{bk.model_id, bk.flat, bk.pool_kind, "public", bk.revision};
-      for (int kind : {REQUEST, WRITEBACK}) {
-        int64_t v = acc.get(kind);
-        if (v <= 0) continue;
-        try {
-          apply_ref(RefDelta{id, kind, int32_t(-v), node_id}, false);
-          cleared++;
-        } catch (...) {
-        }
-      }
+      const Entry* e = find(id, &p);
+      if (!e) continue;
+      RefAccounts& acc = p->refs[e->lineage];
+      const RefAccounts was = acc;
+      acc.request = std::max<int64_t>(0, acc.request - mine.request);
+      acc.writeback = std::max<int64_t>(0, acc.writeback - mine.writeback);
+      if (acc.total() == 0) p->refs.erase(e->lineage);
+      settle_refs(p, *e, was, false);
+      ++released;
     }
-    node_refs_.erase(node_id);
+    node_refs_.erase(held);
   }
+  std::vector<KVBlockID> stripped;
+  auto on_node_l0 = [&](const Location& l) { return l.tier == L0 && l.node_id == node_id; };
   for (auto& [k, n] : namespaces_)
     for (auto& [pk, p] : n->pools)
       for (auto& [flat, e] : p->by_flat) {
         auto& locs = e.meta.locations;
-        size_t before = locs.size();
-        locs.erase(std::remove_if(locs.begin(), locs.end(),
-                                  [&](const Location& l) { return l.tier == L0 && l.node_id == node_id; }),
-                   locs.end());
-        if (locs.size() != before) {
-          emit_upsert(MOVED, e.meta);
-          stripped.push_back(e.meta.id);
-        }
+        auto tail = std::remove_if(locs.begin(), locs.end(), on_node_l0);
+        if (tail == locs.end()) continue;
+        locs.erase(tail, locs.end());
+        emit_upsert(MOVED, e.meta);
+        stripped.push_back(e.meta.id);
       }
-  return {cleared, stripped};
+  return {released, stripped};
 }
 
 // ------------------------------------------------------------------ checkpoint
@@ -843,6 +883,17 @@ CheckpointSnapshot Authority::export_snapshot() {
 }
 
 void Authority::import_snapshot(const CheckpointSnapshot& snap) {
+  // every block must fit its model's hard quota before anything is replaced: a restore
+  // that silently dropped blocks would report success for a partial view
+  std::map<std::pair<std::string, std::string>, int64_t> need;
+  for (auto& b : snap.blocks) need[{b.meta.id.model_id, b.meta.id.revision}] += 1;
+  for (auto& d : snap.models) {
+    const int64_t unit = d.bytes_per_block > 0 ? int64_t(d.bytes_per_block) : 1;
+    const int64_t bytes = need[{d.model_id, d.revision}] * unit;
+    if (d.quota.hard_bytes > 0 && bytes > d.quota.hard_bytes)
+      fail("import_snapshot register rejected: (" + d.model_id + ", " + d.revision + ") holds " +
+           std::to_string(bytes) + " bytes over its hard quota " + std::to_string(d.quota.hard_bytes));
+  }
   namespaces_.clear();
   orphans_.clear();
   node_refs_.clear();
@@ -864,12 +915,9 @@ void Authority::import_snapshot(const CheckpointSnapshot& snap) {
     e.meta.ref_count = 0;
     e.block_id = p->next_block_id++;
     e.prefix_chain = b.prefix_chain;
-    if (e.parent) {
-      auto pit = p->lin_to_flat.find(e.parent);
-      if (pit != p->lin_to_flat.end()) p->by_flat[pit->second].registered_children++;
-    }
     p->lin_to_flat[e.lineage] = b.meta.id.block_hash;
     p->by_flat[b.meta.id.block_hash] = e;
+    link_child(p, e.parent, +1);
     n->used_bytes += n->bytes_per_block();
   }
   checkpoint_seq_ = std::max(checkpoint_seq_, snap.seq);
@@ -1048,21 +1096,26 @@ uint32_t Authority::hit_count_on(const KVBlockID& id, const std::string& node) c
   return c == it->second.end() ? 0 : c->second;
 }
 
+// The hottest blocks (summed hits over every node) that the node does not already hold
+// in L0, hottest first.
 std::vector<KVBlockID> Authority::warmup_plan(const std::string& node_id, size_t k) const {
-  std::vector<std::pair<uint32_t, KVBlockID>> owned;
-  for (auto& [key, n] : namespaces_)
-    for (auto& [pk, p] : n->pools)
-      for (auto& [flat, e] : p->by_flat) {
-        if (owner_on(ring_, flat) != node_id) continue;
+  std::vector<std::pair<uint32_t, KVBlockID>> hot;
+  for (auto& kv : namespaces_)
+    for (auto& pv : kv.second->pools) {
+      const PoolView& p = *pv.second;
+      for (auto& [flat, per_node] : p.hit_counts) {
         uint32_t hits = 0;
-        auto it = p->hit_counts.find(flat);
-        if (it != p->hit_counts.end())
-          for (auto& [nd, c] : it->second) hits += c;
-        if (hits) owned.emplace_back(hits, e.meta.id);
+        for (auto& nc : per_node) hits += nc.second;
+        auto e = p.by_flat.find(flat);
+        if (!hits || e == p.by_flat.end() || has_tier_on(e->second.meta, L0, node_id)) continue;
+        hot.emplace_back(hits, e->second.meta.id);
       }
-  std::stable_sort(owned.begin(), owned.end(), [](auto& a, auto& b) { return a.first > b.first; });
+    }
+  std::stable_sort(hot.begin(), hot.end(), [](auto& x, auto& y) {
+    return x.first != y.first ? x.first > y.first : x.second.block_hash < y.second.block_hash;
+  });
   std::vector<KVBlockID> out;
-  for (size_t i = 0; i < owned.size() && i < k; ++i) out.push_back(owned[i].second);
+  for (size_t i = 0; i < hot.size() && i < k; ++i) out.push_back(hot[i].second);
   return out;
 }
 
@@ -1101,6 +1154,31 @@ bool Authority::preplace_on_register(const std::string& model_id, const std::str
 }
 
 // ------------------------------------------------------------------ defrag
+// L2 segments of one pool view, per (node, segment): occupied slot indices and whether a
+// referenced block (which defrag must not move) sits in the segment.
+namespace {
+struct SegmentUse {
+  std::set<uint64_t> slots;
+  bool frozen = false;
+};
+std::map<std::pair<std::string, uint64_t>, SegmentUse> l2_segments(const PoolView& p, uint64_t slot_bytes) {
+  std::map<std::pair<std::string, uint64_t>, SegmentUse> segs;
+  for (auto& [flat, e] : p.by_flat) {
+    auto r = p.refs.find(e.lineage);
+    const bool held = r != p.refs.end() && r->second.total() > 0;
+    for (auto& l : e.meta.locations)
+      if (l.tier == L2) {
+        auto& u = segs[{l.node_id, l.segment_id}];
+        u.slots.insert(l.offset / slot_bytes);
+        u.frozen |= held;
+      }
+  }
+  return segs;
+}
+bool has_holes(const std::set<uint64_t>& slots) { return !slots.empty() && *slots.rbegin() + 1 != slots.size(); }
+}  // namespace
+
+// Share of the movable (unfrozen) L2 segments that have holes below their highest slot.
 double Authority::l2_fragmentation_ratio(const std::string& m, const std::string& r, int pool_kind,
                                          uint64_t slot_bytes) const {
   if (!slot_bytes) slot_bytes = kDefaultSlotBytes;
@@ -1108,21 +1186,13 @@ double Authority::l2_fragmentation_ratio(const std::string& m, const std::string
   if (!n) return 0.0;
   const PoolView* p = pool(n, resolve_pool_kind(pool_kind));
   if (!p) return 0.0;
-  // per (node, segment): occupied slots vs highest slot index + 1
-  std::map<std::pair<std::string, uint64_t>, std::pair<uint64_t, uint64_t>> seg;  // used, span
-  for (auto& [flat, e] : p->by_flat)
-    for (auto& l : e.meta.locations)
-      if (l.tier == L2) {
-        auto& s = seg[{l.node_id, l.segment_id}];
-        s.first++;
-        s.second = std::max<uint64_t>(s.second, l.offset / slot_bytes + 1);
-      }
-  uint64_t used = 0, span = 0;
-  for (auto& [k, v] : seg) {
-    used += v.first;
-    span += v.second;
+  size_t movable = 0, holey = 0;
+  for (auto& [key, u] : l2_segments(*p, slot_bytes)) {
+    if (u.frozen) continue;
+    ++movable;
+    holey += has_holes(u.slots);
   }
-  return span ? 1.0 - double(used) / double(span) : 0.0;
+  return movable ? double(holey) / double(movable) : 0.0;
 }
 
 std::vector<DefragMove> Authority::plan_defrag(const std::string& m, const std::string& r, int pool_kind, int mode,
@@ -1134,26 +1204,29 @@ std::vector<DefragMove> Authority::plan_defrag(const std::string& m, const std::
   if (!n) fail("TriggerDefrag: unknown namespace (" + m + ")");
   const PoolView* p = pool(n, resolve_pool_kind(pool_kind));
   if (!p) return moves;
-  // occupancy per (node, segment)
+  // occupancy per (node, segment), and the blocks in each occupied slot
   std::map<std::pair<std::string, uint64_t>, std::set<uint64_t>> occ;
+  std::map<std::tuple<std::string, uint64_t, uint64_t>, std::vector<std::pair<KVBlockID, uint64_t>>> in_slot;
   for (auto& [flat, e] : p->by_flat)
     for (auto& l : e.meta.locations)
-      if (l.tier == L2) occ[{l.node_id, l.segment_id}].insert(l.offset / slot_bytes);
+      if (l.tier == L2) {
+        const uint64_t slot = l.offset / slot_bytes;
+        occ[{l.node_id, l.segment_id}].insert(slot);
+        in_slot[{l.node_id, l.segment_id, slot}].emplace_back(e.meta.id, l.offset);
+      }
   if (mode == COMPACT || mode == BOTH) {
-    // move the highest slots of each segment into its lowest holes
+    // fill each segment's lowest holes with its highest occupied slots
+    const auto segs = l2_segments(*p, slot_bytes);
     for (auto& [key, slots] : occ) {
+      if (segs.at(key).frozen) continue;  // a referenced block must not move
       std::set<uint64_t> cur = slots;
       uint64_t hole = 0;
-      while (true) {
-        while (cur.count(hole)) hole++;
+      for (;;) {
+        while (cur.count(hole)) ++hole;
         if (cur.empty() || *cur.rbegin() <= hole) break;
-        uint64_t top = *cur.rbegin();
-        for (auto& [flat, e] : p->by_flat)
-          for (auto& l : e.meta.locations)
-            if (l.tier == L2 && l.node_id == key.first && l.segment_id == key.second && l.offset / slot_bytes == top) {
-              DefragMove mv{e.meta.id, key.first, key.second, l.offset, key.second, hole * slot_bytes, true, key.second};
-              moves.push_back(mv);
-            }
+        const uint64_t top = *cur.rbegin();
+        for (auto& [id, offset] : in_slot[{key.first, key.second, top}])
+          moves.push_back(DefragMove{id, key.first, key.second, offset, key.second, hole * slot_bytes, true, key.second});
         cur.erase(top);
         cur.insert(hole);
       }

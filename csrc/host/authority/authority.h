@@ -17,6 +17,7 @@
 #include <cstdint>
 #include <deque>
 #include <functional>
+#include <list>
 #include <map>
 #include <memory>
 #include <set>
@@ -54,25 +55,49 @@ class FrequencySketch {
   uint64_t reset_at_;
 };
 
-// Inactive index: blocks whose total ref count is zero. Eviction takes leaves
-// only (no registered child in the lineage tree), coldest frequency bucket
-// first, oldest insertion first within a bucket.
+// Zero-ref (evictable) blocks of one pool view, keyed by lineage.
+//
+// Entries are split by shape: a leaf (no registered child) can go now, an inner
+// block waits until its last registered child is gone (the authority reports that
+// through set_leaf). A batch eviction ranks the current leaves once by (frequency
+// bucket, release order), takes the coldest, and ranks again only if the removals
+// turned parents into leaves and the batch is still short: one pass per lineage
+// level instead of one scan per victim.
+//
+// The index holds at most `cap` entries. A release past the cap is not dropped:
+// it waits in an overflow FIFO and enters the index as room frees up, so every
+// zero-ref block eventually becomes evictable and quota planning can count it.
 class InactiveIndex {
  public:
   explicit InactiveIndex(size_t cap) : cap_(cap) {}
-  bool has(uint64_t lin) const { return order_.count(lin) != 0; }
-  size_t size() const { return order_.size(); }
+  bool has(uint64_t lin) const;                 // indexed (not waiting in overflow)
+  size_t size() const { return indexed_; }      // indexed entries (<= cap)
+  size_t waiting() const { return spill_.size(); }
+  size_t evictable() const { return indexed_ + spill_.size(); }
   size_t cap() const { return cap_; }
-  bool insert(uint64_t lin);
-  bool take(uint64_t lin);
-  // Choose up to n victims; `is_leaf` and `freq` are queried for candidates.
-  std::vector<uint64_t> allocate(size_t n, const std::function<bool(uint64_t)>& is_leaf,
-                                 const std::function<uint8_t(uint64_t)>& freq);
+  void release(uint64_t lin, bool leaf);        // ref total reached zero
+  bool retain(uint64_t lin);                    // ref total left zero (or the block is gone)
+  void set_leaf(uint64_t lin, bool leaf);       // child count crossed zero
+  // Takes up to n coldest leaves. `drop` removes each victim's block (which may turn
+  // its parent into a leaf through set_leaf) before the next one is taken.
+  size_t evict(size_t n, const std::function<uint8_t(uint64_t)>& freq, const std::function<void(uint64_t)>& drop);
 
  private:
+  struct Slot {
+    uint64_t tick = 0;
+    bool leaf = true;
+    bool spilled = false;
+  };
+  void admit(uint64_t lin, Slot& s);  // overflow or indexed
+  void refill();
+
   size_t cap_;
   uint64_t tick_ = 0;
-  std::unordered_map<uint64_t, uint64_t> order_;  // lineage -> insertion tick
+  size_t indexed_ = 0;
+  std::unordered_map<uint64_t, Slot> slots_;
+  std::map<uint64_t, uint64_t> leaves_;  // release tick -> lineage (indexed leaves)
+  std::list<uint64_t> spill_;            // overflow, oldest first
+  std::unordered_map<uint64_t, std::list<uint64_t>::iterator> spill_at_;
 };
 
 struct RefAccounts {
@@ -214,23 +239,37 @@ class Authority {
   const PoolView* pool(const Namespace* n, int pk) const;
   Entry* find(const KVBlockID& id, PoolView** pv = nullptr, Namespace** nsp = nullptr);
   const Entry* find(const KVBlockID& id) const;
-  int64_t free_bytes() const;
-  int64_t reclaimable_borrowed(const std::string& m, const std::string& r) const;
-  void reclaim_borrowed(const std::string& m, const std::string& r, int64_t want);
-  std::vector<std::pair<int, std::string>> evict_ns(Namespace* n, size_t count, const std::string& m,
-                                                    const std::string& r);
-  std::vector<std::string> drop_victims(PoolView* p, size_t n);
-  void remove_entry(PoolView* p, const std::string& flat);
-  void emit_upsert(int kind, const BlockMeta& m);
-  void emit_invalidated(const KVBlockID& id);
-  void apply_ref(const RefDelta& d, bool track_node);
+  // admission (own eviction, hard limit, borrowing against pool capacity)
   struct AdmitPlan {
     bool accept = true;
-    size_t own_evict = 0;
-    int64_t reclaim = 0;
+    size_t evict_own = 0;      // own zero-ref blocks to evict first
+    int64_t from_lenders = 0;  // bytes to take back from namespaces above their soft quota
     BackpressureSignal bp;
   };
-  AdmitPlan plan_admit(const std::string& m, const std::string& r, size_t new_blocks) const;
+  AdmitPlan plan_admit(const Namespace& n, size_t fresh_blocks) const;
+  int64_t pool_used_bytes() const;
+  int64_t lendable_bytes(const Namespace& n) const;
+  int64_t take_from_lenders(const Namespace* borrower, int64_t bytes);
+  // eviction
+  size_t evict_in(Namespace* n, PoolView* p, size_t count);
+  size_t evict_ns(Namespace* n, size_t count);
+  void remove_entry(PoolView* p, const std::string& flat);
+  void link_child(PoolView* p, uint64_t parent, int step);
+  // view events
+  void emit_upsert(int kind, const BlockMeta& m);
+  void emit_invalidated(const KVBlockID& id);
+  // refs: settle a block's zero crossing after its ledger changed from `was` (held_between:
+  // it was referenced at some point in between, so ending at zero is a release)
+  void settle_refs(PoolView* p, const Entry& e, const RefAccounts& was, bool held_between);
+  // registration
+  struct RegisterBatch {
+    Namespace* n = nullptr;
+    int pool_kind = TARGET;
+    std::vector<size_t> pos;  // prefix index of each meta
+    size_t fresh = 0;         // distinct hashes not yet registered
+  };
+  RegisterBatch check_register(const std::vector<std::string>& prefix_hashes, const std::vector<BlockMeta>& metas,
+                               bool need_durable);
   void rebuild_ring();
   std::vector<std::pair<std::string, KVBlockID>> all_block_keys() const;
   std::string owner_on(const std::map<uint64_t, std::string>& ring, const std::string& key) const;
