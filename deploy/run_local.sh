@@ -5,7 +5,10 @@
 #   ./deploy/run_local.sh            # LAKE_MODEL_BACKEND=mock -> tiny CPU model
 #   LAKE_MODEL_BACKEND=llama3-8b LAKE_DEVICE=cuda ./deploy/run_local.sh
 #   LAKE_PD_PAIR=1 ./deploy/run_local.sh   # the worker as a PD-split pair (prefill + decode process)
-#   ./deploy/smoke.sh                # in another shell
+#   LAKE_WORKERS=2 ./deploy/run_local.sh   # a second worker (worker-1 on LAKE_WORKER1_ADDR)
+#   ./deploy/smoke.sh                # in another shell (LAKE_WORKERS=2: ./deploy/smoke_pool.sh)
+# Every worker's storage agent is the remote pool agent (LAKE_CP_ADDR + LAKE_KV_ADDR): finished
+# requests' KV pages are written back to the kv-pool and any worker pulls pool-held prefixes.
 set -euo pipefail
 ROOT="$(cd "$(dirname "$0")/.." && pwd)"
 cd "$ROOT"
@@ -19,6 +22,10 @@ export LAKE_HTTP_ADDR="${LAKE_HTTP_ADDR:-127.0.0.1:8080}"
 export LAKE_MODEL_BACKEND="${LAKE_MODEL_BACKEND:-mock}"
 export LAKE_SERVED_MODEL_NAME="${LAKE_SERVED_MODEL_NAME:-mock-llm}"
 export LAKE_NODE_ID="${LAKE_NODE_ID:-worker-0}"
+export LAKE_WORKER1_ADDR="${LAKE_WORKER1_ADDR:-127.0.0.1:50055}"
+if [[ "${LAKE_WORKERS:-1}" == "2" ]]; then
+  export LAKE_WORKER_NODES="worker-0=$LAKE_WORKER_ADDR,worker-1=$LAKE_WORKER1_ADDR"
+fi
 PY="${PYTHON:-python}"
 
 wait_tcp() {
@@ -41,7 +48,7 @@ cleanup() {
 }
 trap cleanup EXIT INT TERM
 
-for hp in "$LAKE_CP_ADDR" "$LAKE_KV_ADDR" "$LAKE_WORKER_ADDR" "$LAKE_AGENT_ADDR" "$LAKE_HTTP_ADDR"; do
+for hp in "$LAKE_CP_ADDR" "$LAKE_KV_ADDR" "$LAKE_WORKER_ADDR" "$LAKE_WORKER1_ADDR" "$LAKE_AGENT_ADDR" "$LAKE_HTTP_ADDR"; do
   if (echo >/dev/tcp/"${hp%:*}"/"${hp##*:}") >/dev/null 2>&1; then
     echo "ERROR: $hp already in use; stop the old stack first" >&2
     exit 1
@@ -67,6 +74,11 @@ else
   "$PY" -m lake_b200.runtime & PIDS+=($!)
 fi
 wait_tcp "$LAKE_WORKER_ADDR" worker 1200
+if [[ "${LAKE_WORKERS:-1}" == "2" ]]; then
+  echo "==> second worker ($LAKE_MODEL_BACKEND)"
+  LAKE_NODE_ID=worker-1 LAKE_WORKER_BIND="$LAKE_WORKER1_ADDR" "$PY" -m lake_b200.runtime & PIDS+=($!)
+  wait_tcp "$LAKE_WORKER1_ADDR" worker-1 1200
+fi
 echo "==> router"
 "$PY" -m lake_b200.router & PIDS+=($!)
 wait_tcp "$LAKE_HTTP_ADDR" router

@@ -321,3 +321,13 @@ class Stub:
             else:
                 call = channel.unary_unary(path, **kw)
             setattr(self, m.name, call)
+
+
+MAX_MESSAGE_BYTES = 256 << 20
+
+
+def message_options() -> list[tuple[str, int]]:
+    """gRPC channel/server options for services that carry KV pages (a Llama-3-8B page is
+    2 MiB; gRPC's default receive limit is 4 MiB)."""
+    return [("grpc.max_send_message_length", MAX_MESSAGE_BYTES),
+            ("grpc.max_receive_message_length", MAX_MESSAGE_BYTES)]

@@ -34,6 +34,7 @@ import torch
 from ... import _host as H
 from ...engine.block_pool import chain_block_hashes
 from ..types import FinishRequest, PoolError, PoolErrorCode, PreparePlan, PrefixHint, ReadyHandle, StepStats
+from .fences import StepFences
 
 L0, L1, L2 = 1, 2, 3
 
@@ -48,10 +49,11 @@ def make_pool_node(model_id: str, page_bytes: int, l0_blocks: int, l1_blocks: in
     return tiers, l1
 
 
-class NativeAgent:
+class NativeAgent(StepFences):
     def __init__(self, engine, node_id: str = "node-0", model_id: str | None = None, revision: str = "",
                  authority: "H.Authority | None" = None, port=None, l1_blocks: int = 64, l2_blocks: int = 256,
                  storage_dir: str | None = None, writeback: str = "all", shared_tiers=None):
+        super().__init__()
         self.eng = engine
         self.node_id = node_id
         self.model_id = model_id or engine.cfg.name
@@ -76,7 +78,6 @@ class NativeAgent:
                                       self.model_id)
         self.stream = torch.cuda.Stream(engine.arena.device) if engine.arena.is_cuda else None
         self.writeback = writeback
-        self._ready_step: int | None = None
         self.written: set[bytes] = set()
         self.stats = {"writeback_blocks": 0, "promoted_blocks": 0, "writeback_ms": 0.0, "promote_ms": 0.0}
         self._staging = torch.zeros(self.page_bytes, dtype=torch.uint8, pin_memory=pin)
@@ -138,8 +139,7 @@ class NativeAgent:
 
     # ------------------------------------------------------------ fences
     def prepare_step(self, plan: PreparePlan) -> ReadyHandle:
-        if self._ready_step is not None:
-            raise PoolError(PoolErrorCode.PROTOCOL_ERROR, f"prepare while step {self._ready_step} is ready")
+        self._check_closed()
         reqs = self.eng.requests
         tables, slots, stats = {}, {}, {}
         for io in plan.write_set:
@@ -158,19 +158,11 @@ class NativeAgent:
             if io.token_start < len(r.prompt):
                 st.prefill_blocks = (min(io.token_end, len(r.prompt)) - io.token_start + self.bs - 1) // self.bs
             stats[io.req_id] = st
-        self._ready_step = plan.step_id
+        self._open(plan.step_id)
         return ReadyHandle(plan.step_id, stats, list(plan.read_set), list(plan.write_set), tables, slots)
 
-    def done(self, step_id: int) -> None:
-        if self._ready_step != step_id:
-            raise PoolError(PoolErrorCode.PROTOCOL_ERROR, f"done step={step_id} ready={self._ready_step}")
-        self._ready_step = None
-
-    def commit_write_extent(self, req_id: str, token_end: int) -> None:
-        return None  # pages are owned by the engine's scheduler; nothing reserved beyond its accounting
-
     # ------------------------------------------------------------ writeback
-    def on_request_finished(self, finish: FinishRequest) -> None:
+    def _finish(self, finish: FinishRequest) -> None:
         req = self.eng.requests.get(finish.req_id)
         if req is None or self.writeback == "none":
             return

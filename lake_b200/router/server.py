@@ -89,6 +89,11 @@ class RouterConfig:
                 node_role=os.environ.get("LAKE_NODE_ROLE", "hybrid"),
                 max_inflight=int(os.environ.get("LAKE_MAX_INFLIGHT", "1") or 1),
                 autoscale=os.environ.get("LAKE_AUTOSCALE", "") in ("1", "true"))
+        # LAKE_WORKER_NODES="worker-0=host:port,worker-1=host:port": several workers behind one router
+        for item in filter(None, (x.strip() for x in os.environ.get("LAKE_WORKER_NODES", "").split(","))):
+            node, _, addr = item.partition("=")
+            if node and addr:
+                c.workers[node] = addr
         return c
 
 

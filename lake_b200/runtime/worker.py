@@ -52,9 +52,9 @@ class WorkerServicer:
 
 
 def serve(bind: str = "0.0.0.0:50053", cfg: RoleConfig | None = None, pool=None, engine=None,
-          max_workers: int = 8, block: bool = True):
+          max_workers: int = 8, block: bool = True, pool_factory=None, node_id: str = "worker-0"):
     cfg = cfg or RoleConfig.from_env()
-    eng = WorkerEngine(cfg, pool=pool, engine=engine)
+    eng = WorkerEngine(cfg, pool=pool, engine=engine, node_id=node_id, pool_factory=pool_factory)
     eng.start()
     server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers))
     proto.add_service(server, "WorkerService", WorkerServicer(eng))
@@ -69,19 +69,46 @@ def serve(bind: str = "0.0.0.0:50053", cfg: RoleConfig | None = None, pool=None,
     return server, eng, port
 
 
+def remote_pool_factory(cp_addr: str, kv_addr: str, node_id: str, model_id: str, pool_node_id: str = "kv-pool",
+                        pull_budget_ms: float = 0.0, revision: str = ""):
+    """pool_factory for a worker whose KV pool is the control plane at `cp_addr` plus the kv-pool
+    byte service at `kv_addr`: prefix pages are pulled from the pool at admission and finished
+    requests' pages are written back to it."""
+    def make(engine):
+        from ..pool.agents.remote import connect
+        from ..pool.pool_iface import PoolIface
+
+        agent = connect(engine, cp_addr, kv_addr, node_id=node_id, model_id=model_id, revision=revision,
+                        pool_node_id=pool_node_id, pull_budget_ms=pull_budget_ms)
+        return PoolIface(agent, node_id=node_id)
+    return make
+
+
 def main() -> None:
+    """Environment: LAKE_WORKER_BIND, LAKE_NODE_ID, LAKE_CP_ADDR (control plane), LAKE_KV_ADDR
+    (kv-pool byte service), LAKE_KV_NODE_ID (the pool node's id in the view, default kv-pool),
+    LAKE_PULL_BUDGET_MS (0 = unbounded). With both addresses the worker's storage agent is the
+    remote pool agent; with only LAKE_CP_ADDR it publishes its resident prefix blocks."""
     logging.basicConfig(level=os.environ.get("LAKE_LOG", "INFO"))
     cfg = RoleConfig.from_env()
-    server, eng, port = serve(os.environ.get("LAKE_WORKER_BIND", "0.0.0.0:50053"), cfg, block=False)
+    node_id = os.environ.get("LAKE_NODE_ID", "worker-0")
     cp_addr = os.environ.get("LAKE_CP_ADDR", "")
-    if cp_addr:  # publish resident prefix blocks to the control plane's view
+    kv_addr = os.environ.get("LAKE_KV_ADDR", "")
+    factory = None
+    if cp_addr and kv_addr:
+        factory = remote_pool_factory(cp_addr, kv_addr, node_id, cfg.served_model_name,
+                                      os.environ.get("LAKE_KV_NODE_ID", "kv-pool"), cfg.pull_budget_ms,
+                                      cfg.model_revision)
+    server, eng, port = serve(os.environ.get("LAKE_WORKER_BIND", "0.0.0.0:50053"), cfg, block=False,
+                              pool_factory=factory, node_id=node_id)
+    if cp_addr and factory is None:  # publish resident prefix blocks to the control plane's view
         from ..engine.llm_engine import page_bytes
         from .cp_reporter import ControlPlaneReporter
 
         e = eng.engine
         ch = grpc.insecure_channel(cp_addr)
         eng.on_finished = ControlPlaneReporter(
-            proto.Stub(ch, "ControlPlaneService"), os.environ.get("LAKE_NODE_ID", "worker-0"),
+            proto.Stub(ch, "ControlPlaneService"), node_id,
             cfg.served_model_name, page_bytes(e.cfg, e.ec.block_size, e.arena.element_size()), e.ec.block_size,
             e.cfg.n_layers)
     try:

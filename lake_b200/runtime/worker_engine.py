@@ -80,9 +80,12 @@ def build_engine(cfg: RoleConfig, **kw):
 
 
 class WorkerEngine:
-    def __init__(self, cfg: RoleConfig, pool=None, engine=None, node_id: str = "worker-0"):
+    def __init__(self, cfg: RoleConfig, pool=None, engine=None, node_id: str = "worker-0", pool_factory=None):
         self.cfg = cfg
         self.pool = pool
+        # pool_factory(engine) -> PoolIface: a pool interface that needs the built engine (the
+        # remote storage agent); attached after the warm-up generation, which stays local
+        self.pool_factory = pool_factory
         self.node_id = node_id
         self.engine = engine
         self.lifecycle = WorkerLifecycle()
@@ -106,6 +109,9 @@ class WorkerEngine:
         if self.pool is not None:
             self.engine.attach_pool(self.pool)
         self._warmup()
+        if self.pool is None and self.pool_factory is not None:
+            self.pool = self.pool_factory(self.engine)
+            self.engine.attach_pool(self.pool)
         self.lifecycle.ready()
         self._thread = threading.Thread(target=self._loop, name="lakeb-step", daemon=True)
         self._thread.start()

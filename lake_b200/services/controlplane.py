@@ -507,7 +507,7 @@ def serve(bind: str = "0.0.0.0:50051", cp: ControlPlane | None = None, max_worke
 
     cp = cp or ControlPlane(checkpoints=FileCheckpointStore(os.environ["LAKE_CP_CHECKPOINT"])
                             if os.environ.get("LAKE_CP_CHECKPOINT") else None)
-    server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers))
+    server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers), options=proto.message_options())
     proto.add_service(server, "ControlPlaneService", cp)
     port = server.add_insecure_port(bind)
     server.start()

@@ -23,7 +23,7 @@ LOG = logging.getLogger("lake_b200.kvpool")
 
 def serve(bind: str, max_workers: int = 16, capacity_bytes: int = 0):
     store = H.ByteStore(capacity_bytes)  # 0 = unbounded
-    server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers))
+    server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers), options=proto.message_options())
     proto.add_service(server, "TcpDataService", TcpDataServer(store))
     port = server.add_insecure_port(bind)
     server.start()

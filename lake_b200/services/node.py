@@ -18,7 +18,7 @@ LOG = logging.getLogger("lake_b200.node")
 
 def serve(bind: str, node_id: str = "worker-0", max_workers: int = 16):
     ts = TransferServer()
-    server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers))
+    server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers), options=proto.message_options())
     proto.add_service(server, "AgentService", AgentServer(node_id))
     proto.add_service(server, "TransferService", ts)
     proto.add_service(server, "TcpDataService", TcpDataServer(ts.store))

@@ -1,68 +1,60 @@
-"""Engine <-> storage-pool contract (PoolIface over the in-memory agent): ready/done fences,
-pull budget, partial hits, deferred finishes, the commit-vs-newer-prepare guard, handle
-validation and error wrapping; and an engine whose steps run through the pool (modelled on the
-reference's python/lake/engine/tests/test_pool_agent.py and test_executor.py behaviours)."""
+"""Engine <-> storage-pool contract: the step fences every agent shares (one open step,
+paired done, finishes held while a step is open), PoolIface's handle validation and error
+wrapping, and an engine whose steps run through the production in-process agent
+(NativeAgent: L1/L2 tiers, PutEnd, authority). Modelled on the behaviours of the reference's
+python/lake/engine/tests/test_pool_agent.py and test_executor.py."""
 import pytest
 
-from lake_b200.pool.agents.memory import InMemoryAgent
+from lake_b200.pool.agents.fences import StepFences
 from lake_b200.pool.pool_iface import PoolIface
 from lake_b200.pool.types import (FinishRequest, ForwardMode, PoolError, PoolErrorCode, PreparePlan, ReadyHandle,
                                   ReqIoSet)
 
 
-def plan(step, reads=(), writes=(("a", 0, 16),), budget=0, partial=False):
-    rs = [ReqIoSet(r, s, e) for r, s, e in reads]
+def plan(step, writes=(("a", 0, 16),)):
     ws = [ReqIoSet(r, s, e) for r, s, e in writes]
-    return PreparePlan(step, ForwardMode.EXTEND, rs, ws, {io.req_id: io.token_end - io.token_start for io in ws},
-                       budget, partial)
+    return PreparePlan(step, ForwardMode.EXTEND, [], ws, {io.req_id: io.token_end - io.token_start for io in ws},
+                       0, False)
 
 
-def test_ready_done_fences_are_strictly_paired():
-    ag = InMemoryAgent()
-    h = ag.prepare_step(plan(1))
-    assert h.step_id == 1 and h.block_table_by_req["a"] == [0]
+class _Recorder(StepFences):
+    def __init__(self):
+        super().__init__()
+        self.finished = []
+
+    def prepare_step(self, p):
+        self._open(p.step_id)
+        return ReadyHandle(p.step_id)
+
+    def _finish(self, f):
+        self.finished.append(f.req_id)
+
+
+def test_step_fences_are_strictly_paired():
+    ag = _Recorder()
+    assert ag.prepare_step(plan(1)).step_id == 1
     with pytest.raises(PoolError) as e:
         ag.prepare_step(plan(2))
     assert e.value.code == PoolErrorCode.PROTOCOL_ERROR
     with pytest.raises(PoolError):
         ag.done(7)
     ag.done(1)
+    with pytest.raises(PoolError):
+        ag.done(1)  # nothing open
     ag.prepare_step(plan(2))
-
-
-def test_pull_budget_timeout_or_partial_hit():
-    ag = InMemoryAgent()
-    ag.force_pull_reqs = {"a"}
-    ag.pull_cost_ms = 50
-    with pytest.raises(PoolError) as e:
-        ag.prepare_step(plan(1, reads=[("a", 0, 32)], writes=[("a", 32, 33)], budget=20))
-    assert e.value.code == PoolErrorCode.TIMEOUT
-    # with partial hits allowed the request is dropped from the step instead
-    h = ag.prepare_step(plan(2, reads=[("a", 0, 32)], writes=[("a", 32, 33), ("b", 0, 16)], budget=20,
-                             partial=True))
-    assert [io.req_id for io in h.effective_write_set] == ["b"]
     ag.done(2)
+    assert ag.fence_stats["steps"] == 2
 
 
-def test_finish_between_fences_is_deferred_until_done():
-    ag = InMemoryAgent()
+def test_finishes_inside_an_open_step_run_at_done_in_order():
+    ag = _Recorder()
+    ag.on_request_finished(FinishRequest("x", "n0"))  # no open step: runs now
     ag.prepare_step(plan(1))
     ag.on_request_finished(FinishRequest("a", "n0"))
-    assert ag.finished == []  # the step still reads/writes "a"
+    ag.on_request_finished(FinishRequest("b", "n0"))
+    assert ag.finished == ["x"]
     ag.done(1)
-    assert ag.finished == ["a"]
-
-
-def test_commit_keeps_a_reservation_a_newer_prepare_raised():
-    ag = InMemoryAgent()
-    ag.prepare_step(plan(1, writes=[("a", 0, 16)]))
-    ag.done(1)
-    ag.prepare_step(plan(2, writes=[("a", 16, 32)]))
-    ag.done(2)
-    ag.commit_write_extent("a", 16)  # stale commit from step 1: step 2 raised the extent
-    assert ag.l0_token_end["a"] == 32
-    ag.commit_write_extent("a", 20)
-    assert ag.l0_token_end["a"] == 20
+    assert ag.finished == ["x", "a", "b"] and ag.fence_stats["held_finishes"] == 2
 
 
 class _Agent:
@@ -125,17 +117,19 @@ def test_pool_iface_validates_handles_and_wraps_errors():
     assert ok.agent.finished == ["a"] and ok.stats.duplicate_finish_calls == 1
 
 
-def test_engine_steps_through_the_pool_and_done_survives_a_failed_step():
+def test_engine_steps_through_the_native_agent_and_done_survives_a_failed_step(tmp_path):
     from lake_b200.engine.llm_engine import LLMEngine
+    from lake_b200.pool.agents.native import NativeAgent
 
-    ag = InMemoryAgent()
-    pool = PoolIface(ag)
     eng = LLMEngine("tiny", device="cpu", max_running=4, max_batched_tokens=64, max_model_len=256, num_blocks=64)
+    ag = NativeAgent(eng, storage_dir=str(tmp_path))
+    pool = PoolIface(ag)
     eng.attach_pool(pool)
     outs = eng.generate([[1, 2, 3, 4, 5] * 7, [9] * 20], max_new_tokens=5)
     assert all(len(o) == 5 for o in outs)
-    assert ag.prepare_calls == ag.done_calls == eng.step_count
-    assert sorted(ag.finished) == sorted(eng.requests)  # every finished request reached the agent
+    assert pool.stats.prepare_calls == pool.stats.done_calls == ag.fence_stats["steps"] == eng.step_count
+    assert pool.stats.finish_calls == len(eng.requests)  # every finished request reached the agent
+    assert ag.stats["writeback_blocks"] == 2 + 1  # 35 + 5 and 20 + 5 tokens: full pages only
     # a forward that raises still closes the step's compute fence
     eng.add_request([7] * 10, max_new_tokens=3)
 
@@ -145,4 +139,4 @@ def test_engine_steps_through_the_pool_and_done_survives_a_failed_step():
     eng.runner.execute = fail
     with pytest.raises(RuntimeError, match="device lost"):
         eng.step()
-    assert ag.prepare_calls == ag.done_calls
+    assert pool.stats.prepare_calls == pool.stats.done_calls
