@@ -665,6 +665,7 @@ PYBIND11_MODULE(LAKEB_MODULE, m) {
   m.def("gemm_pair_mode", []() { return lakeb::gemm_pair_mode(); });
   m.def("set_gemm_streamk_mode", [](int64_t mode) { lakeb::set_gemm_streamk_mode(static_cast<int>(mode)); });
   m.def("set_decode_split_mode", [](int64_t mode) { lakeb::set_decode_split_mode(static_cast<int>(mode)); });
+  m.def("set_prefill_kernel", [](int64_t mode) { lakeb::set_prefill_kernel(static_cast<int>(mode)); });
   m.def("gemm_grid", [](int64_t M, int64_t N, int64_t K, int64_t epi, bool w8) {
     return lakeb::gemm_grid(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), static_cast<int>(epi), 0,
                             w8);

@@ -51,7 +51,41 @@ bool pread_all(int fd, uint8_t* p, uint64_t n, uint64_t off) {
   }
   return true;
 }
+struct RecordHeader {
+  char magic[4];
+  uint16_t version;
+  uint16_t header_bytes;
+  uint32_t flags;
+  uint32_t reserved;
+  uint64_t payload_bytes;
+  uint8_t block_hash[32];
+  uint64_t checksum;
+};
+static_assert(sizeof(RecordHeader) == kBlockHeaderBytes, "block record header is 64 bytes");
+
+inline uint64_t rotl64(uint64_t x, int r) { return (x << r) | (x >> (64 - r)); }
+// SplitMix64's finalizer (S. Vigna): full avalanche of a 64-bit state.
+inline uint64_t mix_final(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
 }  // namespace
+
+// Word-wise multiply-rotate hash over the payload with a SplitMix64 finish: not cryptographic,
+// it detects torn, stale and bit-flipped records (a flipped bit changes every output bit).
+uint64_t payload_checksum(const uint8_t* p, uint64_t n) {
+  uint64_t h = 0x9e3779b97f4a7c15ull ^ n;
+  uint64_t i = 0;
+  for (; i + 8 <= n; i += 8) {
+    uint64_t w;
+    std::memcpy(&w, p + i, 8);
+    h = rotl64(h ^ (w * 0x9e3779b97f4a7c15ull), 29) * 0xc2b2ae3d27d4eb4full;
+  }
+  uint64_t tail = 0;
+  for (uint64_t k = 0; i + k < n; ++k) tail |= uint64_t(p[i + k]) << (8 * k);
+  return mix_final(h ^ tail);
+}
 
 // ------------------------------------------------------------------ segment arena
 SegmentArena::SegmentArena(uint64_t slot_bytes, size_t per_seg)
@@ -204,13 +238,15 @@ TierEngine::TierEngine(TierCaps caps, uint64_t block_bytes, uint8_t* l1_base, co
       l2_dir_(l2_dir),
       l3_dir_(l3_dir),
       model_key_(model_key),
-      arena_(block_bytes, 64) {
+      arena_(block_bytes + kBlockHeaderBytes, 64) {
   if (!block_bytes_) fail("TierEngine: block_bytes must be > 0");
   if (!l2_dir_.empty()) mkdirs(l2_dir_);
   if (!l3_dir_.empty()) mkdirs(l3_dir_ + "/" + model_key_);
   for (int64_t s = int64_t(caps_.l1) - 1; s >= 0; --s) free_slots_.push_back(s);
 }
-TierEngine::~TierEngine() = default;
+TierEngine::~TierEngine() {
+  for (auto& [seg, fd] : seg_fds_) ::close(fd);
+}
 
 void TierEngine::touch(std::list<std::string>& order,
                        std::unordered_map<std::string, std::list<std::string>::iterator>& pos, const std::string& h) {
@@ -223,38 +259,82 @@ void TierEngine::touch(std::list<std::string>& order,
 std::string TierEngine::seg_path(uint64_t seg) const { return l2_dir_ + "/seg_" + std::to_string(seg) + ".bin"; }
 std::string TierEngine::l3_path(const std::string& h) const { return l3_dir_ + "/" + model_key_ + "/" + to_hex(h); }
 
+int TierEngine::segment_fd(uint64_t seg) const {
+  std::lock_guard<std::mutex> g(fd_mu_);
+  auto it = seg_fds_.find(seg);
+  if (it != seg_fds_.end()) return it->second;
+  int fd = ::open(seg_path(seg).c_str(), O_RDWR | O_CREAT, 0644);
+  if (fd >= 0) seg_fds_[seg] = fd;
+  return fd;
+}
+
+bool TierEngine::write_record(int fd, const std::string& h, const uint8_t* bytes, uint64_t off) const {
+  RecordHeader hd{};
+  std::memcpy(hd.magic, kBlockMagic, 4);
+  hd.version = kBlockFormatVersion;
+  hd.header_bytes = kBlockHeaderBytes;
+  hd.payload_bytes = block_bytes_;
+  std::memcpy(hd.block_hash, h.data(), std::min<size_t>(h.size(), 32));
+  hd.checksum = payload_checksum(bytes, block_bytes_);
+  return pwrite_all(fd, bytes, block_bytes_, off + kBlockHeaderBytes) &&
+         pwrite_all(fd, reinterpret_cast<const uint8_t*>(&hd), kBlockHeaderBytes, off);
+}
+
+bool TierEngine::read_record(int fd, const std::string& h, uint8_t* dst, uint64_t off) const {
+  RecordHeader hd;
+  uint8_t want[32] = {0};
+  std::memcpy(want, h.data(), std::min<size_t>(h.size(), 32));
+  const bool ok = pread_all(fd, reinterpret_cast<uint8_t*>(&hd), kBlockHeaderBytes, off) &&
+                  std::memcmp(hd.magic, kBlockMagic, 4) == 0 && hd.version == kBlockFormatVersion &&
+                  hd.header_bytes == kBlockHeaderBytes && hd.payload_bytes == block_bytes_ &&
+                  std::memcmp(hd.block_hash, want, 32) == 0 &&
+                  pread_all(fd, dst, block_bytes_, off + kBlockHeaderBytes) &&
+                  payload_checksum(dst, block_bytes_) == hd.checksum;
+  if (!ok) {
+    std::lock_guard<std::mutex> g(fd_mu_);
+    ++corrupt_reads_;
+  }
+  return ok;
+}
+
+// The record is on the device (fdatasync) before the write reports success: PutEnd registers
+// the block as durable right after this returns.
 bool TierEngine::write_l2(const std::string& h, const uint8_t* bytes) {
   Placement pl = arena_.alloc(h);
   if (l2_dir_.empty()) return true;
-  int fd = ::open(seg_path(pl.segment_id).c_str(), O_WRONLY | O_CREAT, 0644);
-  if (fd < 0) return false;
-  bool ok = pwrite_all(fd, bytes, block_bytes_, pl.offset);
-  ::close(fd);
-  return ok;
+  const int fd = segment_fd(pl.segment_id);
+  return fd >= 0 && write_record(fd, h, bytes, pl.offset) && ::fdatasync(fd) == 0;
 }
 bool TierEngine::read_l2(const std::string& h, uint8_t* dst) const {
   auto pl = arena_.placement(h);
   if (!pl || l2_dir_.empty()) return false;
-  int fd = ::open(seg_path(pl->segment_id).c_str(), O_RDONLY);
-  if (fd < 0) return false;
-  bool ok = pread_all(fd, dst, block_bytes_, pl->offset);
-  ::close(fd);
-  return ok;
+  const int fd = segment_fd(pl->segment_id);
+  return fd >= 0 && read_record(fd, h, dst, pl->offset);
 }
+// L3 objects are written to a temporary name, synced and renamed, then the directory entry
+// is synced, so a crash leaves either the old state or the whole record.
 bool TierEngine::write_l3(const std::string& h, const uint8_t* bytes) {
   if (l3_dir_.empty()) return false;
   std::string tmp = l3_path(h) + ".tmp";
   int fd = ::open(tmp.c_str(), O_WRONLY | O_CREAT | O_TRUNC, 0644);
   if (fd < 0) return false;
-  bool ok = pwrite_all(fd, bytes, block_bytes_, 0);
+  bool ok = write_record(fd, h, bytes, 0) && ::fdatasync(fd) == 0;
   ::close(fd);
-  return ok && ::rename(tmp.c_str(), l3_path(h).c_str()) == 0;
+  ok = ok && ::rename(tmp.c_str(), l3_path(h).c_str()) == 0;
+  if (ok) {
+    int dfd = ::open((l3_dir_ + "/" + model_key_).c_str(), O_RDONLY | O_DIRECTORY);
+    if (dfd >= 0) {
+      ::fsync(dfd);
+      ::close(dfd);
+    }
+  }
+  return ok;
 }
 bool TierEngine::read_l3(const std::string& h, uint8_t* dst) const {
   if (l3_dir_.empty()) return false;
   int fd = ::open(l3_path(h).c_str(), O_RDONLY);
   if (fd < 0) return false;
-  bool ok = pread_all(fd, dst, block_bytes_, 0);
+  bool ok = read_record(fd, h, dst, 0);
   ::close(fd);
   return ok;
 }

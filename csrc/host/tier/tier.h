@@ -18,6 +18,7 @@
 #include <deque>
 #include <functional>
 #include <list>
+#include <mutex>
 #include <map>
 #include <optional>
 #include <string>
@@ -116,6 +117,15 @@ struct DeviceCopy {
 
 enum class BeginPromote : int { Started = 0, AlreadyInFlight = 1, AlreadyL0 = 2, Missing = 3 };
 
+// On-disk record of one block at L2 (a segment slot) and L3 (an object file): a 64-byte
+// header, then the payload. The header names the block (its 32-byte chain hash), the payload
+// length and a 64-bit checksum of the payload, so a torn, stale or foreign slot is detected
+// on read (the read fails and the block counts as missing) instead of returning wrong KV.
+constexpr uint64_t kBlockHeaderBytes = 64;
+constexpr char kBlockMagic[4] = {'L', 'K', 'B', 'K'};
+constexpr uint16_t kBlockFormatVersion = 1;
+uint64_t payload_checksum(const uint8_t* p, uint64_t n);
+
 class TierEngine {
  public:
   // l1_base: pinned host buffer of l1 caps * block_bytes bytes (owned by the caller).
@@ -180,6 +190,8 @@ class TierEngine {
   Relocate colocate_l2_move(const std::string& h, uint64_t segment_id, uint64_t offset);
   SegmentArena& arena() { return arena_; }
   HitStats stats;
+  uint64_t corrupt_reads() const { return corrupt_reads_; }  // records that failed validation
+  uint64_t record_bytes() const { return block_bytes_ + kBlockHeaderBytes; }
 
  private:
   static void touch(std::list<std::string>& order, std::unordered_map<std::string, std::list<std::string>::iterator>& pos,
@@ -190,6 +202,9 @@ class TierEngine {
   bool read_l2(const std::string& h, uint8_t* dst) const;
   bool write_l3(const std::string& h, const uint8_t* bytes);
   bool read_l3(const std::string& h, uint8_t* dst) const;
+  bool write_record(int fd, const std::string& h, const uint8_t* bytes, uint64_t off) const;
+  bool read_record(int fd, const std::string& h, uint8_t* dst, uint64_t off) const;
+  int segment_fd(uint64_t seg) const;
   SideEffects ensure_l2_cap();
   int64_t alloc_l1_slot(SideEffects* fx);
 
@@ -207,6 +222,9 @@ class TierEngine {
   std::unordered_set<std::string> one_shot_, inflight_;
   uint32_t admit_after_ = 2;
   SegmentArena arena_;
+  mutable std::mutex fd_mu_;
+  mutable std::unordered_map<uint64_t, int> seg_fds_;  // open segment files, closed with the engine
+  mutable uint64_t corrupt_reads_ = 0;
 };
 
 // ---------------------------------------------------------------- pipeline

@@ -113,6 +113,8 @@ void register_tier(py::module_& m) {
       .def("l0_len", &TierEngine::l0_len)
       .def("l1_len", &TierEngine::l1_len)
       .def("l2_len", &TierEngine::l2_len)
+      .def("corrupt_reads", &TierEngine::corrupt_reads)
+      .def("record_bytes", &TierEngine::record_bytes)
       .def("hit_count", [](const TierEngine& e, const py::bytes& h) { return e.hit_count(std::string(h)); })
       .def("is_one_shot", [](const TierEngine& e, const py::bytes& h) { return e.is_one_shot(std::string(h)); })
       .def("pin", [](TierEngine& e, const py::bytes& h) { e.pin(std::string(h)); })

@@ -351,8 +351,12 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 
 }  // namespace
 
+static int g_prefill_kernel = 1;
+void set_prefill_kernel(int mode) { g_prefill_kernel = mode; }
+
 int paged_prefill_tc(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream) {
   if (a.num_tiles <= 0) return 0;
+  if (g_prefill_kernel == 1 && prefill_pingpong_ok(a)) return paged_prefill_pingpong(a, q_rows, stream);
   if (a.n_kv_heads <= 0 || a.n_q_heads % a.n_kv_heads) return -1;
   if (a.q_stride % 8 || (reinterpret_cast<uintptr_t>(a.q) & 15)) return -2;
   CUtensorMap kvmap, qmap;

@@ -164,6 +164,12 @@ void set_gemm_streamk_mode(int mode);  // 1: stream-K where it balances SMs (def
 int paged_prefill(const PagedAttnArgs& a, cudaStream_t stream);
 // Same on tcgen05 tensor cores over query tiles of <= 128 rows; q has q_rows rows.
 int paged_prefill_tc(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream);
+// Two query heads of one KV group per CTA (ping-pong softmax/MMA, P and O in TMEM); needs an
+// even number of query heads per KV head. paged_prefill_tc dispatches to it when it applies
+// (set_prefill_kernel(0) keeps the one-head kernel).
+bool prefill_pingpong_ok(const PagedAttnArgs& a);
+int paged_prefill_pingpong(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream);
+void set_prefill_kernel(int mode);  // 1: ping-pong where it applies (default), 0: one head per CTA
 
 // ----------------------------------------------------------------- misc
 int rmsnorm_bf16(const __nv_bfloat16* x, int64_t sx, const __nv_bfloat16* w, __nv_bfloat16* out, int64_t so, int rows,

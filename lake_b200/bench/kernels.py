@@ -79,28 +79,42 @@ def bench_decode(t: Timer, out: list):
 
 
 def bench_prefill(t: Timer, out: list):
-    for nseq, ctx in [(4, 2048), (1, 8192)]:
+    """Causal prefill attention (Llama-3-8B heads, 32q/8kv): fresh prompts and prompts behind a
+    cached prefix (residual queries). The tcgen05 kernels (two heads per CTA, and one head per
+    CTA) against the warp-MMA kernel and torch SDPA (causal, same FLOPs, fresh prompts only)."""
+    from ..ops._ext import native
+
+    for nseq, prefix, new in [(4, 0, 2048), (1, 0, 8192), (4, 4096, 2048)]:
         hq, hkv = 32, 8
+        ctx = prefix + new
         nb = (ctx + 15) // 16
         arena = torch.randn(nseq * nb + 1, 1, 2, hkv, 16, 128, device="cuda").to(BF)
         bt = torch.randperm(nseq * nb, device="cuda").view(nseq, nb).to(torch.int32)
         sl = torch.full((nseq,), ctx, dtype=torch.int32, device="cuda")
-        qs = [i * ctx for i in range(nseq + 1)]
-        tiles = ops.build_prefill_tiles(qs, [0] * nseq, device="cuda")
-        q = torch.randn(nseq * ctx, hq * 128, device="cuda").to(BF)
+        qs = [i * new for i in range(nseq + 1)]
+        tiles = ops.build_prefill_tiles(qs, [prefix] * nseq, device="cuda")
+        q = torch.randn(nseq * new, hq * 128, device="cuda").to(BF)
         o = torch.empty_like(q)
         qs_t = torch.tensor(qs, dtype=torch.int32, device="cuda")
-        ms = t(lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv, 0.088, out=o))
-        tiles64 = ops.build_prefill_tiles(qs, [0] * nseq, tile=64, device="cuda")
+        run = lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv, 0.088, out=o)  # noqa
+        ms = t(run)
+        native().set_prefill_kernel(0)
+        ms_one = t(run)
+        native().set_prefill_kernel(1)
+        tiles64 = ops.build_prefill_tiles(qs, [prefix] * nseq, tile=64, device="cuda")
         ms_mma = t(lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles64, qs_t, None, hq, hkv, 0.088,
                                                        out=o, tensor_core=False))
-        qd = q.view(nseq, ctx, hq, 128).transpose(1, 2)
-        kd = torch.randn(nseq, hq, ctx, 128, device="cuda").to(BF)
-        ms_ref = t(lambda: torch.nn.functional.scaled_dot_product_attention(qd, kd, kd, is_causal=True))
-        fl = nseq * hq * ctx * ctx * 128 * 2  # causal: half of 4*T^2*D
-        out.append(dict(kernel="paged_prefill", nseq=nseq, ctx=ctx, ms=ms, tflops=fl / ms / 1e9,
-                        warp_mma_tflops=fl / ms_mma / 1e9, sdpa_ms=ms_ref,
-                        sdpa_tflops=fl / ms_ref / 1e9))
+        # visible (query, key) pairs: row i of a prompt sees prefix + i + 1 keys
+        pairs = nseq * (new * prefix + new * (new + 1) // 2)
+        fl = 4 * pairs * hq * 128
+        row = dict(kernel="paged_prefill", nseq=nseq, prefix=prefix, new=new, ms=ms, tflops=fl / ms / 1e9,
+                   one_head_ms=ms_one, one_head_tflops=fl / ms_one / 1e9, warp_mma_tflops=fl / ms_mma / 1e9)
+        if prefix == 0:
+            qd = q.view(nseq, new, hq, 128).transpose(1, 2)
+            kd = torch.randn(nseq, hq, new, 128, device="cuda").to(BF)
+            ms_ref = t(lambda: torch.nn.functional.scaled_dot_product_attention(qd, kd, kd, is_causal=True))
+            row.update(sdpa_ms=ms_ref, sdpa_tflops=fl / ms_ref / 1e9, vs_sdpa=ms_ref / ms)
+        out.append(row)
 
 
 def bench_norm(t: Timer, out: list):

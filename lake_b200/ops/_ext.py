@@ -26,6 +26,7 @@ def native():
             _C.set_gemm_pair_mode(int(os.environ.get("LAKEB_GEMM_PAIR", "1") or 0))
             _C.set_gemm_streamk_mode(int(os.environ.get("LAKEB_GEMM_STREAMK", "1") or 0))
             _C.set_decode_split_mode(int(os.environ.get("LAKEB_DECODE_SPLITS", "0") or 0))
+            _C.set_prefill_kernel(int(os.environ.get("LAKEB_PREFILL_KERNEL", "1") or 0))
         except ImportError as e:  # pragma: no cover - depends on the build
             _ERR = e
             raise RuntimeError(

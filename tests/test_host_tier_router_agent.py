@@ -48,6 +48,35 @@ def test_put_durable_l2_cap_demotes_to_l3_and_reads_back(tmp_path):
     assert e.probe(h(9)) == H.AccessKind.MISS
 
 
+def test_durable_records_detect_torn_foreign_and_flipped_bytes(tmp_path):
+    """An L2 slot or L3 object holds a header (magic, version, block hash, payload length,
+    checksum) before the payload: a record whose bytes changed on disk reads as missing."""
+    e = engine(tmp_path, caps=(4, 4, 2))
+    e.put_durable_bytes(h(0), blk(0))
+    e.put_durable_bytes(h(1), blk(1))
+    assert e.read_bytes(h(0)) == blk(0) and e.corrupt_reads() == 0
+    seg, off = e.l2_placement(h(0)).segment_id, e.l2_placement(h(0)).offset
+    assert e.l2_placement(h(1)).offset == off + e.record_bytes()  # slots are header + payload
+    path = tmp_path / "l2" / f"seg_{seg}.bin"
+    raw = bytearray(path.read_bytes())
+    raw[off + 64 + 100] ^= 0x10  # one flipped payload bit
+    path.write_bytes(bytes(raw))
+    assert e.read_bytes(h(0)) is None and e.corrupt_reads() == 1
+    assert e.read_bytes(h(1)) == blk(1)  # the neighbouring slot is intact
+    raw[off + 64 + 100] ^= 0x10
+    raw[off + 24] ^= 0x01  # a header naming another block
+    path.write_bytes(bytes(raw))
+    assert e.read_bytes(h(0)) is None and e.corrupt_reads() == 2
+    # L3: an object cut short (a torn write) is rejected too
+    f = engine(tmp_path / "l3case", caps=(4, 4, 1))
+    f.put_durable_bytes(h(3), blk(3))
+    f.put_durable_bytes(h(4), blk(4))  # L2 cap 1: h(3) moves to L3
+    assert f.l3_present(h(3)) and f.read_bytes(h(3)) == blk(3)
+    obj = tmp_path / "l3case" / "l3" / "m" / h(3).hex()
+    obj.write_bytes(obj.read_bytes()[: 64 + BB // 2])
+    assert f.read_bytes(h(3)) is None and f.corrupt_reads() == 1
+
+
 def test_pinned_l2_blocks_are_not_demoted(tmp_path):
     e = engine(tmp_path, caps=(4, 4, 1))
     e.put_durable_bytes(h(0), blk(0))

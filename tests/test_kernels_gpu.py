@@ -150,11 +150,41 @@ def test_paged_prefill(cuda_dev, hq, hkv, chunks):
     pos_t = torch.tensor(positions, dtype=torch.int32, device=cuda_dev)
     scale = 1 / math.sqrt(128)
     want = ref.paged_attention(q, arena, 1, bt, sl, qs_t, pos_t, hq, hkv, scale)
-    for tc, tile in ((True, 128), (False, 64)):
-        tiles = ops.build_prefill_tiles(qstart, pos0, tile=tile, device=cuda_dev)
-        out = ops.paged_prefill_attention(q, arena, 1, bt, sl, tiles, qs_t, pos_t, hq, hkv, scale, tensor_core=tc)
-        torch.cuda.synchronize()
+    from lake_b200.ops._ext import native
+
+    # tcgen05 with two heads per CTA (even GQA groups), tcgen05 with one head per CTA, warp MMA
+    for tc, tile, kernel in ((True, 128, 1), (True, 128, 0), (False, 64, 1)):
+        native().set_prefill_kernel(kernel)
+        try:
+            tiles = ops.build_prefill_tiles(qstart, pos0, tile=tile, device=cuda_dev)
+            out = ops.paged_prefill_attention(q, arena, 1, bt, sl, tiles, qs_t, pos_t, hq, hkv, scale,
+                                              tensor_core=tc)
+            torch.cuda.synchronize()
+        finally:
+            native().set_prefill_kernel(1)
         _close(out, want)
+    ops.core.check_status()
+
+
+def test_paged_prefill_rescales_when_scores_grow(cuda_dev):
+    """Keys whose scores jump by far more than 2^8 (log2 units) in later 128-key tiles force the
+    two-head kernel's lazy O rescale; the result must still match the fp32 oracle."""
+    hq, hkv, n = 8, 2, 700
+    arena, bt = _fill_cache(cuda_dev, 1, [n], hkv)
+    for page in range(arena.shape[0]):  # K grows with the page's position in the sequence
+        pos = (bt[0] == page).nonzero()
+        if pos.numel():
+            arena[page, 1, 0] *= 1.0 + 1.5 * int(pos[0, 0]) / 8
+    q = (torch.randn(n, hq * 128, device=cuda_dev) * 1.5).to(BF)
+    sl = torch.tensor([n], dtype=torch.int32, device=cuda_dev)
+    qs_t = torch.tensor([0, n], dtype=torch.int32, device=cuda_dev)
+    pos_t = torch.arange(n, dtype=torch.int32, device=cuda_dev)
+    scale = 1 / math.sqrt(128)
+    want = ref.paged_attention(q, arena, 1, bt, sl, qs_t, pos_t, hq, hkv, scale)
+    tiles = ops.build_prefill_tiles([0, n], [0], tile=128, device=cuda_dev)
+    out = ops.paged_prefill_attention(q, arena, 1, bt, sl, tiles, qs_t, pos_t, hq, hkv, scale)
+    torch.cuda.synchronize()
+    _close(out, want)
     ops.core.check_status()
 
 
