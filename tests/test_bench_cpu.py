@@ -41,3 +41,35 @@ def test_sweep_commands():
     many = sweep.command(8, 0.0, [], port=29611)
     assert "torch.distributed.run" in many and "--nproc-per-node=8" in many and "127.0.0.1" in many
     assert "29611" in many and many[many.index("--arrival-rate") + 1] == "0"
+
+
+def test_tier_probes_curves_and_latency(tmp_path, capsys):
+    """The tier-engine probes on this host's files: latency records, capacity curve that does
+    not fall as L0 grows, write-back ops falling as 1/N at constant bytes, block granularity."""
+    import json
+
+    from lake_b200.bench import tier_probes
+
+    tier_probes.main(["--requests", "120", "--dir", str(tmp_path)])
+    recs = [json.loads(l) for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+    by = {}
+    for r in recs:
+        by.setdefault(r["name"], []).append(r)
+    for name in ("tier_put_durable", "tier_promote_l0", "tier_hit_stats", "hit_curve", "promote_calibration",
+                 "block_granularity", "writeback_scan", "admission_experiment", "gc_proxy"):
+        assert name in by, name
+    rates = [r["hit_rate"] for r in by["hit_curve"]]
+    assert rates == sorted(rates)
+    wb = {r["counters"]["batch_n"]: r["counters"] for r in by["writeback_scan"]}
+    assert wb[1]["bytes"] == wb[4]["bytes"] and wb[1]["ops"] == 4 * wb[4]["ops"]
+    reuse = [r["reuse_ratio"] for r in by["block_granularity"]]
+    assert reuse == sorted(reuse, reverse=True) and reuse[0] > 0.99
+
+
+def test_router_probe_reports_latency_queue_and_modes():
+    from lake_b200.bench import router_probe
+
+    recs = {r["name"]: r for r in router_probe.run(requests=24, max_inflight=2, delay_ms=1.0)}
+    assert recs["router_e2e_latency"]["latency_ms"]["p99"] >= recs["router_e2e_latency"]["latency_ms"]["p50"] > 0
+    assert recs["router_queue_wait"]["counters"]["samples"] == 24
+    assert sum(v for k, v in recs["router_mode_distribution"]["counters"].items() if k.startswith("mode_")) == 24
