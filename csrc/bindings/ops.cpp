@@ -380,10 +380,10 @@ void moe_combine(at::Tensor& h, const at::Tensor& comb, const at::Tensor& weight
                  "moe_combine");
 }
 
-void wait_counters(int64_t cnt, int64_t n, int64_t target, c10::optional<at::Tensor> status) {
+void wait_counters(int64_t cnt, int64_t n, int64_t target, c10::optional<at::Tensor> status, int64_t limit_ns) {
   LAKEB_CHECK_RC(lakeb::wait_counters(reinterpret_cast<const unsigned long long*>(static_cast<uintptr_t>(cnt)),
                                        static_cast<int>(n), static_cast<unsigned long long>(target),
-                                       status_ptr(status), cur_stream()),
+                                       status_ptr(status), cur_stream(), static_cast<unsigned long long>(limit_ns)),
                  "wait_counters");
 }
 
@@ -659,7 +659,7 @@ PYBIND11_MODULE(LAKEB_MODULE, m) {
   m.def("moe_combine", &moe_combine, py::arg("h"), py::arg("comb"), py::arg("weights"), py::arg("top_k"),
         py::arg("wait_cnt") = 0, py::arg("wait_n") = 0, py::arg("target") = 0, py::arg("status") = py::none());
   m.def("wait_counters", &wait_counters, py::arg("cnt"), py::arg("n"), py::arg("target"),
-        py::arg("status") = py::none());
+        py::arg("status") = py::none(), py::arg("limit_ns") = 0);
   m.def("moe_dispatch_grid", []() { return lakeb::kMoEDispatchGrid; });
   m.def("set_gemm_pair_mode", [](int64_t mode) { lakeb::set_gemm_pair_mode(static_cast<int>(mode)); });
   m.def("gemm_pair_mode", []() { return lakeb::gemm_pair_mode(); });

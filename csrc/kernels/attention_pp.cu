@@ -47,6 +47,56 @@ __device__ __forceinline__ float ex2(float x) {
   return y;
 }
 
+// Two-lane fp32 arithmetic (sm_100a f32x2): one issue slot for two results.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " mov.b64 rc, {%6, %7};\n fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " add.rn.f32x2 rd, ra, rb;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+
+// 2^x for two lanes on the FMA pipe instead of the transcendental unit: x = n + f with n
+// an integer (rounded through the 1.5 * 2^23 trick) and f in [-0.5, 0.5]; 2^f from a degree-3
+// polynomial fitted here to 2^f on [-0.5, 0.5] by iteratively reweighted least squares on the
+// relative error (max relative error 7.5e-5, below bf16's 2^-9); 2^n is added to the exponent
+// bits. x is clamped at -125 so the result stays a normal float (~2e-38 where the exact value
+// underflows, which no softmax sum can tell from 0).
+__device__ __forceinline__ float2 exp2_poly2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  x.x = fmaxf(x.x, -125.f);
+  x.y = fmaxf(x.y, -125.f);
+  const float2 t = add2(x, make_float2(kRound, kRound));
+  const float2 n = add2(t, make_float2(-kRound, -kRound));
+  const float2 f = add2(x, make_float2(-n.x, -n.y));
+  float2 p = fma2(make_float2(0.05517167f, 0.05517167f), f, make_float2(0.24261114f, 0.24261114f));
+  p = fma2(p, f, make_float2(0.69326097f, 0.69326097f));
+  p = fma2(p, f, make_float2(0.99992806f, 0.99992806f));
+  return make_float2(__int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23)),
+                     __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23)));
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// bf16x2 from two floats by integer rounding (round half up on the dropped 16 bits) and one
+// byte permute: ALU work instead of the conversion unit.
+__device__ __forceinline__ uint32_t pack_bf16x2_int(float lo, float hi) {
+  return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+}
+
 // MN-major shared-memory operand with the 128-byte swizzle: 64-element MN chunks `lbo`
 // bytes apart, 8-row K groups 1024 bytes apart.
 __device__ __forceinline__ uint64_t desc_sw128_mn(uint32_t saddr, uint32_t lbo) {
@@ -81,6 +131,9 @@ __device__ __forceinline__ int64_t page_row(const PagedAttnArgs& a, int64_t phys
   return (((phys * a.num_layers + a.layer) * 2 + kv) * a.n_kv_heads + head) * 16;
 }
 
+// EMUL: every EMUL-th pair of probabilities is computed by exp2_poly2 (0: none); INTPACK:
+// pack P to bf16 with integer ops instead of the converter.
+template <int EMUL, bool INTPACK>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_pingpong_kernel(const __grid_constant__ CUtensorMap kvmap, const __grid_constant__ CUtensorMap qmap,
                             const PagedAttnArgs a) {
@@ -256,39 +309,60 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      // Only 64 scores stay in registers (10 warps cap a thread at 168 registers): columns
-      // 64..127 are read for the max and again for P; columns 0..63 are read once.
+      // the row's 128 scores: four loads in flight, one wait
       const int k0 = j * kTile;
-      const bool need_mask = k0 + kTile - 1 > kmax;
-      uint32_t sv[64];
-      float mx = -CUDART_INF_F;
-      auto load_half = [&](int half) {
-        tmem_ld32(t_s[h] + lane_off + half * 64, *reinterpret_cast<uint32_t(*)[32]>(sv));
-        tmem_ld32(t_s[h] + lane_off + half * 64 + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
-        tmem_ld_wait();
-        if (need_mask) {
+      uint32_t sv[128];
 #pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (k0 + half * 64 + i > kmax) sv[i] = __float_as_uint(-CUDART_INF_F);
-        }
-      };
-      for (int half = 1; half >= 0; --half) {
-        load_half(half);
+      for (int c = 0; c < 4; ++c)
+        tmem_ld32(t_s[h] + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32 * c));
+      tmem_ld_wait();
+      if (k0 + kTile - 1 > kmax) {  // the diagonal or the sequence end: keys past this row's last
 #pragma unroll
-        for (int i = 0; i < 64; i += 2) mx = fmaxf(mx, fmaxf(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])));
+        for (int i = 0; i < 128; ++i)
+          if (k0 + i > kmax) sv[i] = __float_as_uint(-CUDART_INF_F);
       }
-      mx *= sl2;
-      // tcgen05.ld/st are warp-collective: the rescale runs for the whole warp when any of its
-      // rows needs it (rows that do not keep alpha = 1)
+      // row max: eight independent three-input chains, then a short tree
+      float mv[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) mv[c] = max3f(__uint_as_float(sv[c]), __uint_as_float(sv[8 + c]), -CUDART_INF_F);
+#pragma unroll
+      for (int i = 16; i < 128; i += 16)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) mv[c] = max3f(mv[c], __uint_as_float(sv[i + c]), __uint_as_float(sv[i + 8 + c]));
+      float mx = max3f(max3f(mv[0], mv[1], mv[2]), max3f(mv[3], mv[4], mv[5]), fmaxf(mv[6], mv[7])) * sl2;
       const bool grow = mx > m + kRescaleLog2;
-      const float m_new = grow ? mx : m;
+      const float m_old = m;
+      if (grow) m = mx;
+      const float base = m == -CUDART_INF_F ? 0.f : m;
+      float2 rs[4] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      const float2 sl2v = make_float2(sl2, sl2), nbase = make_float2(-base, -base);
+#pragma unroll
+      for (int k = 0; k < 64; ++k) {  // key pair k -> packed column k (written over consumed scores)
+        const float2 z = fma2(make_float2(__uint_as_float(sv[2 * k]), __uint_as_float(sv[2 * k + 1])), sl2v, nbase);
+        float2 p;
+        if (EMUL > 0 && k % EMUL == EMUL - 1) {
+          p = exp2_poly2(z);
+        } else {
+          p.x = ex2(z.x);
+          p.y = ex2(z.y);
+        }
+        rs[k & 3] = add2(rs[k & 3], p);
+        sv[k] = INTPACK ? pack_bf16x2_int(p.x, p.y) : pack_bf16x2(p.x, p.y);
+        if (k == 31) tmem_st32(t_s[h] + lane_off, *reinterpret_cast<uint32_t(*)[32]>(sv));
+      }
+      tmem_st32(t_s[h] + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      rs[0] = add2(add2(rs[0], rs[1]), add2(rs[2], rs[3]));
+      // O and l still hold sums against the old base: bring them to m (after P, so the 128 scores
+      // are no longer live). tcgen05.ld/st are warp-collective: the whole warp rescales when any
+      // of its rows needs it (rows that do not keep alpha = 1).
+      float alpha = 1.f;
       if (__any_sync(0xffffffffu, grow && j > 0)) {
         if (!__all_sync(0xffffffffu, mbar_wait(&o_done[h], (j - 1) & 1, abort_flag, a.status))) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const float alpha = (grow && m != -CUDART_INF_F) ? ex2(m - m_new) : 1.f;
+        alpha = (grow && m_old != -CUDART_INF_F) ? ex2(m_old - m) : 1.f;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t ov[32];
@@ -298,26 +372,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int i = 0; i < 32; ++i) ov[i] = __float_as_uint(__uint_as_float(ov[i]) * alpha);
           tmem_st32(t_o[h] + lane_off + c * 32, ov);
         }
-        l *= alpha;
       }
-      m = m_new;
-      const float base = m == -CUDART_INF_F ? 0.f : m;
-      float rs0 = 0.f, rs1 = 0.f;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {  // 64 keys -> 32 packed bf16x2 columns per store
-        if (half == 1) load_half(1);
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const float p0 = ex2(fmaf(__uint_as_float(sv[i]), sl2, -base));
-          const float p1 = ex2(fmaf(__uint_as_float(sv[i + 1]), sl2, -base));
-          rs0 += p0;
-          rs1 += p1;
-          pk[i >> 1] = pack_bf16x2(p0, p1);
-        }
-        tmem_st32(t_s[h] + lane_off + half * 32, pk);
-      }
-      l += rs0 + rs1;
+      l = fmaf(l, alpha, rs[0].x + rs[0].y);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[h]);
@@ -359,6 +415,22 @@ bool prefill_pingpong_ok(const PagedAttnArgs& a) {
   return G > 0 && G % 2 == 0 && a.n_q_heads % 2 == 0;
 }
 
+namespace {
+// Softmax variants (exp on the FMA pipe, integer bf16 packing), picked with set_prefill_kernel:
+// mode 1 = the default variant, 10 + i = variant i of this table.
+using PrefillKernel = void (*)(CUtensorMap, CUtensorMap, PagedAttnArgs);
+const PrefillKernel kVariants[] = {
+    prefill_pingpong_kernel<0, false>, prefill_pingpong_kernel<0, true>, prefill_pingpong_kernel<4, false>,
+    prefill_pingpong_kernel<4, true>,  prefill_pingpong_kernel<3, true>, prefill_pingpong_kernel<2, true>,
+};
+constexpr int kDefaultVariant = 0;  // measured fastest overall: MUFU exp, converter packing
+int g_variant = kDefaultVariant;
+}  // namespace
+
+void set_prefill_variant(int v) {
+  g_variant = (v >= 0 && v < static_cast<int>(sizeof(kVariants) / sizeof(kVariants[0]))) ? v : kDefaultVariant;
+}
+
 int paged_prefill_pingpong(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream) {
   if (a.num_tiles <= 0) return 0;
   if (!prefill_pingpong_ok(a)) return -1;
@@ -369,9 +441,10 @@ int paged_prefill_pingpong(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t 
   if (rows >= (int64_t(1) << 31)) return -3;
   if (!make_bf16_map(&kvmap, a.arena, rows, 128, 128, 16, 64)) return -4;
   if (!make_bf16_map(&qmap, a.q, q_rows, static_cast<int64_t>(a.n_q_heads) * 128, a.q_stride, 128, 64)) return -5;
-  if (int e = ensure_smem_attr(reinterpret_cast<const void*>(prefill_pingpong_kernel), kSmem)) return e;
+  const PrefillKernel kern = kVariants[g_variant];
+  if (int e = ensure_smem_attr(reinterpret_cast<const void*>(kern), kSmem)) return e;
   dim3 grid(a.num_tiles, a.n_q_heads / 2);
-  prefill_pingpong_kernel<<<grid, kThreads, kSmem, stream>>>(kvmap, qmap, a);
+  kern<<<grid, kThreads, kSmem, stream>>>(kvmap, qmap, a);
   return cudaGetLastError();
 }
 

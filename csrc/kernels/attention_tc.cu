@@ -352,7 +352,11 @@ __global__ void __launch_bounds__(kThreadsTC, 1)
 }  // namespace
 
 static int g_prefill_kernel = 1;
-void set_prefill_kernel(int mode) { g_prefill_kernel = mode; }
+void set_prefill_kernel(int mode) {
+  // 0: one head per CTA; 1: two heads per CTA (default softmax variant); 10 + i: softmax variant i
+  g_prefill_kernel = mode >= 10 ? 1 : mode;
+  set_prefill_variant(mode >= 10 ? mode - 10 : -1);
+}
 
 int paged_prefill_tc(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream) {
   if (a.num_tiles <= 0) return 0;

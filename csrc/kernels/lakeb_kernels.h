@@ -169,7 +169,8 @@ int paged_prefill_tc(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream
 // (set_prefill_kernel(0) keeps the one-head kernel).
 bool prefill_pingpong_ok(const PagedAttnArgs& a);
 int paged_prefill_pingpong(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream);
-void set_prefill_kernel(int mode);  // 1: ping-pong where it applies (default), 0: one head per CTA
+void set_prefill_kernel(int mode);  // 1: ping-pong where it applies (default), 0: one head per CTA, 10+i: variant i
+void set_prefill_variant(int v);    // softmax variant of the ping-pong kernel (-1: default)
 
 // ----------------------------------------------------------------- misc
 int rmsnorm_bf16(const __nv_bfloat16* x, int64_t sx, const __nv_bfloat16* w, __nv_bfloat16* out, int64_t so, int rows,
@@ -251,8 +252,10 @@ int moe_combine(__nv_bfloat16* h, const __nv_bfloat16* comb, const float* weight
                 const unsigned long long* wait_cnt, int wait_n, unsigned long long wait_target, int* status,
                 cudaStream_t stream);
 // Waits until wait_cnt[0..n) >= target (EP: all sources dispatched) - a launch-ordering point.
+// Wait until every cnt[i] >= target; a wait that runs past limit_ns (0: the default 2 s) records
+// kErrTimeoutFlag in *status and the kernel returns.
 int wait_counters(const unsigned long long* cnt, int n, unsigned long long target, int* status,
-                  cudaStream_t stream);
+                  cudaStream_t stream, unsigned long long limit_ns = 0);
 
 // ids[i] < 0 -> prev[-1 - ids[i]] (tokens sampled by the previous, still in-flight step)
 int resolve_tokens(int* ids, const int* prev, int n, int n_prev, cudaStream_t stream);

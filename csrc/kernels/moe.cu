@@ -119,9 +119,10 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
-__global__ void wait_counters_kernel(const unsigned long long* cnt, int n, unsigned long long target, int* status) {
+__global__ void wait_counters_kernel(const unsigned long long* cnt, int n, unsigned long long target, int* status,
+                                     unsigned long long limit_ns) {
   for (int s = 0; s < n; ++s)
-    if (!wait_counter(cnt + s, target, nullptr, status)) return;
+    if (!wait_counter(cnt + s, target, nullptr, status, limit_ns)) return;
 }
 
 }  // namespace
@@ -147,8 +148,8 @@ int moe_combine(__nv_bfloat16* h, const __nv_bfloat16* comb, const float* weight
 }
 
 int wait_counters(const unsigned long long* cnt, int n, unsigned long long target, int* status,
-                  cudaStream_t stream) {
-  wait_counters_kernel<<<1, 1, 0, stream>>>(cnt, n, target, status);
+                  cudaStream_t stream, unsigned long long limit_ns) {
+  wait_counters_kernel<<<1, 1, 0, stream>>>(cnt, n, target, status, limit_ns ? limit_ns : kWaitLimitNs);
   return cudaGetLastError();
 }
 

@@ -100,6 +100,10 @@ def bench_prefill(t: Timer, out: list):
         ms = t(run)
         native().set_prefill_kernel(0)
         ms_one = t(run)
+        variants = {}
+        for v in range(6):  # softmax variants of the two-head kernel
+            native().set_prefill_kernel(10 + v)
+            variants[f"v{v}_ms"] = t(run)
         native().set_prefill_kernel(1)
         tiles64 = ops.build_prefill_tiles(qs, [prefix] * nseq, tile=64, device="cuda")
         ms_mma = t(lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles64, qs_t, None, hq, hkv, 0.088,
@@ -108,7 +112,8 @@ def bench_prefill(t: Timer, out: list):
         pairs = nseq * (new * prefix + new * (new + 1) // 2)
         fl = 4 * pairs * hq * 128
         row = dict(kernel="paged_prefill", nseq=nseq, prefix=prefix, new=new, ms=ms, tflops=fl / ms / 1e9,
-                   one_head_ms=ms_one, one_head_tflops=fl / ms_one / 1e9, warp_mma_tflops=fl / ms_mma / 1e9)
+                   one_head_ms=ms_one, one_head_tflops=fl / ms_one / 1e9, warp_mma_tflops=fl / ms_mma / 1e9,
+                   **variants)
         if prefix == 0:
             qd = q.view(nseq, new, hq, 128).transpose(1, 2)
             kd = torch.randn(nseq, hq, new, 128, device="cuda").to(BF)

@@ -152,8 +152,10 @@ def test_paged_prefill(cuda_dev, hq, hkv, chunks):
     want = ref.paged_attention(q, arena, 1, bt, sl, qs_t, pos_t, hq, hkv, scale)
     from lake_b200.ops._ext import native
 
-    # tcgen05 with two heads per CTA (even GQA groups), tcgen05 with one head per CTA, warp MMA
-    for tc, tile, kernel in ((True, 128, 1), (True, 128, 0), (False, 64, 1)):
+    # tcgen05 with two heads per CTA (even GQA groups; default softmax and its variants 10-15),
+    # tcgen05 with one head per CTA, warp MMA
+    runs = [(True, 128, 1), (True, 128, 0), (False, 64, 1)] + [(True, 128, 10 + v) for v in range(6)]
+    for tc, tile, kernel in runs:
         native().set_prefill_kernel(kernel)
         try:
             tiles = ops.build_prefill_tiles(qstart, pos0, tile=tile, device=cuda_dev)
