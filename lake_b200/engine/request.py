@@ -40,6 +40,7 @@ class Request:
     registered_blocks: int = 0
     bitmask: object | None = None  # optional [ceil(V/32)] int32 allowed-token mask for the next token
     arrival: float = field(default_factory=time.perf_counter)
+    admit_time: float | None = None  # when the scheduler gave it pages (end of its queue wait)
     first_token_time: float | None = None
     finish_time: float | None = None
     token_times: list[float] = field(default_factory=list)

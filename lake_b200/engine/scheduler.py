@@ -22,6 +22,8 @@ with its FutureMap token relay (node_scheduler.py:190-228, future_map.py:13-30).
 """
 from __future__ import annotations
 
+import time
+
 from collections import deque
 from dataclasses import dataclass, field
 
@@ -228,6 +230,8 @@ class Scheduler:
             req.num_cached = cached
             req.registered_blocks = len(hit)
             req.status = RequestStatus.RUNNING
+            if req.admit_time is None:
+                req.admit_time = time.perf_counter()
             self.running.append(req)
             out.prefill.append(Chunk(req, cached, n, cached + n == len(req.prompt)))
             budget -= n

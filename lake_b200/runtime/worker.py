@@ -85,7 +85,8 @@ def remote_pool_factory(cp_addr: str, kv_addr: str, node_id: str, model_id: str,
 
 
 def main() -> None:
-    """Environment: LAKE_WORKER_BIND, LAKE_NODE_ID, LAKE_CP_ADDR (control plane), LAKE_KV_ADDR
+    """Environment: LAKE_WORKER_BIND, LAKE_NODE_ID, LAKE_WORKER_METRICS_ADDR (Prometheus endpoint),
+    LAKE_TRACE_OUT (per-request JSONL trace), LAKE_CP_ADDR (control plane), LAKE_KV_ADDR
     (kv-pool byte service), LAKE_KV_NODE_ID (the pool node's id in the view, default kv-pool),
     LAKE_PULL_BUDGET_MS (0 = unbounded). With both addresses the worker's storage agent is the
     remote pool agent; with only LAKE_CP_ADDR it publishes its resident prefix blocks."""
@@ -101,6 +102,11 @@ def main() -> None:
                                       cfg.model_revision)
     server, eng, port = serve(os.environ.get("LAKE_WORKER_BIND", "0.0.0.0:50053"), cfg, block=False,
                               pool_factory=factory, node_id=node_id)
+    metrics_addr = os.environ.get("LAKE_WORKER_METRICS_ADDR", "")
+    if metrics_addr:  # Prometheus: TTFT/TPOT/queue/e2e histograms, token and step counters
+        from .metrics import serve_metrics
+
+        serve_metrics(eng.metrics, metrics_addr)
     if cp_addr and factory is None:  # publish resident prefix blocks to the control plane's view
         from ..engine.llm_engine import page_bytes
         from .cp_reporter import ControlPlaneReporter

@@ -100,12 +100,16 @@ class WorkerEngine:
         # PD_DISAGG requests are granted pages here and prefilled there
         self.pd_side = None
         self._engine_rid: dict[str, str] = {}  # request id -> the engine's id for it
+        from .metrics import WorkerMetrics
+
+        self.metrics = WorkerMetrics(node_id)
 
     # ------------------------------------------------------------ lifecycle
     def start(self, timeout_s: float = 600.0) -> None:
         self.lifecycle.warm()
         if self.engine is None:
             self.engine = build_engine(self.cfg)
+        self.metrics.engine = self.engine
         if self.pool is not None:
             self.engine.attach_pool(self.pool)
         self._warmup()
@@ -213,9 +217,11 @@ class WorkerEngine:
                     continue
                 eng.step()
                 self.steps += 1
+                self.metrics.steps.inc()
                 self._complete_finished()
             except Exception as e:  # step failure: fail in-flight work and stop accepting
                 LOG.exception("engine step failed")
+                self.metrics.step_failures.inc()
                 self._failed = e
                 err = e if isinstance(e, PoolError) else PoolError(_step_error_code(e), str(e))
                 self._fail_inflight(err)
@@ -236,6 +242,7 @@ class WorkerEngine:
             prefill_tokens = len(req.prompt) - req.num_cached
             job.result = GenerateResult(rid, list(req.output), req.num_cached // bs, (prefill_tokens + bs - 1) // bs,
                                         job.mode.value)
+            self.metrics.observe_finished(req, job.mode.value)
             if self.on_finished is not None:
                 self.on_finished(req)
             job.event.set()

@@ -243,3 +243,35 @@ def test_pd_pair_serves_pd_disagg_requests(tmp_path):
             proc.kill()
             out, _ = proc.communicate()
     assert proc.returncode == 0, out[-2000:]
+
+
+def test_worker_metrics_histograms_and_request_trace(tmp_path):
+    """Finished requests feed the worker's TTFT/TPOT/queue/e2e histograms and token counters,
+    the Prometheus endpoint serves them, and LAKE_TRACE_OUT gets one line per request."""
+    import json
+    import urllib.request
+
+    from lake_b200.runtime.config import RoleConfig
+    from lake_b200.runtime.metrics import serve_metrics
+    from lake_b200.runtime.worker_engine import WorkerEngine
+
+    we = WorkerEngine(RoleConfig(device="cpu", model_backend="mock", max_num_scheduled_tokens=128, num_blocks=64,
+                                 enable_overlap=False), node_id="w-metrics")
+    we.metrics.trace_path = str(tmp_path / "trace.jsonl")
+    we.start()
+    try:
+        for i in range(3):
+            we.submit(f"r{i}", list(range(1 + i, 40 + i)), 4)
+        server = serve_metrics(we.metrics, "127.0.0.1:0")
+        port = server[0].server_port if isinstance(server, tuple) else server.server_port
+        text = urllib.request.urlopen(f"http://127.0.0.1:{port}/metrics", timeout=10).read().decode()
+    finally:
+        we.stop(drain=False)
+    assert 'lake_worker_ttft_seconds_count{mode="COLOCATED"} 3.0' in text
+    assert 'lake_worker_tpot_seconds_count{mode="COLOCATED"} 3.0' in text
+    assert "lake_worker_output_tokens_total 12.0" in text
+    assert "lake_worker_running_requests" in text
+    recs = [json.loads(l) for l in open(tmp_path / "trace.jsonl")]
+    assert [r["request_id"] for r in recs] == ["r0", "r1", "r2"]
+    assert all(r["t_arrival"] <= r["t_admitted"] <= r["t_first_token"] <= r["t_finish"] for r in recs)
+    assert all(r["output_tokens"] == 4 and r["node"] == "w-metrics" for r in recs)
