@@ -369,21 +369,24 @@ void moe_dispatch(const at::Tensor& logits, const at::Tensor& x, at::Tensor& wei
 }
 
 void moe_combine(at::Tensor& h, const at::Tensor& comb, const at::Tensor& weights, int64_t top_k, int64_t wait_cnt,
-                 int64_t wait_n, int64_t target, c10::optional<at::Tensor> status) {
+                 int64_t wait_n, int64_t target, c10::optional<at::Tensor> status, int64_t wait_base) {
   check_bf16_2d(h, "h");
   TORCH_CHECK(h.is_contiguous() && comb.is_contiguous() && comb.scalar_type() == at::kBFloat16, "layouts");
   LAKEB_CHECK_RC(lakeb::moe_combine(bfm(h), bf(comb), weights.data_ptr<float>(), static_cast<int>(h.size(0)),
                                      static_cast<int>(h.size(1)), static_cast<int>(top_k),
                                      reinterpret_cast<const unsigned long long*>(static_cast<uintptr_t>(wait_cnt)),
                                      static_cast<int>(wait_n), static_cast<unsigned long long>(target),
-                                     status_ptr(status), cur_stream()),
+                                     status_ptr(status), cur_stream(),
+                                     reinterpret_cast<const unsigned long long*>(static_cast<uintptr_t>(wait_base))),
                  "moe_combine");
 }
 
-void wait_counters(int64_t cnt, int64_t n, int64_t target, c10::optional<at::Tensor> status, int64_t limit_ns) {
+void wait_counters(int64_t cnt, int64_t n, int64_t target, c10::optional<at::Tensor> status, int64_t limit_ns,
+                   int64_t base) {
   LAKEB_CHECK_RC(lakeb::wait_counters(reinterpret_cast<const unsigned long long*>(static_cast<uintptr_t>(cnt)),
                                        static_cast<int>(n), static_cast<unsigned long long>(target),
-                                       status_ptr(status), cur_stream(), static_cast<unsigned long long>(limit_ns)),
+                                       status_ptr(status), cur_stream(), static_cast<unsigned long long>(limit_ns),
+                                       reinterpret_cast<const unsigned long long*>(static_cast<uintptr_t>(base))),
                  "wait_counters");
 }
 
@@ -657,9 +660,10 @@ PYBIND11_MODULE(LAKEB_MODULE, m) {
         py::arg("top_k"), py::arg("cap"), py::arg("world"), py::arg("rank"), py::arg("gathered"), py::arg("row_slot"),
         py::arg("row_rank"), py::arg("count"), py::arg("done_cnt"), py::arg("status") = py::none());
   m.def("moe_combine", &moe_combine, py::arg("h"), py::arg("comb"), py::arg("weights"), py::arg("top_k"),
-        py::arg("wait_cnt") = 0, py::arg("wait_n") = 0, py::arg("target") = 0, py::arg("status") = py::none());
+        py::arg("wait_cnt") = 0, py::arg("wait_n") = 0, py::arg("target") = 0, py::arg("status") = py::none(),
+        py::arg("wait_base") = 0);
   m.def("wait_counters", &wait_counters, py::arg("cnt"), py::arg("n"), py::arg("target"),
-        py::arg("status") = py::none(), py::arg("limit_ns") = 0);
+        py::arg("status") = py::none(), py::arg("limit_ns") = 0, py::arg("base") = 0);
   m.def("moe_dispatch_grid", []() { return lakeb::kMoEDispatchGrid; });
   m.def("set_gemm_pair_mode", [](int64_t mode) { lakeb::set_gemm_pair_mode(static_cast<int>(mode)); });
   m.def("gemm_pair_mode", []() { return lakeb::gemm_pair_mode(); });

@@ -37,7 +37,8 @@ constexpr int kBK2 = 64;
 constexpr int kStages2 = 6;
 constexpr int kThreads2 = 192;
 constexpr int kStageBytes2 = kBM2 * kBK2 * 2 + (kBN2 / 2) * kBK2 * 2;  // 32 KB
-constexpr int kBarOff2 = kStages2 * kStageBytes2;
+constexpr int kStageOutOff2 = kStages2 * kStageBytes2;  // 4 epilogue warps x 2 KB: coalesced peer stores
+constexpr int kBarOff2 = kStageOutOff2 + 4 * 2048;
 constexpr int kSmem2 = kBarOff2 + (2 * kStages2 + 4) * 8 + 16 + 1024;
 
 __device__ __forceinline__ uint32_t cluster_rank() {
@@ -260,8 +261,9 @@ __global__ void __launch_bounds__(kThreads2, 1)
       const bool row_ok = row < p.M;
       if constexpr (EPI == kEpiQKV) {
         // this CTA's 256 accumulator columns are two whole heads (RoPE, K/V to the arena(s))
-        qkv_head_epilogue(p, tbase, 2 * n_blk, row, row_ok);
-        qkv_head_epilogue(p, tbase + 128, 2 * n_blk + 1, row, row_ok);
+        uint4* stage = reinterpret_cast<uint4*>(smem + kStageOutOff2 + q * 2048);
+        qkv_head_epilogue(p, tbase, 2 * n_blk, row, row_ok, stage);
+        qkv_head_epilogue(p, tbase + 128, 2 * n_blk + 1, row, row_ok, stage);
       } else if constexpr (EPI == kEpiRSPush) {
         // partial rows of this rank's K-slice go straight to the row's owner (P2P stores over NVLink)
         __nv_bfloat16* dst_row = nullptr;

@@ -250,12 +250,13 @@ constexpr int kMoEDispatchGrid = 64;  // fixed, so every rank adds the same coun
 // h[t] += sum_j weights[t, j] * comb[t*top_k + j]   (after waiting for EP combine counters)
 int moe_combine(__nv_bfloat16* h, const __nv_bfloat16* comb, const float* weights, int M, int dim, int top_k,
                 const unsigned long long* wait_cnt, int wait_n, unsigned long long wait_target, int* status,
-                cudaStream_t stream);
+                cudaStream_t stream, const unsigned long long* wait_base = nullptr);
 // Waits until wait_cnt[0..n) >= target (EP: all sources dispatched) - a launch-ordering point.
-// Wait until every cnt[i] >= target; a wait that runs past limit_ns (0: the default 2 s) records
-// kErrTimeoutFlag in *status and the kernel returns.
+// Wait until every cnt[i] >= (*base, when given) + target; a wait that runs past limit_ns (0: the
+// default 2 s) records kErrTimeoutFlag in *status and the kernel returns. A device-resident base
+// keeps the target valid when the launch is replayed from a CUDA graph.
 int wait_counters(const unsigned long long* cnt, int n, unsigned long long target, int* status,
-                  cudaStream_t stream, unsigned long long limit_ns = 0);
+                  cudaStream_t stream, unsigned long long limit_ns = 0, const unsigned long long* base = nullptr);
 
 // ids[i] < 0 -> prev[-1 - ids[i]] (tokens sampled by the previous, still in-flight step)
 int resolve_tokens(int* ids, const int* prev, int n, int n_prev, cudaStream_t stream);

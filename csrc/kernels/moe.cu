@@ -92,11 +92,13 @@ __global__ void __launch_bounds__(kThreads) moe_dispatch_kernel(const MoEDispatc
 
 __global__ void __launch_bounds__(kThreads)
     moe_combine_kernel(__nv_bfloat16* h, const __nv_bfloat16* comb, const float* weights, int M, int dim, int top_k,
-                       const unsigned long long* wait_cnt, int wait_n, unsigned long long target, int* status) {
+                       const unsigned long long* wait_cnt, int wait_n, unsigned long long target, int* status,
+                       const unsigned long long* wait_base) {
   __shared__ int ok_s;
   if (threadIdx.x == 0) {
     bool ok = true;
-    for (int s = 0; s < wait_n && ok; ++s) ok = wait_counter(wait_cnt + s, target, nullptr, status);
+    const unsigned long long goal = (wait_base ? *wait_base : 0ull) + target;
+    for (int s = 0; s < wait_n && ok; ++s) ok = wait_counter(wait_cnt + s, goal, nullptr, status);
     ok_s = ok;
   }
   __syncthreads();
@@ -120,9 +122,10 @@ __global__ void __launch_bounds__(kThreads)
 }
 
 __global__ void wait_counters_kernel(const unsigned long long* cnt, int n, unsigned long long target, int* status,
-                                     unsigned long long limit_ns) {
+                                     unsigned long long limit_ns, const unsigned long long* base) {
+  const unsigned long long goal = (base ? *base : 0ull) + target;
   for (int s = 0; s < n; ++s)
-    if (!wait_counter(cnt + s, target, nullptr, status, limit_ns)) return;
+    if (!wait_counter(cnt + s, goal, nullptr, status, limit_ns)) return;
 }
 
 }  // namespace
@@ -138,18 +141,18 @@ int moe_dispatch(const MoEDispatchArgs& a, cudaStream_t stream) {
 
 int moe_combine(__nv_bfloat16* h, const __nv_bfloat16* comb, const float* weights, int M, int dim, int top_k,
                 const unsigned long long* wait_cnt, int wait_n, unsigned long long wait_target, int* status,
-                cudaStream_t stream) {
+                cudaStream_t stream, const unsigned long long* wait_base) {
   if (M <= 0) return 0;
   if (dim % 2) return -1;
   const int grid = M < 1184 ? M : 1184;
   moe_combine_kernel<<<grid, kThreads, 0, stream>>>(h, comb, weights, M, dim, top_k, wait_cnt, wait_n, wait_target,
-                                                    status);
+                                                    status, wait_base);
   return cudaGetLastError();
 }
 
 int wait_counters(const unsigned long long* cnt, int n, unsigned long long target, int* status,
-                  cudaStream_t stream, unsigned long long limit_ns) {
-  wait_counters_kernel<<<1, 1, 0, stream>>>(cnt, n, target, status, limit_ns ? limit_ns : kWaitLimitNs);
+                  cudaStream_t stream, unsigned long long limit_ns, const unsigned long long* base) {
+  wait_counters_kernel<<<1, 1, 0, stream>>>(cnt, n, target, status, limit_ns ? limit_ns : kWaitLimitNs, base);
   return cudaGetLastError();
 }
 

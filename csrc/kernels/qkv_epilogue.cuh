@@ -23,6 +23,34 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v
   }
 }
 
+// Warp-collective store of one 64-byte piece per lane (32 fp32 -> bf16) to `dst` (this lane's
+// row; nullptr: no store). The pieces pass through `stage` (2 KB of this warp's shared memory)
+// so that each store instruction writes 8 rows x 64 contiguous bytes instead of 32 rows x 16
+// bytes: over NVLink (peer arenas) that is 8 runs of 64 bytes rather than 32 scattered 16-byte
+// writes. Chunk c of row r sits at r*4 + ((c + r/2) & 3) so both the row-wise writes and the
+// chunk-wise reads are free of bank conflicts. Every lane of the warp must call it.
+__device__ __forceinline__ void warp_store_rows64(uint4* stage, __nv_bfloat16* dst, const float* v, int lane) {
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    uint4 u;
+    u.x = pack_bf16x2(v[8 * c + 0], v[8 * c + 1]);
+    u.y = pack_bf16x2(v[8 * c + 2], v[8 * c + 3]);
+    u.z = pack_bf16x2(v[8 * c + 4], v[8 * c + 5]);
+    u.w = pack_bf16x2(v[8 * c + 6], v[8 * c + 7]);
+    stage[lane * 4 + ((c + (lane >> 1)) & 3)] = u;
+  }
+  __syncwarp();
+  const unsigned long long mine = reinterpret_cast<unsigned long long>(dst);
+#pragma unroll
+  for (int it = 0; it < 4; ++it) {
+    const int r = it * 8 + (lane >> 2), c = lane & 3;
+    const unsigned long long d = __shfl_sync(0xffffffffu, mine, r);
+    const uint4 u = stage[r * 4 + ((c + (r >> 1)) & 3)];
+    if (d) reinterpret_cast<uint4*>(d)[c] = u;
+  }
+  __syncwarp();
+}
+
 __device__ __forceinline__ __nv_bfloat16* kv_ptr(const KVArenaView& kv, int64_t slot, int head, int which) {
   const int64_t blk = slot / kv.block_size;
   const int64_t off = slot - blk * kv.block_size;
@@ -31,8 +59,11 @@ __device__ __forceinline__ __nv_bfloat16* kv_ptr(const KVArenaView& kv, int64_t 
 }
 
 // Head `head` of accumulator row `row` (this thread's TMEM lane; `tbase` addresses the head's
-// 128 fp32 columns). Every lane of the warp calls it (the TMEM loads are warp-aligned).
-__device__ __forceinline__ void qkv_head_epilogue(const GemmArgs& p, uint32_t tbase, int head, int row, bool row_ok) {
+// 128 fp32 columns). Every lane of the warp calls it (the TMEM loads are warp-aligned). With
+// `stage` (2 KB of this warp's shared memory) the peer-arena K/V stores are coalesced per warp.
+__device__ __forceinline__ void qkv_head_epilogue(const GemmArgs& p, uint32_t tbase, int head, int row, bool row_ok,
+                                                  uint4* stage = nullptr) {
+  const int lane = threadIdx.x & 31;
   const bool is_q = head < p.n_q_heads;
   const bool is_k = !is_q && head < p.n_q_heads + p.n_kv_heads;
   int pos = 0;
@@ -71,8 +102,8 @@ __device__ __forceinline__ void qkv_head_epilogue(const GemmArgs& p, uint32_t tb
       tmem_ld32(tbase + half * 32, r1);
       tmem_ld32(tbase + 64 + half * 32, r2);
       tmem_ld_wait();
+      float o1[32], o2[32];
       if (row_ok) {
-        float o1[32], o2[32];
         const float2* cs = p.rope_cs + static_cast<int64_t>(pos) * 64 + half * 32;
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
@@ -96,12 +127,17 @@ __device__ __forceinline__ void qkv_head_epilogue(const GemmArgs& p, uint32_t tb
             store_bf16x32(dst + half * 32, o1);
             store_bf16x32(dst + 64 + half * 32, o2);
           }
-          if (pslot >= 0) {
+          if (pslot >= 0 && !stage) {
             __nv_bfloat16* dst = kv_ptr(p.peer_kv, pslot, kvh, 0);
             store_bf16x32(dst + half * 32, o1);
             store_bf16x32(dst + 64 + half * 32, o2);
           }
         }
+      }
+      if (is_k && stage && p.peer_kv.base) {  // warp-uniform: the head is the same for every lane
+        __nv_bfloat16* dst = pslot >= 0 ? kv_ptr(p.peer_kv, pslot, kvh, 0) : nullptr;
+        warp_store_rows64(stage, dst ? dst + half * 32 : nullptr, o1, lane);
+        warp_store_rows64(stage, dst ? dst + 64 + half * 32 : nullptr, o2, lane);
       }
     }
   } else {
@@ -111,13 +147,15 @@ __device__ __forceinline__ void qkv_head_epilogue(const GemmArgs& p, uint32_t tb
       uint32_t r[32];
       tmem_ld32(tbase + c * 32, r);
       tmem_ld_wait();
-      if (row_ok) {
-        float v[32];
+      float v[32];
 #pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      if (row_ok) {
         if (slot >= 0) store_bf16x32(kv_ptr(p.kv, slot, kvh, 1) + c * 32, v);
-        if (pslot >= 0) store_bf16x32(kv_ptr(p.peer_kv, pslot, kvh, 1) + c * 32, v);
+        if (pslot >= 0 && !stage) store_bf16x32(kv_ptr(p.peer_kv, pslot, kvh, 1) + c * 32, v);
       }
+      if (stage && p.peer_kv.base)
+        warp_store_rows64(stage, pslot >= 0 ? kv_ptr(p.peer_kv, pslot, kvh, 1) + c * 32 : nullptr, v, lane);
     }
   }
 }

@@ -248,6 +248,22 @@ def profile(case: str) -> None:
         pos = torch.arange(m, dtype=torch.int32, device="cuda") + 2000
         slots = torch.arange(m, dtype=torch.int64, device="cuda")
         fn = lambda: ops.linear_qkv(x, w, q, cs, pos, slots, arena, 0, hq, hkv)  # noqa: E731
+    elif case == "pd_qkv":
+        # fused P->D at 4096 prompt tokens: QKV GEMM + RoPE + K/V to this GPU's and GPU 1's arena
+        from ..ops._ext import native
+
+        native().enable_peer_access(1)
+        m, hq, hkv, hidden = 4096, 32, 8, 4096
+        nb = m // 16
+        arena = torch.zeros(nb + 1, 1, 2, hkv, 16, 128, device="cuda:0", dtype=BF)
+        peer = torch.zeros(nb + 1, 1, 2, hkv, 16, 128, device="cuda:1", dtype=BF)
+        x = torch.randn(m, hidden, device="cuda").to(BF)
+        w = (torch.randn((hq + 2 * hkv) * 128, hidden, device="cuda") * 0.02).to(BF)
+        q = torch.empty(m, hq * 128, device="cuda", dtype=BF)
+        cs = ref.rope_cache(8192, 5e5, 128, None, device="cuda")
+        pos = torch.arange(m, dtype=torch.int32, device="cuda")
+        slots = torch.arange(m, dtype=torch.int64, device="cuda")
+        fn = lambda: ops.linear_qkv(x, w, q, cs, pos, slots, arena, 0, hq, hkv, peer, slots)  # noqa: E731
     elif case == "moe_decode":
         fn, _ = _moe_case(128)
     else:

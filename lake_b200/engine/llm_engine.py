@@ -165,8 +165,10 @@ class LLMEngine:
                                                               ec.long_prefill_threshold, ec.max_model_len, maxb,
                                                               ec.spec_tokens, ec.spec_ngram))
         self.runner = ModelRunner(self.model, self.arena, max_tokens, ec.max_running, maxb,
-                                  ec.use_cuda_graphs and not (ec.ep and ec.ep[1] > 1), ec.block_size,
+                                  ec.use_cuda_graphs, ec.block_size,
                                   row_multiple=self.tp_world, max_samples=ec.max_running * (1 + ec.spec_tokens))
+        if ec.ep is not None and ec.ep[1] > 1:
+            self.runner.lazy_capture = False
         self.requests: dict[str, Request] = {}
         self.pool_iface = None  # PoolIface (storage-pool fences), attached by attach_pool
         self.overlap = ec.overlap and not (ec.ep and ec.ep[1] > 1) and ec.spec_tokens == 0

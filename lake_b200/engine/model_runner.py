@@ -83,6 +83,9 @@ class ModelRunner:
         self.np_i32 = self.h_i32.numpy()
         self.np_i64 = self.h_i64.numpy()
         self.use_graphs = use_cuda_graphs and self.cuda
+        # capture a bucket's graph on first use; off for expert parallelism, whose capture warm-up
+        # runs the group's exchange and so must happen on every rank at once (capture_graphs)
+        self.lazy_capture = True
         self.graphs: dict[int, tuple] = {}
         self.graph_launches: dict[int, int] = {}
         self.has_peer = False
@@ -300,6 +303,8 @@ class ModelRunner:
         pure_decode = not out.prefill and bitmask is None
         streaming = getattr(self.model, "layer_ready", None) is not None  # weights still loading: run eagerly
         bucket = self._bucket(nd) if (pure_decode and self.use_graphs and not streaming) else None
+        if bucket is not None and bucket not in self.graphs and not self.lazy_capture:
+            bucket = None  # expert-parallel ranks capture only together (capture_graphs): run this step eagerly
         t, s, ntiles, nrows, nd_eff = self._pack(out, pad_decode_to=bucket or 0)
         if not self.cuda:
             self._copy_cpu(t, s, nrows)

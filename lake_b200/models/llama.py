@@ -312,6 +312,8 @@ class DecoderLM:
                 ops.linear_residual(attn, self.w[p + "o_proj"], h, out=h)
                 ops.rms_norm(h, self.w[p + "post_attention_layernorm"], c.rms_eps, out=x)
                 self._mlp(i, x, h, ws, t)
+        if self.moe is not None and self.moe.ep is not None:
+            self.moe.ep.end_step()  # expert-parallel wait targets: the bases advance by this step's totals
         r = b.sample_rows.shape[0]
         if r == 0:
             return ws.tokens[:0]

@@ -19,6 +19,11 @@ serve their experts and signal), so counter totals agree across ranks. A
 buffer of parity p is rewritten two layers later only after a chain of waits
 that includes every reader's finish.
 
+Wait targets are a device-resident base per counter family plus an offset
+within the step (a kernel argument); end_step() adds the step's totals to the
+bases with one small kernel. A step captured in a CUDA graph therefore replays
+with fresh targets, which lets expert-parallel decode steps run from graphs.
+
 Symmetric buffer (one cudaMalloc per rank, IPC-mapped by every peer):
     gathered[2] [epr*cap, hidden] bf16 | slot[2], src[2] [epr*cap] int32 |
     count[2] [epr] int32 | comb[2] [max_tokens*top_k, hidden] bf16 |
@@ -79,8 +84,11 @@ class EPGroup:
         self.src = [self._view(f"r{p}", torch.int32, (rows,)) for p in range(2)]
         self.count = [self._view(f"n{p}", torch.int32, (self.epr,)) for p in range(2)]
         self.comb = [self._view(f"c{p}", torch.bfloat16, (max_tokens * top_k, hidden)) for p in range(2)]
+        # within-step offsets of the wait targets; the device bases hold every earlier step's totals
         self.expect = {("d", p): 0 for p in range(2)}
         self.expect.update({("c", p): 0 for p in range(2)})
+        self._fam = list(self.expect)
+        self.bases = torch.zeros(len(self._fam), dtype=torch.int64, device=self.device)
         self._c = C
         self.down_grid = C.gemm_grid(rows, hidden, hidden, 7)  # grouped: data-parallel, K does not change the grid
         dist.barrier(group=group)
@@ -92,6 +100,18 @@ class EPGroup:
 
     def _ptr(self, rank: int, name: str) -> int:
         return self.base[rank] + self.lay[name]
+
+    def _base(self, fam: str, p: int) -> int:
+        return self.bases.data_ptr() + self._fam.index((fam, p)) * 8
+
+    def end_step(self) -> None:
+        """Close a step: the bases advance by the step's totals (stream-ordered after every
+        kernel of the step, and captured with it) and the offsets restart."""
+        deltas = [self.expect[f] for f in self._fam]
+        if any(deltas):
+            self._c.tp_advance(self.bases.data_ptr(), deltas)
+        for f in self._fam:
+            self.expect[f] = 0
 
     def _cnt(self, rank: int, fam: str, p: int) -> int:
         idx = (0 if fam == "d" else 2 * self.world) + p * self.world
@@ -107,7 +127,7 @@ class EPGroup:
                        [self._ptr(r, f"r{p}") for r in range(W)], [self._ptr(r, f"n{p}") for r in range(W)],
                        [self._cnt(r, "d", p) for r in range(W)], status)
         self.expect[("d", p)] += C.moe_dispatch_grid()
-        C.wait_counters(self._cnt(self.rank, "d", p), W, self.expect[("d", p)], status)
+        C.wait_counters(self._cnt(self.rank, "d", p), W, self.expect[("d", p)], status, base=self._base("d", p))
         C.gemm_grouped(self.gathered[p], w_gate_up, act, 2, self.count[p], self.cap, status=status)
         tp = dict(world=W, rank=self.rank, rows_per_rank=1, rs_cnt=[self._cnt(r, "c", p) for r in range(W)])
         C.gemm_grouped(act, w_down, None, 7, self.count[p], self.cap, row_slot=self.slot[p], row_rank=self.src[p],
@@ -115,4 +135,4 @@ class EPGroup:
         self.expect[("c", p)] += self.down_grid
         self.count[p].zero_()  # consumed; peers refill it two layers on, after waits that follow this point
         C.moe_combine(h, self.comb[p][: t * self.top_k], wts, self.top_k, self._cnt(self.rank, "c", p), W,
-                      self.expect[("c", p)], status)
+                      self.expect[("c", p)], status, wait_base=self._base("c", p))

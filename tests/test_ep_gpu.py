@@ -27,7 +27,7 @@ def _prompts(rank):
     return [[rng.randrange(2048) for _ in range(n)] for n in (3, 50, 120, 17)]
 
 
-def _worker(rank, world, port, out_dir):
+def _worker(rank, world, port, out_dir, graphs=False):
     import torch.distributed as dist
 
     from lake_b200.engine.llm_engine import LLMEngine
@@ -39,6 +39,8 @@ def _worker(rank, world, port, out_dir):
     dist.init_process_group("gloo", rank=rank, world_size=world)
     eng = LLMEngine("tiny-gpu", device=f"cuda:{rank}", max_running=8, max_batched_tokens=128, max_model_len=1024,
                     num_blocks=256, model_overrides=MOE, ep=(rank, world, None))
+    if graphs:  # decode steps replay captured graphs; the EP wait targets come from device bases
+        eng.runner.capture_graphs()
     prompts = _prompts(rank)
     rids = [eng.add_request(p, max_new_tokens=8 + 4 * rank) for p in prompts]  # ranks finish at different steps
     steps = 0
@@ -59,10 +61,11 @@ def _worker(rank, world, port, out_dir):
     dist.destroy_process_group()
 
 
-def test_ep2_moe_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("graphs", [False, True])
+def test_ep2_moe_matches_single_gpu(tmp_path, graphs):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path), graphs), nprocs=2, join=True)
     for r in range(2):
         res = json.load(open(tmp_path / f"ep{r}.json"))
         got = [t for o in res["outs"] for t in o]

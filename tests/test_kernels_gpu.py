@@ -309,3 +309,33 @@ def test_gemm_fp8_weights_match_dequantized(cuda_dev, m, n, k):
     assert (toks.long().cpu() == want.argmax(-1).cpu()).float().mean().item() > 0.97
     torch.cuda.synchronize()
     ops.core.check_status()
+
+
+@pytest.mark.parametrize("m", [1024, 1000, 8192])
+def test_qkv_peer_kv_stores_equal_local(cuda_dev, m):
+    """Fused P->D: the QKV epilogue's K/V rows written into a second GPU's arena over NVLink
+    (coalesced through shared memory in the two-SM kernel) are bit-identical to the local
+    arena's, with slots that cross pages and a ragged last tile."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from lake_b200.ops._ext import native
+
+    native().enable_peer_access(1)
+    hq, hkv, hidden = 32, 8, 4096
+    nb = (m + 15) // 16 + 8
+    arena = torch.zeros(nb, 2, 2, hkv, 16, 128, device=cuda_dev, dtype=BF)
+    peer = torch.zeros(nb, 2, 2, hkv, 16, 128, device="cuda:1", dtype=BF)
+    x = torch.randn(m, hidden, device=cuda_dev).to(BF)
+    w = (torch.randn((hq + 2 * hkv) * 128, hidden, device=cuda_dev) * 0.02).to(BF)
+    q = torch.empty(m, hq * 128, device=cuda_dev, dtype=BF)
+    cs = ref.rope_cache(8192, 5e5, 128, None, device=cuda_dev)
+    pos = torch.arange(m, dtype=torch.int32, device=cuda_dev) + 7
+    slots = torch.randperm(nb * 16, device=cuda_dev)[:m].to(torch.int64)  # scattered over pages
+    pslots = (slots + 16 * 3) % (nb * 16)  # a different placement in the peer arena
+    ops.linear_qkv(x, w, q, cs, pos, slots, arena, 1, hq, hkv, peer, pslots)
+    torch.cuda.synchronize()
+    ops.core.check_status()
+    flat_l = arena[:, 1].permute(0, 3, 1, 2, 4).reshape(nb * 16, 2, hkv, 128)  # [slot, k/v, head, dim]
+    flat_p = peer[:, 1].permute(0, 3, 1, 2, 4).reshape(nb * 16, 2, hkv, 128).to(cuda_dev)
+    assert torch.equal(flat_l[slots], flat_p[pslots])
+    assert flat_l[slots].abs().sum().item() > 0

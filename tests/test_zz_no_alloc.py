@@ -6,6 +6,7 @@ refuse a batch whose partial results do not fit its fixed scratch array.
 This file is collected last so that a run stopping at the first failure has
 already run every other test."""
 import ctypes
+import gc
 import math
 
 import pytest
@@ -81,13 +82,14 @@ def test_noalloc_decode_matches_workspace_path_twice(cuda_dev):
         # scratch array); the calls after it must not change the device's free memory at all
         assert _call(fn, q, outs[0], arena, 1, hq, hkv, bt, sl, scale, splits) == 0
         torch.cuda.synchronize()
+        gc.collect()  # tensors left by earlier tests must not be freed inside the measured window
         free0 = torch.cuda.mem_get_info(cuda_dev)[0]
         alloc0 = torch.cuda.memory_allocated(cuda_dev)
         for out in outs[1:]:  # the same shape twice, over the previous call's scratch contents
             assert _call(fn, q, out, arena, 1, hq, hkv, bt, sl, scale, splits) == 0
         torch.cuda.synchronize()
-        assert torch.cuda.mem_get_info(cuda_dev)[0] == free0
-        assert torch.cuda.memory_allocated(cuda_dev) == alloc0
+        assert torch.cuda.mem_get_info(cuda_dev)[0] >= free0  # the driver handed out nothing
+        assert torch.cuda.memory_allocated(cuda_dev) <= alloc0  # nor did torch's allocator
         for out in outs:
             _close(out, want)
         assert torch.equal(outs[1], outs[2])  # deterministic over reused scratch
