@@ -69,8 +69,11 @@ GemmArgs base_args(const at::Tensor& a, const at::Tensor& w, const c10::optional
   return g;
 }
 
-KVArenaView arena_view(const at::Tensor& arena, int64_t layer) {
-  TORCH_CHECK(arena.is_cuda() && arena.scalar_type() == at::kBFloat16 && arena.dim() == 6 && arena.is_contiguous(),
+// `host_ok`: the arena may be pinned host memory, which the GPU reaches through its unified
+// address (the kernel-side write-behind of decode K/V into the host tier).
+KVArenaView arena_view(const at::Tensor& arena, int64_t layer, bool host_ok = false) {
+  TORCH_CHECK((arena.is_cuda() || (host_ok && arena.is_pinned())) && arena.scalar_type() == at::kBFloat16 &&
+                  arena.dim() == 6 && arena.is_contiguous(),
               "arena must be a contiguous bf16 [blocks, layers, 2, kv_heads, block, 128] tensor");
   TORCH_CHECK(arena.size(5) == 128, "head_dim must be 128");
   check_aligned(arena, "arena");
@@ -198,7 +201,7 @@ void linear_qkv(const at::Tensor& a, const at::Tensor& w, at::Tensor& q_out, con
   g.n_q_heads = static_cast<int>(n_q_heads);
   g.n_kv_heads = static_cast<int>(n_kv_heads);
   if (peer_arena.has_value() && peer_slots.has_value()) {
-    g.peer_kv = arena_view(*peer_arena, layer);
+    g.peer_kv = arena_view(*peer_arena, layer, /*host_ok=*/true);
     TORCH_CHECK(peer_slots->scalar_type() == at::kLong, "peer_slots int64");
     g.peer_slots = peer_slots->data_ptr<int64_t>();
   }

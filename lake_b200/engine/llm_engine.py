@@ -200,6 +200,13 @@ class LLMEngine:
         self.pool_iface = pool
         prefetch = getattr(pool.agent, "prefetch", None)
         self.scheduler.on_admit = prefetch if callable(prefetch) else None
+        mirror = getattr(pool.agent, "mirror_arena", None)
+        if mirror is not None and self.runner.peer_arena is None and self.tp_world == 1:
+            # the agent's host slab becomes the QKV epilogue's second target (kernel write-behind);
+            # graphs captured before this point do not write it and are dropped
+            self.runner.mirror_arena = mirror
+            self.runner.graphs.clear()
+            self.runner.graph_launches.clear()
 
     def abort(self, rid: str) -> bool:
         return self.scheduler.abort(rid)

@@ -66,6 +66,9 @@ class ModelRunner:
         self.h_i64 = torch.zeros(2 * max_tokens + max_samples, dtype=torch.int64, pin_memory=pin)
         self.peer_off = max_tokens + max_samples
         self.peer_arena: torch.Tensor | None = None  # decode instance's arena (IPC-mapped) for fused P->D
+        # host tier slab (pinned, device-mapped) the QKV epilogue also writes decode K/V into, page by
+        # page as `req.mirror_blocks` names them: the D -> pool write-behind done by the kernel
+        self.mirror_arena: torch.Tensor | None = None
         # sampled ids come back through two pinned buffers (one step may be in flight while the
         # previous one is read); d_prev keeps the last step's ids on the device for the next
         # step's PENDING inputs (overlapped scheduling)
@@ -110,7 +113,7 @@ class ModelRunner:
             n_decode=nd, prefill_tiles=self._v(d, "tiles", ntiles * 4, (ntiles, 4)),
             query_start=self._v(d, "qstart", s + 1),
             sample_rows=d64[self.max_tokens: self.max_tokens + nrows], bitmask=bitmask,
-            peer_arena=self.peer_arena if peer else None,
+            peer_arena=(self.peer_arena if self.peer_arena is not None else self.mirror_arena) if peer else None,
             peer_slots=d64[self.peer_off:self.peer_off + t] if peer else None, decode_splits=splits)
 
     # ------------------------------------------------------------ host packing
@@ -129,6 +132,7 @@ class ModelRunner:
         slots = self.np_i64[: self.max_tokens]
         rows = self.np_i64[self.max_tokens: self.max_tokens + self.max_samples]
         pslots = self.np_i64[self.peer_off:]
+        mirror = self.mirror_arena is not None and self.peer_arena is None
         self.has_peer = False
         self.has_pending = False
         row = 0
@@ -158,11 +162,18 @@ class ModelRunner:
                 blk = np.asarray(req.block_ids, dtype=np.int64)
                 slots[row:row + n] = blk[pr // bs] * bs + pr % bs
             rb = req.remote_blocks
+            mb = req.mirror_blocks if mirror else None
             if rb is not None:
                 self.has_peer = True
                 pr = np.arange(p0, p0 + n, dtype=np.int64)
                 rbk = np.asarray(rb, dtype=np.int64)
                 pslots[row:row + n] = rbk[pr // bs] * bs + pr % bs
+            elif mb:
+                self.has_peer = True
+                for j in range(n):  # rows of pages the agent gave a host slot
+                    pg = (p0 + j) // bs
+                    sl = mb.get(pg)
+                    pslots[row + j] = sl * bs + (p0 + j) % bs if sl is not None else -1
             else:
                 pslots[row:row + n] = -1
             nb = len(req.block_ids)
@@ -191,6 +202,7 @@ class ModelRunner:
                     ids[row] = 0
                     pos[row] = 0
                     slots[row] = -1
+                    pslots[row] = -1
                     lens[s] = 0
                     qst[s] = row
                     rows[nrows] = row
@@ -198,6 +210,8 @@ class ModelRunner:
                     row += 1
                     s += 1
         qst[s] = row
+        if mirror and pad_decode_to:
+            self.has_peer = True  # the captured graph always reads the slot list (-1: no host copy)
         pad = -row % self.row_multiple
         if pad:  # rows outside every sequence: no KV write, never sampled
             ids[row:row + pad] = 0
@@ -241,10 +255,13 @@ class ModelRunner:
             return g
         splits = self._splits(bucket)
         t = bucket + (-bucket) % self.row_multiple  # rows as _pack pads them (tensor parallel)
-        batch = self._batch_views(t, bucket, 0, bucket, bucket, splits)
+        mirror = self.mirror_arena is not None and self.peer_arena is None
+        batch = self._batch_views(t, bucket, 0, bucket, bucket, splits, peer=mirror)
         # the captured replay must see valid metadata: zero-length padding sequences
         self.d_i32.zero_()
         self.d_i64[:t].fill_(-1)
+        if mirror:
+            self.d_i64[self.peer_off:self.peer_off + t].fill_(-1)
         self.d_i64[self.max_tokens:self.max_tokens + bucket].copy_(torch.arange(bucket, device=self.device))
         # the warm-up forwards overwrite d_prev, which may hold the in-flight step's sampled ids
         # (overlapped scheduling, graph captured on first use): keep them
@@ -308,7 +325,7 @@ class ModelRunner:
         t, s, ntiles, nrows, nd_eff = self._pack(out, pad_decode_to=bucket or 0)
         if not self.cuda:
             self._copy_cpu(t, s, nrows)
-            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, 1, bitmask, has_remote)
+            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, 1, bitmask, has_remote or self.has_peer)
             toks = self._forward(batch, self.has_pending)
             return ("cpu", toks[: sum(c.n_samples for c in out.chunks)].tolist())
         graph = None
@@ -324,7 +341,8 @@ class ModelRunner:
             graph.replay()
             ops.core.LAUNCHES[0] += self.graph_launches[bucket]
         else:
-            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, self._splits(nd_eff), bitmask, has_remote)
+            batch = self._batch_views(t, s, ntiles, nrows, nd_eff, self._splits(nd_eff), bitmask,
+                                      has_remote or self.has_peer)
             toks = self._forward(batch, self.has_pending)
         if ev1 is not None:
             ev1.record()

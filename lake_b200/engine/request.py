@@ -48,6 +48,9 @@ class Request:
     exec_mode: str = "colocated"
     # pages of this request's KV in a decode instance's arena (prefill side of PD-split)
     remote_blocks: list[int] | None = None
+    # page index -> host tier slot the QKV epilogue also writes this page's K/V into (the kernel
+    # side of the D -> pool write-behind; set by the storage agent)
+    mirror_blocks: dict | None = None
     meta: dict = field(default_factory=dict)
 
     @property

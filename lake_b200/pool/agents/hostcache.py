@@ -15,6 +15,15 @@ HBM eviction: before the block pool hands out a cached page again, the
 compute stream waits for that page's write-behind copy (if still in flight).
 L1 itself is an LRU over pinned slots; its evictions are counted.
 
+Kernel write-behind (mirror=True, the default for non-prefill instances): the
+L1 slab is also the QKV epilogue's second KV target. Before each step the agent
+gives every page of generated tokens that the step writes a reserved L1 slot
+(`req.mirror_blocks`); the epilogue stores those rows' K/V into host memory as
+it produces them (through the slab's device-mapped address), so when the
+request finishes its decode-extended pages are already in L1 and are only
+registered, not copied. Prompt pages (and the page shared by the prompt's end
+and the first generated tokens) still take the copy at finish.
+
 Reference parity: the L0<->L1 promote/demote path of
 rust/tiered-store/src/engine.rs:495-606 and the SGLang-style host cache the
 reference's engine targets (python/lake/engine/agent.py:15-41 contract).
@@ -31,7 +40,7 @@ from ..types import FinishRequest, PreparePlan, ReadyHandle, StepStats
 
 
 class HostCacheAgent:
-    def __init__(self, engine, l1_blocks: int, node_id: str = "node-0"):
+    def __init__(self, engine, l1_blocks: int, node_id: str = "node-0", mirror: bool = True):
         self.eng = engine
         self.node_id = node_id
         self.bs = engine.ec.block_size
@@ -39,16 +48,34 @@ class HostCacheAgent:
         self.page_elems = arena[0].numel()
         cuda = arena.is_cuda
         self.l1 = torch.empty(l1_blocks, self.page_elems, dtype=arena.dtype, pin_memory=cuda)
+        # the slab as a KV arena: the QKV epilogue's host-side write-behind target
+        self.mirror_arena = self.l1.view(l1_blocks, *arena.shape[1:]) if mirror else None
+        self.reserved: set[int] = set()  # slots a running request's epilogue is writing into
         self.slot_of: OrderedDict[bytes, int] = OrderedDict()  # LRU: oldest first
         self.free_slots = list(range(l1_blocks - 1, -1, -1))
         self.pending: dict[int, torch.cuda.Event] = {}  # device page -> write-behind copy event
         self.stream = torch.cuda.Stream(arena.device) if cuda else None
         self.stats = {"writeback_blocks": 0, "promoted_blocks": 0, "l1_evictions": 0, "evict_waits": 0,
-                      "writeback_ms": 0.0, "promote_ms": 0.0}
+                      "writeback_ms": 0.0, "promote_ms": 0.0, "kernel_written_blocks": 0, "copied_blocks": 0,
+                      "mirror_slots_short": 0}
         engine.pool.on_evict = self._on_evict
         self._ready: int | None = None
 
     # ------------------------------------------------------------ L1 slots
+    def _take_slot(self) -> int | None:
+        """A slot outside the LRU (free, else the LRU's oldest); None when every slot is reserved."""
+        if self.free_slots:
+            return self.free_slots.pop()
+        if self.slot_of:
+            _, s = self.slot_of.popitem(last=False)
+            self.stats["l1_evictions"] += 1
+            return s
+        return None
+
+    def _release(self, slot: int) -> None:
+        self.reserved.discard(slot)
+        self.free_slots.append(slot)
+
     def _slot_for(self, h: bytes) -> int:
         s = self.slot_of.get(h)
         if s is not None:
@@ -81,9 +108,28 @@ class HostCacheAgent:
         n_full = min(req.num_computed, len(toks)) // self.bs
         hashes = chain_block_hashes(toks[: n_full * self.bs], self.bs, full_only=True)
         pages = req.meta.get("final_block_ids") or req.block_ids
-        todo = [(h, p) for h, p in zip(hashes, pages) if h not in self.slot_of]
+        mirrored = req.mirror_blocks or {}
+        req.mirror_blocks = None
+        todo = []
+        for i, (h, p) in enumerate(zip(hashes, pages)):
+            slot = mirrored.pop(i, None)
+            if h in self.slot_of:  # another request's copy is already in L1
+                if slot is not None:
+                    self._release(slot)
+                self.slot_of.move_to_end(h)
+                continue
+            if slot is not None:  # written by the QKV epilogue as it was produced: register only
+                self.reserved.discard(slot)
+                self.slot_of[h] = slot
+                self.stats["kernel_written_blocks"] += 1
+            else:
+                todo.append((h, p))
+        for slot in mirrored.values():  # pages that never filled up
+            self._release(slot)
+        self.stats["writeback_blocks"] += len(hashes) - len(todo)
         if not todo:
             return
+        self.stats["copied_blocks"] += len(todo)
         if self.stream is None:
             for h, p in todo:
                 self.l1[self._slot_for(h)].copy_(self._page(p))
@@ -135,7 +181,31 @@ class HostCacheAgent:
         return len(todo)
 
     # ------------------------------------------------------------ fences (pages are the engine's)
+    def _reserve_mirror_pages(self, plan: PreparePlan) -> None:
+        """Give each page of generated tokens this step writes a reserved L1 slot, so the QKV
+        epilogue stores its K/V into host memory as well."""
+        reqs = self.eng.requests
+        for io in plan.write_set:
+            req = reqs.get(io.req_id)
+            if req is None or io.token_end <= io.token_start:
+                continue
+            first = -(-len(req.prompt) // self.bs)  # the first page that holds generated tokens only
+            for pg in range(max(first, io.token_start // self.bs), (io.token_end - 1) // self.bs + 1):
+                mb = req.mirror_blocks
+                if mb is None:
+                    mb = req.mirror_blocks = {}
+                if pg in mb:
+                    continue
+                slot = self._take_slot()
+                if slot is None:
+                    self.stats["mirror_slots_short"] += 1  # the page is copied at finish instead
+                    break
+                mb[pg] = slot
+                self.reserved.add(slot)
+
     def prepare_step(self, plan: PreparePlan) -> ReadyHandle:
+        if self.mirror_arena is not None and self.eng.runner.mirror_arena is self.mirror_arena:
+            self._reserve_mirror_pages(plan)
         self._ready = plan.step_id
         stats = {io.req_id: StepStats() for io in plan.write_set}
         return ReadyHandle(plan.step_id, stats, list(plan.read_set), list(plan.write_set), {}, {})

@@ -154,6 +154,33 @@ def test_host_cache_agent_writeback_and_promote():
     assert got == ref.generate([follow], max_new_tokens=4)[0]
 
 
+def test_kernel_write_behind_of_decode_pages():
+    """Decode-extended pages reach the host tier through the QKV epilogue's second KV target
+    (reserved L1 slots written as the tokens are produced), not a copy at finish: a later turn
+    promoted from those slots produces the same tokens as an engine that recomputes everything."""
+    from lake_b200.pool.agents.hostcache import HostCacheAgent
+    from lake_b200.pool.pool_iface import PoolIface
+
+    rng = np.random.default_rng(5)
+    first = rng.integers(0, 1024, 40).tolist()
+    eng = LLMEngine("tiny", device="cpu", max_running=2, max_batched_tokens=128, max_model_len=512, num_blocks=24)
+    agent = HostCacheAgent(eng, l1_blocks=64)
+    eng.attach_pool(PoolIface(agent))
+    assert eng.runner.mirror_arena is agent.mirror_arena
+    out1 = eng.generate([first], max_new_tokens=60)[0]
+    # 40 prompt + 60 generated tokens: pages 3, 4 and 5 hold generated tokens only and are full
+    assert agent.stats["kernel_written_blocks"] == 3
+    assert agent.stats["copied_blocks"] == 3  # prompt pages 0-2 (page 2 also holds generated tokens)
+    assert not agent.reserved  # the unfinished page's slot went back
+    for p in [rng.integers(0, 1024, 150).tolist() for _ in range(2)]:
+        eng.generate([p], max_new_tokens=2)  # push the first request's pages out of HBM
+    follow = first + out1 + rng.integers(0, 1024, 7).tolist()
+    got = eng.generate([follow], max_new_tokens=5)[0]
+    assert agent.stats["promoted_blocks"] >= 5
+    ref = LLMEngine("tiny", device="cpu", max_running=2, max_batched_tokens=128, max_model_len=512, num_blocks=64)
+    assert got == ref.generate([follow], max_new_tokens=5)[0]
+
+
 def _overlap_run(overlap, num_blocks, eos=None, max_new=24):
     import random
 

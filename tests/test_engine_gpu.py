@@ -133,3 +133,31 @@ def test_engine_fp8_weights_match_dequantized_oracle(cuda_dev):
                                                    for k, v in eng.model.w.items()})
     for p, o in zip(prompts, outs):
         _check_tokens(oracle, p, o)
+
+
+def test_kernel_write_behind_with_graph_decode(cuda_dev):
+    """On the GPU the QKV epilogue (eager and graph-replayed decode steps) writes generated
+    tokens' K/V into the pinned host tier through its device-mapped address; a later turn
+    promoted from those pages decodes the same tokens as an engine without the tier."""
+    import numpy as np
+
+    from lake_b200.pool.agents.hostcache import HostCacheAgent
+    from lake_b200.pool.pool_iface import PoolIface
+
+    rng = np.random.default_rng(9)
+    first = rng.integers(0, 2048, 40).tolist()
+    eng = LLMEngine("tiny-gpu", device="cuda:0", max_running=4, max_batched_tokens=256, max_model_len=1024,
+                    num_blocks=40)
+    agent = HostCacheAgent(eng, l1_blocks=128)
+    eng.attach_pool(PoolIface(agent))
+    eng.runner.capture_graphs()
+    out1 = eng.generate([first], max_new_tokens=60)[0]
+    assert agent.stats["kernel_written_blocks"] == 3 and not agent.reserved
+    for p in [rng.integers(0, 2048, 200).tolist() for _ in range(3)]:
+        eng.generate([p], max_new_tokens=2)
+    follow = first + out1 + rng.integers(0, 2048, 9).tolist()
+    got = eng.generate([follow], max_new_tokens=6)[0]
+    assert agent.stats["promoted_blocks"] >= 5
+    ref = LLMEngine("tiny-gpu", device="cuda:0", max_running=4, max_batched_tokens=256, max_model_len=1024,
+                    num_blocks=128, use_cuda_graphs=False)
+    assert got == ref.generate([follow], max_new_tokens=6)[0]
