@@ -13,8 +13,11 @@ roles here; on N GPUs sessions stick to a replica by session id).
 
 Reported: output tok/s over the whole workload (device time of the engine
 steps, and wall time of the public-API loop), TTFT p50 per turn, prompt
-tokens computed vs reused, L0 hits / L1 promotions, and the same workload
-with prefix reuse disabled as the no-reuse baseline.
+tokens computed vs reused, L0 hits / L1 promotions, D -> pool and pool -> P
+GB/s, L1 spills, pages written into L1 by the QKV epilogue vs copied at finish,
+and (with --durable-blocks) the L2 durable tier's PutEnd commits and L2
+promotions; and the same workload with prefix reuse disabled as the no-reuse
+baseline.
 
     python -m lake_b200.bench.agent                     # 1 GPU
     torchrun --nproc-per-node N -m lake_b200.bench.agent
@@ -43,9 +46,15 @@ def run(args, device, rank, reuse: bool):
     eng = LLMEngine(args.model, device=device, max_running=args.sessions, max_batched_tokens=args.budget,
                     max_model_len=max_len, num_blocks=args.hbm_blocks, enable_prefix_cache=reuse,
                     use_cuda_graphs=True, seed=args.seed)
-    agent = None
+    agent = tier = None
     if reuse:
-        agent = HostCacheAgent(eng, args.l1_blocks)
+        if args.durable_blocks:
+            from lake_b200.pool.agents.durable import DurableTier
+
+            page_bytes = eng.arena[0].numel() * eng.arena.element_size()
+            tier = DurableTier(args.model, page_bytes, eng.cfg.n_layers, eng.ec.block_size,
+                               l2_blocks=args.durable_blocks, storage_dir=args.durable_dir)
+        agent = HostCacheAgent(eng, args.l1_blocks, mirror=not args.no_kernel_writeback, durable=tier)
         eng.attach_pool(PoolIface(agent))
     rng = np.random.default_rng(args.seed * 100 + rank)
     vocab = eng.cfg.vocab
@@ -108,6 +117,14 @@ def run(args, device, rank, reuse: bool):
            "h2d_bytes": eng.runner.h2d_bytes, "d2h_bytes": eng.runner.d2h_bytes}
     if agent is not None:
         res.update({k: (round(v, 2) if isinstance(v, float) else v) for k, v in agent.stats.items()})
+        page = eng.arena[0].numel() * eng.arena.element_size()
+        res["d2pool_gbs"] = round(agent.stats["writeback_blocks"] * page / wall / 1e9, 3)  # D -> pool
+        res["d2p_gbs"] = round(agent.stats["promoted_blocks"] * page / wall / 1e9, 3)  # pool -> P
+        res["l1_spills"] = agent.stats["l1_evictions"]
+    if tier is not None:
+        tier.flush()
+        res.update({f"durable_{k}": (round(v, 2) if isinstance(v, float) else v) for k, v in tier.stats.items()})
+        tier.close()
     eng.runner.time_device = False
     del eng
     torch.cuda.empty_cache()
@@ -125,6 +142,11 @@ def main():
     ap.add_argument("--budget", type=int, default=8192)
     ap.add_argument("--hbm-blocks", type=int, default=12000, help="HBM KV cap in 16-token pages")
     ap.add_argument("--l1-blocks", type=int, default=16000, help="pinned host DRAM pages")
+    ap.add_argument("--durable-blocks", type=int, default=0,
+                    help="L2 pages of the durable tier behind L1 (PutEnd, fdatasync'd records); 0 = off")
+    ap.add_argument("--durable-dir", default=None, help="directory of the durable tier's segment files")
+    ap.add_argument("--no-kernel-writeback", action="store_true",
+                    help="copy decode pages to L1 at finish instead of writing them from the QKV epilogue")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-baseline", action="store_true")
     args = ap.parse_args()

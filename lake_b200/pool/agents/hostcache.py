@@ -40,7 +40,7 @@ from ..types import FinishRequest, PreparePlan, ReadyHandle, StepStats
 
 
 class HostCacheAgent:
-    def __init__(self, engine, l1_blocks: int, node_id: str = "node-0", mirror: bool = True):
+    def __init__(self, engine, l1_blocks: int, node_id: str = "node-0", mirror: bool = True, durable=None):
         self.eng = engine
         self.node_id = node_id
         self.bs = engine.ec.block_size
@@ -51,26 +51,52 @@ class HostCacheAgent:
         # the slab as a KV arena: the QKV epilogue's host-side write-behind target
         self.mirror_arena = self.l1.view(l1_blocks, *arena.shape[1:]) if mirror else None
         self.reserved: set[int] = set()  # slots a running request's epilogue is writing into
+        # optional durable tier (durable.DurableTier): finished pages are committed to L2 with
+        # PutEnd in the background; their slots stay pinned until their bytes are taken
+        self.durable = durable
+        self.pinned: dict[int, int] = {}
+        self._pin_lock = __import__("threading").Lock()
         self.slot_of: OrderedDict[bytes, int] = OrderedDict()  # LRU: oldest first
         self.free_slots = list(range(l1_blocks - 1, -1, -1))
         self.pending: dict[int, torch.cuda.Event] = {}  # device page -> write-behind copy event
         self.stream = torch.cuda.Stream(arena.device) if cuda else None
         self.stats = {"writeback_blocks": 0, "promoted_blocks": 0, "l1_evictions": 0, "evict_waits": 0,
                       "writeback_ms": 0.0, "promote_ms": 0.0, "kernel_written_blocks": 0, "copied_blocks": 0,
-                      "mirror_slots_short": 0}
+                      "mirror_slots_short": 0, "l2_promoted_blocks": 0, "pinned_skips": 0}
         engine.pool.on_evict = self._on_evict
         self._ready: int | None = None
 
     # ------------------------------------------------------------ L1 slots
-    def _take_slot(self) -> int | None:
-        """A slot outside the LRU (free, else the LRU's oldest); None when every slot is reserved."""
-        if self.free_slots:
-            return self.free_slots.pop()
-        if self.slot_of:
-            _, s = self.slot_of.popitem(last=False)
+    def _evict_lru(self) -> int | None:
+        """Take the oldest L1 entry whose slot is not pinned by a durable commit in flight."""
+        with self._pin_lock:
+            pinned = set(self.pinned)
+        for h, s in self.slot_of.items():
+            if s in pinned:
+                self.stats["pinned_skips"] += 1
+                continue
+            del self.slot_of[h]
             self.stats["l1_evictions"] += 1
             return s
         return None
+
+    def _take_slot(self) -> int | None:
+        """A slot outside the LRU (free, else the LRU's oldest unpinned); None when none is left."""
+        if self.free_slots:
+            return self.free_slots.pop()
+        return self._evict_lru()
+
+    def _pin(self, slot: int) -> None:
+        with self._pin_lock:
+            self.pinned[slot] = self.pinned.get(slot, 0) + 1
+
+    def _unpin(self, slot: int) -> None:
+        with self._pin_lock:
+            n = self.pinned.get(slot, 0) - 1
+            if n > 0:
+                self.pinned[slot] = n
+            else:
+                self.pinned.pop(slot, None)
 
     def _release(self, slot: int) -> None:
         self.reserved.discard(slot)
@@ -81,11 +107,9 @@ class HostCacheAgent:
         if s is not None:
             self.slot_of.move_to_end(h)
             return s
-        if self.free_slots:
-            s = self.free_slots.pop()
-        else:
-            _, s = self.slot_of.popitem(last=False)
-            self.stats["l1_evictions"] += 1
+        s = self._take_slot()
+        if s is None:
+            raise RuntimeError("host tier: every L1 slot is reserved or pinned")
         self.slot_of[h] = s
         return s
 
@@ -111,6 +135,7 @@ class HostCacheAgent:
         mirrored = req.mirror_blocks or {}
         req.mirror_blocks = None
         todo = []
+        kernel_written = 0
         for i, (h, p) in enumerate(zip(hashes, pages)):
             slot = mirrored.pop(i, None)
             if h in self.slot_of:  # another request's copy is already in L1
@@ -121,14 +146,38 @@ class HostCacheAgent:
             if slot is not None:  # written by the QKV epilogue as it was produced: register only
                 self.reserved.discard(slot)
                 self.slot_of[h] = slot
-                self.stats["kernel_written_blocks"] += 1
+                kernel_written += 1
             else:
                 todo.append((h, p))
         for slot in mirrored.values():  # pages that never filled up
             self._release(slot)
-        self.stats["writeback_blocks"] += len(hashes) - len(todo)
-        if not todo:
+        self.stats["kernel_written_blocks"] += kernel_written
+        self.stats["writeback_blocks"] += kernel_written
+        ev = None
+        if todo:
+            ev = self._copy_behind(todo)
+        self._commit_durable(req.rid, hashes, ev)
+        self.stats["writeback_ms"] += (time.perf_counter() - t0) * 1000
+
+    def _commit_durable(self, rid: str, hashes: list[bytes], ready) -> None:
+        """Hand the request's full pages (now all in L1) to the durable tier, slots pinned."""
+        if self.durable is None or not hashes:
             return
+        chain = []
+        for h in hashes:
+            slot = self.slot_of.get(h)
+            if slot is None:  # evicted already (L1 smaller than one request): the chain ends here
+                break
+            self._pin(slot)
+            chain.append((h, slot, self.l1[slot].data_ptr(), self.durable.is_durable(h)))
+        if chain and not all(c[3] for c in chain):
+            self.durable.commit(rid, chain, ready, self._unpin)
+        else:
+            for _, slot, _, _ in chain:
+                self._unpin(slot)
+
+    def _copy_behind(self, todo):
+        """Copy the pages device -> L1 (side stream on the GPU); returns the copies' event."""
         self.stats["copied_blocks"] += len(todo)
         if self.stream is None:
             for h, p in todo:
@@ -144,7 +193,7 @@ class HostCacheAgent:
             for _, p in todo:
                 self.pending[p] = ev
         self.stats["writeback_blocks"] += len(todo)
-        self.stats["writeback_ms"] += (time.perf_counter() - t0) * 1000
+        return ev if self.stream is not None else None
 
     # ------------------------------------------------------------ pool -> P
     def prefetch(self, req) -> int:
@@ -156,6 +205,14 @@ class HostCacheAgent:
         todo = []
         for h in hashes[n_local:]:
             s = self.slot_of.get(h)
+            if s is None and self.durable is not None and self.durable.is_durable(h):
+                s = self._take_slot()  # back from L2 (a validated record) into an L1 slot
+                if s is not None and self.durable.read_into(h, self.l1[s].data_ptr()):
+                    self.slot_of[h] = s
+                    self.stats["l2_promoted_blocks"] += 1
+                elif s is not None:
+                    self.free_slots.append(s)
+                    s = None
             if s is None or not pool.can_alloc(1):
                 break
             page = pool.alloc(1)[0]

@@ -181,6 +181,40 @@ def test_kernel_write_behind_of_decode_pages():
     assert got == ref.generate([follow], max_new_tokens=5)[0]
 
 
+def test_host_tier_over_durable_l2_with_putend(tmp_path):
+    """The host-cache agent on the real pool tiers: finished pages are committed in the
+    background with PutEnd to fdatasync'd L2 records and registered with the authority; with an
+    L1 too small to keep them, a later turn promotes them from L2 and decodes the same tokens."""
+    from lake_b200.engine.block_pool import chain_block_hashes
+    from lake_b200.pool.agents.durable import DurableTier
+    from lake_b200.pool.agents.hostcache import HostCacheAgent
+    from lake_b200.pool.pool_iface import PoolIface
+
+    rng = np.random.default_rng(13)
+    first = rng.integers(0, 1024, 72).tolist()
+    eng = LLMEngine("tiny", device="cpu", max_running=2, max_batched_tokens=128, max_model_len=512, num_blocks=24)
+    page_bytes = eng.arena[0].numel() * eng.arena.element_size()
+    tier = DurableTier("tiny", page_bytes, eng.cfg.n_layers, 16, l2_blocks=256, storage_dir=str(tmp_path))
+    agent = HostCacheAgent(eng, l1_blocks=10, durable=tier)
+    eng.attach_pool(PoolIface(agent))
+    out1 = eng.generate([first], max_new_tokens=40)[0]
+    tier.flush()
+    hashes = chain_block_hashes((first + out1)[:6 * 16], 16, full_only=True)
+    r = tier.authority.lookup_prefix("tiny", "", 1, hashes, "node-0")
+    assert r.hit_length == 6 and tier.stats["durable_blocks"] == 6  # 111 tokens with KV: 6 full pages
+    assert all(any(l.tier == 3 for l in b.meta.locations) for b in r.blocks)  # an L2 copy each
+    for p in [rng.integers(0, 1024, 150).tolist() for _ in range(2)]:  # evict HBM and the 10-slot L1
+        eng.generate([p], max_new_tokens=2)
+    tier.flush()
+    assert not agent.pinned
+    follow = first + out1 + rng.integers(0, 1024, 5).tolist()
+    got = eng.generate([follow], max_new_tokens=4)[0]
+    assert agent.stats["l2_promoted_blocks"] > 0 and tier.stats["l2_reads"] > 0
+    ref = LLMEngine("tiny", device="cpu", max_running=2, max_batched_tokens=128, max_model_len=512, num_blocks=64)
+    assert got == ref.generate([follow], max_new_tokens=4)[0]
+    tier.close()
+
+
 def _overlap_run(overlap, num_blocks, eos=None, max_new=24):
     import random
 
