@@ -56,6 +56,9 @@ def parse():
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--running", type=int, default=256)
     ap.add_argument("--budget", type=int, default=8192)
+    ap.add_argument("--itl-ms", type=float, default=45.0,
+                    help="inter-token latency target of single-rank engines: the prefill share of mixed "
+                         "steps is capped to keep the step period under it (0 = off)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--no-overlap", action="store_true",
@@ -239,7 +242,7 @@ def _make_engine(args, local, max_running, **kw):
     kw.setdefault("spec_tokens", args.spec_tokens)
     return LLMEngine(args.model, device=f"cuda:{local}", max_running=max_running, max_batched_tokens=args.budget,
                      max_model_len=args.input_len + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
-                     seed=args.seed, weight_dtype=args.weights, **kw)
+                     seed=args.seed, weight_dtype=args.weights, itl_target_ms=args.itl_ms, **kw)
 
 
 def run_colocated(args, rank, local, barrier, tp=None, ep=None):
@@ -641,6 +644,7 @@ def main():
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",
                        "arrivals": (f"poisson {args.arrival_rate:g} req/s per request source" if args.arrival_rate
                                     else "closed loop: a new request whenever one finishes (saturated)"),
+                       "itl_target_ms": (args.itl_ms or None) if mode != "pd" and args.tp == 1 and not args.ep else None,
                        "step": ("one decode-instance iteration (prefill instances run continuously)" if mode == "pd"
                                 else "one engine iteration: decode all running + chunked prefill of arrivals")},
             "e2e": {"value": round(e2e, 1), "unit": "output tok/s", "h2d_bytes_per_step": int(sm[3].item()),

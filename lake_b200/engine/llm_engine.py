@@ -55,6 +55,10 @@ class EngineConfig:
     # scheduling and metadata packing hide behind the device. A step's tokens are returned by
     # the following step() call. Not combined with a storage pool or expert parallel.
     overlap: bool = False
+    # Inter-token latency target (ms): the scheduler caps the prefill tokens of mixed steps so
+    # the step period stays under it (wall-clock feedback, so single-rank engines only: ranks of
+    # a TP or EP group must schedule identically). 0 = off.
+    itl_target_ms: float = 0.0
     # Speculative decoding (greedy): up to `spec_tokens` draft tokens per decode request from
     # prompt lookup (an earlier occurrence of the last `spec_ngram` tokens), verified in one
     # chunk per request. Steps with drafts run synchronously (no overlap).
@@ -161,9 +165,11 @@ class LLMEngine:
         else:
             self.arena = torch.zeros(shape, dtype=dtype, device=self.device)
         self.pool = BlockPool(num_blocks, ec.block_size, ec.enable_prefix_cache)
+        single = self.tp_world == 1 and not (ec.ep and ec.ep[1] > 1)
         self.scheduler = Scheduler(self.pool, SchedulerConfig(ec.max_running, ec.max_batched_tokens,
                                                               ec.long_prefill_threshold, ec.max_model_len, maxb,
-                                                              ec.spec_tokens, ec.spec_ngram))
+                                                              ec.spec_tokens, ec.spec_ngram,
+                                                              ec.itl_target_ms if single else 0.0))
         self.runner = ModelRunner(self.model, self.arena, max_tokens, ec.max_running, maxb,
                                   ec.use_cuda_graphs, ec.block_size,
                                   row_multiple=self.tp_world, max_samples=ec.max_running * (1 + ec.spec_tokens))

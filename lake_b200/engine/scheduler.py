@@ -78,6 +78,44 @@ class SchedulerConfig:
     max_blocks_per_seq: int = 512
     spec_tokens: int = 0  # draft tokens per decode request (prompt lookup); 0 = off
     spec_ngram: int = 3
+    # inter-token latency target (ms) for the prefill share of mixed steps; 0 = off
+    itl_target_ms: float = 0.0
+    itl_min_prefill: int = 256
+
+
+class ItlGovernor:
+    """Prefill tokens per step, held so that the step period -- the inter-token latency every
+    running decode request sees -- stays under a target.
+
+    The period is the wall time between consecutive step completions. After a step that ran
+    over the target the prefill cap shrinks by target/period (at most halving per step); after a
+    step whose prefill filled the cap and ran under 90 % of the target, it grows by 10 %. The
+    cap never falls below `min_tokens`, so arrivals keep being admitted, and a completion after
+    an idle gap (no step in flight for over four targets) restarts the measurement. Decode rows
+    are never capped: when decode alone exceeds the target, prefill runs at the floor.
+
+    Reference parity: the ITL objective of docs/features/slo.md:15 (P50 < 50 ms), enforced by the
+    node scheduler's per-step budget (python/lake/runtime/node_scheduler.py:396-430)."""
+
+    def __init__(self, target_ms: float, max_tokens: int, min_tokens: int = 256):
+        self.target = target_ms / 1000.0
+        self.max = max_tokens
+        self.min = min(min_tokens, max_tokens)
+        self.cap = max_tokens
+        self.last: float | None = None
+
+    def observe(self, now: float, prefill_tokens: int) -> None:
+        last, self.last = self.last, now
+        if last is None or now - last > 4 * self.target:
+            return
+        period = now - last
+        if period > self.target:
+            self.cap = max(self.min, int(self.cap * max(0.5, self.target / period)))
+        elif period < 0.9 * self.target and prefill_tokens >= 0.8 * self.cap:
+            self.cap = min(self.max, int(self.cap * 1.1) + 1)
+
+    def idle(self) -> None:
+        self.last = None
 
 
 class Scheduler:
@@ -97,6 +135,8 @@ class Scheduler:
 
             self.drafter = NgramDrafter(self.cfg.spec_ngram, self.cfg.spec_tokens)
         self.spec_stats = {"proposed": 0, "accepted": 0, "verify_chunks": 0}
+        self.itl = (ItlGovernor(self.cfg.itl_target_ms, self.cfg.max_batched_tokens, self.cfg.itl_min_prefill)
+                    if self.cfg.itl_target_ms > 0 else None)
 
     # -------------------------------------------------------------- admission
     def add(self, req: Request) -> None:
@@ -199,6 +239,11 @@ class Scheduler:
                 budget -= 1
         # Pass B: continue chunked prefills
         cap = self.cfg.long_prefill_threshold or budget
+        if self.itl is not None:  # the prefill share of a mixed step, under the latency target
+            if out.decode:
+                budget = min(budget, self.itl.cap)
+            else:
+                self.itl.idle()
         for req in list(self.running):
             if budget <= 0:
                 break
@@ -286,6 +331,8 @@ class Scheduler:
             if ch.draft:  # K/V stays valid for the last token and the accepted drafts
                 req.num_computed = ch.start + len(ch.accepted)
             self._register_full_blocks(req)  # after the append: accepted drafts are in its K/V
+        if self.itl is not None:
+            self.itl.observe(now, sum(c.n for c in out.prefill if not c.draft))
         for req in done:
             self.running.remove(req)
             self._register_full_blocks(req)
@@ -325,6 +372,8 @@ class Scheduler:
         Returns (request, token) for every token applied."""
         applied = []
         done = []
+        if self.itl is not None:
+            self.itl.observe(now, sum(c.n for c in out.prefill))
         it = iter(sampled)
         for ch in out.chunks:
             if not ch.sample:

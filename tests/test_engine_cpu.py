@@ -81,6 +81,62 @@ def test_scheduler_preempts_when_out_of_pages():
     assert preempted, "expected a preemption when pages run out"
 
 
+def test_itl_governor_caps_prefill_of_mixed_steps():
+    """A simulated device whose step time is 10 ms + 0.02 ms per prefill token, under a closed
+    loop (a finished request is replaced at once): with a 30 ms target the prefill share of
+    mixed steps settles near 1000 tokens and steady-state periods stay under the target."""
+    pool = BlockPool(8192, 16)
+    s = Scheduler(pool, SchedulerConfig(max_running=64, max_batched_tokens=4096, max_model_len=4096,
+                                        itl_target_ms=30.0, itl_min_prefill=128))
+    def _fresh(k):  # a distinct prompt (no prefix-cache hits), staggered output lengths
+        return Request(rid=f"r{k}", prompt=[(k * 4099 + t) % 100000 for t in range(2000)],
+                       params=SamplingParams(max_new_tokens=20 + (7 * k) % 41))
+
+    n = 0
+    for _ in range(64):
+        s.add(_fresh(n))
+        n += 1
+    now, periods, caps, pre = 0.0, [], [], []
+    for _ in range(400):
+        o = s.schedule()
+        n_pre = sum(c.n for c in o.prefill)
+        dt = 0.010 + 0.00002 * n_pre
+        now += dt
+        if o.decode:
+            periods.append(dt)
+            caps.append(s.itl.cap)
+            pre.append(n_pre)
+        for _ in s.update(o, [0] * sum(c.sample for c in o.chunks), now):
+            s.add(_fresh(n))
+            n += 1
+    assert max(periods[-200:]) <= 0.0315, max(periods[-200:])
+    assert 700 <= min(caps[-200:]) and max(caps[-200:]) <= 1100, (min(caps[-200:]), max(caps[-200:]))
+    assert sum(pre[-200:]) / 200 > 600  # prefill keeps flowing at the cap
+
+
+def test_itl_governor_restarts_after_idle_gap():
+    from lake_b200.engine.scheduler import ItlGovernor
+
+    g = ItlGovernor(20.0, 4096, 256)
+    g.observe(0.0, 4096)
+    g.observe(0.040, 4096)  # over the target: halves at most
+    assert g.cap == 2048
+    g.observe(10.0, 2048)  # an idle gap: no period measured
+    assert g.cap == 2048
+    g.observe(10.010, 2048)  # under 90 % with the cap filled: grows
+    assert g.cap == int(2048 * 1.1) + 1
+    g.observe(10.020, 10)  # under the target but the cap was not binding: unchanged
+    assert g.cap == int(2048 * 1.1) + 1
+    for k in range(50):
+        g.observe(10.1 + k, 0)
+    g2 = ItlGovernor(20.0, 4096, 256)
+    t = 0.0
+    for _ in range(20):
+        t += 0.060
+        g2.observe(t, 4096)
+    assert g2.cap == 256
+
+
 def test_rope_cache_llama3_scaling_keeps_high_freq():
     plain = ref.rope_cache(16, 500000.0)
     scaled = ref.rope_cache(16, 500000.0, scaling={"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
