@@ -56,9 +56,11 @@ def parse():
     ap.add_argument("--output-len", type=int, default=256)
     ap.add_argument("--running", type=int, default=256)
     ap.add_argument("--budget", type=int, default=8192)
-    ap.add_argument("--itl-ms", type=float, default=45.0,
+    ap.add_argument("--itl-ms", type=float, default=0.0,
                     help="inter-token latency target of single-rank engines: the prefill share of mixed "
-                         "steps is capped to keep the step period under it (0 = off)")
+                         "steps is capped to keep the step period under it (0 = off; under a closed loop "
+                         "at fixed concurrency the cap moves requests from the batch to the queue, so "
+                         "TTFT grows by what TPOT gains)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--no-overlap", action="store_true",
@@ -184,6 +186,7 @@ class Window:
         self.decode_rows = 0
         self.prefill_rows = 0
         self.role = "colocated"
+        self.gap_ms = 0.0  # device idle between consecutive timed steps
 
     def count(self, eng):
         out = eng.last_step
@@ -194,7 +197,8 @@ class Window:
     def diag(self, steps):
         return {"role": self.role, "tokens": self.tokens, "dev_ms": round(self.dev_ms, 2),
                 "wall_ms": round(self.wall_s * 1000, 2), "avg_decode_batch": round(self.decode_rows / max(1, steps), 1),
-                "avg_prefill_tokens": round(self.prefill_rows / max(1, steps), 1)}
+                "avg_prefill_tokens": round(self.prefill_rows / max(1, steps), 1),
+                "idle_between_steps_ms": round(self.gap_ms, 2)}
 
 
 class Arrivals:
@@ -302,6 +306,7 @@ def run_colocated(args, rank, local, barrier, tp=None, ep=None):
     barrier()
     w = Window()
     eng.runner.time_device = True
+    eng.runner._prev_ev1, gap0 = None, eng.runner.gap_ms
     opscore.LAUNCHES[0] = 0
     h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
     torch.cuda.synchronize()
@@ -322,6 +327,7 @@ def run_colocated(args, rank, local, barrier, tp=None, ep=None):
     w.launches = opscore.LAUNCHES[0]
     w.h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
     w.d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
+    w.gap_ms = eng.runner.gap_ms - gap0
     eng.runner.time_device = False
     if counts:
         _latency_stats(eng, t0, t0 + w.wall_s, w)
@@ -400,6 +406,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
         pd.serve_prefill(side, until_mark=1)          # populate + warm-up
         barrier()
         eng.runner.time_device = True
+        eng.runner._prev_ev1, gap0 = None, eng.runner.gap_ms
         opscore.LAUNCHES[0] = 0
         h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
         torch.cuda.synchronize()
@@ -420,6 +427,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
         w.launches = opscore.LAUNCHES[0]
         w.h2d = (eng.runner.h2d_bytes - h2d0) / max(1, args.steps)
         w.d2h = (eng.runner.d2h_bytes - d2h0) / max(1, args.steps)
+        w.gap_ms = eng.runner.gap_ms - gap0
         eng.runner.time_device = False
         barrier()
         pd.serve_prefill(side)                        # until EXIT
@@ -432,6 +440,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
         torch.cuda.synchronize()
         barrier()
         eng.runner.time_device = True
+        eng.runner._prev_ev1, gap0 = None, eng.runner.gap_ms
         opscore.LAUNCHES[0] = 0
         h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
         torch.cuda.synchronize()
@@ -448,6 +457,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
         w.launches = opscore.LAUNCHES[0]
         w.h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
         w.d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
+        w.gap_ms = eng.runner.gap_ms - gap0
         eng.runner.time_device = False
         barrier()
         side.follow()                                 # until EXIT
@@ -491,6 +501,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
     torch.cuda.synchronize()
     barrier()
     eng.runner.time_device = True
+    eng.runner._prev_ev1, gap0 = None, eng.runner.gap_ms
     opscore.LAUNCHES[0] = 0
     h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
     kv0 = side.kv_bytes
@@ -510,6 +521,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
     w.h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
     w.d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
     w.kv_bytes = side.kv_bytes - kv0
+    w.gap_ms = eng.runner.gap_ms - gap0
     eng.runner.time_device = False
     _latency_stats(eng, t0, t0 + w.wall_s, w)
     side.mark(2)

@@ -5,6 +5,9 @@
 #include <torch/extension.h>
 
 #include <cstring>
+#include <mutex>
+#include <utility>
+#include <vector>
 
 #include "../kernels/lakeb_kernels.h"
 
@@ -69,11 +72,44 @@ GemmArgs base_args(const at::Tensor& a, const at::Tensor& w, const c10::optional
   return g;
 }
 
-// `host_ok`: the arena may be pinned host memory, which the GPU reaches through its unified
-// address (the kernel-side write-behind of decode K/V into the host tier).
+// Pinned host ranges registered as KV arenas (register_host_arena). The pinned check runs once,
+// at registration: under CUDA-graph capture the runtime's pointer query is not available, so a
+// per-call is_pinned() would reject the arena inside a captured step.
+std::mutex g_host_mu;
+std::vector<std::pair<uintptr_t, size_t>> g_host_arenas;
+
+void register_host_arena(const at::Tensor& t) {
+  TORCH_CHECK(!t.is_cuda() && t.is_pinned() && t.is_contiguous(), "a host KV arena must be contiguous pinned memory");
+  std::lock_guard<std::mutex> lk(g_host_mu);
+  g_host_arenas.emplace_back(reinterpret_cast<uintptr_t>(t.data_ptr()), t.nbytes());
+}
+
+void unregister_host_arena(const at::Tensor& t) {
+  std::lock_guard<std::mutex> lk(g_host_mu);
+  const auto p = reinterpret_cast<uintptr_t>(t.data_ptr());
+  for (auto it = g_host_arenas.begin(); it != g_host_arenas.end(); ++it)
+    if (it->first == p) {
+      g_host_arenas.erase(it);
+      return;
+    }
+}
+
+bool is_registered_host(const at::Tensor& t) {
+  const auto p = reinterpret_cast<uintptr_t>(t.data_ptr());
+  const size_t n = t.nbytes();
+  std::lock_guard<std::mutex> lk(g_host_mu);
+  for (const auto& r : g_host_arenas)
+    if (p >= r.first && p + n <= r.first + r.second) return true;
+  return false;
+}
+
+// `host_ok`: the arena may be registered pinned host memory, which the GPU reaches through its
+// unified address (the kernel-side write-behind of decode K/V into the host tier).
 KVArenaView arena_view(const at::Tensor& arena, int64_t layer, bool host_ok = false) {
-  TORCH_CHECK((arena.is_cuda() || (host_ok && arena.is_pinned())) && arena.scalar_type() == at::kBFloat16 &&
-                  arena.dim() == 6 && arena.is_contiguous(),
+  TORCH_CHECK(arena.is_cuda() || (host_ok && is_registered_host(arena)),
+              "arena must be device memory (or, as a second K/V target, pinned host memory registered with "
+              "register_host_arena)");
+  TORCH_CHECK(arena.scalar_type() == at::kBFloat16 && arena.dim() == 6 && arena.is_contiguous(),
               "arena must be a contiguous bf16 [blocks, layers, 2, kv_heads, block, 128] tensor");
   TORCH_CHECK(arena.size(5) == 128, "head_dim must be 128");
   check_aligned(arena, "arena");
@@ -673,6 +709,8 @@ PYBIND11_MODULE(LAKEB_MODULE, m) {
   m.def("set_gemm_streamk_mode", [](int64_t mode) { lakeb::set_gemm_streamk_mode(static_cast<int>(mode)); });
   m.def("set_decode_split_mode", [](int64_t mode) { lakeb::set_decode_split_mode(static_cast<int>(mode)); });
   m.def("set_prefill_kernel", [](int64_t mode) { lakeb::set_prefill_kernel(static_cast<int>(mode)); });
+  m.def("register_host_arena", &register_host_arena, "accept this pinned host tensor as a second K/V target");
+  m.def("unregister_host_arena", &unregister_host_arena);
   m.def("gemm_grid", [](int64_t M, int64_t N, int64_t K, int64_t epi, bool w8) {
     return lakeb::gemm_grid(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), static_cast<int>(epi), 0,
                             w8);

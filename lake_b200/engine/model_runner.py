@@ -97,6 +97,8 @@ class ModelRunner:
         self.d2h_bytes = 0
         self.last_device_ms = 0.0
         self.time_device = False
+        self.gap_ms = 0.0  # with time_device: summed device time between consecutive timed steps
+        self._prev_ev1 = None
 
     # ------------------------------------------------------------ views
     def _v(self, buf, name, n=None, shape=None):
@@ -367,6 +369,9 @@ class ModelRunner:
         done.synchronize()
         if ev1 is not None:
             self.last_device_ms = ev0.elapsed_time(ev1)
+            if self._prev_ev1 is not None:  # device time between the previous step's end and this one's start
+                self.gap_ms += max(0.0, self._prev_ev1.elapsed_time(ev0))
+            self._prev_ev1 = ev1
         code = int(hs[0])
         if code:  # a kernel of this step recorded an error: clear the word, fail the step
             ops.core.status_word(self.device).zero_()

@@ -50,6 +50,10 @@ class HostCacheAgent:
         self.l1 = torch.empty(l1_blocks, self.page_elems, dtype=arena.dtype, pin_memory=cuda)
         # the slab as a KV arena: the QKV epilogue's host-side write-behind target
         self.mirror_arena = self.l1.view(l1_blocks, *arena.shape[1:]) if mirror else None
+        if self.mirror_arena is not None and cuda:
+            from ...ops._ext import native
+
+            native().register_host_arena(self.l1)  # checked pinned once, outside any graph capture
         self.reserved: set[int] = set()  # slots a running request's epilogue is writing into
         # optional durable tier (durable.DurableTier): finished pages are committed to L2 with
         # PutEnd in the background; their slots stay pinned until their bytes are taken
