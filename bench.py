@@ -5,6 +5,8 @@ request stream.
     python bench.py --gpus N --steps K --warmup W
     torchrun --nproc-per-node N bench.py --gpus N ...     (N > 1, one rank per GPU)
     python bench.py --impl reference                        (reference arm)
+    python bench.py --impl torch ...                        (library arm: same engine and
+                                                             workload, cuBLAS / SDPA / NCCL ops)
 
 One step = one engine iteration: every running request decodes one token and
 newly arrived requests are prefilled (chunked, decode-first). Before timing,
@@ -50,7 +52,10 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="lakeb", choices=["lakeb", "reference"])
+    ap.add_argument("--impl", default="lakeb", choices=["lakeb", "torch", "reference"],
+                    help="lakeb: this framework; torch: the same engine and workload with library ops "
+                         "(cuBLAS, torch SDPA, NCCL all_reduce, peer page copies); reference: the "
+                         "reference's own code")
     ap.add_argument("--model", default="llama3-8b")
     ap.add_argument("--input-len", type=int, default=2048)
     ap.add_argument("--output-len", type=int, default=256)
@@ -246,7 +251,8 @@ def _make_engine(args, local, max_running, **kw):
     kw.setdefault("spec_tokens", args.spec_tokens)
     return LLMEngine(args.model, device=f"cuda:{local}", max_running=max_running, max_batched_tokens=args.budget,
                      max_model_len=args.input_len + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
-                     seed=args.seed, weight_dtype=args.weights, itl_target_ms=args.itl_ms, **kw)
+                     seed=args.seed, weight_dtype=args.weights, itl_target_ms=args.itl_ms,
+                     model_impl="library" if args.impl == "torch" else "native", **kw)
 
 
 def run_colocated(args, rank, local, barrier, tp=None, ep=None):
@@ -591,7 +597,9 @@ def main():
     tp_groups = None
     if args.tp > 1:
         gid = rank // args.tp
-        tp_groups = [dist.new_group(list(range(g * args.tp, (g + 1) * args.tp)), backend="gloo")
+        # the library model's all_reduce runs on NCCL; the native model's group only exchanges handles
+        tp_groups = [dist.new_group(list(range(g * args.tp, (g + 1) * args.tp)),
+                                    backend="nccl" if args.impl == "torch" else "gloo")
                      for g in range(world // args.tp)]
         tp = (rank % args.tp, args.tp, tp_groups[gid])
     clocks = ClockSampler(visible_gpu_indices(world) if rank == 0 else [])
@@ -665,7 +673,7 @@ def main():
             "ttft_p50_ms": round(p50(ttft) * 1000, 2) if ttft else None,
             "tpot_p50_ms": round(p50(tpot) * 1000, 2) if tpot else None,
             "p2d_kv_gbs": round(kv_gbs, 2) if kv_gbs else None,
-            "clocks": ck, "impl": "lakeb", "busiest_ms_by_role": producer_ms or None, "ranks": ranks,
+            "clocks": ck, "impl": args.impl, "busiest_ms_by_role": producer_ms or None, "ranks": ranks,
         }
         print(json.dumps(line))
         from lake_b200.utils.trace import emit

@@ -59,6 +59,10 @@ class EngineConfig:
     # the step period stays under it (wall-clock feedback, so single-rank engines only: ranks of
     # a TP or EP group must schedule identically). 0 = off.
     itl_target_ms: float = 0.0
+    # "native": this package's kernels; "library": the same model from library ops (cuBLAS, torch
+    # SDPA, NCCL all_reduce, peer page copies; models/library.py), the benchmark comparator.
+    # The library model runs eagerly (no CUDA graphs); with tp its group must be an NCCL group.
+    model_impl: str = "native"
     # Speculative decoding (greedy): up to `spec_tokens` draft tokens per decode request from
     # prompt lookup (an earlier occurrence of the last `spec_ngram` tokens), verified in one
     # chunk per request. Steps with drafts run synchronously (no overlap).
@@ -112,7 +116,19 @@ class LLMEngine:
 
             weights = model if has_checkpoint(model) else None
         init = "zeros" if weights else "random"
-        if ec.tp is not None and ec.tp[1] > 1:
+        if ec.model_impl == "library":
+            from ..models.library import LibraryLM
+
+            tp = ec.tp if ec.tp is not None and ec.tp[1] > 1 else None
+            full = DecoderLM(cfg, "cpu", torch.bfloat16, init="zeros", weights=weights).w if weights else None
+            self.model = LibraryLM(cfg, self.device, dtype, seed=ec.seed, tp=tp, weights=full)
+            ec.use_cuda_graphs = False
+            self._arena_cfg = cfg
+            if tp is not None:
+                self.tp_world = tp[1]
+                max_tokens += tp[1]
+                cfg = self._arena_cfg = _local_kv_cfg(cfg, tp[1])
+        elif ec.tp is not None and ec.tp[1] > 1:
             from ..models.llama_tp import TPDecoderLM
             from ..parallel.tp import TPGroup
 
@@ -148,6 +164,9 @@ class LLMEngine:
                 self.runner = None
                 free, _ = torch.cuda.mem_get_info(self.device)
                 act = max_tokens * (cfg.hidden * 4 + cfg.q_size * 4 + cfg.intermediate * 2) + 2 * 1024**3
+                if ec.model_impl == "library":  # unfused intermediates + the decode batch's gathered K/V
+                    act += max_tokens * cfg.intermediate * 8 + 2 * page_bytes(cfg, ec.block_size) // cfg.n_layers \
+                        * ec.max_running * maxb
                 num_blocks = int((free - act) * ec.kv_mem_fraction) // page_bytes(cfg, ec.block_size)
             else:
                 num_blocks = 256
@@ -273,6 +292,9 @@ class LLMEngine:
             dst += r.remote_blocks[:nb]
             r.meta["peer_copied"] = True
         if not src:
+            return
+        if hasattr(self.model, "copy_pages"):  # library comparator: peer memcpy per page run
+            self.model.copy_pages(self.arena, self.runner.peer_arena, src, dst)
             return
         from .. import ops
 

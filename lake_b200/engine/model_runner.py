@@ -51,6 +51,7 @@ class ModelRunner:
             self.max_splits = max(ops.decode_splits(n, cfg.n_kv_heads // row_multiple, max_blocks_per_seq)
                                   for n in range(1, max_seqs + 1))
         self.ws = model.new_workspace(max_tokens, max_samples, max_seqs, self.max_splits)
+        self.host_meta = getattr(model, "wants_host_meta", False)
         # int32 staging: ids | pos | seq_lens | qstart | tiles | block_tables
         self.max_tiles = max_tokens // 64 + max_seqs
         self._lay = {}
@@ -297,7 +298,7 @@ class ModelRunner:
         """Model forward with the overlapped-scheduling token relay around it: PENDING inputs
         are read from d_prev first, and this step's sampled ids are kept in d_prev after."""
         if resolve:
-            ops.resolve_tokens(batch.input_ids, self.d_prev)
+            (getattr(self.model, "resolve_tokens", None) or ops.resolve_tokens)(batch.input_ids, self.d_prev)
         toks = self.model.forward(batch, self.arena, self.ws)
         n = toks.shape[0]
         if n and self.relay:
@@ -345,6 +346,9 @@ class ModelRunner:
         else:
             batch = self._batch_views(t, s, ntiles, nrows, nd_eff, self._splits(nd_eff), bitmask,
                                       has_remote or self.has_peer)
+            if self.host_meta:
+                batch.host = {"rows": out.num_tokens, "lens": self._v(self.np_i32, "lens", s).tolist(),
+                              "qstart": self._v(self.np_i32, "qstart", s + 1).tolist()}
             toks = self._forward(batch, self.has_pending)
         if ev1 is not None:
             ev1.record()

@@ -56,6 +56,9 @@ class ForwardBatch:
     peer_slots: torch.Tensor | None = None  # [T] int64 slots in the peer arena
     decode_splits: int = 1
     want_logits: bool = False
+    # host copies of the step metadata, for models that need sequence boundaries on the host
+    # (set by the runner when the model asks for them: {"rows", "lens", "qstart"})
+    host: dict | None = None
 
     @property
     def num_tokens(self) -> int:
