@@ -265,24 +265,26 @@ __global__ void __launch_bounds__(kThreads2, 1)
         qkv_head_epilogue(p, tbase, 2 * n_blk, row, row_ok, stage);
         qkv_head_epilogue(p, tbase + 128, 2 * n_blk + 1, row, row_ok, stage);
       } else if constexpr (EPI == kEpiRSPush) {
-        // partial rows of this rank's K-slice go straight to the row's owner (P2P stores over NVLink)
+        // partial rows of this rank's K-slice go straight to the row's owner (P2P stores over
+        // NVLink), staged per warp so each store instruction writes 8 rows x 64 contiguous bytes
         __nv_bfloat16* dst_row = nullptr;
         if (row_ok) {
           const int d = row / p.tp.rows_per_rank;
           const int lr = row - d * p.tp.rows_per_rank;
           dst_row = p.tp.rs_recv[d] + (static_cast<int64_t>(p.tp.rank) * p.tp.rows_per_rank + lr) * p.ldc;
         }
+        uint4* stage = reinterpret_cast<uint4*>(smem + kStageOutOff2 + q * 2048);
 #pragma unroll 1
         for (int c = 0; c < kBN2 / 32; ++c) {
           uint32_t r[32];
           tmem_ld32(tbase + c * 32, r);
           tmem_ld_wait();
           const int col0 = n_blk * kBN2 + c * 32;
-          if (dst_row && col0 < p.N) {
+          if (col0 < p.N) {  // warp-uniform
             float v[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            store32_bf16(dst_row + col0, v);
+            warp_store_rows64(stage, dst_row ? dst_row + col0 : nullptr, v, lane);
           }
         }
       } else if constexpr (EPI == kEpiSwiGLU) {

@@ -90,7 +90,7 @@ __device__ __forceinline__ float block_sum(float x, float* red) {
 }
 
 template <int EPT>
-__global__ void __launch_bounds__(kNormThreads) tp_norm_push_kernel(const TPNormArgs a) {
+__global__ void __launch_bounds__(kNormThreads, 8) tp_norm_push_kernel(const TPNormArgs a) {
   using V = Vec<EPT>;
   __shared__ float red[kNormThreads / 32];
   __shared__ int ok_s;
@@ -111,9 +111,6 @@ __global__ void __launch_bounds__(kNormThreads) tp_norm_push_kernel(const TPNorm
   if (!ok_s) return;
 
   const int col0 = tid * EPT;
-  float w[EPT];
-#pragma unroll
-  for (int c = 0; c < V::kChunks; ++c) load_bf16<V::kChunk>(a.w + col0 + c * V::kChunk, w + c * V::kChunk);
 
   for (int row = blockIdx.x; row < a.rows_per_rank; row += gridDim.x) {
     float v[EPT];
@@ -121,6 +118,7 @@ __global__ void __launch_bounds__(kNormThreads) tp_norm_push_kernel(const TPNorm
 #pragma unroll
     for (int c = 0; c < V::kChunks; ++c) load_bf16<V::kChunk>(hrow + c * V::kChunk, v + c * V::kChunk);
     if (a.recv) {
+#pragma unroll 2
       for (int s = 0; s < a.world; ++s) {
         const __nv_bfloat16* prow =
             a.recv + (static_cast<int64_t>(s) * a.rows_per_rank + row) * a.dim + col0;
@@ -144,7 +142,9 @@ __global__ void __launch_bounds__(kNormThreads) tp_norm_push_kernel(const TPNorm
     const float inv = rsqrtf(block_sum(ss, red) / a.dim + a.eps);
     float y[EPT];
 #pragma unroll
-    for (int j = 0; j < EPT; ++j) y[j] = v[j] * inv * w[j];
+    for (int c = 0; c < V::kChunks; ++c) load_bf16<V::kChunk>(a.w + col0 + c * V::kChunk, y + c * V::kChunk);
+#pragma unroll
+    for (int j = 0; j < EPT; ++j) y[j] *= v[j] * inv;
     const int g = a.rank * a.rows_per_rank + row;
     const int drow = a.row_map ? a.row_map[g] : g;
     if (drow >= 0) {
@@ -187,8 +187,10 @@ __global__ void tp_argmax_combine_kernel(const TPPtrs amax, int world,
 
 }  // namespace
 
+// Up to eight CTAs per SM, so a whole prefill shard's rows are in flight at once (each row is a
+// chain of dependent loads, a block reduction and the pushes: latency-, not bandwidth-bound).
 int tp_norm_grid(int rows_per_rank) {
-  const int g = 2 * 148;
+  const int g = 8 * 148;
   return rows_per_rank < g ? (rows_per_rank > 0 ? rows_per_rank : 1) : g;
 }
 
