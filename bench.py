@@ -18,19 +18,22 @@ the timed steps run the steady state of the serving loop.
 `value` = output tokens / device time of the window, the MAX over every rank of
 its summed per-step device time (CUDA events around each step's kernels): the
 colocated ranks, or under PD-split both the decode ranks (K steps) and the
-prefill ranks (every prefill step they ran inside the same window, which can
-overrun it by up to one prefill step); `e2e.value` = the same tokens / the max
-over ranks of the wall time of the window's public-API `LLMEngine.step()` calls,
-which include scheduling, the pinned host->device copy of each step's metadata
-and the device->host read of the sampled tokens.
+prefill ranks (their device time inside the decode ranks' window: a prefill step
+that straddles an edge of the window counts in proportion to the share of its
+host interval inside it); `e2e.value` = the same tokens / the max over ranks of
+the wall time of the window's public-API `LLMEngine.step()` calls, which include
+scheduling, the pinned host->device copy of each step's metadata and the
+device->host read of the sampled tokens.
 
-PD-split (the default from 2 GPUs): one prefill and one decode instance of N/2
-GPUs each (2 GPUs: 1 + 1; 4: TP2 + TP2; 8: TP4 + TP4, the tensor-parallel
-groups running the fused NVLink collectives). The prefill instance's QKV
-epilogue writes K/V straight into the decode instance's paged arena over NVLink
-(TP rank i into TP rank i). `--tp 1` instead runs single-GPU instances with ~60%
-of the GPUs prefilling (2+2, 5+3; a decode instance fed by several prefill
-instances).
+PD-split (the default from 2 GPUs): single-GPU prefill and decode instances with
+~60% of the GPUs prefilling (2 GPUs: 1 + 1; 4: 2 + 2; 8: 5 + 3, a decode instance
+fed by up to two prefill instances). A prefill instance's QKV epilogue writes K/V
+straight into its decode instance's paged arena over NVLink. `--tp T` runs
+tensor-parallel instances of T GPUs instead (one prefill and one decode instance
+of T GPUs each at N = 2T, the TP groups running the fused NVLink collectives; TP
+rank i stores into TP rank i); measured on 8 B200s, TP4 + TP4 moves fewer tokens
+per GPU than single-GPU instances (a TP4 prefill instance prefills at about half
+the per-GPU rate of a single-GPU one).
 """
 from __future__ import annotations
 
@@ -74,7 +77,7 @@ def parse():
                     help="default: pd for an even number of GPUs >= 2, else colocated")
     ap.add_argument("--tp", type=int, default=0,
                     help="tensor-parallel instance size (pd: prefill and decode instances of this many GPUs; "
-                         "0 = half the GPUs per instance from 4 GPUs up, else 1)")
+                         "0 = 1, single-GPU instances)")
     ap.add_argument("--ep", action="store_true",
                     help="expert parallel (MoE models): over the decode ranks in pd mode, over all ranks colocated")
     ap.add_argument("--weights", choices=["bf16", "fp8"], default="bf16",
@@ -88,6 +91,12 @@ def parse():
                          "(colocated engine or decode instance); 0 = closed loop (saturated)")
     ap.add_argument("--prefill-queue", type=int, default=8,
                     help="pd mode: grants outstanding at a prefill rank (bounds queueing delay)")
+    ap.add_argument("--local-prefill", type=int, default=1,
+                    help="pd mode: a single-GPU decode instance whose prefill partners are saturated "
+                         "prefills new requests itself (1, default) or only queues them (0)")
+    ap.add_argument("--decode-itl-ms", type=float, default=20.0,
+                    help="pd mode: step-period target of single-GPU decode instances that prefill "
+                         "locally (caps the prefill share of their mixed steps)")
     pre, _ = ap.parse_known_args()
     if pre.config:
         from lake_b200.utils.config_files import apply_env, bench_defaults, load_run_config
@@ -192,6 +201,24 @@ class Window:
         self.prefill_rows = 0
         self.role = "colocated"
         self.gap_ms = 0.0  # device idle between consecutive timed steps
+        self.t0 = 0.0      # host clock (time.perf_counter, system-wide monotonic) at the window start
+        self.local_prefills = 0  # PD decode leader: requests it prefilled itself in the window
+        self.steps_log: list[tuple] = []  # prefill ranks: (start, end, device ms, first tokens) per step
+
+    def clip_to(self, w0: float, w1: float) -> None:
+        """Prefill rank under PD-split: keep the part of its work inside the decode ranks' timed
+        window [w0, w1] (host clock). A step that straddles an edge counts its device time in
+        proportion to the share of its host interval inside the window; a step's first tokens
+        count when the step ended inside the window."""
+        busy, toks, end = 0.0, 0, w0
+        for ts, te, dev, ft in self.steps_log:
+            if te > ts:
+                busy += dev * max(0.0, min(te, w1) - max(ts, w0)) / (te - ts)
+            if w0 <= te <= w1:
+                toks += ft
+            end = max(end, min(te, w1))
+        self.dev_ms, self.tokens = busy, toks
+        self.wall_s = max(0.0, end - max(w0, self.t0))
 
     def count(self, eng):
         out = eng.last_step
@@ -200,9 +227,12 @@ class Window:
             self.prefill_rows += sum(c.n for c in out.prefill)
 
     def diag(self, steps):
+        if self.steps_log:  # prefill rank: per prefill step of its own
+            steps = len(self.steps_log)
         return {"role": self.role, "tokens": self.tokens, "dev_ms": round(self.dev_ms, 2),
                 "wall_ms": round(self.wall_s * 1000, 2), "avg_decode_batch": round(self.decode_rows / max(1, steps), 1),
                 "avg_prefill_tokens": round(self.prefill_rows / max(1, steps), 1),
+                "local_prefills": self.local_prefills,
                 "idle_between_steps_ms": round(self.gap_ms, 2)}
 
 
@@ -249,9 +279,10 @@ def _make_engine(args, local, max_running, **kw):
 
     kw.setdefault("overlap", not args.no_overlap)
     kw.setdefault("spec_tokens", args.spec_tokens)
+    kw.setdefault("itl_target_ms", args.itl_ms)
     return LLMEngine(args.model, device=f"cuda:{local}", max_running=max_running, max_batched_tokens=args.budget,
                      max_model_len=args.input_len + args.output_len + 16, use_cuda_graphs=not args.no_graphs,
-                     seed=args.seed, weight_dtype=args.weights, itl_target_ms=args.itl_ms,
+                     seed=args.seed, weight_dtype=args.weights,
                      model_impl="library" if args.impl == "torch" else "native", **kw)
 
 
@@ -392,8 +423,12 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
     ep = (rank - n_p, n_d, ep_group) if (ep_group is not None and role == "decode") else None
     # decode instances overlap host scheduling with the device; prefill instances report each
     # first token as soon as its step completes (overlap would hold it back one long step)
+    # a single-GPU decode instance takes its saturated partners' overflow prefill in mixed steps
+    # whose period the inter-token latency governor holds near --decode-itl-ms
+    args.local_prefill = int(args.local_prefill and T == 1 and ep is None and role == "decode")
     eng = _make_engine(args, local, running, shared_arena=(role == "decode"), tp=tp, ep=ep,
-                       overlap=role == "decode" and not args.no_overlap)
+                       overlap=role == "decode" and not args.no_overlap,
+                       itl_target_ms=args.decode_itl_ms if args.local_prefill else 0.0)
 
     def agree(flag: bool) -> bool:
         # expert-parallel decode ranks step in lockstep: loop conditions are agreed on
@@ -417,19 +452,24 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
         h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
         torch.cuda.synchronize()
         t0 = time.perf_counter()
-        n0 = side.first_tokens
-        acc = {"dev": 0.0}
+        last_ft = [side.first_tokens]
 
         def on_step():
-            acc["dev"] += eng.runner.last_device_ms
+            # (host start, host end, device ms, first tokens) of each prefill step: the window's
+            # device time and tokens are clipped to the decode ranks' window afterwards
+            ft = side.first_tokens
+            w.steps_log.append((side.step_t0, time.perf_counter(), eng.runner.last_device_ms,
+                                ft - last_ft[0] if leader else 0))
+            last_ft[0] = ft
             w.count(eng)
 
         pd.serve_prefill(side, until_mark=2, on_step=on_step)
         torch.cuda.synchronize()
         w.role = "prefill"
+        w.t0 = t0
         w.wall_s = time.perf_counter() - t0
-        w.dev_ms = acc["dev"]
-        w.tokens = side.first_tokens - n0 if leader else 0
+        w.dev_ms = sum(x[2] for x in w.steps_log)
+        w.tokens = sum(x[3] for x in w.steps_log)
         w.launches = opscore.LAUNCHES[0]
         w.h2d = (eng.runner.h2d_bytes - h2d0) / max(1, args.steps)
         w.d2h = (eng.runner.d2h_bytes - d2h0) / max(1, args.steps)
@@ -459,6 +499,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
 
         side.follow(on_step)                          # the timed window (phase 2)
         torch.cuda.synchronize()
+        w.t0 = t0
         w.wall_s = time.perf_counter() - t0
         w.launches = opscore.LAUNCHES[0]
         w.h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
@@ -477,11 +518,21 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
 
     src = Arrivals(args.arrival_rate, args.seed * 1000 + rank + 7)
 
+    side.queue_depth = args.prefill_queue
+
     def top_up():
         # keep the prefill partner's queue short (bounded TTFT) and the decode batch <= running
         while (len(side.pending) < args.prefill_queue * len(side.links) and side.inflight < args.running
                and src.due() > 0):
             if not side.submit(new_prompt(args.input_len), args.output_len):
+                return
+            src.take()
+        # overflow: every prefill partner is saturated and the batch still has room -> prefill here
+        # (colocated on this instance, chunked into its mixed steps under the step-period cap),
+        # one request at a time
+        while (args.local_prefill and side.saturated and side.inflight < args.running and src.due() > 0
+               and not eng.scheduler.waiting and not any(r.is_prefill for r in eng.scheduler.running)):
+            if not side.submit(new_prompt(args.input_len), args.output_len, local=True):
                 return
             src.take()
 
@@ -510,7 +561,7 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
     eng.runner._prev_ev1, gap0 = None, eng.runner.gap_ms
     opscore.LAUNCHES[0] = 0
     h2d0, d2h0 = eng.runner.h2d_bytes, eng.runner.d2h_bytes
-    kv0 = side.kv_bytes
+    kv0, local0 = side.kv_bytes, side.local
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     w.role = "decode"
@@ -522,11 +573,13 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
         w.count(eng)
         top_up()
     torch.cuda.synchronize()
+    w.t0 = t0
     w.wall_s = time.perf_counter() - t0
     w.launches = opscore.LAUNCHES[0]
     w.h2d = (eng.runner.h2d_bytes - h2d0) / args.steps
     w.d2h = (eng.runner.d2h_bytes - d2h0) / args.steps
     w.kv_bytes = side.kv_bytes - kv0
+    w.local_prefills = side.local - local0
     w.gap_ms = eng.runner.gap_ms - gap0
     eng.runner.time_device = False
     _latency_stats(eng, t0, t0 + w.wall_s, w)
@@ -579,11 +632,8 @@ def main():
         if world > 1:
             dist.barrier(group=group)
 
-    if args.tp == 0:  # auto: half the GPUs per PD-split instance (8 GPUs: TP4 prefill + TP4 decode)
+    if args.tp == 0:  # auto: single-GPU instances (the highest tokens per GPU measured)
         args.tp = 1
-        if args.mode in (None, "pd") and not args.ep and world >= 4:
-            while args.tp * 2 <= min(4, world // 2) and world % (args.tp * 2) == 0:
-                args.tp *= 2
     if world % args.tp:
         raise SystemExit("--tp must divide the GPU count")
     mode = args.mode or ("pd" if world // args.tp >= 2 else "colocated")
@@ -614,7 +664,13 @@ def main():
 
     # aggregate over ranks (max of times, sum of counts) through the gloo group. The window's
     # device time is the busiest rank's: decode (or colocated) ranks' K steps, or a prefill rank's
-    # summed step time over the same window (PD-split), whichever is larger.
+    # device time inside the decode ranks' window (PD-split), whichever is larger.
+    if mode == "pd" and world > 1:
+        spans = [None] * world
+        dist.all_gather_object(spans, (role, w.t0, w.t0 + w.wall_s), group=group)
+        dec = [(a, b) for r, a, b in spans if r == "decode"]
+        if role == "prefill" and dec:
+            w.clip_to(min(a for a, _ in dec), max(b for _, b in dec))
     t = torch.tensor([w.dev_ms, w.wall_s * 1000.0, float(w.tokens),
                       w.h2d, w.d2h, float(w.launches), float(w.kv_bytes), w.dev_ms], dtype=torch.float64)
     lat = (w.ttft, w.tpot, w.diag(args.steps))

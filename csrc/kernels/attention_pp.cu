@@ -131,9 +131,26 @@ __device__ __forceinline__ int64_t page_row(const PagedAttnArgs& a, int64_t phys
   return (((phys * a.num_layers + a.layer) * 2 + kv) * a.n_kv_heads + head) * 16;
 }
 
+// Timeline of one CTA (the first launched: the heaviest query tile of head pair 0), recorded by
+// the TRACE variant in SM clock cycles: slot [j * 16 + e] holds event e of K/V tile j (see
+// kTr* below), slot [1023] the CTA's start. Read back with prefill_trace_read().
+constexpr int kTraceSlots = 1024;
+__device__ long long g_pp_trace[kTraceSlots];
+enum : int {
+  kTrMmaP0 = 0,      // MMA issuer: P of head A ready (before PV_A(j))
+  kTrMmaP1 = 1,      // MMA issuer: P of head B ready (before PV_B(j))
+  kTrMmaK = 2,       // MMA issuer: K tile j+1 landed (before S_A(j+1))
+  kTrSmWake = 3,     // softmax head h (+4 for B): S(j) ready
+  kTrSmLoaded = 4,   // scores in registers
+  kTrSmExp = 5,      // P computed, TMEM stores issued
+  kTrSmArrive = 6,   // P handed to the MMA issuer
+  kTrLoadK = 11,     // producer: K stage free for tile j
+  kTrLoadV = 12,     // producer: V stage free for tile j
+};
+
 // EMUL: every EMUL-th pair of probabilities is computed by exp2_poly2 (0: none); INTPACK:
-// pack P to bf16 with integer ops instead of the converter.
-template <int EMUL, bool INTPACK>
+// pack P to bf16 with integer ops instead of the converter; TRACE: record the timeline above.
+template <int EMUL, bool INTPACK, bool TRACE = false>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_pingpong_kernel(const __grid_constant__ CUtensorMap kvmap, const __grid_constant__ CUtensorMap qmap,
                             const PagedAttnArgs a) {
@@ -155,6 +172,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tile_idx = a.num_tiles - 1 - static_cast<int>(blockIdx.x);
   const int4 tile = a.tiles[tile_idx];
   const int seq = tile.x, qrow0 = tile.y, nq = tile.z, pos0 = tile.w;
+  const bool traced = TRACE && blockIdx.x == 0 && blockIdx.y == 0 && (threadIdx.x & 31) == 0;
+  auto tr = [&](int j, int e) {
+    if (traced && j >= 0 && j < kTraceSlots / 16 - 1) g_pp_trace[j * 16 + e] = clock64();
+  };
+  if (traced && threadIdx.x == 0) g_pp_trace[kTraceSlots - 1] = clock64();
   const int qh0 = 2 * static_cast<int>(blockIdx.y);  // heads qh0 (A) and qh0 + 1 (B)
   const int kvh = qh0 / (a.n_q_heads / a.n_kv_heads);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -219,6 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          tr(j, kv ? kTrLoadV : kTrLoadK);
           uint8_t* dst = smem + (kv ? kV : kK) + s * kOperand;
           mbar_expect_tx(full, kOperand);
 #pragma unroll
@@ -274,6 +297,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
+          tr(j, h ? kTrMmaP1 : kTrMmaP0);
           tc_fence_after();
           issue_pv(h, j);
           if (h == 1) umma_commit(&v_empty[s]);
@@ -283,6 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
                 break;
               }
+              tr(j, kTrMmaK);
               tc_fence_after();
             }
             issue_s(h, j + 1);  // after PV(h, j) in issue order: P's columns are read before S overwrites them
@@ -300,6 +325,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int qpos = pos0 + r;
     const int kmax = min(qpos, len - 1);  // last key this row may see
     const float sl2 = a.scale * kLog2e;
+    const bool tw = (warp & 3) == 2;  // warps 2 and 6 record the softmax timeline
+    const int te = h ? 4 : 0;
     float m = -CUDART_INF_F;  // running max in log2 units (the base of P; may trail the true max by < 8)
     float l = 0.f;
     bool ok = true;
@@ -308,6 +335,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         ok = false;
         break;
       }
+      if (tw) tr(j, kTrSmWake + te);
       tc_fence_after();
       // the row's 128 scores: four loads in flight, one wait
       const int k0 = j * kTile;
@@ -316,6 +344,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int c = 0; c < 4; ++c)
         tmem_ld32(t_s[h] + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32 * c));
       tmem_ld_wait();
+      if (tw) tr(j, kTrSmLoaded + te);
       if (k0 + kTile - 1 > kmax) {  // the diagonal or the sequence end: keys past this row's last
 #pragma unroll
         for (int i = 0; i < 128; ++i)
@@ -351,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (k == 31) tmem_st32(t_s[h] + lane_off, *reinterpret_cast<uint32_t(*)[32]>(sv));
       }
       tmem_st32(t_s[h] + lane_off + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      if (tw) tr(j, kTrSmExp + te);
       rs[0] = add2(add2(rs[0], rs[1]), add2(rs[2], rs[3]));
       // O and l still hold sums against the old base: bring them to m (after P, so the 128 scores
       // are no longer live). tcgen05.ld/st are warp-collective: the whole warp rescales when any
@@ -377,6 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[h]);
+      if (tw) tr(j, kTrSmArrive + te);
     }
     if (ok && n_tiles > 0 &&
         __all_sync(0xffffffffu, mbar_wait(&o_done[h], (n_tiles - 1) & 1, abort_flag, a.status))) {
@@ -422,6 +453,7 @@ using PrefillKernel = void (*)(CUtensorMap, CUtensorMap, PagedAttnArgs);
 const PrefillKernel kVariants[] = {
     prefill_pingpong_kernel<0, false>, prefill_pingpong_kernel<0, true>, prefill_pingpong_kernel<4, false>,
     prefill_pingpong_kernel<4, true>,  prefill_pingpong_kernel<3, true>, prefill_pingpong_kernel<2, true>,
+    prefill_pingpong_kernel<0, false, true>,  // 6: default softmax with the timeline recorded
 };
 constexpr int kDefaultVariant = 0;  // measured fastest overall: MUFU exp, converter packing
 int g_variant = kDefaultVariant;
@@ -429,6 +461,11 @@ int g_variant = kDefaultVariant;
 
 void set_prefill_variant(int v) {
   g_variant = (v >= 0 && v < static_cast<int>(sizeof(kVariants) / sizeof(kVariants[0]))) ? v : kDefaultVariant;
+}
+
+int prefill_trace_read(long long* host, int n) {
+  if (n > kTraceSlots) n = kTraceSlots;
+  return cudaMemcpyFromSymbol(host, g_pp_trace, n * sizeof(long long));
 }
 
 int paged_prefill_pingpong(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream) {

@@ -171,6 +171,8 @@ bool prefill_pingpong_ok(const PagedAttnArgs& a);
 int paged_prefill_pingpong(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream);
 void set_prefill_kernel(int mode);  // 1: ping-pong where it applies (default), 0: one head per CTA, 10+i: variant i
 void set_prefill_variant(int v);    // softmax variant of the ping-pong kernel (-1: default)
+// Timeline slots recorded by the traced ping-pong variant (SM clock cycles), copied to host memory.
+int prefill_trace_read(long long* host, int n);
 
 // ----------------------------------------------------------------- misc
 int rmsnorm_bf16(const __nv_bfloat16* x, int64_t sx, const __nv_bfloat16* w, __nv_bfloat16* out, int64_t so, int rows,

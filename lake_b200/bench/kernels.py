@@ -122,6 +122,53 @@ def bench_prefill(t: Timer, out: list):
         out.append(row)
 
 
+def prefill_timeline(t: Timer, out: list):
+    """Per-tile timeline of the two-head prefill kernel's heaviest CTA (4 x 2048 causal, 16 K/V
+    tiles): the traced variant records SM clock cycles at each hand-off (scores ready, scores in
+    registers, P computed, P handed over, MMA issuer sees P / K). Reports the median over the
+    steady-state tiles of each phase."""
+    from ..ops._ext import native
+
+    nseq, new, hq, hkv = 4, 2048, 32, 8
+    nb = (new + 15) // 16
+    arena = torch.randn(nseq * nb + 1, 1, 2, hkv, 16, 128, device="cuda").to(BF)
+    bt = torch.randperm(nseq * nb, device="cuda").view(nseq, nb).to(torch.int32)
+    sl = torch.full((nseq,), new, dtype=torch.int32, device="cuda")
+    qs = [i * new for i in range(nseq + 1)]
+    tiles = ops.build_prefill_tiles(qs, [0] * nseq, device="cuda")
+    q = torch.randn(nseq * new, hq * 128, device="cuda").to(BF)
+    o = torch.empty_like(q)
+    qs_t = torch.tensor(qs, dtype=torch.int32, device="cuda")
+    native().set_prefill_kernel(16)
+    for _ in range(3):
+        ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv, 0.088, out=o)
+    torch.cuda.synchronize()
+    native().set_prefill_kernel(1)
+    tr = native().prefill_trace().tolist()
+    start = tr[1023]
+    ev = [[tr[j * 16 + e] for e in range(16)] for j in range(16)]
+    rows = []
+    for j in range(16):
+        e = ev[j]
+        rows.append(dict(
+            j=j,
+            a_wait_s=e[3] - (ev[j - 1][6] if j else start),  # softmax A idle between tiles
+            a_ld=e[4] - e[3], a_exp=e[5] - e[4], a_st=e[6] - e[5],
+            b_wait_s=e[7] - (ev[j - 1][10] if j else start),
+            b_ld=e[8] - e[7], b_exp=e[9] - e[8], b_st=e[10] - e[9],
+            mma_sees_pA=e[0] - e[6], mma_sees_pB=e[1] - e[10],
+            period=(ev[j][3] - ev[j - 1][3]) if j else None))
+    med = {}
+    for k in rows[0]:
+        if k == "j":
+            continue
+        xs = sorted(r[k] for r in rows[2:14] if r[k] is not None)
+        med[k] = xs[len(xs) // 2]
+    out.append(dict(kernel="prefill_pingpong timeline (cycles, median of tiles 2-13)", **med))
+    for r in rows:
+        out.append(dict(kernel="prefill_pingpong tile", **r))
+
+
 def bench_norm(t: Timer, out: list):
     x = torch.randn(8192, 4096, device="cuda").to(BF)
     w = torch.rand(4096, device="cuda").to(BF)
@@ -287,7 +334,7 @@ def main(argv=None):
     res: list = []
     for name in args.only.split(","):
         {"gemm": bench_gemm, "decode": bench_decode, "prefill": bench_prefill, "norm": bench_norm,
-         "moe": bench_moe, "pd_qkv": bench_pd_qkv}[name](t, res)
+         "moe": bench_moe, "pd_qkv": bench_pd_qkv, "prefill_timeline": prefill_timeline}[name](t, res)
     for r in res:
         print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}))
 

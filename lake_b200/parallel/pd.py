@@ -143,6 +143,7 @@ class DecodeSide:
         # prefilled here instead of on a prefill instance, when its cached share is at least this
         self.direct_min_hit = direct_min_hit
         self.direct = 0
+        self.local = 0  # requests prefilled here because the prefill partners were saturated
         self.links = links  # (to_p, from_p) per prefill partner (the leader's; empty on followers)
         self.ctl = ctl
         self.pending: dict[int, tuple] = {}
@@ -166,18 +167,22 @@ class DecodeSide:
         hashes = chain_block_hashes(prompt, bs, full_only=True)[:(len(prompt) - 1) // bs]
         return self.eng.pool.peek(hashes) * bs
 
-    def submit(self, prompt: list[int], max_new_tokens: int) -> str | None:
+    def submit(self, prompt: list[int], max_new_tokens: int, local: bool = False) -> str | None:
         """Start a request: returns the engine request id it will run under ("pd-N" once its
-        prefill instance reports back, "dd-N" when prefilled here), or None if no pages are free."""
-        if (self.direct_min_hit > 0 and len(prompt) > 1
-                and self.local_hit(prompt) >= self.direct_min_hit * len(prompt)):
+        prefill instance reports back, "dd-N" when prefilled here), or None if no pages are free.
+        `local`: prefill it here in any case (COLOCATED on this instance: its prefill partners
+        are saturated and this instance's chunked mixed steps take the overflow)."""
+        if local:
+            self.local += 1
+        if local or (self.direct_min_hit > 0 and len(prompt) > 1
+                     and self.local_hit(prompt) >= self.direct_min_hit * len(prompt)):
             # D-direct (reference mode selection: local hit -> D_DIRECT): extend the cached prefix here
             rid = f"dd-{self.next_idx}"
             if self.ctl is not None:
                 self.events.append((EV_DIRECT, self.next_idx, max_new_tokens, 0, list(prompt), []))
             self.next_idx += 1
             self.eng.add_request(list(prompt), max_new_tokens, rid=rid)
-            self.direct += 1
+            self.direct += 0 if local else 1
             return rid
         blocks = self.eng.reserve_blocks(len(prompt))
         if self.ctl is not None:
@@ -280,6 +285,13 @@ class DecodeSide:
     def inflight(self) -> int:
         return len(self.pending) + len(self.eng.scheduler.running) + len(self.eng.scheduler.waiting)
 
+    @property
+    def saturated(self) -> bool:
+        """Every prefill partner has at least `queue` grants outstanding (see `queue_depth`)."""
+        return bool(self.links) and min(self.outstanding) >= self.queue_depth
+
+    queue_depth = 8
+
 
 class PrefillSide:
     def __init__(self, eng: LLMEngine, from_d: ShmRing | None, to_d: ShmRing | None, ctl: GroupCtl | None = None):
@@ -291,6 +303,7 @@ class PrefillSide:
         self.first_tokens = 0
         self.events: list[tuple] = []
         self.steps = 0
+        self.step_t0 = 0.0  # host clock (time.perf_counter) when the last step began
 
     @property
     def is_follower(self) -> bool:
@@ -316,6 +329,7 @@ class PrefillSide:
                 self.exit = True
 
     def step(self) -> int:
+        self.step_t0 = time.perf_counter()
         self.poll()
         if self.ctl is not None:
             self.ctl.send(_pack_events(self.events))
@@ -354,6 +368,7 @@ class PrefillSide:
                 self.eng.add_remote_prefill(prompt, blocks, rid=f"pd-{idx}")
             if kind == G_EVENTS:
                 continue
+            self.step_t0 = time.perf_counter()
             self.eng.step()
             self.steps += 1
             if self.eng.device.type == "cuda":

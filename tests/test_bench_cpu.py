@@ -33,6 +33,20 @@ def test_pd_layouts():
     assert b.pd_layout(8, 1, n_experts=8) == (4, 4)  # expert-parallel decode ranks divide the experts
 
 
+def test_prefill_window_clipping():
+    """A prefill rank's device time and first tokens are cut to the decode ranks' window: steps
+    inside count fully, a straddling step by its share of the window, steps after it not at all."""
+    b = _bench()
+    w = b.Window()
+    w.role, w.t0 = "prefill", 10.0
+    # (host start, host end, device ms, first tokens)
+    w.steps_log = [(10.0, 10.1, 90.0, 4), (10.1, 10.2, 95.0, 4), (10.2, 10.4, 180.0, 4), (10.4, 10.5, 90.0, 4)]
+    w.clip_to(10.0, 10.3)
+    assert abs(w.dev_ms - (90.0 + 95.0 + 90.0)) < 1e-6  # half of the 180 ms straddling step
+    assert w.tokens == 8  # the straddling step ended after the window
+    assert abs(w.wall_s - 0.3) < 1e-9
+
+
 def test_sweep_commands():
     from lake_b200.bench import sweep
 

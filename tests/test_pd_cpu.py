@@ -1,7 +1,8 @@
 """PD-split on CPU with two gloo ranks: the prefill rank writes K/V into the
 decode rank's arena (shared /dev/shm mapping standing in for NVLink P2P) and the
 decode rank's tokens must equal a colocated single-process run (the 2-layer
-plumbing model, fp32)."""
+plumbing model, fp32), including a request the decode instance prefills itself
+(overflow of a saturated prefill partner)."""
 import json
 import os
 import random
@@ -39,12 +40,14 @@ def _worker(rank, port, out_dir):
         pd.serve_prefill(side)
     else:
         prompts = _prompts()
-        for p in prompts:
-            assert side.submit(p, 8)
+        # the last request is prefilled on the decode instance itself (overflow while its prefill
+        # partner is saturated): same tokens, no grant
+        rids = [side.submit(p, 8, local=(i == len(prompts) - 1)) for i, p in enumerate(prompts)]
+        assert all(rids) and rids[-1].startswith("dd-") and side.local == 1
         while side.inflight:
             side.poll()
             eng.step()
-        outs = [eng.requests[f"pd-{i}"].output for i in range(len(prompts))]
+        outs = [eng.requests[r].output for r in rids]
         ref = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512, num_blocks=96)
         want = ref.generate(prompts, max_new_tokens=8)
         side.shutdown()

@@ -1,11 +1,17 @@
-"""Tensor parallel over NVLink peer memory on two GPUs.
+"""Tensor parallel over NVLink peer memory on 2, 4 and 8 GPUs (each size runs when the box
+has that many GPUs).
 
 1. Fused collectives vs an fp32 PyTorch reference: row-parallel GEMM whose
    epilogue pushes partial rows to their owners (reduce-scatter), the owner's
    reduce + residual + RMSNorm + all-gather push, and a column-parallel SwiGLU
    GEMM that waits per row shard.
-2. A TP=2 engine generates the same greedy tokens as the TP=1 engine (bf16
-   rounding of the split partial sums may flip a near-tie; >= 90% agreement).
+2. A TP engine generates the same greedy tokens as the TP=1 engine (bf16
+   rounding of the split partial sums may flip a near-tie, after which that
+   sequence diverges: >= 90% agreement at TP=2, >= 80% at TP=4 and 8, where the
+   partial sums are split four and eight ways; the fused-op numerics in 1 are
+   the exactness check).
+   At TP=2 the model is `tiny-gpu`; at TP=4 and 8 it is widened to one KV head
+   per rank (2 query heads, 256 hidden and 256 FFN columns per rank).
 """
 import json
 import os
@@ -73,6 +79,12 @@ def _fused_numerics(rank, world, out):
         out[f"m{M}"] = dict(err_h=err_h, err_y=err_y, err_act=err_act)
 
 
+def _overrides(world):
+    if world == 2:
+        return {}
+    return {"hidden": 256 * world, "n_q_heads": 2 * world, "n_kv_heads": world, "intermediate": 256 * world}
+
+
 def _worker(rank, world, port, out_dir):
     import torch.distributed as dist
 
@@ -88,8 +100,9 @@ def _worker(rank, world, port, out_dir):
     rng = random.Random(5)
     prompts = [[rng.randrange(2048) for _ in range(n)] for n in (7, 64, 150, 33, 1, 90)]
     # decode steps replay CUDA graphs (collective targets device-resident); mixed steps run eagerly
+    ov = _overrides(world)
     eng = LLMEngine("tiny-gpu", device=f"cuda:{rank}", max_running=8, max_batched_tokens=256, max_model_len=1024,
-                    num_blocks=256, use_cuda_graphs=True, tp=(rank, world, None))
+                    num_blocks=256, use_cuda_graphs=True, tp=(rank, world, None), model_overrides=ov)
     eng.runner.capture_graphs()
     outs = eng.generate(prompts, max_new_tokens=8)
     core.check_status()
@@ -97,43 +110,46 @@ def _worker(rank, world, port, out_dir):
     del eng
     # block-scaled fp8 weights under TP (the fp8 kernels' own grids size the counter waits)
     eng8 = LLMEngine("tiny-gpu", device=f"cuda:{rank}", max_running=8, max_batched_tokens=256, max_model_len=1024,
-                     num_blocks=256, use_cuda_graphs=True, tp=(rank, world, None), weight_dtype="fp8")
+                     num_blocks=256, use_cuda_graphs=True, tp=(rank, world, None), weight_dtype="fp8",
+                     model_overrides=ov)
     eng8.runner.capture_graphs()
     res["outs8"] = eng8.generate(prompts, max_new_tokens=8)
     core.check_status()
     del eng8
     if rank == 0:
         want = LLMEngine("tiny-gpu", device="cuda:0", max_running=8, max_batched_tokens=256, max_model_len=1024,
-                         num_blocks=256, use_cuda_graphs=False).generate(prompts, max_new_tokens=8)
+                         num_blocks=256, use_cuda_graphs=False, model_overrides=ov).generate(prompts, max_new_tokens=8)
         res["want"] = want
         res["want8"] = LLMEngine("tiny-gpu", device="cuda:0", max_running=8, max_batched_tokens=256,
                                  max_model_len=1024, num_blocks=256, use_cuda_graphs=False,
-                                 weight_dtype="fp8").generate(prompts, max_new_tokens=8)
+                                 weight_dtype="fp8", model_overrides=ov).generate(prompts, max_new_tokens=8)
     with open(os.path.join(out_dir, f"res{rank}.json"), "w") as f:
         json.dump(res, f)
     dist.barrier()
     dist.destroy_process_group()
 
 
-def test_tp2_fused_collectives_and_engine(tmp_path):
-    if torch.cuda.device_count() < 2:
-        pytest.skip("needs 2 GPUs")
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_fused_collectives_and_engine(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     os.environ["NCCL_NVLS_ENABLE"] = "0"
-    mp.spawn(_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
-    r0 = json.load(open(tmp_path / "res0.json"))
-    r1 = json.load(open(tmp_path / "res1.json"))
-    for r in (r0, r1):
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    rs = [json.load(open(tmp_path / f"res{r}.json")) for r in range(world)]
+    r0 = rs[0]
+    for r in rs:
         for m in ("m300", "m1100"):
             assert r[m]["err_h"] < 0.1, (m, r[m])
             assert r[m]["err_y"] < 0.1, (m, r[m])
             assert r[m]["err_act"] < 3e-2, (m, r[m])
-    assert r0["outs"] == r1["outs"]  # every rank computes the same tokens
+    assert all(r["outs"] == r0["outs"] for r in rs)  # every rank computes the same tokens
     flat_got = [t for o in r0["outs"] for t in o]
     flat_want = [t for o in r0["want"] for t in o]
     agree = sum(a == b for a, b in zip(flat_got, flat_want)) / len(flat_want)
-    assert agree >= 0.9, (agree, r0["outs"], r0["want"])
-    assert r0["outs8"] == r1["outs8"]
+    need = 0.9 if world == 2 else 0.8
+    assert agree >= need, (agree, r0["outs"], r0["want"])
+    assert all(r["outs8"] == r0["outs8"] for r in rs)
     got8 = [t for o in r0["outs8"] for t in o]
     want8 = [t for o in r0["want8"] for t in o]
     agree8 = sum(a == b for a, b in zip(got8, want8)) / len(want8)
-    assert agree8 >= 0.9, (agree8, r0["outs8"], r0["want8"])
+    assert agree8 >= need, (agree8, r0["outs8"], r0["want8"])
