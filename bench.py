@@ -25,10 +25,11 @@ the wall time of the window's public-API `LLMEngine.step()` calls, which include
 scheduling, the pinned host->device copy of each step's metadata and the
 device->host read of the sampled tokens.
 
-PD-split (the default from 2 GPUs): single-GPU prefill and decode instances with
-~60% of the GPUs prefilling (2 GPUs: 1 + 1; 4: 2 + 2; 8: 5 + 3, a decode instance
-fed by up to two prefill instances). A prefill instance's QKV epilogue writes K/V
-straight into its decode instance's paged arena over NVLink. `--tp T` runs
+PD-split (the default from 2 GPUs): single-GPU prefill and decode instances in
+pairs (2 GPUs: 1 + 1; 4: 2 + 2; 8: 4 + 4). A prefill instance's QKV epilogue
+writes K/V straight into its decode instance's paged arena over NVLink; a decode
+instance whose prefill partner is saturated prefills further requests itself in
+mixed steps held near a 20 ms step period (--local-prefill, --decode-itl-ms). `--tp T` runs
 tensor-parallel instances of T GPUs instead (one prefill and one decode instance
 of T GPUs each at N = 2T, the TP groups running the fused NVLink collectives; TP
 rank i stores into TP rank i); measured on 8 B200s, TP4 + TP4 moves fewer tokens
@@ -373,11 +374,14 @@ def run_colocated(args, rank, local, barrier, tp=None, ep=None):
 
 
 def pd_split(world: int, prefill_ranks: int = 0) -> tuple[int, int]:
-    """(prefill, decode) instance counts. Prefill of a 2048-token prompt costs more GPU time
-    than its 256 decode steps at full batch, so ~60% of the GPUs prefill: 1+1, 2+2, 5+3."""
+    """(prefill, decode) instance counts: pairs (1+1, 2+2, 4+4). Prefill of a 2048-token prompt
+    costs more GPU time than its 256 decode steps at full batch, so a decode instance fed by one
+    prefill instance has room left, which it fills with its own prefills of the overflow
+    (--local-prefill); measured on 8 B200s, 5 prefill + 3 decode instances without that left
+    two decode instances at batch 256 and their partners waiting, the third at batch 80."""
     if 0 < prefill_ranks < world:
         return prefill_ranks, world - prefill_ranks
-    n_d = max(1, round(world * 0.4))
+    n_d = max(1, world // 2)
     return world - n_d, n_d
 
 

@@ -709,6 +709,9 @@ PYBIND11_MODULE(LAKEB_MODULE, m) {
   m.def("set_gemm_streamk_mode", [](int64_t mode) { lakeb::set_gemm_streamk_mode(static_cast<int>(mode)); });
   m.def("set_decode_split_mode", [](int64_t mode) { lakeb::set_decode_split_mode(static_cast<int>(mode)); });
   m.def("set_prefill_kernel", [](int64_t mode) { lakeb::set_prefill_kernel(static_cast<int>(mode)); });
+  m.def("prefill_trace_enable", [](bool on) {
+    LAKEB_CHECK_RC(lakeb::prefill_trace_enable(on ? 1 : 0), "prefill_trace_enable");
+  });
   m.def("prefill_trace", []() {
     auto t = at::zeros({1024}, at::TensorOptions().dtype(at::kLong));
     LAKEB_CHECK_RC(lakeb::prefill_trace_read(reinterpret_cast<long long*>(t.data_ptr<int64_t>()), 1024), "prefill_trace_read");

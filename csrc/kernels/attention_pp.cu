@@ -131,11 +131,13 @@ __device__ __forceinline__ int64_t page_row(const PagedAttnArgs& a, int64_t phys
   return (((phys * a.num_layers + a.layer) * 2 + kv) * a.n_kv_heads + head) * 16;
 }
 
-// Timeline of one CTA (the first launched: the heaviest query tile of head pair 0), recorded by
-// the TRACE variant in SM clock cycles: slot [j * 16 + e] holds event e of K/V tile j (see
-// kTr* below), slot [1023] the CTA's start. Read back with prefill_trace_read().
+// Timeline of one CTA (the first launched: the heaviest query tile of head pair 0), recorded
+// while g_pp_trace_on is set (prefill_trace_enable) in SM clock cycles: slot [j * 16 + e] holds
+// event e of K/V tile j (see kTr* below), slot [1023] the CTA's start. Read back with
+// prefill_trace_read().
 constexpr int kTraceSlots = 1024;
 __device__ long long g_pp_trace[kTraceSlots];
+__device__ int g_pp_trace_on;
 enum : int {
   kTrMmaP0 = 0,      // MMA issuer: P of head A ready (before PV_A(j))
   kTrMmaP1 = 1,      // MMA issuer: P of head B ready (before PV_B(j))
@@ -149,8 +151,8 @@ enum : int {
 };
 
 // EMUL: every EMUL-th pair of probabilities is computed by exp2_poly2 (0: none); INTPACK:
-// pack P to bf16 with integer ops instead of the converter; TRACE: record the timeline above.
-template <int EMUL, bool INTPACK, bool TRACE = false>
+// pack P to bf16 with integer ops instead of the converter.
+template <int EMUL, bool INTPACK>
 __global__ void __launch_bounds__(kThreads, 1)
     prefill_pingpong_kernel(const __grid_constant__ CUtensorMap kvmap, const __grid_constant__ CUtensorMap qmap,
                             const PagedAttnArgs a) {
@@ -172,7 +174,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tile_idx = a.num_tiles - 1 - static_cast<int>(blockIdx.x);
   const int4 tile = a.tiles[tile_idx];
   const int seq = tile.x, qrow0 = tile.y, nq = tile.z, pos0 = tile.w;
-  const bool traced = TRACE && blockIdx.x == 0 && blockIdx.y == 0 && (threadIdx.x & 31) == 0;
+  const bool traced = blockIdx.x == 0 && blockIdx.y == 0 && (threadIdx.x & 31) == 0 && g_pp_trace_on;
   auto tr = [&](int j, int e) {
     if (traced && j >= 0 && j < kTraceSlots / 16 - 1) g_pp_trace[j * 16 + e] = clock64();
   };
@@ -453,7 +455,6 @@ using PrefillKernel = void (*)(CUtensorMap, CUtensorMap, PagedAttnArgs);
 const PrefillKernel kVariants[] = {
     prefill_pingpong_kernel<0, false>, prefill_pingpong_kernel<0, true>, prefill_pingpong_kernel<4, false>,
     prefill_pingpong_kernel<4, true>,  prefill_pingpong_kernel<3, true>, prefill_pingpong_kernel<2, true>,
-    prefill_pingpong_kernel<0, false, true>,  // 6: default softmax with the timeline recorded
 };
 constexpr int kDefaultVariant = 0;  // measured fastest overall: MUFU exp, converter packing
 int g_variant = kDefaultVariant;
@@ -462,6 +463,8 @@ int g_variant = kDefaultVariant;
 void set_prefill_variant(int v) {
   g_variant = (v >= 0 && v < static_cast<int>(sizeof(kVariants) / sizeof(kVariants[0]))) ? v : kDefaultVariant;
 }
+
+int prefill_trace_enable(int on) { return cudaMemcpyToSymbol(g_pp_trace_on, &on, sizeof(int)); }
 
 int prefill_trace_read(long long* host, int n) {
   if (n > kTraceSlots) n = kTraceSlots;

@@ -171,7 +171,8 @@ bool prefill_pingpong_ok(const PagedAttnArgs& a);
 int paged_prefill_pingpong(const PagedAttnArgs& a, int64_t q_rows, cudaStream_t stream);
 void set_prefill_kernel(int mode);  // 1: ping-pong where it applies (default), 0: one head per CTA, 10+i: variant i
 void set_prefill_variant(int v);    // softmax variant of the ping-pong kernel (-1: default)
-// Timeline slots recorded by the traced ping-pong variant (SM clock cycles), copied to host memory.
+// Timeline of the ping-pong kernel's first CTA (SM clock cycles): recording on/off, read back.
+int prefill_trace_enable(int on);
 int prefill_trace_read(long long* host, int n);
 
 // ----------------------------------------------------------------- misc

@@ -124,9 +124,9 @@ def bench_prefill(t: Timer, out: list):
 
 def prefill_timeline(t: Timer, out: list):
     """Per-tile timeline of the two-head prefill kernel's heaviest CTA (4 x 2048 causal, 16 K/V
-    tiles): the traced variant records SM clock cycles at each hand-off (scores ready, scores in
-    registers, P computed, P handed over, MMA issuer sees P / K). Reports the median over the
-    steady-state tiles of each phase."""
+    tiles) for each softmax variant: the kernel records SM clock cycles at each hand-off (scores
+    ready, scores in registers, P computed, P handed over, MMA issuer sees P / K). Reports the
+    median over the steady-state tiles (2-13) of each phase."""
     from ..ops._ext import native
 
     nseq, new, hq, hkv = 4, 2048, 32, 8
@@ -139,34 +139,28 @@ def prefill_timeline(t: Timer, out: list):
     q = torch.randn(nseq * new, hq * 128, device="cuda").to(BF)
     o = torch.empty_like(q)
     qs_t = torch.tensor(qs, dtype=torch.int32, device="cuda")
-    native().set_prefill_kernel(16)
-    for _ in range(3):
-        ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv, 0.088, out=o)
-    torch.cuda.synchronize()
-    native().set_prefill_kernel(1)
-    tr = native().prefill_trace().tolist()
-    start = tr[1023]
-    ev = [[tr[j * 16 + e] for e in range(16)] for j in range(16)]
-    rows = []
-    for j in range(16):
-        e = ev[j]
-        rows.append(dict(
-            j=j,
-            a_wait_s=e[3] - (ev[j - 1][6] if j else start),  # softmax A idle between tiles
-            a_ld=e[4] - e[3], a_exp=e[5] - e[4], a_st=e[6] - e[5],
-            b_wait_s=e[7] - (ev[j - 1][10] if j else start),
-            b_ld=e[8] - e[7], b_exp=e[9] - e[8], b_st=e[10] - e[9],
-            mma_sees_pA=e[0] - e[6], mma_sees_pB=e[1] - e[10],
-            period=(ev[j][3] - ev[j - 1][3]) if j else None))
-    med = {}
-    for k in rows[0]:
-        if k == "j":
-            continue
-        xs = sorted(r[k] for r in rows[2:14] if r[k] is not None)
-        med[k] = xs[len(xs) // 2]
-    out.append(dict(kernel="prefill_pingpong timeline (cycles, median of tiles 2-13)", **med))
-    for r in rows:
-        out.append(dict(kernel="prefill_pingpong tile", **r))
+    C = native()
+    for v in range(6):
+        C.set_prefill_kernel(10 + v)
+        C.prefill_trace_enable(True)
+        for _ in range(3):
+            ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv, 0.088, out=o)
+        torch.cuda.synchronize()
+        C.prefill_trace_enable(False)
+        tr = C.prefill_trace().tolist()
+        ev = [[tr[j * 16 + e] for e in range(16)] for j in range(16)]
+        rows = []
+        for j in range(2, 14):
+            e = ev[j]
+            rows.append(dict(
+                a_wait_s=e[3] - ev[j - 1][6], a_ld=e[4] - e[3], a_exp=e[5] - e[4], a_st=e[6] - e[5],
+                b_wait_s=e[7] - ev[j - 1][10], b_ld=e[8] - e[7], b_exp=e[9] - e[8], b_st=e[10] - e[9],
+                mma_sees_pA=e[0] - e[6], mma_sees_pB=e[1] - e[10], period=ev[j][3] - ev[j - 1][3]))
+        med = {k: sorted(r[k] for r in rows)[len(rows) // 2] for k in rows[0]}
+        out.append(dict(kernel="prefill_pingpong timeline (cycles, median of tiles 2-13)", variant=v,
+                        ms=t(lambda: ops.paged_prefill_attention(q, arena, 0, bt, sl, tiles, qs_t, None, hq, hkv,
+                                                                 0.088, out=o)), **med))
+    C.set_prefill_kernel(1)
 
 
 def bench_norm(t: Timer, out: list):

@@ -84,12 +84,16 @@ class Workspace:
 
 class DecoderLM:
     def __init__(self, cfg: ModelConfig, device: torch.device | str = "cpu", dtype: torch.dtype | None = None,
-                 seed: int = 0, init: str = "random", ep=None, weights: str | None = None):
+                 seed: int = 0, init: str = "random", ep=None, weights: str | None = None, shard=None):
+        """`shard(name, tensor) -> tensor`: applied to each weight as soon as it is generated, so
+        a tensor-parallel rank keeps only its slice and never holds the whole model (the values
+        are those of the unsharded model with the same seed)."""
         self.cfg = cfg
         self.device = torch.device(device)
         self.dtype = dtype or (torch.float32 if self.device.type == "cpu" else torch.bfloat16)
         self.scale = 1.0 / math.sqrt(cfg.head_dim)
         self.w: dict[str, torch.Tensor] = {}
+        self._shard = shard
         if init in ("random", "zeros"):  # zeros: allocate only (a checkpoint overwrites every tensor)
             self._random_init(seed, zeros=init == "zeros")
         if weights:
@@ -115,6 +119,8 @@ class DecoderLM:
             t = torch.empty(shape, dtype=torch.float32, device=self.device)
             t.normal_(0.0, std, generator=gen)
             t = t.to(self.dtype)
+        if self._shard is not None:
+            t = self._shard(name, t)
         self.w[name] = t
         return t
 

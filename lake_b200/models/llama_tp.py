@@ -84,10 +84,17 @@ class TPDecoderLM:
         self.vocab_local = cfg.vocab // T
         # local "view" of the config for the runner (kv heads of this rank's arena)
         if full_weights is None:
-            full = DecoderLM(cfg, self.device, self.dtype, seed=seed)
-            full_weights = full.w
+            # generate layer by layer and keep this rank's slice of each weight (a 70B model's
+            # full bf16 weights would not fit next to the shards)
+            def keep(n, t):
+                s = shard_weights({n: t}, cfg, group.rank, T)[n]
+                return s.clone() if s.numel() < t.numel() else s  # a slice view would pin the whole tensor
+
+            full = DecoderLM(cfg, self.device, self.dtype, seed=seed, shard=keep)
+            self.w = full.w
             self.rope_cs = full.rope_cs
             self.scale = full.scale
+            del full
         else:
             from ..oracle import ops_ref as ref
             import math
@@ -95,8 +102,9 @@ class TPDecoderLM:
             self.rope_cs = ref.rope_cache(cfg.max_position, cfg.rope_theta, cfg.head_dim, cfg.rope_scaling,
                                           device=self.device)
             self.scale = 1.0 / math.sqrt(cfg.head_dim)
-        self.w = {k: v.to(self.device) for k, v in shard_weights(full_weights, cfg, self.rank, T).items()}
-        del full_weights
+        if full_weights is not None:
+            self.w = {k: v.to(self.device) for k, v in shard_weights(full_weights, cfg, self.rank, T).items()}
+            del full_weights
         if weight_dtype == "fp8":  # block-scaled e4m3 projections (W8A16 GEMMs); norms/embeddings stay bf16
             from ..ops.fp8 import quantize_blockwise
 

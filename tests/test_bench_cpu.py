@@ -28,7 +28,8 @@ def test_poisson_arrivals_rate_and_closed_loop():
 
 def test_pd_layouts():
     b = _bench()
-    assert b.pd_split(2) == (1, 1) and b.pd_split(4) == (2, 2) and b.pd_split(8) == (5, 3)
+    assert b.pd_split(2) == (1, 1) and b.pd_split(4) == (2, 2) and b.pd_split(8) == (4, 4)
+    assert b.pd_split(8, prefill_ranks=5) == (5, 3)
     assert b.pd_layout(8, 4) == (1, 1) and b.pd_layout(4, 2) == (1, 1)
     assert b.pd_layout(8, 1, n_experts=8) == (4, 4)  # expert-parallel decode ranks divide the experts
 

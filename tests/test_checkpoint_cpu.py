@@ -120,3 +120,21 @@ def test_qwen3_checkpoint_roundtrip_with_tied_embeddings(tmp_path):
     for i in range(cfg.n_layers):
         assert torch.equal(eng.model.w[f"layers.{i}.q_norm"].float(), src.model.w[f"layers.{i}.q_norm"].float())
     assert eng.generate(prompts, max_new_tokens=5) == want
+
+
+def test_layerwise_sharded_init_equals_sharded_full_model():
+    """A tensor-parallel rank generates its weights one tensor at a time and keeps only its
+    slice; the slices equal those cut from the whole model built with the same seed."""
+    from lake_b200.models.config import get_config
+    from lake_b200.models.llama import DecoderLM
+    from lake_b200.models.llama_tp import shard_weights
+
+    cfg = get_config("tiny-gpu")
+    full = DecoderLM(cfg, "cpu", torch.float32, seed=3)
+    for rank in range(2):
+        want = shard_weights(full.w, cfg, rank, 2)
+        got = DecoderLM(cfg, "cpu", torch.float32, seed=3,
+                        shard=lambda n, t, r=rank: shard_weights({n: t}, cfg, r, 2)[n].clone()).w
+        assert want.keys() == got.keys()
+        for k in want:
+            assert torch.equal(want[k], got[k]), k
