@@ -709,6 +709,20 @@ PYBIND11_MODULE(LAKEB_MODULE, m) {
   m.def("set_gemm_streamk_mode", [](int64_t mode) { lakeb::set_gemm_streamk_mode(static_cast<int>(mode)); });
   m.def("set_decode_split_mode", [](int64_t mode) { lakeb::set_decode_split_mode(static_cast<int>(mode)); });
   m.def("set_prefill_kernel", [](int64_t mode) { lakeb::set_prefill_kernel(static_cast<int>(mode)); });
+  m.def("set_gemm_w8a8_min_m", [](int64_t m) { lakeb::set_gemm_w8a8_min_m(static_cast<int>(m)); });
+  m.def("gemm_w8a8_reserve", [](int64_t m, int64_t k) { return lakeb::gemm_w8a8_reserve(m, k); },
+        "reserve the current device's W8A8 activation workspace for M x K (outside graph capture)");
+  m.def("quantize_fp8_rows", [](const at::Tensor& x, at::Tensor& q, at::Tensor& s) {
+    TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.stride(1) == 1, "x bf16 [M, K]");
+    TORCH_CHECK(q.scalar_type() == at::kByte && q.sizes() == x.sizes() && q.is_contiguous(), "q uint8 [M, K]");
+    TORCH_CHECK(s.scalar_type() == at::kFloat && s.dim() == 2 && s.size(0) == x.size(0) &&
+                    s.size(1) == x.size(1) / 128 && s.is_contiguous(), "s fp32 [M, K/128]");
+    LAKEB_CHECK_RC(lakeb::quantize_fp8_rows(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+                                            static_cast<int>(x.size(0)), static_cast<int>(x.size(1)),
+                                            q.data_ptr<uint8_t>(), q.size(1), s.data_ptr<float>(),
+                                            static_cast<int>(s.size(1)), cur_stream()),
+                   "quantize_fp8_rows");
+  });
   m.def("prefill_trace_enable", [](bool on) {
     LAKEB_CHECK_RC(lakeb::prefill_trace_enable(on ? 1 : 0), "prefill_trace_enable");
   });

@@ -145,7 +145,27 @@ __device__ __forceinline__ int sk_owner(long long u, long long total, int grid) 
   return static_cast<int>(((u + 1) * grid - 1) / total);
 }
 
-template <int BN, int STAGES, int EPI, bool W8 = false>
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T with e4m3 operands (both K-major, K = 32 per
+// instruction, the same 32 bytes of a 128-byte swizzle row that one bf16 K = 16 step covers).
+__device__ __forceinline__ void umma_e4m3(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n"
+      " .reg .pred p;\n"
+      " setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n"
+      "}\n" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+// Instruction descriptor: e4m3 x e4m3 -> fp32 (A and B format fields 0 = E4M3), both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_e4m3(int M, int N) {
+  return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// A8: W8A8 (fp8 A and B in shared memory, kind::f8f6f4, 128-deep k-blocks, scales applied per
+// k-block by the epilogue warps); W8: W8A16 (fp8 B converted to bf16 in shared memory).
+template <int BN, int STAGES, int EPI, bool W8 = false, bool A8 = false>
 __global__ void __launch_bounds__(threads_of<W8>(), 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const GemmArgs p) {
@@ -167,8 +187,11 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
   const int num_m_group = p.groups ? p.group_rows / kBM : num_m;
   const int num_n = (p.N + BN - 1) / BN;
   const int num_tiles = num_m * num_n;
-  const int num_kb_all = (p.K + kBK - 1) / kBK;
-  constexpr uint32_t kTmemCols = (2 * BN <= 32) ? 32 : (2 * BN <= 64 ? 64 : (2 * BN <= 128 ? 128 : (2 * BN <= 256 ? 256 : 512)));
+  // k-blocks: 64 bf16 or 128 e4m3, 128 bytes of a row either way
+  const int num_kb_all = A8 ? (p.K + 127) / 128 : (p.K + kBK - 1) / kBK;
+  // two accumulators (A8: two k-block partials and the final sum)
+  constexpr int kAccCols = A8 ? 3 * BN : 2 * BN;
+  constexpr uint32_t kTmemCols = (kAccCols <= 32) ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -233,9 +256,10 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
             tma_load_2d(sa, &tmA, &land[stage], kb * kBK, m_blk * kBM);
             tma_load_2d(sb8, &tmB, &land[stage], kb * kBK, grp * p.N + n_blk * BN);
           } else {
+            const int kx = kb * (A8 ? 128 : kBK);  // element offset along K (bytes for e4m3)
             mbar_expect_tx(&full[stage], S::kStageBytes);
-            tma_load_2d(sa, &tmA, &full[stage], kb * kBK, m_blk * kBM);
-            tma_load_2d(sb, &tmB, &full[stage], kb * kBK, grp * p.N + n_blk * BN);
+            tma_load_2d(sa, &tmA, &full[stage], kx, m_blk * kBM);
+            tma_load_2d(sb, &tmB, &full[stage], kx, grp * p.N + n_blk * BN);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -246,6 +270,39 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
       if (!ok) {
         // Drain loads already in flight before the CTA's shared memory is released.
         for (int s = 0; s < STAGES; ++s) mbar_wait(W8 ? &land[s] : &full[s], 0, nullptr, nullptr, 50000000ull);
+      }
+    }
+  } else if (A8 && warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (W8A8)
+    // each k-block goes to its own TMEM partial (alternating two), handed to the epilogue warps
+    if (lane == 0) {
+      constexpr uint32_t idesc8 = umma_idesc_e4m3(kBM, BN);
+      uint32_t stage = 0, phase = 0, g = 0;
+      bool ok = true;
+      WorkIter it(p, num_tiles, num_kb_all);
+      int tile, kb0, kb1;
+      while (ok && it.next(tile, kb0, kb1)) {
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
+          const int b = g & 1;
+          if (!mbar_wait(&tmem_empty[b], ((g >> 1) & 1) ^ 1, abort_flag, p.status) ||
+              !mbar_wait(&full[stage], phase, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * S::kStageBytes);
+          const uint64_t ad = umma_desc_sw128(sa);
+          const uint64_t bd = umma_desc_sw128(sa + S::kABytes);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)  // 32 e4m3 (32 bytes) along K per instruction
+            umma_e4m3(tmem_base + b * BN, ad + 2 * k, bd + 2 * k, idesc8, k != 0);
+          umma_commit(&empty[stage]);
+          umma_commit(&tmem_full[b]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
       }
     }
   } else if (warp == 1) {
@@ -334,187 +391,245 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
     int t = 0;
     WorkIter it(p, num_tiles, num_kb_all);
     int tile, kb0, kb1;
-    while (it.next(tile, kb0, kb1)) {
-      int m_blk, n_blk, grp;
-      tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
-      if (!tile_live(p, m_blk, num_m_group, grp)) continue;
-      const int acc = t & 1;
-      const uint32_t acc_phase = (t >> 1) & 1;
-      ++t;
-      if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, p.status)) break;
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
-      const int row = m_blk * kBM + row_in_tile;
-      const bool row_ok = row < p.M && (!p.groups || row - grp * p.group_rows < __ldg(p.group_count + grp));
-
-      if (p.streamk && (kb0 != 0 || kb1 != num_kb_all)) {
-        // Stream-K: this CTA holds part of the tile's K range. Add it into the tile's workspace
-        // slot (named by the tile's last contributor, unique per cut tile); the last contributor
-        // to arrive loads the full sum back into its accumulator and runs the epilogue below.
-        const long long total = static_cast<long long>(num_tiles) * num_kb_all;
-        const long long u_first = static_cast<long long>(tile) * num_kb_all;
-        const int first = sk_owner(u_first, total, gridDim.x);
-        const int slot = sk_owner(u_first + num_kb_all - 1, total, gridDim.x);
-        float* wrow = p.split_ws + (static_cast<int64_t>(slot) * kBM + row_in_tile) * BN;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          tmem_ld_wait();
-          if (row_ok) {
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + c * 32 + 4 * i),
-                           "f"(__uint_as_float(r[4 * i])), "f"(__uint_as_float(r[4 * i + 1])),
-                           "f"(__uint_as_float(r[4 * i + 2])), "f"(__uint_as_float(r[4 * i + 3]))
-                           : "memory");
-          }
-        }
-        __threadfence();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (warp == 2 && lane == 0) *split_last = atomicAdd(p.split_cnt + slot, 1) == slot - first;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (!*split_last) {
-          tc_fence_before();
-          mbar_arrive(&tmem_empty[acc]);
-          continue;
-        }
-        __threadfence();
-        // tcgen05.st is warp-aligned: every lane issues it (rows past M store zeros)
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          float4* src = reinterpret_cast<float4*>(wrow + c * 32);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (row_ok) {
-              f = __ldcg(src + i);
-              __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
-            }
-            r[4 * i] = __float_as_uint(f.x);
-            r[4 * i + 1] = __float_as_uint(f.y);
-            r[4 * i + 2] = __float_as_uint(f.z);
-            r[4 * i + 3] = __float_as_uint(f.w);
-          }
-          tmem_st32(tbase + c * 32, r);
-        }
-        tmem_st_wait();
-        if (warp == 2 && lane == 0) p.split_cnt[slot] = 0;
-      }
-      if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32) {
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          tmem_ld_wait();
-          const int col0 = n_blk * BN + c * 32;
-          if (row_ok && col0 < p.N) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            if constexpr (EPI == kEpiStoreF32) {
-              float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + row * p.ldc + col0);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-            } else {
-              if constexpr (EPI == kEpiResidual) {
-                float rv[32];
-                load_bf16x32(p.R + row * p.ldr + col0, rv);
-#pragma unroll
-                for (int j = 0; j < 32; ++j) v[j] += rv[j];
+    // the fused epilogue of one tile whose fp32 accumulator sits at `tbase` in tensor memory
+    auto tile_epilogue = [&](uint32_t tbase, int n_blk, int row, bool row_ok) {
+        if constexpr (EPI == kEpiStoreBf16 || EPI == kEpiResidual || EPI == kEpiStoreF32) {
+  #pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c * 32, r);
+            tmem_ld_wait();
+            const int col0 = n_blk * BN + c * 32;
+            if (row_ok && col0 < p.N) {
+              float v[32];
+  #pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+              if constexpr (EPI == kEpiStoreF32) {
+                float4* dst = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.C) + row * p.ldc + col0);
+  #pragma unroll
+                for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              } else {
+                if constexpr (EPI == kEpiResidual) {
+                  float rv[32];
+                  load_bf16x32(p.R + row * p.ldr + col0, rv);
+  #pragma unroll
+                  for (int j = 0; j < 32; ++j) v[j] += rv[j];
+                }
+                store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
               }
+            }
+          }
+        } else if constexpr (EPI == kEpiRSPush) {
+          // partial sums of this rank's K-slice go straight to the row's owner (P2P stores over NVLink)
+          __nv_bfloat16* dst_row = nullptr;
+          if (row_ok) {
+            const int d = row / p.tp.rows_per_rank;
+            const int lr = row - d * p.tp.rows_per_rank;
+            dst_row = p.tp.rs_recv[d] + (static_cast<int64_t>(p.tp.rank) * p.tp.rows_per_rank + lr) * p.ldc;
+          }
+  #pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c * 32, r);
+            tmem_ld_wait();
+            const int col0 = n_blk * BN + c * 32;
+            if (row_ok && col0 < p.N) {
+              float v[32];
+  #pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+              store_bf16x32(dst_row + col0, v);
+            }
+          }
+        } else if constexpr (EPI == kEpiScatter) {
+          // indirect row store: the token slot this gathered row came from (local or a peer's buffer)
+          __nv_bfloat16* dst_row = nullptr;
+          if (row_ok) {
+            const int slot = p.row_slot[row];
+            if (slot >= 0) dst_row = p.tp.rs_recv[p.row_rank ? p.row_rank[row] : 0] + static_cast<int64_t>(slot) * p.ldc;
+          }
+  #pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c * 32, r);
+            tmem_ld_wait();
+            const int col0 = n_blk * BN + c * 32;
+            if (dst_row && col0 < p.N) {
+              float v[32];
+  #pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+              store_bf16x32(dst_row + col0, v);
+            }
+          }
+        } else if constexpr (EPI == kEpiSwiGLU) {
+          constexpr int H = BN / 2;
+  #pragma unroll 1
+          for (int c = 0; c < H / 32; ++c) {
+            uint32_t g[32], u[32];
+            tmem_ld32(tbase + c * 32, g);
+            tmem_ld32(tbase + H + c * 32, u);
+            tmem_ld_wait();
+            const int col0 = n_blk * H + c * 32;
+            if (row_ok) {
+              float v[32];
+  #pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
               store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
             }
           }
-        }
-      } else if constexpr (EPI == kEpiRSPush) {
-        // partial sums of this rank's K-slice go straight to the row's owner (P2P stores over NVLink)
-        __nv_bfloat16* dst_row = nullptr;
-        if (row_ok) {
-          const int d = row / p.tp.rows_per_rank;
-          const int lr = row - d * p.tp.rows_per_rank;
-          dst_row = p.tp.rs_recv[d] + (static_cast<int64_t>(p.tp.rank) * p.tp.rows_per_rank + lr) * p.ldc;
-        }
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          tmem_ld_wait();
-          const int col0 = n_blk * BN + c * 32;
-          if (row_ok && col0 < p.N) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            store_bf16x32(dst_row + col0, v);
-          }
-        }
-      } else if constexpr (EPI == kEpiScatter) {
-        // indirect row store: the token slot this gathered row came from (local or a peer's buffer)
-        __nv_bfloat16* dst_row = nullptr;
-        if (row_ok) {
-          const int slot = p.row_slot[row];
-          if (slot >= 0) dst_row = p.tp.rs_recv[p.row_rank ? p.row_rank[row] : 0] + static_cast<int64_t>(slot) * p.ldc;
-        }
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          tmem_ld_wait();
-          const int col0 = n_blk * BN + c * 32;
-          if (dst_row && col0 < p.N) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-            store_bf16x32(dst_row + col0, v);
-          }
-        }
-      } else if constexpr (EPI == kEpiSwiGLU) {
-        constexpr int H = BN / 2;
-#pragma unroll 1
-        for (int c = 0; c < H / 32; ++c) {
-          uint32_t g[32], u[32];
-          tmem_ld32(tbase + c * 32, g);
-          tmem_ld32(tbase + H + c * 32, u);
-          tmem_ld_wait();
-          const int col0 = n_blk * H + c * 32;
-          if (row_ok) {
-            float v[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[j] = silu_f(__uint_as_float(g[j])) * __uint_as_float(u[j]);
-            store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.C) + row * p.ldc + col0, v);
-          }
-        }
-      } else if constexpr (EPI == kEpiQKV) {
-        static_assert(BN == 128, "QKV epilogue maps one 128-wide head per tile");
-        qkv_head_epilogue(p, tbase, n_blk, row, row_ok);
-      } else if constexpr (EPI == kEpiArgmax) {
-        unsigned long long best = 0ull;
-#pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tbase + c * 32, r);
-          tmem_ld_wait();
-          const int col0 = n_blk * BN + c * 32;
-          if (row_ok && col0 < p.N) {
-            uint32_t allow = 0xFFFFFFFFu;
-            if (p.bitmask) allow = p.bitmask[static_cast<int64_t>(row) * p.bitmask_words + (col0 >> 5)];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if ((allow >> j) & 1u) {
-                const unsigned long long key =
-                    (static_cast<unsigned long long>(float_order_key(__uint_as_float(r[j]))) << 32) |
-                    static_cast<unsigned long long>(0xFFFFFFFFu -
-                                                    static_cast<uint32_t>(col0 + j + p.tp.col_offset));
-                best = key > best ? key : best;
+        } else if constexpr (EPI == kEpiQKV) {
+          static_assert(BN == 128, "QKV epilogue maps one 128-wide head per tile");
+          qkv_head_epilogue(p, tbase, n_blk, row, row_ok);
+        } else if constexpr (EPI == kEpiArgmax) {
+          unsigned long long best = 0ull;
+  #pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c * 32, r);
+            tmem_ld_wait();
+            const int col0 = n_blk * BN + c * 32;
+            if (row_ok && col0 < p.N) {
+              uint32_t allow = 0xFFFFFFFFu;
+              if (p.bitmask) allow = p.bitmask[static_cast<int64_t>(row) * p.bitmask_words + (col0 >> 5)];
+  #pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if ((allow >> j) & 1u) {
+                  const unsigned long long key =
+                      (static_cast<unsigned long long>(float_order_key(__uint_as_float(r[j]))) << 32) |
+                      static_cast<unsigned long long>(0xFFFFFFFFu -
+                                                      static_cast<uint32_t>(col0 + j + p.tp.col_offset));
+                  best = key > best ? key : best;
+                }
               }
             }
           }
+          if (row_ok && best) atomicMax(p.amax + row, best);
         }
-        if (row_ok && best) atomicMax(p.amax + row, best);
+    };
+    if constexpr (A8) {
+      // W8A8: one 128-deep k-block per TMEM partial (double-buffered with the MMA issuer); each row's
+      // fp32 sum of partial x (activation scale x weight block scale) stays in registers, then goes to
+      // the third TMEM region, which the shared epilogue reads like any accumulator
+      static_assert(!A8 || BN == 128, "W8A8 tiles are one weight scale block wide");
+      const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
+      uint32_t g = 0;
+      while (it.next(tile, kb0, kb1)) {
+        int m_blk, n_blk;
+        tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+        const int row = m_blk * kBM + row_in_tile;
+        const bool row_ok = row < p.M;
+        const float* sa_row = p.a_scale + static_cast<int64_t>(row_ok ? row : 0) * p.a_scale_ld;
+        const float* sb_row = p.b_scale + static_cast<int64_t>(n_blk) * p.b_scale_ld;
+        float sum[BN];
+#pragma unroll
+        for (int i = 0; i < BN; ++i) sum[i] = 0.f;
+        bool ok = true;
+        for (int kb = kb0; kb < kb1; ++kb, ++g) {
+          const int b = g & 1;
+          if (!mbar_wait(&tmem_full[b], (g >> 1) & 1, abort_flag, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const float sc = (row_ok ? __ldg(sa_row + kb) : 0.f) * __ldg(sb_row + kb);
+          const uint32_t pb = tmem_base + b * BN + lane_off;
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(pb + c * 32, r);
+            tmem_ld_wait();
+            if (c == BN / 32 - 1) {  // the whole partial has been read: the MMA may overwrite it
+              tc_fence_before();
+              mbar_arrive(&tmem_empty[b]);
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sum[c * 32 + j] = fmaf(__uint_as_float(r[j]), sc, sum[c * 32 + j]);
+          }
+        }
+        if (!ok) break;
+        const uint32_t fb = tmem_base + 2 * BN + lane_off;
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(sum[c * 32 + j]);
+          tmem_st32(fb + c * 32, r);
+        }
+        tmem_st_wait();
+        tile_epilogue(fb, n_blk, row, row_ok);
       }
-      tc_fence_before();
-      mbar_arrive(&tmem_empty[acc]);
+    } else {
+      while (it.next(tile, kb0, kb1)) {
+        int m_blk, n_blk, grp;
+        tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
+        if (!tile_live(p, m_blk, num_m_group, grp)) continue;
+        const int acc = t & 1;
+        const uint32_t acc_phase = (t >> 1) & 1;
+        ++t;
+        if (!mbar_wait(&tmem_full[acc], acc_phase, abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + acc * BN + (static_cast<uint32_t>(q * 32) << 16);
+        const int row = m_blk * kBM + row_in_tile;
+        const bool row_ok = row < p.M && (!p.groups || row - grp * p.group_rows < __ldg(p.group_count + grp));
+
+        if (p.streamk && (kb0 != 0 || kb1 != num_kb_all)) {
+          // Stream-K: this CTA holds part of the tile's K range. Add it into the tile's workspace
+          // slot (named by the tile's last contributor, unique per cut tile); the last contributor
+          // to arrive loads the full sum back into its accumulator and runs the epilogue below.
+          const long long total = static_cast<long long>(num_tiles) * num_kb_all;
+          const long long u_first = static_cast<long long>(tile) * num_kb_all;
+          const int first = sk_owner(u_first, total, gridDim.x);
+          const int slot = sk_owner(u_first + num_kb_all - 1, total, gridDim.x);
+          float* wrow = p.split_ws + (static_cast<int64_t>(slot) * kBM + row_in_tile) * BN;
+  #pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tbase + c * 32, r);
+            tmem_ld_wait();
+            if (row_ok) {
+  #pragma unroll
+              for (int i = 0; i < 8; ++i)
+                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(wrow + c * 32 + 4 * i),
+                             "f"(__uint_as_float(r[4 * i])), "f"(__uint_as_float(r[4 * i + 1])),
+                             "f"(__uint_as_float(r[4 * i + 2])), "f"(__uint_as_float(r[4 * i + 3]))
+                             : "memory");
+            }
+          }
+          __threadfence();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (warp == 2 && lane == 0) *split_last = atomicAdd(p.split_cnt + slot, 1) == slot - first;
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (!*split_last) {
+            tc_fence_before();
+            mbar_arrive(&tmem_empty[acc]);
+            continue;
+          }
+          __threadfence();
+          // tcgen05.st is warp-aligned: every lane issues it (rows past M store zeros)
+  #pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            float4* src = reinterpret_cast<float4*>(wrow + c * 32);
+  #pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+              if (row_ok) {
+                f = __ldcg(src + i);
+                __stcg(src + i, make_float4(0.f, 0.f, 0.f, 0.f));
+              }
+              r[4 * i] = __float_as_uint(f.x);
+              r[4 * i + 1] = __float_as_uint(f.y);
+              r[4 * i + 2] = __float_as_uint(f.z);
+              r[4 * i + 3] = __float_as_uint(f.w);
+            }
+            tmem_st32(tbase + c * 32, r);
+          }
+          tmem_st_wait();
+          if (warp == 2 && lane == 0) p.split_cnt[slot] = 0;
+        }
+        tile_epilogue(tbase, n_blk, row, row_ok);
+        tc_fence_before();
+        mbar_arrive(&tmem_empty[acc]);
+      }
     }
     // Cross-GPU signal: this CTA's stores are visible system-wide before the counters move.
     // (every epilogue thread reaches the named barrier; only a CTA that did not abort signals)
@@ -561,6 +676,42 @@ int launch(const GemmArgs& a, cudaStream_t stream) {
   if (a.streamk) grid = a.streamk;  // the dispatcher's stream-K grid
   kern<<<grid, threads_of<W8>(), S::kAlloc, stream>>>(ma, mb, a);
   return cudaGetLastError();
+}
+
+// W8A8 launch: e4m3 A (quantised activations) and B (weights), 128 x 128 tiles (one weight scale
+// block per tile), six 32 KB stages.
+template <int EPI>
+int launch_a8(const GemmArgs& a, cudaStream_t stream) {
+  using S = GemmSmem<128, 6>;
+  CUtensorMap ma, mb;
+  if (!make_fp8_sw128_map(&ma, a.A8, a.M, a.K, a.lda8, kBM)) return -10;
+  if (!make_fp8_sw128_map(&mb, a.B8, a.N, a.K, a.ldb8, 128)) return -11;
+  auto kern = gemm_bf16_kernel<128, 6, EPI, false, true>;
+  if (int e = ensure_smem_attr(reinterpret_cast<const void*>(kern), S::kAlloc)) return e;
+  kern<<<grid_for(a.M, a.N, 128, 0), threads_of<false>(), S::kAlloc, stream>>>(ma, mb, a);
+  return cudaGetLastError();
+}
+
+// Block-scaled e4m3 quantisation: one warp per (row, 128-column block), four values per lane.
+__global__ void __launch_bounds__(256) quantize_fp8_rows_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                 int M, int kblocks, uint8_t* __restrict__ q,
+                                                                 int64_t ldq, float* __restrict__ s, int s_ld) {
+  const int w = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (w >= M * kblocks) return;
+  const int m = w / kblocks, kb = w - m * kblocks;
+  const uint2 raw = *reinterpret_cast<const uint2*>(x + static_cast<int64_t>(m) * ldx + kb * 128 + lane * 4);
+  const float2 v01 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+  const float2 v23 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+  float amax = fmaxf(fmaxf(fabsf(v01.x), fabsf(v01.y)), fmaxf(fabsf(v23.x), fabsf(v23.y)));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const float scale = amax > 0.f ? amax / 448.f : 1.f;
+  const float inv = 1.f / scale;
+  const __nv_fp8x2_storage_t lo = __nv_cvt_float2_to_fp8x2(make_float2(v01.x * inv, v01.y * inv), __NV_SATFINITE, __NV_E4M3);
+  const __nv_fp8x2_storage_t hi = __nv_cvt_float2_to_fp8x2(make_float2(v23.x * inv, v23.y * inv), __NV_SATFINITE, __NV_E4M3);
+  *reinterpret_cast<uint32_t*>(q + static_cast<int64_t>(m) * ldq + kb * 128 + lane * 4) =
+      static_cast<uint32_t>(lo) | (static_cast<uint32_t>(hi) << 16);
+  if (lane == 0) s[static_cast<int64_t>(m) * s_ld + kb] = scale;
 }
 
 // Tile width: 256 keeps the tensor cores busiest, but a small M (decode batches) leaves most SMs
@@ -670,7 +821,8 @@ static bool sk_epilogue(int epi) {
 }
 
 static int tile_width(int M, int N, int epi, bool w8) {
-  if (w8) return epi == kEpiQKV ? 128 : 256;
+  // fp8 SwiGLU weights interleave gate and up per 128 rows ([gate 64 | up 64]): 128-wide tiles
+  if (w8) return (epi == kEpiQKV || epi == kEpiSwiGLU) ? 128 : 256;
   return bn_for(M, N, epi, false);
 }
 
@@ -698,6 +850,68 @@ int gemm_grid(int M, int N, int K, int epi, int max_ctas, bool w8) {
 void set_gemm_pair_mode(int mode) { g_pair_mode = mode; }
 int gemm_pair_mode() { return g_pair_mode; }
 
+// W8A8 activation workspace per device: e4m3 rows [M x K] and their scales [M x K/128], reserved
+// outside any graph capture (gemm_w8a8_reserve); a GEMM that does not fit runs as W8A16.
+static int g_w8a8_min_m = 256;
+void set_gemm_w8a8_min_m(int m) { g_w8a8_min_m = m; }
+static uint8_t* s_a8_q[16] = {};
+static float* s_a8_s[16] = {};
+static int64_t s_a8_cap[16] = {};  // elements of s_a8_q
+
+bool gemm_w8a8_reserve(int64_t M, int64_t K) {
+  const int dev = cur_device();
+  if (dev < 0 || M <= 0 || K <= 0) return false;
+  const int64_t need = M * ((K + 127) / 128 * 128);
+  if (s_a8_cap[dev] >= need) return true;
+  uint8_t* q = nullptr;
+  float* sc = nullptr;
+  if (cudaMalloc(&q, need) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (cudaMalloc(&sc, need / 128 * sizeof(float)) != cudaSuccess) {
+    cudaGetLastError();
+    cudaFree(q);
+    return false;
+  }
+  cudaDeviceSynchronize();  // the previous buffers may still be read by queued kernels
+  cudaFree(s_a8_q[dev]);
+  cudaFree(s_a8_s[dev]);
+  s_a8_q[dev] = q;
+  s_a8_s[dev] = sc;
+  s_a8_cap[dev] = need;
+  return true;
+}
+
+static bool a8_workspace(int64_t elems, uint8_t** q, float** sc) {
+  const int dev = cur_device();
+  if (dev < 0 || s_a8_cap[dev] < elems) return false;
+  *q = s_a8_q[dev];
+  *sc = s_a8_s[dev];
+  return true;
+}
+
+// W8A8 takes plain single-GPU fp8 GEMMs at prefill sizes; tensor-parallel (peer-signalling or
+// peer-waiting), grouped and CTA-capped calls stay W8A16.
+static bool a8_eligible(const GemmArgs& a, int epi) {
+  if (g_w8a8_min_m <= 0 || a.M < g_w8a8_min_m || a.groups || a.max_ctas || !a.A || !a.b_scale) return false;
+  if (a.tp.ag_cnt || a.tp.rs_cnt[0] || a.tp.done_cnt[0] || a.K % 128 || a.lda % 8 || a.ldb8 % 16) return false;
+  if ((reinterpret_cast<uintptr_t>(a.A) & 15) || (reinterpret_cast<uintptr_t>(a.B8) & 15)) return false;
+  return epi == kEpiStoreBf16 || epi == kEpiResidual || epi == kEpiSwiGLU || epi == kEpiStoreF32 ||
+         epi == kEpiQKV || epi == kEpiArgmax;
+}
+
+int quantize_fp8_rows(const __nv_bfloat16* x, int64_t ldx, int M, int K, uint8_t* q, int64_t ldq, float* s,
+                      int s_ld, cudaStream_t stream) {
+  if (M <= 0) return 0;
+  if (K % 128 || ldx % 4 || ldq % 4 || (reinterpret_cast<uintptr_t>(x) & 7) || (reinterpret_cast<uintptr_t>(q) & 3))
+    return -12;
+  const int64_t warps = static_cast<int64_t>(M) * (K / 128);
+  quantize_fp8_rows_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(x, ldx, M, K / 128, q, ldq, s,
+                                                                                       s_ld);
+  return cudaGetLastError();
+}
+
 int gemm_bf16(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   if (a_in.M <= 0 || a_in.N <= 0 || a_in.K <= 0) return 0;
   GemmArgs a = a_in;
@@ -718,6 +932,28 @@ int gemm_bf16(const GemmArgs& a_in, int epi, cudaStream_t stream) {
   if (a.tp.ag_cnt && (a.tp.world < 1 || a.tp.world > kMaxTP)) return -6;
   if (epi == kEpiQKV && a.N != (a.n_q_heads + 2 * a.n_kv_heads) * 128) return -3;
   const bool w8 = a.B8 != nullptr;
+  if (w8 && a8_eligible(a, epi)) {
+    // W8A8: quantise this call's activations into the device workspace, then the fp8 MMA kernel
+    uint8_t* q = nullptr;
+    float* sc = nullptr;
+    if (a8_workspace(static_cast<int64_t>(a.M) * a.K, &q, &sc)) {
+      const int kbs = a.K / 128;
+      if (int e = quantize_fp8_rows(a.A, a.lda, a.M, a.K, q, a.K, sc, kbs, stream)) return e;
+      a.A8 = q;
+      a.lda8 = a.K;
+      a.a_scale = sc;
+      a.a_scale_ld = kbs;
+      switch (epi) {
+        case kEpiStoreBf16: return launch_a8<kEpiStoreBf16>(a, stream);
+        case kEpiResidual: return launch_a8<kEpiResidual>(a, stream);
+        case kEpiSwiGLU: return launch_a8<kEpiSwiGLU>(a, stream);
+        case kEpiStoreF32: return launch_a8<kEpiStoreF32>(a, stream);
+        case kEpiQKV: return launch_a8<kEpiQKV>(a, stream);
+        case kEpiArgmax: return launch_a8<kEpiArgmax>(a, stream);
+        default: break;
+      }
+    }
+  }
   // plan order shared with gemm_grid(): two-SM kernel, else stream-K, else data-parallel
   if (!w8 && use_pair(a.M, a.N, epi, a.groups != 0, a.max_ctas, a.tp.done_cnt[0] != nullptr))
     return gemm_bf16_pair(a, epi, stream);
@@ -730,7 +966,7 @@ int gemm_bf16(const GemmArgs& a_in, int epi, cudaStream_t stream) {
     switch (epi) {
       case kEpiStoreBf16: return launch<256, 3, kEpiStoreBf16, true>(a, stream);
       case kEpiResidual: return launch<256, 3, kEpiResidual, true>(a, stream);
-      case kEpiSwiGLU: return launch<256, 3, kEpiSwiGLU, true>(a, stream);
+      case kEpiSwiGLU: return launch<128, 5, kEpiSwiGLU, true>(a, stream);
       case kEpiStoreF32: return launch<256, 3, kEpiStoreF32, true>(a, stream);
       case kEpiArgmax: return launch<256, 3, kEpiArgmax, true>(a, stream);
       case kEpiQKV: return launch<128, 5, kEpiQKV, true>(a, stream);

@@ -108,7 +108,25 @@ struct GemmArgs {
   // kEpiScatter destinations (rows indexed like A)
   const int* row_slot = nullptr;
   const int* row_rank = nullptr;
+  // fp8 activations (W8A8; the dispatcher fills these for fp8 weights at prefill sizes): A8 is e4m3
+  // [M, K] bytes with one fp32 scale per row and 128-column block, a_scale[m * a_scale_ld + k / 128].
+  // The MMAs run kind::f8f6f4 per 128-deep k-block into a TMEM partial and the epilogue warps add
+  // each partial, times a_scale x b_scale, into fp32 registers (one scale pair per k-block)
+  const uint8_t* A8 = nullptr;
+  int64_t lda8 = 0;
+  const float* a_scale = nullptr;
+  int a_scale_ld = 0;
 };
+
+// Block-scaled e4m3 quantisation of bf16 rows: q[m, k] = x[m, k] / s[m, k/128] with
+// s = amax(|x[m, 128-block]|) / 448 (1 for an all-zero block). K % 128 == 0.
+int quantize_fp8_rows(const __nv_bfloat16* x, int64_t ldx, int M, int K, uint8_t* q, int64_t ldq, float* s,
+                      int s_ld, cudaStream_t stream);
+// Smallest M at which gemm_bf16 runs fp8-weight GEMMs as W8A8 (0 = never: always W8A16).
+void set_gemm_w8a8_min_m(int m);
+// Runs fp8-weight GEMMs with M >= the threshold as W8A8 from now on when the device's activation
+// workspace holds M x K (allocated here; call outside graph capture). Returns false on failure.
+bool gemm_w8a8_reserve(int64_t M, int64_t K);
 
 // Two-SM (cta_group::2) GEMM for large M; epilogues: store bf16, residual, SwiGLU, fp32.
 int gemm_bf16_pair(const GemmArgs& args, int epi, cudaStream_t stream);

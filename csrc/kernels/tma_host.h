@@ -18,6 +18,9 @@ bool encode_bf16_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t co
 // Byte-element 2-D map without swizzle (fp8 operands staged for conversion).
 bool make_u8_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows,
                  int box_cols);
+// e4m3 operand map for tcgen05 (kind::f8f6f4): byte elements, boxes of box_rows x 128 bytes with the
+// 128-byte swizzle (one swizzle row = one 128-deep k-block), zero fill outside the bounds.
+bool make_fp8_sw128_map(CUtensorMap* out, const void* ptr, int64_t rows, int64_t cols, int64_t ld, int box_rows);
 int num_sms();
 
 // Raises a kernel's dynamic shared-memory limit to `bytes` on the CURRENT device.

@@ -157,6 +157,10 @@ class LLMEngine:
             self._arena_cfg = cfg
             if ec.weight_dtype == "fp8" and self.device.type == "cuda":
                 self.model.quantize_fp8()
+                # fp8 GEMMs at prefill sizes run W8A8: the activations' e4m3 workspace for the largest step
+                from ..ops._ext import native
+
+                native().gemm_w8a8_reserve(max_tokens, max(cfg.hidden, cfg.q_size, cfg.intermediate))
         num_blocks = ec.num_blocks
         if not num_blocks:
             if self.device.type == "cuda":

@@ -211,11 +211,12 @@ class DecoderLM:
     def quantize_fp8(self) -> None:
         """Replace the dense projection weights by block-scaled e4m3 (W8A16 GEMMs); norms,
         embeddings and MoE experts stay bf16."""
-        from ..ops.fp8 import quantize_blockwise
+        from ..ops.fp8 import quantize_blockwise, quantize_gate_up
 
         for k in list(self.w):
             if k.endswith(("qkv_proj", "o_proj", "gate_up_proj", "down_proj")) and "experts" not in k:
-                self.w[k] = quantize_blockwise(self.w[k])
+                gu = k.endswith("gate_up_proj") and self.cfg.intermediate % 128 == 0
+                self.w[k] = quantize_gate_up(self.w[k]) if gu else quantize_blockwise(self.w[k])
         if not self.cfg.tie_embeddings:
             self.w["lm_head"] = quantize_blockwise(self.w["lm_head"])
         torch.cuda.empty_cache()

@@ -106,10 +106,12 @@ class TPDecoderLM:
             self.w = {k: v.to(self.device) for k, v in shard_weights(full_weights, cfg, self.rank, T).items()}
             del full_weights
         if weight_dtype == "fp8":  # block-scaled e4m3 projections (W8A16 GEMMs); norms/embeddings stay bf16
-            from ..ops.fp8 import quantize_blockwise
+            from ..ops.fp8 import quantize_blockwise, quantize_gate_up
 
             for k in list(self.w):
-                if k.endswith(("qkv_proj", "o_proj", "gate_up_proj", "down_proj")) or k == "lm_head":
+                if k.endswith("gate_up_proj"):
+                    self.w[k] = quantize_gate_up(self.w[k])
+                elif k.endswith(("qkv_proj", "o_proj", "down_proj")) or k == "lm_head":
                     self.w[k] = quantize_blockwise(self.w[k])
         torch.cuda.empty_cache()
         self.tp_world = T

@@ -96,11 +96,14 @@ def linear_swiglu(a: torch.Tensor, w_gate_up: torch.Tensor, out: torch.Tensor | 
     if out is None:
         out = torch.empty(a.shape[0], w_gate_up.shape[0] // 2, dtype=a.dtype, device=a.device)
     if a.is_cuda:
+        if isinstance(w_gate_up, Fp8Weight) and w_gate_up.swiglu_tile != 128:
+            raise ValueError("fp8 SwiGLU weights use the 128-row gate/up interleave (ops.fp8.quantize_gate_up)")
         wq, ws = unpack(w_gate_up)
         native().linear_swiglu(a, wq, out, status_word(a.device), None, ws)
         LAUNCHES[0] += 1
         return out
-    out.copy_(ref.swiglu_from_interleaved(ref.linear(a, _dense(w_gate_up))).to(out.dtype))
+    tile = w_gate_up.swiglu_tile if isinstance(w_gate_up, Fp8Weight) else 256
+    out.copy_(ref.swiglu_from_interleaved(ref.linear(a, _dense(w_gate_up)), tile).to(out.dtype))
     return out
 
 

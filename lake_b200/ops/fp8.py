@@ -21,6 +21,7 @@ BLOCK = 128
 class Fp8Weight:
     q: torch.Tensor  # uint8 [N, K] (e4m3 bit patterns)
     s: torch.Tensor  # fp32 [ceil(N/128), ceil(K/128)]
+    swiglu_tile: int = 256  # gate/up interleave of a SwiGLU weight: rows [gate tile/2 | up tile/2] per tile
 
     @property
     def shape(self):
@@ -34,20 +35,26 @@ class Fp8Weight:
     def is_cuda(self):
         return self.q.is_cuda
 
-    def dequant(self, dtype=torch.float32) -> torch.Tensor:
+    def dequant(self, dtype=torch.float32, swiglu_tile: int | None = None) -> torch.Tensor:
+        """Dense weight; `swiglu_tile` re-lays a SwiGLU weight out in that gate/up interleave."""
         n, k = self.q.shape
         w = self.q.view(torch.float8_e4m3fn).to(torch.float32)
         s = self.s.repeat_interleave(BLOCK, 0)[:n].repeat_interleave(BLOCK, 1)[:, :k]
-        return (w * s).to(dtype)
+        d = w * s
+        if swiglu_tile == 256 and self.swiglu_tile == 128:  # [half][gate|up] -> [gate|up][half] per 256 rows
+            d = d.view(n // 256, 2, 2, 64, k).permute(0, 2, 1, 3, 4).reshape(n, k)
+        return d.to(dtype)
 
     def rows(self, a: int, b: int) -> "Fp8Weight":
         """Rows [a, b) (block-aligned a) as a new weight, e.g. one rank's tensor-parallel shard."""
         assert a % BLOCK == 0
-        return Fp8Weight(self.q[a:b].contiguous(), self.s[a // BLOCK:(b + BLOCK - 1) // BLOCK].contiguous())
+        return Fp8Weight(self.q[a:b].contiguous(), self.s[a // BLOCK:(b + BLOCK - 1) // BLOCK].contiguous(),
+                         self.swiglu_tile)
 
     def cols(self, a: int, b: int) -> "Fp8Weight":
         assert a % BLOCK == 0
-        return Fp8Weight(self.q[:, a:b].contiguous(), self.s[:, a // BLOCK:(b + BLOCK - 1) // BLOCK].contiguous())
+        return Fp8Weight(self.q[:, a:b].contiguous(), self.s[:, a // BLOCK:(b + BLOCK - 1) // BLOCK].contiguous(),
+                         self.swiglu_tile)
 
 
 def quantize_blockwise(w: torch.Tensor) -> Fp8Weight:
@@ -61,6 +68,30 @@ def quantize_blockwise(w: torch.Tensor) -> Fp8Weight:
     s = amax / E4M3_MAX
     q = (blocks / s[:, None, :, None]).clamp(-E4M3_MAX, E4M3_MAX).view(nb * BLOCK, kb * BLOCK)[:n, :k]
     return Fp8Weight(q.contiguous().to(torch.float8_e4m3fn).view(torch.uint8), s.contiguous())
+
+
+def quantize_gate_up(w: torch.Tensor) -> Fp8Weight:
+    """Block-scaled e4m3 of a SwiGLU weight in the 256-row interleave ([gate 128 | up 128] per 256
+    rows), re-interleaved per 128 rows ([gate 64 | up 64]) first: the fp8 GEMMs run 128-wide tiles
+    (one weight scale block per tile), each holding the gate and up rows of 64 outputs."""
+    n, k = w.shape
+    assert n % 256 == 0
+    w = w.view(n // 256, 2, 2, 64, k).permute(0, 2, 1, 3, 4).reshape(n, k)  # [blk][gate|up][half] -> [blk][half][gate|up]
+    q = quantize_blockwise(w)
+    q.swiglu_tile = 128
+    return q
+
+
+def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Reference of the W8A8 activation quantisation: e4m3 values (as float32) and fp32 scales
+    [M, K/128], s = amax(|128-block|) / 448 (1 for an all-zero block), q = x * (1 / s) rounded to
+    nearest e4m3 (saturating at 448)."""
+    m, k = x.shape
+    xb = x.float().view(m, k // BLOCK, BLOCK)
+    amax = xb.abs().amax(-1)
+    s = torch.where(amax > 0, amax / E4M3_MAX, torch.ones_like(amax))
+    q = (xb * (1.0 / s)[..., None]).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).to(torch.float32)
+    return q.view(m, k), s
 
 
 def unpack(w):

@@ -116,23 +116,32 @@ def test_engine_qwen3_qk_norm_matches_oracle(cuda_dev):
         _check_tokens(eng.model, p, o)
 
 
-def test_engine_fp8_weights_match_dequantized_oracle(cuda_dev):
-    """Block-scaled e4m3 projection weights (W8A16 GEMMs) vs the oracle on the dequantised weights."""
+@pytest.mark.parametrize("w8a8", [False, True])
+def test_engine_fp8_weights_match_dequantized_oracle(cuda_dev, w8a8):
+    """Block-scaled e4m3 projection weights vs the oracle on the dequantised weights: W8A16 GEMMs
+    (steps below the W8A8 threshold), and with the threshold at one row, W8A8 for every step
+    (e4m3 activations per row and 128-column block, kind::f8f6f4 MMAs)."""
     from types import SimpleNamespace
 
+    from lake_b200.ops._ext import native
     from lake_b200.ops.fp8 import Fp8Weight
 
-    eng = LLMEngine("tiny-gpu", device="cuda:0", max_running=8, max_batched_tokens=200, max_model_len=1024,
-                    num_blocks=256, weight_dtype="fp8")
-    assert isinstance(eng.model.w["layers.0.qkv_proj"], Fp8Weight)
-    rng = random.Random(8)
-    prompts = [[rng.randrange(eng.cfg.vocab) for _ in range(n)] for n in (5, 70, 130)]
-    outs = eng.generate(prompts, max_new_tokens=6)
-    torch.cuda.synchronize()
-    oracle = SimpleNamespace(cfg=eng.model.cfg, w={k: (v.dequant(torch.bfloat16) if isinstance(v, Fp8Weight) else v)
-                                                   for k, v in eng.model.w.items()})
+    native().set_gemm_w8a8_min_m(1 if w8a8 else 256)
+    try:
+        eng = LLMEngine("tiny-gpu", device="cuda:0", max_running=8, max_batched_tokens=200, max_model_len=1024,
+                        num_blocks=256, weight_dtype="fp8", use_cuda_graphs=not w8a8)
+        assert isinstance(eng.model.w["layers.0.qkv_proj"], Fp8Weight)
+        rng = random.Random(8)
+        prompts = [[rng.randrange(eng.cfg.vocab) for _ in range(n)] for n in (5, 70, 130)]
+        outs = eng.generate(prompts, max_new_tokens=6)
+        torch.cuda.synchronize()
+    finally:
+        native().set_gemm_w8a8_min_m(256)
+    oracle = SimpleNamespace(cfg=eng.model.cfg,
+                             w={k: (v.dequant(torch.bfloat16, swiglu_tile=256) if isinstance(v, Fp8Weight) else v)
+                                for k, v in eng.model.w.items()})
     for p, o in zip(prompts, outs):
-        _check_tokens(oracle, p, o)
+        _check_tokens(oracle, p, o, tol_frac=0.12 if w8a8 else 0.08)
 
 
 def test_kernel_write_behind_with_graph_decode(cuda_dev):

@@ -6,6 +6,7 @@ import torch
 
 from lake_b200 import ops
 from lake_b200.oracle import ops_ref as ref
+from lake_b200.ops.fp8 import quantize_blockwise, quantize_gate_up
 
 pytestmark = pytest.mark.gpu
 
@@ -286,7 +287,6 @@ def test_gemm_split_k_small_m_matches_fp32(cuda_dev, m, n, k):
 @pytest.mark.parametrize("m,n,k", [(300, 1024, 512), (64, 4096, 4096), (2048, 2304, 1024)])
 def test_gemm_fp8_weights_match_dequantized(cuda_dev, m, n, k):
     """W8A16: block-scaled e4m3 weights dequantised in shared memory by converter warps."""
-    from lake_b200.ops.fp8 import quantize_blockwise
 
     g = torch.Generator(device="cuda").manual_seed(m + k)
     a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
@@ -302,13 +302,60 @@ def test_gemm_fp8_weights_match_dequantized(cuda_dev, m, n, k):
     res = ops.linear_residual(a, w8, r)
     assert (res.float() - (want + r.float())).abs().max().item() < tol + 2e-2
     if n % 256 == 0:
-        act = ops.linear_swiglu(a, w8)
-        ref_act = ref.swiglu_from_interleaved(want)
+        gu8 = quantize_gate_up(w)  # fp8 SwiGLU weights: gate/up interleaved per 128 rows
+        gu_want = a.float() @ gu8.dequant().to(torch.bfloat16).float().t()
+        act = ops.linear_swiglu(a, gu8)
+        ref_act = ref.swiglu_from_interleaved(gu_want, 128)
         assert (act.float() - ref_act).abs().max().item() < 3e-2 * ref_act.abs().max().item() + 1e-3
     toks = ops.linear_argmax(a, w8)
     assert (toks.long().cpu() == want.argmax(-1).cpu()).float().mean().item() > 0.97
     torch.cuda.synchronize()
     ops.core.check_status()
+
+
+@pytest.mark.parametrize("m,n,k", [(300, 1024, 512), (1000, 2304, 1024), (4096, 6144, 4096)])
+def test_gemm_w8a8_matches_quantized_operands(cuda_dev, m, n, k):
+    """W8A8: the activations quantised to e4m3 per row and 128-column block, kind::f8f6f4 MMAs per
+    128-deep k-block, each k-block's product scaled by its two block scales in fp32. Equal to the
+    fp32 product of the dequantised operands up to the bf16 output rounding; the kernel's
+    quantisation equal to the PyTorch restatement of it."""
+    from lake_b200.ops._ext import native
+    from lake_b200.ops.fp8 import quantize_rows
+
+    C = native()
+    C.set_gemm_w8a8_min_m(1)
+    try:
+        assert C.gemm_w8a8_reserve(m, k)
+        g = torch.Generator(device="cuda").manual_seed(m + n)
+        a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
+        a[:7, :128] *= 30.0  # activation blocks with very different scales
+        w = torch.randn(n, k, device="cuda", generator=g) / k ** 0.5
+        w[:128, :128] *= 40.0
+        w8 = quantize_blockwise(w)
+        aq, asc = quantize_rows(a)
+        q = torch.empty(m, k, dtype=torch.uint8, device="cuda")
+        s = torch.empty(m, k // 128, dtype=torch.float32, device="cuda")
+        C.quantize_fp8_rows(a, q, s)
+        assert torch.equal(s, asc)
+        assert (q.view(torch.float8_e4m3fn).float() == aq).float().mean().item() > 0.999
+        ad = (aq.view(m, k // 128, 128) * asc[..., None]).view(m, k)
+        want = ad @ w8.dequant().t()
+        tol = 1e-2 * want.abs().max().item()
+        assert (ops.linear(a, w8).float() - want).abs().max().item() < tol
+        r = torch.randn(m, n, device="cuda", generator=g).to(torch.bfloat16)
+        res = ops.linear_residual(a, w8, r)
+        assert (res.float() - (want + r.float())).abs().max().item() < tol + 2e-2
+        if n % 256 == 0:
+            gu8 = quantize_gate_up(w)
+            act = ops.linear_swiglu(a, gu8)
+            ref_act = ref.swiglu_from_interleaved(ad @ gu8.dequant().t(), 128)
+            assert (act.float() - ref_act).abs().max().item() < 2e-2 * ref_act.abs().max().item() + 1e-3
+        toks = ops.linear_argmax(a, w8)
+        assert (toks.long().cpu() == want.argmax(-1).cpu()).float().mean().item() > 0.97
+        torch.cuda.synchronize()
+        ops.core.check_status()
+    finally:
+        C.set_gemm_w8a8_min_m(256)
 
 
 @pytest.mark.parametrize("m", [1024, 1000, 8192])
