@@ -37,15 +37,17 @@ struct GemmSmem {
   static constexpr int kB8Bytes = W8 ? BN * kBK : 0;  // fp8 staging of B (W8A16)
   static constexpr int kStageBytes = kABytes + kBBytes + kB8Bytes;
   static constexpr int kBarOffset = STAGES * kStageBytes;
-  // full[S], empty[S], land[S] (W8), tmem_full[2], tmem_empty[2], tmem slot, abort flag, split flag
-  static constexpr int kBytes = kBarOffset + (3 * STAGES + 4) * 8 + 16;
+  // full[S], empty[S], land[S] (W8), tmem_full[3], tmem_empty[3] (two accumulators; W8A8: three
+  // k-block partials), final_ready, final_free (W8A8), tmem slot, abort flag, split flag
+  static constexpr int kBytes = kBarOffset + (3 * STAGES + 8) * 8 + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
-// Threads per CTA: TMA warp, MMA warp, 4 epilogue warps (+ 4 fp8 converter warps for W8A16).
-template <bool W8>
+// Threads per CTA: TMA warp, MMA warp, 4 epilogue warps (+ 4 fp8 converter warps for W8A16; W8A8:
+// 8 epilogue warps, two per TMEM lane quarter, each promoting 64 of the tile's 128 columns).
+template <bool W8, bool A8 = false>
 constexpr int threads_of() {
-  return W8 ? 320 : 192;
+  return (W8 || A8) ? 320 : 192;
 }
 
 // Dequantise one 64-byte fp8 row (64 e4m3 values of one output column n) into a bf16 row of the
@@ -145,6 +147,16 @@ __device__ __forceinline__ int sk_owner(long long u, long long total, int grid) 
   return static_cast<int>(((u + 1) * grid - 1) / total);
 }
 
+// Two-lane fp32 fused multiply-add (one f32x2 instruction).
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{\n .reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n"
+      " mov.b64 rc, {%6, %7};\n fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;\n}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+
 // D[tmem] (+)= A[smem desc] * B[smem desc]^T with e4m3 operands (both K-major, K = 32 per
 // instruction, the same 32 bytes of a 128-byte swizzle row that one bf16 K = 16 step covers).
 __device__ __forceinline__ void umma_e4m3(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
@@ -166,7 +178,7 @@ __host__ __device__ constexpr uint32_t umma_idesc_e4m3(int M, int N) {
 // A8: W8A8 (fp8 A and B in shared memory, kind::f8f6f4, 128-deep k-blocks, scales applied per
 // k-block by the epilogue warps); W8: W8A16 (fp8 B converted to bf16 in shared memory).
 template <int BN, int STAGES, int EPI, bool W8 = false, bool A8 = false>
-__global__ void __launch_bounds__(threads_of<W8>(), 1)
+__global__ void __launch_bounds__(threads_of<W8, A8>(), 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const GemmArgs p) {
   using S = GemmSmem<BN, STAGES, W8>;
@@ -176,8 +188,10 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
   uint64_t* empty = full + STAGES;
   uint64_t* land = empty + STAGES;  // W8: A + fp8 B landed (the converters then fill full[])
   uint64_t* tmem_full = land + STAGES;
-  uint64_t* tmem_empty = tmem_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tmem_empty + 2);
+  uint64_t* tmem_empty = tmem_full + 3;
+  uint64_t* final_ready = tmem_empty + 3;  // W8A8: both column halves of the tile's sum are in TMEM
+  uint64_t* final_free = final_ready + 1;  // W8A8: the epilogue has read the previous tile's sum
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(final_free + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* split_last = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
@@ -189,8 +203,8 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
   const int num_tiles = num_m * num_n;
   // k-blocks: 64 bf16 or 128 e4m3, 128 bytes of a row either way
   const int num_kb_all = A8 ? (p.K + 127) / 128 : (p.K + kBK - 1) / kBK;
-  // two accumulators (A8: two k-block partials and the final sum)
-  constexpr int kAccCols = A8 ? 3 * BN : 2 * BN;
+  // two accumulators (A8: three k-block partials and the final sum)
+  constexpr int kAccCols = A8 ? 4 * BN : 2 * BN;
   constexpr uint32_t kTmemCols = (kAccCols <= 32) ? 32 : (kAccCols <= 64 ? 64 : (kAccCols <= 128 ? 128 : (kAccCols <= 256 ? 256 : 512)));
 
   if (threadIdx.x == 0) {
@@ -199,10 +213,12 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
       mbar_init(&empty[s], 1);
       mbar_init(&land[s], 1);
     }
-    for (int a = 0; a < 2; ++a) {
+    for (int a = 0; a < 3; ++a) {
       mbar_init(&tmem_full[a], 1);
-      mbar_init(&tmem_empty[a], 128);
+      mbar_init(&tmem_empty[a], A8 ? 256 : 128);
     }
+    mbar_init(final_ready, 128);
+    mbar_init(final_free, 128);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -283,8 +299,8 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
       int tile, kb0, kb1;
       while (ok && it.next(tile, kb0, kb1)) {
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
-          const int b = g & 1;
-          if (!mbar_wait(&tmem_empty[b], ((g >> 1) & 1) ^ 1, abort_flag, p.status) ||
+          const int b = g % 3;
+          if (!mbar_wait(&tmem_empty[b], ((g / 3) & 1) ^ 1, abort_flag, p.status) ||
               !mbar_wait(&full[stage], phase, abort_flag, p.status)) {
             ok = false;
             break;
@@ -506,12 +522,16 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
         }
     };
     if constexpr (A8) {
-      // W8A8: one 128-deep k-block per TMEM partial (double-buffered with the MMA issuer); each row's
-      // fp32 sum of partial x (activation scale x weight block scale) stays in registers, then goes to
-      // the third TMEM region, which the shared epilogue reads like any accumulator
+      // W8A8: one 128-deep k-block per TMEM partial (three, rotating with the MMA issuer). Warps 2-9
+      // promote: warp pair (w, w + 4) shares a TMEM lane quarter, each summing 64 columns of its 32
+      // rows as partial x (activation scale x weight block scale) in fp32 registers. At the tile's
+      // end both halves go to the fourth TMEM region, which warps 2-5 read like any accumulator
+      // in the shared epilogue (final_ready / final_free hand the region over, with bounded waits).
       static_assert(!A8 || BN == 128, "W8A8 tiles are one weight scale block wide");
       const uint32_t lane_off = static_cast<uint32_t>(q * 32) << 16;
-      uint32_t g = 0;
+      const int hc = (warp - 2) >> 2;  // column half of this warp
+      const uint32_t fb = tmem_base + 3 * BN + lane_off;
+      uint32_t g = 0, tt = 0;
       while (it.next(tile, kb0, kb1)) {
         int m_blk, n_blk;
         tile_coords(tile, num_m, p.tp.m_rot, m_blk, n_blk);
@@ -519,43 +539,59 @@ __global__ void __launch_bounds__(threads_of<W8>(), 1)
         const bool row_ok = row < p.M;
         const float* sa_row = p.a_scale + static_cast<int64_t>(row_ok ? row : 0) * p.a_scale_ld;
         const float* sb_row = p.b_scale + static_cast<int64_t>(n_blk) * p.b_scale_ld;
-        float sum[BN];
+        float2 sum[32];
 #pragma unroll
-        for (int i = 0; i < BN; ++i) sum[i] = 0.f;
+        for (int i = 0; i < 32; ++i) sum[i] = make_float2(0.f, 0.f);
         bool ok = true;
         for (int kb = kb0; kb < kb1; ++kb, ++g) {
-          const int b = g & 1;
-          if (!mbar_wait(&tmem_full[b], (g >> 1) & 1, abort_flag, p.status)) {
+          const int b = g % 3;
+          if (!mbar_wait(&tmem_full[b], (g / 3) & 1, abort_flag, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const float sc = (row_ok ? __ldg(sa_row + kb) : 0.f) * __ldg(sb_row + kb);
-          const uint32_t pb = tmem_base + b * BN + lane_off;
+          const uint32_t pb = tmem_base + b * BN + lane_off + hc * 64;
+          uint32_t r0[32], r1[32];
+          tmem_ld32(pb, r0);
+          tmem_ld32(pb + 32, r1);
+          tmem_ld_wait();
+          tc_fence_before();
+          mbar_arrive(&tmem_empty[b]);  // the partial is in registers: the MMA may overwrite it
+          const float2 s2 = make_float2(sc, sc);
 #pragma unroll
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(pb + c * 32, r);
-            tmem_ld_wait();
-            if (c == BN / 32 - 1) {  // the whole partial has been read: the MMA may overwrite it
-              tc_fence_before();
-              mbar_arrive(&tmem_empty[b]);
-            }
-#pragma unroll
-            for (int j = 0; j < 32; ++j) sum[c * 32 + j] = fmaf(__uint_as_float(r[j]), sc, sum[c * 32 + j]);
+          for (int j = 0; j < 16; ++j) {
+            sum[j] = ffma2(make_float2(__uint_as_float(r0[2 * j]), __uint_as_float(r0[2 * j + 1])), s2, sum[j]);
+            sum[16 + j] = ffma2(make_float2(__uint_as_float(r1[2 * j]), __uint_as_float(r1[2 * j + 1])), s2,
+                                sum[16 + j]);
           }
         }
         if (!ok) break;
-        const uint32_t fb = tmem_base + 2 * BN + lane_off;
+        // warps 6-9 write their half only after warps 2-5 have read the previous tile's sum
+        if (hc == 1 && tt > 0 && !mbar_wait(final_free, (tt - 1) & 1, abort_flag, p.status)) break;
+        tc_fence_after();
+        uint32_t r[32];
 #pragma unroll
-        for (int c = 0; c < BN / 32; ++c) {
-          uint32_t r[32];
+        for (int c = 0; c < 2; ++c) {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) r[j] = __float_as_uint(sum[c * 32 + j]);
-          tmem_st32(fb + c * 32, r);
+          for (int j = 0; j < 16; ++j) {
+            r[2 * j] = __float_as_uint(sum[16 * c + j].x);
+            r[2 * j + 1] = __float_as_uint(sum[16 * c + j].y);
+          }
+          tmem_st32(fb + hc * 64 + c * 32, r);
         }
         tmem_st_wait();
-        tile_epilogue(fb, n_blk, row, row_ok);
+        tc_fence_before();
+        if (hc == 1) {
+          mbar_arrive(final_ready);
+        } else {
+          if (!mbar_wait(final_ready, tt & 1, abort_flag, p.status)) break;  // the other half is in
+          tc_fence_after();
+          tile_epilogue(fb, n_blk, row, row_ok);
+          tc_fence_before();
+          mbar_arrive(final_free);
+        }
+        ++tt;
       }
     } else {
       while (it.next(tile, kb0, kb1)) {
@@ -688,7 +724,7 @@ int launch_a8(const GemmArgs& a, cudaStream_t stream) {
   if (!make_fp8_sw128_map(&mb, a.B8, a.N, a.K, a.ldb8, 128)) return -11;
   auto kern = gemm_bf16_kernel<128, 6, EPI, false, true>;
   if (int e = ensure_smem_attr(reinterpret_cast<const void*>(kern), S::kAlloc)) return e;
-  kern<<<grid_for(a.M, a.N, 128, 0), threads_of<false>(), S::kAlloc, stream>>>(ma, mb, a);
+  kern<<<grid_for(a.M, a.N, 128, 0), threads_of<false, true>(), S::kAlloc, stream>>>(ma, mb, a);
   return cudaGetLastError();
 }
 

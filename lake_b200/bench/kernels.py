@@ -6,7 +6,8 @@ after warm-up, L2 flushed between iterations.
     python -m lake_b200.bench.kernels --profile CASE   # 3 launches of one kernel, for an ncu capture
 
 Profile cases (inputs larger than the 126 MB L2, a few GB on the device at most):
-gemm_gate_up (M=4096 K=4096 N=28672), decode (256 seqs x 2304 ctx, 1 layer),
+gemm_gate_up (M=4096 K=4096 N=28672), gemm_w8a8_gate_up (the same shape with block-scaled fp8
+weights, W8A8), decode (256 seqs x 2304 ctx, 1 layer),
 prefill_tc (4 x 2048), moe_decode (8 experts, 128 tokens top-2, grouped GEMM),
 gemm_decode_qkv (M=80 QKV + RoPE + KV write, stream-K; 50 MB of weights: ncu flushes
 the caches between passes, so its DRAM figures still count the weight stream).
@@ -62,6 +63,32 @@ def bench_gemm(t: Timer, out: list):
         byt = (m * k + n * k + m * n) * 2
         out.append(dict(kernel="gemm_bf16", shape=name, m=m, n=n, k=k, ms=ms, tflops=fl / ms / 1e9,
                         gbs=byt / ms / 1e6, cublas_ms=ms_ref, cublas_tflops=fl / ms_ref / 1e9))
+
+
+def bench_gemm_fp8(t: Timer, out: list):
+    """Block-scaled fp8 weights at prefill sizes: W8A8 (e4m3 activations, kind::f8f6f4 MMAs; the
+    time includes quantising the activations) and W8A16 (weights dequantised to bf16 in shared
+    memory) against the bf16 GEMM of the same shape."""
+    from ..ops._ext import native
+    from ..ops.fp8 import quantize_blockwise
+
+    C = native()
+    for m, n, k, name in [(8192, 6144, 4096, "qkv"), (8192, 4096, 4096, "o_proj"), (8192, 28672, 4096, "gate_up"),
+                          (8192, 4096, 14336, "down")]:
+        a = torch.randn(m, k, device="cuda").to(BF)
+        w = (torch.randn(n, k, device="cuda") / math.sqrt(k)).to(BF)
+        w8 = quantize_blockwise(w)
+        c = torch.empty(m, n, device="cuda", dtype=BF)
+        C.gemm_w8a8_reserve(m, k)
+        ms_a8 = t(lambda: ops.linear(a, w8, out=c))
+        C.set_gemm_w8a8_min_m(0)
+        ms_a16 = t(lambda: ops.linear(a, w8, out=c))
+        C.set_gemm_w8a8_min_m(256)
+        ms_bf16 = t(lambda: ops.linear(a, w, out=c))
+        fl = 2 * m * n * k
+        out.append(dict(kernel="gemm_fp8", shape=name, m=m, n=n, k=k, w8a8_ms=ms_a8, w8a8_tflops=fl / ms_a8 / 1e9,
+                        w8a16_ms=ms_a16, w8a16_tflops=fl / ms_a16 / 1e9, bf16_ms=ms_bf16,
+                        bf16_tflops=fl / ms_bf16 / 1e9))
 
 
 def bench_decode(t: Timer, out: list):
@@ -256,6 +283,16 @@ def profile(case: str) -> None:
         w = (torch.randn(28672, 4096, device="cuda") * 0.02).to(BF)
         c = torch.empty(4096, 28672, device="cuda", dtype=BF)
         fn = lambda: ops.linear(a, w, out=c)  # noqa: E731
+    elif case == "gemm_w8a8_gate_up":
+        # block-scaled fp8 weights, W8A8 (activation quantisation kernel + the fp8 MMA GEMM)
+        from ..ops._ext import native
+        from ..ops.fp8 import quantize_blockwise
+
+        a = torch.randn(4096, 4096, device="cuda").to(BF)
+        w8 = quantize_blockwise(torch.randn(28672, 4096, device="cuda") * 0.02)
+        c = torch.empty(4096, 28672, device="cuda", dtype=BF)
+        native().gemm_w8a8_reserve(4096, 4096)
+        fn = lambda: ops.linear(a, w8, out=c)  # noqa: E731
     elif case == "decode":
         nseq, ctx, hq, hkv = 256, 2304, 32, 8
         nb = ctx // 16
@@ -327,7 +364,7 @@ def main(argv=None):
     t = Timer(args.iters)
     res: list = []
     for name in args.only.split(","):
-        {"gemm": bench_gemm, "decode": bench_decode, "prefill": bench_prefill, "norm": bench_norm,
+        {"gemm": bench_gemm, "gemm_fp8": bench_gemm_fp8, "decode": bench_decode, "prefill": bench_prefill, "norm": bench_norm,
          "moe": bench_moe, "pd_qkv": bench_pd_qkv, "prefill_timeline": prefill_timeline}[name](t, res)
     for r in res:
         print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}))

@@ -24,6 +24,7 @@ Weight names follow the vLLM packed layout the reference uses
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -32,6 +33,10 @@ from .. import ops
 from ..oracle import ops_ref as ref
 from ..utils.trace import nvtx
 from .config import ModelConfig
+
+# Mixed steps run the decode rows' attention on a side stream beside the prefill rows' attention
+# (LAKEB_ATTN_OVERLAP=1).
+ATTN_OVERLAP = [os.environ.get("LAKEB_ATTN_OVERLAP", "0") == "1"]
 
 
 @dataclass
@@ -253,6 +258,24 @@ class DecoderLM:
         c = self.cfg
         q, out = ws.q[:t], ws.attn[:t]
         nd = b.n_decode
+        side = self._attn_side_stream() if (nd and t > nd) else None
+        if side is not None:
+            # mixed step: the decode rows' attention (K/V-bandwidth-bound) runs on a side stream
+            # beside the prefill rows' attention (tensor-core-bound); both only read q and the
+            # arena and write disjoint rows of `out`
+            main = torch.cuda.current_stream(self.device)
+            ev_in, ev_out = torch.cuda.Event(), torch.cuda.Event()
+            ev_in.record(main)
+            side.wait_event(ev_in)
+            with torch.cuda.stream(side):
+                ops.paged_decode_attention(q[:nd], arena, i, b.block_tables[:nd], b.seq_lens[:nd], c.n_q_heads,
+                                           c.n_kv_heads, self.scale, out=out[:nd], splits=b.decode_splits,
+                                           ws_o=ws.ws_o, ws_ml=ws.ws_ml)
+                ev_out.record(side)
+            ops.paged_prefill_attention(q, arena, i, b.block_tables, b.seq_lens, b.prefill_tiles, b.query_start,
+                                        b.positions, c.n_q_heads, c.n_kv_heads, self.scale, out=out)
+            main.wait_event(ev_out)
+            return out
         if nd:
             ops.paged_decode_attention(q[:nd], arena, i, b.block_tables[:nd], b.seq_lens[:nd], c.n_q_heads,
                                        c.n_kv_heads, self.scale, out=out[:nd], splits=b.decode_splits,
@@ -261,6 +284,16 @@ class DecoderLM:
             ops.paged_prefill_attention(q, arena, i, b.block_tables, b.seq_lens, b.prefill_tiles, b.query_start,
                                         b.positions, c.n_q_heads, c.n_kv_heads, self.scale, out=out)
         return out
+
+    def _attn_side_stream(self):
+        """Side stream of the mixed-step attention overlap (LAKEB_ATTN_OVERLAP=1; off outside CUDA
+        and while a graph is being captured)."""
+        if self.device.type != "cuda" or not ATTN_OVERLAP[0] or torch.cuda.is_current_stream_capturing():
+            return None
+        st = getattr(self, "_side", None)
+        if st is None:
+            st = self._side = torch.cuda.Stream(self.device)
+        return st
 
     def _qkv(self, i: int, x: torch.Tensor, b: ForwardBatch, arena: torch.Tensor, ws: Workspace, t: int):
         c = self.cfg

@@ -89,8 +89,10 @@ def quantize_rows(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     m, k = x.shape
     xb = x.float().view(m, k // BLOCK, BLOCK)
     amax = xb.abs().amax(-1)
-    s = torch.where(amax > 0, amax / E4M3_MAX, torch.ones_like(amax))
-    q = (xb * (1.0 / s)[..., None]).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).to(torch.float32)
+    # tensor / tensor and reciprocal are IEEE divisions (a Python-scalar divisor would become a
+    # multiplication by its reciprocal), as in the kernel
+    s = torch.where(amax > 0, amax / torch.full_like(amax, E4M3_MAX), torch.ones_like(amax))
+    q = (xb * torch.reciprocal(s)[..., None]).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).to(torch.float32)
     return q.view(m, k), s
 
 

@@ -286,7 +286,18 @@ def test_gemm_split_k_small_m_matches_fp32(cuda_dev, m, n, k):
 
 @pytest.mark.parametrize("m,n,k", [(300, 1024, 512), (64, 4096, 4096), (2048, 2304, 1024)])
 def test_gemm_fp8_weights_match_dequantized(cuda_dev, m, n, k):
-    """W8A16: block-scaled e4m3 weights dequantised in shared memory by converter warps."""
+    """W8A16: block-scaled e4m3 weights dequantised in shared memory by converter warps (the W8A8
+    path is switched off here; it has its own test)."""
+    from lake_b200.ops._ext import native
+
+    native().set_gemm_w8a8_min_m(0)
+    try:
+        _fp8_weights_case(m, n, k)
+    finally:
+        native().set_gemm_w8a8_min_m(256)
+
+
+def _fp8_weights_case(m, n, k):
 
     g = torch.Generator(device="cuda").manual_seed(m + k)
     a = (torch.randn(m, k, device="cuda", generator=g) * 0.5).to(torch.bfloat16)
@@ -337,7 +348,7 @@ def test_gemm_w8a8_matches_quantized_operands(cuda_dev, m, n, k):
         s = torch.empty(m, k // 128, dtype=torch.float32, device="cuda")
         C.quantize_fp8_rows(a, q, s)
         assert torch.equal(s, asc)
-        assert (q.view(torch.float8_e4m3fn).float() == aq).float().mean().item() > 0.999
+        assert (q.view(torch.float8_e4m3fn).float() == aq).float().mean().item() > 0.9999
         ad = (aq.view(m, k // 128, 128) * asc[..., None]).view(m, k)
         want = ad @ w8.dequant().t()
         tol = 1e-2 * want.abs().max().item()
