@@ -6,7 +6,8 @@ after warm-up, L2 flushed between iterations.
     python -m lake_b200.bench.kernels --profile CASE   # 3 launches of one kernel, for an ncu capture
 
 Profile cases (inputs larger than the 126 MB L2, a few GB on the device at most):
-gemm_gate_up (M=4096 K=4096 N=28672), gemm_w8a8_gate_up (the same shape with block-scaled fp8
+tp2_rs / tp2_norm / tp2_swiglu_ag / tp4_* (the fused tensor-parallel kernels of one MLP hop at
+4096 tokens, driven from GPU 0), gemm_gate_up (M=4096 K=4096 N=28672), gemm_w8a8_gate_up (the same shape with block-scaled fp8
 weights, W8A8), decode (256 seqs x 2304 ctx, 1 layer),
 prefill_tc (4 x 2048), moe_decode (8 experts, 128 tokens top-2, grouped GEMM),
 gemm_decode_qkv (M=80 QKV + RoPE + KV write, stream-K; 50 MB of weights: ncu flushes
@@ -276,9 +277,77 @@ def bench_moe(t: Timer, out: list):
                         experts=8, ms=ms, weight_gbs=wbytes / ms / 1e6))
 
 
+def _tp_case(world: int, what: str, tokens: int = 8192):
+    """One fused tensor-parallel kernel of the Llama-3-8B MLP hop as TP rank 0 of `world`, driven
+    from one process: GPU 0 runs the kernel and its P2P stores land in buffers on GPUs 1..world-1
+    (peer access, as the IPC-mapped buffers of a real group). The other ranks never run, so their
+    counter slots on GPU 0 are preset: GPU 0's waits pass at once and the capture shows the
+    kernel's own work and NVLink traffic.
+      rs   : down_proj GEMM (K = FFN / world) whose epilogue pushes each partial row to its owner
+      norm : reduce of the world partials + residual + RMSNorm + all-gather push to every rank
+      swiglu_ag : gate_up GEMM (N = 2 FFN / world) over the all-gathered rows + SwiGLU"""
+    from ..ops import tp as tpops
+    from ..ops._ext import native
+
+    C = native()
+    if torch.cuda.device_count() < world:
+        raise SystemExit(f"needs {world} GPUs")
+    torch.cuda.set_device(0)
+    for d in range(1, world):
+        C.enable_peer_access(d)
+    H, I = 4096, 14336
+    mr = tokens // world
+    devs = [torch.device("cuda", d) for d in range(world)]
+    recv = [torch.zeros(world * mr, H, dtype=BF, device=dv) for dv in devs]
+    afull = [torch.zeros(world * mr, H, dtype=BF, device=dv) for dv in devs]
+    cnt = [torch.zeros(2 * world, dtype=torch.int64, device=dv) for dv in devs]  # [rs world | ag world]
+    cnt[0].fill_(1 << 60)
+    ptr = [c.data_ptr() for c in cnt]
+    if what == "rs":
+        a = torch.randn(world * mr, I // world, device="cuda").to(BF)
+        w = (torch.randn(H, I // world, device="cuda") * 0.02).to(BF)
+        tp = dict(world=world, rank=0, rows_per_rank=mr, m_rot=(mr // 128) % max(1, (world * mr) // 128),
+                  rs_recv=[r.data_ptr() for r in recv], rs_cnt=ptr)
+        return lambda: tpops.linear_rs(a, w, tp), 2 * world * mr * H * (I // world)
+    if what == "norm":
+        h = torch.randn(mr, H, device="cuda").to(BF)
+        wn = torch.ones(H, device="cuda").to(BF)
+        tp = dict(world=world, rank=0, rows_per_rank=mr, dst=[x.data_ptr() for x in afull], dst_ld=H,
+                  ag_cnt=[p + 8 * world for p in ptr], store_h=1, recv=recv[0].data_ptr(), rs_cnt=ptr[0], rs_off=1)
+        return lambda: tpops.norm_push(h, wn, 1e-5, tp), 0
+    if what == "swiglu_ag":
+        wgu = (torch.randn(2 * I // world, H, device="cuda") * 0.02).to(BF)
+        act = torch.empty(world * mr, I // world, device="cuda", dtype=BF)
+        tp = dict(world=world, rank=0, rows_per_rank=mr, ag_cnt=ptr[0] + 8 * world, ag_off=1, m_rot=0)
+        return lambda: tpops.linear_swiglu_ag(afull[0], wgu, act, tp), 2 * world * mr * (2 * I // world) * H
+    raise SystemExit(f"unknown tensor-parallel case {what}")
+
+
+def bench_tp_kernels(t: Timer, out: list):
+    """The fused TP kernels of one MLP hop at TP = 2 and 4 (8192 tokens), each driven from GPU 0
+    (see _tp_case): CUDA-event times, GEMM rates, and the bytes each kernel pushes over NVLink."""
+    for world in (2, 4):
+        if torch.cuda.device_count() < world:
+            continue
+        for what in ("rs", "norm", "swiglu_ag"):
+            fn, fl = _tp_case(world, what)
+            ms = t(fn)
+            mr, H = 8192 // world, 4096
+            nv = {"rs": (world - 1) * mr * H * 2, "norm": (world - 1) * mr * H * 2, "swiglu_ag": 0}[what]
+            row = dict(kernel=f"tp{world}_{what}", tokens=8192, ms=ms, nvlink_mb=nv / 1e6,
+                       nvlink_gbs=nv / ms / 1e6 if nv else None)
+            if fl:
+                row["tflops"] = fl / ms / 1e9
+            out.append(row)
+            torch.cuda.synchronize()
+            ops.core.check_status()
+
+
 def profile(case: str) -> None:
     """Three launches of one kernel on a small case (for `ncu -k <kernel> -c 3`)."""
-    if case == "gemm_gate_up":
+    if case.startswith("tp") and case[2:3].isdigit():  # tp2_rs, tp4_norm, tp2_swiglu_ag, ...
+        fn, _ = _tp_case(int(case[2]), case.split("_", 1)[1], tokens=4096)
+    elif case == "gemm_gate_up":
         a = torch.randn(4096, 4096, device="cuda").to(BF)
         w = (torch.randn(28672, 4096, device="cuda") * 0.02).to(BF)
         c = torch.empty(4096, 28672, device="cuda", dtype=BF)
@@ -365,7 +434,8 @@ def main(argv=None):
     res: list = []
     for name in args.only.split(","):
         {"gemm": bench_gemm, "gemm_fp8": bench_gemm_fp8, "decode": bench_decode, "prefill": bench_prefill, "norm": bench_norm,
-         "moe": bench_moe, "pd_qkv": bench_pd_qkv, "prefill_timeline": prefill_timeline}[name](t, res)
+         "moe": bench_moe, "pd_qkv": bench_pd_qkv, "prefill_timeline": prefill_timeline,
+         "tp": bench_tp_kernels}[name](t, res)
     for r in res:
         print(json.dumps({k: (round(v, 4) if isinstance(v, float) else v) for k, v in r.items()}))
 
