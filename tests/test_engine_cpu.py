@@ -437,3 +437,24 @@ def test_overlap_timeline_launches_next_step_before_collecting():
     assert launches == collects and len(launches) >= 6  # each step collected once, in launch order
     for i in range(len(launches) - 1):  # collect(n) only after launch(n + 1)
         assert timeline.index(("collect", launches[i])) > timeline.index(("launch", launches[i + 1]))
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+def test_idle_expert_parallel_rank_takes_every_step(overlap):
+    """An expert-parallel rank with nothing scheduled still launches one (zero-token) forward
+    per engine step, synchronous or overlapped, so the group's exchange counts stay aligned with
+    ranks that have work."""
+    eng = LLMEngine("tiny", device="cpu", max_running=4, max_batched_tokens=64, max_model_len=256, num_blocks=64,
+                    overlap=overlap)
+    eng.ec.ep = (1, 2, None)  # as rank 1 of a 2-rank group (the exchange itself needs GPUs)
+    calls = []
+    eng.runner.execute_null = lambda: calls.append(len(calls))
+    for _ in range(3):
+        assert eng.step() == []
+    assert len(calls) == 3
+    eng.add_request([5, 6, 7], max_new_tokens=2)
+    while eng.has_unfinished():
+        eng.step()
+    n = len(calls)
+    eng.step()
+    assert len(calls) == n + 1
