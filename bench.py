@@ -721,6 +721,10 @@ def main():
                        "global_batch": args.running * (n_d if mode == "pd" else world // args.tp),
                        "seq_len": args.input_len + args.output_len, "input_len": args.input_len,
                        "output_len": args.output_len, "parallelism": par, "mode": mode,
+                       "layout_note": ("single-GPU prefill/decode pairs, decode instances prefilling their saturated "
+                                       "partners' overflow; the named TP4 prefill + TP4 decode layout runs with --tp 4 "
+                                       "and measured fewer tokens per GPU on 8 B200s"
+                                       if mode == "pd" and args.tp == 1 and not args.ep else None),
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",
                        "arrivals": (f"poisson {args.arrival_rate:g} req/s per request source" if args.arrival_rate
                                     else "closed loop: a new request whenever one finishes (saturated)"),
