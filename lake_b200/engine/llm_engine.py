@@ -357,11 +357,6 @@ class LLMEngine:
         out.prefill = [c for c in out.prefill if c.req.status == RequestStatus.RUNNING]
         res, self._drained = self._drained, []
         if out.is_empty:
-            if self.ec.ep is not None and self.ec.ep[1] > 1:
-                # every call launches one forward on every expert-parallel rank: an idle rank joins
-                # the group's exchange with a zero-token step (stream-ordered after the in-flight one)
-                self.runner.execute_null()
-                self.step_count += 1
             return res + self._finish_inflight()
         bitmask = self._bitmask(out)
         if bitmask is not None:

@@ -439,13 +439,11 @@ def test_overlap_timeline_launches_next_step_before_collecting():
         assert timeline.index(("collect", launches[i])) > timeline.index(("launch", launches[i + 1]))
 
 
-@pytest.mark.parametrize("overlap", [False, True])
-def test_idle_expert_parallel_rank_takes_every_step(overlap):
+def test_idle_expert_parallel_rank_takes_every_step():
     """An expert-parallel rank with nothing scheduled still launches one (zero-token) forward
-    per engine step, synchronous or overlapped, so the group's exchange counts stay aligned with
-    ranks that have work."""
-    eng = LLMEngine("tiny", device="cpu", max_running=4, max_batched_tokens=64, max_model_len=256, num_blocks=64,
-                    overlap=overlap)
+    per engine step (expert-parallel engines step synchronously), so the group's exchange counts
+    stay aligned with ranks that have work."""
+    eng = LLMEngine("tiny", device="cpu", max_running=4, max_batched_tokens=64, max_model_len=256, num_blocks=64)
     eng.ec.ep = (1, 2, None)  # as rank 1 of a 2-rank group (the exchange itself needs GPUs)
     calls = []
     eng.runner.execute_null = lambda: calls.append(len(calls))
