@@ -887,7 +887,10 @@ void set_gemm_pair_mode(int mode) { g_pair_mode = mode; }
 int gemm_pair_mode() { return g_pair_mode; }
 
 // W8A8 activation workspace per device: e4m3 rows [M x K] and their scales [M x K/128], reserved
-// outside any graph capture (gemm_w8a8_reserve); a GEMM that does not fit runs as W8A16.
+// outside any graph capture (gemm_w8a8_reserve); a GEMM that does not fit runs as W8A16. Every
+// W8A8 GEMM of a device quantises into the same buffer, so W8A8 GEMMs run on one stream at a time
+// (as the engine issues them); two streams issuing them concurrently would overwrite each other's
+// activations.
 static int g_w8a8_min_m = 256;
 void set_gemm_w8a8_min_m(int m) { g_w8a8_min_m = m; }
 static uint8_t* s_a8_q[16] = {};

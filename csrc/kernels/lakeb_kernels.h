@@ -126,6 +126,7 @@ int quantize_fp8_rows(const __nv_bfloat16* x, int64_t ldx, int M, int K, uint8_t
 void set_gemm_w8a8_min_m(int m);
 // Runs fp8-weight GEMMs with M >= the threshold as W8A8 from now on when the device's activation
 // workspace holds M x K (allocated here; call outside graph capture). Returns false on failure.
+// The workspace is shared by the device's W8A8 GEMMs: issue them from one stream at a time.
 bool gemm_w8a8_reserve(int64_t M, int64_t K);
 
 // Two-SM (cta_group::2) GEMM for large M; epilogues: store bf16, residual, SwiGLU, fp32.
