@@ -92,6 +92,9 @@ def parse():
                          "(colocated engine or decode instance); 0 = closed loop (saturated)")
     ap.add_argument("--prefill-queue", type=int, default=8,
                     help="pd mode: grants outstanding at a prefill rank (bounds queueing delay)")
+    ap.add_argument("--pd-mesh", action="store_true",
+                    help="pd mode, single-GPU instances: every prefill instance serves every decode instance "
+                         "(a prefill step holds one destination's prompts), ~60%% of the GPUs prefilling")
     ap.add_argument("--local-prefill", type=int, default=1,
                     help="pd mode: a single-GPU decode instance whose prefill partners are saturated "
                          "prefills new requests itself (1, default) or only queues them (0)")
@@ -385,14 +388,22 @@ def pd_split(world: int, prefill_ranks: int = 0) -> tuple[int, int]:
     return world - n_d, n_d
 
 
-def pd_layout(world: int, tp: int, prefill_instances: int = 0, n_experts: int = 0) -> tuple[int, int]:
+def pd_layout(world: int, tp: int, prefill_instances: int = 0, n_experts: int = 0,
+              mesh: bool = False) -> tuple[int, int]:
     """(prefill, decode) instance counts for instances of `tp` GPUs each. With expert-parallel
     decode (`n_experts` > 0) the decode ranks form one EP group, so their count divides the
-    expert count: the divisor nearest the ~40% share (8 GPUs: 4 + 4)."""
+    expert count: the divisor nearest the ~40% share (8 GPUs: 4 + 4). With `mesh` (every
+    prefill instance serves every decode instance) ~60 % of the GPUs prefill (2: 1 + 1,
+    4: 2 + 2, 8: 5 + 3), the share at which one prefill GPU's prompts keep ~0.6 decode GPUs busy
+    at a full batch."""
     if n_experts and not prefill_instances:
         share = world * 0.4
         n_d = min((d for d in range(1, world) if n_experts % d == 0), key=lambda d: (abs(d - share), -d))
         return world - n_d, n_d
+    if mesh and not prefill_instances:
+        n = world // tp
+        n_d = max(1, round(n * 0.4))
+        return n - n_d, n_d
     return pd_split(world // tp, prefill_instances)
 
 
@@ -412,12 +423,15 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
     from lake_b200.parallel import pd
 
     T = args.tp
-    n_p, n_d = pd_layout(world, T, args.prefill_ranks, _n_experts(args) if args.ep else 0)
+    mesh = bool(args.pd_mesh) and T == 1 and not args.ep
+    n_p, n_d = pd_layout(world, T, args.prefill_ranks, _n_experts(args) if args.ep else 0, mesh)
     inst = rank // T
     members = list(range(inst * T, inst * T + T))
     leader = members[0] == rank
     role = "prefill" if inst < n_p else "decode"
-    if role == "prefill":
+    if mesh:  # every prefill instance serves every decode instance
+        partner = list(range(n_p, n_p + n_d)) if role == "prefill" else list(range(n_p))
+    elif role == "prefill":
         d_inst = n_p + inst % n_d
         partner = list(range(d_inst * T, d_inst * T + T))  # the decode instance's ranks
     else:
@@ -444,8 +458,11 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=ep_group)
         return bool(t.item())
     job = os.environ.get("TORCHELASTIC_RUN_ID", "bench").replace("-", "")[:16] + str(os.getpid() if world == 1 else 0)
-    side = pd.connect_pair(eng, role, rank, partner if T > 1 or role == "decode" else partner[0], group, job=job,
-                           members=members)
+    if mesh and role == "prefill":
+        side = pd.connect_pair(eng, role, rank, None, group, job=job, members=members, decode_instances=partner)
+    else:
+        side = pd.connect_pair(eng, role, rank, partner if T > 1 or role == "decode" else partner[0], group,
+                               job=job, members=members)
     w = Window()
     if role == "prefill":
         pd.serve_prefill(side, until_mark=1)          # populate + warm-up
@@ -704,8 +721,10 @@ def main():
     if rank == 0:
         p50 = (lambda xs: sorted(xs)[len(xs) // 2] if xs else None)
         kv_gbs = sm[6].item() / (wall_ms / 1000.0) / 1e9 if sm[6].item() else None
-        n_p, n_d = pd_layout(world, args.tp, args.prefill_ranks, _n_experts(args) if args.ep else 0)
+        mesh = bool(args.pd_mesh) and args.tp == 1 and not args.ep
+        n_p, n_d = pd_layout(world, args.tp, args.prefill_ranks, _n_experts(args) if args.ep else 0, mesh)
         par = (f"pd: {n_p} prefill + {n_d} decode instances (tp{args.tp} each)" +
+               (", every prefill instance serving every decode instance" if mesh else "") +
                (f", decode ranks expert-parallel ep{n_d} (fused dispatch/combine)" if ep_group is not None else "")
                ) if mode == "pd" else (
             f"dp{world // args.tp} x tp{args.tp} (fused NVLink collectives)" if args.tp > 1 else
@@ -724,7 +743,8 @@ def main():
                        "layout_note": ("single-GPU prefill/decode pairs, decode instances prefilling their saturated "
                                        "partners' overflow; the named TP4 prefill + TP4 decode layout runs with --tp 4 "
                                        "and measured fewer tokens per GPU on 8 B200s"
-                                       if mode == "pd" and args.tp == 1 and not args.ep else None),
+                                       if mode == "pd" and args.tp == 1 and not args.ep and not args.pd_mesh
+                                       else None),
                        "l2": "inputs larger than L2 (16 GB weights, >60 GB KV read per step)",
                        "arrivals": (f"poisson {args.arrival_rate:g} req/s per request source" if args.arrival_rate
                                     else "closed loop: a new request whenever one finishes (saturated)"),

@@ -199,6 +199,7 @@ class LLMEngine:
         if ec.ep is not None and ec.ep[1] > 1:
             self.runner.lazy_capture = False
         self.requests: dict[str, Request] = {}
+        self.peer_arenas: list = []  # decode arenas of a prefill instance serving several (set_peer_arenas)
         self.pool_iface = None  # PoolIface (storage-pool fences), attached by attach_pool
         self.overlap = ec.overlap and not (ec.ep and ec.ep[1] > 1) and ec.spec_tokens == 0
         self.inflight = None  # (SchedulerOutput, runner handle) of the launched, unfinished step
@@ -274,14 +275,37 @@ class LLMEngine:
         return req
 
     def add_remote_prefill(self, prompt: list[int], remote_blocks: list[int], rid: str | None = None,
-                           arrival: float | None = None) -> str:
+                           arrival: float | None = None, dest: int = 0) -> str:
         """Prefill side of PD-split: compute the prompt, write its K/V into the decode
-        instance's pages `remote_blocks` (runner.peer_arena) and sample the first token."""
-        if self.runner.peer_arena is None:
+        instance's pages `remote_blocks` (runner.peer_arena, or with several decode instances
+        attached through set_peer_arenas, the arena of instance `dest`) and sample the first
+        token."""
+        if self.runner.peer_arena is None and not self.peer_arenas:
             raise RuntimeError("no peer arena attached (parallel.pd attaches the decode instance's arena)")
+        if self.peer_arenas and not 0 <= dest < len(self.peer_arenas):
+            raise ValueError(f"destination {dest} not among the {len(self.peer_arenas)} attached decode arenas")
         rid = self.add_request(prompt, max_new_tokens=1, rid=rid, arrival=arrival)
-        self.requests[rid].remote_blocks = list(remote_blocks)
+        req = self.requests[rid]
+        req.remote_blocks = list(remote_blocks)
+        req.meta["pd_dest"] = dest
         return rid
+
+    def set_peer_arenas(self, arenas: list) -> None:
+        """A prefill instance serving several decode instances: their arenas, indexed by the
+        `dest` of add_remote_prefill. Each step then holds remote prefills of one destination
+        only (the scheduler groups them) and its K/V stores go to that destination's arena."""
+        self.peer_arenas = list(arenas)
+        self.runner.peer_arena = self.peer_arenas[0] if self.peer_arenas else None
+        self.scheduler.group_of = ((lambda r: r.meta.get("pd_dest") if r.remote_blocks is not None else None)
+                                   if len(self.peer_arenas) > 1 else None)
+
+    def _select_peer(self, out: SchedulerOutput) -> None:
+        """Point the runner at the destination arena of this step's remote prefills."""
+        if len(self.peer_arenas) > 1:
+            for ch in out.prefill:
+                if ch.req.remote_blocks is not None:
+                    self.runner.peer_arena = self.peer_arenas[ch.req.meta.get("pd_dest", 0)]
+                    return
 
     def _copy_cached_to_peer(self, out: SchedulerOutput) -> None:
         """Prefix pages served from this instance's cache are not recomputed, so their
@@ -326,6 +350,7 @@ class LLMEngine:
                 self.step_count += 1
             return []
         bitmask = self._bitmask(out)
+        self._select_peer(out)
         if self.runner.peer_arena is not None:
             self._copy_cached_to_peer(out)
         if self.pool_iface is not None:
@@ -361,6 +386,7 @@ class LLMEngine:
         bitmask = self._bitmask(out)
         if bitmask is not None:
             res += self._finish_inflight()  # the masks apply to the tokens after the in-flight ones
+        self._select_peer(out)
         if self.runner.peer_arena is not None:
             self._copy_cached_to_peer(out)
         handle = self.runner.launch(out, bitmask)

@@ -31,6 +31,9 @@ from .block_pool import BlockPool, chain_block_hashes
 from .request import PENDING, Request, RequestStatus
 
 
+_NO_GROUP = object()  # no prefill group chosen for the step yet
+
+
 @dataclass
 class Chunk:
     req: Request
@@ -137,6 +140,11 @@ class Scheduler:
         self.spec_stats = {"proposed": 0, "accepted": 0, "verify_chunks": 0}
         self.itl = (ItlGovernor(self.cfg.itl_target_ms, self.cfg.max_batched_tokens, self.cfg.itl_min_prefill)
                     if self.cfg.itl_target_ms > 0 else None)
+        # group_of(req) -> key or None: prefill chunks of one step all share one key (requests
+        # whose key is None join any step). A prefill instance serving several decode instances
+        # keys each remote prefill by its destination, because a step's K/V stores go to one
+        # destination arena. None = no constraint.
+        self.group_of = None
 
     # -------------------------------------------------------------- admission
     def add(self, req: Request) -> None:
@@ -244,19 +252,36 @@ class Scheduler:
                 budget = min(budget, self.itl.cap)
             else:
                 self.itl.idle()
+        group = _NO_GROUP
         for req in list(self.running):
             if budget <= 0:
                 break
             if not req.is_prefill or req.status != RequestStatus.RUNNING:
                 continue
+            if self.group_of is not None:
+                key = self.group_of(req)
+                if key is not None:
+                    if group is _NO_GROUP:
+                        group = key
+                    elif key != group:
+                        continue  # another destination: a later step
             n = min(len(req.prompt) - req.num_computed, budget, cap)
             if not self._ensure_blocks(req, req.num_computed + n, out):
                 break
             out.prefill.append(Chunk(req, req.num_computed, n, req.num_computed + n == len(req.prompt)))
             budget -= n
-        # Pass C: admit
+        # Pass C: admit (with a group constraint: the oldest waiting request of the step's group,
+        # or of any group when the step has none yet)
         while self.waiting and budget > 0 and len(self.running) < self.cfg.max_running:
-            req = self.waiting[0]
+            idx = 0
+            if self.group_of is not None and group is not _NO_GROUP:
+                idx = next((i for i, r in enumerate(self.waiting)
+                            if self.group_of(r) is None or self.group_of(r) == group), -1)
+                if idx < 0:
+                    break
+            req = self.waiting[idx]
+            if self.group_of is not None and group is _NO_GROUP and self.group_of(req) is not None:
+                group = self.group_of(req)
             if not req.block_hashes:
                 req.block_hashes = chain_block_hashes(req.prompt, self.bs, full_only=True)
             usable = req.block_hashes[: (len(req.prompt) - 1) // self.bs]
@@ -269,7 +294,7 @@ class Scheduler:
             if not self.pool.can_alloc(need):
                 self.pool.release(hit)
                 break
-            self.waiting.popleft()
+            del self.waiting[idx]
             req.block_ids = hit + self.pool.alloc(need)
             req.num_computed = cached
             req.num_cached = cached

@@ -294,12 +294,23 @@ class DecodeSide:
 
 
 class PrefillSide:
-    def __init__(self, eng: LLMEngine, from_d: ShmRing | None, to_d: ShmRing | None, ctl: GroupCtl | None = None):
+    """Prefill instance's side of PD-split. It may serve several decode instances
+    (one-to-many, single-GPU instances): `links` holds one (from_d, to_d) ring pair per decode
+    instance, a grant's destination is the link it came on, and it exits once every decode
+    instance has sent EXIT."""
+
+    def __init__(self, eng: LLMEngine, from_d: ShmRing | None, to_d: ShmRing | None, ctl: GroupCtl | None = None,
+                 links: list[tuple[ShmRing, ShmRing]] | None = None):
         self.eng = eng
-        self.from_d, self.to_d = from_d, to_d  # the leader's links (None on followers)
+        self.links = links if links is not None else ([(from_d, to_d)] if from_d is not None else [])
+        if len(self.links) > 1 and ctl is not None:
+            raise ValueError("a tensor-parallel prefill instance feeds one decode instance")
+        self.from_d, self.to_d = (self.links[0] if self.links else (from_d, to_d))  # the leader's first link
         self.ctl = ctl
         self.marks: list[int] = []
         self.exit = False
+        self.exits = 0
+        self.origin: dict[str, tuple[int, int]] = {}  # engine request id -> (link, the decode side's index)
         self.first_tokens = 0
         self.events: list[tuple] = []
         self.steps = 0
@@ -310,23 +321,34 @@ class PrefillSide:
         return self.ctl is not None and not self.ctl.is_leader
 
     def poll(self) -> None:
-        while True:
-            m = self.from_d.get()
-            if m is None:
-                return
-            kind = int(m[0])
-            if kind == GRANT:
-                idx, nb = int(m[1]), int(m[3])
-                blocks = m[4:4 + nb].tolist()
-                plen = int(m[4 + nb])
-                prompt = m[5 + nb:5 + nb + plen].tolist()
-                self.eng.add_remote_prefill(prompt, blocks, rid=f"pd-{idx}")
-                if self.ctl is not None:
-                    self.events.append((EV_GRANT, idx, 0, 0, prompt, blocks))
-            elif kind == MARK:
-                self.marks.append(int(m[1]))
-            elif kind == EXIT:
-                self.exit = True
+        for li, (from_d, _) in enumerate(self.links):
+            while True:
+                m = from_d.get()
+                if m is None:
+                    break
+                kind = int(m[0])
+                if kind == GRANT:
+                    idx, nb = int(m[1]), int(m[3])
+                    blocks = m[4:4 + nb].tolist()
+                    plen = int(m[4 + nb])
+                    prompt = m[5 + nb:5 + nb + plen].tolist()
+                    rid = f"pd-{idx}" if len(self.links) == 1 else f"pd{li}-{idx}"
+                    self.origin[rid] = (li, idx)
+                    self.eng.add_remote_prefill(prompt, blocks, rid=rid, dest=li if len(self.links) > 1 else 0)
+                    if self.ctl is not None:
+                        self.events.append((EV_GRANT, idx, 0, 0, prompt, blocks))
+                elif kind == MARK:
+                    self.marks.append(int(m[1]))
+                elif kind == EXIT:
+                    self.exits += 1
+                    self.exit = self.exits >= len(self.links)
+
+    def mark_complete(self, code: int) -> bool:
+        """Every decode instance this side serves has sent MARK `code` (consumed here)."""
+        if self.marks.count(code) < max(1, len(self.links)):
+            return False
+        self.marks = [c for c in self.marks if c != code]
+        return True
 
     def step(self) -> int:
         self.step_t0 = time.perf_counter()
@@ -341,8 +363,10 @@ class PrefillSide:
                 torch.cuda.synchronize(self.eng.device)
             self.ctl.wait_acks(self.steps)  # every rank's K/V stores into D's arenas completed
         for o in outs:
-            idx = int(o.rid.split("-", 1)[1])
-            self.to_d.put_wait([DONE, idx, o.new_tokens[0]])
+            li, idx = self.origin.pop(o.rid, (0, None))
+            if idx is None:
+                idx = int(o.rid.split("-", 1)[1])
+            self.links[li][1].put_wait([DONE, idx, o.new_tokens[0]])
         self.first_tokens += len(outs)
         return len(outs)
 
@@ -381,7 +405,8 @@ class PrefillSide:
         return not self.eng.has_unfinished()
 
     def close(self) -> None:
-        _close_rings([r for r in (self.from_d, self.to_d) if r is not None], self.ctl)
+        _close_rings([r for link in self.links for r in link if r is not None] or
+                     [r for r in (self.from_d, self.to_d) if r is not None], self.ctl)
 
 
 def _close_rings(rings, ctl) -> None:
@@ -402,7 +427,8 @@ def ring_names(job: str, d_rank: int, p_rank: int) -> tuple[str, str]:
 
 
 def connect_pair(eng: LLMEngine, role: str, rank: int, partner, group, job: str,
-                 shm_path: str | None = None, members: list[int] | None = None):
+                 shm_path: str | None = None, members: list[int] | None = None,
+                 decode_instances: list[int] | None = None):
     """Wire prefill and decode instances. Each decode instance D exports its arena and its
     leader creates one ring pair per prefill partner; a prefill instance P maps its D's
     arena and its leader opens their rings. Collective over `group` (every rank calls it).
@@ -411,7 +437,12 @@ def connect_pair(eng: LLMEngine, role: str, rank: int, partner, group, job: str,
     single-GPU instance); an instance is named by its leader `members[0]`. `partner` is, on
     the decode side, the list of prefill leaders feeding this instance; on the prefill side,
     the decode instance's member list (or its single rank). P's TP rank i maps the arena of
-    D's TP rank i (the same KV heads)."""
+    D's TP rank i (the same KV heads).
+
+    `decode_instances` (prefill side, single-GPU instances): the ranks of several single-GPU
+    decode instances this prefill instance serves (one-to-many); it maps every one of their
+    arenas and opens a ring pair to each. Each of those decode instances lists this rank among
+    its `partner` prefill leaders."""
     import torch.distributed as dist
 
     world = dist.get_world_size(group)
@@ -431,6 +462,23 @@ def connect_pair(eng: LLMEngine, role: str, rank: int, partner, group, job: str,
         ctl.open()
     if role == "decode":
         return DecodeSide(eng, links, ctl)
+    if decode_instances:
+        if len(members) > 1:
+            raise ValueError("a tensor-parallel prefill instance feeds one decode instance")
+        if eng.arena.is_cuda:
+            torch.cuda.set_device(eng.arena.device)
+        arenas = []
+        for d in decode_instances:
+            peer = import_tensor([g for g in gathered if g[0] == d][0][2])
+            if peer.shape[1:] != eng.arena.shape[1:]:
+                raise ValueError(f"peer arena layout {tuple(peer.shape)} does not match {tuple(eng.arena.shape)}")
+            arenas.append(peer)
+        eng.set_peer_arenas(arenas)
+        plinks = []
+        for d in decode_instances:
+            a, b = ring_names(job, d, rank)
+            plinks.append((ShmRing(a), ShmRing(b)))
+        return PrefillSide(eng, None, None, None, links=plinks)
     d_members = list(partner) if isinstance(partner, (list, tuple)) else [partner]
     if len(d_members) != len(members):
         raise ValueError(f"prefill instance of {len(members)} ranks cannot feed a decode instance of "
@@ -460,13 +508,13 @@ def serve_prefill(side: PrefillSide, until_mark: int | None = None, idle_sleep_s
                 return
         return
     while not side.exit:
-        if until_mark is not None and until_mark in side.marks:
-            side.marks.remove(until_mark)
+        if until_mark is not None and side.mark_complete(until_mark):
             side.phase(until_mark)
             return
         if side.idle():
             side.poll()
-            if side.idle() and not side.exit and (until_mark is None or until_mark not in side.marks):
+            if side.idle() and not side.exit and (until_mark is None or side.marks.count(until_mark)
+                                                  < max(1, len(side.links))):
                 time.sleep(idle_sleep_s)
             continue
         side.step()

@@ -32,6 +32,7 @@ def test_pd_layouts():
     assert b.pd_split(8, prefill_ranks=5) == (5, 3)
     assert b.pd_layout(8, 4) == (1, 1) and b.pd_layout(4, 2) == (1, 1)
     assert b.pd_layout(8, 1, n_experts=8) == (4, 4)  # expert-parallel decode ranks divide the experts
+    assert [b.pd_layout(n, 1, mesh=True) for n in (2, 4, 8)] == [(1, 1), (2, 2), (5, 3)]
 
 
 def test_prefill_window_clipping():

@@ -117,6 +117,80 @@ def test_pd_many_prefill_to_one_decode(tmp_path):
     assert res["outs"] == res["want"]
 
 
+def _worker_mesh(rank, port, out_dir):
+    """Two prefill ranks [0, 1] each serve both decode ranks [2, 3] (many-to-many): a prefill
+    step holds the grants of one decode instance only and stores its K/V into that instance's
+    arena; every decode instance's tokens equal a colocated run."""
+    import time
+
+    import torch.distributed as dist
+
+    from lake_b200.engine.llm_engine import LLMEngine
+    from lake_b200.parallel import pd
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=4)
+    decoders = dist.new_group([2, 3])  # collective: every rank creates it
+    role = "prefill" if rank < 2 else "decode"
+    eng = LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512,
+                    num_blocks=96, shared_arena=(role == "decode"))
+    if role == "prefill":
+        side = pd.connect_pair(eng, role, rank, None, None, job=f"x{port}", shm_path=eng.arena_path,
+                               decode_instances=[2, 3])
+        steps = []
+        real_step = eng.step
+
+        def step():  # record each step's destinations
+            out = real_step()
+            if eng.last_step is not None:
+                steps.append(sorted({c.req.meta.get("pd_dest") for c in eng.last_step.prefill}))
+            return out
+
+        eng.step = step
+        pd.serve_prefill(side)
+        res = {"dests": steps}
+    else:
+        side = pd.connect_pair(eng, role, rank, [0, 1], None, job=f"x{port}", shm_path=eng.arena_path)
+        prompts = _prompts() if rank == 2 else [p[::-1] for p in _prompts()]
+        for p in prompts:
+            assert side.submit(p, 6)
+        t0 = time.perf_counter()
+        while side.inflight:
+            side.poll()
+            if eng.has_unfinished():
+                eng.step()
+            else:
+                time.sleep(0.001)
+            assert time.perf_counter() - t0 < 120
+        res = {"outs": [eng.requests[f"pd-{i}"].output for i in range(len(prompts))],
+               "want": LLMEngine("tiny", device="cpu", max_running=8, max_batched_tokens=64, max_model_len=512,
+                                 num_blocks=96).generate(prompts, max_new_tokens=6),
+               "linked": len(side.links)}
+        dist.barrier(group=decoders)  # both decode instances done before either exits
+        side.shutdown()
+    with open(os.path.join(out_dir, f"x{rank}.json"), "w") as f:
+        json.dump(res, f)
+    dist.barrier()
+    side.close()
+    dist.destroy_process_group()
+    if eng.arena_path:
+        from lake_b200.parallel.peer import unlink_shared
+
+        unlink_shared(eng.arena_path)
+
+
+def test_pd_many_to_many_prefill_serves_several_decode_instances(tmp_path):
+    port = _free_port()
+    mp.spawn(_worker_mesh, args=(port, str(tmp_path)), nprocs=4, join=True)
+    for r in (2, 3):
+        res = json.load(open(tmp_path / f"x{r}.json"))
+        assert res["outs"] == res["want"] and res["linked"] == 2
+    dests = [d for r in (0, 1) for d in json.load(open(tmp_path / f"x{r}.json"))["dests"]]
+    assert all(len(d) <= 1 for d in dests)  # one destination per prefill step
+    assert {x for d in dests for x in d} == {0, 1}  # and both destinations were served
+
+
 def _worker_groups(rank, port, out_dir):
     """Two-rank prefill instance [0, 1] feeds a two-rank decode instance [2, 3]: the leaders
     decide, the followers replay (page grants, adoptions, steps) through GroupCtl, and P's
