@@ -73,9 +73,15 @@ std::vector<std::string> PutEndSession::flush_durable(tier::TierEngine& store) {
     if (b.bytes.size() != store.block_bytes())
       throw std::invalid_argument("flush: block size mismatch (" + std::to_string(b.bytes.size()) + " vs " +
                                   std::to_string(store.block_bytes()) + ")");
-    auto [t, fx] = store.put_durable(b.id.block_hash, b.bytes.data());
-    (void)t;
-    demoted.insert(demoted.end(), fx.l2_demoted_to_l3.begin(), fx.l2_demoted_to_l3.end());
+    // A block is named by the chain hash of its content: one that is already durable (an
+    // earlier attempt of this commit, or another request's) is not written again, so a retry
+    // neither moves its L2 record away from the slot the control plane was told about nor
+    // brings a block the cap moved to L3 back into L2.
+    if (!store.has_durable_backing(b.id.block_hash)) {
+      auto [t, fx] = store.put_durable(b.id.block_hash, b.bytes.data());
+      (void)t;
+      demoted.insert(demoted.end(), fx.l2_demoted_to_l3.begin(), fx.l2_demoted_to_l3.end());
+    }
     b.durable = store.has_durable_backing(b.id.block_hash);
     if (!b.durable) throw std::runtime_error("flush: block not settled on L2|L3");
   }

@@ -130,6 +130,20 @@ Placement SegmentArena::place_at(const std::string& h, uint64_t seg, uint64_t of
   return pl;
 }
 
+Placement SegmentArena::alloc_spare(const std::string& h) { return alloc(spare_key(h)); }
+
+void SegmentArena::commit_spare(const std::string& h) {
+  auto sp = where_.find(spare_key(h));
+  if (sp == where_.end()) fail("commit_spare: no spare slot");
+  const Placement pl = sp->second;
+  where_.erase(sp);
+  free(h);
+  segs_[pl.segment_id][pl.offset / slot_bytes_] = h;
+  where_[h] = pl;
+}
+
+void SegmentArena::drop_spare(const std::string& h) { free(spare_key(h)); }
+
 bool SegmentArena::free(const std::string& h) {
   auto it = where_.find(h);
   if (it == where_.end()) return false;
@@ -240,7 +254,8 @@ TierEngine::TierEngine(TierCaps caps, uint64_t block_bytes, uint8_t* l1_base, co
       model_key_(model_key),
       arena_(block_bytes + kBlockHeaderBytes, 64) {
   if (!block_bytes_) fail("TierEngine: block_bytes must be > 0");
-  if (!l2_dir_.empty()) mkdirs(l2_dir_);
+  if (l2_dir_.empty()) fail("TierEngine: an L2 directory is required (L2 is the durable recovery point)");
+  mkdirs(l2_dir_);
   if (!l3_dir_.empty()) mkdirs(l3_dir_ + "/" + model_key_);
   for (int64_t s = int64_t(caps_.l1) - 1; s >= 0; --s) free_slots_.push_back(s);
 }
@@ -301,13 +316,25 @@ bool TierEngine::read_record(int fd, const std::string& h, uint8_t* dst, uint64_
 // the block as durable right after this returns.
 bool TierEngine::write_l2(const std::string& h, const uint8_t* bytes) {
   Placement pl = arena_.alloc(h);
-  if (l2_dir_.empty()) return true;
   const int fd = segment_fd(pl.segment_id);
   return fd >= 0 && write_record(fd, h, bytes, pl.offset) && ::fdatasync(fd) == 0;
 }
+// Copy-on-write overwrite of a resident block: the new record goes to a spare slot and
+// replaces the old one only once it is on the device, so a failed write leaves the previous
+// record readable where the control plane last saw it.
+bool TierEngine::overwrite_l2(const std::string& h, const uint8_t* bytes) {
+  const Placement pl = arena_.alloc_spare(h);
+  const int fd = segment_fd(pl.segment_id);
+  if (fd < 0 || !write_record(fd, h, bytes, pl.offset) || ::fdatasync(fd) != 0) {
+    arena_.drop_spare(h);
+    return false;
+  }
+  arena_.commit_spare(h);
+  return true;
+}
 bool TierEngine::read_l2(const std::string& h, uint8_t* dst) const {
   auto pl = arena_.placement(h);
-  if (!pl || l2_dir_.empty()) return false;
+  if (!pl) return false;
   const int fd = segment_fd(pl->segment_id);
   return fd >= 0 && read_record(fd, h, dst, pl->offset);
 }
@@ -390,6 +417,20 @@ void TierEngine::drop_l0(const std::string& h) {
   }
 }
 
+void TierEngine::l2_forget(const std::string& h) {
+  l2_.erase(h);
+  arena_.free(h);
+  auto it = l2_pos_.find(h);
+  if (it != l2_pos_.end()) {
+    l2_order_.erase(it->second);
+    l2_pos_.erase(it);
+  }
+}
+
+// Two-phase: the victims (least recently written, unpinned; a pinned block keeps its LRU
+// position) are chosen and their L3 objects written before any leaves L2, so a cap that cannot
+// be met (every candidate pinned) or an L3 write that fails changes nothing (an L3 object this
+// call created is removed again).
 SideEffects TierEngine::ensure_l2_cap() {
   SideEffects fx;
   if (!caps_.l2) return fx;
@@ -403,37 +444,42 @@ SideEffects TierEngine::ensure_l2_cap() {
   }
   if (evictable > caps_.l2) fail("l2 over cap: all victims pinned (unpin before put)");
   std::vector<uint8_t> buf(block_bytes_);
+  std::vector<std::string> created;
   for (auto& v : victims) {
-    bool ok = read_l2(v, buf.data()) || l2_dir_.empty();
-    if (ok && !l3_present(v)) write_l3(v, buf.data());
-    l2_.erase(v);
-    arena_.free(v);
-    auto it = l2_pos_.find(v);
-    l2_order_.erase(it->second);
-    l2_pos_.erase(it);
+    if (l3_present(v)) continue;
+    if (read_l2(v, buf.data()) && write_l3(v, buf.data())) {
+      created.push_back(v);
+      continue;
+    }
+    for (auto& c : created) ::unlink(l3_path(c).c_str());
+    fail("l2 over cap: moving a block to L3 failed");
+  }
+  for (auto& v : victims) {
+    l2_forget(v);
     fx.l2_demoted_to_l3.push_back(v);
   }
   return fx;
 }
 
 std::pair<TierId, SideEffects> TierEngine::put_durable(const std::string& h, const uint8_t* bytes) {
-  bool had = l2_.count(h) != 0;
-  if (!write_l2(h, bytes)) fail("put_durable: L2 write failed");
+  if (l2_.count(h)) {
+    // Blocks are named by the chain hash of their content, so an overwrite carries the same
+    // bytes (it refreshes a torn record); the resident count is unchanged, so no cap demotion.
+    if (!overwrite_l2(h, bytes)) fail("put_durable: L2 write failed (the previous record is kept)");
+    touch(l2_order_, l2_pos_, h);
+    return {TierId::L2, SideEffects{}};
+  }
+  if (!write_l2(h, bytes)) {
+    arena_.free(h);
+    fail("put_durable: L2 write failed");
+  }
   l2_.insert(h);
   touch(l2_order_, l2_pos_, h);
   SideEffects fx;
   try {
     fx = ensure_l2_cap();
   } catch (...) {
-    if (!had) {  // two-phase: undo the insert, leave no state change behind
-      l2_.erase(h);
-      arena_.free(h);
-      auto it = l2_pos_.find(h);
-      if (it != l2_pos_.end()) {
-        l2_order_.erase(it->second);
-        l2_pos_.erase(it);
-      }
-    }
+    l2_forget(h);  // two-phase: undo the insert, leave no state change behind
     throw;
   }
   if (l2_.count(h)) return {TierId::L2, fx};
@@ -561,6 +607,7 @@ std::optional<DeviceCopy> TierEngine::promote_to_l0(const std::string& h, std::v
     l1_[h] = slot;
     touch(l1_order_, l1_pos_, h);
   }
+  if (!l2_.count(h) && l3_present(h)) rehydrate_l2(h, l1_ptr(slot), fx);
   // reserve an L0 page, demoting under pressure
   int64_t page = -1;
   if (l0_.size() < caps_.l0) page = alloc_page ? alloc_page() : -1;
@@ -581,19 +628,33 @@ std::optional<DeviceCopy> TierEngine::promote_to_l0(const std::string& h, std::v
 bool TierEngine::demote_l2_to_l3(const std::string& h) {
   if (!l2_.count(h)) return false;
   if (pin_count(h)) fail("demote_l2_to_l3: block pinned");
-  std::vector<uint8_t> buf(block_bytes_);
-  if (!l2_dir_.empty()) {
+  if (!l3_present(h)) {
+    std::vector<uint8_t> buf(block_bytes_);
     if (!read_l2(h, buf.data())) fail("demote_l2_to_l3: L2 read failed");
-    if (!l3_present(h) && !write_l3(h, buf.data())) fail("demote_l2_to_l3: L3 write failed");
+    if (!write_l3(h, buf.data())) fail("demote_l2_to_l3: L3 write failed");
   }
-  l2_.erase(h);
-  arena_.free(h);
-  auto it = l2_pos_.find(h);
-  if (it != l2_pos_.end()) {
-    l2_order_.erase(it->second);
-    l2_pos_.erase(it);
-  }
+  l2_forget(h);
   return true;
+}
+
+// A block read back from L3 gets an L2 record again (the node's local recovery point for its
+// working set), under the L2 cap; with every L2 resident pinned it stays L3-only.
+void TierEngine::rehydrate_l2(const std::string& h, const uint8_t* bytes, SideEffects* fx) {
+  bool room = !caps_.l2 || l2_.size() < caps_.l2;
+  for (auto it = l2_order_.begin(); !room && it != l2_order_.end(); ++it) room = pin_count(*it) == 0;
+  if (!room) return;  // the cap could only be met by demoting this block again
+  if (!write_l2(h, bytes)) {
+    arena_.free(h);
+    return;
+  }
+  l2_.insert(h);
+  touch(l2_order_, l2_pos_, h);
+  try {
+    SideEffects d = ensure_l2_cap();
+    if (fx) fx->l2_demoted_to_l3.insert(fx->l2_demoted_to_l3.end(), d.l2_demoted_to_l3.begin(), d.l2_demoted_to_l3.end());
+  } catch (const std::invalid_argument&) {  // an L3 write of the victim failed: stay L3-only
+    l2_forget(h);
+  }
 }
 
 void TierEngine::discard(const std::string& h) {
@@ -608,14 +669,7 @@ void TierEngine::discard(const std::string& h) {
       l1_pos_.erase(it);
     }
   }
-  if (l2_.erase(h)) {
-    arena_.free(h);
-    auto it = l2_pos_.find(h);
-    if (it != l2_pos_.end()) {
-      l2_order_.erase(it->second);
-      l2_pos_.erase(it);
-    }
-  }
+  if (l2_.count(h)) l2_forget(h);
   pins_.erase(h);
   hits_.erase(h);
   one_shot_.erase(h);
@@ -623,27 +677,25 @@ void TierEngine::discard(const std::string& h) {
 }
 
 std::vector<Relocate> TierEngine::compact_l2_segment(uint64_t seg) {
-  std::vector<uint8_t> buf(block_bytes_);
   // read every block first, then rewrite at the compacted slots
   std::vector<std::pair<std::string, std::vector<uint8_t>>> data;
   for (auto& h : arena_.hashes_in_segment(seg)) {
     std::vector<uint8_t> b(block_bytes_);
-    if (!l2_dir_.empty() && !read_l2(h, b.data())) fail("compact: L2 read failed");
+    if (!read_l2(h, b.data())) fail("compact: L2 read failed");
     data.emplace_back(h, std::move(b));
   }
   auto moves = arena_.compact(seg);
-  if (!l2_dir_.empty())
-    for (auto& mv : moves)
-      for (auto& [h, b] : data)
-        if (h == mv.hash) write_l2(h, b.data());
+  for (auto& mv : moves)
+    for (auto& [h, b] : data)
+      if (h == mv.hash) write_l2(h, b.data());
   return moves;
 }
 
 Relocate TierEngine::colocate_l2_move(const std::string& h, uint64_t seg, uint64_t offset) {
   std::vector<uint8_t> buf(block_bytes_);
-  if (!l2_dir_.empty() && !read_l2(h, buf.data())) fail("colocate: L2 read failed");
+  if (!read_l2(h, buf.data())) fail("colocate: L2 read failed");
   Relocate r = arena_.relocate(h, seg, offset);
-  if (!l2_dir_.empty()) write_l2(h, buf.data());
+  write_l2(h, buf.data());
   return r;
 }
 
@@ -672,7 +724,17 @@ std::pair<size_t, std::vector<LocationEvent>> TierPipeline::tick(size_t max_step
         case ActionKind::FillMiss: {
           SideEffects fx;
           std::vector<DeviceCopy> ev_copies;
+          const bool was_l2 = eng_->is_l2_durable(a.hash);
           auto c = eng_->promote_to_l0(a.hash, &ev_copies, &fx, alloc_page);
+          for (auto& v : fx.l2_demoted_to_l3) {  // the cap demotions of an L3 block's rehydration
+            if (v == a.hash) continue;
+            ev.push_back({LocKind::Absent, v, 3, node_, 0, 0});
+            ev.push_back({LocKind::L3Present, v, 4, node_, 0, 0});
+          }
+          if (!was_l2 && eng_->is_l2_durable(a.hash)) {
+            auto pl = eng_->l2_placement(a.hash);
+            ev.push_back({LocKind::Present, a.hash, 3, node_, pl ? pl->segment_id : 0, pl ? pl->offset : 0});
+          }
           for (auto& x : ev_copies) {
             copies->push_back(x);
             ev.push_back({LocKind::Absent, x.hash, 1, node_, 0, 0});

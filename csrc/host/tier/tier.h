@@ -53,6 +53,11 @@ class SegmentArena {
   size_t slots_per_segment() const { return per_seg_; }
   std::optional<Placement> placement(const std::string& h) const;
   Placement alloc(const std::string& h);
+  // A second slot for a new record of `h` while its current slot stays valid; commit_spare
+  // makes it h's placement (freeing the old slot), drop_spare gives it back.
+  Placement alloc_spare(const std::string& h);
+  void commit_spare(const std::string& h);
+  void drop_spare(const std::string& h);
   Placement place_at(const std::string& h, uint64_t segment_id, uint64_t offset);
   bool free(const std::string& h);
   std::vector<Relocate> compact(uint64_t segment_id);
@@ -64,6 +69,7 @@ class SegmentArena {
   std::vector<std::string> hashes_in_segment(uint64_t segment_id) const;
 
  private:
+  static std::string spare_key(const std::string& h) { return std::string("\0spare:", 7) + h; }
   uint64_t slot_bytes_;
   size_t per_seg_;
   std::map<uint64_t, std::vector<std::string>> segs_;  // segment -> slot owners ("" = free)
@@ -150,6 +156,8 @@ class TierEngine {
   size_t l0_len() const { return l0_.size(); }
   size_t l1_len() const { return l1_.size(); }
   size_t l2_len() const { return l2_.size(); }
+  // L2 residents from least to most recently written (the cap-demotion order)
+  std::vector<std::string> l2_order() const { return {l2_order_.begin(), l2_order_.end()}; }
   size_t l3_len() const;
   uint32_t hit_count(const std::string& h) const;
   bool is_one_shot(const std::string& h) const { return one_shot_.count(h) != 0; }
@@ -163,7 +171,9 @@ class TierEngine {
   void note_l0(const std::string& h, int64_t page);
   void drop_l0(const std::string& h);
 
-  // durable write: bytes (host) -> L2 segment slot; demotes L2 -> L3 over the cap
+  // durable write: bytes (host) -> L2 segment slot; demotes L2 -> L3 over the cap. On an
+  // error nothing changed: a new block is absent from L2 and L3, an overwritten one keeps its
+  // previous record, and the L2 LRU order is the one before the call.
   std::pair<TierId, SideEffects> put_durable(const std::string& h, const uint8_t* bytes);
   // copy a block's bytes into `dst` from the fastest host tier (L1 > L2 > L3)
   bool read_host(const std::string& h, uint8_t* dst) const;
@@ -173,7 +183,9 @@ class TierEngine {
 
   // Bring a block into an L1 slot (from L2/L3) and reserve an L0 page for it.
   // Returns the device copy to perform (L1 slot -> L0 page); an L0 victim that
-  // must first be copied out is reported in `evict` (page -> its L1 slot).
+  // must first be copied out is reported in `evict` (page -> its L1 slot). A block
+  // read from L3 also gets an L2 record again under the L2 cap (its demotions are
+  // reported in fx->l2_demoted_to_l3); with every L2 resident pinned it stays L3-only.
   std::optional<DeviceCopy> promote_to_l0(const std::string& h, std::vector<DeviceCopy>* evict, SideEffects* fx,
                                           const std::function<int64_t()>& alloc_page);
   BeginPromote begin_promote(const std::string& h);
@@ -199,6 +211,9 @@ class TierEngine {
   std::string seg_path(uint64_t seg) const;
   std::string l3_path(const std::string& h) const;
   bool write_l2(const std::string& h, const uint8_t* bytes);
+  bool overwrite_l2(const std::string& h, const uint8_t* bytes);
+  void l2_forget(const std::string& h);
+  void rehydrate_l2(const std::string& h, const uint8_t* bytes, SideEffects* fx);
   bool read_l2(const std::string& h, uint8_t* dst) const;
   bool write_l3(const std::string& h, const uint8_t* bytes);
   bool read_l3(const std::string& h, uint8_t* dst) const;

@@ -113,6 +113,12 @@ void register_tier(py::module_& m) {
       .def("l0_len", &TierEngine::l0_len)
       .def("l1_len", &TierEngine::l1_len)
       .def("l2_len", &TierEngine::l2_len)
+      .def("l2_order",
+           [](const TierEngine& e) {
+             py::list o;
+             for (auto& h : e.l2_order()) o.append(py::bytes(h));
+             return o;
+           })
       .def("corrupt_reads", &TierEngine::corrupt_reads)
       .def("record_bytes", &TierEngine::record_bytes)
       .def("hit_count", [](const TierEngine& e, const py::bytes& h) { return e.hit_count(std::string(h)); })

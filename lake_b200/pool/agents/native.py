@@ -111,11 +111,13 @@ class NativeAgent(StepFences):
             if not pool.can_alloc(1):
                 break
             page = pool.alloc(1)[0]
+            was_l2 = self.tiers.is_l2_durable(h)
             try:
                 cp, evict, fx = self.tiers.promote_to_l0(h, lambda: page)
             except ValueError:
                 pool.release([page])
                 break
+            self._mirror_l2_moves(h, was_l2, fx)
             if cp is not None:
                 src = self.l1[cp.slot * self.page_bytes:(cp.slot + 1) * self.page_bytes]
                 dst = self._page_view(page)
@@ -136,6 +138,21 @@ class NativeAgent(StepFences):
         self.stats["promoted_blocks"] += promoted
         self.stats["promote_ms"] += (time.perf_counter() - t0) * 1000
         return promoted
+
+    def _mirror_l2_moves(self, h: bytes, was_l2: bool, fx) -> None:
+        """A promotion from L3 writes the block back to L2 (the node's recovery point for its
+        working set) and may move the coldest L2 block to L3 under the cap; the control plane
+        learns both, as the reference's engine mirrors them (rust/tiered-store/src/engine.rs:
+        506-527)."""
+        for v in fx.l2_demoted_to_l3:
+            if v == h:
+                continue
+            vid = self._ids([v])[0]
+            self.port.publish_location(vid, L2, self.node_id, 0, 0, False)
+            self.port.set_l3_present(vid, True)
+        if not was_l2 and self.tiers.is_l2_durable(h):
+            pl = self.tiers.l2_placement(h)
+            self.port.publish_location(self._ids([h])[0], L2, self.node_id, pl.segment_id, pl.offset, True)
 
     # ------------------------------------------------------------ fences
     def prepare_step(self, plan: PreparePlan) -> ReadyHandle:

@@ -140,3 +140,37 @@ def test_engine_steps_through_the_native_agent_and_done_survives_a_failed_step(t
     with pytest.raises(RuntimeError, match="device lost"):
         eng.step()
     assert pool.stats.prepare_calls == pool.stats.done_calls
+
+
+def test_promotion_from_l3_is_written_back_to_l2_and_mirrored_on_the_control_plane(tmp_path):
+    """One pool node (L2 cap of 2 blocks) shared by two engines: the first writes a 5-page
+    prompt back (3 pages end in L3), the second promotes all 5 at admission. Every promotion
+    from L3 gives the page an L2 record again and moves the coldest L2 page to L3; afterwards
+    the authority's L2 locations and L3 flags agree with the tier engine page by page."""
+    from lake_b200 import _host as H
+    from lake_b200.engine.block_pool import chain_block_hashes
+    from lake_b200.engine.llm_engine import LLMEngine
+    from lake_b200.pool.agents.native import NativeAgent, make_pool_node
+
+    kw = dict(device="cpu", max_running=4, max_batched_tokens=128, max_model_len=256, num_blocks=64)
+    a_eng, b_eng = LLMEngine("tiny", **kw), LLMEngine("tiny", **kw)
+    page = a_eng.arena[0].numel() * a_eng.arena.element_size()
+    node = make_pool_node("tiny", page, a_eng.pool.num_blocks, l1_blocks=8, l2_blocks=2, storage_dir=str(tmp_path))
+    authority = H.Authority()
+    a_ag = NativeAgent(a_eng, "n0", authority=authority, shared_tiers=node)
+    b_ag = NativeAgent(b_eng, "n0", authority=authority, shared_tiers=node)
+    a_eng.attach_pool(PoolIface(a_ag, node_id="n0"))
+    b_eng.attach_pool(PoolIface(b_ag, node_id="n0"))
+    prompt = list(range(3, 3 + 5 * 16 + 1))
+    a_eng.generate([prompt], max_new_tokens=1)
+    tiers = node[0]
+    hashes = chain_block_hashes(prompt, 16, full_only=True)[:5]
+    assert sum(tiers.is_l2_durable(h) for h in hashes) == 2 and sum(tiers.l3_present(h) for h in hashes) == 3
+    b_eng.generate([prompt], max_new_tokens=1)
+    assert b_ag.stats["promoted_blocks"] == 5
+    assert [tiers.is_l2_durable(h) for h in hashes] == [False, False, False, True, True]  # the last two promoted
+    for h in hashes:
+        meta = authority.locate([H.KVBlockID("tiny", h)])[0]
+        on_l2 = any(loc.tier == 3 and loc.node_id == "n0" for loc in meta.locations)
+        assert on_l2 == tiers.is_l2_durable(h)
+        assert meta.l3_present and tiers.l3_present(h)  # all five passed through L3
