@@ -242,6 +242,28 @@ size_t apply_location_events(ControlPlanePort& cp, const std::string& model_id, 
   return n;
 }
 
+size_t enqueue_defrag_moves(tier::TierPipeline& pipe, const std::vector<cp::DefragMove>& moves) {
+  size_t n = 0;
+  for (auto& m : moves) {
+    if (!m.node_id.empty() && m.node_id != pipe.node_id()) continue;
+    tier::Action a;
+    if (m.compact_segment) {
+      a.kind = tier::ActionKind::CompactSegment;
+      a.segment_id = m.segment_id;
+    } else if (!m.id.block_hash.empty()) {
+      a.kind = tier::ActionKind::CoLocateMove;
+      a.hash = m.id.block_hash;
+      a.segment_id = m.to_segment;
+      a.offset = m.to_offset;
+    } else {
+      continue;
+    }
+    pipe.enqueue(a);
+    ++n;
+  }
+  return n;
+}
+
 // ------------------------------------------------------------------ backpressure
 void BackpressureMemory::record(const cp::BackpressureSignal& s) {
   last_ = s;

@@ -97,6 +97,14 @@ size_t apply_location_events(ControlPlanePort& cp, const std::string& model_id, 
 
 // Backpressure memory: the last hard-quota signal stays "fresh" for ttl_s and is
 // attached to load-report acks.
+// Defrag moves the control plane planned (Authority::plan_defrag) queued on this node's tier
+// pipeline: segment compactions and co-locate moves. A move addressed to another node is
+// skipped (moving a block across nodes needs a transfer). Returns the number queued.
+size_t enqueue_defrag_moves(tier::TierPipeline& pipe, const std::vector<cp::DefragMove>& moves);
+// The control plane's PauseBackground switch applied to the node's background bandwidth: a
+// paused pool admits no pipeline action (promotions, demotions and defrag wait).
+inline void sync_background_pause(tier::BandwidthPool& bw, bool paused) { bw.set_paused(paused); }
+
 class BackpressureMemory {
  public:
   explicit BackpressureMemory(double ttl_s = 30.0) : ttl_(ttl_s) {}

@@ -90,6 +90,8 @@ void register_agent(py::module_& m) {
   m.def("apply_location_events", &apply_location_events, py::arg("port"), py::arg("model_id"), py::arg("revision"),
         py::arg("pool_kind"), py::arg("events"));
 
+  m.def("enqueue_defrag_moves", &enqueue_defrag_moves, py::arg("pipeline"), py::arg("moves"));
+  m.def("sync_background_pause", &sync_background_pause, py::arg("bandwidth"), py::arg("paused"));
   py::class_<BackpressureMemory>(m, "BackpressureMemory")
       .def(py::init<double>(), py::arg("ttl_s") = 30.0)
       .def("record", &BackpressureMemory::record)

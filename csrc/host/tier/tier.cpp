@@ -706,7 +706,7 @@ std::pair<size_t, std::vector<LocationEvent>> TierPipeline::tick(size_t max_step
                                                                  const std::function<int64_t()>& alloc_page,
                                                                  std::vector<DeviceCopy>* copies) {
   std::vector<LocationEvent> ev;
-  size_t done = 0;
+  size_t done = 0, failed = 0;
   std::deque<Action> retry;
   while (done < max_steps && !q_.empty()) {
     Action a = q_.front();
@@ -772,10 +772,11 @@ std::pair<size_t, std::vector<LocationEvent>> TierPipeline::tick(size_t max_step
           break;
         }
       }
+      ++done;
     } catch (const std::exception&) {
       if (++a.failures < kMaxFailures) retry.push_back(a);
+      if (++failed >= max_steps) break;  // a tick spends at most max_steps attempts on failures
     }
-    ++done;
   }
   for (auto& a : retry) q_.push_back(a);
   return {done, ev};

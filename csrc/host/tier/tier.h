@@ -266,8 +266,11 @@ class TierPipeline {
   TierPipeline(TierEngine* engine, BandwidthPool* bw, std::string node_id);
   void enqueue(const Action& a) { q_.push_back(a); }
   size_t pending() const { return q_.size(); }
-  // Run up to max_steps actions. `alloc_page` provides L0 pages; device copies
-  // produced by promotions/demotions are appended to `copies`.
+  const std::string& node_id() const { return node_; }
+  // Run up to max_steps actions and return how many succeeded. An action that fails goes
+  // back to the queue until it has failed kMaxFailures times, then it is dropped; one the
+  // bandwidth window cannot pay for ends the tick and stays at the front. `alloc_page`
+  // provides L0 pages; device copies produced by promotions/demotions are appended to `copies`.
   std::pair<size_t, std::vector<LocationEvent>> tick(size_t max_steps, uint64_t now_ms,
                                                      const std::function<int64_t()>& alloc_page,
                                                      std::vector<DeviceCopy>* copies);

@@ -215,6 +215,7 @@ void register_tier(py::module_& m) {
       .def(py::init<TierEngine*, BandwidthPool*, std::string>(), py::keep_alive<1, 2>(), py::keep_alive<1, 3>())
       .def("enqueue", &TierPipeline::enqueue)
       .def("pending", &TierPipeline::pending)
+      .def("node_id", &TierPipeline::node_id)
       .def("tick", [](TierPipeline& p, size_t steps, uint64_t now_ms, const std::function<int64_t()>& alloc) {
         std::vector<DeviceCopy> copies;
         auto r = p.tick(steps, now_ms, alloc, &copies);

@@ -4,8 +4,11 @@ and demote through L0/L1, L0 pressure reporting its collateral demotion, an L3 r
 lands back in L2, L3-only backing allowing an L0 demotion, pins blocking demotion, the L2 cap
 moving a cold block to L3 (exactly one of L2 / L3), pinned blocks keeping their LRU position,
 an all-pinned cap failure rolling back with the LRU order unchanged, hit counts, one-shot
-admission and eviction order, and promote de-duplication. Storage failures are made on the
-host: a directory sits where the engine wants to create a segment file or an L3 object."""
+admission and eviction order, and promote de-duplication; and the tier pipeline's cases
+(pipeline.rs:315-445, storage-agent putend.rs:1706-1790): collateral L0 events, the bandwidth
+window, requeue then drop of a failing action, compaction and a control-plane co-locate plan
+held by PauseBackground. Storage failures are made on the host: a directory sits where the
+engine wants to create a segment file or an L3 object."""
 import pytest
 
 from lake_b200 import _host as H
@@ -325,3 +328,104 @@ def test_async_promote_dedups_in_flight_requests(tmp_path):
 def test_an_engine_needs_an_l2_directory(tmp_path):
     with pytest.raises(ValueError, match="L2 directory"):
         H.TierEngine(H.TierCaps(1, 0, 1), BB, 0, "", str(tmp_path / "l3"), "m")
+
+
+# ------------------------------------------------------------------ pipeline (rust/tiered-store/src/pipeline.rs:315-445)
+def _pipe(e, budget=1 << 30):
+    bw = H.BandwidthPool(budget, 1000)
+    return H.TierPipeline(e, bw, "n0"), bw
+
+
+def test_pipeline_promotion_emits_the_collateral_l0_absent(tmp_path):
+    e = _engine(tmp_path, (1, 8, 8))
+    _put(e, "a")
+    _put(e, "b")
+    p, _ = _pipe(e)
+    pages = _pages()
+    p.enqueue(H.Action(H.ActionKind.PROMOTE, _h("a")))
+    assert p.tick(1, 0, pages)[0] == 1
+    p.enqueue(H.Action(H.ActionKind.PROMOTE, _h("b")))
+    n, events, copies = p.tick(1, 0, pages)
+    assert n == 1
+    assert any(ev.kind == H.LocKind.ABSENT and ev.hash == _h("a") and ev.tier == 1 for ev in events)
+    assert [(c.hash, c.to_device) for c in copies] == [(_h("a"), False), (_h("b"), True)]  # copy out first
+
+
+def test_pipeline_waits_for_the_next_window_when_the_budget_is_spent(tmp_path):
+    e = _engine(tmp_path, (4, 8, 8))
+    _put(e, "a")
+    _put(e, "b")
+    p, _ = _pipe(e, budget=3 * BB)  # an L2 promotion is charged two block moves
+    pages = _pages()
+    p.enqueue(H.Action(H.ActionKind.PROMOTE, _h("a")))
+    p.enqueue(H.Action(H.ActionKind.PROMOTE, _h("b")))
+    n, _, _ = p.tick(8, 0, pages)
+    assert n == 1 and p.pending() == 1 and e.local_tier(_h("b")) != H.TierId.L0
+    assert p.tick(8, 500, pages)[0] == 0  # same window
+    assert p.tick(8, 1000, pages)[0] == 1 and e.local_tier(_h("b")) == H.TierId.L0
+
+
+def test_pipeline_requeues_a_failed_action_then_drops_it(tmp_path):
+    e = _engine(tmp_path, (4, 8, 8))
+    p, _ = _pipe(e)
+    p.enqueue(H.Action(H.ActionKind.PROMOTE, _h("missing")))
+    assert p.tick(1, 0, _pages())[0] == 0 and p.pending() == 1  # failed: back in the queue
+    assert p.tick(1, 0, _pages())[0] == 0 and p.pending() == 1
+    assert p.tick(1, 0, _pages())[0] == 0 and p.pending() == 0  # third failure: dropped
+
+
+def test_pipeline_compaction_waits_while_paused_then_emits_moves(tmp_path):
+    e = _engine(tmp_path, (4, 8, 8))
+    for n in ("a", "b", "c", "d"):
+        _put(e, n)
+    e.discard(_h("b"))  # a hole at slot 1
+    p, bw = _pipe(e)
+    p.enqueue(H.Action(H.ActionKind.COMPACT_SEGMENT, segment_id=1))
+    H.sync_background_pause(bw, True)
+    assert p.tick(8, 0, _pages())[0] == 0 and p.pending() == 1
+    assert e.l2_placement(_h("d")).offset == 3 * e.record_bytes()
+    H.sync_background_pause(bw, False)
+    n, events, _ = p.tick(8, 0, _pages())
+    assert n == 1
+    assert [(ev.kind, ev.hash, ev.segment_id, ev.offset) for ev in events] == [
+        (H.LocKind.MOVED, _h("d"), 1, e.record_bytes())]
+    assert e.l2_placement(_h("d")).offset == e.record_bytes()
+    assert all(e.read_bytes(_h(n)) == _blk(n) for n in ("a", "c", "d")) and e.corrupt_reads() == 0
+
+
+def test_a_colocate_plan_runs_on_the_pipeline_and_moves_the_authority_location(tmp_path):
+    """The control plane plans a co-locate move for a chain whose second block sits in another
+    segment than its parent; the node queues it (paused background bandwidth holds it), runs it, and the
+    MOVED event puts the block's L2 location next to its parent (putend.rs:1706-1790)."""
+    e = _engine(tmp_path, (4, 8, 128))
+    _put(e, "h0")
+    for i in range(1, 64):
+        _put(e, f"x{i}")  # fills segment 1
+    _put(e, "h1")
+    assert e.l2_placement(_h("h1")).segment_id == 2
+    e.discard(_h("x1"))  # the slot next to h0 is free on the node
+    slot = e.record_bytes()
+    a = H.Authority()
+    a.register_model(H.ModelDescriptor("m", "", 2, 16, BB))
+    metas = [H.BlockMeta(H.KVBlockID("m", _h(n)), [H.Location(3, "n0", e.l2_placement(_h(n)).segment_id,
+                                                              e.l2_placement(_h(n)).offset)])
+             for n in ("h0", "h1")]
+    a.register_blocks("n0", [_h("h0"), _h("h1")], metas)
+    moves = a.plan_defrag("m", "", 1, 2, slot)  # COLOCATE
+    assert [(m.id.block_hash, m.to_segment, m.to_offset) for m in moves] == [(_h("h1"), 1, slot)]
+    other = H.DefragMove()
+    other.node_id = "n1"
+    other.compact_segment = True
+    other.segment_id = 1
+    p, bw = _pipe(e)
+    H.sync_background_pause(bw, True)
+    assert H.enqueue_defrag_moves(p, moves + [other]) == 1  # the other node's move is not ours
+    assert p.tick(8, 0, _pages())[0] == 0
+    H.sync_background_pause(bw, False)
+    n, events, _ = p.tick(8, 0, _pages())
+    assert n == 1
+    assert H.apply_location_events(H.AuthorityPort(a), "m", "", 1, events) == 1
+    loc = [l for l in a.locate([H.KVBlockID("m", _h("h1"))])[0].locations if l.tier == 3]
+    assert [(l.segment_id, l.offset) for l in loc] == [(1, slot)]
+    pl = e.l2_placement(_h("h1"))
+    assert (pl.segment_id, pl.offset) == (1, slot) and e.read_bytes(_h("h1")) == _blk("h1")
