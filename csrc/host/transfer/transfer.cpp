@@ -98,6 +98,11 @@ uint64_t TransferEngine::register_segment(const std::string& name, uintptr_t ptr
   return id;
 }
 
+// [offset, offset + length) inside a segment of `capacity` bytes, without the sum wrapping
+static bool in_range(uint64_t offset, uint64_t length, uint64_t capacity) {
+  return length <= capacity && offset <= capacity - length;
+}
+
 void TransferEngine::free_segment(uint64_t id) {
   Segment s;
   {
@@ -135,7 +140,7 @@ void TransferEngine::write_segment(uint64_t id, uint64_t offset, const std::stri
     std::lock_guard<std::mutex> g(mu_);
     s = seg(id);
   }
-  if (offset + data.size() > s.capacity) fail("write_segment: out of range");
+  if (!in_range(offset, data.size(), s.capacity)) fail("write_segment: out of range");
   if (s.device >= 0) {
     DeviceGuard dg(s.device);
     cuda_check(cudaMemcpy(s.base + offset, data.data(), data.size(), cudaMemcpyHostToDevice), "cudaMemcpy");
@@ -150,7 +155,7 @@ std::string TransferEngine::read_segment(uint64_t id, uint64_t offset, uint64_t 
     std::lock_guard<std::mutex> g(mu_);
     s = seg(id);
   }
-  if (offset + length > s.capacity) fail("read_segment: out of range");
+  if (!in_range(offset, length, s.capacity)) fail("read_segment: out of range");
   std::string out(length, '\0');
   if (s.device >= 0) {
     DeviceGuard dg(s.device);
@@ -181,8 +186,8 @@ void TransferEngine::submit_transfer(uint64_t batch_id, const std::vector<Transf
     if (op.src_tier < 1 || op.src_tier > 3) fail("invalid source tier " + std::to_string(op.src_tier));
     const Segment& s = seg(op.src_segment);
     const Segment& d = seg(op.dst_segment);
-    if (op.src_offset + op.length > s.capacity) fail("submit_transfer: source range out of segment");
-    if (op.dst_offset + op.length > d.capacity) fail("submit_transfer: target range out of segment");
+    if (!in_range(op.src_offset, op.length, s.capacity)) fail("submit_transfer: source range out of segment");
+    if (!in_range(op.dst_offset, op.length, d.capacity)) fail("submit_transfer: target range out of segment");
   }
   for (auto& op : ops) {
     const Segment& s = seg(op.src_segment);
