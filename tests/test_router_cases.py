@@ -1,10 +1,14 @@
-"""Router core (C++) under the scenarios the reference's Go router tests pin
-(go/router/pq_test.go:83-370, affinity_test.go:43-184): priority order and FIFO within a
-priority, preemption that requeues its victim, no preemption at equal priority or by a
-backpressured model, no shedding under overload, backpressure that defers but never drops,
-the load snapshot, cancellation, and the affinity / rendezvous node choice (L0 preference,
-in-flight guard, deterministic cold path equal to the pure HRW argmax, minimal migration when
-a node joins, overflow past the guard)."""
+"""Router core (C++) and the router loop under the scenarios the reference's Go router tests
+pin (go/router/pq_test.go:83-370, affinity_test.go:43-184, modeselect_test.go:16-140,
+mirror_test.go:28-200, autoscale_test.go:30-405): priority order and FIFO within a priority,
+preemption that requeues its victim, no preemption at equal priority or by a backpressured
+model, no shedding under overload, backpressure that defers but never drops, the load
+snapshot, cancellation; the affinity / rendezvous node choice (L0 preference, in-flight guard,
+deterministic cold path equal to the pure HRW argmax, minimal migration when a node joins,
+overflow past the guard); the three execution modes and the bandwidth gate; the view mirror's
+snapshot, anchor, de-duplication, gap and prefix lookup; the autoscaler's sustain, cooldown,
+bounds and streak reset; and the router loop's mirror-first prefix hint with authority
+fallback, hit reports with autoscale off, and a queue-driven scale-out that widens admission."""
 import random
 import time
 
@@ -211,3 +215,254 @@ def test_cold_path_overflows_past_the_guard_and_returns_home_when_all_are_full()
         while nodes.inflight(n) < 4:
             nodes.inc_inflight(n)
     assert H.pick_node(nodes, None, "m", [], key, 4) == home
+
+
+# ------------------------------------------------------------------ mode select (modeselect_test.go:16-75)
+R = H.Role
+PD, COLO, DD = H.ExecMode.PD_DISAGG, H.ExecMode.COLOCATED, H.ExecMode.D_DIRECT
+
+
+def test_a_pool_hit_on_a_dedicated_role_goes_pd():
+    hint = H.PrefixHint(16, 2, 0, False)
+    assert H.select_exec_mode(hint, 16, R.PREFILL, 0) == PD
+    assert H.select_exec_mode(hint, 16, R.DECODE, 0) == PD
+    assert H.select_exec_mode(hint, 16, R.PREFILL, 10) == PD  # the path is fast enough to move KV
+
+
+def test_the_bandwidth_gate_recomputes_a_pool_hit_on_a_slow_path():
+    hint = H.PrefixHint(16, 2, 0, False)
+    assert H.TRANSFER_BW_THRESHOLD_GBPS == 1.0
+    assert H.select_exec_mode(hint, 16, R.PREFILL, 0.5) == COLO
+    assert H.select_exec_mode(hint, 16, R.DECODE, 0.99) == COLO
+    # a local hit needs no transfer: the gate does not apply
+    assert H.select_exec_mode(H.PrefixHint(8, 1, 1, True), 16, R.HYBRID, 0.3) == DD
+    # a miss has nothing to move: the role decides
+    assert H.select_exec_mode(H.PrefixHint(), 16, R.PREFILL, 0.3) == PD
+
+
+def test_a_local_hit_goes_d_direct_on_every_role():
+    for role in (R.HYBRID, R.PREFILL, R.DECODE):
+        assert H.select_exec_mode(H.PrefixHint(8, 1, 1, True), 16, role, 0) == DD
+
+
+def test_hybrid_workers_colocate_misses_and_pool_hits():
+    assert H.select_exec_mode(H.PrefixHint(), 8, R.HYBRID, 0) == COLO
+    assert H.select_exec_mode(H.PrefixHint(8, 1, 0, False), 16, R.HYBRID, 0) == COLO
+    assert H.select_exec_mode(H.PrefixHint(0, 0, 0, True), 0, R.HYBRID, 0) == COLO  # empty prompt
+
+
+# ------------------------------------------------------------------ view mirror (mirror_test.go:28-200)
+REGISTERED, INVALIDATED, MOVED = 0, 1, 2
+
+
+def _event(kind, hsh, nodes=(), pool_kind=1, block_kind=0):
+    e = H.ViewEvent()
+    e.kind = kind
+    e.id = H.KVBlockID("m", hsh, pool_kind)
+    e.locations = [H.Location(1, n, 1, 0) for n in nodes]
+    e.l3_present = True
+    e.block_kind = block_kind
+    return e
+
+
+def _update(seq, events=()):
+    u = H.ViewUpdate()
+    u.seq = seq
+    u.events = list(events)
+    return u
+
+
+def _local(m, hsh, node, pool_kind=1):
+    got = m.prefix_lookup("m", "", pool_kind, [hsh], node)
+    return None if not got else got[0].local_hit
+
+
+def test_mirror_snapshot_anchor_increment_dedupe_and_invalidation():
+    m = H.ViewMirror()
+    assert m.apply(_update(0, [_event(REGISTERED, b"h0"), _event(REGISTERED, b"h1", ["n0"])])) == 0
+    assert m.apply(_update(3)) == 0 and m.last_seq() == 3  # an anchor moves the sequence only
+    assert m.apply(_update(4, [_event(MOVED, b"h1", ["n1"])])) == 0
+    assert _local(m, b"h1", "n1") is True and _local(m, b"h1", "n0") is False
+    assert m.apply(_update(2, [_event(REGISTERED, b"h9")])) == 0  # seq <= last: dropped
+    assert _local(m, b"h9", "") is None
+    assert m.apply(_update(5, [_event(INVALIDATED, b"h0")])) == 0
+    assert _local(m, b"h0", "") is None and m.size() == 1
+
+
+def test_a_snapshot_resets_the_sequence_after_a_control_plane_restart():
+    m = H.ViewMirror()
+    m.apply(_update(0, [_event(REGISTERED, b"old")]))
+    m.apply(_update(100))
+    assert m.last_seq() == 100
+    m.apply(_update(0, [_event(REGISTERED, b"new")]))  # the restarted authority counts from 1 again
+    assert m.last_seq() == 0 and _local(m, b"old", "") is None
+    m.apply(_update(1))
+    assert m.apply(_update(2, [_event(REGISTERED, b"h2")])) == 0
+    assert _local(m, b"h2", "") is False and m.last_seq() == 2
+
+
+def test_a_gap_is_reported_and_changes_nothing():
+    m = H.ViewMirror()
+    m.apply(_update(0, [_event(REGISTERED, b"h0")]))
+    m.apply(_update(1))
+    assert m.apply(_update(3, [_event(REGISTERED, b"h1")])) == 2  # wants seq 2
+    assert m.last_seq() == 1 and _local(m, b"h1", "") is None
+
+
+def test_mirror_prefix_lookup_is_contiguous_per_requester_and_per_pool():
+    m = H.ViewMirror()
+    m.apply(_update(0, [_event(REGISTERED, b"h0", ["n0"]), _event(REGISTERED, b"h1"),
+                        _event(REGISTERED, b"h2", ["n1"])]))
+    got = m.prefix_lookup("m", "", 1, [b"h0", b"h1", b"h2"], "n0")
+    assert [b.local_hit for b in got] == [True, False, False]  # all three found, only h0 on n0
+    assert m.prefix_lookup("m", "", 1, [b"hx", b"h0"], "n0") == []  # the first miss ends the match
+    assert m.prefix_lookup("m", "", 2, [b"h0"], "n0") == []  # the draft pool is its own namespace
+
+
+# ------------------------------------------------------------------ autoscaler (autoscale_test.go:30-80)
+def _scaler():
+    return H.Autoscaler(H.AutoscaleConfig(1, 3, 4, 0, 3, 60.0))  # min, max, out at 4, in at 0, 3 periods, 60 s
+
+
+def test_autoscale_decisions_sustain_cooldown_bounds_and_streak_reset():
+    NONE, OUT, IN = H.ScaleDecision.NONE, H.ScaleDecision.SCALE_OUT, H.ScaleDecision.SCALE_IN
+    a = _scaler()
+    assert [a.evaluate(0, 5, 1, 1) for _ in range(3)] == [NONE, NONE, OUT]  # three hot periods
+    assert a.evaluate(10, 5, 1, 2) == NONE  # cooldown
+    assert a.evaluate(120, 5, 1, 3) == NONE  # at max nodes
+    b = _scaler()
+    b.evaluate(0, 5, 1, 1)
+    b.evaluate(0, 2, 1, 1)  # a middle value resets the streak
+    b.evaluate(0, 5, 1, 1)
+    assert b.evaluate(0, 5, 1, 1) == NONE
+    c = _scaler()
+    assert [c.evaluate(0, 0, 0, 2) for _ in range(3)] == [NONE, NONE, IN]  # three idle periods
+    assert all(c.evaluate(120 * (i + 1), 0, 0, 1) == NONE for i in range(5))  # never below min nodes
+
+
+def test_node_registry_ids_grow_and_the_newest_ready_node_drains_first():
+    n = H.NodeRegistry(["worker-0"])
+    assert n.next_id() == "worker-1"
+    n.add("worker-1")
+    assert n.next_id() == "worker-2" and n.last_ready() == "worker-1"
+    assert n.mark_draining("worker-1") and n.count() == 1 and n.draining() == ["worker-1"]
+    assert n.ready_ids() == ["worker-0"]  # a draining node takes no new request
+    n.unmark_draining("worker-1")
+    assert n.count() == 2 and n.draining() == []
+
+
+# ------------------------------------------------------------------ router loop (modeselect_test.go:77-140, autoscale_test.go:183-405)
+class _FakeCP:
+    """The control-plane calls the router makes, recorded; LookupPrefix answers from `lookup`."""
+
+    def __init__(self, lookup=None):
+        from lake_b200.api import proto
+
+        self.pb = proto.messages()
+        self.lookup, self.calls, self.hits = lookup, [], []
+
+    async def LookupPrefix(self, req, timeout=None):
+        self.calls.append("lookup")
+        if self.lookup is None:
+            raise AssertionError("the control plane was asked")
+        return self.lookup(req)
+
+    async def ReportHits(self, req, timeout=None):
+        self.hits.append((req.node_id, [bytes(i.block_hash) for i in req.ids]))
+        return self.pb.Ack(ok=True)
+
+    async def JoinShardNode(self, req, timeout=None):
+        self.calls.append(("join", req.node_id))
+        return self.pb.JoinShardNodeResponse(ok=True)
+
+
+class _FakeAgent:
+    def __init__(self):
+        self.placed = 0
+
+    async def PlaceBlocks(self, req, timeout=None):
+        self.placed += 1
+
+
+def _router(cp, agent=None, **cfg):
+    from lake_b200.router.server import Router, RouterConfig
+
+    class R(Router):
+        pass
+
+    R.cp = property(lambda self: cp)
+    R.agent = property(lambda self: agent)
+    return R(RouterConfig(workers={"worker-0": "127.0.0.1:1"}, **cfg))
+
+
+def _prompt_hashes(r, n_blocks=2):
+    from lake_b200.engine.block_pool import chain_block_hashes
+
+    tokens = list(range(1, n_blocks * r.cfg.block_size + 1))
+    return tokens, chain_block_hashes(tokens, r.cfg.block_size, full_only=True)
+
+
+def test_a_mirror_hit_makes_the_hint_without_a_control_plane_call():
+    import asyncio
+
+    cp = _FakeCP()
+    r = _router(cp)
+    tokens, hs = _prompt_hashes(r)
+    r.mirror.apply(_update(0, [_event(REGISTERED, hs[0], ["worker-0"])]))
+    hint = asyncio.run(r.prefix_hint("m", hs, len(tokens), "worker-0"))
+    assert (hint.reused_blocks, hint.computed_tokens, hint.local_hit) == (1, r.cfg.block_size, True)
+    hint = asyncio.run(r.prefix_hint("m", hs, len(tokens), "worker-1"))
+    assert (hint.reused_blocks, hint.local_hit) == (1, False)  # the same block, held elsewhere: a pool hit
+    assert cp.calls == []
+
+
+def test_a_mirror_miss_falls_back_to_the_authority_and_a_double_miss_is_cold():
+    import asyncio
+
+    def answer(req):
+        return cp.pb.LookupPrefixResponse(hit_length=1, blocks=[cp.pb.ReusableBlock(
+            id=cp.pb.KVBlockID(model_id=req.model_id, block_hash=req.prefix_hashes[0]))])
+
+    cp = _FakeCP(answer)
+    r = _router(cp)
+    tokens, hs = _prompt_hashes(r)
+    hint = asyncio.run(r.prefix_hint("m", hs, len(tokens), "worker-0"))
+    assert cp.calls == ["lookup"]
+    assert (hint.reused_blocks, hint.computed_tokens, hint.local_hit) == (1, r.cfg.block_size, False)
+    cold = _FakeCP(lambda req: cold.pb.LookupPrefixResponse())
+    hint = asyncio.run(_router(cold).prefix_hint("m", hs, len(tokens), "worker-0"))
+    assert (hint.reused_blocks, hint.computed_tokens, hint.local_hit) == (0, 0, False)
+
+
+def test_the_tick_reports_hits_with_autoscale_off():
+    import asyncio
+
+    cp = _FakeCP()
+    r = _router(cp, autoscale=False)
+    tokens, hs = _prompt_hashes(r)
+    r.mirror.apply(_update(0, [_event(REGISTERED, hs[0], ["worker-0"])]))
+    asyncio.run(r.prefix_hint("m", hs, len(tokens), "worker-0"))
+    asyncio.run(r.autoscale_tick())
+    assert cp.hits == [("worker-0", [hs[0]])]
+    assert not any(isinstance(c, tuple) for c in cp.calls)  # no scaling with autoscale off
+
+
+def test_queue_depth_drives_a_scale_out_that_widens_admission_and_places_nothing():
+    import asyncio
+
+    cp, agent = _FakeCP(), _FakeAgent()
+    r = _router(cp, agent, autoscale=True, max_inflight=1)
+    r.scaler = H.Autoscaler(H.AutoscaleConfig(1, 3, 2, 0, 1, 0.0))
+    r.pq = H.PQScheduler(1, 1.0)
+    for _ in range(3):
+        r.pq.submit(0, "m")
+    r.pq.start_eligible()
+    assert (r.pq.in_flight(), r.pq.queue_len()) == (1, 2)
+    tokens, hs = _prompt_hashes(r)
+    r.mirror.apply(_update(0, [_event(REGISTERED, hs[0], ["worker-0"])]))
+    asyncio.run(r.prefix_hint("m", hs, len(tokens), "worker-0"))
+    asyncio.run(r.autoscale_tick())
+    assert cp.calls == [("join", "worker-1")] and r.nodes.count() == 2
+    assert r.pq.load_snapshot("r").remaining_cap == 1  # two per-node slots, one in use
+    assert len(r.pq.start_eligible()) == 1
+    assert cp.hits == [("worker-0", [hs[0]])] and agent.placed == 0  # hits go to the pool side
