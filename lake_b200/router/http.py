@@ -49,8 +49,9 @@ def make_app(router: Router, tokenizer: Tokenizer | None = None) -> web.Applicat
             return web.Response(status=400, text="invalid JSON request")
         try:
             tokens = tokenizer.encode_request(data)
-        except Exception as e:  # a message the chat template cannot render
-            return web.Response(status=400, text=f"cannot tokenize request: {e}")
+        except Exception as e:  # a message the chat template cannot render; the detail stays in the log
+            LOG.info("cannot tokenize request: %s", e)
+            return web.Response(status=400, text="cannot tokenize request")
         max_new = int(data.get("max_tokens") or 0) or 4
         model = data.get("model") or "mock-llm"
         session = req.headers.get("X-Lake-Session-Id", "").encode()

@@ -7,8 +7,10 @@ snapshot, cancellation; the affinity / rendezvous node choice (L0 preference, in
 deterministic cold path equal to the pure HRW argmax, minimal migration when a node joins,
 overflow past the guard); the three execution modes and the bandwidth gate; the view mirror's
 snapshot, anchor, de-duplication, gap and prefix lookup; the autoscaler's sustain, cooldown,
-bounds and streak reset; and the router loop's mirror-first prefix hint with authority
-fallback, hit reports with autoscale off, and a queue-driven scale-out that widens admission."""
+bounds and streak reset; the router loop's mirror-first prefix hint with authority fallback,
+hit reports with autoscale off, and a queue-driven scale-out that widens admission; and the HTTP
+front (server_test.go:268-405): the body limit, generic error texts that leak no backend
+detail, D-direct dispatch from a mirror hit, and a cold request with the authority down."""
 import random
 import time
 
@@ -466,3 +468,139 @@ def test_queue_depth_drives_a_scale_out_that_widens_admission_and_places_nothing
     assert r.pq.load_snapshot("r").remaining_cap == 1  # two per-node slots, one in use
     assert len(r.pq.start_eligible()) == 1
     assert cp.hits == [("worker-0", [hs[0]])] and agent.placed == 0  # hits go to the pool side
+
+
+# ------------------------------------------------------------------ HTTP front (server_test.go:268-405)
+class _Call:
+    """A finished unary call the router can await and cancel."""
+
+    def __init__(self, resp):
+        self.resp, self._cancelled = resp, False
+
+    def __await__(self):
+        return self.resp
+        yield  # noqa: unreachable (makes this a generator)
+
+    def cancel(self):
+        self._cancelled = True
+
+    def cancelled(self):
+        return self._cancelled
+
+
+def _rpc_error(code, details):
+    import grpc
+
+    return grpc.aio.AioRpcError(code, grpc.aio.Metadata(), grpc.aio.Metadata(), details=details)
+
+
+class _DownCP(_FakeCP):
+    async def LookupPrefix(self, req, timeout=None):
+        import grpc
+
+        raise _rpc_error(grpc.StatusCode.UNAVAILABLE, "control plane down")
+
+
+def _http(dispatch, cp=None):
+    """A router app whose agent answers Dispatch with `dispatch(pb, req)` and whose worker
+    answers Generate with one token in the requested mode."""
+    from lake_b200.api import proto
+    from lake_b200.router.http import make_app
+    from lake_b200.router.server import Router, RouterConfig
+
+    pb = proto.messages()
+    seen = {}
+
+    class Agent:
+        async def Dispatch(self, req, timeout=None):
+            seen["dispatch"] = req
+            return dispatch(pb, req)
+
+    class Worker:
+        def Generate(self, req, timeout=None):
+            seen["generate"] = req
+            return _Call(pb.GenerateResponse(request_id=req.request_id, mode=req.exec_mode, output_tokens=[5]))
+
+    class R(Router):
+        agent = property(lambda self: Agent())
+
+        def worker(self, node):
+            return Worker()
+
+    R.cp = property(lambda self: cp or _DownCP())
+    r = R(RouterConfig(workers={"worker-0": "127.0.0.1:1"}, request_timeout_s=5))
+    return r, make_app(r), seen
+
+
+def _post(app, **kw):
+    import asyncio
+
+    from aiohttp.test_utils import TestClient, TestServer
+
+    async def run():
+        async with TestClient(TestServer(app)) as c:
+            resp = await c.post("/v1/chat/completions", **kw)
+            return resp.status, await resp.text()
+
+    return asyncio.run(run())
+
+
+def _ok(pb, req):
+    return pb.Ack(ok=True)
+
+
+CHAT = {"model": "m", "messages": [{"role": "user", "content": "hi"}]}
+
+
+def test_a_body_over_the_limit_is_413():
+    from lake_b200.router.server import MAX_BODY
+
+    _, app, _ = _http(_ok)
+    assert _post(app, data=b"x" * (MAX_BODY + 1))[0] == 413
+
+
+def test_invalid_json_gets_a_generic_message():
+    _, app, _ = _http(_ok)
+    status, text = _post(app, data=b"{")
+    assert status == 400 and text == "invalid JSON request"  # no parser detail
+
+
+def test_an_upstream_error_does_not_leak_its_message():
+    import grpc
+
+    def down(pb, req):
+        raise _rpc_error(grpc.StatusCode.UNAVAILABLE, "secret backend details")
+
+    _, app, _ = _http(down)
+    status, text = _post(app, json=CHAT)
+    assert status == 503 and "secret" not in text
+
+
+def test_a_rejected_dispatch_does_not_leak_its_reason():
+    _, app, _ = _http(lambda pb, req: pb.Ack(ok=False, err="secret quota details"))
+    status, text = _post(app, json=CHAT)
+    assert status == 502 and "secret" not in text
+
+
+def test_a_mirror_hit_dispatches_d_direct_with_the_hint():
+    import json
+
+    r, app, seen = _http(_ok)
+    prompt = list(range(100, 100 + 2 * r.cfg.block_size))
+    hs = H.chain_block_hashes(prompt, r.cfg.block_size, True)
+    r.mirror.apply(_update(0, [_event(REGISTERED, hs[0], ["worker-0"])]))
+    status, text = _post(app, json={"model": "m", "prompt_token_ids": prompt, "max_tokens": 1})
+    assert status == 200 and json.loads(text)["lake"]["mode"] == "D_DIRECT"
+    assert seen["dispatch"].mode == "D_DIRECT"
+    g = seen["generate"]
+    assert (g.exec_mode, g.local_hit, g.reused_blocks, g.computed_tokens) == ("D_DIRECT", True, 1, r.cfg.block_size)
+
+
+def test_a_cold_miss_with_the_authority_down_runs_colocated_without_reuse():
+    import json
+
+    r, app, seen = _http(_ok)
+    status, text = _post(app, json={"model": "m", "prompt_token_ids": list(range(1, 40)), "max_tokens": 1})
+    assert status == 200 and json.loads(text)["lake"]["mode"] == "COLOCATED"
+    g = seen["generate"]
+    assert (g.exec_mode, g.reused_blocks, g.computed_tokens, g.local_hit) == ("COLOCATED", 0, 0, False)
