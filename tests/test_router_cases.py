@@ -10,7 +10,10 @@ snapshot, anchor, de-duplication, gap and prefix lookup; the autoscaler's sustai
 bounds and streak reset; the router loop's mirror-first prefix hint with authority fallback,
 hit reports with autoscale off, and a queue-driven scale-out that widens admission; and the HTTP
 front (server_test.go:268-405): the body limit, generic error texts that leak no backend
-detail, D-direct dispatch from a mirror hit, and a cold request with the authority down."""
+detail, D-direct dispatch from a mirror hit, and a cold request with the authority down; the
+view sync loop resuming after a gap and taking a fallback snapshot, and the load sync loop
+uploading reports and applying the backpressure an ack carries (viewsync_test.go:85-200,
+loadsync_test.go:82-140)."""
 import random
 import time
 
@@ -604,3 +607,165 @@ def test_a_cold_miss_with_the_authority_down_runs_colocated_without_reuse():
     assert status == 200 and json.loads(text)["lake"]["mode"] == "COLOCATED"
     g = seen["generate"]
     assert (g.exec_mode, g.reused_blocks, g.computed_tokens, g.local_hit) == ("COLOCATED", 0, 0, False)
+
+
+# ------------------------------------------------------------------ view / load sync loops (viewsync_test.go:85-200, loadsync_test.go:82-140)
+class _Stream:
+    """A server stream: yields `items` (raising an item that is an exception), then either ends
+    with `end` raised or stays open until cancelled."""
+
+    def __init__(self, items, end=None):
+        self.items, self.end, self.cancelled = items, end, False
+
+    def cancel(self):
+        self.cancelled = True
+
+    def __aiter__(self):
+        return self._gen()
+
+    async def _gen(self):
+        import asyncio
+
+        for it in self.items:
+            if self.cancelled:
+                return
+            yield it
+        if self.end is not None:
+            raise self.end
+        while not self.cancelled:
+            await asyncio.sleep(0.001)
+
+
+def _pb_update(pb, seq, regs=(), moved=()):
+    ev = [pb.ViewEvent(kind=0, id=pb.KVBlockID(model_id="m", block_hash=h, pool_kind=1), l3_present=True)
+          for h in regs]
+    ev += [pb.ViewEvent(kind=2, id=pb.KVBlockID(model_id="m", block_hash=h, pool_kind=1),
+                        locations=[pb.Location(tier=1, node_id=n, segment_id=1)]) for h, n in moved]
+    return pb.ViewUpdate(seq=seq, events=ev)
+
+
+def _run_view_sync(script):
+    """Runs the router's view sync against a control plane answering SubscribeView call k with
+    script(pb, k); returns the router and the resume sequence of each call."""
+    import asyncio
+
+    from lake_b200.api import proto
+
+    pb = proto.messages()
+    resumes = []
+
+    class CP(_FakeCP):
+        def SubscribeView(self, req, timeout=None):
+            resumes.append(req.resume_from_seq)
+            return script(pb, len(resumes) - 1)
+
+    r = _router(CP())
+
+    async def run(want_seq):
+        t = asyncio.create_task(r._view_sync(reconnect_s=0.001))
+        for _ in range(3000):
+            if r.mirror.last_seq() == want_seq and len(resumes) >= 2:
+                break
+            await asyncio.sleep(0.001)
+        t.cancel()
+        try:
+            await t
+        except asyncio.CancelledError:
+            pass
+
+    return r, resumes, run
+
+
+def test_view_sync_resumes_after_a_gap_and_replays_to_alignment():
+    import asyncio
+    import grpc
+
+    def script(pb, k):
+        if k == 0:  # snapshot, anchor 1, then seq 3: seq 2 was missed
+            return _Stream([_pb_update(pb, 0, regs=[b"h0"]), _pb_update(pb, 1), _pb_update(pb, 3, regs=[b"h1"])],
+                           end=_rpc_error(grpc.StatusCode.UNAVAILABLE, "drop"))
+        assert k == 1
+        return _Stream([_pb_update(pb, 2, moved=[(b"h0", "n0")]), _pb_update(pb, 3, regs=[b"h1"])])
+
+    r, resumes, run = _run_view_sync(script)
+    asyncio.run(run(3))
+    assert r.mirror.last_seq() == 3 and resumes == [0, 1]
+    assert _local(r.mirror, b"h0", "n0") is True and _local(r.mirror, b"h1", "") is False
+
+
+def test_view_sync_takes_the_snapshot_a_control_plane_falls_back_to():
+    import asyncio
+    import grpc
+
+    def script(pb, k):
+        if k == 0:
+            return _Stream([_pb_update(pb, 0, regs=[b"h0", b"h1"]), _pb_update(pb, 1)],
+                           end=_rpc_error(grpc.StatusCode.UNAVAILABLE, "drop"))
+        return _Stream([_pb_update(pb, 0, regs=[b"h1"]), _pb_update(pb, 5)])  # resume point evicted
+
+    r, resumes, run = _run_view_sync(script)
+    asyncio.run(run(5))
+    assert r.mirror.last_seq() == 5 and resumes == [0, 1]
+    assert _local(r.mirror, b"h0", "") is None and _local(r.mirror, b"h1", "") is False
+
+
+def test_load_sync_uploads_reports_and_applies_backpressure_from_the_ack():
+    import asyncio
+
+    from lake_b200.api import proto
+
+    pb = proto.messages()
+    sent, bp_on = [], []
+
+    class Bidi:
+        def __init__(self):
+            self.q = asyncio.Queue()
+
+        async def write(self, rep):
+            sent.append(rep)
+            sig = pb.BackpressureSignal(model_id="m-bp", reason="HARD_QUOTA", deficit_bytes=64) if bp_on else None
+            await self.q.put(pb.Ack(ok=True, backpressure=sig) if sig else pb.Ack(ok=True))
+
+        def cancel(self):
+            self.q.put_nowait(None)
+
+        def __aiter__(self):
+            return self
+
+        async def __anext__(self):
+            item = await self.q.get()
+            if item is None:
+                raise StopAsyncIteration
+            return item
+
+    class Agent:
+        def ReportLoad(self):
+            return Bidi()
+
+    r = _router(_FakeCP(), Agent())
+    r.pq = H.PQScheduler(1, 5.0)
+
+    async def run():
+        t = asyncio.create_task(r._load_sync(interval_s=0.001))
+        for _ in range(2000):
+            if sent:
+                break
+            await asyncio.sleep(0.001)
+        assert sent and sent[0].node_id == "router"
+        bp_on.append(True)
+        for _ in range(2000):
+            if r.pq.backpressured("m-bp"):
+                break
+            await asyncio.sleep(0.001)
+        t.cancel()
+        try:
+            await t
+        except asyncio.CancelledError:
+            pass
+
+    asyncio.run(run())
+    assert r.pq.backpressured("m-bp") and not r.pq.backpressured("other")
+    bp, _ = r.pq.submit(5, "m-bp")
+    other, _ = r.pq.submit(5, "other")
+    assert r.pq.start_eligible() == [other]  # the backpressured model waits, the other one runs
+    assert r.pq.queue_len() == 1
