@@ -163,7 +163,7 @@ class WorkerLifecycle:
         return self._state
 
     def advance(self, to: WorkerState) -> None:
-        if to == self._state:
+        if to == self._state or self._state == WorkerState.TERMINATE:  # terminal: nothing follows it
             return
         if to in (WorkerState.DRAIN, WorkerState.TERMINATE):
             self._state = to

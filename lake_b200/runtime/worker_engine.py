@@ -93,6 +93,10 @@ class WorkerEngine:
         self._inflight: dict[str, _Inbound] = {}
         self._thread: threading.Thread | None = None
         self._stop = threading.Event()
+        # intake: submit() enqueues under this lock and only while open; stop() and a step
+        # failure close it before they reject what is queued, so no submitter is left waiting
+        self._intake = threading.Lock()
+        self._intake_open = True
         self._failed: Exception | None = None
         self.steps = 0
         self.on_finished = None  # optional callback(request) after a request completes
@@ -127,16 +131,38 @@ class WorkerEngine:
         self.engine.generate(toks, max_new_tokens=1)
 
     def stop(self, drain: bool = True, timeout_s: float = 60.0) -> None:
+        """Stop the step loop. With `drain`, requests already accepted finish first (up to
+        timeout_s). Every request still queued or in flight then fails with "worker stopped". If
+        the loop does not exit within timeout_s (a step is still running), the worker stays in
+        DRAIN and its in-flight requests are left to the loop, which fails them when it exits:
+        they are not touched here while a step may still use them. Calling stop again, or on a
+        worker that never started, is harmless."""
+        if self.state == WorkerState.TERMINATE:
+            return
+        self.lifecycle.drain()
         if drain:
-            self.lifecycle.drain()
             t0 = time.monotonic()
             while (self._inflight or not self._inbox.empty()) and time.monotonic() - t0 < timeout_s:
+                if self._thread is None or not self._thread.is_alive():
+                    break
                 time.sleep(0.01)
+        self._close_intake()
         self._stop.set()
         if self._thread is not None:
             self._thread.join(timeout=timeout_s)
-        self._fail_inflight(PoolError(PoolErrorCode.DOWNSTREAM, "worker stopped"))
+            if self._thread.is_alive():
+                LOG.warning("step loop still running after %.1fs; it fails its requests when it exits", timeout_s)
+                return
+        self._fail_all(PoolError(PoolErrorCode.DOWNSTREAM, "worker stopped"))
         self.lifecycle.terminate()
+
+    def _close_intake(self) -> None:
+        with self._intake:
+            self._intake_open = False
+
+    def _fail_all(self, err: Exception) -> None:
+        self._fail_inflight(err)
+        self._reject_inbound(err)
 
     @property
     def state(self) -> WorkerState:
@@ -165,7 +191,10 @@ class WorkerEngine:
         hint = hint or PrefixHint()
         mode = ExecMode(exec_mode) if exec_mode else select_exec_mode(hint, len(prompt), self.cfg.role)
         job = _Inbound(rid, list(prompt), int(max_new_tokens), mode, hint)
-        self._inbox.put(job)
+        with self._intake:
+            if not self._intake_open:
+                raise PoolError(PoolErrorCode.CAPACITY, f"worker not running ({self.state.value})")
+            self._inbox.put(job)
         if not job.event.wait(timeout_s):
             raise PoolError(PoolErrorCode.TIMEOUT, f"request {rid} did not finish in {timeout_s}s")
         res = job.result
@@ -206,6 +235,15 @@ class WorkerEngine:
 
     def _loop(self) -> None:
         eng = self.engine
+        try:
+            self._run_steps(eng)
+        finally:
+            if self._stop.is_set():  # a stop that may have given up waiting: the loop cleans up
+                self._close_intake()
+                self._fail_all(PoolError(PoolErrorCode.DOWNSTREAM, "worker stopped"))
+                self.lifecycle.terminate()
+
+    def _run_steps(self, eng) -> None:
         while not self._stop.is_set():
             try:
                 self._drain_inbound(block=not self._busy())
@@ -224,8 +262,8 @@ class WorkerEngine:
                 self.metrics.step_failures.inc()
                 self._failed = e
                 err = e if isinstance(e, PoolError) else PoolError(_step_error_code(e), str(e))
-                self._fail_inflight(err)
-                self._reject_inbound(err)
+                self._close_intake()
+                self._fail_all(err)
                 self.lifecycle.drain()
                 return
 
