@@ -707,8 +707,13 @@ ViewUpdate Authority::commit_pending() {
   u.events = std::move(pending_);
   pending_.clear();
   log_.push_back(u);
-  while (log_.size() > kViewLogCap) log_.pop_front();
+  while (log_.size() > log_cap_) log_.pop_front();
   return u;
+}
+
+void Authority::set_view_log_cap(size_t n) {
+  log_cap_ = n ? n : 1;
+  while (log_.size() > log_cap_) log_.pop_front();
 }
 
 std::vector<ViewUpdate> Authority::replay_after(uint64_t from_seq, bool* ok) const {

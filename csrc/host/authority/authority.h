@@ -178,6 +178,9 @@ class Authority {
   std::vector<ViewUpdate> replay_after(uint64_t from_seq, bool* ok) const;
   ViewUpdate snapshot() const;  // seq 0, REGISTERED for every block
   uint64_t last_seq() const { return next_seq_ - 1; }
+  // Committed updates kept for resuming subscribers (older resume points get a snapshot).
+  void set_view_log_cap(size_t n);
+  size_t view_log_cap() const { return log_cap_; }
   size_t pending_events() const { return pending_.size(); }
 
   // ----- reconcile / GC
@@ -284,6 +287,7 @@ class Authority {
   uint64_t checkpoint_seq_ = 0;
   // view log
   std::deque<ViewUpdate> log_;
+  size_t log_cap_ = kViewLogCap;
   uint64_t next_seq_ = 1;
   std::vector<ViewEvent> pending_;
   // shard ring

@@ -267,6 +267,8 @@ PYBIND11_MODULE(_host, m) {
            })
       .def("snapshot", &Authority::snapshot)
       .def("last_seq", &Authority::last_seq)
+      .def("set_view_log_cap", &Authority::set_view_log_cap)
+      .def("view_log_cap", &Authority::view_log_cap)
       .def("pending_events", &Authority::pending_events)
       .def("report_orphans", &Authority::report_orphans)
       .def("discard_blocks", &Authority::discard_blocks)
