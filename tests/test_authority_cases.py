@@ -812,3 +812,48 @@ def test_drain_pushes_l2_first_then_remove():
     a.publish_location(bid(b"d0"), L2, "n1", 1, 0, True)
     a.remove_shard_node("n0")
     assert a.ready_nodes() == ["n1"]
+
+
+def test_drain_of_many_blocks_moves_ownership_and_remove_waits_for_the_copies():
+    """rust/controlplane/src/lib.rs:3864-3907: every L2 block on the drained node is a push
+    candidate, none is owned by it any more, and removal waits until its copies are gone."""
+    a = H.Authority()
+    model(a)
+    a.join_shard_node("n0", 32)
+    a.join_shard_node("n1", 32)
+    names = [f"d{i:02}".encode() for i in range(20)]
+    for n in names:
+        reg(a, [n], [meta(n, node="n1")], node="n1")
+    migs, push = a.drain_shard_node("n1")
+    assert sorted(p.block_hash for p in push) == sorted(names)
+    assert migs and all(m.from_node == "n1" and m.push_l2_first for m in migs)
+    assert all(a.shard_owner(p.block_hash) != "n1" for p in push)
+    with pytest.raises(ValueError, match="placements remain"):
+        a.remove_shard_node("n1")
+    for p in push:
+        a.publish_location(p, L2, "n1", 1, 0, False)
+    a.remove_shard_node("n1")
+    assert a.ready_nodes() == ["n0"]
+
+
+def test_remove_is_refused_while_an_l2_copy_remains_and_the_node_stays_draining():
+    a = H.Authority()
+    model(a)
+    a.join_shard_node("n0", 16)
+    a.join_shard_node("n1", 16)
+    reg(a, [b"stuck"], [meta(b"stuck", node="n1")], node="n1")
+    a.drain_shard_node("n1")
+    with pytest.raises(ValueError, match="placements remain"):
+        a.remove_shard_node("n1")
+    assert a.ready_nodes() == ["n0"] and [(e.node_id, e.draining) for e in a.shard_map().nodes if e.node_id == "n1"] == [("n1", True)]
+
+
+def test_drain_keeps_target_and_draft_identities_apart():
+    a = H.Authority()
+    model(a)
+    a.join_shard_node("n0", 16)
+    a.join_shard_node("n1", 16)
+    reg(a, [b"same"], [meta(b"same", node="n1")], node="n1")
+    reg(a, [b"same"], [meta(b"same", node="n1", pk=DRAFT)], node="n1")
+    _, push = a.drain_shard_node("n1")
+    assert sorted(p.pool_kind for p in push if p.block_hash == b"same") == [TARGET, DRAFT]
