@@ -40,8 +40,13 @@ void AuthorityPort::set_l3_present(const KVBlockID& id, bool present) {
 }
 
 // ------------------------------------------------------------------ PutEnd
-PutEndSession::PutEndSession(std::string rid, std::string node, std::string model, std::string rev)
-    : request_id_(std::move(rid)), node_id_(std::move(node)), model_id_(std::move(model)), revision_(std::move(rev)) {}
+PutEndSession::PutEndSession(std::string rid, std::string node, std::string model, std::string rev,
+                             std::string storage_node)
+    : request_id_(std::move(rid)),
+      node_id_(std::move(node)),
+      model_id_(std::move(model)),
+      revision_(std::move(rev)),
+      storage_node_(storage_node.empty() ? node_id_ : std::move(storage_node)) {}
 
 void PutEndSession::put_start(const std::string& h, const uint8_t* bytes, size_t n) {
   prefix_.push_back(h);
@@ -59,7 +64,7 @@ std::vector<BlockMeta> PutEndSession::metas(const tier::TierEngine& store) const
     m.block_kind = cp::T_TYPE;
     if (store.is_l2_durable(b.id.block_hash)) {
       auto pl = store.l2_placement(b.id.block_hash);
-      m.locations.push_back(Location{cp::L2, node_id_, pl ? pl->segment_id : 1, pl ? pl->offset : 0});
+      m.locations.push_back(Location{cp::L2, storage_node_, pl ? pl->segment_id : 1, pl ? pl->offset : 0});
     }
     m.l3_present = store.l3_present(b.id.block_hash);
     out.push_back(std::move(m));
@@ -130,7 +135,7 @@ void PutEndSession::commit_through(ControlPlanePort& cp, tier::TierEngine& store
       for (auto& b : blocks_) ours |= b.id.block_hash == h;
       if (ours) continue;
       KVBlockID id{model_id_, h, cp::TARGET, "public", revision_};
-      cp.publish_location(id, cp::L2, node_id_, 0, 0, false);
+      cp.publish_location(id, cp::L2, storage_node_, 0, 0, false);
       cp.set_l3_present(id, true);
     }
   } catch (...) {
@@ -152,7 +157,7 @@ void PutEndSession::commit_through(ControlPlanePort& cp, tier::TierEngine& store
   try {
     for (auto& b : blocks_) {
       if (store.l3_present(b.id.block_hash)) cp.set_l3_present(b.id, true);
-      if (!store.is_l2_durable(b.id.block_hash)) cp.publish_location(b.id, cp::L2, node_id_, 0, 0, false);
+      if (!store.is_l2_durable(b.id.block_hash)) cp.publish_location(b.id, cp::L2, storage_node_, 0, 0, false);
     }
     if (!hold_open_) {
       cp.report_refs(deltas(cp::REQUEST, +1));

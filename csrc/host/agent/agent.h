@@ -59,7 +59,11 @@ class AuthorityPort : public ControlPlanePort {
 
 class PutEndSession {
  public:
-  PutEndSession(std::string request_id, std::string node_id, std::string model_id, std::string revision = "");
+  // node_id: the node that commits (its refs, register hold and barrier). storage_node: the node
+  // whose L2 holds the blocks (their L2 locations); empty = node_id. They differ when several
+  // engines share one pool node's tiers.
+  PutEndSession(std::string request_id, std::string node_id, std::string model_id, std::string revision = "",
+                std::string storage_node = "");
   void put_start(const std::string& block_hash, const uint8_t* bytes, size_t n);
   // Extend the prefix chain with a block that is already durable (no bytes, not re-registered).
   void add_prefix(const std::string& block_hash) {
@@ -83,7 +87,7 @@ class PutEndSession {
   };
   std::vector<cp::RefDelta> deltas(int kind, int32_t d) const;
   bool release_hold(ControlPlanePort& cp);
-  std::string request_id_, node_id_, model_id_, revision_;
+  std::string request_id_, node_id_, model_id_, revision_, storage_node_;
   std::vector<std::string> prefix_;
   std::vector<Pending> blocks_;
   bool writeback_open_ = false;

@@ -67,8 +67,8 @@ void register_agent(py::module_& m) {
       .def(py::init<cp::Authority*>(), py::keep_alive<1, 2>());
 
   py::class_<PutEndSession>(m, "PutEndSession")
-      .def(py::init<std::string, std::string, std::string, std::string>(), py::arg("request_id"), py::arg("node_id"),
-           py::arg("model_id"), py::arg("revision") = "")
+      .def(py::init<std::string, std::string, std::string, std::string, std::string>(), py::arg("request_id"),
+           py::arg("node_id"), py::arg("model_id"), py::arg("revision") = "", py::arg("storage_node") = "")
       .def("put_start",
            [](PutEndSession& s, const py::bytes& h, const py::bytes& data) {
              std::string d(data);

@@ -77,8 +77,8 @@ def run(seed: int = 0, requests: int = 8, prefix: int = 128, unique: int = 32, o
     page = p_eng.arena[0].numel() * p_eng.arena.element_size()
     with tempfile.TemporaryDirectory(prefix="lakeb_pool_") as root:
         node = make_pool_node("tiny", page, p_eng.pool.num_blocks, l1_blocks=64, l2_blocks=512, storage_dir=root)
-        p_agent = NativeAgent(p_eng, "prefill-0", authority=authority, shared_tiers=node)
-        d_agent = NativeAgent(d_eng, "decode-0", authority=authority, shared_tiers=node)
+        p_agent = NativeAgent(p_eng, "prefill-0", authority=authority, shared_tiers=node, storage_node_id="pool-0")
+        d_agent = NativeAgent(d_eng, "decode-0", authority=authority, shared_tiers=node, storage_node_id="pool-0")
         p_eng.attach_pool(PoolIface(p_agent, node_id="prefill-0"))
         d_eng.attach_pool(PoolIface(d_agent, node_id="decode-0"))
 

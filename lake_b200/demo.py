@@ -35,7 +35,8 @@ def run(device: str = "cpu", block_size: int = 16) -> dict:
         pool_node = make_pool_node(model, page, engines["worker-0"].pool.num_blocks, l1_blocks=16, l2_blocks=64,
                                    storage_dir=root)
         for n, eng in engines.items():
-            eng.attach_pool(PoolIface(NativeAgent(eng, n, authority=authority, shared_tiers=pool_node), node_id=n))
+            eng.attach_pool(PoolIface(NativeAgent(eng, n, authority=authority, shared_tiers=pool_node,
+                                                  storage_node_id="pool-0"), node_id=n))
         system = list(range(1, 49))  # three full blocks shared by both requests
         for name, node, prompt in (("A", "worker-0", system + [100, 101]), ("B", "worker-1", system + [200, 201])):
             mirror.apply(authority.snapshot())

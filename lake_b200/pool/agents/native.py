@@ -52,10 +52,14 @@ def make_pool_node(model_id: str, page_bytes: int, l0_blocks: int, l1_blocks: in
 class NativeAgent(StepFences):
     def __init__(self, engine, node_id: str = "node-0", model_id: str | None = None, revision: str = "",
                  authority: "H.Authority | None" = None, port=None, l1_blocks: int = 64, l2_blocks: int = 256,
-                 storage_dir: str | None = None, writeback: str = "all", shared_tiers=None):
+                 storage_dir: str | None = None, writeback: str = "all", shared_tiers=None,
+                 storage_node_id: str | None = None):
         super().__init__()
         self.eng = engine
         self.node_id = node_id
+        # the node whose tiers hold the written-back blocks (their L2 locations): this engine's
+        # node, or the pool node whose tiers several engines share (shared_tiers)
+        self.storage_node_id = storage_node_id or node_id
         self.model_id = model_id or engine.cfg.name
         self.revision = revision
         self.bs = engine.ec.block_size
@@ -148,11 +152,11 @@ class NativeAgent(StepFences):
             if v == h:
                 continue
             vid = self._ids([v])[0]
-            self.port.publish_location(vid, L2, self.node_id, 0, 0, False)
+            self.port.publish_location(vid, L2, self.storage_node_id, 0, 0, False)
             self.port.set_l3_present(vid, True)
         if not was_l2 and self.tiers.is_l2_durable(h):
             pl = self.tiers.l2_placement(h)
-            self.port.publish_location(self._ids([h])[0], L2, self.node_id, pl.segment_id, pl.offset, True)
+            self.port.publish_location(self._ids([h])[0], L2, self.storage_node_id, pl.segment_id, pl.offset, True)
 
     # ------------------------------------------------------------ fences
     def prepare_step(self, plan: PreparePlan) -> ReadyHandle:
@@ -197,7 +201,7 @@ class NativeAgent(StepFences):
         todo = [(h, p) for h, p in zip(hashes, pages) if h not in self.written]
         if not todo:
             return 0
-        sess = H.PutEndSession(req.rid, self.node_id, self.model_id, self.revision)
+        sess = H.PutEndSession(req.rid, self.node_id, self.model_id, self.revision, self.storage_node_id)
         started = False
         for h, page in zip(hashes, pages):
             if h in self.written and not started:

@@ -174,3 +174,34 @@ def test_promotion_from_l3_is_written_back_to_l2_and_mirrored_on_the_control_pla
         on_l2 = any(loc.tier == 3 and loc.node_id == "n0" for loc in meta.locations)
         assert on_l2 == tiers.is_l2_durable(h)
         assert meta.l3_present and tiers.l3_present(h)  # all five passed through L3
+
+
+def test_a_shared_pool_node_owns_the_l2_locations_and_outlives_an_engine(tmp_path):
+    """Two engines (worker-0, worker-1) share one pool node's tiers: what worker-0 writes back is
+    registered with its L2 copy on the pool node, so reconciling worker-0 as dead leaves the
+    durable copy in place and worker-1 still reuses the prefix from the pool."""
+    from lake_b200 import _host as H
+    from lake_b200.engine.block_pool import chain_block_hashes
+    from lake_b200.engine.llm_engine import LLMEngine
+    from lake_b200.pool.agents.native import NativeAgent, make_pool_node
+
+    kw = dict(device="cpu", max_running=4, max_batched_tokens=128, max_model_len=256, num_blocks=64)
+    a_eng, b_eng = LLMEngine("tiny", **kw), LLMEngine("tiny", **kw)
+    page = a_eng.arena[0].numel() * a_eng.arena.element_size()
+    node = make_pool_node("tiny", page, a_eng.pool.num_blocks, l1_blocks=8, l2_blocks=32, storage_dir=str(tmp_path))
+    authority = H.Authority()
+    for n, eng in (("worker-0", a_eng), ("worker-1", b_eng)):
+        eng.attach_pool(PoolIface(NativeAgent(eng, n, authority=authority, shared_tiers=node,
+                                              storage_node_id="pool-0"), node_id=n))
+    prompt = list(range(3, 3 + 3 * 16 + 1))
+    a_eng.generate([prompt], max_new_tokens=1)
+    hashes = chain_block_hashes(prompt, 16, full_only=True)[:3]
+    metas = authority.locate([H.KVBlockID("tiny", h) for h in hashes])
+    assert all([(loc.tier, loc.node_id) for loc in m.locations if loc.tier == 3] == [(3, "pool-0")] for m in metas)
+    authority.reconcile_dead_node("worker-0")
+    metas = authority.locate([H.KVBlockID("tiny", h) for h in hashes])
+    assert all(any(loc.tier == 3 and loc.node_id == "pool-0" for loc in m.locations) for m in metas)
+    rid = b_eng.add_request(prompt, max_new_tokens=1)
+    while b_eng.has_unfinished():
+        b_eng.step()
+    assert b_eng.requests[rid].num_cached == 3 * 16  # the three blocks came from the pool

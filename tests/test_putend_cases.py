@@ -255,3 +255,25 @@ def test_register_request_carries_each_blocks_arena_slot(tmp_path):
     s.commit_through(H.AuthorityPort(a), e)
     la = [l for l in _meta(a, "a").locations if l.tier == L2][0]
     assert (la.segment_id, la.offset) == (pa.segment_id, pa.offset)
+
+
+def test_a_session_names_the_storage_node_for_l2_and_the_committing_node_for_the_rest(tmp_path):
+    """Engines sharing a pool node commit as themselves (refs, hold, barrier) while the L2
+    locations name the pool node whose tiers hold the bytes."""
+    a, e = _auth(), _engine(tmp_path, (4, 4, 8))
+    seen = []
+
+    class Rec(Port):
+        def request_barrier(self, rid, node):
+            seen.append(("barrier", node))
+            super().request_barrier(rid, node)
+
+        def report_refs(self, deltas):
+            seen.extend(("ref", d.node_id) for d in deltas)
+            super().report_refs(deltas)
+
+    s = H.PutEndSession("r-shared", "eng-0", "m", "", "pool-0")
+    s.put_start(_h("x"), _blk("x"))
+    s.commit_through(Rec(a), e)
+    assert [(l.tier, l.node_id) for l in _meta(a, "x").locations if l.tier == L2] == [(L2, "pool-0")]
+    assert seen and all(node == "eng-0" for _, node in seen)
