@@ -9,7 +9,8 @@ SubscribeView protocol: the subscriber is attached to the broadcast first, then
 the initial sequence is taken under the lock - the full snapshot (seq 0) plus
 an empty anchor update carrying the last issued seq, or, for
 resume_from_seq > 0, the replay of the missed updates (falling back to the
-snapshot when the bounded replay log no longer covers it). Live updates with
+snapshot when the bounded replay log, ``LAKE_VIEW_LOG_CAP`` updates (default 1024), no
+longer covers it, or when the resume point is ahead of what this process issued). Live updates with
 seq <= the last delivered one are dropped (snapshot/broadcast overlap); a seq-0
 update (a restored checkpoint) resets the watermark and is always forwarded.
 A subscriber whose queue overflows is resynchronised with a fresh snapshot.
@@ -507,6 +508,8 @@ def serve(bind: str = "0.0.0.0:50051", cp: ControlPlane | None = None, max_worke
 
     cp = cp or ControlPlane(checkpoints=FileCheckpointStore(os.environ["LAKE_CP_CHECKPOINT"])
                             if os.environ.get("LAKE_CP_CHECKPOINT") else None)
+    if os.environ.get("LAKE_VIEW_LOG_CAP"):  # updates kept for resuming subscribers
+        cp.auth.set_view_log_cap(int(os.environ["LAKE_VIEW_LOG_CAP"]))
     server = grpc.server(futures.ThreadPoolExecutor(max_workers=max_workers), options=proto.message_options())
     proto.add_service(server, "ControlPlaneService", cp)
     port = server.add_insecure_port(bind)
