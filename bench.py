@@ -560,16 +560,26 @@ def run_pd(args, rank, world, local, group, barrier, tp_groups=None, ep_group=No
     # populate: run the closed loop until a full request lifetime of completions has passed,
     # so the decode batch holds requests at every stage of their output
     target = max(32, args.running // 4)
-    t_pop = time.perf_counter()
+    t_pop = t_note = time.perf_counter()
+    pop_steps = 0
     while agree(len(eng.scheduler.finished) < target):
         side.poll()
         if eng.has_unfinished() or ep is not None:
             side.step()  # (an idle expert-parallel rank still joins the group's exchange)
+            pop_steps += 1
         else:
             time.sleep(0.0005)
         top_up()
-        if time.perf_counter() - t_pop > 600:
-            raise RuntimeError("populate did not reach steady state in 600 s")
+        now = time.perf_counter()
+        if now - t_note > 30:  # a slow populate says where it stands (a stall shows which side waits)
+            t_note = now
+            print(f"rank {rank} populate {now - t_pop:.0f}s: {pop_steps} steps, finished "
+                  f"{len(eng.scheduler.finished)}/{target}, running {len(eng.scheduler.running)}, "
+                  f"waiting {len(eng.scheduler.waiting)}, prefill queue {len(side.pending)}, "
+                  f"in flight {side.inflight}", file=sys.stderr, flush=True)
+        if now - t_pop > 240:
+            raise RuntimeError(f"rank {rank}: populate did not reach steady state in 240 s "
+                               f"({len(eng.scheduler.finished)}/{target} requests finished)")
     for _ in range(args.warmup):
         side.poll()
         side.step()
