@@ -120,11 +120,15 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 }
 
 // Wait until *cnt >= target. Returns false after the time bound (status gets
-// kErrTimeoutFlag) or when the CTA's abort flag is raised.
+// kErrTimeoutFlag) or when the CTA's abort flag is raised. A wait that starts while the status
+// word already holds kErrTimeoutFlag (an earlier wait of this step ran out; the host clears the
+// word when it reports it after the step) fails at once, so a lost peer costs one time bound per
+// step rather than one per wait.
 __device__ __forceinline__ bool wait_counter(const unsigned long long* cnt, unsigned long long target,
                                              volatile int* abort_flag, int* status,
                                              uint64_t limit_ns = kWaitLimitNs) {
   if (ld_acquire_sys(cnt) >= target) return true;
+  if (status && *reinterpret_cast<volatile int*>(status) == kErrTimeoutFlag) return false;
   const uint64_t t0 = globaltimer_ns();
   for (uint32_t i = 1;; ++i) {
     if (ld_acquire_sys(cnt) >= target) return true;
