@@ -23,7 +23,7 @@ def run(device: str = "cpu", block_size: int = 16) -> dict:
     from .pool.agents.native import NativeAgent, make_pool_node
     from .pool.pool_iface import PoolIface
 
-    model = "tiny"
+    model = "tiny" if device == "cpu" else "tiny-gpu"  # the GPU kernels want head_dim 128 (bf16)
     kw = dict(device=device, max_running=4, max_batched_tokens=256, max_model_len=512, num_blocks=64,
               block_size=block_size)
     authority = H.Authority()
