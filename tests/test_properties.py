@@ -6,7 +6,9 @@ in the spirit of the reference's vendored block-manager property tests
   with a reference is never evicted, eviction frees at most what was asked, and a prefix lookup
   finds a contiguous run of registered blocks;
 * tier engine: L2 never holds more than its cap, every written block stays durable and reads
-  back its own bytes, and a pinned block never leaves L2."""
+  back its own bytes, and a pinned block never leaves L2;
+* router priority queue: no request is lost (each one is started and finished, or cancelled),
+  in flight never exceeds the slots, and a preempted request is requeued."""
 import pytest
 
 hypothesis = pytest.importorskip("hypothesis")
@@ -129,3 +131,59 @@ def test_tier_engine_cap_durability_and_pin_invariants(tmp_path_factory, ops):
             assert e.read_bytes(hj) == data[j]
         assert all(e.is_l2_durable(_h(9, j)) for j in pinned_in_l2)  # a pinned block stayed in L2
     assert e.corrupt_reads() == 0
+
+
+pq_ops = st.lists(st.one_of(
+    st.tuples(st.just("submit"), st.integers(0, 3), st.sampled_from(["m", "x"])),
+    st.tuples(st.just("finish"), st.integers(0, 30), st.booleans()),
+    st.tuples(st.just("cancel"), st.integers(0, 30)),
+    st.tuples(st.just("start"),),
+), max_size=60)
+
+
+@settings(max_examples=80, deadline=None)
+@given(st.integers(1, 3), pq_ops)
+def test_priority_queue_loses_no_request_and_respects_its_slots(slots, ops):
+    """Every submitted ticket ends started-and-finished or cancelled; in flight never exceeds
+    the slots; a preempted ticket is requeued, not dropped (reference: go/router/pq.go no-shed)."""
+    pq = H.PQScheduler(slots, 1.0)
+    waiting, running, cancelled, done = set(), set(), set(), set()
+    for op in ops:
+        if op[0] == "submit":
+            t, _ = pq.submit(op[1], op[2])
+            waiting.add(t)
+        elif op[0] == "start":
+            for t in pq.start_eligible():
+                assert t in waiting
+                waiting.discard(t)
+                running.add(t)
+        elif op[0] == "finish" and running:
+            t = sorted(running)[op[1] % len(running)]
+            pq.finish(t, preempted=op[2])
+            running.discard(t)
+            if op[2] and t not in cancelled:
+                waiting.add(t)  # a preempted request goes back to the queue
+            else:
+                done.add(t)
+        elif op[0] == "cancel" and (waiting or running):
+            pool = sorted(waiting | running)
+            t = pool[op[1] % len(pool)]
+            if pq.cancel(t):
+                assert t in waiting
+                waiting.discard(t)
+                cancelled.add(t)
+            else:
+                assert t in running
+                cancelled.add(t)  # abandoned: it is not requeued when it ends
+        assert pq.in_flight() == len(running) <= slots
+        assert pq.queue_len() == len(waiting)
+    while waiting or running:  # drain: everything left starts and finishes
+        for t in list(running):
+            pq.finish(t, preempted=False)
+            running.discard(t)
+            done.add(t)
+        for t in pq.start_eligible():
+            waiting.discard(t)
+            running.add(t)
+        if not running and waiting:
+            raise AssertionError(f"{len(waiting)} queued requests can never start")
